@@ -1,0 +1,482 @@
+// Python bindings of the sm_100a kernels and the domain runtime (torch extension `_C`).
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include "hcp/core/runtime.h"
+#include "kernels/attn_fwd_sm100.h"
+#include "kernels/decode.h"
+#include "kernels/elementwise.h"
+#include "kernels/gemm_sm100.h"
+
+namespace {
+
+using hcp::ArenaGeom;
+
+#define HCP_CHECK_OK(err) TORCH_CHECK((err) == nullptr, "hcp kernel: ", (err))
+
+void check_cuda_bf16(const torch::Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
+  TORCH_CHECK(t.scalar_type() == torch::kBFloat16, name, " must be bfloat16");
+}
+
+template <typename T>
+T* ptr_or_null(const c10::optional<torch::Tensor>& t) {
+  return (t.has_value() && t->defined()) ? reinterpret_cast<T*>(t->data_ptr()) : nullptr;
+}
+
+int sm_count(int dev) {
+  static int cached[64] = {0};
+  if (dev < 0 || dev >= 64) return 148;
+  if (cached[dev] == 0) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    cached[dev] = n > 0 ? n : 148;
+  }
+  return cached[dev];
+}
+
+cudaStream_t cur_stream() { return at::cuda::getCurrentCUDAStream().stream(); }
+
+// ----------------------------------------------------------------------------- kernels
+void gemm(torch::Tensor A, torch::Tensor B, torch::Tensor C, int64_t epi,
+          c10::optional<torch::Tensor> bias, c10::optional<torch::Tensor> R,
+          c10::optional<torch::Tensor> status) {
+  check_cuda_bf16(A, "A");
+  check_cuda_bf16(B, "B");
+  check_cuda_bf16(C, "C");
+  TORCH_CHECK(A.dim() == 2 && B.dim() == 2 && C.dim() == 2, "gemm expects 2-D tensors");
+  TORCH_CHECK(A.stride(1) == 1 && B.stride(1) == 1 && C.stride(1) == 1, "inner dim must be contiguous");
+  TORCH_CHECK(A.size(1) == B.size(1), "K mismatch");
+  const c10::cuda::CUDAGuard g(A.device());
+  hcp::gemm::GemmArgs a{};
+  a.A = reinterpret_cast<const __nv_bfloat16*>(A.data_ptr());
+  a.lda = A.stride(0);
+  a.B = reinterpret_cast<const __nv_bfloat16*>(B.data_ptr());
+  a.ldb = B.stride(0);
+  a.C = reinterpret_cast<__nv_bfloat16*>(C.data_ptr());
+  a.ldc = C.stride(0);
+  a.M = int(A.size(0));
+  a.N = int(B.size(0));
+  a.K = int(A.size(1));
+  a.epi = int(epi);
+  a.bias = ptr_or_null<const __nv_bfloat16>(bias);
+  if (R.has_value() && R->defined()) {
+    check_cuda_bf16(*R, "R");
+    a.R = reinterpret_cast<const __nv_bfloat16*>(R->data_ptr());
+    a.ldr = R->stride(0);
+  }
+  const int64_t n_out = (epi == hcp::gemm::kEpiSwiGLU) ? a.N / 2 : a.N;
+  TORCH_CHECK(C.size(0) == a.M && C.size(1) == n_out, "C has the wrong shape");
+  a.status = ptr_or_null<int>(status);
+  a.num_sms = sm_count(A.get_device());
+  HCP_CHECK_OK(hcp::gemm::gemm_bf16(a, cur_stream()));
+}
+
+void attn_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o,
+              c10::optional<torch::Tensor> lse, torch::Tensor q_pos, int64_t L,
+              int64_t kv_head_stride, double scale, bool causal, int64_t kv_start_tile,
+              c10::optional<torch::Tensor> status) {
+  check_cuda_bf16(q, "q");
+  check_cuda_bf16(k, "k");
+  check_cuda_bf16(v, "v");
+  check_cuda_bf16(o, "o");
+  TORCH_CHECK(q.dim() == 3 && q.is_contiguous(), "q must be [T, H, D] contiguous");
+  TORCH_CHECK(o.sizes() == q.sizes() && o.is_contiguous(), "o must match q");
+  TORCH_CHECK(q_pos.scalar_type() == torch::kInt32 && q_pos.is_cuda(), "q_pos must be int32 cuda");
+  TORCH_CHECK(q_pos.numel() == q.size(0), "q_pos length");
+  const int Hkv = int(k.size(0));
+  TORCH_CHECK(k.size(k.dim() - 1) == q.size(2), "head dim mismatch");
+  const c10::cuda::CUDAGuard g(q.device());
+  hcp::attn::AttnArgs a{};
+  a.Q = reinterpret_cast<const __nv_bfloat16*>(q.data_ptr());
+  a.K = reinterpret_cast<const __nv_bfloat16*>(k.data_ptr());
+  a.V = reinterpret_cast<const __nv_bfloat16*>(v.data_ptr());
+  a.O = reinterpret_cast<__nv_bfloat16*>(o.data_ptr());
+  a.lse = ptr_or_null<float>(lse);
+  if (lse.has_value() && lse->defined()) {
+    TORCH_CHECK(lse->scalar_type() == torch::kFloat32 && lse->numel() == q.size(0) * q.size(1),
+                "lse must be fp32 [H, T]");
+  }
+  a.q_pos = q_pos.data_ptr<int>();
+  a.T = int(q.size(0));
+  a.H = int(q.size(1));
+  a.Hkv = Hkv;
+  a.D = int(q.size(2));
+  a.L = int(L);
+  a.kv_head_stride = kv_head_stride;
+  TORCH_CHECK(kv_head_stride >= L * a.D, "kv_head_stride too small");
+  a.scale = float(scale);
+  a.causal = causal ? 1 : 0;
+  a.kv_start_tile = int(kv_start_tile);
+  a.status = ptr_or_null<int>(status);
+  HCP_CHECK_OK(hcp::attn::attn_fwd(a, cur_stream()));
+}
+
+void embedding(torch::Tensor ids, torch::Tensor W, torch::Tensor out,
+               c10::optional<torch::Tensor> status) {
+  check_cuda_bf16(W, "W");
+  check_cuda_bf16(out, "out");
+  TORCH_CHECK(ids.scalar_type() == torch::kInt32 && ids.is_cuda(), "ids must be int32 cuda");
+  const c10::cuda::CUDAGuard g(W.device());
+  HCP_CHECK_OK(hcp::ew::embedding(ids.data_ptr<int>(), reinterpret_cast<const __nv_bfloat16*>(W.data_ptr()),
+                                  reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), int(ids.numel()),
+                                  int(W.size(1)), int(W.size(0)), ptr_or_null<int>(status), cur_stream()));
+}
+
+void rmsnorm(torch::Tensor x, torch::Tensor w, torch::Tensor y, double eps) {
+  check_cuda_bf16(x, "x");
+  check_cuda_bf16(w, "w");
+  check_cuda_bf16(y, "y");
+  TORCH_CHECK(x.stride(-1) == 1 && y.stride(-1) == 1, "rows must be contiguous");
+  const c10::cuda::CUDAGuard g(x.device());
+  const int hidden = int(x.size(-1));
+  const int T = int(x.numel() / hidden);
+  HCP_CHECK_OK(hcp::ew::rmsnorm(reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()),
+                                reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()),
+                                reinterpret_cast<__nv_bfloat16*>(y.data_ptr()), T, hidden,
+                                x.dim() > 1 ? x.stride(-2) : hidden, y.dim() > 1 ? y.stride(-2) : hidden,
+                                float(eps), cur_stream()));
+}
+
+void gemv(torch::Tensor x, torch::Tensor W, int64_t epi, c10::optional<torch::Tensor> bias,
+          c10::optional<torch::Tensor> y_f32, c10::optional<torch::Tensor> y_bf16,
+          c10::optional<torch::Tensor> argmax) {
+  check_cuda_bf16(x, "x");
+  check_cuda_bf16(W, "W");
+  const c10::cuda::CUDAGuard g(x.device());
+  hcp::dec::GemvArgs a{};
+  a.x = reinterpret_cast<const __nv_bfloat16*>(x.data_ptr());
+  a.ldx = x.stride(0);
+  a.W = reinterpret_cast<const __nv_bfloat16*>(W.data_ptr());
+  a.B = int(x.size(0));
+  a.N = int(W.size(0));
+  a.K = int(W.size(1));
+  TORCH_CHECK(x.size(1) == a.K, "gemv K mismatch");
+  a.epi = int(epi);
+  a.bias = ptr_or_null<const __nv_bfloat16>(bias);
+  a.y_f32 = ptr_or_null<float>(y_f32);
+  a.y_bf16 = ptr_or_null<__nv_bfloat16>(y_bf16);
+  if (y_f32.has_value() && y_f32->defined()) a.ldy = y_f32->stride(0);
+  else if (y_bf16.has_value() && y_bf16->defined()) a.ldy = y_bf16->stride(0);
+  a.argmax = ptr_or_null<unsigned long long>(argmax);
+  a.num_sms = sm_count(x.get_device());
+  if (epi == hcp::dec::kGemvArgmax) TORCH_CHECK(a.argmax != nullptr, "argmax buffer required");
+  if (epi == hcp::dec::kGemvF32) TORCH_CHECK(a.y_f32 != nullptr, "y_f32 required");
+  if (epi == hcp::dec::kGemvResidual || epi == hcp::dec::kGemvSwiGLU)
+    TORCH_CHECK(a.y_bf16 != nullptr, "y_bf16 required");
+  HCP_CHECK_OK(hcp::dec::gemv(a, cur_stream()));
+}
+
+void fill_u64(torch::Tensor t, int64_t v) {
+  TORCH_CHECK(t.is_cuda() && t.element_size() == 8, "fill_u64 needs a cuda 64-bit tensor");
+  const c10::cuda::CUDAGuard g(t.device());
+  HCP_CHECK_OK(hcp::dec::fill_u64(reinterpret_cast<unsigned long long*>(t.data_ptr()), int(t.numel()),
+                                  static_cast<unsigned long long>(v), cur_stream()));
+}
+
+void argmax_finalize(torch::Tensor packed, c10::optional<torch::Tensor> tok32,
+                     c10::optional<torch::Tensor> tok64) {
+  const c10::cuda::CUDAGuard g(packed.device());
+  HCP_CHECK_OK(hcp::dec::argmax_finalize(reinterpret_cast<const unsigned long long*>(packed.data_ptr()),
+                                         int(packed.numel()), ptr_or_null<int>(tok32),
+                                         ptr_or_null<long long>(tok64), cur_stream()));
+}
+
+void add_u64(torch::Tensor t, int64_t v) {
+  const c10::cuda::CUDAGuard g(t.device());
+  HCP_CHECK_OK(hcp::dec::add_u64(reinterpret_cast<unsigned long long*>(t.data_ptr()),
+                                 static_cast<unsigned long long>(v), cur_stream()));
+}
+
+int64_t num_sms(int64_t dev) { return sm_count(int(dev)); }
+
+// ----------------------------------------------------------------------------- runtime
+class PyRuntime {
+ public:
+  PyRuntime(int64_t rank, int64_t world, int64_t device, int64_t layers, int64_t pages,
+            int64_t page, int64_t hkv, int64_t d, int64_t num_heads, int64_t stage_cap,
+            int64_t max_batch, int64_t wait_budget_ms) {
+    hcp::RuntimeConfig c;
+    c.rank = int(rank);
+    c.world = int(world);
+    c.device = int(device);
+    c.geom = ArenaGeom{int(layers), int(pages), int(page), int(hkv), int(d)};
+    c.num_heads = int(num_heads);
+    c.stage_cap = int(stage_cap);
+    c.max_batch = int(max_batch);
+    c.num_sms = sm_count(int(device));
+    c.peer_wait_budget_ns = uint64_t(wait_budget_ms) * 1000000ull;
+    auto st = rt_.Init(c);
+    TORCH_CHECK(st.ok(), "runtime init: ", st.ToString());
+  }
+
+  py::bytes export_handle() {
+    auto h = rt_.ExportHandle();
+    TORCH_CHECK(!h.empty(), "cudaIpcGetMemHandle failed");
+    return py::bytes(reinterpret_cast<const char*>(h.data()), h.size());
+  }
+
+  void open_peers(const std::vector<py::bytes>& handles) {
+    std::vector<std::vector<uint8_t>> hs;
+    for (const auto& b : handles) {
+      std::string s = b;
+      hs.emplace_back(s.begin(), s.end());
+    }
+    auto st = rt_.OpenPeers(hs);
+    TORCH_CHECK(st.ok(), "open_peers: ", st.ToString());
+  }
+
+  void open_peers_local(const std::vector<PyRuntime*>& peers) {
+    std::vector<hcp::DomainRuntime*> ps;
+    for (auto* p : peers) ps.push_back(&p->rt_);
+    auto st = rt_.OpenPeersLocal(ps);
+    TORCH_CHECK(st.ok(), "open_peers_local: ", st.ToString());
+  }
+
+  hcp::RingLayerArgs layer_args(torch::Tensor qkv, torch::Tensor pos, torch::Tensor cos_t,
+                                torch::Tensor sin_t, int64_t layer,
+                                c10::optional<torch::Tensor> page_table, int64_t slot_base,
+                                int64_t L, int64_t kv_start_tile, double scale, bool causal,
+                                torch::Tensor q_out, torch::Tensor o_out,
+                                c10::optional<torch::Tensor> lse_out, int64_t epoch) {
+    check_cuda_bf16(qkv, "qkv");
+    check_cuda_bf16(q_out, "q_out");
+    check_cuda_bf16(o_out, "o_out");
+    TORCH_CHECK(pos.scalar_type() == torch::kInt32, "pos must be int32");
+    TORCH_CHECK(cos_t.scalar_type() == torch::kFloat32 && sin_t.scalar_type() == torch::kFloat32, "cos/sin fp32");
+    const auto& c = rt_.config();
+    hcp::RingLayerArgs a;
+    a.qkv = qkv.data_ptr();
+    a.ld_qkv = qkv.stride(0);
+    a.pos = pos.data_ptr<int>();
+    a.cos_t = cos_t.data_ptr<float>();
+    a.sin_t = sin_t.data_ptr<float>();
+    a.max_pos = int(cos_t.size(0));
+    a.T = int(qkv.size(0));
+    a.H = int(q_out.size(1));
+    TORCH_CHECK(qkv.size(1) >= (a.H + 2 * c.geom.hkv) * c.geom.d, "qkv too narrow");
+    a.layer = int(layer);
+    if (page_table.has_value() && page_table->defined()) {
+      TORCH_CHECK(page_table->scalar_type() == torch::kInt32, "page table int32");
+      a.page_table = page_table->data_ptr<int>();
+      a.slot_cap = int(page_table->numel()) * c.geom.page;
+    }
+    a.slot_base = int(slot_base);
+    a.L = int(L);
+    a.kv_start_tile = int(kv_start_tile);
+    a.scale = float(scale);
+    a.causal = causal ? 1 : 0;
+    a.q_out = q_out.data_ptr();
+    a.o_out = o_out.data_ptr();
+    a.lse_out = ptr_or_null<float>(lse_out);
+    a.epoch = uint64_t(epoch);
+    return a;
+  }
+
+  void push_layer(torch::Tensor qkv, torch::Tensor pos, torch::Tensor cos_t, torch::Tensor sin_t,
+                  int64_t layer, c10::optional<torch::Tensor> page_table, int64_t slot_base,
+                  int64_t L, int64_t kv_start_tile, double scale, bool causal, torch::Tensor q_out,
+                  torch::Tensor o_out, c10::optional<torch::Tensor> lse_out, int64_t epoch) {
+    const c10::cuda::CUDAGuard g(qkv.device());
+    auto a = layer_args(qkv, pos, cos_t, sin_t, layer, page_table, slot_base, L, kv_start_tile,
+                        scale, causal, q_out, o_out, lse_out, epoch);
+    auto st = rt_.PushLayer(a, cur_stream());
+    TORCH_CHECK(st.ok(), "push_layer: ", st.ToString());
+  }
+
+  void attend_layer(torch::Tensor qkv, torch::Tensor pos, torch::Tensor cos_t, torch::Tensor sin_t,
+                    int64_t layer, c10::optional<torch::Tensor> page_table, int64_t slot_base,
+                    int64_t L, int64_t kv_start_tile, double scale, bool causal,
+                    torch::Tensor q_out, torch::Tensor o_out, c10::optional<torch::Tensor> lse_out,
+                    int64_t epoch) {
+    const c10::cuda::CUDAGuard g(qkv.device());
+    auto a = layer_args(qkv, pos, cos_t, sin_t, layer, page_table, slot_base, L, kv_start_tile,
+                        scale, causal, q_out, o_out, lse_out, epoch);
+    auto st = rt_.AttendLayer(a, cur_stream());
+    TORCH_CHECK(st.ok(), "attend_layer: ", st.ToString());
+  }
+
+  void qkv_decode(torch::Tensor qkv_f32, torch::Tensor pos, torch::Tensor cos_t, torch::Tensor sin_t,
+                  int64_t layer, torch::Tensor page_tables, torch::Tensor owner, torch::Tensor slot,
+                  torch::Tensor q_out) {
+    TORCH_CHECK(qkv_f32.scalar_type() == torch::kFloat32 && qkv_f32.is_contiguous(), "qkv must be fp32 contiguous");
+    check_cuda_bf16(q_out, "q_out");
+    TORCH_CHECK(owner.scalar_type() == torch::kInt32 && slot.scalar_type() == torch::kInt32, "owner/slot int32");
+    TORCH_CHECK(owner.dim() == 2 && owner.is_contiguous() && slot.sizes() == owner.sizes(), "owner/slot [B, layers]");
+    const c10::cuda::CUDAGuard g(qkv_f32.device());
+    const auto& c = rt_.config();
+    hcp::ew::QkvDecodeArgs a{};
+    a.qkv = qkv_f32.data_ptr<float>();
+    a.pos = pos.data_ptr<int>();
+    a.cos_t = cos_t.data_ptr<float>();
+    a.sin_t = sin_t.data_ptr<float>();
+    a.max_pos = int(cos_t.size(0));
+    a.B = int(qkv_f32.size(0));
+    a.H = int(q_out.size(1));
+    a.Hkv = c.geom.hkv;
+    a.D = c.geom.d;
+    TORCH_CHECK(qkv_f32.size(1) == (a.H + 2 * a.Hkv) * a.D, "qkv width");
+    a.q_out = reinterpret_cast<__nv_bfloat16*>(q_out.data_ptr());
+    a.arena = static_cast<__nv_bfloat16*>(rt_.arena());
+    a.geom = c.geom;
+    a.layer = int(layer);
+    a.page_tables = page_tables.data_ptr<int>();
+    a.pt_stride = int(page_tables.stride(0));
+    a.slot_cap = int(page_tables.size(1)) * c.geom.page;
+    a.owner = owner.data_ptr<int>();
+    a.slot = slot.data_ptr<int>();
+    a.owner_stride = int(owner.size(1));
+    a.status = rt_.status();
+    HCP_CHECK_OK(hcp::ew::qkv_decode(a, cur_stream()));
+  }
+
+  void decode_attn(torch::Tensor q, int64_t layer, torch::Tensor page_tables, torch::Tensor n_tokens,
+                   double scale, int64_t splits, torch::Tensor part_o, torch::Tensor part_lse,
+                   torch::Tensor counters, c10::optional<torch::Tensor> epoch_src,
+                   int64_t epoch_mul, int64_t epoch_add) {
+    check_cuda_bf16(q, "q");
+    const c10::cuda::CUDAGuard g(q.device());
+    const auto& c = rt_.config();
+    hcp::dec::DecodeAttnArgs a{};
+    a.q = reinterpret_cast<const __nv_bfloat16*>(q.data_ptr());
+    a.arena = static_cast<const __nv_bfloat16*>(rt_.arena());
+    a.geom = c.geom;
+    a.layer = int(layer);
+    a.page_tables = page_tables.data_ptr<int>();
+    a.pt_stride = int(page_tables.stride(0));
+    a.n_tokens = n_tokens.data_ptr<int>();
+    a.B = int(q.size(0));
+    a.H = int(q.size(1));
+    a.Hkv = c.geom.hkv;
+    a.D = c.geom.d;
+    TORCH_CHECK(a.B <= c.max_batch, "decode batch larger than the runtime's max_batch");
+    a.scale = float(scale);
+    a.splits = int(splits);
+    a.part_o = part_o.data_ptr<float>();
+    a.part_lse = part_lse.data_ptr<float>();
+    TORCH_CHECK(part_o.numel() >= int64_t(a.B) * a.H * a.splits * a.D, "part_o too small");
+    TORCH_CHECK(part_lse.numel() >= int64_t(a.B) * a.H * a.splits, "part_lse too small");
+    TORCH_CHECK(counters.numel() >= int64_t(a.B) * a.Hkv + 1 && counters.scalar_type() == torch::kInt32,
+                "counters must be int32 [B*Hkv + 1]");
+    a.split_counter = reinterpret_cast<unsigned int*>(counters.data_ptr());
+    a.grid_counter = a.split_counter + a.B * a.Hkv;
+    a.xslot_ptrs = rt_.xslot_table();
+    a.n_ranks = c.world;
+    a.my_rank = c.rank;
+    a.ready_ptrs = rt_.dec_ready_table();
+    a.epoch_parity_src = epoch_src.has_value() && epoch_src->defined()
+                             ? reinterpret_cast<const unsigned long long*>(epoch_src->data_ptr())
+                             : nullptr;
+    a.epoch_mul = uint64_t(epoch_mul);
+    a.epoch_add = uint64_t(epoch_add);
+    a.status = rt_.status();
+    HCP_CHECK_OK(hcp::dec::decode_attn(a, cur_stream()));
+  }
+
+  void decode_combine(torch::Tensor out, int64_t B, int64_t H, c10::optional<torch::Tensor> epoch_src,
+                      int64_t epoch_mul, int64_t epoch_add) {
+    check_cuda_bf16(out, "out");
+    const c10::cuda::CUDAGuard g(out.device());
+    const auto& c = rt_.config();
+    hcp::dec::DecodeCombineArgs a{};
+    a.xslot = rt_.xslot();
+    a.ready = c.world > 1 ? rt_.flags() + hcp::kFlagDecReady : nullptr;
+    a.epoch_src = epoch_src.has_value() && epoch_src->defined()
+                      ? reinterpret_cast<const unsigned long long*>(epoch_src->data_ptr())
+                      : nullptr;
+    a.epoch_mul = uint64_t(epoch_mul);
+    a.epoch_add = uint64_t(epoch_add);
+    a.n_ranks = c.world;
+    a.B = int(B);
+    a.H = int(H);
+    a.D = c.geom.d;
+    a.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+    a.budget_ns = c.peer_wait_budget_ns;
+    a.status = rt_.status();
+    HCP_CHECK_OK(hcp::dec::decode_combine(a, cur_stream()));
+  }
+
+  torch::Tensor arena() {
+    const auto& c = rt_.config();
+    auto opts = torch::TensorOptions().dtype(torch::kBFloat16).device(torch::kCUDA, c.device);
+    return torch::from_blob(rt_.arena(), {c.geom.layers, c.geom.pages, 2, c.geom.hkv, c.geom.page, c.geom.d}, opts);
+  }
+  torch::Tensor stage(int64_t parity) {
+    const auto& c = rt_.config();
+    auto opts = torch::TensorOptions().dtype(torch::kBFloat16).device(torch::kCUDA, c.device);
+    return torch::from_blob(rt_.stage(int(parity)), {2, c.geom.hkv, c.stage_cap, c.geom.d}, opts);
+  }
+  torch::Tensor flags() {
+    const auto& c = rt_.config();
+    auto opts = torch::TensorOptions().dtype(torch::kInt64).device(torch::kCUDA, c.device);
+    return torch::from_blob(rt_.flags(), {hcp::kFlagWords}, opts);
+  }
+  torch::Tensor status_words() {
+    const auto& c = rt_.config();
+    auto opts = torch::TensorOptions().dtype(torch::kInt32).device(torch::kCUDA, c.device);
+    return torch::from_blob(rt_.status(), {hcp::kStatusWords}, opts);
+  }
+  void check() {
+    auto st = rt_.CheckDevice(cur_stream());
+    TORCH_CHECK(st.ok(), "device status: ", st.ToString());
+  }
+  void shutdown() { rt_.Shutdown(); }
+  int64_t region_bytes() { return int64_t(rt_.region_bytes()); }
+  int64_t rank() { return rt_.config().rank; }
+  int64_t world() { return rt_.config().world; }
+
+ private:
+  hcp::DomainRuntime rt_;
+};
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "hetero_cp_ringattn_b200 sm_100a kernels and domain runtime";
+  m.def("gemm", &gemm, "tcgen05 GEMM with fused epilogue", py::arg("A"), py::arg("B"), py::arg("C"),
+        py::arg("epi") = 0, py::arg("bias") = py::none(), py::arg("R") = py::none(),
+        py::arg("status") = py::none());
+  m.def("attn_fwd", &attn_fwd, "tcgen05 flash attention with LSE and position-causal skip");
+  m.def("embedding", &embedding, py::arg("ids"), py::arg("W"), py::arg("out"), py::arg("status") = py::none());
+  m.def("rmsnorm", &rmsnorm);
+  m.def("gemv", &gemv, py::arg("x"), py::arg("W"), py::arg("epi"), py::arg("bias") = py::none(),
+        py::arg("y_f32") = py::none(), py::arg("y_bf16") = py::none(), py::arg("argmax") = py::none());
+  m.def("fill_u64", &fill_u64);
+  m.def("argmax_finalize", &argmax_finalize, py::arg("packed"), py::arg("tok32") = py::none(),
+        py::arg("tok64") = py::none());
+  m.def("add_u64", &add_u64);
+  m.def("num_sms", &num_sms);
+  m.attr("EPI_STORE") = int(hcp::gemm::kEpiStore);
+  m.attr("EPI_BIAS") = int(hcp::gemm::kEpiBias);
+  m.attr("EPI_RESIDUAL") = int(hcp::gemm::kEpiResidual);
+  m.attr("EPI_SWIGLU") = int(hcp::gemm::kEpiSwiGLU);
+  m.attr("GEMV_F32") = int(hcp::dec::kGemvF32);
+  m.attr("GEMV_RESIDUAL") = int(hcp::dec::kGemvResidual);
+  m.attr("GEMV_SWIGLU") = int(hcp::dec::kGemvSwiGLU);
+  m.attr("GEMV_ARGMAX") = int(hcp::dec::kGemvArgmax);
+  m.attr("FLAG_WORDS") = int(hcp::kFlagWords);
+  py::class_<PyRuntime>(m, "Runtime")
+      .def(py::init<int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t,
+                    int64_t, int64_t, int64_t, int64_t>(),
+           py::arg("rank"), py::arg("world"), py::arg("device"), py::arg("layers"), py::arg("pages"),
+           py::arg("page"), py::arg("hkv"), py::arg("d"), py::arg("num_heads"),
+           py::arg("stage_cap"), py::arg("max_batch"), py::arg("wait_budget_ms"))
+      .def("export_handle", &PyRuntime::export_handle)
+      .def("open_peers", &PyRuntime::open_peers)
+      .def("open_peers_local", &PyRuntime::open_peers_local)
+      .def("push_layer", &PyRuntime::push_layer)
+      .def("attend_layer", &PyRuntime::attend_layer)
+      .def("qkv_decode", &PyRuntime::qkv_decode)
+      .def("decode_attn", &PyRuntime::decode_attn)
+      .def("decode_combine", &PyRuntime::decode_combine)
+      .def("arena", &PyRuntime::arena)
+      .def("stage", &PyRuntime::stage)
+      .def("flags", &PyRuntime::flags)
+      .def("status_words", &PyRuntime::status_words)
+      .def("check", &PyRuntime::check)
+      .def("shutdown", &PyRuntime::shutdown)
+      .def("region_bytes", &PyRuntime::region_bytes)
+      .def("rank", &PyRuntime::rank)
+      .def("world", &PyRuntime::world);
+}

@@ -1,0 +1,131 @@
+// Domain runtime: owns one rank's device memory for context-parallel inference and its NVLink
+// peer mappings.
+//
+// Parity: the reference's RingAttnRuntime interface (include/hcp_ringattn/core/
+// ringattn_runtime.h:13-28: Init / RunRingAttentionLayer / Shutdown) whose only implementation
+// is a no-op validator (src/ringattn_runtime.cc:10-70). Here Init binds the GPU and allocates
+// the shared region, OpenPeers maps every peer's region through CUDA IPC, and
+// RunRingAttentionLayer launches the fused KV push + ring attention kernels for one layer.
+//
+// Shared region (one cudaMalloc, exported with one IPC handle; identical offsets on every rank):
+//   flags     uint64[kFlagWords]                           (kv_ready / consumed / dec_ready / ...)
+//   xslot     fp32 [2][world][max_batch][H][D+1]          decode (O, LSE) exchange slots
+//   stage     bf16 [2 parity][2 K/V][Hkv][stage_cap][D]   position-ordered prefill KV
+//   arena     bf16 [layers][pages][2][Hkv][page][D]       paged KV cache shard
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <vector>
+
+#include "hcp/core/status.h"
+#include "hcp/core/types.h"
+#include "../../../kernels/kv_layout.h"
+
+namespace hcp {
+
+struct RuntimeConfig {
+  int rank = 0;
+  int world = 1;
+  int device = 0;
+  ArenaGeom geom{};       // layers, pages, page, hkv, d
+  int num_heads = 0;      // H (decode exchange slot width)
+  int stage_cap = 0;      // staging capacity in positions (max prompt / context length)
+  int max_batch = 8;      // decode rows
+  int num_sms = 148;
+  uint64_t peer_wait_budget_ns = 5000000000ull;
+};
+
+struct RingLayerArgs {
+  // projection output [T, (H + 2 Hkv) D] (q | k | v, bias already added)
+  const void* qkv = nullptr;
+  long ld_qkv = 0;
+  const int* pos = nullptr;         // [T] global positions of this rank's tokens
+  const float* cos_t = nullptr;     // [max_pos, D/2]
+  const float* sin_t = nullptr;
+  int max_pos = 0;
+  int T = 0;
+  int H = 0;
+  int layer = 0;
+  const int* page_table = nullptr;  // this request's pages (same ids for all layers)
+  int slot_base = 0;
+  int slot_cap = 0;
+  int L = 0;                        // total context length (positions 0..L-1)
+  int kv_start_tile = 0;            // first kv tile of this rank's own chunk
+  float scale = 0.f;
+  int causal = 1;
+  void* q_out = nullptr;            // [T, H, D] scratch
+  void* o_out = nullptr;            // [T, H, D]
+  float* lse_out = nullptr;         // [H, T] (optional)
+  uint64_t epoch = 0;               // strictly increasing per layer step (same on all ranks)
+};
+
+class DomainRuntime {
+ public:
+  DomainRuntime() = default;
+  ~DomainRuntime();
+  DomainRuntime(const DomainRuntime&) = delete;
+  DomainRuntime& operator=(const DomainRuntime&) = delete;
+
+  Status Init(const RuntimeConfig& cfg);
+  // CUDA IPC handle of the shared region (64 bytes).
+  std::vector<uint8_t> ExportHandle() const;
+  // handles[r] for every rank r (own entry ignored).
+  Status OpenPeers(const std::vector<std::vector<uint8_t>>& handles);
+  // Emulated peers inside one process (tests): peers[r] are other runtimes on the same GPU.
+  Status OpenPeersLocal(const std::vector<DomainRuntime*>& peers);
+  // PushLayer: RoPE + KV write + P2P push of this rank's K/V into every rank's staging buffer.
+  // AttendLayer: wait (bounded) for every rank's push, run ring attention, release the buffer.
+  // RunRingAttentionLayer = PushLayer + AttendLayer. Emulated multi-rank runs on one GPU call
+  // PushLayer for every rank before any AttendLayer, so no launch ever waits on a later one.
+  Status RunRingAttentionLayer(const RingLayerArgs& a, cudaStream_t stream);
+  Status PushLayer(const RingLayerArgs& a, cudaStream_t stream);
+  Status AttendLayer(const RingLayerArgs& a, cudaStream_t stream);
+  Status Shutdown();
+
+  // Reads and clears the device status words (synchronises the given stream first).
+  Status CheckDevice(cudaStream_t stream);
+
+  const RuntimeConfig& config() const { return cfg_; }
+  bool initialized() const { return base_ != nullptr; }
+  uint8_t* base() const { return base_; }
+  size_t region_bytes() const { return region_bytes_; }
+  unsigned long long* flags() const { return reinterpret_cast<unsigned long long*>(base_ + off_flags_); }
+  float* xslot() const { return reinterpret_cast<float*>(base_ + off_xslot_); }
+  void* stage(int parity) const { return base_ + off_stage_ + size_t(parity) * stage_parity_bytes_; }
+  void* arena() const { return base_ + off_arena_; }
+  size_t arena_bytes() const { return arena_bytes_; }
+  size_t stage_parity_bytes() const { return stage_parity_bytes_; }
+  size_t xslot_bytes() const { return xslot_bytes_; }
+  int* status() const { return status_; }
+  unsigned int* counters() const { return counters_; }
+  // device pointer tables (arrays in device memory, indexed by rank)
+  void* const* stage_table(int parity) const { return stage_tab_[parity]; }
+  unsigned long long* const* kv_ready_table() const { return kv_ready_tab_; }
+  unsigned long long* const* consumed_table() const { return consumed_tab_; }
+  unsigned long long* const* dec_ready_table() const { return dec_ready_tab_; }
+  float* const* xslot_table() const { return xslot_tab_; }
+  // host copies of peer region bases (index = rank)
+  const std::vector<uint8_t*>& peer_bases() const { return peer_base_; }
+
+ private:
+  Status BuildTables();
+
+  RuntimeConfig cfg_{};
+  uint8_t* base_ = nullptr;
+  size_t region_bytes_ = 0;
+  size_t off_flags_ = 0, off_xslot_ = 0, off_stage_ = 0, off_arena_ = 0;
+  size_t xslot_bytes_ = 0, stage_parity_bytes_ = 0, arena_bytes_ = 0;
+  int* status_ = nullptr;            // kStatusWords int32
+  unsigned int* counters_ = nullptr; // 64 uint32 (last-CTA-done counters)
+  void** stage_tab_[2] = {nullptr, nullptr};
+  unsigned long long** kv_ready_tab_ = nullptr;
+  unsigned long long** consumed_tab_ = nullptr;
+  unsigned long long** dec_ready_tab_ = nullptr;
+  float** xslot_tab_ = nullptr;
+  std::vector<uint8_t*> peer_base_;
+  std::vector<bool> peer_opened_ipc_;
+};
+
+}  // namespace hcp

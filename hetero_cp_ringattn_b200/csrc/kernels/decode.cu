@@ -1,0 +1,440 @@
+// Decode-path kernels (B <= 8 rows per step):
+//
+//  * gemv_*: weight-streaming GEMV y[B,N] = x[B,K] W[N,K]^T with fused epilogues (fp32 out + bias
+//    for QKV, in-place residual add for O/down projections, SwiGLU on 128-row interleaved
+//    gate||up weights, fp32 logits + packed argmax for the LM head). Decode is bound by reading
+//    the weights once per step, so these run on the CUDA cores at HBM bandwidth instead of
+//    padding M=1..8 up to a 128-row tensor-core tile.
+//  * K2 cp decode: split-KV flash-decoding over this rank's paged KV shard (GQA group packed in
+//    one CTA), the split combine in the last CTA of each (row, kv-head), then the rank's partial
+//    (O, LSE) is stored straight into every rank's exchange slots through NVLink peer mappings,
+//    followed by a release flag; `decode_combine` waits (bounded) for all ranks' flags and does
+//    the log-sum-exp combine in rank order, so every rank computes bit-identical outputs.
+//
+// Parity: replaces the reference's decode routes: the Q-ring partial/merge
+// (rust/src/model/attention/ring.rs:625-663, 682-818: local (O, LSE), N-1 serial hops, merge
+// with durable KV) and the self-driving packet walk (rust/src/model/self_driving.rs:333-675,
+// rust/src/worker_sdk/tch_backend.rs:634-904). All ranks compute their partial concurrently and
+// exchange O(B*H*D) bytes once per layer instead of N-1 serial network hops.
+#include "common.cuh"
+#include "decode.h"
+#include "kv_layout.h"
+
+namespace hcp {
+namespace dec {
+
+using namespace hcp::dev;
+
+constexpr float kLog2e = 1.4426950408889634f;
+
+__device__ __forceinline__ void dot8_acc(const uint4 w, const uint4 x, float& acc) {
+  const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
+  const uint32_t xv[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    acc = fmaf(bf16_lo(wv[j]), bf16_lo(xv[j]), acc);
+    acc = fmaf(bf16_hi(wv[j]), bf16_hi(xv[j]), acc);
+  }
+}
+
+__device__ __forceinline__ uint4 ld_stream(const uint4* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
+__device__ __forceinline__ unsigned long long pack_argmax(float v, int idx) {
+  uint32_t u = __float_as_uint(v);
+  u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);  // order-preserving float -> uint
+  return (static_cast<unsigned long long>(u) << 32) | (0xFFFFFFFFu - uint32_t(idx));
+}
+
+// One warp computes ROWS output rows (or ROWS gate/up pairs for SwiGLU) for all B inputs.
+template <int EPI, int B, int ROWS>
+__global__ void __launch_bounds__(256) gemv_kernel(GemvArgs a) {
+  const int lane = threadIdx.x % 32;
+  const int warp_global = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
+  const int total_warps = (gridDim.x * blockDim.x) / 32;
+  const int kvec = a.K / 8;
+  const int out_rows = (EPI == kGemvSwiGLU) ? a.N / 2 : a.N;
+  for (int base = warp_global * ROWS; base < out_rows; base += total_warps * ROWS) {
+    float acc[ROWS][B];
+    float acc_u[ROWS][B];
+#pragma unroll
+    for (int r = 0; r < ROWS; ++r)
+#pragma unroll
+      for (int b = 0; b < B; ++b) acc[r][b] = acc_u[r][b] = 0.f;
+    int wrow[ROWS], urow[ROWS];
+#pragma unroll
+    for (int r = 0; r < ROWS; ++r) {
+      int o = base + r;
+      if (o >= out_rows) o = out_rows - 1;
+      if (EPI == kGemvSwiGLU) {
+        wrow[r] = (o / 128) * 256 + (o % 128);
+        urow[r] = wrow[r] + 128;
+      } else {
+        wrow[r] = o;
+        urow[r] = o;
+      }
+    }
+#pragma unroll 2
+    for (int k = lane; k < kvec; k += 32) {
+      uint4 w[ROWS], u[ROWS];
+#pragma unroll
+      for (int r = 0; r < ROWS; ++r) {
+        w[r] = ld_stream(reinterpret_cast<const uint4*>(a.W + (long)wrow[r] * a.K) + k);
+        if (EPI == kGemvSwiGLU)
+          u[r] = ld_stream(reinterpret_cast<const uint4*>(a.W + (long)urow[r] * a.K) + k);
+      }
+#pragma unroll
+      for (int b = 0; b < B; ++b) {
+        const uint4 xv = __ldg(reinterpret_cast<const uint4*>(a.x + (long)b * a.ldx) + k);
+#pragma unroll
+        for (int r = 0; r < ROWS; ++r) {
+          dot8_acc(w[r], xv, acc[r][b]);
+          if (EPI == kGemvSwiGLU) dot8_acc(u[r], xv, acc_u[r][b]);
+        }
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < ROWS; ++r)
+#pragma unroll
+      for (int b = 0; b < B; ++b) {
+        acc[r][b] = warp_sum(acc[r][b]);
+        if (EPI == kGemvSwiGLU) acc_u[r][b] = warp_sum(acc_u[r][b]);
+      }
+    if (lane == 0) {
+#pragma unroll
+      for (int r = 0; r < ROWS; ++r) {
+        const int o = base + r;
+        if (o >= out_rows) continue;
+#pragma unroll
+        for (int b = 0; b < B; ++b) {
+          float v = acc[r][b];
+          if (EPI == kGemvF32) {
+            if (a.bias) v += __bfloat162float(a.bias[o]);
+            a.y_f32[(long)b * a.ldy + o] = v;
+          } else if (EPI == kGemvResidual) {
+            __nv_bfloat16* y = a.y_bf16 + (long)b * a.ldy + o;
+            *y = __float2bfloat16(__bfloat162float(__float2bfloat16(v)) + __bfloat162float(*y));
+          } else if (EPI == kGemvSwiGLU) {
+            const float g = __bfloat162float(__float2bfloat16(v));
+            const float uu = __bfloat162float(__float2bfloat16(acc_u[r][b]));
+            const float s = g / (1.f + fast_exp2(-g * kLog2e));
+            a.y_bf16[(long)b * a.ldy + o] = __float2bfloat16(s * uu);
+          } else if (EPI == kGemvArgmax) {
+            if (a.y_f32) a.y_f32[(long)b * a.ldy + o] = v;
+          }
+        }
+      }
+    }
+    if (EPI == kGemvArgmax) {
+      // per-warp candidates -> global packed max (lane 0 holds the reduced values)
+      if (lane == 0) {
+#pragma unroll
+        for (int b = 0; b < B; ++b) {
+          unsigned long long best = 0;
+#pragma unroll
+          for (int r = 0; r < ROWS; ++r) {
+            const int o = base + r;
+            if (o < out_rows) {
+              const unsigned long long c = pack_argmax(acc[r][b], o);
+              best = c > best ? c : best;
+            }
+          }
+          atomicMax(a.argmax + b, best);
+        }
+      }
+    }
+  }
+}
+
+template <int EPI>
+static cudaError_t gemv_dispatch_b(const GemvArgs& a, int grid, cudaStream_t s) {
+  constexpr int R = (EPI == kGemvSwiGLU) ? 2 : 4;
+  switch (a.B) {
+    case 1: gemv_kernel<EPI, 1, R><<<grid, 256, 0, s>>>(a); break;
+    case 2: gemv_kernel<EPI, 2, R><<<grid, 256, 0, s>>>(a); break;
+    case 4: gemv_kernel<EPI, 4, R><<<grid, 256, 0, s>>>(a); break;
+    case 8: gemv_kernel<EPI, 8, 2><<<grid, 256, 0, s>>>(a); break;
+    default: return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
+const char* gemv(const GemvArgs& a, cudaStream_t s) {
+  if (a.K % 8 || a.ldx % 8) return "gemv: K and ldx must be multiples of 8";
+  if (a.B != 1 && a.B != 2 && a.B != 4 && a.B != 8) return "gemv: B must be 1, 2, 4 or 8";
+  if (a.epi == kGemvSwiGLU && a.N % 256) return "gemv: SwiGLU needs N % 256 == 0";
+  if ((reinterpret_cast<uintptr_t>(a.W) | reinterpret_cast<uintptr_t>(a.x)) & 15)
+    return "gemv: W/x must be 16-byte aligned";
+  const int grid = a.num_sms * 4;
+  cudaError_t e;
+  switch (a.epi) {
+    case kGemvF32: e = gemv_dispatch_b<kGemvF32>(a, grid, s); break;
+    case kGemvResidual: e = gemv_dispatch_b<kGemvResidual>(a, grid, s); break;
+    case kGemvSwiGLU: e = gemv_dispatch_b<kGemvSwiGLU>(a, grid, s); break;
+    case kGemvArgmax: e = gemv_dispatch_b<kGemvArgmax>(a, grid, s); break;
+    default: return "gemv: unknown epilogue";
+  }
+  return e == cudaSuccess ? nullptr : cudaGetErrorString(e);
+}
+
+// ----------------------------------------------------------------------------- K2 decode attention
+// grid (splits, Hkv, B), 128 threads. Each group of D/8 lanes handles one token at a time.
+template <int D, int G>
+__global__ void __launch_bounds__(128) decode_attn_kernel(DecodeAttnArgs a) {
+  constexpr int LPG = D / 8;        // lanes per token
+  constexpr int TPW = 32 / LPG;     // tokens per warp step
+  constexpr int GROUPS = 4 * TPW;   // token groups per CTA
+  const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int lane = threadIdx.x % 32, warp = threadIdx.x / 32;
+  const int gl = lane % LPG;                  // lane within group
+  const int grp = warp * TPW + lane / LPG;    // group id within CTA
+  const int n = a.n_tokens[b];
+  const int per = (n + a.splits - 1) / a.splits;
+  const int s0 = split * per;
+  const int s1 = min(n, s0 + per);
+  const int H = a.Hkv * G;
+
+  // q slice (pre-scaled into the log2 domain)
+  float q[G][8];
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    const uint4 v = *reinterpret_cast<const uint4*>(a.q + ((long)b * H + h * G + g) * D + gl * 8);
+    const uint32_t vv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      q[g][2 * j] = bf16_lo(vv[j]) * a.scale * kLog2e;
+      q[g][2 * j + 1] = bf16_hi(vv[j]) * a.scale * kLog2e;
+    }
+  }
+  float m[G], l[G], acc[G][8];
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    m[g] = -INFINITY;
+    l[g] = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[g][j] = 0.f;
+  }
+  const int* pt = a.page_tables + (long)b * a.pt_stride;
+  for (int t = s0 + grp; t < s1; t += GROUPS) {
+    const int page = pt[t / a.geom.page];
+    const int row = t % a.geom.page;
+    const __nv_bfloat16* kp = a.arena + a.geom.offset(a.layer, page, 0, h, row) + gl * 8;
+    const __nv_bfloat16* vp = kp + a.geom.kv_stride();
+    const uint4 kv = *reinterpret_cast<const uint4*>(kp);
+    const uint4 vv4 = *reinterpret_cast<const uint4*>(vp);
+    const uint32_t kw[4] = {kv.x, kv.y, kv.z, kv.w};
+    const uint32_t vw[4] = {vv4.x, vv4.y, vv4.z, vv4.w};
+    float vf[8];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      vf[2 * j] = bf16_lo(vw[j]);
+      vf[2 * j + 1] = bf16_hi(vw[j]);
+    }
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      float sc = 0.f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        sc = fmaf(q[g][2 * j], bf16_lo(kw[j]), sc);
+        sc = fmaf(q[g][2 * j + 1], bf16_hi(kw[j]), sc);
+      }
+#pragma unroll
+      for (int o = LPG / 2; o > 0; o >>= 1) sc += __shfl_xor_sync(0xffffffffu, sc, o);
+      const float mn = fmaxf(m[g], sc);
+      const float al = fast_exp2(m[g] - mn);
+      const float pp = fast_exp2(sc - mn);
+      l[g] = l[g] * al + pp;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[g][j] = fmaf(acc[g][j], al, pp * vf[j]);
+      m[g] = mn;
+    }
+  }
+  // CTA reduction over the GROUPS token groups through shared memory
+  __shared__ float sm_m[GROUPS][G];
+  __shared__ float sm_l[GROUPS][G];
+  __shared__ float sm_acc[GROUPS][G][D];
+  if (gl == 0) {
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      sm_m[grp][g] = m[g];
+      sm_l[grp][g] = l[g];
+    }
+  }
+#pragma unroll
+  for (int g = 0; g < G; ++g)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) sm_acc[grp][g][gl * 8 + j] = acc[g][j];
+  __syncthreads();
+  // each thread finalises (g, d) entries: G * D outputs over 128 threads
+  float* po = a.part_o + ((long)(b * H + h * G) * a.splits + split) * D;   // [B,H,splits,D]
+  float* pml = a.part_lse + (long)(b * H + h * G) * a.splits + split;      // [B,H,splits]
+  for (int i = threadIdx.x; i < G * D; i += blockDim.x) {
+    const int g = i / D, d = i % D;
+    float mx = -INFINITY;
+    for (int r = 0; r < GROUPS; ++r) mx = fmaxf(mx, sm_m[r][g]);
+    float ls = 0.f, o = 0.f;
+    if (mx > -INFINITY) {
+      for (int r = 0; r < GROUPS; ++r) {
+        const float w = fast_exp2(sm_m[r][g] - mx);
+        ls += sm_l[r][g] * w;
+        o += sm_acc[r][g][d] * w;
+      }
+    }
+    po[(long)g * a.splits * D + d] = ls > 0.f ? o / ls : 0.f;
+    if (d == 0) pml[(long)g * a.splits] = ls > 0.f ? mx + __log2f(ls) : -INFINITY;
+  }
+  // last CTA of this (b, h) combines the splits and publishes the rank partial
+  __shared__ bool is_last;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const unsigned prev = atomicAdd(a.split_counter + b * a.Hkv + h, 1u);
+    is_last = (prev == unsigned(a.splits) - 1);
+  }
+  __syncthreads();
+  if (!is_last) return;
+  __threadfence();
+  const unsigned long long epoch =
+      a.epoch_parity_src ? (*a.epoch_parity_src * a.epoch_mul + a.epoch_add) : a.epoch_add;
+  const int parity = int(epoch & 1ull);
+  for (int i = threadIdx.x; i < G * (D + 1); i += blockDim.x) {
+    const int g = i / (D + 1), d = i % (D + 1);
+    const float* pl = a.part_lse + (long)(b * H + h * G + g) * a.splits;
+    float mx = -INFINITY;
+    for (int s = 0; s < a.splits; ++s) mx = fmaxf(mx, ((volatile const float*)pl)[s]);
+    float val;
+    if (mx == -INFINITY) {
+      val = (d < D) ? 0.f : -INFINITY;
+    } else {
+      float ws = 0.f, o = 0.f;
+      const float* pof = a.part_o + (long)(b * H + h * G + g) * a.splits * D;
+      for (int s = 0; s < a.splits; ++s) {
+        const float w = fast_exp2(((volatile const float*)pl)[s] - mx);
+        ws += w;
+        if (d < D) o += w * ((volatile const float*)pof)[(long)s * D + d];
+      }
+      val = (d < D) ? o / ws : mx + __log2f(ws);
+    }
+    // exchange slot layout: [2 parity][N src][B][H][D+1] fp32
+    const long off = (((long)parity * a.n_ranks + a.my_rank) * a.B * H + (long)b * H + h * G + g) * (D + 1) + d;
+    for (int r = 0; r < a.n_ranks; ++r) a.xslot_ptrs[r][off] = val;
+  }
+  if (threadIdx.x == 0) a.split_counter[b * a.Hkv + h] = 0;
+  // grid-wide last CTA signals every rank that this rank's partial has landed
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    const unsigned prev = atomicAdd(a.grid_counter, 1u);
+    if (prev == unsigned(a.B * a.Hkv) - 1) {
+      __threadfence_system();
+      for (int r = 0; r < a.n_ranks; ++r) st_release_sys(a.ready_ptrs[r], epoch);
+      *a.grid_counter = 0;
+    }
+  }
+}
+
+// grid (B), block 256: wait for every rank's partial (bounded), then LSE-combine in rank order.
+__global__ void decode_combine_kernel(DecodeCombineArgs a) {
+  const int b = blockIdx.x;
+  const unsigned long long e = a.epoch_src ? (*a.epoch_src * a.epoch_mul + a.epoch_add) : a.epoch_add;
+  const int parity = int(e & 1ull);
+  __shared__ int ok;
+  if (threadIdx.x == 0) ok = 1;
+  __syncthreads();
+  if (threadIdx.x < a.n_ranks && a.ready != nullptr) {
+    if (!wait_flag_geq_sys(a.ready + threadIdx.x, e, a.budget_ns, a.status, 401, threadIdx.x)) ok = 0;
+  }
+  __syncthreads();
+  const int H = a.H, D = a.D;
+  const float* xs = a.xslot + (long)parity * a.n_ranks * a.B * H * (D + 1);
+  for (int i = threadIdx.x; i < H * D; i += blockDim.x) {
+    const int hh = i / D, d = i % D;
+    float out = 0.f;
+    if (ok) {
+      float mx = -INFINITY;
+      for (int r = 0; r < a.n_ranks; ++r)
+        mx = fmaxf(mx, ((volatile const float*)xs)[(((long)r * a.B + b) * H + hh) * (D + 1) + D]);
+      if (mx > -INFINITY) {
+        float ws = 0.f, o = 0.f;
+        for (int r = 0; r < a.n_ranks; ++r) {
+          const long base = (((long)r * a.B + b) * H + hh) * (D + 1);
+          const float w = fast_exp2(((volatile const float*)xs)[base + D] - mx);
+          ws += w;
+          o += w * ((volatile const float*)xs)[base + d];
+        }
+        out = o / ws;
+      }
+    }
+    a.out[(long)b * H * D + i] = __float2bfloat16(out);
+  }
+}
+
+template <int D, int G>
+static cudaError_t launch_attn(const DecodeAttnArgs& a, cudaStream_t s) {
+  dim3 grid(a.splits, a.Hkv, a.B);
+  decode_attn_kernel<D, G><<<grid, 128, 0, s>>>(a);
+  return cudaGetLastError();
+}
+
+const char* decode_attn(const DecodeAttnArgs& a, cudaStream_t s) {
+  const int G = a.H / a.Hkv;
+  if (a.H % a.Hkv) return "decode_attn: H % Hkv";
+  if (a.n_ranks < 1 || a.n_ranks > kMaxRanks) return "decode_attn: bad n_ranks";
+  cudaError_t e = cudaErrorInvalidValue;
+#define HCP_DEC_CASE(DD, GG) \
+  if (a.D == DD && G == GG) e = launch_attn<DD, GG>(a, s);
+  HCP_DEC_CASE(64, 1) HCP_DEC_CASE(64, 2) HCP_DEC_CASE(64, 4) HCP_DEC_CASE(64, 8)
+  HCP_DEC_CASE(128, 1) HCP_DEC_CASE(128, 2) HCP_DEC_CASE(128, 4) HCP_DEC_CASE(128, 8)
+#undef HCP_DEC_CASE
+  if (e == cudaErrorInvalidValue) return "decode_attn: unsupported (D, H/Hkv)";
+  return e == cudaSuccess ? nullptr : cudaGetErrorString(e);
+}
+
+const char* decode_combine(const DecodeCombineArgs& a, cudaStream_t s) {
+  if (a.n_ranks > 256) return "decode_combine: too many ranks";
+  decode_combine_kernel<<<a.B, 256, 0, s>>>(a);
+  return cudaGetLastError() == cudaSuccess ? nullptr : "decode_combine: launch failed";
+}
+
+// ----------------------------------------------------------------------------- small helpers
+__global__ void fill_u64_kernel(unsigned long long* p, int n, unsigned long long v) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) p[i] = v;
+}
+
+__global__ void argmax_finalize_kernel(const unsigned long long* packed, int B, int* tokens_out,
+                                       long long* tokens_out64) {
+  const int b = threadIdx.x;
+  if (b < B) {
+    const int idx = int(0xFFFFFFFFu - uint32_t(packed[b] & 0xFFFFFFFFull));
+    if (tokens_out) tokens_out[b] = idx;
+    if (tokens_out64) tokens_out64[b] = idx;
+  }
+}
+
+__global__ void add_u64_kernel(unsigned long long* p, unsigned long long v) { *p += v; }
+
+const char* fill_u64(unsigned long long* p, int n, unsigned long long v, cudaStream_t s) {
+  if (n == 0) return nullptr;
+  fill_u64_kernel<<<(n + 255) / 256, 256, 0, s>>>(p, n, v);
+  return cudaGetLastError() == cudaSuccess ? nullptr : "fill_u64: launch failed";
+}
+
+const char* argmax_finalize(const unsigned long long* packed, int B, int* tok, long long* tok64,
+                            cudaStream_t s) {
+  argmax_finalize_kernel<<<1, 32, 0, s>>>(packed, B, tok, tok64);
+  return cudaGetLastError() == cudaSuccess ? nullptr : "argmax_finalize: launch failed";
+}
+
+const char* add_u64(unsigned long long* p, unsigned long long v, cudaStream_t s) {
+  add_u64_kernel<<<1, 1, 0, s>>>(p, v);
+  return cudaGetLastError() == cudaSuccess ? nullptr : "add_u64: launch failed";
+}
+
+}  // namespace dec
+}  // namespace hcp

@@ -1,0 +1,80 @@
+// Host interface of the decode-path kernels (GEMV, K2 cp decode attention + combine).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include "kv_layout.h"
+
+namespace hcp {
+namespace dec {
+
+enum GemvEpilogue : int {
+  kGemvF32 = 0,       // y_f32 = x W^T (+ bias)
+  kGemvResidual = 1,  // y_bf16 += bf16(x W^T)     (in place)
+  kGemvSwiGLU = 2,    // y_bf16[:, j] = silu(g_j) * u_j, W rows interleaved [128 gate | 128 up]
+  kGemvArgmax = 3,    // optional y_f32 logits + packed argmax per row into `argmax`
+};
+
+struct GemvArgs {
+  const __nv_bfloat16* x;  // [B, K]
+  long ldx;
+  const __nv_bfloat16* W;  // [N, K]
+  int B, N, K;
+  int epi;
+  const __nv_bfloat16* bias;
+  float* y_f32;
+  __nv_bfloat16* y_bf16;
+  long ldy;
+  unsigned long long* argmax;  // [B] packed (value, index); caller zeroes it
+  int num_sms;
+};
+
+struct DecodeAttnArgs {
+  const __nv_bfloat16* q;      // [B, H, D]
+  const __nv_bfloat16* arena;  // local paged KV arena
+  ArenaGeom geom;
+  int layer;
+  const int* page_tables;      // [B, pt_stride]
+  int pt_stride;
+  const int* n_tokens;         // [B] local KV rows per request (incl. the appended token)
+  int B, H, Hkv, D;
+  float scale;
+  int splits;
+  float* part_o;               // [B, H, splits, D] scratch
+  float* part_lse;             // [B, H, splits] scratch (log2 domain)
+  unsigned int* split_counter; // [B * Hkv] zero-initialised
+  unsigned int* grid_counter;  // [1] zero-initialised
+  // exchange: every rank's slot array (P2P mapped), own rank index, flags
+  float* const* xslot_ptrs;    // device array [n_ranks]
+  int n_ranks;
+  int my_rank;
+  unsigned long long* const* ready_ptrs;  // device array [n_ranks]: &dec_ready[my_rank] on rank r
+  const unsigned long long* epoch_parity_src;  // device step counter (may be null)
+  unsigned long long epoch_mul;  // epoch = (*src) * mul + add
+  unsigned long long epoch_add;
+  int* status;
+};
+
+struct DecodeCombineArgs {
+  const float* xslot;          // local exchange slots [2][N][B][H][D+1]
+  const unsigned long long* ready;  // local dec_ready[N] (null: no wait, single rank)
+  const unsigned long long* epoch_src;
+  unsigned long long epoch_mul;
+  unsigned long long epoch_add;
+  int n_ranks, B, H, D;
+  __nv_bfloat16* out;          // [B, H*D]
+  unsigned long long budget_ns;
+  int* status;
+};
+
+const char* gemv(const GemvArgs& a, cudaStream_t s);
+const char* decode_attn(const DecodeAttnArgs& a, cudaStream_t s);
+const char* decode_combine(const DecodeCombineArgs& a, cudaStream_t s);
+const char* fill_u64(unsigned long long* p, int n, unsigned long long v, cudaStream_t s);
+const char* argmax_finalize(const unsigned long long* packed, int B, int* tok, long long* tok64,
+                            cudaStream_t s);
+const char* add_u64(unsigned long long* p, unsigned long long v, cudaStream_t s);
+
+}  // namespace dec
+}  // namespace hcp

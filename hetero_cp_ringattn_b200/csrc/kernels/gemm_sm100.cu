@@ -1,0 +1,402 @@
+// K3/K6: persistent tcgen05 GEMM  C[M,N] = A[M,K] * B[N,K]^T  (bf16 in, fp32 accumulate in TMEM)
+// with fused epilogues: plain store, +bias (Qwen2 QKV), +residual (O-proj / down-proj, may run
+// in place on the residual stream), and SwiGLU (gate||up weight interleaved in 128-row blocks,
+// writes silu(gate) * up).
+//
+// Replaces the reference's cuBLAS GEMM call sites (rust/src/model/attention/ring.rs:1865-1876
+// QKV, :2022-2027 O-proj; rust/src/model/layers/mlp.rs:42-67 SwiGLU MLP; model.rs:310-333 LM
+// head), which the reference dispatches through libtorch.
+//
+// Design (sm_100a):
+//   * one CTA per SM (persistent), 128x256 output tile, BK = 64 (one 128-byte swizzle atom),
+//     4-stage TMA ring for A/B tiles (local memory only, no multicast);
+//   * warp 0: TMA producer; warp 1: single-thread tcgen05.mma issuer (M=128, N=256, K=16);
+//     warp 2: TMEM allocator; warps 4-7: epilogue (thread i owns accumulator row i);
+//   * two 256-column TMEM accumulators so the epilogue of tile i overlaps the mainloop of i+1;
+//   * every mbarrier wait is bounded and reports through the status word.
+#include <cudaTypedefs.h>
+
+#include "common.cuh"
+#include "gemm_sm100.h"
+
+namespace hcp {
+namespace gemm {
+
+using namespace hcp::dev;
+
+constexpr int BM = 128;
+constexpr int BN = 256;
+constexpr int BK = 64;
+constexpr int STAGES = 4;
+constexpr int A_STAGE = BM * BK * 2;  // 16 KB
+constexpr int B_STAGE = BN * BK * 2;  // 32 KB
+constexpr int TMEM_COLS = 512;
+constexpr int SMEM_BYTES = 1024 + STAGES * (A_STAGE + B_STAGE) + 256;
+
+struct Params {
+  int M, N, K;
+  int num_m_tiles, num_n_tiles;
+  __nv_bfloat16* C;
+  long ldc;
+  const __nv_bfloat16* bias;
+  const __nv_bfloat16* R;
+  long ldr;
+  int* status;
+};
+
+__device__ __forceinline__ void tile_coords(int tile, const Params& p, int& mb, int& nb) {
+  // n fastest: concurrently running CTAs share A tiles through L2 and sweep all of B.
+  mb = tile / p.num_n_tiles;
+  nb = tile % p.num_n_tiles;
+}
+
+template <int EPI>
+__device__ __forceinline__ void epilogue_tile(const Params& p, uint32_t tacc, int mb, int nb,
+                                              int row_in_tile) {
+  const int m = mb * BM + row_in_tile;
+  const bool row_ok = m < p.M;
+  uint32_t r[32];
+  if constexpr (EPI == kEpiSwiGLU) {
+    // tile columns [0,128) are gate rows, [128,256) the matching up rows
+    const int out_n0 = nb * (BN / 2);
+#pragma unroll 1
+    for (int c = 0; c < 4; ++c) {
+      uint32_t u[32];
+      tmem_ld32(tacc + c * 32, r);
+      tmem_ld32(tacc + 128 + c * 32, u);
+      tmem_wait_ld();
+      const int n0 = out_n0 + c * 32;
+      if (row_ok) {
+        __nv_bfloat16* dst = p.C + (long)m * p.ldc + n0;
+        uint32_t packed[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          float g0 = __uint_as_float(r[2 * i]), g1 = __uint_as_float(r[2 * i + 1]);
+          float u0 = __uint_as_float(u[2 * i]), u1 = __uint_as_float(u[2 * i + 1]);
+          // silu(g) = g / (1 + 2^(-g * log2 e)); the gate is rounded to bf16 first, as the
+          // reference's bf16 GEMM output would be
+          g0 = __bfloat162float(__float2bfloat16(g0));
+          g1 = __bfloat162float(__float2bfloat16(g1));
+          u0 = __bfloat162float(__float2bfloat16(u0));
+          u1 = __bfloat162float(__float2bfloat16(u1));
+          float s0 = g0 / (1.0f + fast_exp2(-g0 * 1.4426950408889634f));
+          float s1 = g1 / (1.0f + fast_exp2(-g1 * 1.4426950408889634f));
+          packed[i] = pack_bf16x2(s0 * u0, s1 * u1);
+        }
+        const int nout = (p.N / 2);
+        if (n0 + 32 <= nout) {
+          uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            d4[i] = make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2],
+                               packed[4 * i + 3]);
+        } else {
+          for (int i = 0; i < 32; ++i) {
+            if (n0 + i < nout) {
+              uint32_t w = packed[i / 2];
+              uint16_t h = (i & 1) ? uint16_t(w >> 16) : uint16_t(w & 0xffff);
+              reinterpret_cast<uint16_t*>(dst)[i] = h;
+            }
+          }
+        }
+      }
+    }
+  } else {
+    const int n_base = nb * BN;
+#pragma unroll 1
+    for (int c = 0; c < BN / 32; ++c) {
+      tmem_ld32(tacc + c * 32, r);
+      tmem_wait_ld();
+      const int n0 = n_base + c * 32;
+      if (!row_ok || n0 >= p.N) continue;
+      float v[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+      const bool full = (n0 + 32 <= p.N);
+      if constexpr (EPI == kEpiBias) {
+        if (full) {
+          const uint4* b4 = reinterpret_cast<const uint4*>(p.bias + n0);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            uint4 w = b4[i];
+            uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              v[8 * i + 2 * j] += bf16_lo(ww[j]);
+              v[8 * i + 2 * j + 1] += bf16_hi(ww[j]);
+            }
+          }
+        } else {
+          for (int i = 0; i < 32; ++i)
+            if (n0 + i < p.N) v[i] += __bfloat162float(p.bias[n0 + i]);
+        }
+      }
+      if constexpr (EPI == kEpiResidual) {
+        const __nv_bfloat16* rsrc = p.R + (long)m * p.ldr + n0;
+        if (full) {
+          const uint4* r4 = reinterpret_cast<const uint4*>(rsrc);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            uint4 w = r4[i];
+            uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              // round the GEMM result to bf16 before the add, like a bf16 GEMM + bf16 add
+              v[8 * i + 2 * j] = __bfloat162float(__float2bfloat16(v[8 * i + 2 * j])) +
+                                 bf16_lo(ww[j]);
+              v[8 * i + 2 * j + 1] =
+                  __bfloat162float(__float2bfloat16(v[8 * i + 2 * j + 1])) + bf16_hi(ww[j]);
+            }
+          }
+        } else {
+          for (int i = 0; i < 32; ++i)
+            if (n0 + i < p.N)
+              v[i] = __bfloat162float(__float2bfloat16(v[i])) + __bfloat162float(rsrc[i]);
+        }
+      }
+      __nv_bfloat16* dst = p.C + (long)m * p.ldc + n0;
+      if (full) {
+        uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          d4[i] = make_uint4(pack_bf16x2(v[8 * i], v[8 * i + 1]),
+                             pack_bf16x2(v[8 * i + 2], v[8 * i + 3]),
+                             pack_bf16x2(v[8 * i + 4], v[8 * i + 5]),
+                             pack_bf16x2(v[8 * i + 6], v[8 * i + 7]));
+      } else {
+        for (int i = 0; i < 32; ++i)
+          if (n0 + i < p.N) dst[i] = __float2bfloat16(v[i]);
+      }
+    }
+  }
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(256, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * A_STAGE;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + STAGES * B_STAGE);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + STAGES;
+  uint64_t* acc_full = bars + 2 * STAGES;
+  uint64_t* acc_empty = bars + 2 * STAGES + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 4);
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 4);
+    }
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 2) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int total_tiles = p.num_m_tiles * p.num_n_tiles;
+  const int k_iters = (p.K + BK - 1) / BK;
+
+  if (warp == 0) {
+    if (elect_one()) {
+      int it = 0;
+      for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x) {
+        int mb, nb;
+        tile_coords(tile, p, mb, nb);
+        bool ok = true;
+        for (int k = 0; k < k_iters; ++k, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          if (!mbar_wait(&empty[s], ph ^ 1, p.status, 101)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[s], A_STAGE + B_STAGE);
+          tma_load_2d(sA + s * A_STAGE, &tmA, &full[s], k * BK, mb * BM);
+          tma_load_2d(sB + s * B_STAGE, &tmB, &full[s], k * BK, nb * BN);
+        }
+        if (!ok) break;
+      }
+    }
+  } else if (warp == 1) {
+    if (elect_one()) {
+      constexpr uint32_t idesc = idesc_bf16_f32(BM, BN, false, false);
+      int it = 0;
+      int local = 0;
+      for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x, ++local) {
+        const int b = local & 1;
+        const uint32_t aph = (local >> 1) & 1;
+        if (!mbar_wait(&acc_empty[b], aph ^ 1, p.status, 102)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + uint32_t(b * BN);
+        bool ok = true;
+        for (int k = 0; k < k_iters; ++k, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          if (!mbar_wait(&full[s], ph, p.status, 103)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sA + s * A_STAGE);
+          const uint32_t b0 = smem_u32(sB + s * B_STAGE);
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            const uint64_t ad = sdesc_sw128(a0 + kk * 32, 16, 1024);
+            const uint64_t bd = sdesc_sw128(b0 + kk * 32, 16, 1024);
+            umma_bf16_ss(d_tmem, ad, bd, idesc, (k | kk) != 0 ? 1u : 0u);
+          }
+          umma_commit(&empty[s]);
+        }
+        if (!ok) break;
+        umma_commit(&acc_full[b]);
+      }
+    }
+  } else if (warp >= 4) {
+    const int q = warp - 4;
+    const int row_in_tile = q * 32 + lane;
+    int local = 0;
+    for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x, ++local) {
+      const int b = local & 1;
+      const uint32_t aph = (local >> 1) & 1;
+      if (!mbar_wait(&acc_full[b], aph, p.status, 104)) break;
+      tc_fence_after();
+      int mb, nb;
+      tile_coords(tile, p, mb, nb);
+      const uint32_t tacc = tmem_base + (uint32_t(q * 32) << 16) + uint32_t(b * BN);
+      epilogue_tile<EPI>(p, tacc, mb, nb, row_in_tile);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[b]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+// ----------------------------------------------------------------------------- host side
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (fn == nullptr) {
+    cudaDriverEntryPointQueryResult q;
+    void* ptr = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  }
+  return fn;
+}
+
+bool make_tma_2d_bf16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
+                      uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer) {
+  auto fn = encode_fn();
+  if (fn == nullptr) return false;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_stride_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims,
+                  strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+bool make_tma_3d_bf16(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uint64_t d2,
+                      uint64_t stride1_bytes, uint64_t stride2_bytes, uint32_t b0, uint32_t b1,
+                      uint32_t b2) {
+  auto fn = encode_fn();
+  if (fn == nullptr) return false;
+  cuuint64_t dims[3] = {d0, d1, d2};
+  cuuint64_t strides[2] = {stride1_bytes, stride2_bytes};
+  cuuint32_t box[3] = {b0, b1, b2};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims,
+                  strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+template <int EPI>
+static cudaError_t launch(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p,
+                          int grid, cudaStream_t stream) {
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(gemm_kernel<EPI>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    if (e != cudaSuccess) return e;
+    attr_set = true;
+  }
+  gemm_kernel<EPI><<<grid, 256, SMEM_BYTES, stream>>>(ta, tb, p);
+  return cudaGetLastError();
+}
+
+const char* gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
+  if (a.M <= 0 || a.N <= 0 || a.K <= 0) return "gemm: empty problem";
+  if ((a.lda * 2) % 16 || (a.ldb * 2) % 16) return "gemm: lda/ldb must be multiples of 8 elements";
+  if ((reinterpret_cast<uintptr_t>(a.A) | reinterpret_cast<uintptr_t>(a.B)) & 15)
+    return "gemm: A/B base must be 16-byte aligned";
+  if (a.epi == kEpiSwiGLU && (a.N % BN) != 0) return "gemm: SwiGLU needs N % 256 == 0";
+  if (a.epi != kEpiSwiGLU && ((a.ldc * 2) % 16 || (reinterpret_cast<uintptr_t>(a.C) & 15)))
+    return "gemm: C must be 16-byte aligned with ldc % 8 == 0";
+  if (a.epi == kEpiResidual && (a.R == nullptr || (a.ldr * 2) % 16 ||
+                                (reinterpret_cast<uintptr_t>(a.R) & 15)))
+    return "gemm: residual must be 16-byte aligned with ldr % 8 == 0";
+  if (a.epi == kEpiBias && a.bias == nullptr) return "gemm: bias missing";
+  CUtensorMap ta, tb;
+  if (!make_tma_2d_bf16(&ta, a.A, a.K, a.M, uint64_t(a.lda) * 2, BK, BM))
+    return "gemm: TMA descriptor for A failed";
+  if (!make_tma_2d_bf16(&tb, a.B, a.K, a.N, uint64_t(a.ldb) * 2, BK, BN))
+    return "gemm: TMA descriptor for B failed";
+  Params p;
+  p.M = a.M;
+  p.N = a.N;
+  p.K = a.K;
+  p.num_m_tiles = (a.M + BM - 1) / BM;
+  p.num_n_tiles = (a.N + BN - 1) / BN;
+  p.C = a.C;
+  p.ldc = a.ldc;
+  p.bias = a.bias;
+  p.R = a.R;
+  p.ldr = a.ldr;
+  p.status = a.status;
+  const int tiles = p.num_m_tiles * p.num_n_tiles;
+  const int grid = tiles < a.num_sms ? tiles : a.num_sms;
+  cudaError_t e;
+  switch (a.epi) {
+    case kEpiStore: e = launch<kEpiStore>(ta, tb, p, grid, stream); break;
+    case kEpiBias: e = launch<kEpiBias>(ta, tb, p, grid, stream); break;
+    case kEpiResidual: e = launch<kEpiResidual>(ta, tb, p, grid, stream); break;
+    case kEpiSwiGLU: e = launch<kEpiSwiGLU>(ta, tb, p, grid, stream); break;
+    default: return "gemm: unknown epilogue";
+  }
+  return e == cudaSuccess ? nullptr : cudaGetErrorString(e);
+}
+
+}  // namespace gemm
+}  // namespace hcp

@@ -1,0 +1,45 @@
+// Host interface of the sm_100a tcgen05 GEMM (K3/K6) and the TMA descriptor helpers.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace hcp {
+namespace gemm {
+
+enum Epilogue : int {
+  kEpiStore = 0,     // C = A B^T
+  kEpiBias = 1,      // C = A B^T + bias[n]
+  kEpiResidual = 2,  // C = bf16(A B^T) + R   (R may alias C)
+  kEpiSwiGLU = 3,    // C[:, j] = silu(G_j) * U_j with B rows interleaved [128 gate | 128 up]
+};
+
+struct GemmArgs {
+  const __nv_bfloat16* A;  // [M, K] row-major (K contiguous)
+  long lda;
+  const __nv_bfloat16* B;  // [N, K] row-major (nn.Linear weight layout)
+  long ldb;
+  __nv_bfloat16* C;        // [M, N] (SwiGLU: [M, N/2])
+  long ldc;
+  int M, N, K;
+  int epi;
+  const __nv_bfloat16* bias;
+  const __nv_bfloat16* R;
+  long ldr;
+  int* status;             // device status words (may be null)
+  int num_sms;
+};
+
+// Returns nullptr on success, otherwise a static error string.
+const char* gemm_bf16(const GemmArgs& args, cudaStream_t stream);
+
+bool make_tma_2d_bf16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
+                      uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer);
+bool make_tma_3d_bf16(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uint64_t d2,
+                      uint64_t stride1_bytes, uint64_t stride2_bytes, uint32_t b0, uint32_t b1,
+                      uint32_t b2);
+
+}  // namespace gemm
+}  // namespace hcp

@@ -1,0 +1,516 @@
+"""Llama / Qwen2 context-parallel inference engine: one instance per rank (one process per GPU).
+
+Parity (reference call stacks):
+  * prefill: rust/src/model/model.rs:195-343 (`LlamaModel::forward`), layers/mod.rs:59-90,
+    attention/ring.rs:1841-2028 (QKV -> RoPE -> KV cache update -> ring attention -> O proj),
+    worker_sdk/tch_backend.rs:126-236 (`do_prefill`, last-token logits on the rank holding the
+    final position);
+  * decode: the Q-ring / self-driving routes (ring.rs:682-818, self_driving.rs:333-675,
+    tch_backend.rs:634-904) with KV growth placed by `FrozenKvAssigneeSchedule`
+    (self_driving.rs:12-120); here every rank computes the token's layer in parallel, attends
+    over its own shard and combines (O, LSE) with the other ranks inside the decode kernels;
+  * release: tch_backend.rs:1077 (`release_request`).
+
+Hot path (CUDA): embedding, RMSNorm, tcgen05 GEMMs with fused bias / residual / SwiGLU epilogues,
+the runtime's fused RoPE + KV write + NVLink push and ring attention (prefill), weight-streaming
+GEMVs, KV append, split-KV attention with the in-kernel cross-rank (O, LSE) exchange, and the
+LM-head GEMV with a fused argmax (decode). The decode step is captured in a CUDA graph.
+
+Host path (CPU tensors, gloo process group): the same algorithm with the plain PyTorch oracles
+and torch.distributed all-gathers standing in for the NVLink exchange. It exists for CPU-rank
+tests of the distributed logic; it is never used when the engine runs on a GPU.
+"""
+
+from __future__ import annotations
+
+import dataclasses
+import math
+import time
+from typing import Dict, List, Optional, Sequence
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+from ..config import EnvConfig, ModelConfig
+from ..errors import CapacityError, RingError
+from ..kv.arena import KvArenaManager, RequestKv
+from ..ops import kernels as K
+from ..ops import reference as ref
+from ..ops._ext import native
+from ..parallel.schedule import FrozenKvAssigneeSchedule
+from ..parallel.strategy import RingStrategy, build_assignment, build_domain_positions
+from ..utils.perf import PerfLog
+from .weights import PreparedWeights
+
+
+@dataclasses.dataclass
+class RequestState:
+    req_id: int
+    prompt_len: int
+    chunks: list
+    strategy: RingStrategy
+    positions: np.ndarray            # this rank's prompt positions (local order)
+    owner_of_last: int
+    horizon: int
+    assignee: np.ndarray             # [horizon, layers] rank storing (token, layer) KV
+    decode_offset: int = 0
+    context_len: int = 0             # tokens with KV (prompt + decoded)
+    kv: Optional[RequestKv] = None
+    host_kv: Optional[list] = None   # CPU path: per layer (k [n,Hkv,D], v, pos [n])
+    keep_kv: bool = False
+
+
+class LlamaCPEngine:
+    def __init__(self, cfg: ModelConfig, weights: PreparedWeights, *, rank: int = 0,
+                 world: int = 1, device: Optional[torch.device] = None,
+                 group: Optional["dist.ProcessGroup"] = None, max_context: int = 8192,
+                 max_batch: int = 8, page_size: int = 256, kv_pages: Optional[int] = None,
+                 decode_reserve: int = 512, env: Optional[EnvConfig] = None,
+                 use_graphs: bool = True, perf_log: Optional[PerfLog] = None):
+        cfg.validate()
+        self.cfg = cfg
+        self.w = weights
+        self.rank = rank
+        self.world = world
+        self.group = group
+        self.env = env or EnvConfig.from_env()
+        self.device = device or weights.embed.device
+        self.cuda = self.device.type == "cuda"
+        self.max_context = int(max_context)
+        self.max_batch = int(max_batch)
+        self.page_size = int(page_size)
+        self.H, self.Hkv, self.D = cfg.num_heads, cfg.kv_heads, cfg.head_dim
+        self.L = cfg.num_layers
+        self.scale = 1.0 / math.sqrt(self.D)
+        self.use_graphs = use_graphs and self.cuda
+        self.perf = perf_log or PerfLog.from_env(self.env)
+        if kv_pages is None:
+            kv_pages = -(-self.max_context // self.page_size) + \
+                max_batch * -(-decode_reserve // self.page_size) + 2
+        self.kv = KvArenaManager(kv_pages, self.page_size, self.L)
+        max_pos = self.max_context + max(decode_reserve, 1) + 8
+        cos, sin = ref.rope_cos_sin(torch.arange(max_pos, device=self.device), self.D, cfg.rope_theta)
+        self.cos, self.sin = cos.contiguous(), sin.contiguous()
+        self.reqs: Dict[int, RequestState] = {}
+        self.prefill_epoch = 0
+        self.rt = None
+        if self.cuda:
+            self.rt = native().Runtime(rank, world, self.device.index or 0, self.L, kv_pages,
+                                       self.page_size, self.Hkv, self.D, self.H,
+                                       self.max_context, self.max_batch,
+                                       self.env.p2p_spin_budget_ms)
+            if world > 1:
+                handles = [None] * world
+                dist.all_gather_object(handles, self.rt.export_handle(), group=group)
+                self.rt.open_peers(handles)
+                dist.barrier(group=group)
+            self.dec_step = torch.zeros(1, dtype=torch.int64, device=self.device)
+            self._graphs: Dict[int, "DecodeGraph"] = {}
+            self.num_sms = native().num_sms(self.device.index or 0)
+
+    # ------------------------------------------------------------------ helpers
+    def close(self) -> None:
+        self._graphs = {} if self.cuda else None
+        if self.rt is not None:
+            if self.world > 1 and dist.is_initialized():
+                dist.barrier(group=self.group)
+            self.rt.shutdown()
+            self.rt = None
+
+    def check_device(self) -> None:
+        if self.rt is not None:
+            self.rt.check()
+
+    def layout(self, chunks: Sequence[int], strategy) -> tuple:
+        assignment = build_assignment(chunks, strategy)
+        positions = build_domain_positions(assignment, len(chunks))
+        return assignment, positions
+
+    def _schedule(self, req_id: int, tickets: Sequence[int], horizon: int) -> np.ndarray:
+        if horizon <= 0:
+            return np.zeros((0, self.L), dtype=np.int64)
+        sched = FrozenKvAssigneeSchedule(tickets, req_id, horizon * self.L)
+        seq = np.asarray(sched.sequence, dtype=np.int64)
+        ordinals = (sched.phase + np.arange(horizon * self.L)) % len(seq)
+        return seq[ordinals].reshape(horizon, self.L)
+
+    # ------------------------------------------------------------------ prefill
+    @torch.no_grad()
+    def prefill(self, req_id: int, prompt_ids: torch.Tensor, chunks: Sequence[int],
+                strategy="vanilla", decode_horizon: int = 128,
+                tickets: Optional[Sequence[int]] = None, return_logits: bool = False,
+                keep_kv: bool = False):
+        """SPMD prefill of one request. Every rank passes the same full prompt and chunk split.
+
+        Returns (first_token: int64 device tensor [1], logits or None). The first token is
+        broadcast from the rank holding the last prompt position."""
+        strategy = RingStrategy.parse(strategy)
+        chunks = [int(c) for c in chunks]
+        if len(chunks) != self.world:
+            raise RingError(f"{len(chunks)} chunks for {self.world} ranks")
+        Lp = sum(chunks)
+        if Lp + decode_horizon > self.cos.shape[0] or Lp > self.max_context:
+            raise CapacityError(f"prompt {Lp} (+{decode_horizon}) exceeds the engine's context "
+                                f"capacity {self.max_context}")
+        if self.cfg.max_position_embeddings and Lp + decode_horizon > self.cfg.max_position_embeddings:
+            raise CapacityError(f"prompt {Lp} + {decode_horizon} exceeds max_position_embeddings "
+                                f"{self.cfg.max_position_embeddings}")
+        if req_id in self.reqs:
+            raise RingError(f"request {req_id} already active on rank {self.rank}")
+        assignment, positions = self.layout(chunks, strategy)
+        my_pos = positions[self.rank]
+        T = len(my_pos)
+        tickets = list(tickets) if tickets is not None else list(chunks)
+        assignee = self._schedule(req_id, tickets, decode_horizon)
+        growth = int((assignee == self.rank).sum(0).max()) if decode_horizon else 0
+        st = RequestState(req_id=req_id, prompt_len=Lp, chunks=chunks, strategy=strategy,
+                          positions=my_pos, owner_of_last=int(assignment[Lp - 1]),
+                          horizon=decode_horizon, assignee=assignee, context_len=Lp,
+                          keep_kv=keep_kv)
+        t0 = time.perf_counter()
+        if self.cuda:
+            st.kv = self.kv.reserve(req_id, T, T + growth, my_pos)
+            st.kv.pt_device = torch.tensor(st.kv.pages, dtype=torch.int32, device=self.device)
+            ids_local = prompt_ids.to(self.device, non_blocking=True)[torch.from_numpy(my_pos).to(self.device)]
+            tok, logits = self._prefill_cuda(st, ids_local.int(), Lp, return_logits)
+        else:
+            ids_local = prompt_ids[torch.from_numpy(my_pos)]
+            tok, logits = self._prefill_host(st, ids_local, Lp, return_logits)
+        self.reqs[req_id] = st
+        if self.perf.enabled:
+            self.perf.emit("prefill", rank=self.rank, request=req_id, tokens=T, prompt=Lp,
+                           host_ms=(time.perf_counter() - t0) * 1e3, world=self.world)
+        return tok, logits
+
+    def _prefill_cuda(self, st: RequestState, ids: torch.Tensor, Lp: int, return_logits: bool):
+        w, dev = self.w, self.device
+        T = ids.numel()
+        pos = torch.from_numpy(st.positions.astype(np.int32)).to(dev, non_blocking=True)
+        x = K.embedding(ids, w.embed)
+        xn = torch.empty_like(x)
+        q_buf = torch.empty(T, self.H, self.D, dtype=torch.bfloat16, device=dev)
+        o_buf = torch.empty_like(q_buf)
+        start_tile = int(st.positions[0]) // 128 if st.strategy is RingStrategy.VANILLA else 0
+        for li, lw in enumerate(w.layers):
+            K.rmsnorm(x, lw.in_norm, self.cfg.rms_norm_eps, out=xn)
+            qkv = K.gemm(xn, lw.wqkv, "bias" if lw.bqkv is not None else "store", bias=lw.bqkv)
+            self.prefill_epoch += 1
+            args = (qkv, pos, self.cos, self.sin, li, st.kv.pt_device, 0, Lp, start_tile,
+                    self.scale, True, q_buf, o_buf, None, self.prefill_epoch)
+            self.rt.push_layer(*args)
+            self.rt.attend_layer(*args)
+            del qkv
+            K.gemm(o_buf.view(T, self.H * self.D), lw.wo, "residual", residual=x)
+            K.rmsnorm(x, lw.post_norm, self.cfg.rms_norm_eps, out=xn)
+            g = K.gemm(xn, lw.wgu, "swiglu")
+            K.gemm(g, lw.wd, "residual", residual=x)
+            del g
+        return self._first_token_cuda(st, x, return_logits)
+
+    def _first_token_cuda(self, st: RequestState, x: torch.Tensor, return_logits: bool):
+        dev = self.device
+        tok = torch.zeros(1, dtype=torch.int64, device=dev)
+        logits = None
+        if self.rank == st.owner_of_last:
+            row = int(np.nonzero(st.positions == st.prompt_len - 1)[0][0])
+            xl = torch.empty(1, self.cfg.hidden_size, dtype=torch.bfloat16, device=dev)
+            K.rmsnorm(x[row:row + 1], self.w.final_norm, self.cfg.rms_norm_eps, out=xl)
+            am = torch.zeros(1, dtype=torch.int64, device=dev)
+            logits = torch.empty(1, self.cfg.vocab_size, dtype=torch.float32, device=dev)
+            K.gemv(xl, self.w.lm_head, "argmax", y_f32=logits, argmax=am)
+            native().argmax_finalize(am, None, tok)
+        if self.world > 1:
+            dist.broadcast(tok, src=st.owner_of_last, group=self.group)
+            if return_logits:
+                if logits is None:
+                    logits = torch.empty(1, self.cfg.vocab_size, dtype=torch.float32, device=dev)
+                dist.broadcast(logits, src=st.owner_of_last, group=self.group)
+        return tok, (logits[0] if (return_logits and logits is not None) else None)
+
+    # ------------------------------------------------------------------ host (CPU) prefill
+    def _gather_rows(self, t: torch.Tensor) -> List[torch.Tensor]:
+        if self.world == 1:
+            return [t]
+        n = torch.tensor([t.shape[0]], dtype=torch.int64)
+        sizes = [torch.zeros_like(n) for _ in range(self.world)]
+        dist.all_gather(sizes, n, group=self.group)
+        mx = int(max(int(s) for s in sizes))
+        pad = torch.zeros((mx,) + tuple(t.shape[1:]), dtype=t.dtype)
+        pad[: t.shape[0]] = t
+        bufs = [torch.zeros_like(pad) for _ in range(self.world)]
+        dist.all_gather(bufs, pad, group=self.group)
+        return [b[: int(s)] for b, s in zip(bufs, sizes)]
+
+    def _prefill_host(self, st: RequestState, ids: torch.Tensor, Lp: int, return_logits: bool):
+        w, cfg = self.w, self.cfg
+        T = ids.numel()
+        pos = torch.from_numpy(st.positions)
+        x = w.embed[ids.long()].float()
+        st.host_kv = []
+        for li, lw in enumerate(w.layers):
+            h = ref.rmsnorm(x, lw.in_norm, cfg.rms_norm_eps)
+            qkv = ref.linear(h, lw.wqkv, lw.bqkv)
+            q = ref.apply_rope(qkv[:, : self.H * self.D].view(T, self.H, self.D), pos, cfg.rope_theta)
+            k = ref.apply_rope(qkv[:, self.H * self.D:(self.H + self.Hkv) * self.D].view(T, self.Hkv, self.D),
+                               pos, cfg.rope_theta)
+            v = qkv[:, (self.H + self.Hkv) * self.D:].reshape(T, self.Hkv, self.D)
+            st.host_kv.append([k.clone(), v.clone(), pos.clone()])
+            ks = self._gather_rows(k)
+            vs = self._gather_rows(v)
+            ps = self._gather_rows(pos)
+            kk = torch.zeros(Lp, self.Hkv, self.D, dtype=k.dtype)
+            vv = torch.zeros_like(kk)
+            for a, b, p in zip(ks, vs, ps):
+                kk[p] = a
+                vv[p] = b
+            o, _ = ref.full_attention(q, kk, vv, pos, torch.arange(Lp), causal=True)
+            x = x + ref.linear(o.reshape(T, self.H * self.D), lw.wo)
+            h = ref.rmsnorm(x, lw.post_norm, cfg.rms_norm_eps)
+            x = x + ref.linear(K.swiglu_from_interleaved(ref.linear(h, lw.wgu)), lw.wd)
+        tok = torch.zeros(1, dtype=torch.int64)
+        logits = torch.zeros(cfg.vocab_size, dtype=torch.float32)
+        if self.rank == st.owner_of_last:
+            row = int(np.nonzero(st.positions == Lp - 1)[0][0])
+            xl = ref.rmsnorm(x[row:row + 1], w.final_norm, cfg.rms_norm_eps)
+            logits = ref.linear(xl, w.lm_head)[0].float()
+            tok[0] = int(torch.argmax(logits))
+        if self.world > 1:
+            dist.broadcast(tok, src=st.owner_of_last, group=self.group)
+            dist.broadcast(logits, src=st.owner_of_last, group=self.group)
+        return tok, (logits if return_logits else None)
+
+    # ------------------------------------------------------------------ decode
+    def _decode_meta(self, req_ids: Sequence[int]):
+        """Per-step host metadata: positions, KV owner/slot per (row, layer), local KV lengths."""
+        B = len(req_ids)
+        pos = np.zeros(B, dtype=np.int32)
+        owner = np.zeros((B, self.L), dtype=np.int32)
+        slot = np.zeros((B, self.L), dtype=np.int32)
+        ntok = np.zeros((self.L, B), dtype=np.int32)
+        for b, rid in enumerate(req_ids):
+            st = self.reqs[rid]
+            t = st.decode_offset
+            if t >= st.horizon:
+                raise CapacityError(f"request {rid} exhausted its decode horizon {st.horizon}")
+            pos[b] = st.context_len
+            own = (st.assignee[t] == self.rank)
+            if self.cuda:
+                counts = st.kv.layer_counts
+                for li in np.nonzero(own)[0]:
+                    st.kv.check_room(int(li))
+                owner[b] = own
+                slot[b] = counts
+                ntok[:, b] = counts + own
+            else:
+                owner[b] = own
+        return pos, owner, slot, ntok
+
+    def _advance(self, req_ids: Sequence[int], owner: np.ndarray, pos: np.ndarray) -> None:
+        for b, rid in enumerate(req_ids):
+            st = self.reqs[rid]
+            if self.cuda:
+                for li in np.nonzero(owner[b])[0]:
+                    st.kv.slot_pos[li, st.kv.layer_counts[li]] = pos[b]
+                st.kv.layer_counts += owner[b]
+            st.decode_offset += 1
+            st.context_len += 1
+
+    @torch.no_grad()
+    def decode_step(self, req_ids: Sequence[int], tokens: torch.Tensor) -> torch.Tensor:
+        """One greedy decode step for a batch of requests. `tokens` [B] holds each row's last
+        token (int64 or int32, on the engine device). Returns the next tokens [B] (int64)."""
+        B = len(req_ids)
+        if B == 0:
+            return tokens
+        pos, owner, slot, ntok = self._decode_meta(req_ids)
+        if self.cuda:
+            out = self._decode_cuda(req_ids, tokens, pos, owner, slot, ntok)
+        else:
+            out = self._decode_host(req_ids, tokens, pos, owner)
+        self._advance(req_ids, owner, pos)
+        return out
+
+    def _graph_for(self, B: int) -> "DecodeGraph":
+        g = self._graphs.get(B)
+        if g is None:
+            g = DecodeGraph(self, B)
+            self._graphs[B] = g
+        return g
+
+    def _decode_cuda(self, req_ids, tokens, pos, owner, slot, ntok):
+        B = len(req_ids)
+        bucket = 1 if B == 1 else 2 if B == 2 else 4 if B <= 4 else 8
+        if B > self.max_batch or bucket > self.max_batch:
+            raise CapacityError(f"decode batch {B} exceeds max_batch {self.max_batch}")
+        g = self._graph_for(bucket)
+        return g.run(req_ids, tokens, pos, owner, slot, ntok)
+
+    def _decode_host(self, req_ids, tokens, pos, owner):
+        w, cfg = self.w, self.cfg
+        B = len(req_ids)
+        x = w.embed[tokens.long().view(-1)].float()
+        posn = torch.from_numpy(pos.astype(np.int64))
+        for li, lw in enumerate(w.layers):
+            h = ref.rmsnorm(x, lw.in_norm, cfg.rms_norm_eps)
+            qkv = ref.linear(h, lw.wqkv, lw.bqkv)
+            q = ref.apply_rope(qkv[:, : self.H * self.D].view(B, self.H, self.D), posn, cfg.rope_theta)
+            k = ref.apply_rope(qkv[:, self.H * self.D:(self.H + self.Hkv) * self.D].view(B, self.Hkv, self.D),
+                               posn, cfg.rope_theta)
+            v = qkv[:, (self.H + self.Hkv) * self.D:].reshape(B, self.Hkv, self.D)
+            outs = []
+            for b, rid in enumerate(req_ids):
+                st = self.reqs[rid]
+                kv = st.host_kv[li]
+                if owner[b, li]:
+                    kv[0] = torch.cat([kv[0], k[b:b + 1]])
+                    kv[1] = torch.cat([kv[1], v[b:b + 1]])
+                    kv[2] = torch.cat([kv[2], posn[b:b + 1]])
+                if kv[0].shape[0]:
+                    o, lse = ref.full_attention(q[b:b + 1], kv[0], kv[1], causal=False)
+                else:
+                    o = torch.zeros(1, self.H, self.D)
+                    lse = torch.full((self.H, 1), float("-inf"))
+                os_ = self._gather_rows(o)
+                ls_ = self._gather_rows(lse.transpose(0, 1).contiguous())
+                om, _ = ref.merge_partials(os_, [l.transpose(0, 1) for l in ls_])
+                outs.append(om)
+            o = torch.cat(outs)
+            x = x + ref.linear(o.reshape(B, self.H * self.D), lw.wo)
+            h = ref.rmsnorm(x, lw.post_norm, cfg.rms_norm_eps)
+            x = x + ref.linear(K.swiglu_from_interleaved(ref.linear(h, lw.wgu)), lw.wd)
+        xl = ref.rmsnorm(x, w.final_norm, cfg.rms_norm_eps)
+        logits = ref.linear(xl, w.lm_head)
+        return torch.argmax(logits, dim=-1)
+
+    # ------------------------------------------------------------------ release / generate
+    def release(self, req_id: int) -> bool:
+        st = self.reqs.pop(req_id, None)
+        if st is None:
+            return False
+        if self.cuda:
+            self.kv.release(req_id)
+        return True
+
+    @torch.no_grad()
+    def generate(self, req_id: int, prompt_ids: torch.Tensor, max_new_tokens: int,
+                 chunks: Sequence[int], strategy="vanilla", tickets=None,
+                 stop_ids: Optional[Sequence[int]] = None) -> torch.Tensor:
+        """Greedy generation (SPMD across ranks). Returns the generated ids [n] on the device.
+
+        The decode loop never reads tokens back to the host unless `stop_ids` is given."""
+        first, _ = self.prefill(req_id, prompt_ids, chunks, strategy, decode_horizon=max(1, max_new_tokens),
+                                tickets=tickets)
+        toks = [first.view(1)]
+        cur = first.view(1)
+        try:
+            for _ in range(max_new_tokens - 1):
+                cur = self.decode_step([req_id], cur).view(1)
+                toks.append(cur)
+                if stop_ids is not None and int(cur) in stop_ids:
+                    break
+        finally:
+            self.release(req_id)
+        return torch.cat(toks)
+
+
+class DecodeGraph:
+    """Static buffers + a captured CUDA graph for one decode batch size."""
+
+    def __init__(self, eng: LlamaCPEngine, B: int):
+        self.e = eng
+        self.B = B
+        dev = eng.device
+        cfg = eng.cfg
+        L = eng.L
+        self.max_pages = eng.kv.alloc.num_pages
+        self.tokens = torch.zeros(B, dtype=torch.int32, device=dev)
+        self.out_tok = torch.zeros(B, dtype=torch.int64, device=dev)
+        self.pos = torch.zeros(B, dtype=torch.int32, device=dev)
+        self.owner = torch.zeros(B, L, dtype=torch.int32, device=dev)
+        self.slot = torch.zeros(B, L, dtype=torch.int32, device=dev)
+        self.ntok = torch.zeros(L, B, dtype=torch.int32, device=dev)
+        self.pt = torch.zeros(B, self.max_pages, dtype=torch.int32, device=dev)
+        pin = dict(pin_memory=True)
+        self.h_pos = torch.zeros(B, dtype=torch.int32, **pin)
+        self.h_owner = torch.zeros(B, L, dtype=torch.int32, **pin)
+        self.h_slot = torch.zeros(B, L, dtype=torch.int32, **pin)
+        self.h_ntok = torch.zeros(L, B, dtype=torch.int32, **pin)
+        self.h_pt = torch.zeros(B, self.max_pages, dtype=torch.int32, **pin)
+        self.x = torch.zeros(B, cfg.hidden_size, dtype=torch.bfloat16, device=dev)
+        self.xn = torch.zeros_like(self.x)
+        self.qkv = torch.zeros(B, cfg.qkv_size, dtype=torch.float32, device=dev)
+        self.q = torch.zeros(B, eng.H, eng.D, dtype=torch.bfloat16, device=dev)
+        self.o = torch.zeros(B, eng.H * eng.D, dtype=torch.bfloat16, device=dev)
+        self.g = torch.zeros(B, eng.w.intermediate_padded, dtype=torch.bfloat16, device=dev)
+        self.logits = torch.zeros(B, cfg.vocab_size, dtype=torch.float32, device=dev)
+        self.am = torch.zeros(B, dtype=torch.int64, device=dev)
+        self.splits = max(1, min(64, -(-2 * eng.num_sms // (B * eng.Hkv))))
+        self.part_o = torch.zeros(B * eng.H * self.splits * eng.D, dtype=torch.float32, device=dev)
+        self.part_l = torch.zeros(B * eng.H * self.splits, dtype=torch.float32, device=dev)
+        self.counters = torch.zeros(B * eng.Hkv + 1, dtype=torch.int32, device=dev)
+        self.graph = None
+        self.copied = None
+
+    def body(self) -> None:
+        e, w, cfg = self.e, self.e.w, self.e.cfg
+        rt = e.rt
+        nat = native()
+        nat.add_u64(e.dec_step, 1)
+        K.embedding(self.tokens, w.embed, out=self.x)
+        for li, lw in enumerate(w.layers):
+            K.rmsnorm(self.x, lw.in_norm, cfg.rms_norm_eps, out=self.xn)
+            K.gemv(self.xn, lw.wqkv, "f32", bias=lw.bqkv, y_f32=self.qkv)
+            rt.qkv_decode(self.qkv, self.pos, e.cos, e.sin, li, self.pt, self.owner, self.slot, self.q)
+            rt.decode_attn(self.q, li, self.pt, self.ntok[li], e.scale, self.splits, self.part_o,
+                           self.part_l, self.counters, e.dec_step, e.L, li + 1)
+            rt.decode_combine(self.o, self.B, e.H, e.dec_step, e.L, li + 1)
+            K.gemv(self.o, lw.wo, "residual", y_bf16=self.x)
+            K.rmsnorm(self.x, lw.post_norm, cfg.rms_norm_eps, out=self.xn)
+            K.gemv(self.xn, lw.wgu, "swiglu", y_bf16=self.g)
+            K.gemv(self.g, lw.wd, "residual", y_bf16=self.x)
+        K.rmsnorm(self.x, w.final_norm, cfg.rms_norm_eps, out=self.xn)
+        nat.fill_u64(self.am, 0)
+        K.gemv(self.xn, w.lm_head, "argmax", y_f32=self.logits, argmax=self.am)
+        nat.argmax_finalize(self.am, self.tokens, self.out_tok)
+
+    def run(self, req_ids, tokens, pos, owner, slot, ntok) -> torch.Tensor:
+        n = len(req_ids)
+        # the pinned host buffers are reused every step: wait until the previous step's
+        # host-to-device copies have executed before overwriting them
+        if self.copied is not None:
+            self.copied.synchronize()
+        self.h_pos.zero_()
+        self.h_owner.zero_()
+        self.h_slot.zero_()
+        self.h_ntok.zero_()
+        self.h_pos[:n] = torch.from_numpy(pos)
+        self.h_owner[:n] = torch.from_numpy(owner)
+        self.h_slot[:n] = torch.from_numpy(slot)
+        self.h_ntok[:, :n] = torch.from_numpy(ntok)
+        for b, rid in enumerate(req_ids):
+            pages = self.e.reqs[rid].kv.pages
+            self.h_pt[b, : len(pages)] = torch.tensor(pages, dtype=torch.int32)
+        self.pos.copy_(self.h_pos, non_blocking=True)
+        self.owner.copy_(self.h_owner, non_blocking=True)
+        self.slot.copy_(self.h_slot, non_blocking=True)
+        self.ntok.copy_(self.h_ntok, non_blocking=True)
+        self.pt.copy_(self.h_pt, non_blocking=True)
+        if self.copied is None:
+            self.copied = torch.cuda.Event()
+        self.copied.record()
+        if n < self.B:
+            self.tokens.zero_()
+        self.tokens[:n].copy_(tokens.view(-1)[:n].to(torch.int32))
+        if not self.e.use_graphs:
+            self.body()
+        else:
+            if self.graph is None:
+                # every kernel of the body writes into preallocated buffers and sets no function
+                # attributes, so the graph is captured directly (no eager warm-up step, which
+                # would advance the cross-rank exchange epochs and overwrite `tokens`)
+                self.graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(self.graph):
+                    self.body()
+            self.graph.replay()
+        return self.out_tok[:n].clone()

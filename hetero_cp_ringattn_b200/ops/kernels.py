@@ -1,0 +1,146 @@
+"""Python front-ends of the sm_100a kernels.
+
+CUDA tensors always go to the native kernels (the extension must be present: see `_ext.native`);
+CPU tensors use the plain PyTorch oracles in `reference.py`, which is what the CPU-rank tests run.
+"""
+
+from __future__ import annotations
+
+import math
+from typing import Optional
+
+import torch
+
+from . import reference as ref
+from ._ext import native
+
+EPI = {"store": 0, "bias": 1, "residual": 2, "swiglu": 3}
+GEMV = {"f32": 0, "residual": 1, "swiglu": 2, "argmax": 3}
+SWIGLU_BLOCK = 128  # gate/up rows are interleaved in blocks of 128
+
+
+# --------------------------------------------------------------------------- weight layouts
+def interleave_gate_up(gate: torch.Tensor, up: torch.Tensor, block: int = SWIGLU_BLOCK) -> torch.Tensor:
+    """[I, K] gate and up -> [2 * I_pad, K] with rows [g0..g127, u0..u127, g128.., u128.., ...].
+
+    I is zero-padded to a multiple of `block` (silu(0) * 0 = 0, and the down projection gets
+    matching zero columns via `pad_down_proj`)."""
+    i, k = gate.shape
+    ip = -(-i // block) * block
+    if ip != i:
+        gate = torch.cat([gate, gate.new_zeros(ip - i, k)])
+        up = torch.cat([up, up.new_zeros(ip - i, k)])
+    g = gate.view(ip // block, block, k)
+    u = up.view(ip // block, block, k)
+    return torch.stack([g, u], dim=1).reshape(2 * ip, k).contiguous()
+
+
+def pad_down_proj(down: torch.Tensor, block: int = SWIGLU_BLOCK) -> torch.Tensor:
+    n, i = down.shape
+    ip = -(-i // block) * block
+    if ip == i:
+        return down.contiguous()
+    return torch.cat([down, down.new_zeros(n, ip - i)], dim=1).contiguous()
+
+
+def swiglu_from_interleaved(y: torch.Tensor, block: int = SWIGLU_BLOCK) -> torch.Tensor:
+    """CPU helper: split an interleaved gate||up projection and apply SwiGLU."""
+    t, n2 = y.shape
+    v = y.view(t, n2 // (2 * block), 2, block)
+    return ref.swiglu(v[:, :, 0].reshape(t, -1), v[:, :, 1].reshape(t, -1))
+
+
+# --------------------------------------------------------------------------- GEMM
+def gemm(a: torch.Tensor, w: torch.Tensor, epi: str = "store", bias: Optional[torch.Tensor] = None,
+         residual: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
+         status: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """out = a @ w.T with a fused epilogue (`store`, `bias`, `residual`, `swiglu`)."""
+    m, n = a.shape[0], w.shape[0]
+    n_out = n // 2 if epi == "swiglu" else n
+    if not a.is_cuda:
+        y = a.float() @ w.float().t()
+        if epi == "bias":
+            y = y + bias.float()
+        if epi == "residual":
+            y = y.to(a.dtype).float() + residual.float()
+        if epi == "swiglu":
+            return swiglu_from_interleaved(y.to(a.dtype))
+        y = y.to(a.dtype)
+        if out is not None:
+            out.copy_(y)
+            return out
+        return y
+    if out is None:
+        out = residual if (epi == "residual" and residual is not None) else torch.empty(
+            m, n_out, dtype=a.dtype, device=a.device)
+    native().gemm(a, w, out, EPI[epi], bias, residual, status)
+    return out
+
+
+# --------------------------------------------------------------------------- attention
+def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, q_pos: torch.Tensor, L: int,
+              causal: bool = True, scale: Optional[float] = None, kv_start_tile: int = 0,
+              want_lse: bool = True, status: Optional[torch.Tensor] = None):
+    """Flash attention of q [T,H,D] over position-ordered k/v [Hkv, Lcap, D] (rows 0..L-1).
+
+    Returns (o [T,H,D], lse [H,T] natural log or None)."""
+    t, h, d = q.shape
+    scale = scale if scale is not None else 1.0 / math.sqrt(d)
+    if not q.is_cuda:
+        kk = k[:, :L].transpose(0, 1)
+        vv = v[:, :L].transpose(0, 1)
+        o, lse = ref.full_attention(q.float(), kk.float(), vv.float(), q_pos.long(),
+                                    torch.arange(L), causal=causal, scale=scale)
+        return o.to(q.dtype), (lse if want_lse else None)
+    o = torch.empty_like(q)
+    lse = torch.empty(h, t, dtype=torch.float32, device=q.device) if want_lse else None
+    native().attn_fwd(q, k, v, o, lse, q_pos, L, k.stride(0), scale, causal, kv_start_tile, status)
+    return o, lse
+
+
+# --------------------------------------------------------------------------- norm / embedding
+def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float, out: Optional[torch.Tensor] = None):
+    if not x.is_cuda:
+        y = ref.rmsnorm(x, w, eps)
+        if out is not None:
+            out.copy_(y)
+            return out
+        return y
+    if out is None:
+        out = torch.empty_like(x)
+    native().rmsnorm(x, w, out, eps)
+    return out
+
+
+def embedding(ids: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = None,
+              status: Optional[torch.Tensor] = None):
+    if not w.is_cuda:
+        return w[ids.long()]
+    if out is None:
+        out = torch.empty(ids.numel(), w.shape[1], dtype=w.dtype, device=w.device)
+    native().embedding(ids, w, out, status)
+    return out
+
+
+# --------------------------------------------------------------------------- GEMV (decode)
+def gemv(x: torch.Tensor, w: torch.Tensor, epi: str, bias=None, y_f32=None, y_bf16=None,
+         argmax=None):
+    if not x.is_cuda:
+        y = x.float() @ w.float().t()
+        if epi == "f32":
+            if bias is not None:
+                y = y + bias.float()
+            y_f32.copy_(y)
+            return y_f32
+        if epi == "residual":
+            y_bf16.copy_((y.to(x.dtype).float() + y_bf16.float()).to(x.dtype))
+            return y_bf16
+        if epi == "swiglu":
+            y_bf16.copy_(swiglu_from_interleaved(y.to(x.dtype)))
+            return y_bf16
+        if epi == "argmax":
+            if y_f32 is not None:
+                y_f32.copy_(y)
+            return y.argmax(-1)
+    native().gemv(x, w, GEMV[epi], bias, y_f32, y_bf16, argmax)
+    return y_bf16 if y_bf16 is not None else y_f32

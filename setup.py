@@ -1,0 +1,47 @@
+"""Build the sm_100a extension in-tree:  python setup.py build_ext --inplace
+
+Only sm_100a code is generated (`-gencode arch=compute_100a,code=sm_100a`); torch's own
+TORCH_CUDA_ARCH_LIST is bypassed by passing the arch flags explicitly.
+"""
+
+import os
+from pathlib import Path
+
+from setuptools import setup
+from torch.utils.cpp_extension import BuildExtension, CUDAExtension
+
+ROOT = Path(__file__).resolve().parent
+PKG = "hetero_cp_ringattn_b200"
+CSRC = ROOT / PKG / "csrc"
+
+os.environ.setdefault("TORCH_CUDA_ARCH_LIST", "10.0a")
+os.environ.setdefault("MAX_JOBS", str(os.cpu_count() or 8))
+
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+NVCC_FLAGS = ARCH + ["-O3", "-std=c++17", "-lineinfo", "--use_fast_math", "-Xptxas=-v",
+                     "-U__CUDA_NO_HALF_OPERATORS__", "-U__CUDA_NO_HALF_CONVERSIONS__",
+                     "-U__CUDA_NO_BFLOAT16_CONVERSIONS__", "-U__CUDA_NO_BFLOAT162_OPERATORS__",
+                     "--expt-relaxed-constexpr"]
+SOURCES = [
+    "bindings.cpp",
+    "core/runtime.cu",
+    "kernels/gemm_sm100.cu",
+    "kernels/attn_fwd_sm100.cu",
+    "kernels/elementwise.cu",
+    "kernels/decode.cu",
+]
+
+setup(
+    name=PKG,
+    version="0.1.0",
+    packages=[PKG],
+    ext_modules=[
+        CUDAExtension(
+            name=f"{PKG}._C",
+            sources=[str(CSRC / s) for s in SOURCES],
+            include_dirs=[str(CSRC / "include"), str(CSRC)],
+            extra_compile_args={"cxx": ["-O3", "-std=c++17"], "nvcc": NVCC_FLAGS},
+        )
+    ],
+    cmdclass={"build_ext": BuildExtension.with_options(use_ninja=True)},
+)

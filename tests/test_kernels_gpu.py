@@ -1,0 +1,176 @@
+"""Numerics of the sm_100a kernels against plain PyTorch fp32 references (GPU only)."""
+
+import math
+
+import pytest
+import torch
+
+from hetero_cp_ringattn_b200.ops import kernels as K
+from hetero_cp_ringattn_b200.ops import reference as ref
+from hetero_cp_ringattn_b200.ops._ext import native
+
+pytestmark = pytest.mark.gpu
+
+
+def rel_err(a, b):
+    a = a.float()
+    b = b.float()
+    return float((a - b).abs().max() / b.abs().max().clamp_min(1e-6))
+
+
+def status_tensor(dev):
+    return torch.zeros(8, dtype=torch.int32, device=dev)
+
+
+def assert_status_clean(st):
+    torch.cuda.synchronize()
+    assert int(st[0]) == 0, f"device status {st.tolist()}"
+
+
+@pytest.mark.parametrize("m,n,k", [(128, 256, 64), (300, 512, 256), (1000, 768, 1000), (4096, 3072, 2048)])
+def test_gemm_store(dev, m, n, k):
+    torch.manual_seed(0)
+    a = torch.randn(m, k, device=dev, dtype=torch.bfloat16)
+    w = torch.randn(n, k, device=dev, dtype=torch.bfloat16) / math.sqrt(k)
+    st = status_tensor(dev)
+    y = K.gemm(a, w, "store", status=st)
+    assert_status_clean(st)
+    r = a.float() @ w.float().t()
+    assert rel_err(y, r) < 1e-2
+
+
+def test_gemm_bias_residual(dev):
+    torch.manual_seed(1)
+    m, n, k = 513, 1280, 512
+    a = torch.randn(m, k, device=dev, dtype=torch.bfloat16)
+    w = torch.randn(n, k, device=dev, dtype=torch.bfloat16) / math.sqrt(k)
+    b = torch.randn(n, device=dev, dtype=torch.bfloat16)
+    st = status_tensor(dev)
+    y = K.gemm(a, w, "bias", bias=b, status=st)
+    r = a.float() @ w.float().t() + b.float()
+    assert rel_err(y, r) < 1e-2
+    res = torch.randn(m, n, device=dev, dtype=torch.bfloat16)
+    expect = (a.float() @ w.float().t()).bfloat16().float() + res.float()
+    y2 = K.gemm(a, w, "residual", residual=res, status=st)  # in place on res
+    assert_status_clean(st)
+    assert y2.data_ptr() == res.data_ptr()
+    assert rel_err(y2, expect) < 1e-2
+
+
+def test_gemm_swiglu(dev):
+    torch.manual_seed(2)
+    m, i, k = 700, 512, 384
+    a = torch.randn(m, k, device=dev, dtype=torch.bfloat16)
+    g = torch.randn(i, k, device=dev, dtype=torch.bfloat16) / math.sqrt(k)
+    u = torch.randn(i, k, device=dev, dtype=torch.bfloat16) / math.sqrt(k)
+    wgu = K.interleave_gate_up(g, u)
+    st = status_tensor(dev)
+    y = K.gemm(a, wgu, "swiglu", status=st)
+    assert_status_clean(st)
+    gg = (a.float() @ g.float().t()).bfloat16().float()
+    uu = (a.float() @ u.float().t()).bfloat16().float()
+    r = torch.nn.functional.silu(gg) * uu
+    assert y.shape == (m, i)
+    assert rel_err(y, r) < 2e-2
+
+
+def _stage(k_tok, v_tok, cap):
+    """[L, Hkv, D] tokens in position order -> staging [Hkv, cap, D] K and V."""
+    L, hkv, d = k_tok.shape
+    ks = torch.zeros(hkv, cap, d, dtype=k_tok.dtype, device=k_tok.device)
+    vs = torch.zeros_like(ks)
+    ks[:, :L] = k_tok.transpose(0, 1)
+    vs[:, :L] = v_tok.transpose(0, 1)
+    return ks, vs
+
+
+@pytest.mark.parametrize("d", [64, 128])
+@pytest.mark.parametrize("layout", ["prefix", "suffix", "striped", "noncausal"])
+def test_attention(dev, d, layout):
+    torch.manual_seed(3)
+    L, h, hkv = 700, 8, 2
+    q_all = torch.randn(L, h, d, device=dev, dtype=torch.bfloat16)
+    k_all = torch.randn(L, hkv, d, device=dev, dtype=torch.bfloat16)
+    v_all = torch.randn(L, hkv, d, device=dev, dtype=torch.bfloat16)
+    if layout == "prefix":
+        pos = torch.arange(0, 300, device=dev)
+    elif layout == "suffix":
+        pos = torch.arange(300, L, device=dev)
+    elif layout == "striped":
+        pos = torch.arange(1, L, 3, device=dev)
+    else:
+        pos = torch.arange(100, 400, device=dev)
+    causal = layout != "noncausal"
+    q = q_all[pos].contiguous()
+    ks, vs = _stage(k_all, v_all, cap=1024)
+    st = status_tensor(dev)
+    start = int(pos[0]) // 128 if layout == "suffix" else 0
+    o, lse = K.attention(q, ks, vs, pos.int(), L, causal=causal, kv_start_tile=start, status=st)
+    assert_status_clean(st)
+    ro, rl = ref.full_attention(q.float(), k_all.float(), v_all.float(), pos, torch.arange(L, device=dev),
+                                causal=causal)
+    assert (o.float() - ro).abs().max() < 2e-2
+    assert (lse - rl).abs().max() < 2e-2
+
+
+def test_attention_long_gqa(dev):
+    torch.manual_seed(4)
+    L, h, hkv, d = 4096, 32, 8, 64
+    q = torch.randn(L, h, d, device=dev, dtype=torch.bfloat16)
+    k = torch.randn(L, hkv, d, device=dev, dtype=torch.bfloat16)
+    v = torch.randn(L, hkv, d, device=dev, dtype=torch.bfloat16)
+    pos = torch.arange(L, device=dev)
+    ks, vs = _stage(k, v, cap=L)
+    st = status_tensor(dev)
+    o, lse = K.attention(q, ks, vs, pos.int(), L, causal=True, status=st)
+    assert_status_clean(st)
+    ro, rl = ref.full_attention(q.float(), k.float(), v.float(), pos, pos, causal=True)
+    assert (o.float() - ro).abs().max() < 2e-2
+    assert (lse - rl).abs().max() < 2e-2
+
+
+def test_rmsnorm_embedding(dev):
+    torch.manual_seed(5)
+    x = torch.randn(1000, 2048, device=dev, dtype=torch.bfloat16)
+    w = torch.rand(2048, device=dev, dtype=torch.bfloat16) + 0.5
+    y = K.rmsnorm(x, w, 1e-5)
+    r = ref.rmsnorm(x.float(), w.float(), 1e-5)
+    assert rel_err(y, r) < 1e-2
+    emb = torch.randn(500, 256, device=dev, dtype=torch.bfloat16)
+    ids = torch.randint(0, 500, (77,), device=dev, dtype=torch.int32)
+    e = K.embedding(ids, emb)
+    assert torch.equal(e, emb[ids.long()])
+
+
+@pytest.mark.parametrize("b", [1, 2, 4, 8])
+def test_gemv(dev, b):
+    torch.manual_seed(6)
+    kdim, n = 2048, 3072
+    x = torch.randn(b, kdim, device=dev, dtype=torch.bfloat16)
+    w = torch.randn(n, kdim, device=dev, dtype=torch.bfloat16) / math.sqrt(kdim)
+    bias = torch.randn(n, device=dev, dtype=torch.bfloat16)
+    y = torch.empty(b, n, device=dev, dtype=torch.float32)
+    K.gemv(x, w, "f32", bias=bias, y_f32=y)
+    r = x.float() @ w.float().t() + bias.float()
+    assert rel_err(y, r) < 1e-3
+    res = torch.randn(b, n, device=dev, dtype=torch.bfloat16)
+    expect = (x.float() @ w.float().t()).bfloat16().float() + res.float()
+    K.gemv(x, w, "residual", y_bf16=res)
+    assert rel_err(res, expect) < 1e-2
+    g = torch.randn(1024, kdim, device=dev, dtype=torch.bfloat16) / math.sqrt(kdim)
+    u = torch.randn(1024, kdim, device=dev, dtype=torch.bfloat16) / math.sqrt(kdim)
+    out = torch.empty(b, 1024, device=dev, dtype=torch.bfloat16)
+    K.gemv(x, K.interleave_gate_up(g, u), "swiglu", y_bf16=out)
+    gg = (x.float() @ g.float().t()).bfloat16().float()
+    uu = (x.float() @ u.float().t()).bfloat16().float()
+    assert rel_err(out, torch.nn.functional.silu(gg) * uu) < 2e-2
+    vocab = 50000
+    wl = torch.randn(vocab, kdim, device=dev, dtype=torch.bfloat16)
+    am = torch.zeros(b, dtype=torch.int64, device=dev)
+    logits = torch.empty(b, vocab, device=dev, dtype=torch.float32)
+    K.gemv(x, wl, "argmax", y_f32=logits, argmax=am)
+    tok = torch.empty(b, dtype=torch.int64, device=dev)
+    native().argmax_finalize(am, None, tok)
+    rl = x.float() @ wl.float().t()
+    assert torch.equal(tok, logits.argmax(-1))
+    assert rel_err(logits, rl) < 1e-3

@@ -1,0 +1,150 @@
+"""Domain runtime on the GPU: KV push + ring attention and the decode (O, LSE) exchange, for one
+rank and for ranks emulated inside one process on one GPU (push phase for every rank before any
+attend phase, so no launch ever waits on a later launch)."""
+
+import math
+
+import pytest
+import torch
+
+from hetero_cp_ringattn_b200.ops import reference as ref
+from hetero_cp_ringattn_b200.ops._ext import native
+from hetero_cp_ringattn_b200.parallel.strategy import layout_positions
+
+pytestmark = pytest.mark.gpu
+
+H, HKV, D, PAGE = 8, 2, 64, 256
+
+
+def make_rt(rank, world, cap=2048, pages=16, layers=2):
+    return native().Runtime(rank, world, 0, layers, pages, PAGE, HKV, D, H, cap, 8, 2000)
+
+
+def tables(dev, max_pos=4096):
+    cos, sin = ref.rope_cos_sin(torch.arange(max_pos, device=dev), D, 10000.0)
+    return cos.contiguous(), sin.contiguous()
+
+
+def reference_layer(qkv_all, pos_all, theta=10000.0):
+    q = qkv_all[:, : H * D].view(-1, H, D)
+    k = qkv_all[:, H * D:(H + HKV) * D].view(-1, HKV, D)
+    v = qkv_all[:, (H + HKV) * D:].view(-1, HKV, D)
+    q = ref.apply_rope(q.float(), pos_all, theta)
+    k = ref.apply_rope(k.float(), pos_all, theta)
+    o, lse = ref.full_attention(q, k, v.float(), pos_all, pos_all, causal=True)
+    return q, k, v, o, lse
+
+
+def run_ranks(dev, chunks, strategy, layer=0, epoch=1, rts=None):
+    L = sum(chunks)
+    n = len(chunks)
+    torch.manual_seed(7)
+    qkv_all = (torch.randn(L, (H + 2 * HKV) * D, device=dev) * 0.5).bfloat16()
+    pos_all = torch.arange(L, device=dev)
+    cos, sin = tables(dev)
+    positions = [torch.as_tensor(p, device=dev) for p in layout_positions(chunks, strategy)]
+    if rts is None:
+        rts = [make_rt(r, n) for r in range(n)]
+        if n > 1:
+            for rt in rts:
+                rt.open_peers_local(rts)
+    outs = []
+    args = []
+    for r in range(n):
+        p = positions[r]
+        qkv = qkv_all[p].contiguous()
+        pt = torch.arange(r * 4, r * 4 + 4, dtype=torch.int32, device=dev)  # 4 pages
+        q_out = torch.empty(len(p), H, D, device=dev, dtype=torch.bfloat16)
+        o_out = torch.empty_like(q_out)
+        lse = torch.empty(H, len(p), device=dev, dtype=torch.float32)
+        start = int(p[0]) // 128 if strategy == "vanilla" else 0
+        a = (qkv, p.int().contiguous(), cos, sin, layer, pt, 0, L, start, 1.0 / math.sqrt(D), True,
+             q_out, o_out, lse, epoch)
+        args.append(a)
+        outs.append((o_out, lse))
+    for r in range(n):
+        rts[r].push_layer(*args[r])
+    for r in range(n):
+        rts[r].attend_layer(*args[r])
+    torch.cuda.synchronize()
+    for rt in rts:
+        rt.check()
+    _, k_ref, v_ref, o_ref, lse_ref = reference_layer(qkv_all, pos_all)
+    for r in range(n):
+        p = positions[r]
+        o, lse = outs[r]
+        assert (o.float() - o_ref[p]).abs().max() < 2e-2, f"rank {r}"
+        assert (lse - lse_ref[:, p]).abs().max() < 2e-2
+        # the local arena holds this rank's K/V rows in local order
+        arena = rts[r].arena()
+        pages = torch.arange(r * 4, r * 4 + 4, device=dev)
+        kk = arena[layer, pages, 0].permute(1, 0, 2, 3).reshape(HKV, -1, D)[:, : len(p)]
+        assert (kk.float().transpose(0, 1) - k_ref[p]).abs().max() < 2e-2
+    return rts, qkv_all, positions
+
+
+def test_single_rank_layer(dev):
+    run_ranks(dev, [700], "vanilla")
+
+
+@pytest.mark.parametrize("strategy", ["vanilla", "zigzag", "striped"])
+def test_emulated_two_ranks(dev, strategy):
+    run_ranks(dev, [400, 300], strategy)
+
+
+def test_emulated_uneven_three_ranks_two_layers(dev):
+    rts, _, _ = run_ranks(dev, [500, 500, 100], "vanilla", layer=0, epoch=1)
+    run_ranks(dev, [500, 500, 100], "zigzag", layer=1, epoch=2, rts=rts)
+    run_ranks(dev, [500, 500, 100], "vanilla", layer=0, epoch=3, rts=rts)
+
+
+@pytest.mark.parametrize("world,b", [(1, 1), (2, 1), (3, 4)])
+def test_decode_exchange(dev, world, b):
+    torch.manual_seed(9)
+    counts = [300, 257, 129][:world]
+    rts = [make_rt(r, world) for r in range(world)]
+    if world > 1:
+        for rt in rts:
+            rt.open_peers_local(rts)
+    q = torch.randn(b, H, D, device=dev, dtype=torch.bfloat16)
+    ks, vs = [], []
+    pts = []
+    for r in range(world):
+        arena = rts[r].arena()
+        n = counts[r]
+        k = torch.randn(n, HKV, D, device=dev, dtype=torch.bfloat16)
+        v = torch.randn(n, HKV, D, device=dev, dtype=torch.bfloat16)
+        pages = [3, 1]  # non-contiguous page ids
+        for i in range(n):
+            pg, row = pages[i // PAGE], i % PAGE
+            arena[1, pg, 0, :, row] = k[i]
+            arena[1, pg, 1, :, row] = v[i]
+        ks.append(k)
+        vs.append(v)
+        pts.append(torch.tensor([pages] * b, dtype=torch.int32, device=dev))
+    splits = 4
+    outs = []
+    bufs = []
+    for r in range(world):
+        part_o = torch.empty(b * H * splits * D, device=dev)
+        part_l = torch.empty(b * H * splits, device=dev)
+        cnt = torch.zeros(b * HKV + 1, dtype=torch.int32, device=dev)
+        ntok = torch.full((b,), counts[r], dtype=torch.int32, device=dev)
+        bufs.append((part_o, part_l, cnt, ntok))
+        rts[r].decode_attn(q, 1, pts[r], ntok, 1.0 / math.sqrt(D), splits, part_o, part_l, cnt, None, 1, 5)
+    for r in range(world):
+        out = torch.empty(b, H * D, device=dev, dtype=torch.bfloat16)
+        rts[r].decode_combine(out, b, H, None, 1, 5)
+        outs.append(out)
+    torch.cuda.synchronize()
+    for rt in rts:
+        rt.check()
+    k_all = torch.cat(ks)
+    v_all = torch.cat(vs)
+    L = k_all.shape[0]
+    for bb in range(b):
+        ro, _ = ref.full_attention(q[bb:bb + 1].float(), k_all.float(), v_all.float(), causal=False)
+        for r in range(world):
+            assert (outs[r][bb].view(H, D).float() - ro[0]).abs().max() < 2e-2
+    for r in range(1, world):
+        assert torch.equal(outs[r], outs[0]), "ranks must produce bit-identical combined outputs"
