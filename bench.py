@@ -1,0 +1,225 @@
+"""Headline benchmark: long-context prefill tok/s + TTFT and decode tok/s, CP = N ranks on one node.
+
+Config (BASELINE config #2): Llama-3.2-1B-shaped decoder (16 layers, hidden 2048, 32 heads,
+8 KV heads, head_dim 64, SwiGLU 8192, vocab 128256, RoPE theta 5e5), bf16, random-init weights
+N(0, 0.02), a 32768-token prompt of uniform-random token ids, then 128 greedy tokens; equal chunks
+(zigzag layout for N > 1 so every rank carries the same causal work). One "step" is one full
+request: prefill of the whole prompt + 127 decode steps.
+
+  python bench.py --gpus N --steps K --warmup W          (N > 1: launched under torchrun)
+  python bench.py --impl reference ...                   (the reference's own code path)
+
+Rank 0 prints one JSON line. `value` is prefill tokens/s for the whole job (prompt tokens divided
+by the device-timed prefill time, max over ranks). Weights (~2.5 GB) and activations are far
+larger than the 126 MB L2, so no explicit L2 flush is done between steps.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import sys
+import time
+
+import torch
+
+BASELINE_PREFILL_TOK_S = None  # BASELINE.json "published" is empty: no same-metric number to divide by
+
+CONFIGS = {
+    "llama-3.2-1b-32k": dict(model="llama-3.2-1b", prompt=32768, new_tokens=128),
+    "qwen2.5-3b-64k": dict(model="qwen2.5-3b", prompt=65536, new_tokens=128),
+    "llama-3-8b-128k": dict(model="llama-3-8b", prompt=131072, new_tokens=256),
+    "tiny": dict(model="tiny-gpu", prompt=4096, new_tokens=16),
+}
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="hcp", choices=["hcp", "reference"])
+    ap.add_argument("--config", default="llama-3.2-1b-32k", choices=sorted(CONFIGS))
+    ap.add_argument("--strategy", default=None, help="vanilla|striped|zigzag (default: zigzag for N>1)")
+    ap.add_argument("--ratio", default=None, help="capacity ratio override, e.g. 5:5:1")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-graphs", action="store_true")
+    return ap.parse_args()
+
+
+def reference_unavailable(args) -> None:
+    """The reference is a Rust/tch-rs + QUIC program: it has no Python packaging (no setup.py or
+    pyproject.toml, so the offline pip install into baseline/_ref fails) and needs cargo/rustc and
+    crates.io, which this image does not have."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank == 0:
+        print(json.dumps({
+            "impl": "reference",
+            "unavailable": "stark-sim/hetero-cp-ringattn is a Rust (cargo + tch-rs + quinn) project "
+                           "with no Python package: pip install into baseline/_ref fails ('Neither "
+                           "setup.py nor pyproject.toml found') and no cargo/rustc/crates are available "
+                           "offline to build it",
+            "n_gpus": args.gpus,
+        }), flush=True)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        reference_unavailable(args)
+        return 0
+
+    from hetero_cp_ringattn_b200.config import preset, parse_ratio
+    from hetero_cp_ringattn_b200.models.llama import LlamaCPEngine
+    from hetero_cp_ringattn_b200.models.weights import PreparedWeights
+    from hetero_cp_ringattn_b200.parallel.capacity import chunks_from_ratio, equal_chunks
+    from hetero_cp_ringattn_b200.utils import launches
+    from hetero_cp_ringattn_b200.utils.perf import ClockSampler, max_over_ranks
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        if world == 1 and args.gpus > 1:
+            raise SystemExit("--gpus N > 1 must be launched with torchrun --nproc-per-node N")
+        raise SystemExit(f"WORLD_SIZE={world} but --gpus={args.gpus}")
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    group = None
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                                timeout=timedelta(seconds=600))
+        group = dist.new_group(backend="gloo", timeout=timedelta(seconds=600))
+
+    spec = CONFIGS[args.config]
+    cfg = preset(spec["model"])
+    Lp, new_tokens = spec["prompt"], spec["new_tokens"]
+    strategy = args.strategy or ("zigzag" if world > 1 else "vanilla")
+    if args.ratio:
+        chunks = chunks_from_ratio(Lp, parse_ratio(args.ratio))
+    else:
+        chunks = equal_chunks(Lp, world)
+
+    weights = PreparedWeights.random(cfg, seed=0, device=dev)
+    eng = LlamaCPEngine(cfg, weights, rank=rank, world=world, device=dev, group=group,
+                        max_context=Lp, max_batch=1, decode_reserve=new_tokens + 8,
+                        use_graphs=not args.no_graphs)
+    gen = torch.Generator().manual_seed(1234)
+    prompt = torch.randint(0, cfg.vocab_size, (Lp,), generator=gen, dtype=torch.int64).pin_memory()
+    prompt_dev = prompt.to(dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(group=group)
+        torch.cuda.synchronize()
+
+    req = [100]
+
+    def one_request(dev_prompt):
+        """Device-timed request: prefill (events) + decode (events). Returns (prefill_ms, decode_ms)."""
+        req[0] += 1
+        e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+        e0.record()
+        tok, _ = eng.prefill(req[0], dev_prompt, chunks, strategy, decode_horizon=new_tokens)
+        e1.record()
+        cur = tok
+        for _ in range(new_tokens - 1):
+            cur = eng.decode_step([req[0]], cur)
+        e2.record()
+        eng.release(req[0])
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1), e1.elapsed_time(e2), cur
+
+    for _ in range(args.warmup):
+        one_request(prompt_dev)
+    barrier()
+    launches.reset()
+    pre_ms, dec_ms = [], []
+    with ClockSampler(local_rank) as clocks:
+        barrier()
+        t_all0 = torch.cuda.Event(enable_timing=True)
+        t_all1 = torch.cuda.Event(enable_timing=True)
+        t_all0.record()
+        for _ in range(args.steps):
+            p, d, _ = one_request(prompt_dev)
+            pre_ms.append(p)
+            dec_ms.append(d)
+        t_all1.record()
+        barrier()
+    n_launch = launches.total() // max(1, args.steps)
+    total_ms = max_over_ranks(t_all0.elapsed_time(t_all1) / args.steps, group)
+    prefill_ms = max_over_ranks(sum(pre_ms) / len(pre_ms), group)
+    decode_ms = max_over_ranks(sum(dec_ms) / len(dec_ms), group)
+    eng.check_device()
+
+    # ---------------------------------------------------------------- end to end (public API)
+    e2e = None
+    if not args.no_e2e:
+        h2d = int(len(prompt)) * prompt.element_size()
+        ttfts, totals = [], []
+        for i in range(max(1, min(args.steps, 3)) + 1):
+            barrier()
+            t0 = time.perf_counter()
+            req[0] += 1
+            tok, _ = eng.prefill(req[0], prompt, chunks, strategy, decode_horizon=new_tokens)
+            first = int(tok.item())  # device -> host read of the first token (TTFT)
+            t1 = time.perf_counter()
+            cur = tok
+            outs = [tok]
+            for _ in range(new_tokens - 1):
+                cur = eng.decode_step([req[0]], cur)
+                outs.append(cur.view(1))
+            gen_ids = torch.cat(outs).cpu()  # device -> host read of the generated tokens
+            t2 = time.perf_counter()
+            eng.release(req[0])
+            if i > 0:  # first iteration is a warm-up of the host path
+                ttfts.append(t1 - t0)
+                totals.append(t2 - t0)
+        ttft = max_over_ranks(sum(ttfts) / len(ttfts), group)
+        total = max_over_ranks(sum(totals) / len(totals), group)
+        e2e = {"value": Lp / ttft, "unit": "prompt tokens/s (end to end: pinned prompt H2D, "
+               "prefill, first-token D2H)", "ttft_ms": ttft * 1e3, "request_ms": total * 1e3,
+               "decode_tok_s": (new_tokens - 1) / max(1e-9, total - ttft),
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 8 + new_tokens * 8}
+
+    clk = clocks.summary()
+    value = Lp / (prefill_ms / 1e3)
+    if rank == 0:
+        out = {
+            "metric": "prefill tok/s & TTFT @32k and decode tok/s (CP=N B200, max over ranks)",
+            "value": value,
+            "unit": "prompt tokens/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": total_ms,
+            "higher_is_better": True,
+            "scaling": "strong",
+            "vs_baseline": (value / BASELINE_PREFILL_TOK_S) if BASELINE_PREFILL_TOK_S else None,
+            "dtype": "bf16",
+            "data": "synthetic: uniform-random prompt token ids, random-init N(0,0.02) weights",
+            "ttft_ms": prefill_ms,
+            "decode_ms_per_token": decode_ms / max(1, new_tokens - 1),
+            "decode_tok_s": (new_tokens - 1) / (decode_ms / 1e3),
+            "gpu_launches": n_launch,
+            "config": {"model": spec["model"], "global_batch": 1, "seq_len": Lp,
+                       "new_tokens": new_tokens, "parallelism": f"cp{world}",
+                       "chunks": chunks, "strategy": strategy,
+                       "l2": "no flush: weights + activations (>2.5 GB) exceed the 126 MB L2",
+                       "step": "one request = prefill of the prompt + 127 decode steps"},
+            "clocks": clk,
+            "e2e": e2e,
+        }
+        print(json.dumps(out), flush=True)
+    eng.close()
+    if world > 1:
+        dist.barrier(group=group)
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,242 @@
+"""Command-line entry points.
+
+Parity: the reference's single binary with modes (rust/src/cli.rs:14-165, lib.rs:211-634):
+  * `correctness` - the ring-vs-dense oracle suite with tolerance tiers and a JSON report
+    (`--report-path`, `--tolerance-tier`, `--stress-test`; lib.rs:107-199);
+  * `infer` - single-node inference with `--export-logits` in the reference's binary layout
+    ([vocab u64 LE][steps u64 LE] then f32 rows; rust/src/infer.rs:74-79);
+  * `serve` - coordinator + workers: one torchrun job, rank 0 coordinates and serves the HTTP API
+    (`/v1/completions`, `/health`, `/metrics`), every rank runs the worker command loop
+    (coordinator.rs:76-273 and worker.rs:77-143 flags that still apply on one NVSwitch box:
+    --model-dir, --prompt/--prompt-file/--prompts-file, --max-tokens, --temperature, --top-p,
+    --chunk-sizes, --capacity-aware, --ring-strategy, --trace-jsonl, --max-batch-size,
+    --activation-reserve-mb, --session-continuation-tokens, --http-addr);
+  * `gen-prompt` - an exact-N-token random prompt (rust/src/bin/gen_prompt.rs).
+
+  python -m hetero_cp_ringattn_b200 correctness --report-path reports/ring.json
+  torchrun --nproc-per-node 8 -m hetero_cp_ringattn_b200 serve --model-preset llama-3.2-1b --http-addr 127.0.0.1:8000
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import logging
+import os
+import struct
+import sys
+from typing import List, Optional
+
+import torch
+
+
+def _add_model_args(ap):
+    ap.add_argument("--model-dir", default=None, help="HF directory (config.json + *.safetensors)")
+    ap.add_argument("--model-preset", default="tiny-gpu", help="random-init shape when no model dir")
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--max-context", type=int, default=32768)
+    ap.add_argument("--max-batch-size", type=int, default=4)
+    ap.add_argument("--device", default=None, help="cuda|cuda:N|cpu (HCP_TORCH_DEVICE)")
+
+
+def _load_model(args, device):
+    from .config import ModelConfig, preset
+    from .models.weights import ModelWeights, PreparedWeights
+    dtype = torch.bfloat16 if device.type == "cuda" else torch.float32
+    if args.model_dir:
+        cfg = ModelConfig.from_file(os.path.join(args.model_dir, "config.json"))
+        w = ModelWeights.from_dir(args.model_dir, device="cpu", dtype=dtype, cfg=cfg)
+        return cfg, PreparedWeights.from_weights(w, device=device, dtype=dtype, free_source=True)
+    cfg = preset(args.model_preset)
+    if device.type == "cuda":
+        return cfg, PreparedWeights.random(cfg, seed=args.seed, device=device, dtype=dtype)
+    w = ModelWeights.random_init(cfg, seed=args.seed, dtype=dtype)
+    return cfg, PreparedWeights.from_weights(w, dtype=dtype)
+
+
+def _device(args) -> torch.device:
+    name = args.device or os.environ.get("HCP_TORCH_DEVICE") or os.environ.get("HCP_TCH_DEVICE")
+    if not name:
+        name = "cuda" if torch.cuda.is_available() else "cpu"
+    if name == "cuda":
+        name = f"cuda:{int(os.environ.get('LOCAL_RANK', '0'))}"
+    return torch.device(name)
+
+
+def cmd_correctness(args) -> int:
+    from .correctness import run_suite, write_report
+    from .errors import ToleranceTier
+    tier = ToleranceTier.parse(args.tolerance_tier)
+    rep = run_suite(tier, stress_seeds=args.stress_test)
+    for c in rep["cases"]:
+        w = c["worst_seed"]
+        print(f"[{'PASS' if c['passed'] else 'FAIL'}] {c['name']}: out max_abs={w['output']['max_abs_err']:.3e} "
+              f"lse max_abs={w['lse']['max_abs_err']:.3e}")
+    if args.report_path:
+        os.makedirs(os.path.dirname(os.path.abspath(args.report_path)), exist_ok=True)
+        write_report(rep, args.report_path)
+    print("overall:", "PASS" if rep["passed"] else "FAIL")
+    return 0 if rep["passed"] else 1
+
+
+def write_logits(path: str, rows: List[torch.Tensor]) -> None:
+    """[vocab u64 LE][steps u64 LE] + f32 LE rows (prefill row first, then one per decode step)."""
+    vocab = rows[0].numel()
+    with open(path, "wb") as f:
+        f.write(struct.pack("<QQ", vocab, len(rows) - 1))
+        for r in rows:
+            f.write(r.detach().float().cpu().numpy().astype("<f4").tobytes())
+
+
+def read_logits(path: str):
+    import numpy as np
+    with open(path, "rb") as f:
+        vocab, steps = struct.unpack("<QQ", f.read(16))
+        data = np.frombuffer(f.read(), dtype="<f4").reshape(steps + 1, vocab)
+    return vocab, steps, data
+
+
+def cmd_infer(args) -> int:
+    from .models.llama import LlamaCPEngine
+    from .serve.tokenizer import load_tokenizer
+    dev = _device(args)
+    cfg, w = _load_model(args, dev)
+    tok = load_tokenizer(args.model_dir, cfg.vocab_size)
+    prompt = args.prompt
+    if args.prompt_file:
+        prompt = open(args.prompt_file).read()
+    ids = torch.tensor(tok.encode(prompt or "hello"), dtype=torch.int64)
+    eng = LlamaCPEngine(cfg, w, device=dev, max_context=max(args.max_context, ids.numel()),
+                        max_batch=1, decode_reserve=args.max_tokens + 8)
+    first, logits = eng.prefill(1, ids, [ids.numel()], decode_horizon=max(1, args.max_tokens),
+                                return_logits=True)
+    rows = [logits.float().cpu()]
+    out = [int(first)]
+    cur = first
+    for _ in range(args.max_tokens - 1):
+        cur = eng.decode_step([1], cur)
+        out.append(int(cur.view(-1)[0]))
+        if args.export_logits:
+            rows.append(eng.last_logits(1)[0].float().cpu())
+    if args.export_logits:
+        write_logits(args.export_logits, rows)
+    print(json.dumps({"prompt_tokens": ids.numel(), "tokens": out, "text": tok.decode(out)}))
+    eng.close()
+    return 0
+
+
+def cmd_serve(args) -> int:
+    import torch.distributed as dist
+    from .models.llama import LlamaCPEngine
+    from .parallel.capacity import query_device_capacity_mb
+    from .serve import protocol as P
+    from .serve.coordinator import Coordinator, CoordinatorArgs
+    from .serve.http_server import ApiServer, ApiState
+    from .serve.tokenizer import load_tokenizer
+    from .serve.worker import Worker
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    dev = _device(args)
+    group = None
+    from datetime import timedelta
+    timeout = timedelta(seconds=int(os.environ.get("HCP_QUIC_TIMEOUT_SECS", "600")))
+    if world > 1:
+        if dev.type == "cuda":
+            torch.cuda.set_device(dev)
+            dist.init_process_group("nccl", device_id=dev, timeout=timeout)
+        else:
+            dist.init_process_group("gloo", timeout=timeout)
+        group = dist.new_group(backend="gloo", timeout=timeout)
+    cfg, w = _load_model(args, dev)
+    eng = LlamaCPEngine(cfg, w, rank=rank, world=world, device=dev, group=group,
+                        max_context=args.max_context, max_batch=args.max_batch_size)
+    control = P.ControlPlane(group, rank, world)
+    worker = Worker(eng, control)
+    caps = control.all_gather(query_device_capacity_mb(str(dev)))  # the handshake
+    if rank != 0:
+        worker.loop()
+        eng.close()
+        return 0
+    tok = load_tokenizer(args.model_dir, cfg.vocab_size)
+    ca = CoordinatorArgs(strategy=args.ring_strategy,
+                         chunk_sizes=[int(x) for x in args.chunk_sizes.split(",")] if args.chunk_sizes else None,
+                         capacity_aware=args.capacity_aware,
+                         ratio=[int(x) for x in args.ratio.split(":")] if args.ratio else None,
+                         max_batch_size=args.max_batch_size,
+                         activation_reserve_mb=args.activation_reserve_mb,
+                         session_continuation_tokens=args.session_continuation_tokens,
+                         trace_jsonl=args.trace_jsonl, eos_ids=cfg.eos_token_id)
+    coord = Coordinator(worker, control, tok, cfg, ca, capacities_mb=caps)
+    prompts = []
+    if args.prompt:
+        prompts.append(args.prompt)
+    if args.prompts_file:
+        prompts += [ln.rstrip("\n") for ln in open(args.prompts_file) if ln.strip()]
+    try:
+        if prompts and not args.http_addr:
+            for p in prompts:
+                r = coord.generate(tok.encode(p), args.max_tokens, args.temperature, args.top_p)
+                print(json.dumps({"prompt": p, "text": tok.decode(r.get("tokens", [])), **r}), flush=True)
+        else:
+            host, port = (args.http_addr or "127.0.0.1:8000").rsplit(":", 1)
+            srv = ApiServer(ApiState(coord, tok, args.model_dir or cfg.name, world), host, int(port)).start()
+            print(f"[coordinator] serving on http://{host}:{srv.port}", flush=True)
+            coord.run_forever()
+    except KeyboardInterrupt:
+        pass
+    finally:
+        coord.shutdown()
+        eng.close()
+    return 0
+
+
+def cmd_gen_prompt(args) -> int:
+    g = torch.Generator().manual_seed(args.seed)
+    ids = torch.randint(0, args.vocab, (args.tokens,), generator=g)
+    print(json.dumps(ids.tolist()))
+    return 0
+
+
+def main(argv: Optional[List[str]] = None) -> int:
+    logging.basicConfig(level=os.environ.get("HCP_LOG", "WARNING"))
+    ap = argparse.ArgumentParser(prog="hcp")
+    sub = ap.add_subparsers(dest="cmd", required=True)
+    c = sub.add_parser("correctness")
+    c.add_argument("--report-path", default=None)
+    c.add_argument("--tolerance-tier", default="strict")
+    c.add_argument("--stress-test", type=int, default=5)
+    c.set_defaults(fn=cmd_correctness)
+    i = sub.add_parser("infer")
+    _add_model_args(i)
+    i.add_argument("--prompt", default=None)
+    i.add_argument("--prompt-file", default=None)
+    i.add_argument("--max-tokens", type=int, default=10)
+    i.add_argument("--export-logits", default=None)
+    i.set_defaults(fn=cmd_infer)
+    s = sub.add_parser("serve", aliases=["coordinator", "worker"])
+    _add_model_args(s)
+    s.add_argument("--prompt", default=None)
+    s.add_argument("--prompts-file", default=None)
+    s.add_argument("--max-tokens", type=int, default=20)
+    s.add_argument("--temperature", type=float, default=0.0)
+    s.add_argument("--top-p", type=float, default=1.0)
+    s.add_argument("--chunk-sizes", default=None)
+    s.add_argument("--capacity-aware", action="store_true")
+    s.add_argument("--ratio", default=None, help="capacity ratio override, e.g. 5:5:1")
+    s.add_argument("--ring-strategy", default="vanilla", choices=["vanilla", "striped", "zigzag"])
+    s.add_argument("--trace-jsonl", default=None)
+    s.add_argument("--activation-reserve-mb", type=int, default=1536)
+    s.add_argument("--session-continuation-tokens", type=int, default=64)
+    s.add_argument("--http-addr", default=None)
+    s.set_defaults(fn=cmd_serve)
+    g = sub.add_parser("gen-prompt")
+    g.add_argument("--tokens", type=int, required=True)
+    g.add_argument("--vocab", type=int, default=128256)
+    g.add_argument("--seed", type=int, default=0)
+    g.set_defaults(fn=cmd_gen_prompt)
+    args = ap.parse_args(argv)
+    return args.fn(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -239,7 +239,8 @@ class PyRuntime {
                                 c10::optional<torch::Tensor> page_table, int64_t slot_base,
                                 int64_t L, int64_t kv_start_tile, double scale, bool causal,
                                 torch::Tensor q_out, torch::Tensor o_out,
-                                c10::optional<torch::Tensor> lse_out, int64_t epoch) {
+                                c10::optional<torch::Tensor> lse_out, int64_t epoch,
+                                c10::optional<torch::Tensor> existing_slot_pos) {
     check_cuda_bf16(qkv, "qkv");
     check_cuda_bf16(q_out, "q_out");
     check_cuda_bf16(o_out, "o_out");
@@ -271,16 +272,23 @@ class PyRuntime {
     a.o_out = o_out.data_ptr();
     a.lse_out = ptr_or_null<float>(lse_out);
     a.epoch = uint64_t(epoch);
+    if (existing_slot_pos.has_value() && existing_slot_pos->defined() && existing_slot_pos->numel() > 0) {
+      TORCH_CHECK(existing_slot_pos->scalar_type() == torch::kInt32, "existing_slot_pos int32");
+      TORCH_CHECK(a.page_table != nullptr, "existing rows need the page table");
+      a.existing_slot_pos = existing_slot_pos->data_ptr<int>();
+      a.existing_n = int(existing_slot_pos->numel());
+    }
     return a;
   }
 
   void push_layer(torch::Tensor qkv, torch::Tensor pos, torch::Tensor cos_t, torch::Tensor sin_t,
                   int64_t layer, c10::optional<torch::Tensor> page_table, int64_t slot_base,
                   int64_t L, int64_t kv_start_tile, double scale, bool causal, torch::Tensor q_out,
-                  torch::Tensor o_out, c10::optional<torch::Tensor> lse_out, int64_t epoch) {
+                  torch::Tensor o_out, c10::optional<torch::Tensor> lse_out, int64_t epoch,
+                  c10::optional<torch::Tensor> existing_slot_pos) {
     const c10::cuda::CUDAGuard g(qkv.device());
     auto a = layer_args(qkv, pos, cos_t, sin_t, layer, page_table, slot_base, L, kv_start_tile,
-                        scale, causal, q_out, o_out, lse_out, epoch);
+                        scale, causal, q_out, o_out, lse_out, epoch, existing_slot_pos);
     auto st = rt_.PushLayer(a, cur_stream());
     TORCH_CHECK(st.ok(), "push_layer: ", st.ToString());
   }
@@ -289,10 +297,10 @@ class PyRuntime {
                     int64_t layer, c10::optional<torch::Tensor> page_table, int64_t slot_base,
                     int64_t L, int64_t kv_start_tile, double scale, bool causal,
                     torch::Tensor q_out, torch::Tensor o_out, c10::optional<torch::Tensor> lse_out,
-                    int64_t epoch) {
+                    int64_t epoch, c10::optional<torch::Tensor> existing_slot_pos) {
     const c10::cuda::CUDAGuard g(qkv.device());
     auto a = layer_args(qkv, pos, cos_t, sin_t, layer, page_table, slot_base, L, kv_start_tile,
-                        scale, causal, q_out, o_out, lse_out, epoch);
+                        scale, causal, q_out, o_out, lse_out, epoch, existing_slot_pos);
     auto st = rt_.AttendLayer(a, cur_stream());
     TORCH_CHECK(st.ok(), "attend_layer: ", st.ToString());
   }
@@ -465,8 +473,14 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       .def("export_handle", &PyRuntime::export_handle)
       .def("open_peers", &PyRuntime::open_peers)
       .def("open_peers_local", &PyRuntime::open_peers_local)
-      .def("push_layer", &PyRuntime::push_layer)
-      .def("attend_layer", &PyRuntime::attend_layer)
+      .def("push_layer", &PyRuntime::push_layer, py::arg("qkv"), py::arg("pos"), py::arg("cos_t"),
+           py::arg("sin_t"), py::arg("layer"), py::arg("page_table"), py::arg("slot_base"), py::arg("L"),
+           py::arg("kv_start_tile"), py::arg("scale"), py::arg("causal"), py::arg("q_out"),
+           py::arg("o_out"), py::arg("lse_out"), py::arg("epoch"), py::arg("existing_slot_pos") = py::none())
+      .def("attend_layer", &PyRuntime::attend_layer, py::arg("qkv"), py::arg("pos"), py::arg("cos_t"),
+           py::arg("sin_t"), py::arg("layer"), py::arg("page_table"), py::arg("slot_base"), py::arg("L"),
+           py::arg("kv_start_tile"), py::arg("scale"), py::arg("causal"), py::arg("q_out"),
+           py::arg("o_out"), py::arg("lse_out"), py::arg("epoch"), py::arg("existing_slot_pos") = py::none())
       .def("qkv_decode", &PyRuntime::qkv_decode)
       .def("decode_attn", &PyRuntime::decode_attn)
       .def("decode_combine", &PyRuntime::decode_combine)

@@ -156,6 +156,21 @@ Status DomainRuntime::PushLayer(const RingLayerArgs& a, cudaStream_t stream) {
                                       status_, stream);
     if (e) return Status::Internal(e);
   }
+  // 2a. continuation: re-push this rank's already-stored rows of the session
+  if (a.existing_n > 0) {
+    ew::StagePushArgs sp{};
+    sp.arena = static_cast<const __nv_bfloat16*>(arena());
+    sp.geom = cfg_.geom;
+    sp.layer = a.layer;
+    sp.page_table = a.page_table;
+    sp.slot_pos = a.existing_slot_pos;
+    sp.n = a.existing_n;
+    sp.stage_ptrs = stage_tab_[parity];
+    sp.n_stage = n;
+    sp.stage_cap = cfg_.stage_cap;
+    const char* e = ew::stage_push(sp, stream);
+    if (e) return Status::Internal(e);
+  }
   // 2. RoPE + Q write + arena write + push K/V to every rank's staging buffer, then kv_ready
   ew::QkvPrefillArgs q{};
   q.qkv = static_cast<const __nv_bfloat16*>(a.qkv);

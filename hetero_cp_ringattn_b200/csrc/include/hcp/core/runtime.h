@@ -59,6 +59,9 @@ struct RingLayerArgs {
   void* o_out = nullptr;            // [T, H, D]
   float* lse_out = nullptr;         // [H, T] (optional)
   uint64_t epoch = 0;               // strictly increasing per layer step (same on all ranks)
+  // session continuation: already-stored slots [0, existing_n) of this layer to re-push
+  const int* existing_slot_pos = nullptr;
+  int existing_n = 0;
 };
 
 class DomainRuntime {

@@ -220,13 +220,21 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(DecodeAttnArgs a) {
     for (int j = 0; j < 8; ++j) acc[g][j] = 0.f;
   }
   const int* pt = a.page_tables + (long)b * a.pt_stride;
-  for (int t = s0 + grp; t < s1; t += GROUPS) {
-    const int page = pt[t / a.geom.page];
-    const int row = t % a.geom.page;
-    const __nv_bfloat16* kp = a.arena + a.geom.offset(a.layer, page, 0, h, row) + gl * 8;
-    const __nv_bfloat16* vp = kp + a.geom.kv_stride();
-    const uint4 kv = *reinterpret_cast<const uint4*>(kp);
-    const uint4 vv4 = *reinterpret_cast<const uint4*>(vp);
+  // The loop bound is warp-uniform (it depends on the warp, not the lane group) because the
+  // body reduces scores with full-warp shuffles; a lane group past the end of the split runs
+  // the iteration with `valid == false` and leaves its state untouched.
+  for (int base = s0 + warp * TPW; base < s1; base += GROUPS) {
+    const int t = base + lane / LPG;
+    const bool valid = t < s1;
+    uint4 kv = make_uint4(0u, 0u, 0u, 0u), vv4 = make_uint4(0u, 0u, 0u, 0u);
+    if (valid) {
+      const int page = pt[t / a.geom.page];
+      const int row = t % a.geom.page;
+      const __nv_bfloat16* kp = a.arena + a.geom.offset(a.layer, page, 0, h, row) + gl * 8;
+      const __nv_bfloat16* vp = kp + a.geom.kv_stride();
+      kv = *reinterpret_cast<const uint4*>(kp);
+      vv4 = *reinterpret_cast<const uint4*>(vp);
+    }
     const uint32_t kw[4] = {kv.x, kv.y, kv.z, kv.w};
     const uint32_t vw[4] = {vv4.x, vv4.y, vv4.z, vv4.w};
     float vf[8];
@@ -245,6 +253,7 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(DecodeAttnArgs a) {
       }
 #pragma unroll
       for (int o = LPG / 2; o > 0; o >>= 1) sc += __shfl_xor_sync(0xffffffffu, sc, o);
+      if (!valid) continue;
       const float mn = fmaxf(m[g], sc);
       const float al = fast_exp2(m[g] - mn);
       const float pp = fast_exp2(sc - mn);

@@ -163,6 +163,27 @@ __global__ void qkv_prefill_kernel(QkvPrefillArgs a) {
   }
 }
 
+// Re-push rows already stored in the local arena (slots [0, n) of `layer`, global positions
+// slot_pos[0..n)) into every rank's staging buffer: used when a continuation segment attends to a
+// session's existing KV (prompt + decoded tokens spread over the ranks).
+__global__ void stage_push_kernel(StagePushArgs a) {
+  const int slot = blockIdx.x;
+  if (slot >= a.n) return;
+  const int pos = a.slot_pos[slot];
+  if (pos < 0 || pos >= a.stage_cap) return;
+  const int page = a.page_table[slot / a.geom.page];
+  const int row = slot % a.geom.page;
+  const int Hkv = a.geom.hkv, D = a.geom.d, dvec = D / 8;
+  for (int i = threadIdx.x; i < 2 * Hkv * dvec; i += blockDim.x) {
+    const int kv = i / (Hkv * dvec), rem = i % (Hkv * dvec);
+    const int h = rem / dvec, e = rem % dvec;
+    const uint4 val = *reinterpret_cast<const uint4*>(a.arena + a.geom.offset(a.layer, page, kv, h, row) + e * 8);
+    const long soff = ((long)(kv * Hkv + h) * a.stage_cap + pos) * D + e * 8;
+    for (int r = 0; r < a.n_stage; ++r)
+      *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(a.stage_ptrs[r]) + soff) = val;
+  }
+}
+
 // Wait (bounded) until every peer has released the staging buffer parity we are about to write:
 // consumed[r] >= epoch - 2 for all ranks r. One CTA, one warp.
 __global__ void wait_consumed_kernel(const unsigned long long* consumed, int n,
@@ -257,6 +278,12 @@ const char* qkv_prefill(const QkvPrefillArgs& a, cudaStream_t s) {
   }
   qkv_prefill_kernel<<<a.T, 256, smem, s>>>(a);
   return cudaGetLastError() == cudaSuccess ? nullptr : "qkv_prefill: launch failed";
+}
+
+const char* stage_push(const StagePushArgs& a, cudaStream_t s) {
+  if (a.n == 0) return nullptr;
+  stage_push_kernel<<<a.n, 128, 0, s>>>(a);
+  return cudaGetLastError() == cudaSuccess ? nullptr : "stage_push: launch failed";
 }
 
 const char* wait_consumed(const unsigned long long* consumed, int n, unsigned long long need,

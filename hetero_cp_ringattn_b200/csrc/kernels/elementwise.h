@@ -56,12 +56,25 @@ struct QkvDecodeArgs {
   int* status;
 };
 
+struct StagePushArgs {
+  const __nv_bfloat16* arena;
+  ArenaGeom geom;
+  int layer;
+  const int* page_table;
+  const int* slot_pos;        // [n] global position of each stored slot
+  int n;
+  void* const* stage_ptrs;
+  int n_stage;
+  int stage_cap;
+};
+
 const char* embedding(const int* ids, const __nv_bfloat16* W, __nv_bfloat16* out, int T,
                       int hidden, int vocab, int* status, cudaStream_t s);
 const char* rmsnorm(const __nv_bfloat16* x, const __nv_bfloat16* w, __nv_bfloat16* y, int T,
                     int hidden, long ldx, long ldy, float eps, cudaStream_t s);
 const char* qkv_prefill(const QkvPrefillArgs& a, cudaStream_t s);
 const char* qkv_decode(const QkvDecodeArgs& a, cudaStream_t s);
+const char* stage_push(const StagePushArgs& a, cudaStream_t s);
 const char* wait_consumed(const unsigned long long* consumed, int n, unsigned long long need,
                           unsigned long long budget_ns, int* status, cudaStream_t s);
 const char* signal_peers(unsigned long long* const* ptrs, int n, unsigned long long epoch,

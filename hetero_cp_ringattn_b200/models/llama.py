@@ -40,6 +40,7 @@ from ..ops import reference as ref
 from ..ops._ext import native
 from ..parallel.schedule import FrozenKvAssigneeSchedule
 from ..parallel.strategy import RingStrategy, build_assignment, build_domain_positions
+from ..utils import launches
 from ..utils.perf import PerfLog
 from .weights import PreparedWeights
 
@@ -200,6 +201,7 @@ class LlamaCPEngine:
                     self.scale, True, q_buf, o_buf, None, self.prefill_epoch)
             self.rt.push_layer(*args)
             self.rt.attend_layer(*args)
+            launches.count(2 + (3 if self.world > 1 else 0) - (1 if self.world > 1 and self.prefill_epoch <= 2 else 0))
             del qkv
             K.gemm(o_buf.view(T, self.H * self.D), lw.wo, "residual", residual=x)
             K.rmsnorm(x, lw.post_norm, self.cfg.rms_norm_eps, out=xn)
@@ -220,6 +222,7 @@ class LlamaCPEngine:
             logits = torch.empty(1, self.cfg.vocab_size, dtype=torch.float32, device=dev)
             K.gemv(xl, self.w.lm_head, "argmax", y_f32=logits, argmax=am)
             native().argmax_finalize(am, None, tok)
+            launches.count()
         if self.world > 1:
             dist.broadcast(tok, src=st.owner_of_last, group=self.group)
             if return_logits:
@@ -344,6 +347,7 @@ class LlamaCPEngine:
         if B > self.max_batch or bucket > self.max_batch:
             raise CapacityError(f"decode batch {B} exceeds max_batch {self.max_batch}")
         g = self._graph_for(bucket)
+        self._last_bucket = bucket
         return g.run(req_ids, tokens, pos, owner, slot, ntok)
 
     def _decode_host(self, req_ids, tokens, pos, owner):
@@ -381,7 +385,140 @@ class LlamaCPEngine:
             x = x + ref.linear(K.swiglu_from_interleaved(ref.linear(h, lw.wgu)), lw.wd)
         xl = ref.rmsnorm(x, w.final_norm, cfg.rms_norm_eps)
         logits = ref.linear(xl, w.lm_head)
+        self._host_logits = logits
         return torch.argmax(logits, dim=-1)
+
+    def last_logits(self, n: int) -> Optional[torch.Tensor]:
+        """Logits [n, vocab] of the most recent decode step (for non-greedy sampling)."""
+        if self.cuda:
+            if not self._graphs:
+                return None
+            g = self._graphs.get(self._last_bucket)
+            return None if g is None else g.logits[:n]
+        return getattr(self, "_host_logits", None)
+
+    # ------------------------------------------------------------------ continuation (sessions)
+    def _segment_chunks(self, S: int, tickets: Sequence[int]) -> List[int]:
+        from ..parallel.capacity import allocate_by_capacity
+        if S >= self.world:
+            return allocate_by_capacity(S, list(tickets))
+        order = sorted(range(self.world), key=lambda r: (-int(tickets[r]), r))
+        out = [0] * self.world
+        for r in order[:S]:
+            out[r] = 1
+        return out
+
+    @torch.no_grad()
+    def append(self, req_id: int, tokens: torch.Tensor, position_ids: Sequence[int],
+               tickets: Sequence[int], return_logits: bool = False, extra_horizon: int = 128):
+        """Continuation segment on a kept session: the segment's KV is placed capacity-weighted
+        (vanilla split of the segment by `tickets`), existing KV never moves, and the segment's
+        queries attend to the whole session through the ring. Returns (next_token, logits)."""
+        st = self.reqs.get(req_id)
+        if st is None:
+            raise CapacityError(f"request {req_id} has no session KV on rank {self.rank}")
+        S = int(tokens.numel())
+        L0 = st.context_len
+        if list(position_ids) != list(range(L0, L0 + S)):
+            raise RingError(f"continuation positions must continue the session at {L0}")
+        if L0 + S > self.max_context:
+            raise CapacityError(f"session length {L0 + S} exceeds context capacity {self.max_context}")
+        seg = self._segment_chunks(S, tickets)
+        off = sum(seg[: self.rank])
+        T = seg[self.rank]
+        my_pos = np.arange(L0 + off, L0 + off + T, dtype=np.int64)
+        last_owner = max(r for r in range(self.world) if seg[r] > 0)
+        new_horizon = st.decode_offset + extra_horizon
+        sched_tab = self._schedule(req_id, tickets, new_horizon)
+        if self.cuda:
+            kv = st.kv
+            growth = int((sched_tab[st.decode_offset:] == self.rank).sum(0).max()) if extra_horizon else 0
+            self.kv.extend(req_id, T + growth)
+            kv.pt_device = torch.tensor(kv.pages, dtype=torch.int32, device=self.device)
+            tok, logits = self._append_cuda(st, tokens.to(self.device)[off:off + T].int(), my_pos,
+                                            L0 + S, last_owner, return_logits)
+            for li in range(self.L):
+                c = int(kv.layer_counts[li])
+                kv.slot_pos[li, c:c + T] = my_pos
+            kv.layer_counts += T
+        else:
+            tok, logits = self._append_host(st, tokens[off:off + T], my_pos, L0 + S, last_owner,
+                                            return_logits)
+        st.context_len = L0 + S
+        st.assignee = sched_tab
+        st.horizon = new_horizon
+        return tok, logits
+
+    def _append_cuda(self, st, ids, my_pos, Ltot, last_owner, return_logits):
+        w, dev = self.w, self.device
+        T = ids.numel()
+        pos = torch.from_numpy(my_pos.astype(np.int32)).to(dev)
+        kv = st.kv
+        x = K.embedding(ids, w.embed) if T else torch.empty(0, self.cfg.hidden_size, dtype=torch.bfloat16, device=dev)
+        xn = torch.empty_like(x)
+        q_buf = torch.empty(T, self.H, self.D, dtype=torch.bfloat16, device=dev)
+        o_buf = torch.empty_like(q_buf)
+        start_tile = int(my_pos[0]) // 128 if T else 0
+        empty_qkv = torch.empty(0, self.cfg.qkv_size, dtype=torch.bfloat16, device=dev)
+        for li, lw in enumerate(w.layers):
+            c = int(kv.layer_counts[li])
+            existing = torch.from_numpy(kv.slot_pos[li, :c].astype(np.int32)).to(dev)
+            if T:
+                K.rmsnorm(x, lw.in_norm, self.cfg.rms_norm_eps, out=xn)
+                qkv = K.gemm(xn, lw.wqkv, "bias" if lw.bqkv is not None else "store", bias=lw.bqkv)
+            else:
+                qkv = empty_qkv
+            self.prefill_epoch += 1
+            args = (qkv, pos, self.cos, self.sin, li, kv.pt_device, c, Ltot, start_tile, self.scale,
+                    True, q_buf, o_buf, None, self.prefill_epoch, existing)
+            self.rt.push_layer(*args)
+            self.rt.attend_layer(*args)
+            if T:
+                K.gemm(o_buf.view(T, self.H * self.D), lw.wo, "residual", residual=x)
+                K.rmsnorm(x, lw.post_norm, self.cfg.rms_norm_eps, out=xn)
+                g = K.gemm(xn, lw.wgu, "swiglu")
+                K.gemm(g, lw.wd, "residual", residual=x)
+        st_last = dataclasses.replace(st, positions=my_pos, prompt_len=Ltot, owner_of_last=last_owner)
+        return self._first_token_cuda(st_last, x, return_logits)
+
+    def _append_host(self, st, ids, my_pos, Ltot, last_owner, return_logits):
+        w, cfg = self.w, self.cfg
+        T = ids.numel()
+        pos = torch.from_numpy(my_pos)
+        x = w.embed[ids.long()].float()
+        for li, lw in enumerate(w.layers):
+            kv = st.host_kv[li]
+            if T:
+                h = ref.rmsnorm(x, lw.in_norm, cfg.rms_norm_eps)
+                qkv = ref.linear(h, lw.wqkv, lw.bqkv)
+                q = ref.apply_rope(qkv[:, : self.H * self.D].view(T, self.H, self.D), pos, cfg.rope_theta)
+                k = ref.apply_rope(qkv[:, self.H * self.D:(self.H + self.Hkv) * self.D].view(T, self.Hkv, self.D),
+                                   pos, cfg.rope_theta)
+                v = qkv[:, (self.H + self.Hkv) * self.D:].reshape(T, self.Hkv, self.D)
+                kv[0] = torch.cat([kv[0], k])
+                kv[1] = torch.cat([kv[1], v])
+                kv[2] = torch.cat([kv[2], pos])
+            ks, vs, ps = self._gather_rows(kv[0]), self._gather_rows(kv[1]), self._gather_rows(kv[2])
+            if T:
+                kk = torch.zeros(Ltot, self.Hkv, self.D, dtype=torch.float32)
+                vv = torch.zeros_like(kk)
+                for a, b, p in zip(ks, vs, ps):
+                    kk[p] = a.float()
+                    vv[p] = b.float()
+                o, _ = ref.full_attention(q, kk, vv, pos, torch.arange(Ltot), causal=True)
+                x = x + ref.linear(o.reshape(T, self.H * self.D), lw.wo)
+                h = ref.rmsnorm(x, lw.post_norm, cfg.rms_norm_eps)
+                x = x + ref.linear(K.swiglu_from_interleaved(ref.linear(h, lw.wgu)), lw.wd)
+        tok = torch.zeros(1, dtype=torch.int64)
+        logits = torch.zeros(cfg.vocab_size, dtype=torch.float32)
+        if self.rank == last_owner:
+            xl = ref.rmsnorm(x[-1:], w.final_norm, cfg.rms_norm_eps)
+            logits = ref.linear(xl, w.lm_head)[0].float()
+            tok[0] = int(torch.argmax(logits))
+        if self.world > 1:
+            dist.broadcast(tok, src=last_owner, group=self.group)
+            dist.broadcast(logits, src=last_owner, group=self.group)
+        return tok, (logits if return_logits else None)
 
     # ------------------------------------------------------------------ release / generate
     def release(self, req_id: int) -> bool:
@@ -457,6 +594,7 @@ class DecodeGraph:
         rt = e.rt
         nat = native()
         nat.add_u64(e.dec_step, 1)
+        launches.count()
         K.embedding(self.tokens, w.embed, out=self.x)
         for li, lw in enumerate(w.layers):
             K.rmsnorm(self.x, lw.in_norm, cfg.rms_norm_eps, out=self.xn)
@@ -465,6 +603,7 @@ class DecodeGraph:
             rt.decode_attn(self.q, li, self.pt, self.ntok[li], e.scale, self.splits, self.part_o,
                            self.part_l, self.counters, e.dec_step, e.L, li + 1)
             rt.decode_combine(self.o, self.B, e.H, e.dec_step, e.L, li + 1)
+            launches.count(3)
             K.gemv(self.o, lw.wo, "residual", y_bf16=self.x)
             K.rmsnorm(self.x, lw.post_norm, cfg.rms_norm_eps, out=self.xn)
             K.gemv(self.xn, lw.wgu, "swiglu", y_bf16=self.g)
@@ -473,6 +612,7 @@ class DecodeGraph:
         nat.fill_u64(self.am, 0)
         K.gemv(self.xn, w.lm_head, "argmax", y_f32=self.logits, argmax=self.am)
         nat.argmax_finalize(self.am, self.tokens, self.out_tok)
+        launches.count(2)
 
     def run(self, req_ids, tokens, pos, owner, slot, ntok) -> torch.Tensor:
         n = len(req_ids)
@@ -510,7 +650,10 @@ class DecodeGraph:
                 # attributes, so the graph is captured directly (no eager warm-up step, which
                 # would advance the cross-rank exchange epochs and overwrite `tokens`)
                 self.graph = torch.cuda.CUDAGraph()
-                with torch.cuda.graph(self.graph):
-                    self.body()
+                with launches.capture() as cap:
+                    with torch.cuda.graph(self.graph):
+                        self.body()
+                self.graph_launches = cap.launches
             self.graph.replay()
+            launches.count(self.graph_launches)
         return self.out_tok[:n].clone()

@@ -13,6 +13,7 @@ import torch
 
 from . import reference as ref
 from ._ext import native
+from ..utils import launches
 
 EPI = {"store": 0, "bias": 1, "residual": 2, "swiglu": 3}
 GEMV = {"f32": 0, "residual": 1, "swiglu": 2, "argmax": 3}
@@ -74,6 +75,7 @@ def gemm(a: torch.Tensor, w: torch.Tensor, epi: str = "store", bias: Optional[to
         out = residual if (epi == "residual" and residual is not None) else torch.empty(
             m, n_out, dtype=a.dtype, device=a.device)
     native().gemm(a, w, out, EPI[epi], bias, residual, status)
+    launches.count()
     return out
 
 
@@ -95,6 +97,7 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, q_pos: torch.Te
     o = torch.empty_like(q)
     lse = torch.empty(h, t, dtype=torch.float32, device=q.device) if want_lse else None
     native().attn_fwd(q, k, v, o, lse, q_pos, L, k.stride(0), scale, causal, kv_start_tile, status)
+    launches.count()
     return o, lse
 
 
@@ -109,6 +112,7 @@ def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float, out: Optional[torch.Te
     if out is None:
         out = torch.empty_like(x)
     native().rmsnorm(x, w, out, eps)
+    launches.count()
     return out
 
 
@@ -119,6 +123,7 @@ def embedding(ids: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = 
     if out is None:
         out = torch.empty(ids.numel(), w.shape[1], dtype=w.dtype, device=w.device)
     native().embedding(ids, w, out, status)
+    launches.count()
     return out
 
 
@@ -143,4 +148,5 @@ def gemv(x: torch.Tensor, w: torch.Tensor, epi: str, bias=None, y_f32=None, y_bf
                 y_f32.copy_(y)
             return y.argmax(-1)
     native().gemv(x, w, GEMV[epi], bias, y_f32, y_bf16, argmax)
+    launches.count()
     return y_bf16 if y_bf16 is not None else y_f32

@@ -1,0 +1,302 @@
+"""Coordinator: request admission, chunking, KV byte ledger, sessions, iterative decode batching.
+
+Parity: rust/src/distributed/coordinator.rs:
+  * chunk selection (:900-960): explicit `--chunk-sizes`, `--capacity-aware` (handshake capacities
+    minus `--activation-reserve-mb`, default 1536), else equal splits; plus ratio overrides;
+  * ring strategy (:57-74, :962);
+  * KV byte admission with a per-domain ledger and rollback on failure (:784-871, :1678);
+  * sessions: `keep_kv` keeps a finished request's KV, `append` continues it (:1246-1407,
+    :1746-1822), with `--session-continuation-tokens` of headroom (:1719-1730);
+  * iterative scheduling (:2563-2916): pending -> prefill -> active, one decode step per iteration
+    for every active request (batched), streaming deltas, stop on EOS / max_tokens;
+  * trace JSONL (:621-782): enqueue / prefill-accepted / first-token / completed timestamps,
+    reserved / released KV bytes.
+It runs inside rank 0's process; every engine step is issued to all ranks over the control plane.
+"""
+
+from __future__ import annotations
+
+import dataclasses
+import itertools
+import json
+import logging
+import threading
+import time
+from typing import Dict, List, Optional, Sequence
+
+from ..errors import CapacityError, ProtocolError
+from ..models.sampling import sample_token
+from ..parallel.capacity import (DEFAULT_ACTIVATION_RESERVE_MB, KvLedger, UNKNOWN_CAPACITY,
+                                 chunk_sizes)
+from . import protocol as P
+from .scheduler import ActiveRequest, BatchScheduler, Job
+
+log = logging.getLogger("hcp.coordinator")
+
+
+@dataclasses.dataclass
+class CoordinatorArgs:
+    strategy: str = "vanilla"
+    chunk_sizes: Optional[List[int]] = None
+    capacity_aware: bool = False
+    ratio: Optional[List[int]] = None
+    max_batch_size: int = 4
+    activation_reserve_mb: int = DEFAULT_ACTIVATION_RESERVE_MB
+    session_continuation_tokens: int = 64
+    trace_jsonl: Optional[str] = None
+    eos_ids: Optional[List[int]] = None
+
+
+class TraceSink:
+    def __init__(self, path: Optional[str]):
+        self.path = path
+        self.lock = threading.Lock()
+
+    def emit(self, kind: str, **kw) -> None:
+        if not self.path:
+            return
+        with self.lock, open(self.path, "a") as f:
+            f.write(json.dumps({"ts": time.time(), "event": kind, **kw}) + "\n")
+
+
+@dataclasses.dataclass
+class Session:
+    request_id: int
+    context_len: int
+    chunks: List[int]
+    last_token: int
+
+
+class Metrics:
+    def __init__(self):
+        self.total = 0
+        self.completed = 0
+        self.failed = 0
+        self.lock = threading.Lock()
+
+    def bump(self, field: str, n: int = 1) -> None:
+        with self.lock:
+            setattr(self, field, getattr(self, field) + n)
+
+
+class Coordinator:
+    def __init__(self, worker, control: P.ControlPlane, tokenizer, cfg, args: CoordinatorArgs,
+                 capacities_mb: Optional[Sequence[int]] = None):
+        self.worker = worker
+        self.control = control
+        self.tok = tokenizer
+        self.cfg = cfg
+        self.args = args
+        self.world = control.world
+        self.sched = BatchScheduler(args.max_batch_size)
+        self.trace = TraceSink(args.trace_jsonl)
+        self.metrics = Metrics()
+        self.sessions: Dict[str, Session] = {}
+        self._ids = itertools.count(1)
+        caps = list(capacities_mb) if capacities_mb else [UNKNOWN_CAPACITY] * self.world
+        self.capacities_mb = caps
+        budgets = []
+        for c in caps:
+            if c == UNKNOWN_CAPACITY:
+                budgets.append(1 << 62)
+            else:
+                budgets.append(max(0, int(c) - args.activation_reserve_mb) * 1024 * 1024)
+        self.ledger = KvLedger(budgets)
+        self.bytes_per_token_layer = cfg.kv_bytes_per_token_per_layer(2)
+        self._stop = threading.Event()
+        self.lock = threading.Lock()   # serialises engine steps issued by API threads
+
+    # ------------------------------------------------------------------ submission
+    def next_request_id(self) -> int:
+        return next(self._ids)
+
+    def submit(self, job: Job) -> None:
+        self.metrics.bump("total")
+        if job.append or job.keep_kv:
+            if not job.session_id:
+                raise ProtocolError(("append" if job.append else "keep_kv") + "=true requires session_id")
+        if job.append and job.session_id not in self.sessions:
+            raise ProtocolError(f"unknown or expired session {job.session_id!r}")
+        self.trace.emit("enqueue", request=job.request_id, prompt_tokens=len(job.prompt_ids))
+        self.sched.enqueue(job)
+
+    # ------------------------------------------------------------------ engine commands
+    def run_command(self, cmd):
+        with self.lock:
+            self.control.broadcast(cmd)
+            resp = self.worker.execute(cmd)
+            all_resp = self.control.gather(resp)
+        errs = [r for r in (all_resp or [resp]) if isinstance(r, P.Error)]
+        if errs:
+            raise ProtocolError("; ".join(f"rank error: {e.message}" for e in errs))
+        return resp
+
+    def shutdown(self) -> None:
+        self._stop.set()
+        with self.lock:
+            self.control.broadcast(P.Shutdown())
+
+    # ------------------------------------------------------------------ admission
+    def _chunks(self, n: int) -> List[int]:
+        return chunk_sizes(n, self.world, explicit=self.args.chunk_sizes,
+                           capacities_mb=self.capacities_mb, capacity_aware=self.args.capacity_aware,
+                           ratio=self.args.ratio, activation_reserve_mb=self.args.activation_reserve_mb)
+
+    def _tickets(self, chunks: Sequence[int]) -> List[int]:
+        if self.args.ratio:
+            return list(self.args.ratio)
+        return [max(1, c) for c in chunks]
+
+    def _reserve(self, rid: int, chunks: Sequence[int], horizon: int) -> List[int]:
+        tickets = self._tickets(chunks)
+        tot = sum(tickets)
+        per = []
+        for c, t in zip(chunks, tickets):
+            growth = -(-horizon * t // tot) + 1
+            per.append((c + growth) * self.cfg.num_layers * self.bytes_per_token_layer)
+        self.ledger.try_reserve(rid, per)
+        self.trace.emit("kv_reserved", request=rid, bytes=per)
+        return per
+
+    def _prefill(self, job: Job) -> None:
+        rid = job.request_id
+        if job.append:
+            return self._append(job)
+        chunks = self._chunks(len(job.prompt_ids))
+        horizon = max(1, job.max_tokens) + (self.args.session_continuation_tokens if job.keep_kv else 0)
+        self._reserve(rid, chunks, horizon)
+        try:
+            resp = self.run_command(P.Prefill(rid, list(job.prompt_ids), chunks, self.args.strategy,
+                                              horizon, self._tickets(chunks), job.keep_kv))
+        except Exception:
+            self.ledger.release(rid)
+            raise
+        self.trace.emit("prefill_accepted", request=rid, chunks=chunks,
+                        hops_per_prefill=self.cfg.num_layers * max(0, self.world - 1))
+        req = ActiveRequest(job=job, chunks=chunks, next_position=len(job.prompt_ids))
+        self._emit_token(req, resp.token)
+
+    def _append(self, job: Job) -> None:
+        sess = self.sessions[job.session_id]
+        rid = sess.request_id
+        n = len(job.prompt_ids)
+        positions = list(range(sess.context_len, sess.context_len + n))
+        resp = self.run_command(P.StationaryContinuation(rid, list(job.prompt_ids), positions,
+                                                         self._tickets(sess.chunks), 0))
+        job.request_id = rid
+        req = ActiveRequest(job=job, chunks=sess.chunks, next_position=sess.context_len + n)
+        self._emit_token(req, resp.token)
+
+    def _emit_token(self, req: ActiveRequest, argmax_token: int) -> None:
+        job = req.job
+        tok = argmax_token
+        if job.temperature > 0 and self.worker.last_logits is not None:
+            logits = self.worker.last_logits
+            tok = sample_token(logits[0] if logits.dim() > 1 else logits, job.temperature, job.top_p)
+        req.generated.append(tok)
+        req.next_token = tok
+        if req.first_token_at is None:
+            req.first_token_at = time.time()
+            self.trace.emit("first_token", request=job.request_id,
+                            ttft_s=req.first_token_at - job.enqueued_at)
+        eos = set(job.stop_ids or self.args.eos_ids or [])
+        if tok in eos:
+            req.finish_reason = "stop"
+        elif len(req.generated) >= job.max_tokens:
+            req.finish_reason = "length"
+        if job.on_token:
+            job.on_token(tok, req.finish_reason)
+        if req.finish_reason:
+            self._finish(req)
+        elif job.request_id not in self.sched.active:
+            self.sched.activate(req)
+
+    def _finish(self, req: ActiveRequest) -> None:
+        job = req.job
+        self.sched.complete(job.request_id)
+        if job.keep_kv or job.append:
+            ctx = req.next_position + len(req.generated) - 1
+            self.sessions[job.session_id] = Session(job.request_id, ctx, req.chunks, req.next_token)
+            # the last generated token has no KV yet: the next append starts with it
+        else:
+            self.run_command(P.ReleaseRequest(job.request_id))
+            released = self.ledger.release(job.request_id)
+            self.trace.emit("kv_released", request=job.request_id, bytes=released)
+        self.metrics.bump("completed")
+        self.trace.emit("completed", request=job.request_id, completion_tokens=len(req.generated),
+                        finish_reason=req.finish_reason,
+                        decode_hops=self.cfg.num_layers * max(0, self.world - 1) * max(0, len(req.generated) - 1))
+        if job.done:
+            job.done({"request_id": job.request_id, "tokens": list(req.generated),
+                      "prompt_tokens": len(job.prompt_ids), "finish_reason": req.finish_reason})
+
+    def _fail(self, job: Job, err: Exception) -> None:
+        self.metrics.bump("failed")
+        self.sched.complete(job.request_id)
+        if not job.append:
+            self.ledger.release(job.request_id)
+        self.trace.emit("failed", request=job.request_id, error=str(err))
+        if job.done:
+            job.done({"request_id": job.request_id, "error": str(err)})
+
+    # ------------------------------------------------------------------ iteration
+    def iteration(self) -> bool:
+        did = False
+        while self.sched.has_capacity():
+            job = self.sched.pop_pending()
+            if job is None:
+                break
+            did = True
+            try:
+                self._prefill(job)
+            except CapacityError as e:
+                if self.sched.active:
+                    self.sched.requeue_front(job)   # wait for KV to be released
+                    break
+                self._fail(job, e)
+            except Exception as e:
+                self._fail(job, e)
+        active = self.sched.active_list()
+        if active:
+            did = True
+            pairs = [[a.job.request_id, a.next_token] for a in active]
+            try:
+                resp = self.run_command(P.DecodeBatch(pairs))
+            except Exception as e:
+                for a in active:
+                    self._fail(a.job, e)
+                return did
+            logits = self.worker.last_logits
+            for i, (a, (_, tok)) in enumerate(zip(active, resp.request_tokens)):
+                if a.job.temperature > 0 and logits is not None:
+                    tok = sample_token(logits[i], a.job.temperature, a.job.top_p)
+                a.generated.append(tok)
+                a.next_token = tok
+                eos = set(a.job.stop_ids or self.args.eos_ids or [])
+                if tok in eos:
+                    a.finish_reason = "stop"
+                elif len(a.generated) >= a.job.max_tokens:
+                    a.finish_reason = "length"
+                if a.job.on_token:
+                    a.job.on_token(tok, a.finish_reason)
+                if a.finish_reason:
+                    self._finish(a)
+        return did
+
+    def run_forever(self) -> None:
+        while not self._stop.is_set():
+            if not self.iteration():
+                self.sched.wait_for_work(0.02)
+
+    # ------------------------------------------------------------------ convenience (CLI batch)
+    def generate(self, prompt_ids: Sequence[int], max_tokens: int = 20, temperature: float = 0.0,
+                 top_p: float = 1.0, session_id=None, keep_kv=False, append=False) -> dict:
+        out = {}
+        job = Job(request_id=self.next_request_id(), prompt_ids=list(prompt_ids),
+                  max_tokens=max_tokens, temperature=temperature, top_p=top_p,
+                  session_id=session_id, keep_kv=keep_kv, append=append,
+                  done=lambda r: out.update(r))
+        self.submit(job)
+        while not out:
+            self.iteration()
+        return out

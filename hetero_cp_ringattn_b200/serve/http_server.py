@@ -1,0 +1,178 @@
+"""OpenAI-style HTTP API: POST /v1/completions (+ SSE streaming), GET /health, GET /metrics.
+
+Parity: rust/src/api/server.rs:39-205 and api/types.rs:4-142: request fields (`model`, `prompt`,
+`max_tokens` default 20, `temperature` 0.0, `top_p` 1.0, `stream`, `stop`, `session_id`,
+`keep_kv`, `append`), fail-closed session validation (append / keep_kv require session_id ->
+400), `text_completion` responses with usage, SSE chunks terminated by `data: [DONE]`,
+`/health` {status, workers_connected, num_domains} and `/metrics` {total, completed, failed,
+queued, active}. Served by the standard library's threaded HTTP server (no extra dependency).
+"""
+
+from __future__ import annotations
+
+import json
+import queue
+import threading
+import time
+from http.server import BaseHTTPRequestHandler, ThreadingHTTPServer
+from typing import Optional
+
+from ..errors import ProtocolError
+from .scheduler import Job
+
+
+def validate_session_fields(body: dict) -> Optional[str]:
+    if body.get("append") and not body.get("session_id"):
+        return "append=true requires session_id"
+    if body.get("keep_kv") and not body.get("session_id"):
+        return "keep_kv=true requires session_id"
+    return None
+
+
+class ApiState:
+    def __init__(self, coordinator, tokenizer, model_name: str, num_domains: int):
+        self.coord = coordinator
+        self.tok = tokenizer
+        self.model_name = model_name
+        self.num_domains = num_domains
+        self.workers_connected = num_domains
+
+
+def make_handler(state: ApiState):
+    class Handler(BaseHTTPRequestHandler):
+        protocol_version = "HTTP/1.1"
+
+        def log_message(self, fmt, *args):  # quiet
+            pass
+
+        def _json(self, code: int, obj) -> None:
+            data = json.dumps(obj).encode()
+            self.send_response(code)
+            self.send_header("Content-Type", "application/json")
+            self.send_header("Content-Length", str(len(data)))
+            self.send_header("Access-Control-Allow-Origin", "*")
+            self.end_headers()
+            self.wfile.write(data)
+
+        def _text(self, code: int, msg: str) -> None:
+            data = msg.encode()
+            self.send_response(code)
+            self.send_header("Content-Type", "text/plain; charset=utf-8")
+            self.send_header("Content-Length", str(len(data)))
+            self.end_headers()
+            self.wfile.write(data)
+
+        def do_GET(self):
+            if self.path == "/health":
+                return self._json(200, {"status": "ok", "workers_connected": state.workers_connected,
+                                        "num_domains": state.num_domains})
+            if self.path == "/metrics":
+                m = state.coord.metrics
+                return self._json(200, {"total_requests": m.total, "completed_requests": m.completed,
+                                        "failed_requests": m.failed,
+                                        "queued_requests": state.coord.sched.queued,
+                                        "active_requests": len(state.coord.sched.active)})
+            return self._text(404, "not found")
+
+        def do_POST(self):
+            if self.path != "/v1/completions":
+                return self._text(404, "not found")
+            n = int(self.headers.get("Content-Length", "0"))
+            try:
+                body = json.loads(self.rfile.read(n) or b"{}")
+            except json.JSONDecodeError as e:
+                return self._text(400, f"invalid JSON: {e}")
+            if not isinstance(body.get("prompt"), str):
+                return self._text(422, "prompt (string) is required")
+            err = validate_session_fields(body)
+            coord = state.coord
+            if err:
+                coord.metrics.bump("total")
+                coord.metrics.bump("failed")
+                return self._text(400, err)
+            rid = coord.next_request_id()
+            created = int(time.time())
+            model = body.get("model") or state.model_name
+            ids = state.tok.encode(body["prompt"])
+            stop_ids = None
+            if body.get("stop"):
+                stop_ids = [i for s in body["stop"] for i in state.tok.encode(s)[:1]]
+            events: "queue.Queue" = queue.Queue()
+            job = Job(request_id=rid, prompt_ids=ids, max_tokens=int(body.get("max_tokens", 20)),
+                      temperature=float(body.get("temperature", 0.0)),
+                      top_p=float(body.get("top_p", 1.0)), session_id=body.get("session_id"),
+                      keep_kv=bool(body.get("keep_kv", False)), append=bool(body.get("append", False)),
+                      stop_ids=stop_ids,
+                      on_token=lambda t, fr: events.put(("tok", t, fr)),
+                      done=lambda r: events.put(("done", r, None)))
+            try:
+                coord.submit(job)
+            except ProtocolError as e:
+                coord.metrics.bump("failed")
+                return self._text(400, str(e))
+            if body.get("stream"):
+                return self._stream(rid, created, model, events)
+            toks = []
+            while True:
+                kind, a, b = events.get()
+                if kind == "done":
+                    res = a
+                    break
+            if "error" in res:
+                return self._text(500, res["error"])
+            text = state.tok.decode(res["tokens"])
+            pt, ct = res["prompt_tokens"], len(res["tokens"])
+            return self._json(200, {
+                "id": f"hcp-completion-{rid}", "object": "text_completion", "created": created,
+                "model": model,
+                "choices": [{"text": text, "index": 0, "logprobs": None,
+                             "finish_reason": res["finish_reason"]}],
+                "usage": {"prompt_tokens": pt, "completion_tokens": ct, "total_tokens": pt + ct}})
+
+        def _stream(self, rid, created, model, events):
+            self.send_response(200)
+            self.send_header("Content-Type", "text/event-stream")
+            self.send_header("Cache-Control", "no-cache")
+            self.send_header("Connection", "close")
+            self.end_headers()
+
+            def send(data: str):
+                self.wfile.write(f"data: {data}\n\n".encode())
+                self.wfile.flush()
+
+            while True:
+                kind, a, b = events.get()
+                if kind == "tok":
+                    chunk = {"id": f"hcp-completion-{rid}", "object": "text_completion",
+                             "created": created, "model": model,
+                             "choices": [{"text": state.tok.decode([a]), "index": 0,
+                                          "finish_reason": b}]}
+                    send(json.dumps(chunk))
+                elif kind == "done":
+                    if "error" in a:
+                        send(json.dumps({"error": a["error"]}))
+                    break
+            send("[DONE]")
+            self.close_connection = True
+
+    return Handler
+
+
+class ApiServer:
+    def __init__(self, state: ApiState, host: str = "127.0.0.1", port: int = 0):
+        self.httpd = ThreadingHTTPServer((host, port), make_handler(state))
+        self.httpd.daemon_threads = True
+        self.thread = None
+
+    @property
+    def port(self) -> int:
+        return self.httpd.server_address[1]
+
+    def start(self) -> "ApiServer":
+        self.thread = threading.Thread(target=self.httpd.serve_forever, daemon=True)
+        self.thread.start()
+        return self
+
+    def stop(self) -> None:
+        self.httpd.shutdown()
+        self.httpd.server_close()

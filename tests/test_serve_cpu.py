@@ -1,0 +1,167 @@
+"""Control protocol, scheduler, coordinator and HTTP API on a single CPU rank.
+
+Parity: rust/src/distributed/protocol.rs:555-763 (validators, frames), scheduler.rs:171-420,
+api/server.rs:211-438 (API contract incl. SSE [DONE], /health, /metrics), api/types.rs:159-214
+(session field validation), worker_sdk/tch_backend.rs:1765 (decode after release fails).
+"""
+
+import json
+import threading
+import urllib.error
+import urllib.request
+
+import pytest
+import torch
+
+from hetero_cp_ringattn_b200.config import preset
+from hetero_cp_ringattn_b200.errors import ProtocolError
+from hetero_cp_ringattn_b200.models import reference_model
+from hetero_cp_ringattn_b200.models.llama import LlamaCPEngine
+from hetero_cp_ringattn_b200.models.weights import ModelWeights, PreparedWeights
+from hetero_cp_ringattn_b200.serve import protocol as P
+from hetero_cp_ringattn_b200.serve.coordinator import Coordinator, CoordinatorArgs
+from hetero_cp_ringattn_b200.serve.http_server import ApiServer, ApiState
+from hetero_cp_ringattn_b200.serve.scheduler import BatchScheduler, Job
+from hetero_cp_ringattn_b200.serve.tokenizer import ByteTokenizer
+from hetero_cp_ringattn_b200.serve.worker import Worker
+
+
+def test_protocol_roundtrip_and_partial_frames():
+    for msg in [P.Prefill(1, [1, 2, 3], [2, 1], "zigzag", 8, [5, 1], True), P.Decode(3, 7),
+                P.DecodeBatch([[1, 2], [3, 4]]), P.StationaryDecode(1, 2, 3, [1, 1], 0, 0, 4),
+                P.ReleaseRequest(9), P.Shutdown(), P.PrefillDone(1, 5, 3), P.Error(1, "x")]:
+        frame = P.encode(msg)
+        assert P.decode(frame) == msg
+        with pytest.raises(ProtocolError):
+            P.decode(frame[:-1])
+    with pytest.raises(ProtocolError):
+        P.decode(b"\x00\x00\x00\x05{\"ty")
+    hs = P.pack_handshake(3, 4096)
+    assert len(hs) == 16 and P.unpack_handshake(hs) == (3, 4096)
+
+
+def test_validators():
+    P.validate_stationary_decode(2, [1, 1], 1, 0, 4)
+    for args in [(0, [], 0, 0, 1), (2, [1], 0, 0, 1), (2, [0, 0], 0, 0, 1), (2, [1, 1], 2, 0, 1),
+                 (2, [1, 1], 0, 0, 0), (2, [1, 1], 0, 4, 4)]:
+        with pytest.raises(ProtocolError):
+            P.validate_stationary_decode(*args)
+    P.validate_stationary_continuation(2, [1, 2], [5, 6], [1, 1], 0)
+    for args in [(2, [], [], [1, 1], 0), (2, [1], [1, 2], [1, 1], 0), (2, [1], [1], [1], 0),
+                 (2, [1], [1], [0, 0], 0), (2, [1], [1], [1, 1], 3)]:
+        with pytest.raises(ProtocolError):
+            P.validate_stationary_continuation(*args)
+
+
+def test_scheduler_fifo_and_capacity():
+    s = BatchScheduler(max_batch_size=2)
+    for i in range(3):
+        s.enqueue(Job(request_id=i, prompt_ids=[1]))
+    from hetero_cp_ringattn_b200.serve.scheduler import ActiveRequest
+    a = s.pop_pending()
+    s.activate(ActiveRequest(job=a, chunks=[1]))
+    b = s.pop_pending()
+    s.activate(ActiveRequest(job=b, chunks=[1]))
+    assert (a.request_id, b.request_id) == (0, 1)
+    assert s.pop_pending() is None  # full
+    s.complete(0)
+    assert s.pop_pending().request_id == 2
+    with pytest.raises(ValueError):
+        BatchScheduler(0)
+
+
+@pytest.fixture(scope="module")
+def stack():
+    cfg = preset("tiny")
+    w = ModelWeights.random_init(cfg, seed=0, dtype=torch.float32, std=0.2)
+    pw = PreparedWeights.from_weights(w, dtype=torch.float32)
+    eng = LlamaCPEngine(cfg, pw, device=torch.device("cpu"), max_context=512)
+    control = P.ControlPlane()
+    worker = Worker(eng, control)
+    tok = ByteTokenizer(cfg.vocab_size)
+    coord = Coordinator(worker, control, tok, cfg, CoordinatorArgs(max_batch_size=4))
+    return cfg, w, eng, coord, tok
+
+
+def test_coordinator_generate_matches_reference(stack):
+    cfg, w, eng, coord, tok = stack
+    ids = tok.encode("hello heterogeneous ring")
+    res = coord.generate(ids, max_tokens=5)
+    ref_tokens, _ = reference_model.greedy_generate(w, torch.tensor(ids), 4)
+    assert res["tokens"] == ref_tokens
+    assert res["finish_reason"] == "length"
+    assert not eng.reqs  # released
+
+
+def test_coordinator_batches_concurrent_requests(stack):
+    cfg, w, eng, coord, tok = stack
+    outs = {}
+    jobs = []
+    for i, text in enumerate(["abc", "a much longer prompt here", "xyz!"]):
+        ids = tok.encode(text)
+        jobs.append((ids, i))
+        coord.submit(Job(request_id=coord.next_request_id(), prompt_ids=ids, max_tokens=4,
+                         done=lambda r, i=i: outs.__setitem__(i, r)))
+    while len(outs) < 3:
+        coord.iteration()
+    for ids, i in jobs:
+        ref_tokens, _ = reference_model.greedy_generate(w, torch.tensor(ids), 3)
+        assert outs[i]["tokens"] == ref_tokens
+
+
+def test_decode_after_release_fails(stack):
+    cfg, w, eng, coord, tok = stack
+    r = coord.worker.execute(P.Prefill(999, [1, 2, 3], [3], "vanilla", 4))
+    assert isinstance(r, P.PrefillDone)
+    assert isinstance(coord.worker.execute(P.ReleaseRequest(999)), P.Ack)
+    r = coord.worker.execute(P.DecodeBatch([[999, r.token]]))
+    assert isinstance(r, P.Error)
+
+
+def _post(port, body, raw=False):
+    req = urllib.request.Request(f"http://127.0.0.1:{port}/v1/completions",
+                                 data=json.dumps(body).encode(),
+                                 headers={"Content-Type": "application/json"})
+    with urllib.request.urlopen(req, timeout=60) as r:
+        data = r.read().decode()
+    return data if raw else json.loads(data)
+
+
+def test_http_api(stack):
+    cfg, w, eng, coord, tok = stack
+    stop = threading.Event()
+    loop = threading.Thread(target=lambda: [coord.iteration() or stop.wait(0.005) for _ in iter(stop.is_set, True)],
+                            daemon=True)
+    loop.start()
+    srv = ApiServer(ApiState(coord, tok, "tiny", 1)).start()
+    try:
+        with urllib.request.urlopen(f"http://127.0.0.1:{srv.port}/health", timeout=10) as r:
+            h = json.loads(r.read())
+        assert h == {"status": "ok", "workers_connected": 1, "num_domains": 1}
+        res = _post(srv.port, {"prompt": "ring attention", "max_tokens": 4})
+        assert res["object"] == "text_completion"
+        assert res["usage"]["completion_tokens"] == 4
+        assert res["usage"]["total_tokens"] == res["usage"]["prompt_tokens"] + 4
+        ids = tok.encode("ring attention")
+        ref_tokens, _ = reference_model.greedy_generate(w, torch.tensor(ids), 3)
+        assert res["choices"][0]["text"] == tok.decode(ref_tokens)
+        sse = _post(srv.port, {"prompt": "ring attention", "max_tokens": 3, "stream": True}, raw=True)
+        events = [ln[6:] for ln in sse.split("\n") if ln.startswith("data: ")]
+        assert events[-1] == "[DONE]"
+        chunks = [json.loads(e) for e in events[:-1]]
+        assert len(chunks) == 3 and chunks[-1]["choices"][0]["finish_reason"] == "length"
+        with pytest.raises(urllib.error.HTTPError) as ei:
+            _post(srv.port, {"prompt": "x", "append": True})
+        assert ei.value.code == 400
+        with pytest.raises(urllib.error.HTTPError) as ei:
+            _post(srv.port, {"prompt": "x", "keep_kv": True})
+        assert ei.value.code == 400
+        with urllib.request.urlopen(f"http://127.0.0.1:{srv.port}/metrics", timeout=10) as r:
+            m = json.loads(r.read())
+        assert m["completed_requests"] >= 2 and m["failed_requests"] >= 2
+        assert set(m) == {"total_requests", "completed_requests", "failed_requests",
+                          "queued_requests", "active_requests"}
+    finally:
+        srv.stop()
+        stop.set()
+        loop.join(timeout=5)
