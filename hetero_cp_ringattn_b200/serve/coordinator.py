@@ -179,9 +179,12 @@ class Coordinator:
     def _append(self, job: Job) -> None:
         sess = self.sessions[job.session_id]
         rid = sess.request_id
-        n = len(job.prompt_ids)
+        # the session's last generated token was never fed back, so it has no KV yet: it leads
+        # the continuation segment
+        seg = [sess.last_token] + list(job.prompt_ids)
+        n = len(seg)
         positions = list(range(sess.context_len, sess.context_len + n))
-        resp = self.run_command(P.StationaryContinuation(rid, list(job.prompt_ids), positions,
+        resp = self.run_command(P.StationaryContinuation(rid, seg, positions,
                                                          self._tickets(sess.chunks), 0))
         job.request_id = rid
         req = ActiveRequest(job=job, chunks=sess.chunks, next_position=sess.context_len + n)

@@ -110,3 +110,57 @@ def test_gloo_ranks_match_single_device(chunks, strategy, tickets):
         res = torch.load(out)
     assert (res["logits"] - ref_logits[0]).abs().max() < 1e-4
     assert res["tokens"] == ref_tokens
+
+
+def _session_worker(rank, world, port, out_path):
+    if world > 1:
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        cfg, w = tiny_weights()
+        pw = PreparedWeights.from_weights(w, dtype=torch.float32)
+        eng = LlamaCPEngine(cfg, pw, rank=rank, world=world, device=torch.device("cpu"), max_context=256)
+        g = torch.Generator().manual_seed(11)
+        a = torch.randint(0, cfg.vocab_size, (23,), generator=g)
+        b = torch.randint(0, cfg.vocab_size, (9,), generator=g)
+        chunks = [12, 11][:world] if world > 1 else [23]
+        tok, _ = eng.prefill(3, a, chunks, "vanilla", decode_horizon=4, keep_kv=True)
+        toks = [int(tok)]
+        cur = tok
+        for _ in range(3):
+            cur = eng.decode_step([3], cur)
+            toks.append(int(cur))
+        seg = torch.tensor([toks[-1]] + b.tolist())
+        L0 = eng.reqs[3].context_len
+        tok2, _ = eng.append(3, seg, list(range(L0, L0 + seg.numel())), [1] * world)
+        more = [int(tok2)]
+        cur = tok2
+        for _ in range(3):
+            cur = eng.decode_step([3], cur)
+            more.append(int(cur))
+        if rank == 0:
+            torch.save({"a": a, "b": b, "toks": toks, "more": more}, out_path)
+        if world > 1:
+            dist.barrier()
+    finally:
+        if world > 1:
+            dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [1, 2])
+def test_session_append_matches_reference(world):
+    with tempfile.TemporaryDirectory() as d:
+        out = os.path.join(d, "s.pt")
+        if world == 1:
+            _session_worker(0, 1, 0, out)
+        else:
+            mp.start_processes(_session_worker, args=(world, free_port(), out), nprocs=world,
+                               join=True, start_method="spawn")
+        r = torch.load(out)
+    cfg, w = tiny_weights()
+    ref_first, _ = reference_model.greedy_generate(w, r["a"], 3)
+    assert r["toks"] == ref_first
+    full = torch.cat([r["a"], torch.tensor(r["toks"]), r["b"]])
+    ref_more, _ = reference_model.greedy_generate(w, full, 3)
+    assert r["more"] == ref_more
