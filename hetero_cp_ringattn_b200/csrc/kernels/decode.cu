@@ -447,3 +447,169 @@ const char* add_u64(unsigned long long* p, unsigned long long v, cudaStream_t s)
 
 }  // namespace dec
 }  // namespace hcp
+
+// ============================================================================================
+// Allocation-free single-rank decode attention (see decode_noalloc.h for the contract).
+//
+// For callers that cannot allocate device memory: the split-KV scratch (partials, counters, the
+// one-rank exchange slot and its pointer tables) lives in `g_decode_noalloc_scratch`, a
+// file-scope array every device holds while the library is loaded. Host code never passes the
+// array's name to a kernel (in host code it is only a stand-in for the symbol); it passes the
+// device address obtained once per device with cudaGetSymbolAddress.
+// ============================================================================================
+#include <mutex>
+#include <string>
+
+#include "decode_noalloc.h"
+
+namespace {
+
+constexpr unsigned long long kNoAllocBytes = HCP_DECODE_NOALLOC_SCRATCH_BYTES;
+constexpr int kNoAllocMaxDevices = 64;
+
+static __device__ __align__(256) unsigned char g_decode_noalloc_scratch[HCP_DECODE_NOALLOC_SCRATCH_BYTES];
+
+std::mutex g_noalloc_mu;
+void* g_noalloc_addr[kNoAllocMaxDevices] = {nullptr};
+thread_local std::string g_noalloc_err;
+
+// Byte layout inside the scratch array (all offsets 256-byte aligned).
+struct NoAllocLayout {
+  unsigned long long counters, tables, flag, part_o, part_lse, xslot, total;
+};
+
+unsigned long long align256(unsigned long long v) { return (v + 255ull) & ~255ull; }
+
+NoAllocLayout noalloc_layout(int B, int H, int Hkv, int D, int splits) {
+  NoAllocLayout l{};
+  unsigned long long off = 0;
+  l.counters = off;
+  off = align256(off + sizeof(unsigned int) * (unsigned long long)(B * Hkv + 1));
+  l.tables = off;  // float* xslot_ptrs[1]; unsigned long long* ready_ptrs[1]
+  off = align256(off + 2 * sizeof(void*));
+  l.flag = off;
+  off = align256(off + sizeof(unsigned long long));
+  l.part_o = off;
+  off = align256(off + sizeof(float) * (unsigned long long)B * H * splits * D);
+  l.part_lse = off;
+  off = align256(off + sizeof(float) * (unsigned long long)B * H * splits);
+  l.xslot = off;
+  off = align256(off + sizeof(float) * 2ull * B * H * (D + 1));
+  l.total = off;
+  return l;
+}
+
+// Resets the state that must start at zero and points the one-entry tables at the scratch.
+__global__ void noalloc_setup_kernel(unsigned char* base, NoAllocLayout l, int n_counters) {
+  unsigned int* counters = reinterpret_cast<unsigned int*>(base + l.counters);
+  for (int i = threadIdx.x; i < n_counters; i += blockDim.x) counters[i] = 0u;
+  if (threadIdx.x == 0) {
+    void** tables = reinterpret_cast<void**>(base + l.tables);
+    tables[0] = base + l.xslot;
+    tables[1] = base + l.flag;
+    *reinterpret_cast<unsigned long long*>(base + l.flag) = 0ull;
+  }
+}
+
+int noalloc_fail(int code, const std::string& msg) {
+  g_noalloc_err = msg;
+  return code;
+}
+
+}  // namespace
+
+extern "C" unsigned long long hcp_decode_attention_noalloc_scratch_bytes(int batch, int heads,
+                                                                         int hkv, int d,
+                                                                         int splits) {
+  return noalloc_layout(batch, heads, hkv, d, splits).total;
+}
+
+extern "C" const char* hcp_decode_attention_noalloc_error(void) { return g_noalloc_err.c_str(); }
+
+extern "C" int hcp_decode_attention_noalloc(const void* q, const void* arena, int layers,
+                                            int pages, int page, int hkv, int d, int layer,
+                                            const int* page_tables, int pt_stride,
+                                            const int* n_tokens, int batch, int heads,
+                                            float scale, int splits, void* out,
+                                            cudaStream_t stream) {
+  g_noalloc_err.clear();
+  if (!q || !arena || !page_tables || !n_tokens || !out)
+    return noalloc_fail(-1, "hcp_decode_attention_noalloc: null pointer argument");
+  if (batch < 1 || heads < 1 || hkv < 1 || splits < 1 || layers < 1 || pages < 1 || page < 1)
+    return noalloc_fail(-2, "hcp_decode_attention_noalloc: sizes must be positive");
+  if (layer < 0 || layer >= layers)
+    return noalloc_fail(-3, "hcp_decode_attention_noalloc: layer out of range");
+  if (d != 64 && d != 128) return noalloc_fail(-4, "hcp_decode_attention_noalloc: head_dim must be 64 or 128");
+  if (heads % hkv) return noalloc_fail(-5, "hcp_decode_attention_noalloc: heads % kv_heads != 0");
+  const int G = heads / hkv;
+  if (G != 1 && G != 2 && G != 4 && G != 8)
+    return noalloc_fail(-6, "hcp_decode_attention_noalloc: heads / kv_heads must be 1, 2, 4 or 8");
+  const NoAllocLayout lay = noalloc_layout(batch, heads, hkv, d, splits);
+  if (lay.total > kNoAllocBytes)
+    return noalloc_fail(-7, "hcp_decode_attention_noalloc: problem needs " + std::to_string(lay.total) +
+                                " bytes of scratch, more than the static maximum of " +
+                                std::to_string(kNoAllocBytes) + " bytes; lower batch or splits");
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return noalloc_fail(int(e), cudaGetErrorString(e));
+  if (dev < 0 || dev >= kNoAllocMaxDevices)
+    return noalloc_fail(-8, "hcp_decode_attention_noalloc: device index out of range");
+  unsigned char* base = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (g_noalloc_addr[dev] == nullptr) {
+      // one-time set-up for this device (device `dev` is current): device address of the array
+      void* p = nullptr;
+      e = cudaGetSymbolAddress(&p, g_decode_noalloc_scratch);
+      if (e != cudaSuccess) return noalloc_fail(int(e), std::string("cudaGetSymbolAddress: ") + cudaGetErrorString(e));
+      g_noalloc_addr[dev] = p;
+    }
+    base = static_cast<unsigned char*>(g_noalloc_addr[dev]);
+  }
+  noalloc_setup_kernel<<<1, 256, 0, stream>>>(base, lay, batch * hkv + 1);
+  hcp::dec::DecodeAttnArgs a{};
+  a.q = static_cast<const __nv_bfloat16*>(q);
+  a.arena = static_cast<const __nv_bfloat16*>(arena);
+  a.geom = hcp::ArenaGeom{layers, pages, page, hkv, d};
+  a.layer = layer;
+  a.page_tables = page_tables;
+  a.pt_stride = pt_stride;
+  a.n_tokens = n_tokens;
+  a.B = batch;
+  a.H = heads;
+  a.Hkv = hkv;
+  a.D = d;
+  a.scale = scale;
+  a.splits = splits;
+  a.part_o = reinterpret_cast<float*>(base + lay.part_o);
+  a.part_lse = reinterpret_cast<float*>(base + lay.part_lse);
+  a.split_counter = reinterpret_cast<unsigned int*>(base + lay.counters);
+  a.grid_counter = a.split_counter + batch * hkv;
+  a.xslot_ptrs = reinterpret_cast<float* const*>(base + lay.tables);
+  a.n_ranks = 1;
+  a.my_rank = 0;
+  a.ready_ptrs = reinterpret_cast<unsigned long long* const*>(base + lay.tables + sizeof(void*));
+  a.epoch_parity_src = nullptr;
+  a.epoch_mul = 0;
+  a.epoch_add = 1;
+  a.status = nullptr;
+  const char* err = hcp::dec::decode_attn(a, stream);
+  if (err) return noalloc_fail(-9, err);
+  hcp::dec::DecodeCombineArgs c{};
+  c.xslot = reinterpret_cast<const float*>(base + lay.xslot);
+  c.ready = nullptr;
+  c.epoch_src = nullptr;
+  c.epoch_mul = 0;
+  c.epoch_add = 1;
+  c.n_ranks = 1;
+  c.B = batch;
+  c.H = heads;
+  c.D = d;
+  c.out = static_cast<__nv_bfloat16*>(out);
+  c.budget_ns = 0;
+  c.status = nullptr;
+  err = hcp::dec::decode_combine(c, stream);
+  if (err) return noalloc_fail(-10, err);
+  e = cudaGetLastError();
+  return e == cudaSuccess ? 0 : noalloc_fail(int(e), cudaGetErrorString(e));
+}
