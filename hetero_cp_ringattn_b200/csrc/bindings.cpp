@@ -141,7 +141,7 @@ void rmsnorm(torch::Tensor x, torch::Tensor w, torch::Tensor y, double eps) {
 
 void gemv(torch::Tensor x, torch::Tensor W, int64_t epi, c10::optional<torch::Tensor> bias,
           c10::optional<torch::Tensor> y_f32, c10::optional<torch::Tensor> y_bf16,
-          c10::optional<torch::Tensor> argmax) {
+          c10::optional<torch::Tensor> argmax, c10::optional<torch::Tensor> norm_w, double eps) {
   check_cuda_bf16(x, "x");
   check_cuda_bf16(W, "W");
   const c10::cuda::CUDAGuard g(x.device());
@@ -161,6 +161,9 @@ void gemv(torch::Tensor x, torch::Tensor W, int64_t epi, c10::optional<torch::Te
   else if (y_bf16.has_value() && y_bf16->defined()) a.ldy = y_bf16->stride(0);
   a.argmax = ptr_or_null<unsigned long long>(argmax);
   a.num_sms = sm_count(x.get_device());
+  a.norm_w = ptr_or_null<const __nv_bfloat16>(norm_w);
+  a.eps = float(eps);
+  if (a.norm_w) TORCH_CHECK(norm_w->numel() == a.K && norm_w->scalar_type() == torch::kBFloat16, "norm_w [K] bf16");
   if (epi == hcp::dec::kGemvArgmax) TORCH_CHECK(a.argmax != nullptr, "argmax buffer required");
   if (epi == hcp::dec::kGemvF32) TORCH_CHECK(a.y_f32 != nullptr, "y_f32 required");
   if (epi == hcp::dec::kGemvResidual || epi == hcp::dec::kGemvSwiGLU)
@@ -405,6 +408,16 @@ class PyRuntime {
     HCP_CHECK_OK(hcp::dec::decode_combine(a, cur_stream()));
   }
 
+  // Bounded device-side wait until flags[first + r] >= target for r < n (the same kernel the ring
+  // uses for peer flags). Used by tests to exercise the timeout path on a flag nothing sets.
+  void wait_flags(int64_t first, int64_t n, int64_t target, int64_t budget_ms) {
+    const auto& c = rt_.config();
+    TORCH_CHECK(first >= 0 && n > 0 && first + n <= hcp::kFlagWords && n <= 32, "flag range");
+    const c10::cuda::CUDAGuard g(c10::Device(c10::DeviceType::CUDA, c.device));
+    HCP_CHECK_OK(hcp::ew::wait_consumed(rt_.flags() + first, int(n), uint64_t(target),
+                                        uint64_t(budget_ms) * 1000000ull, rt_.status(), cur_stream()));
+  }
+
   torch::Tensor arena() {
     const auto& c = rt_.config();
     auto opts = torch::TensorOptions().dtype(torch::kBFloat16).device(torch::kCUDA, c.device);
@@ -449,7 +462,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("embedding", &embedding, py::arg("ids"), py::arg("W"), py::arg("out"), py::arg("status") = py::none());
   m.def("rmsnorm", &rmsnorm);
   m.def("gemv", &gemv, py::arg("x"), py::arg("W"), py::arg("epi"), py::arg("bias") = py::none(),
-        py::arg("y_f32") = py::none(), py::arg("y_bf16") = py::none(), py::arg("argmax") = py::none());
+        py::arg("y_f32") = py::none(), py::arg("y_bf16") = py::none(), py::arg("argmax") = py::none(),
+        py::arg("norm_w") = py::none(), py::arg("eps") = 1e-6);
   m.def("fill_u64", &fill_u64);
   m.def("argmax_finalize", &argmax_finalize, py::arg("packed"), py::arg("tok32") = py::none(),
         py::arg("tok64") = py::none());
@@ -484,6 +498,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       .def("qkv_decode", &PyRuntime::qkv_decode)
       .def("decode_attn", &PyRuntime::decode_attn)
       .def("decode_combine", &PyRuntime::decode_combine)
+      .def("wait_flags", &PyRuntime::wait_flags)
       .def("arena", &PyRuntime::arena)
       .def("stage", &PyRuntime::stage)
       .def("flags", &PyRuntime::flags)

@@ -5,18 +5,26 @@
 // Replaces the reference's ring block step `process_kv_block` (rust/src/model/attention/
 // ring.rs:201-370: S = Q K^T * s, global-position causal mask, row max, exp, row sum, P V,
 // online rescale of (m, l, O), fully-future block skip) and its q-chunk / micro-block loops
-// (ring.rs:861-1399). Instead of materialising a [qc, kc] score tensor per block and ~10 ATen
-// launches, one CTA streams KV tiles through shared memory and keeps S and O in TMEM.
+// (ring.rs:861-1399). Instead of materialising a [qc, kc] score tensor per block with ~10 ATen
+// launches, one CTA streams KV tiles through shared memory and keeps S, P and O in TMEM.
 //
 // KV operand: a position-ordered K/V staging buffer [Hkv, L, D] (row p holds the key of global
-// position p). In context-parallel runs the ring module fills it with this rank's own shard and
-// the peers' shards over NVLink; the kernel's kv-tile order starts at `kv_start_tile` (this
-// rank's own chunk) so local tiles are consumed while remote ones are still arriving, and an
-// optional per-tile ready flag array lets the producer wait (bounded) for a tile to land.
+// position p). In context-parallel runs every rank pushes its rows into every rank's staging
+// buffer over NVLink; the kernel's kv-tile order starts at `kv_start_tile` (this rank's own
+// chunk) and an optional per-tile ready-flag array lets the producer wait (bounded) for a tile.
 //
-// CTA layout (256 threads): warp 0 TMA producer, warp 1 MMA issuer, warp 2 TMEM allocator,
-// warp 3 idle, warps 4-7 softmax/correction/epilogue (thread i <-> q row i <-> TMEM lane i).
-// TMEM: S double buffer (2 x 128 fp32 columns) + O (D columns).
+// CTA layout (384 threads, one CTA per SM): two q tiles of 128 rows of one head share every K/V
+// tile.
+//   warp 0      TMA producer (Q0, Q1 once; K/V tiles through a STAGES-deep ring)
+//   warp 1      MMA issuer: S_i = Q_i K^T (SS) and O_i += P_i V (TS: P read from TMEM)
+//   warp 2      TMEM allocator
+//   warps 4-7   softmax / correction / epilogue of q tile 0 (thread <-> row <-> TMEM lane)
+//   warps 8-11  the same for q tile 1
+// The MMA warp ping-pongs between the tiles, so the tensor core works on one tile's products
+// while the other tile's warpgroup runs its softmax. TMEM: S_i at column 128 i (P_i, packed
+// bf16, overwrites the first 64 columns of S_i in place), O_i at column 256 + D i.
+// Softmax: two passes over S (row max, then exponentials), tree reductions, lazy O rescale
+// (only when the running max grows by more than 2^8), half of the exponentials on the FMA pipe.
 #include "attn_fwd_sm100.h"
 #include "common.cuh"
 #include "gemm_sm100.h"
@@ -26,18 +34,19 @@ namespace attn {
 
 using namespace hcp::dev;
 
-constexpr int BQ = 128;      // q rows per CTA
+constexpr int BQ = 128;      // q rows per tile
 constexpr int BKV = 128;     // kv rows per tile
-constexpr float kRescaleThreshold = 8.0f;  // log2 units: lazy O rescale (values bounded by 2^8)
+constexpr int QT = 2;        // q tiles per CTA
+constexpr int THREADS = 384;
+constexpr float kRescaleThreshold = 8.0f;  // log2 units
 
 template <int D>
 struct Cfg {
-  static constexpr int ATOMS = D / 64;                 // 128-byte swizzle atoms along D
-  static constexpr int Q_BYTES = BQ * D * 2;
+  static constexpr int ATOMS = D / 64;           // 128-byte swizzle atoms along D
+  static constexpr int Q_BYTES = BQ * D * 2;     // one q tile
   static constexpr int KV_BYTES = BKV * D * 2;
   static constexpr int STAGES = (D == 64) ? 3 : 2;
-  static constexpr int P_BYTES = BQ * BKV * 2;
-  static constexpr int SMEM = 1024 + Q_BYTES + 2 * STAGES * KV_BYTES + P_BYTES + 512;
+  static constexpr int SMEM = 1024 + QT * Q_BYTES + 2 * STAGES * KV_BYTES + 1024;
   static constexpr int TMEM_COLS = 512;
   static constexpr int O_COL = 256;
 };
@@ -49,7 +58,7 @@ struct KParams {
   float* lse;
   float scale_log2;
   int causal;
-  int num_q_tiles;
+  int num_pairs;        // ceil(num_q_tiles / 2)
   int kv_start_tile;
   const unsigned long long* kv_ready;  // optional [Hkv][num_kv_tiles] ready epochs
   unsigned long long kv_epoch;
@@ -66,38 +75,37 @@ __device__ __forceinline__ int kv_tile_at(int j, int n, int start) {
 }
 
 template <int D>
-__global__ void __launch_bounds__(256, 1)
+__global__ void __launch_bounds__(THREADS, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, KParams p) {
   using C = Cfg<D>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
-  uint8_t* sQ = smem;
-  uint8_t* sK = sQ + C::Q_BYTES;
+  uint8_t* sQ = smem;                               // [QT][ATOMS][128 rows x 128 B]
+  uint8_t* sK = sQ + QT * C::Q_BYTES;
   uint8_t* sV = sK + C::STAGES * C::KV_BYTES;
-  uint8_t* sP = sV + C::STAGES * C::KV_BYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + C::P_BYTES);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + C::STAGES * C::KV_BYTES);
   uint64_t* q_full = bars;
   uint64_t* k_full = bars + 1;
   uint64_t* k_empty = k_full + C::STAGES;
   uint64_t* v_full = k_empty + C::STAGES;
   uint64_t* v_empty = v_full + C::STAGES;
-  uint64_t* s_full = v_empty + C::STAGES;  // [2]
-  uint64_t* p_full = s_full + 2;
-  uint64_t* pv_done = p_full + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pv_done + 1);
-  int* s_qmin = reinterpret_cast<int*>(tmem_slot + 1);
-  int* s_qmax = s_qmin + 1;
+  uint64_t* s_full = v_empty + C::STAGES;  // [QT]
+  uint64_t* p_full = s_full + QT;          // [QT]
+  uint64_t* o_done = p_full + QT;          // [QT]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_done + QT);
+  int* s_qmin = reinterpret_cast<int*>(tmem_slot + 1);  // [QT]
+  int* s_qmax = s_qmin + QT;                            // [QT]
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
 
-  // heaviest q tiles first (largest positions last in local order): LPT-like balance
-  const int q_tile = p.num_q_tiles - 1 - int(blockIdx.x) / p.H;
+  // heaviest tile pairs first (largest positions are last in local order): LPT-like balance
+  const int pair = p.num_pairs - 1 - int(blockIdx.x) / p.H;
   const int head = int(blockIdx.x) % p.H;
   const int kv_head = head / (p.H / p.Hkv);
-  const int row0 = q_tile * BQ;
+  const int row0 = pair * QT * BQ;
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -107,12 +115,13 @@ __global__ void __launch_bounds__(256, 1)
       mbar_init(&v_full[s], 1);
       mbar_init(&v_empty[s], 1);
     }
-    mbar_init(&s_full[0], 1);
-    mbar_init(&s_full[1], 1);
-    mbar_init(p_full, 128);
-    mbar_init(pv_done, 1);
-    *s_qmin = 0x7fffffff;
-    *s_qmax = -1;
+    for (int i = 0; i < QT; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 128);
+      mbar_init(&o_done[i], 1);
+      s_qmin[i] = 0x7fffffff;
+      s_qmax[i] = -1;
+    }
     fence_barrier_init();
   }
   if (warp == 2) {
@@ -122,34 +131,39 @@ __global__ void __launch_bounds__(256, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  // q position range of this tile; softmax warps 4-7 own rows 0..127 (thread 128 + i <-> row i)
+  // softmax warps own the rows: thread 128 + 128 i + r <-> row r of q tile i
+  const int tile = (warp >= 4) ? (warp - 4) / 4 : 0;
   int my_pos = -1;
-  if (threadIdx.x >= 128) {
-    const int r = row0 + int(threadIdx.x) - 128;
+  if (warp >= 4) {
+    const int r = row0 + tile * BQ + (int(threadIdx.x) - 128 - tile * 128);
     if (r < p.T) my_pos = p.q_pos[r];
     if (my_pos >= 0) {
-      atomicMin(s_qmin, my_pos);
-      atomicMax(s_qmax, my_pos);
+      atomicMin(&s_qmin[tile], my_pos);
+      atomicMax(&s_qmax[tile], my_pos);
     }
   }
   __syncthreads();
   const uint32_t tmem_base = *tmem_slot;
-  const int qmin = *s_qmin;
-  const int qmax = *s_qmax;
+  const int qmax_all = max(s_qmax[0], s_qmax[1]);
   const int kv_tiles_L = (p.L + BKV - 1) / BKV;
-  int n_tiles = p.causal ? (qmax >= 0 ? qmax / BKV + 1 : 0) : kv_tiles_L;
+  int n_tiles = p.causal ? (qmax_all >= 0 ? qmax_all / BKV + 1 : 0) : kv_tiles_L;
   if (n_tiles > kv_tiles_L) n_tiles = kv_tiles_L;
   const int start = p.kv_start_tile < n_tiles ? p.kv_start_tile : 0;
+  const bool tile1_live = (row0 + BQ) < p.T;
 
   if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
     if (elect_one() && n_tiles > 0) {
       tma_prefetch_desc(&tmQ);
       tma_prefetch_desc(&tmK);
       tma_prefetch_desc(&tmV);
-      mbar_arrive_expect_tx(q_full, C::Q_BYTES);
+      mbar_arrive_expect_tx(q_full, QT * C::Q_BYTES);
 #pragma unroll
-      for (int a = 0; a < C::ATOMS; ++a)
-        tma_load_3d(sQ + a * (BQ * 128), &tmQ, q_full, a * 64, head, row0);
+      for (int i = 0; i < QT; ++i)
+#pragma unroll
+        for (int a = 0; a < C::ATOMS; ++a)
+          tma_load_3d(sQ + i * C::Q_BYTES + a * (BQ * 128), &tmQ, q_full, a * 64, head,
+                      row0 + i * BQ);
       for (int j = 0; j < n_tiles; ++j) {
         const int t = kv_tile_at(j, n_tiles, start);
         const int s = j % C::STAGES;
@@ -173,89 +187,122 @@ __global__ void __launch_bounds__(256, 1)
       }
     }
   } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
     if (elect_one() && n_tiles > 0) {
       constexpr uint32_t idesc_s = idesc_bf16_f32(BQ, BKV, false, false);
       constexpr uint32_t idesc_o = idesc_bf16_f32(BQ, D, false, true);
       const uint32_t sq = smem_u32(sQ);
-      const uint32_t sp = smem_u32(sP);
-      bool ok = mbar_wait(q_full, 0, p.status, 203);
-      tc_fence_after();
-      auto issue_pv = [&](int jj) -> bool {
-        const int s = jj % C::STAGES;
-        const uint32_t ph = (jj / C::STAGES) & 1;
-        if (!mbar_wait(p_full, jj & 1, p.status, 204)) return false;
-        if (!mbar_wait(&v_full[s], ph, p.status, 205)) return false;
-        tc_fence_after();
-        const uint32_t sv = smem_u32(sV + s * C::KV_BYTES);
-#pragma unroll
-        for (int kk = 0; kk < BKV / 16; ++kk) {
-          // A = P (K-major, 2 atoms of 64 kv), B = V tile (MN-major: D contiguous)
-          const uint64_t ad = sdesc_sw128(sp + (kk / 4) * (BQ * 128) + (kk % 4) * 32, 16, 1024);
-          const uint64_t bd = sdesc_sw128(sv + kk * 2048, BKV * 128, 1024);
-          umma_bf16_ss(tmem_base + C::O_COL, ad, bd, idesc_o, (jj > 0 || kk > 0) ? 1u : 0u);
-        }
-        umma_commit(pv_done);
-        umma_commit(&v_empty[s]);
-        return true;
-      };
-      for (int j = 0; ok && j < n_tiles; ++j) {
-        const int s = j % C::STAGES;
-        const uint32_t ph = (j / C::STAGES) & 1;
-        if (!mbar_wait(&k_full[s], ph, p.status, 206)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
+      auto issue_qk = [&](int i, int s) {
         const uint32_t sk = smem_u32(sK + s * C::KV_BYTES);
-        const uint32_t d_s = tmem_base + uint32_t((j & 1) * BKV);
+        const uint32_t qb = sq + i * C::Q_BYTES;
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off = (kk / 4) * (BQ * 128) + (kk % 4) * 32;
           const uint32_t offk = (kk / 4) * (BKV * 128) + (kk % 4) * 32;
-          umma_bf16_ss(d_s, sdesc_sw128(sq + off, 16, 1024), sdesc_sw128(sk + offk, 16, 1024),
-                       idesc_s, kk > 0 ? 1u : 0u);
+          umma_bf16_ss(tmem_base + i * BKV, sdesc_sw128(qb + off, 16, 1024),
+                       sdesc_sw128(sk + offk, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
         }
-        umma_commit(&s_full[j & 1]);
-        umma_commit(&k_empty[s]);
-        if (j >= 1 && !issue_pv(j - 1)) ok = false;
+      };
+      auto issue_pv = [&](int i, int s, bool acc) {
+        const uint32_t sv = smem_u32(sV + s * C::KV_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < BKV / 16; ++kk) {
+          // A = P_i in TMEM (K = kv, 16 bf16 per step = 8 columns), B = V tile (MN-major)
+          umma_bf16_ts(tmem_base + C::O_COL + i * D, tmem_base + i * BKV + kk * 8,
+                       sdesc_sw128(sv + kk * 2048, BKV * 128, 1024), idesc_o,
+                       (acc || kk > 0) ? 1u : 0u);
+        }
+      };
+      bool ok = mbar_wait(q_full, 0, p.status, 203) && mbar_wait(&k_full[0], 0, p.status, 206);
+      if (ok) {
+        tc_fence_after();
+        issue_qk(0, 0);
+        umma_commit(&s_full[0]);
+        issue_qk(1, 0);
+        umma_commit(&s_full[1]);
+        umma_commit(&k_empty[0]);
       }
-      if (ok) issue_pv(n_tiles - 1);
+      for (int j = 0; ok && j < n_tiles; ++j) {
+        const int s = j % C::STAGES;
+        const int s1 = (j + 1) % C::STAGES;
+        const bool more = j + 1 < n_tiles;
+        // q tile 0: O0 += P0 V_j, then S0 = Q0 K_{j+1}^T
+        if (!mbar_wait(&p_full[0], j & 1, p.status, 204) ||
+            !mbar_wait(&v_full[s], (j / C::STAGES) & 1, p.status, 205)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        issue_pv(0, s, j > 0);
+        if (more) {
+          if (!mbar_wait(&k_full[s1], ((j + 1) / C::STAGES) & 1, p.status, 206)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          issue_qk(0, s1);
+          umma_commit(&s_full[0]);
+        } else {
+          umma_commit(&o_done[0]);
+        }
+        // q tile 1: O1 += P1 V_j, then S1 = Q1 K_{j+1}^T
+        if (!mbar_wait(&p_full[1], j & 1, p.status, 207)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        issue_pv(1, s, j > 0);
+        umma_commit(&v_empty[s]);
+        if (more) {
+          issue_qk(1, s1);
+          umma_commit(&s_full[1]);
+          umma_commit(&k_empty[s1]);
+        } else {
+          umma_commit(&o_done[1]);
+        }
+      }
     }
   } else if (warp >= 4) {
-    const int q = warp - 4;
-    const int row = q * 32 + lane;
-    const int grow = row0 + row;
-    const uint32_t lane_base = tmem_base + (uint32_t(q * 32) << 16);
+    // ------------------------------------------------------------------ softmax warpgroups
+    const int q4 = warp % 4;
+    const int row = q4 * 32 + lane;
+    const int grow = row0 + tile * BQ + row;
+    const uint32_t lane_off = uint32_t(q4 * 32) << 16;
+    const uint32_t s_addr = tmem_base + lane_off + uint32_t(tile * BKV);
+    const uint32_t o_addr = tmem_base + lane_off + uint32_t(C::O_COL + tile * D);
+    const int qmin = s_qmin[tile];
+    const bool live = (tile == 0) || tile1_live;
     float m_ref = -INFINITY;  // max used for exponentiation (log2 domain)
     float l_sum = 0.f;
     bool ok = true;
     for (int j = 0; j < n_tiles; ++j) {
       const int t = kv_tile_at(j, n_tiles, start);
-      if (!mbar_wait(&s_full[j & 1], (j >> 1) & 1, p.status, 207)) {
+      if (!mbar_wait(&s_full[tile], j & 1, p.status, 208)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      uint32_t sr[128];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld32(lane_base + uint32_t((j & 1) * BKV + c * 32), sr + 32 * c);
-      tmem_wait_ld();
       const int kv0 = t * BKV;
       const bool need_mask = (p.causal && kv0 + BKV - 1 > qmin) || (kv0 + BKV > p.L) || my_pos < 0;
-      float s[128];
+      const int lim = p.causal ? min(my_pos, p.L - 1) : p.L - 1;  // last visible kv position
+      // pass 1: row max of the scaled scores (four independent partial maxima per chunk)
       float tmax = -INFINITY;
 #pragma unroll
-      for (int c = 0; c < 128; ++c) {
-        float x = __uint_as_float(sr[c]) * p.scale_log2;
-        if (need_mask) {
-          const int kp = kv0 + c;
-          const bool masked = (kp >= p.L) || my_pos < 0 || (p.causal && kp > my_pos);
-          x = masked ? -INFINITY : x;
+      for (int c = 0; c < 4; ++c) {
+        uint32_t r[32];
+        tmem_ld32(s_addr + c * 32, r);
+        tmem_wait_ld();
+        float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          float x = __uint_as_float(r[e]);
+          if (need_mask && kv0 + c * 32 + e > lim) x = -INFINITY;
+          m4[e & 3] = fmaxf(m4[e & 3], x);
         }
-        s[c] = x;
-        tmax = fmaxf(tmax, x);
+        tmax = fmaxf(tmax, fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])));
       }
-      // lazy rescale: only move the reference max when it grows by more than the threshold
+      tmax = tmax * p.scale_log2;
+      // lazy rescale: the reference max only moves when it grows by more than the threshold
       float alpha = 1.f;
       bool resc = false;
       if (tmax > m_ref + kRescaleThreshold || (m_ref == -INFINITY && tmax > -INFINITY)) {
@@ -264,62 +311,59 @@ __global__ void __launch_bounds__(256, 1)
         resc = true;
       }
       const float m_use = (m_ref == -INFINITY) ? 0.f : m_ref;
-      float rs = 0.f;
-      uint32_t pk[64];
-#pragma unroll
-      for (int c = 0; c < 64; ++c) {
-        const float p0 = fast_exp2(s[2 * c] - m_use);
-        const float p1 = fast_exp2(s[2 * c + 1] - m_use);
-        rs += p0 + p1;
-        pk[c] = pack_bf16x2(p0, p1);
-      }
-      l_sum = l_sum * alpha + rs;
-      // PV of the previous tile must be complete before P is overwritten / O is rescaled
-      if (j >= 1) {
-        if (!mbar_wait(pv_done, (j - 1) & 1, p.status, 208)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        if (__any_sync(0xffffffffu, resc)) {
+      // PV_i(j-1) completed before S_i(j) did (same issuing thread, in-order commits): O_i is
+      // stable here and can be rescaled in place
+      if (j > 0 && __any_sync(0xffffffffu, resc)) {
 #pragma unroll 1
-          for (int c = 0; c < D / 32; ++c) {
-            uint32_t o[32];
-            tmem_ld32(lane_base + uint32_t(C::O_COL + c * 32), o);
-            tmem_wait_ld();
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t o[32];
+          tmem_ld32(o_addr + c * 32, o);
+          tmem_wait_ld();
 #pragma unroll
-            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-            tmem_st32(lane_base + uint32_t(C::O_COL + c * 32), o);
+          for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+          tmem_st32(o_addr + c * 32, o);
+        }
+      }
+      // pass 2: P = 2^(s * scale - m), packed to bf16 into the first 64 columns of S_i
+      float rs[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t r[32];
+        tmem_ld32(s_addr + c * 32, r);
+        tmem_wait_ld();
+        uint32_t pk[16];
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+          float x0 = fmaf(__uint_as_float(r[e]), p.scale_log2, -m_use);
+          float x1 = fmaf(__uint_as_float(r[e + 1]), p.scale_log2, -m_use);
+          if (need_mask) {
+            if (kv0 + c * 32 + e > lim) x0 = -INFINITY;
+            if (kv0 + c * 32 + e + 1 > lim) x1 = -INFINITY;
           }
-          tmem_wait_st();
+          // odd chunks on the FMA pipe, even chunks on the MUFU
+          const float p0 = (c & 1) ? poly_exp2(x0) : fast_exp2(x0);
+          const float p1 = (c & 1) ? poly_exp2(x1) : fast_exp2(x1);
+          rs[(e >> 1) & 3] += p0 + p1;
+          pk[e >> 1] = pack_bf16x2(p0, p1);
         }
+        tmem_st16(s_addr + c * 16, pk);
       }
-      // write P (bf16) into the K-major 128B-swizzled operand tile: row `row`, 2 atoms of 64 kv
-#pragma unroll
-      for (int a = 0; a < 2; ++a) {
-        uint8_t* base = sP + a * (BQ * 128) + row * 128;
-#pragma unroll
-        for (int ch = 0; ch < 8; ++ch) {
-          const int pos = (ch ^ (row & 7)) * 16;
-          const int w = a * 32 + ch * 4;
-          *reinterpret_cast<uint4*>(base + pos) = make_uint4(pk[w], pk[w + 1], pk[w + 2], pk[w + 3]);
-        }
-      }
-      fence_proxy_async_smem();
+      tmem_wait_st();
+      l_sum = l_sum * alpha + ((rs[0] + rs[1]) + (rs[2] + rs[3]));
       tc_fence_before();
-      mbar_arrive(p_full);
+      mbar_arrive(&p_full[tile]);
     }
-    // epilogue: O / l, LSE
-    if (ok && n_tiles > 0 && mbar_wait(pv_done, (n_tiles - 1) & 1, p.status, 209)) {
+    // epilogue: O / l and LSE
+    if (ok && n_tiles > 0 && mbar_wait(&o_done[tile], 0, p.status, 209)) {
       tc_fence_after();
       const float inv = l_sum > 0.f ? 1.f / l_sum : 0.f;
       __nv_bfloat16* dst = p.O + ((long)grow * p.H + head) * D;
 #pragma unroll 1
       for (int c = 0; c < D / 32; ++c) {
         uint32_t o[32];
-        tmem_ld32(lane_base + uint32_t(C::O_COL + c * 32), o);
+        tmem_ld32(o_addr + c * 32, o);
         tmem_wait_ld();
-        if (grow < p.T) {
+        if (live && grow < p.T) {
           uint4* d4 = reinterpret_cast<uint4*>(dst + c * 32);
 #pragma unroll
           for (int i = 0; i < 4; ++i)
@@ -329,12 +373,12 @@ __global__ void __launch_bounds__(256, 1)
                                pack_bf16x2(__uint_as_float(o[8 * i + 6]) * inv, __uint_as_float(o[8 * i + 7]) * inv));
         }
       }
-      if (grow < p.T && p.lse != nullptr) {
+      if (live && grow < p.T && p.lse != nullptr) {
         p.lse[(long)head * p.T + grow] =
             l_sum > 0.f ? (m_ref + __log2f(l_sum)) * 0.6931471805599453f : -INFINITY;
       }
-    } else if (n_tiles == 0 && grow < p.T) {
-      // no visible key (only possible for padding rows / empty KV): O = 0, LSE = -inf
+    } else if (n_tiles == 0 && live && grow < p.T) {
+      // no visible key (padding rows / empty KV): O = 0, LSE = -inf
       __nv_bfloat16* dst = p.O + ((long)grow * p.H + head) * D;
       for (int i = 0; i < D; ++i) dst[i] = __float2bfloat16(0.f);
       if (p.lse != nullptr) p.lse[(long)head * p.T + grow] = -INFINITY;
@@ -349,8 +393,8 @@ __global__ void __launch_bounds__(256, 1)
 }
 
 template <int D>
-static cudaError_t launch(const AttnArgs& a, const CUtensorMap& tq, const CUtensorMap& tk,
-                          const CUtensorMap& tv, const KParams& p, cudaStream_t stream) {
+static cudaError_t launch(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
+                          const KParams& p, cudaStream_t stream) {
   static bool attr = false;
   if (!attr) {
     cudaError_t e = cudaFuncSetAttribute(attn_fwd_kernel<D>,
@@ -358,8 +402,8 @@ static cudaError_t launch(const AttnArgs& a, const CUtensorMap& tq, const CUtens
     if (e != cudaSuccess) return e;
     attr = true;
   }
-  const int grid = p.num_q_tiles * p.H;
-  attn_fwd_kernel<D><<<grid, 256, Cfg<D>::SMEM, stream>>>(tq, tk, tv, p);
+  const int grid = p.num_pairs * p.H;
+  attn_fwd_kernel<D><<<grid, THREADS, Cfg<D>::SMEM, stream>>>(tq, tk, tv, p);
   return cudaGetLastError();
 }
 
@@ -393,15 +437,15 @@ const char* attn_fwd(const AttnArgs& a, cudaStream_t stream) {
   p.lse = a.lse;
   p.scale_log2 = a.scale * 1.4426950408889634f;
   p.causal = a.causal;
-  p.num_q_tiles = (a.T + BQ - 1) / BQ;
+  const int num_q_tiles = (a.T + BQ - 1) / BQ;
+  p.num_pairs = (num_q_tiles + QT - 1) / QT;
   p.kv_start_tile = a.kv_start_tile;
   p.kv_ready = a.kv_ready;
   p.kv_epoch = a.kv_epoch;
   p.num_kv_tiles_total = (a.L + BKV - 1) / BKV;
   p.wait_budget_ns = a.wait_budget_ns;
   p.status = a.status;
-  cudaError_t e = a.D == 64 ? launch<64>(a, tq, tk, tv, p, stream)
-                            : launch<128>(a, tq, tk, tv, p, stream);
+  cudaError_t e = a.D == 64 ? launch<64>(tq, tk, tv, p, stream) : launch<128>(tq, tk, tv, p, stream);
   return e == cudaSuccess ? nullptr : cudaGetErrorString(e);
 }
 

@@ -177,6 +177,45 @@ __device__ __forceinline__ void umma_bf16_ss(uint32_t tmem_d, uint64_t adesc, ui
       : "memory");
 }
 
+// D[tmem] (+)= A[tmem] * B[smem desc]: A (M x K, bf16, two elements per 32-bit column) is read
+// from tensor memory, K-major; used for O += P V with P kept in TMEM.
+__device__ __forceinline__ void umma_bf16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc,
+                                             uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// 32 lanes x 16 consecutive 32-bit columns.
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* r) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+      "r"(r[15])
+      : "memory");
+}
+
+// 2^x for x <= 0 on the FMA pipe: Cody-Waite split x = i + f (i = floor(x), f in [0, 1)), a
+// degree-3 least-squares polynomial for 2^f (relative error < 8e-5, fitted for this code base),
+// and the integer i added to the exponent field. The polynomial dips just below 1 at f = 0
+// (biased exponent 126), so i must stay >= -125 for the exponent add to stay in range; inputs
+// at or below -125 return exactly 0 (masked scores).
+__device__ __forceinline__ float poly_exp2(float x) {
+  const float xc = fmaxf(x, -125.f);
+  const float fi = floorf(xc);
+  const float f = xc - fi;
+  float p = fmaf(0.07790716377386663f, f, 0.22623319419985655f);
+  p = fmaf(p, f, 0.6957770964274217f);
+  p = fmaf(p, f, 0.9999278266445136f);
+  const float r = __int_as_float(__float_as_int(p) + (int(fi) << 23));
+  return x <= -125.f ? 0.f : r;
+}
+
 // Arrive on an mbarrier once all previously issued tcgen05.mma of this thread have completed.
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
   asm volatile(

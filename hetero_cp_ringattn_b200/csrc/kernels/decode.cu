@@ -51,117 +51,187 @@ __device__ __forceinline__ unsigned long long pack_argmax(float v, int idx) {
   return (static_cast<unsigned long long>(u) << 32) | (0xFFFFFFFFu - uint32_t(idx));
 }
 
-// One warp computes ROWS output rows (or ROWS gate/up pairs for SwiGLU) for all B inputs.
-template <int EPI, int B, int ROWS>
-__global__ void __launch_bounds__(256) gemv_kernel(GemvArgs a) {
-  const int lane = threadIdx.x % 32;
-  const int warp_global = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
-  const int total_warps = (gridDim.x * blockDim.x) / 32;
+// One CTA (8 warps) computes R output rows (R gate/up pairs for SwiGLU) for all B inputs. The
+// whole CTA splits K: thread t reads uint4 columns t, t + 256, ... of each row, so every thread
+// issues its R row loads for several k steps back to back (no dependent-load chains), and the
+// partial dot products are reduced across the 8 warps through shared memory.
+// NORM: the input rows are RMS-normalised on the fly (statistics recomputed per CTA from the
+// 2-8 input rows, which is cheaper than a separate normalisation launch for decode).
+constexpr int GEMV_THREADS = 256;
+
+template <int EPI, int B, int R, bool NORM>
+__global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(GemvArgs a) {
+  extern __shared__ uint4 xs[];                     // NORM: normalised x, [B][K/8]
+  __shared__ float red[GEMV_THREADS / 32][2 * R * B];
+  __shared__ float rstd[B];
+  const int tid = threadIdx.x, lane = tid % 32, warp = tid / 32;
   const int kvec = a.K / 8;
   const int out_rows = (EPI == kGemvSwiGLU) ? a.N / 2 : a.N;
-  for (int base = warp_global * ROWS; base < out_rows; base += total_warps * ROWS) {
-    float acc[ROWS][B];
-    float acc_u[ROWS][B];
+  const int base = blockIdx.x * R;
+  if (NORM) {
+    // sum of squares per input row, then the normalised bf16 row into shared memory
+    float ss[B];
 #pragma unroll
-    for (int r = 0; r < ROWS; ++r)
+    for (int b = 0; b < B; ++b) ss[b] = 0.f;
+    for (int k = tid; k < kvec; k += GEMV_THREADS) {
 #pragma unroll
-      for (int b = 0; b < B; ++b) acc[r][b] = acc_u[r][b] = 0.f;
-    int wrow[ROWS], urow[ROWS];
+      for (int b = 0; b < B; ++b) {
+        const uint4 v = __ldg(reinterpret_cast<const uint4*>(a.x + (long)b * a.ldx) + k);
+        const uint32_t vv[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-    for (int r = 0; r < ROWS; ++r) {
-      int o = base + r;
-      if (o >= out_rows) o = out_rows - 1;
+        for (int j = 0; j < 4; ++j) ss[b] += bf16_lo(vv[j]) * bf16_lo(vv[j]) + bf16_hi(vv[j]) * bf16_hi(vv[j]);
+      }
+    }
+#pragma unroll
+    for (int b = 0; b < B; ++b) {
+      const float v = warp_sum(ss[b]);
+      if (lane == 0) red[warp][b] = v;
+    }
+    __syncthreads();
+    if (tid < B) {
+      float t = 0.f;
+      for (int w = 0; w < GEMV_THREADS / 32; ++w) t += red[w][tid];
+      rstd[tid] = rsqrtf(t / float(a.K) + a.eps);
+    }
+    __syncthreads();
+    for (int k = tid; k < kvec; k += GEMV_THREADS) {
+      const uint4 wv = __ldg(reinterpret_cast<const uint4*>(a.norm_w) + k);
+      const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+      for (int b = 0; b < B; ++b) {
+        const uint4 v = __ldg(reinterpret_cast<const uint4*>(a.x + (long)b * a.ldx) + k);
+        const uint32_t vv[4] = {v.x, v.y, v.z, v.w};
+        uint32_t o[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float lo = __bfloat162float(__float2bfloat16(bf16_lo(vv[j]) * rstd[b])) * bf16_lo(ww[j]);
+          const float hi = __bfloat162float(__float2bfloat16(bf16_hi(vv[j]) * rstd[b])) * bf16_hi(ww[j]);
+          o[j] = pack_bf16x2(lo, hi);
+        }
+        xs[b * kvec + k] = make_uint4(o[0], o[1], o[2], o[3]);
+      }
+    }
+    __syncthreads();
+  }
+  int wrow[R], urow[R];
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    int o = base + r;
+    if (o >= out_rows) o = out_rows - 1;
+    if (EPI == kGemvSwiGLU) {
+      wrow[r] = (o / 128) * 256 + (o % 128);
+      urow[r] = wrow[r] + 128;
+    } else {
+      wrow[r] = o;
+      urow[r] = o;
+    }
+  }
+  float acc[R][B], accu[R][B];
+#pragma unroll
+  for (int r = 0; r < R; ++r)
+#pragma unroll
+    for (int b = 0; b < B; ++b) acc[r][b] = accu[r][b] = 0.f;
+#pragma unroll 4
+  for (int k = tid; k < kvec; k += GEMV_THREADS) {
+    uint4 w[R], u[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      w[r] = ld_stream(reinterpret_cast<const uint4*>(a.W + (long)wrow[r] * a.K) + k);
+      if (EPI == kGemvSwiGLU) u[r] = ld_stream(reinterpret_cast<const uint4*>(a.W + (long)urow[r] * a.K) + k);
+    }
+#pragma unroll
+    for (int b = 0; b < B; ++b) {
+      const uint4 xv = NORM ? xs[b * kvec + k] : __ldg(reinterpret_cast<const uint4*>(a.x + (long)b * a.ldx) + k);
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        dot8_acc(w[r], xv, acc[r][b]);
+        if (EPI == kGemvSwiGLU) dot8_acc(u[r], xv, accu[r][b]);
+      }
+    }
+  }
+  if (NORM) __syncthreads();  // `red` is reused below
+#pragma unroll
+  for (int r = 0; r < R; ++r)
+#pragma unroll
+    for (int b = 0; b < B; ++b) {
+      const float v = warp_sum(acc[r][b]);
+      if (lane == 0) red[warp][r * B + b] = v;
       if (EPI == kGemvSwiGLU) {
-        wrow[r] = (o / 128) * 256 + (o % 128);
-        urow[r] = wrow[r] + 128;
-      } else {
-        wrow[r] = o;
-        urow[r] = o;
+        const float vu = warp_sum(accu[r][b]);
+        if (lane == 0) red[warp][R * B + r * B + b] = vu;
       }
     }
-#pragma unroll 2
-    for (int k = lane; k < kvec; k += 32) {
-      uint4 w[ROWS], u[ROWS];
+  __syncthreads();
+  if (tid < R * B) {
+    const int r = tid / B, b = tid % B;
+    const int o = base + r;
+    float v = 0.f, vu = 0.f;
 #pragma unroll
-      for (int r = 0; r < ROWS; ++r) {
-        w[r] = ld_stream(reinterpret_cast<const uint4*>(a.W + (long)wrow[r] * a.K) + k);
-        if (EPI == kGemvSwiGLU)
-          u[r] = ld_stream(reinterpret_cast<const uint4*>(a.W + (long)urow[r] * a.K) + k);
-      }
-#pragma unroll
-      for (int b = 0; b < B; ++b) {
-        const uint4 xv = __ldg(reinterpret_cast<const uint4*>(a.x + (long)b * a.ldx) + k);
-#pragma unroll
-        for (int r = 0; r < ROWS; ++r) {
-          dot8_acc(w[r], xv, acc[r][b]);
-          if (EPI == kGemvSwiGLU) dot8_acc(u[r], xv, acc_u[r][b]);
-        }
+    for (int w = 0; w < GEMV_THREADS / 32; ++w) {
+      v += red[w][r * B + b];
+      if (EPI == kGemvSwiGLU) vu += red[w][R * B + r * B + b];
+    }
+    if (o < out_rows) {
+      if (EPI == kGemvF32) {
+        if (a.bias) v += __bfloat162float(a.bias[o]);
+        a.y_f32[(long)b * a.ldy + o] = v;
+      } else if (EPI == kGemvResidual) {
+        __nv_bfloat16* y = a.y_bf16 + (long)b * a.ldy + o;
+        *y = __float2bfloat16(__bfloat162float(__float2bfloat16(v)) + __bfloat162float(*y));
+      } else if (EPI == kGemvSwiGLU) {
+        const float g = __bfloat162float(__float2bfloat16(v));
+        const float uu = __bfloat162float(__float2bfloat16(vu));
+        const float sg = g / (1.f + fast_exp2(-g * kLog2e));
+        a.y_bf16[(long)b * a.ldy + o] = __float2bfloat16(sg * uu);
+      } else if (EPI == kGemvArgmax) {
+        if (a.y_f32) a.y_f32[(long)b * a.ldy + o] = v;
+        red[0][2 * R * B - 1 - tid] = v;  // keep for the per-CTA argmax below (disjoint slots)
       }
     }
+  }
+  if (EPI == kGemvArgmax) {
+    __syncthreads();
+    if (tid < B) {
+      unsigned long long best = 0;
 #pragma unroll
-    for (int r = 0; r < ROWS; ++r)
-#pragma unroll
-      for (int b = 0; b < B; ++b) {
-        acc[r][b] = warp_sum(acc[r][b]);
-        if (EPI == kGemvSwiGLU) acc_u[r][b] = warp_sum(acc_u[r][b]);
-      }
-    if (lane == 0) {
-#pragma unroll
-      for (int r = 0; r < ROWS; ++r) {
+      for (int r = 0; r < R; ++r) {
         const int o = base + r;
-        if (o >= out_rows) continue;
-#pragma unroll
-        for (int b = 0; b < B; ++b) {
-          float v = acc[r][b];
-          if (EPI == kGemvF32) {
-            if (a.bias) v += __bfloat162float(a.bias[o]);
-            a.y_f32[(long)b * a.ldy + o] = v;
-          } else if (EPI == kGemvResidual) {
-            __nv_bfloat16* y = a.y_bf16 + (long)b * a.ldy + o;
-            *y = __float2bfloat16(__bfloat162float(__float2bfloat16(v)) + __bfloat162float(*y));
-          } else if (EPI == kGemvSwiGLU) {
-            const float g = __bfloat162float(__float2bfloat16(v));
-            const float uu = __bfloat162float(__float2bfloat16(acc_u[r][b]));
-            const float s = g / (1.f + fast_exp2(-g * kLog2e));
-            a.y_bf16[(long)b * a.ldy + o] = __float2bfloat16(s * uu);
-          } else if (EPI == kGemvArgmax) {
-            if (a.y_f32) a.y_f32[(long)b * a.ldy + o] = v;
-          }
+        if (o < out_rows) {
+          const unsigned long long c = pack_argmax(red[0][2 * R * B - 1 - (r * B + tid)], o);
+          best = c > best ? c : best;
         }
       }
-    }
-    if (EPI == kGemvArgmax) {
-      // per-warp candidates -> global packed max (lane 0 holds the reduced values)
-      if (lane == 0) {
-#pragma unroll
-        for (int b = 0; b < B; ++b) {
-          unsigned long long best = 0;
-#pragma unroll
-          for (int r = 0; r < ROWS; ++r) {
-            const int o = base + r;
-            if (o < out_rows) {
-              const unsigned long long c = pack_argmax(acc[r][b], o);
-              best = c > best ? c : best;
-            }
-          }
-          atomicMax(a.argmax + b, best);
-        }
-      }
+      atomicMax(a.argmax + tid, best);
     }
   }
 }
 
-template <int EPI>
-static cudaError_t gemv_dispatch_b(const GemvArgs& a, int grid, cudaStream_t s) {
+template <int EPI, bool NORM>
+static cudaError_t gemv_launch(const GemvArgs& a, cudaStream_t s) {
   constexpr int R = (EPI == kGemvSwiGLU) ? 2 : 4;
+  const int out_rows = (EPI == kGemvSwiGLU) ? a.N / 2 : a.N;
+  const int grid = (out_rows + R - 1) / R;
+  const size_t smem = NORM ? size_t(a.B) * a.K * 2 : 0;
+  auto go = [&](auto kernel) -> cudaError_t {
+    if (smem > 48 * 1024) {
+      cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+      if (e != cudaSuccess) return e;
+    }
+    kernel<<<grid, GEMV_THREADS, smem, s>>>(a);
+    return cudaGetLastError();
+  };
   switch (a.B) {
-    case 1: gemv_kernel<EPI, 1, R><<<grid, 256, 0, s>>>(a); break;
-    case 2: gemv_kernel<EPI, 2, R><<<grid, 256, 0, s>>>(a); break;
-    case 4: gemv_kernel<EPI, 4, R><<<grid, 256, 0, s>>>(a); break;
-    case 8: gemv_kernel<EPI, 8, 2><<<grid, 256, 0, s>>>(a); break;
+    case 1: return go(gemv_kernel<EPI, 1, R, NORM>);
+    case 2: return go(gemv_kernel<EPI, 2, R, NORM>);
+    case 4: return go(gemv_kernel<EPI, 4, R, NORM>);
+    case 8: return go(gemv_kernel<EPI, 8, R, NORM>);
     default: return cudaErrorInvalidValue;
   }
-  return cudaGetLastError();
+}
+
+template <int EPI>
+static cudaError_t gemv_dispatch(const GemvArgs& a, cudaStream_t s) {
+  return a.norm_w ? gemv_launch<EPI, true>(a, s) : gemv_launch<EPI, false>(a, s);
 }
 
 const char* gemv(const GemvArgs& a, cudaStream_t s) {
@@ -170,13 +240,13 @@ const char* gemv(const GemvArgs& a, cudaStream_t s) {
   if (a.epi == kGemvSwiGLU && a.N % 256) return "gemv: SwiGLU needs N % 256 == 0";
   if ((reinterpret_cast<uintptr_t>(a.W) | reinterpret_cast<uintptr_t>(a.x)) & 15)
     return "gemv: W/x must be 16-byte aligned";
-  const int grid = a.num_sms * 4;
+  if (a.norm_w && (size_t(a.B) * a.K * 2 > 200 * 1024)) return "gemv: fused norm needs B*K*2 <= 200 KB";
   cudaError_t e;
   switch (a.epi) {
-    case kGemvF32: e = gemv_dispatch_b<kGemvF32>(a, grid, s); break;
-    case kGemvResidual: e = gemv_dispatch_b<kGemvResidual>(a, grid, s); break;
-    case kGemvSwiGLU: e = gemv_dispatch_b<kGemvSwiGLU>(a, grid, s); break;
-    case kGemvArgmax: e = gemv_dispatch_b<kGemvArgmax>(a, grid, s); break;
+    case kGemvF32: e = gemv_dispatch<kGemvF32>(a, s); break;
+    case kGemvResidual: e = gemv_dispatch<kGemvResidual>(a, s); break;
+    case kGemvSwiGLU: e = gemv_dispatch<kGemvSwiGLU>(a, s); break;
+    case kGemvArgmax: e = gemv_dispatch<kGemvArgmax>(a, s); break;
     default: return "gemv: unknown epilogue";
   }
   return e == cudaSuccess ? nullptr : cudaGetErrorString(e);
@@ -222,45 +292,55 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(DecodeAttnArgs a) {
   const int* pt = a.page_tables + (long)b * a.pt_stride;
   // The loop bound is warp-uniform (it depends on the warp, not the lane group) because the
   // body reduces scores with full-warp shuffles; a lane group past the end of the split runs
-  // the iteration with `valid == false` and leaves its state untouched.
-  for (int base = s0 + warp * TPW; base < s1; base += GROUPS) {
-    const int t = base + lane / LPG;
-    const bool valid = t < s1;
-    uint4 kv = make_uint4(0u, 0u, 0u, 0u), vv4 = make_uint4(0u, 0u, 0u, 0u);
-    if (valid) {
-      const int page = pt[t / a.geom.page];
-      const int row = t % a.geom.page;
-      const __nv_bfloat16* kp = a.arena + a.geom.offset(a.layer, page, 0, h, row) + gl * 8;
-      const __nv_bfloat16* vp = kp + a.geom.kv_stride();
-      kv = *reinterpret_cast<const uint4*>(kp);
-      vv4 = *reinterpret_cast<const uint4*>(vp);
-    }
-    const uint32_t kw[4] = {kv.x, kv.y, kv.z, kv.w};
-    const uint32_t vw[4] = {vv4.x, vv4.y, vv4.z, vv4.w};
-    float vf[8];
+  // the step with `valid == false` and leaves its state untouched. UNR token steps are loaded
+  // before any is consumed, so each lane keeps 2 * UNR 16-byte loads in flight.
+  constexpr int UNR = 4;
+  for (int base = s0 + warp * TPW; base < s1; base += GROUPS * UNR) {
+    uint4 kvs[UNR], vvs[UNR];
+    bool valid[UNR];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      vf[2 * j] = bf16_lo(vw[j]);
-      vf[2 * j + 1] = bf16_hi(vw[j]);
+    for (int u = 0; u < UNR; ++u) {
+      const int t = base + u * GROUPS + lane / LPG;
+      valid[u] = t < s1;
+      kvs[u] = make_uint4(0u, 0u, 0u, 0u);
+      vvs[u] = make_uint4(0u, 0u, 0u, 0u);
+      if (valid[u]) {
+        const int page = pt[t / a.geom.page];
+        const int row = t % a.geom.page;
+        const __nv_bfloat16* kp = a.arena + a.geom.offset(a.layer, page, 0, h, row) + gl * 8;
+        kvs[u] = *reinterpret_cast<const uint4*>(kp);
+        vvs[u] = *reinterpret_cast<const uint4*>(kp + a.geom.kv_stride());
+      }
     }
 #pragma unroll
-    for (int g = 0; g < G; ++g) {
-      float sc = 0.f;
+    for (int u = 0; u < UNR; ++u) {
+      const uint32_t kw[4] = {kvs[u].x, kvs[u].y, kvs[u].z, kvs[u].w};
+      const uint32_t vw[4] = {vvs[u].x, vvs[u].y, vvs[u].z, vvs[u].w};
+      float vf[8];
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        sc = fmaf(q[g][2 * j], bf16_lo(kw[j]), sc);
-        sc = fmaf(q[g][2 * j + 1], bf16_hi(kw[j]), sc);
+        vf[2 * j] = bf16_lo(vw[j]);
+        vf[2 * j + 1] = bf16_hi(vw[j]);
       }
 #pragma unroll
-      for (int o = LPG / 2; o > 0; o >>= 1) sc += __shfl_xor_sync(0xffffffffu, sc, o);
-      if (!valid) continue;
-      const float mn = fmaxf(m[g], sc);
-      const float al = fast_exp2(m[g] - mn);
-      const float pp = fast_exp2(sc - mn);
-      l[g] = l[g] * al + pp;
+      for (int g = 0; g < G; ++g) {
+        float sc = 0.f;
 #pragma unroll
-      for (int j = 0; j < 8; ++j) acc[g][j] = fmaf(acc[g][j], al, pp * vf[j]);
-      m[g] = mn;
+        for (int j = 0; j < 4; ++j) {
+          sc = fmaf(q[g][2 * j], bf16_lo(kw[j]), sc);
+          sc = fmaf(q[g][2 * j + 1], bf16_hi(kw[j]), sc);
+        }
+#pragma unroll
+        for (int o = LPG / 2; o > 0; o >>= 1) sc += __shfl_xor_sync(0xffffffffu, sc, o);
+        if (!valid[u]) continue;
+        const float mn = fmaxf(m[g], sc);
+        const float al = fast_exp2(m[g] - mn);
+        const float pp = fast_exp2(sc - mn);
+        l[g] = l[g] * al + pp;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[g][j] = fmaf(acc[g][j], al, pp * vf[j]);
+        m[g] = mn;
+      }
     }
   }
   // CTA reduction over the GROUPS token groups through shared memory
@@ -347,40 +427,38 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(DecodeAttnArgs a) {
   }
 }
 
-// grid (B), block 256: wait for every rank's partial (bounded), then LSE-combine in rank order.
+// grid (B, H), block D: wait for every rank's partial (bounded), then LSE-combine in rank
+// order (the same order on every rank, so every rank produces bit-identical outputs).
 __global__ void decode_combine_kernel(DecodeCombineArgs a) {
-  const int b = blockIdx.x;
+  const int b = blockIdx.x, hh = blockIdx.y, d = threadIdx.x;
   const unsigned long long e = a.epoch_src ? (*a.epoch_src * a.epoch_mul + a.epoch_add) : a.epoch_add;
   const int parity = int(e & 1ull);
   __shared__ int ok;
   if (threadIdx.x == 0) ok = 1;
   __syncthreads();
-  if (threadIdx.x < a.n_ranks && a.ready != nullptr) {
+  if (a.ready != nullptr && threadIdx.x < a.n_ranks) {
     if (!wait_flag_geq_sys(a.ready + threadIdx.x, e, a.budget_ns, a.status, 401, threadIdx.x)) ok = 0;
   }
   __syncthreads();
   const int H = a.H, D = a.D;
   const float* xs = a.xslot + (long)parity * a.n_ranks * a.B * H * (D + 1);
-  for (int i = threadIdx.x; i < H * D; i += blockDim.x) {
-    const int hh = i / D, d = i % D;
-    float out = 0.f;
-    if (ok) {
-      float mx = -INFINITY;
-      for (int r = 0; r < a.n_ranks; ++r)
-        mx = fmaxf(mx, ((volatile const float*)xs)[(((long)r * a.B + b) * H + hh) * (D + 1) + D]);
-      if (mx > -INFINITY) {
-        float ws = 0.f, o = 0.f;
-        for (int r = 0; r < a.n_ranks; ++r) {
-          const long base = (((long)r * a.B + b) * H + hh) * (D + 1);
-          const float w = fast_exp2(((volatile const float*)xs)[base + D] - mx);
-          ws += w;
-          o += w * ((volatile const float*)xs)[base + d];
-        }
-        out = o / ws;
+  float out = 0.f;
+  if (ok) {
+    float mx = -INFINITY;
+    for (int r = 0; r < a.n_ranks; ++r)
+      mx = fmaxf(mx, __ldcg(xs + (((long)r * a.B + b) * H + hh) * (D + 1) + D));
+    if (mx > -INFINITY) {
+      float ws = 0.f, o = 0.f;
+      for (int r = 0; r < a.n_ranks; ++r) {
+        const long base = (((long)r * a.B + b) * H + hh) * (D + 1);
+        const float w = fast_exp2(__ldcg(xs + base + D) - mx);
+        ws += w;
+        o += w * __ldcg(xs + base + d);
       }
+      out = o / ws;
     }
-    a.out[(long)b * H * D + i] = __float2bfloat16(out);
   }
+  a.out[((long)b * H + hh) * D + d] = __float2bfloat16(out);
 }
 
 template <int D, int G>
@@ -405,8 +483,8 @@ const char* decode_attn(const DecodeAttnArgs& a, cudaStream_t s) {
 }
 
 const char* decode_combine(const DecodeCombineArgs& a, cudaStream_t s) {
-  if (a.n_ranks > 256) return "decode_combine: too many ranks";
-  decode_combine_kernel<<<a.B, 256, 0, s>>>(a);
+  if (a.n_ranks > a.D) return "decode_combine: more ranks than head_dim threads";
+  decode_combine_kernel<<<dim3(a.B, a.H), a.D, 0, s>>>(a);
   return cudaGetLastError() == cudaSuccess ? nullptr : "decode_combine: launch failed";
 }
 

@@ -28,6 +28,8 @@ struct GemvArgs {
   long ldy;
   unsigned long long* argmax;  // [B] packed (value, index); caller zeroes it
   int num_sms;
+  const __nv_bfloat16* norm_w; // optional fused input RMSNorm weight [K]
+  float eps;
 };
 
 struct DecodeAttnArgs {

@@ -582,7 +582,7 @@ class DecodeGraph:
         self.g = torch.zeros(B, eng.w.intermediate_padded, dtype=torch.bfloat16, device=dev)
         self.logits = torch.zeros(B, cfg.vocab_size, dtype=torch.float32, device=dev)
         self.am = torch.zeros(B, dtype=torch.int64, device=dev)
-        self.splits = max(1, min(64, -(-2 * eng.num_sms // (B * eng.Hkv))))
+        self.splits = max(1, min(128, -(-4 * eng.num_sms // (B * eng.Hkv))))
         self.part_o = torch.zeros(B * eng.H * self.splits * eng.D, dtype=torch.float32, device=dev)
         self.part_l = torch.zeros(B * eng.H * self.splits, dtype=torch.float32, device=dev)
         self.counters = torch.zeros(B * eng.Hkv + 1, dtype=torch.int32, device=dev)
@@ -596,21 +596,20 @@ class DecodeGraph:
         nat.add_u64(e.dec_step, 1)
         launches.count()
         K.embedding(self.tokens, w.embed, out=self.x)
+        eps = cfg.rms_norm_eps
         for li, lw in enumerate(w.layers):
-            K.rmsnorm(self.x, lw.in_norm, cfg.rms_norm_eps, out=self.xn)
-            K.gemv(self.xn, lw.wqkv, "f32", bias=lw.bqkv, y_f32=self.qkv)
+            K.gemv(self.x, lw.wqkv, "f32", bias=lw.bqkv, y_f32=self.qkv, norm_w=lw.in_norm, eps=eps)
             rt.qkv_decode(self.qkv, self.pos, e.cos, e.sin, li, self.pt, self.owner, self.slot, self.q)
             rt.decode_attn(self.q, li, self.pt, self.ntok[li], e.scale, self.splits, self.part_o,
                            self.part_l, self.counters, e.dec_step, e.L, li + 1)
             rt.decode_combine(self.o, self.B, e.H, e.dec_step, e.L, li + 1)
             launches.count(3)
             K.gemv(self.o, lw.wo, "residual", y_bf16=self.x)
-            K.rmsnorm(self.x, lw.post_norm, cfg.rms_norm_eps, out=self.xn)
-            K.gemv(self.xn, lw.wgu, "swiglu", y_bf16=self.g)
+            K.gemv(self.x, lw.wgu, "swiglu", y_bf16=self.g, norm_w=lw.post_norm, eps=eps)
             K.gemv(self.g, lw.wd, "residual", y_bf16=self.x)
-        K.rmsnorm(self.x, w.final_norm, cfg.rms_norm_eps, out=self.xn)
         nat.fill_u64(self.am, 0)
-        K.gemv(self.xn, w.lm_head, "argmax", y_f32=self.logits, argmax=self.am)
+        K.gemv(self.x, w.lm_head, "argmax", y_f32=self.logits, argmax=self.am, norm_w=w.final_norm,
+               eps=eps)
         nat.argmax_finalize(self.am, self.tokens, self.out_tok)
         launches.count(2)
 

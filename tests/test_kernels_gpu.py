@@ -174,3 +174,24 @@ def test_gemv(dev, b):
     rl = x.float() @ wl.float().t()
     assert torch.equal(tok, logits.argmax(-1))
     assert rel_err(logits, rl) < 1e-3
+
+
+@pytest.mark.parametrize("b", [1, 8])
+def test_gemv_fused_rmsnorm(dev, b):
+    torch.manual_seed(7)
+    kdim, n = 2048, 1024
+    x = torch.randn(b, kdim, device=dev, dtype=torch.bfloat16) * 3
+    nw = (torch.rand(kdim, device=dev) + 0.5).bfloat16()
+    w = torch.randn(n, kdim, device=dev, dtype=torch.bfloat16) / math.sqrt(kdim)
+    y = torch.empty(b, n, device=dev, dtype=torch.float32)
+    K.gemv(x, w, "f32", y_f32=y, norm_w=nw, eps=1e-5)
+    xn = K.rmsnorm(x, nw, 1e-5)
+    r = xn.float() @ w.float().t()
+    assert rel_err(y, r) < 1e-3
+    g = torch.randn(512, kdim, device=dev, dtype=torch.bfloat16) / math.sqrt(kdim)
+    u = torch.randn(512, kdim, device=dev, dtype=torch.bfloat16) / math.sqrt(kdim)
+    out = torch.empty(b, 512, device=dev, dtype=torch.bfloat16)
+    K.gemv(x, K.interleave_gate_up(g, u), "swiglu", y_bf16=out, norm_w=nw, eps=1e-5)
+    gg = (xn.float() @ g.float().t()).bfloat16().float()
+    uu = (xn.float() @ u.float().t()).bfloat16().float()
+    assert rel_err(out, torch.nn.functional.silu(gg) * uu) < 2e-2
