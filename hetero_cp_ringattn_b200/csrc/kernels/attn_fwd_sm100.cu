@@ -94,7 +94,8 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint64_t* s_full = v_empty + C::STAGES;  // [QT]
   uint64_t* p_full = s_full + QT;          // [QT]
   uint64_t* o_done = p_full + QT;          // [QT]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_done + QT);
+  uint64_t* turn = o_done + QT;            // [QT] softmax ping-pong between the two warpgroups
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(turn + QT);
   int* s_qmin = reinterpret_cast<int*>(tmem_slot + 1);  // [QT]
   int* s_qmax = s_qmin + QT;                            // [QT]
 
@@ -119,6 +120,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_init(&s_full[i], 1);
       mbar_init(&p_full[i], 128);
       mbar_init(&o_done[i], 1);
+      mbar_init(&turn[i], 128);
       s_qmin[i] = 0x7fffffff;
       s_qmax[i] = -1;
     }
@@ -275,9 +277,15 @@ __global__ void __launch_bounds__(THREADS, 1)
     float m_ref = -INFINITY;  // max used for exponentiation (log2 domain)
     float l_sum = 0.f;
     bool ok = true;
+    const float2 sc2 = make_float2(p.scale_log2, p.scale_log2);
     for (int j = 0; j < n_tiles; ++j) {
       const int t = kv_tile_at(j, n_tiles, start);
-      if (!mbar_wait(&s_full[tile], j & 1, p.status, 208)) {
+      // ping-pong: tile 1 runs its softmax for step j after tile 0 finished step j, tile 0 runs
+      // step j after tile 1 finished step j - 1, so one warpgroup's exponentials overlap the
+      // tensor core's work on the other tile
+      if (tile == 1) ok = mbar_wait(&turn[1], j & 1, p.status, 211);
+      else if (j > 0) ok = mbar_wait(&turn[0], (j - 1) & 1, p.status, 212);
+      if (!ok || !mbar_wait(&s_full[tile], j & 1, p.status, 208)) {
         ok = false;
         break;
       }
@@ -285,23 +293,28 @@ __global__ void __launch_bounds__(THREADS, 1)
       const int kv0 = t * BKV;
       const bool need_mask = (p.causal && kv0 + BKV - 1 > qmin) || (kv0 + BKV > p.L) || my_pos < 0;
       const int lim = p.causal ? min(my_pos, p.L - 1) : p.L - 1;  // last visible kv position
-      // pass 1: row max of the scaled scores (four independent partial maxima per chunk)
-      float tmax = -INFINITY;
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t r[32];
-        tmem_ld32(s_addr + c * 32, r);
+      // pass 1: the whole score row in one batch of TMEM loads, row max with 3-input maxima
+      float tmax;
+      {
+        uint32_t r[128];
+        tmem_ld32(s_addr, r);
+        tmem_ld32(s_addr + 32, r + 32);
+        tmem_ld32(s_addr + 64, r + 64);
+        tmem_ld32(s_addr + 96, r + 96);
         tmem_wait_ld();
+        if (need_mask) {
+#pragma unroll
+          for (int e = 0; e < 128; ++e)
+            if (kv0 + e > lim) r[e] = __float_as_uint(-INFINITY);
+        }
         float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          float x = __uint_as_float(r[e]);
-          if (need_mask && kv0 + c * 32 + e > lim) x = -INFINITY;
-          m4[e & 3] = fmaxf(m4[e & 3], x);
-        }
-        tmax = fmaxf(tmax, fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])));
+        for (int e = 0; e < 128; e += 8)
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            m4[k] = max3f(m4[k], __uint_as_float(r[e + 2 * k]), __uint_as_float(r[e + 2 * k + 1]));
+        tmax = max3f(m4[0], m4[1], fmaxf(m4[2], m4[3])) * p.scale_log2;
       }
-      tmax = tmax * p.scale_log2;
       // lazy rescale: the reference max only moves when it grows by more than the threshold
       float alpha = 1.f;
       bool resc = false;
@@ -324,34 +337,43 @@ __global__ void __launch_bounds__(THREADS, 1)
           tmem_st32(o_addr + c * 32, o);
         }
       }
-      // pass 2: P = 2^(s * scale - m), packed to bf16 into the first 64 columns of S_i
-      float rs[4] = {0.f, 0.f, 0.f, 0.f};
+      // pass 2: P = 2^(s * scale - m) in two halves of 64 columns, packed to bf16 into the first
+      // 64 columns of S_i (half h lands on columns already consumed). Packed f32x2 arithmetic;
+      // 3 of every 8 pairs take the FMA-pipe polynomial, the rest the MUFU.
+      float2 rs0 = make_float2(0.f, 0.f), rs1 = make_float2(0.f, 0.f);
+      const float2 negm = make_float2(-m_use, -m_use);
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t r[32];
-        tmem_ld32(s_addr + c * 32, r);
+      for (int hh = 0; hh < 2; ++hh) {
+        uint32_t r[64];
+        tmem_ld32(s_addr + hh * 64, r);
+        tmem_ld32(s_addr + hh * 64 + 32, r + 32);
         tmem_wait_ld();
-        uint32_t pk[16];
+        uint32_t pk[32];
 #pragma unroll
-        for (int e = 0; e < 32; e += 2) {
-          float x0 = fmaf(__uint_as_float(r[e]), p.scale_log2, -m_use);
-          float x1 = fmaf(__uint_as_float(r[e + 1]), p.scale_log2, -m_use);
+        for (int e = 0; e < 64; e += 2) {
+          float2 x = __ffma2_rn(make_float2(__uint_as_float(r[e]), __uint_as_float(r[e + 1])), sc2, negm);
           if (need_mask) {
-            if (kv0 + c * 32 + e > lim) x0 = -INFINITY;
-            if (kv0 + c * 32 + e + 1 > lim) x1 = -INFINITY;
+            if (kv0 + hh * 64 + e > lim) x.x = -INFINITY;
+            if (kv0 + hh * 64 + e + 1 > lim) x.y = -INFINITY;
           }
-          // odd chunks on the FMA pipe, even chunks on the MUFU
-          const float p0 = (c & 1) ? poly_exp2(x0) : fast_exp2(x0);
-          const float p1 = (c & 1) ? poly_exp2(x1) : fast_exp2(x1);
-          rs[(e >> 1) & 3] += p0 + p1;
-          pk[e >> 1] = pack_bf16x2(p0, p1);
+          float2 pp;
+          if (((e >> 1) & 7) >= 5) {
+            pp = poly_exp2_x2(x);
+          } else {
+            pp.x = fast_exp2(x.x);
+            pp.y = fast_exp2(x.y);
+          }
+          if ((e >> 1) & 1) rs1 = __fadd2_rn(rs1, pp);
+          else rs0 = __fadd2_rn(rs0, pp);
+          pk[e >> 1] = pack_bf16x2(pp.x, pp.y);
         }
-        tmem_st16(s_addr + c * 16, pk);
+        tmem_st32(s_addr + hh * 32, pk);
       }
       tmem_wait_st();
-      l_sum = l_sum * alpha + ((rs[0] + rs[1]) + (rs[2] + rs[3]));
+      l_sum = l_sum * alpha + ((rs0.x + rs0.y) + (rs1.x + rs1.y));
       tc_fence_before();
       mbar_arrive(&p_full[tile]);
+      mbar_arrive(&turn[tile ^ 1]);
     }
     // epilogue: O / l and LSE
     if (ok && n_tiles > 0 && mbar_wait(&o_done[tile], 0, p.status, 209)) {

@@ -118,7 +118,7 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
-// ------------------------------------------------------------------------------- TMA (no multicast)
+// ------------------------------------------------------------------------------- TMA (per-CTA loads)
 __device__ __forceinline__ void tma_prefetch_desc(const void* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
 }
@@ -200,20 +200,34 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* r) {
       : "memory");
 }
 
-// 2^x for x <= 0 on the FMA pipe: Cody-Waite split x = i + f (i = floor(x), f in [0, 1)), a
-// degree-3 least-squares polynomial for 2^f (relative error < 8e-5, fitted for this code base),
-// and the integer i added to the exponent field. The polynomial dips just below 1 at f = 0
-// (biased exponent 126), so i must stay >= -125 for the exponent add to stay in range; inputs
-// at or below -125 return exactly 0 (masked scores).
-__device__ __forceinline__ float poly_exp2(float x) {
-  const float xc = fmaxf(x, -125.f);
-  const float fi = floorf(xc);
-  const float f = xc - fi;
-  float p = fmaf(0.07790716377386663f, f, 0.22623319419985655f);
-  p = fmaf(p, f, 0.6957770964274217f);
-  p = fmaf(p, f, 0.9999278266445136f);
-  const float r = __int_as_float(__float_as_int(p) + (int(fi) << 23));
-  return x <= -125.f ? 0.f : r;
+// Two 2^x on the FMA/ALU pipes (no MUFU, no float->int conversion): Cody-Waite split
+// x = n + f with n = round(x) obtained by adding and subtracting 1.5 * 2^23 (the integer lands in
+// the low mantissa bits of the sum), f in [-0.5, 0.5], a degree-3 least-squares polynomial for 2^f
+// (relative error < 8e-5, fitted for this code base), and n added to the exponent field. Inputs
+// at or below -125 (masked scores) return exactly 0.
+__device__ __forceinline__ float2 poly_exp2_x2(float2 x) {
+  constexpr float kRound = 12582912.f;  // 1.5 * 2^23, bit pattern 0x4B400000
+  const float2 xc = make_float2(fmaxf(x.x, -125.f), fmaxf(x.y, -125.f));
+  const float2 j = __fadd2_rn(xc, make_float2(kRound, kRound));
+  const float2 n = __fadd2_rn(j, make_float2(-kRound, -kRound));
+  const float2 f = __ffma2_rn(n, make_float2(-1.f, -1.f), xc);
+  float2 p = __ffma2_rn(make_float2(0.05508868380751203f, 0.05508868380751203f), f,
+                        make_float2(0.24260405145947925f, 0.24260405145947925f));
+  p = __ffma2_rn(p, f, make_float2(0.6932762416819613f, 0.6932762416819613f));
+  p = __ffma2_rn(p, f, make_float2(0.9999289403695117f, 0.9999289403695117f));
+  const int nx = __float_as_int(j.x) - 0x4B400000;
+  const int ny = __float_as_int(j.y) - 0x4B400000;
+  float2 r = make_float2(__int_as_float(__float_as_int(p.x) + (nx << 23)),
+                         __int_as_float(__float_as_int(p.y) + (ny << 23)));
+  r.x = x.x <= -125.f ? 0.f : r.x;
+  r.y = x.y <= -125.f ? 0.f : r.y;
+  return r;
+}
+
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
 }
 
 // Arrive on an mbarrier once all previously issued tcgen05.mma of this thread have completed.

@@ -9,7 +9,7 @@
 //
 // Design (sm_100a):
 //   * one CTA per SM (persistent), 128x256 output tile, BK = 64 (one 128-byte swizzle atom),
-//     4-stage TMA ring for A/B tiles (local memory only, no multicast);
+//     4-stage TMA ring for A/B tiles (each CTA loads its own tiles from local memory);
 //   * warp 0: TMA producer; warp 1: single-thread tcgen05.mma issuer (M=128, N=256, K=16);
 //     warp 2: TMEM allocator; warps 4-7: epilogue (thread i owns accumulator row i);
 //   * two 256-column TMEM accumulators so the epilogue of tile i overlaps the mainloop of i+1;

@@ -1,0 +1,49 @@
+"""Ring-attention oracle suite on CPU: the reference's seven cases (non-causal MHA, uneven chunks and
+blocks, 1-4 domains) plus causal / GQA / zigzag / striped extensions and the benchmark plumbing case
+(1024/512 split, 16 query heads, 4 KV heads, D=64, fp32, tolerance 1e-4 on O and LSE)."""
+
+import json
+
+import pytest
+import torch
+
+from hetero_cp_ringattn_b200 import correctness as C
+from hetero_cp_ringattn_b200.cli import main as cli_main
+from hetero_cp_ringattn_b200.errors import ToleranceTier
+
+
+@pytest.mark.parametrize("name,cfg", C.default_cases() + C.extended_cases(), ids=lambda x: x if isinstance(x, str) else "")
+def test_ring_model_matches_full_attention_f64(name, cfg):
+    rep = C.run_case(name, cfg, seeds=[0, 1] if cfg.global_seq_len <= 256 else [0],
+                     tier=ToleranceTier.STRICT)
+    assert rep["passed"], rep["worst_seed"]
+
+
+def test_baseline_plumbing_case_fp32():
+    cfg = C.CaseConfig([1024, 512], [1024, 512], 16, 64, num_kv_heads=4, causal=True)
+    r = C.run_case_single_seed(cfg, seed=0, dtype=torch.float32)
+    assert r["output"]["max_abs_err"] < 1e-4
+    assert r["lse"]["max_abs_err"] < 1e-4
+
+
+def test_merge_partials_is_exact():
+    from hetero_cp_ringattn_b200.ops import reference as ref
+    torch.manual_seed(0)
+    q = torch.randn(7, 4, 16, dtype=torch.float64)
+    k = torch.randn(30, 2, 16, dtype=torch.float64)
+    v = torch.randn(30, 2, 16, dtype=torch.float64)
+    o, lse = ref.full_attention(q, k, v, causal=False)
+    parts = [ref.full_attention(q, k[a:b], v[a:b], causal=False) for a, b in [(0, 11), (11, 12), (12, 30)]]
+    om, lm = ref.merge_partials([p[0] for p in parts], [p[1] for p in parts])
+    assert (om - o).abs().max() < 1e-12 and (lm - lse).abs().max() < 1e-12
+    # an empty shard (lse = -inf) contributes nothing
+    e = (torch.zeros_like(o), torch.full_like(lse, float("-inf")))
+    om2, lm2 = ref.merge_partials([e[0], o], [e[1], lse])
+    assert (om2 - o).abs().max() < 1e-12 and (lm2 - lse).abs().max() < 1e-12
+
+
+def test_cli_correctness_report(tmp_path):
+    path = tmp_path / "ring.json"
+    assert cli_main(["correctness", "--report-path", str(path), "--stress-test", "1"]) == 0
+    rep = json.loads(path.read_text())
+    assert rep["passed"] and len(rep["cases"]) == 10
