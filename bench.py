@@ -39,7 +39,12 @@ def parse():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--impl", default="hcp", choices=["hcp", "reference"])
+    ap.add_argument("--impl", default="hcp", choices=["hcp", "reference", "torch-restatement"],
+                    help="hcp: this framework; reference: the unmodified reference (unavailable "
+                         "here); torch-restatement: the reference's algorithm restated in stock "
+                         "PyTorch (benchmarks/ref_ring_torch.py), for a same-box comparison")
+    ap.add_argument("--restatement-decode", type=int, default=32,
+                    help="decode steps timed for the torch restatement")
     ap.add_argument("--config", default="llama-3.2-1b-32k", choices=sorted(CONFIGS))
     ap.add_argument("--strategy", default=None, help="vanilla|striped|zigzag (default: zigzag for N>1)")
     ap.add_argument("--ratio", default=None, help="capacity ratio override, e.g. 5:5:1")
@@ -64,11 +69,76 @@ def reference_unavailable(args) -> None:
         }), flush=True)
 
 
+def run_restatement(args) -> int:
+    """Time the PyTorch restatement of the reference's algorithm on the same config."""
+    import torch.distributed as dist
+    from benchmarks.ref_ring_torch import RefRingModel, hf_random_weights
+    from hetero_cp_ringattn_b200.config import preset
+    from hetero_cp_ringattn_b200.parallel.capacity import equal_chunks
+    from hetero_cp_ringattn_b200.utils.perf import max_over_ranks
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                                timeout=timedelta(seconds=900))
+    spec = CONFIGS[args.config]
+    cfg = preset(spec["model"])
+    Lp = spec["prompt"]
+    chunks = equal_chunks(Lp, world)
+    model = RefRingModel(cfg, hf_random_weights(cfg, dev), rank, world, dev)
+    prompt = torch.randint(0, cfg.vocab_size, (Lp,), generator=torch.Generator().manual_seed(1234))
+    steps_dec = max(1, args.restatement_decode)
+
+    def one():
+        e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+        e0.record()
+        tok = model.prefill(prompt, chunks)
+        e1.record()
+        for _ in range(steps_dec):
+            tok = model.decode_step(tok)
+        e2.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1), e1.elapsed_time(e2)
+
+    for _ in range(max(1, args.warmup)):
+        one()
+    pre, dec = [], []
+    for _ in range(args.steps):
+        p, d = one()
+        pre.append(p)
+        dec.append(d)
+    prefill_ms = max_over_ranks(sum(pre) / len(pre))
+    decode_ms = max_over_ranks(sum(dec) / len(dec))
+    if rank == 0:
+        print(json.dumps({
+            "impl": "torch-restatement",
+            "note": "stock-PyTorch restatement of the reference's ring algorithm "
+                    "(benchmarks/ref_ring_torch.py); not the reference itself",
+            "metric": "prefill tok/s & TTFT @32k and decode tok/s (CP=N B200, max over ranks)",
+            "value": Lp / (prefill_ms / 1e3), "unit": "prompt tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ttft_ms": prefill_ms,
+            "decode_ms_per_token": decode_ms / steps_dec,
+            "decode_tok_s": steps_dec / (decode_ms / 1e3), "dtype": "bf16",
+            "config": {"model": spec["model"], "seq_len": Lp, "chunks": chunks,
+                       "strategy": "vanilla", "parallelism": f"cp{world}"},
+        }), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         reference_unavailable(args)
         return 0
+    if args.impl == "torch-restatement":
+        return run_restatement(args)
 
     from hetero_cp_ringattn_b200.config import preset, parse_ratio
     from hetero_cp_ringattn_b200.models.llama import LlamaCPEngine

@@ -190,6 +190,48 @@ def cmd_serve(args) -> int:
     return 0
 
 
+def cmd_compare_logits(args) -> int:
+    """Compare two logits exports (the reference's scripts/compare_logits.py): per-step max/mean
+    absolute difference and argmax agreement."""
+    import numpy as np
+    va, sa, a = read_logits(args.a)
+    vb, sb, b = read_logits(args.b)
+    if va != vb:
+        print(json.dumps({"error": f"vocab mismatch {va} vs {vb}"}))
+        return 1
+    n = min(sa, sb) + 1
+    rows = []
+    for i in range(n):
+        d = np.abs(a[i].astype(np.float64) - b[i].astype(np.float64))
+        rows.append({"step": i, "max_abs": float(d.max()), "mean_abs": float(d.mean()),
+                     "argmax_match": bool(int(a[i].argmax()) == int(b[i].argmax()))})
+    worst = max(r["max_abs"] for r in rows)
+    ok = worst <= args.tolerance and all(r["argmax_match"] for r in rows)
+    print(json.dumps({"steps": n, "worst_max_abs": worst, "passed": ok, "per_step": rows}))
+    return 0 if ok else 1
+
+
+def cmd_perf_summary(args) -> int:
+    """Aggregate an HCP_PERF_LOG JSONL file per event (the reference's parse_worker_perf.py)."""
+    import collections
+    agg = collections.defaultdict(lambda: collections.defaultdict(float))
+    counts = collections.Counter()
+    for line in open(args.path):
+        try:
+            ev = json.loads(line)
+        except json.JSONDecodeError:
+            continue
+        name = ev.get("event", "?")
+        counts[name] += 1
+        for k, v in ev.items():
+            if isinstance(v, (int, float)) and not isinstance(v, bool) and k not in ("ts", "layer", "domain"):
+                agg[name][k] += v
+    out = {name: {"count": counts[name], **{k: v / counts[name] for k, v in fields.items()}}
+           for name, fields in agg.items()}
+    print(json.dumps(out, indent=2))
+    return 0
+
+
 def cmd_gen_prompt(args) -> int:
     g = torch.Generator().manual_seed(args.seed)
     ids = torch.randint(0, args.vocab, (args.tokens,), generator=g)
@@ -229,6 +271,14 @@ def main(argv: Optional[List[str]] = None) -> int:
     s.add_argument("--session-continuation-tokens", type=int, default=64)
     s.add_argument("--http-addr", default=None)
     s.set_defaults(fn=cmd_serve)
+    cl = sub.add_parser("compare-logits")
+    cl.add_argument("a")
+    cl.add_argument("b")
+    cl.add_argument("--tolerance", type=float, default=2e-2)
+    cl.set_defaults(fn=cmd_compare_logits)
+    ps = sub.add_parser("perf-summary")
+    ps.add_argument("path")
+    ps.set_defaults(fn=cmd_perf_summary)
     g = sub.add_parser("gen-prompt")
     g.add_argument("--tokens", type=int, required=True)
     g.add_argument("--vocab", type=int, default=128256)

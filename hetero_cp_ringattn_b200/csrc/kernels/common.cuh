@@ -204,7 +204,8 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* r) {
 // x = n + f with n = round(x) obtained by adding and subtracting 1.5 * 2^23 (the integer lands in
 // the low mantissa bits of the sum), f in [-0.5, 0.5], a degree-3 least-squares polynomial for 2^f
 // (relative error < 8e-5, fitted for this code base), and n added to the exponent field. Inputs
-// at or below -125 (masked scores) return exactly 0.
+// are clamped at -125, so masked scores (-inf) return 2^-125 (about 2e-38), which is zero for
+// every sum they enter.
 __device__ __forceinline__ float2 poly_exp2_x2(float2 x) {
   constexpr float kRound = 12582912.f;  // 1.5 * 2^23, bit pattern 0x4B400000
   const float2 xc = make_float2(fmaxf(x.x, -125.f), fmaxf(x.y, -125.f));
@@ -217,11 +218,8 @@ __device__ __forceinline__ float2 poly_exp2_x2(float2 x) {
   p = __ffma2_rn(p, f, make_float2(0.9999289403695117f, 0.9999289403695117f));
   const int nx = __float_as_int(j.x) - 0x4B400000;
   const int ny = __float_as_int(j.y) - 0x4B400000;
-  float2 r = make_float2(__int_as_float(__float_as_int(p.x) + (nx << 23)),
-                         __int_as_float(__float_as_int(p.y) + (ny << 23)));
-  r.x = x.x <= -125.f ? 0.f : r.x;
-  r.y = x.y <= -125.f ? 0.f : r.y;
-  return r;
+  return make_float2(__int_as_float(__float_as_int(p.x) + (nx << 23)),
+                     __int_as_float(__float_as_int(p.y) + (ny << 23)));
 }
 
 __device__ __forceinline__ float max3f(float a, float b, float c) {

@@ -26,6 +26,7 @@ namespace dec {
 using namespace hcp::dev;
 
 constexpr float kLog2e = 1.4426950408889634f;
+constexpr int kMaxDecodeSplits = 128;
 
 __device__ __forceinline__ void dot8_acc(const uint4 w, const uint4 x, float& acc) {
   const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
@@ -208,7 +209,7 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(GemvArgs a) {
 
 template <int EPI, bool NORM>
 static cudaError_t gemv_launch(const GemvArgs& a, cudaStream_t s) {
-  constexpr int R = (EPI == kGemvSwiGLU) ? 2 : 4;
+  constexpr int R = 4;  // output rows (gate/up pairs for SwiGLU) per CTA
   const int out_rows = (EPI == kGemvSwiGLU) ? a.N / 2 : a.N;
   const int grid = (out_rows + R - 1) / R;
   const size_t smem = NORM ? size_t(a.B) * a.K * 2 : 0;
@@ -391,23 +392,51 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(DecodeAttnArgs a) {
   const unsigned long long epoch =
       a.epoch_parity_src ? (*a.epoch_parity_src * a.epoch_mul + a.epoch_add) : a.epoch_add;
   const int parity = int(epoch & 1ull);
+  // split weights: all LSEs into shared memory at once (L2 reads, the other CTAs' writes are
+  // visible after the fence + counter), then one warp per head reduces max and weight sum
+  __shared__ float s_w[G][kMaxDecodeSplits];
+  __shared__ float s_mx[G], s_ws[G];
+  for (int i = threadIdx.x; i < G * a.splits; i += blockDim.x) {
+    const int g = i / a.splits, s = i % a.splits;
+    s_w[g][s] = __ldcg(a.part_lse + (long)(b * H + h * G + g) * a.splits + s);
+  }
+  __syncthreads();
+  for (int g = warp; g < G; g += 4) {
+    float mx = -INFINITY;
+    for (int s = lane; s < a.splits; s += 32) mx = fmaxf(mx, s_w[g][s]);
+    mx = warp_max(mx);
+    float ws = 0.f;
+    for (int s = lane; s < a.splits; s += 32) {
+      const float w = mx == -INFINITY ? 0.f : fast_exp2(s_w[g][s] - mx);
+      s_w[g][s] = w;
+      ws += w;
+    }
+    ws = warp_sum(ws);
+    if (lane == 0) {
+      s_mx[g] = mx;
+      s_ws[g] = ws;
+    }
+  }
+  __syncthreads();
   for (int i = threadIdx.x; i < G * (D + 1); i += blockDim.x) {
     const int g = i / (D + 1), d = i % (D + 1);
-    const float* pl = a.part_lse + (long)(b * H + h * G + g) * a.splits;
-    float mx = -INFINITY;
-    for (int s = 0; s < a.splits; ++s) mx = fmaxf(mx, ((volatile const float*)pl)[s]);
     float val;
-    if (mx == -INFINITY) {
+    if (s_mx[g] == -INFINITY) {
       val = (d < D) ? 0.f : -INFINITY;
+    } else if (d == D) {
+      val = s_mx[g] + __log2f(s_ws[g]);
     } else {
-      float ws = 0.f, o = 0.f;
-      const float* pof = a.part_o + (long)(b * H + h * G + g) * a.splits * D;
-      for (int s = 0; s < a.splits; ++s) {
-        const float w = fast_exp2(((volatile const float*)pl)[s] - mx);
-        ws += w;
-        if (d < D) o += w * ((volatile const float*)pof)[(long)s * D + d];
+      const float* pof = a.part_o + (long)(b * H + h * G + g) * a.splits * D + d;
+      float o0 = 0.f, o1 = 0.f, o2 = 0.f, o3 = 0.f;
+      int s = 0;
+      for (; s + 4 <= a.splits; s += 4) {
+        o0 = fmaf(s_w[g][s], __ldcg(pof + (long)s * D), o0);
+        o1 = fmaf(s_w[g][s + 1], __ldcg(pof + (long)(s + 1) * D), o1);
+        o2 = fmaf(s_w[g][s + 2], __ldcg(pof + (long)(s + 2) * D), o2);
+        o3 = fmaf(s_w[g][s + 3], __ldcg(pof + (long)(s + 3) * D), o3);
       }
-      val = (d < D) ? o / ws : mx + __log2f(ws);
+      for (; s < a.splits; ++s) o0 = fmaf(s_w[g][s], __ldcg(pof + (long)s * D), o0);
+      val = ((o0 + o1) + (o2 + o3)) / s_ws[g];
     }
     // exchange slot layout: [2 parity][N src][B][H][D+1] fp32
     const long off = (((long)parity * a.n_ranks + a.my_rank) * a.B * H + (long)b * H + h * G + g) * (D + 1) + d;
@@ -472,6 +501,7 @@ const char* decode_attn(const DecodeAttnArgs& a, cudaStream_t s) {
   const int G = a.H / a.Hkv;
   if (a.H % a.Hkv) return "decode_attn: H % Hkv";
   if (a.n_ranks < 1 || a.n_ranks > kMaxRanks) return "decode_attn: bad n_ranks";
+  if (a.splits < 1 || a.splits > kMaxDecodeSplits) return "decode_attn: splits must be in [1, 128]";
   cudaError_t e = cudaErrorInvalidValue;
 #define HCP_DEC_CASE(DD, GG) \
   if (a.D == DD && G == GG) e = launch_attn<DD, GG>(a, s);

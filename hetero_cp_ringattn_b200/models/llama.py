@@ -193,14 +193,24 @@ class LlamaCPEngine:
         q_buf = torch.empty(T, self.H, self.D, dtype=torch.bfloat16, device=dev)
         o_buf = torch.empty_like(q_buf)
         start_tile = int(st.positions[0]) // 128 if st.strategy is RingStrategy.VANILLA else 0
+        trace = self.perf.enabled
         for li, lw in enumerate(w.layers):
+            if trace:
+                ev = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
+                ev[0].record()
             K.rmsnorm(x, lw.in_norm, self.cfg.rms_norm_eps, out=xn)
             qkv = K.gemm(xn, lw.wqkv, "bias" if lw.bqkv is not None else "store", bias=lw.bqkv)
             self.prefill_epoch += 1
             args = (qkv, pos, self.cos, self.sin, li, st.kv.pt_device, 0, Lp, start_tile,
                     self.scale, True, q_buf, o_buf, None, self.prefill_epoch)
+            if trace:
+                ev[1].record()
             self.rt.push_layer(*args)
+            if trace:
+                ev[2].record()
             self.rt.attend_layer(*args)
+            if trace:
+                ev[3].record()
             launches.count(2 + (3 if self.world > 1 else 0) - (1 if self.world > 1 and self.prefill_epoch <= 2 else 0))
             del qkv
             K.gemm(o_buf.view(T, self.H * self.D), lw.wo, "residual", residual=x)
@@ -208,7 +218,29 @@ class LlamaCPEngine:
             g = K.gemm(xn, lw.wgu, "swiglu")
             K.gemm(g, lw.wd, "residual", residual=x)
             del g
+            if trace:
+                ev[4].record()
+                self._emit_layer(st, li, T, Lp, ev)
         return self._first_token_cuda(st, x, return_logits)
+
+    def _emit_layer(self, st: RequestState, layer: int, T: int, Lp: int, ev) -> None:
+        """`ring_attention` perf event (the reference's HCP_PERF_LOG schema, ring.rs:1376-1395),
+        device-timed with CUDA events; bytes are the bf16 compact-GQA K/V rows this rank pushed to
+        its peers over NVLink and the rows its peers pushed to it."""
+        ev[4].synchronize()
+        row_bytes = 2 * self.Hkv * self.D * 2
+        sent = T * row_bytes * (self.world - 1)
+        recv = (Lp - T) * row_bytes
+        attn_ms = ev[2].elapsed_time(ev[3])
+        self.perf.emit("ring_attention", domain=self.rank, layer=layer, request=st.req_id,
+                       total_ms=ev[0].elapsed_time(ev[4]), qkv_ms=ev[0].elapsed_time(ev[1]),
+                       send_ms=ev[1].elapsed_time(ev[2]), local_compute_ms=attn_ms,
+                       peer_compute_ms=0.0, recv_ms=0.0, forward_ms=0.0, flush_ms=0.0,
+                       mlp_ms=ev[3].elapsed_time(ev[4]), kv_sent_bytes=sent, kv_recv_bytes=recv,
+                       wire_sent_bytes=sent, wire_recv_bytes=recv, micro_blocks=-(-Lp // 128),
+                       num_domains=self.world, seq_len=T, overlap=True,
+                       attn_tflops=4.0 * self.H * self.D * float(np.sum(st.positions + 1)) /
+                       max(attn_ms, 1e-6) / 1e9)
 
     def _first_token_cuda(self, st: RequestState, x: torch.Tensor, return_logits: bool):
         dev = self.device
@@ -549,6 +581,32 @@ class LlamaCPEngine:
         finally:
             self.release(req_id)
         return torch.cat(toks)
+
+    @torch.no_grad()
+    def generate_batch(self, prompts: Sequence[torch.Tensor], max_new_tokens: int,
+                       chunks_for=None, strategy="vanilla", first_id: int = 1 << 20) -> List[torch.Tensor]:
+        """Greedy generation for several prompts (rust/src/model/generator.rs:123-270
+        `BatchGenerator`): each prompt is prefilled (with its own chunk split), then every decode
+        step advances all rows in one batched step. Returns the generated ids per prompt."""
+        from ..parallel.capacity import equal_chunks
+        chunks_for = chunks_for or (lambda n: equal_chunks(n, self.world))
+        rids = list(range(first_id, first_id + len(prompts)))
+        firsts = []
+        try:
+            for rid, p in zip(rids, prompts):
+                tok, _ = self.prefill(rid, p, chunks_for(int(p.numel())), strategy,
+                                      decode_horizon=max(1, max_new_tokens))
+                firsts.append(tok.view(1))
+            cur = torch.cat(firsts)
+            outs = [cur]
+            for _ in range(max_new_tokens - 1):
+                cur = self.decode_step(rids, cur).view(-1)
+                outs.append(cur)
+        finally:
+            for rid in rids:
+                self.release(rid)
+        allt = torch.stack(outs, dim=1)
+        return [allt[i] for i in range(len(prompts))]
 
 
 class DecodeGraph:
