@@ -1,6 +1,6 @@
 """Headline benchmark: long-context prefill tok/s + TTFT and decode tok/s, CP = N ranks on one node.
 
-Config (BASELINE config #2): Llama-3.2-1B-shaped decoder (16 layers, hidden 2048, 32 heads,
+Config: Llama-3.2-1B-shaped decoder (16 layers, hidden 2048, 32 heads,
 8 KV heads, head_dim 64, SwiGLU 8192, vocab 128256, RoPE theta 5e5), bf16, random-init weights
 N(0, 0.02), a 32768-token prompt of uniform-random token ids, then 128 greedy tokens; equal chunks
 (zigzag layout for N > 1 so every rank carries the same causal work). One "step" is one full
@@ -24,7 +24,7 @@ import time
 
 import torch
 
-BASELINE_PREFILL_TOK_S = None  # BASELINE.json "published" is empty: no same-metric number to divide by
+BASELINE_PREFILL_TOK_S = None  # no published same-metric number of the reference to divide by
 
 CONFIGS = {
     "llama-3.2-1b-32k": dict(model="llama-3.2-1b", prompt=32768, new_tokens=128),
@@ -50,6 +50,8 @@ def parse():
     ap.add_argument("--ratio", default=None, help="capacity ratio override, e.g. 5:5:1")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-graphs", action="store_true")
+    ap.add_argument("--decode-batch", type=int, default=1,
+                    help="also time batched decode of B requests that share the prompt length")
     return ap.parse_args()
 
 
@@ -174,9 +176,12 @@ def main():
         chunks = equal_chunks(Lp, world)
 
     weights = PreparedWeights.random(cfg, seed=0, device=dev)
+    B = max(1, args.decode_batch)
+    page = 256
+    kv_pages = B * (-(-max(chunks) // page) + -(-(new_tokens + 8) // page)) + 2
     eng = LlamaCPEngine(cfg, weights, rank=rank, world=world, device=dev, group=group,
-                        max_context=Lp, max_batch=1, decode_reserve=new_tokens + 8,
-                        use_graphs=not args.no_graphs)
+                        max_context=Lp, max_batch=B, decode_reserve=new_tokens + 8,
+                        kv_pages=kv_pages, use_graphs=not args.no_graphs)
     gen = torch.Generator().manual_seed(1234)
     prompt = torch.randint(0, cfg.vocab_size, (Lp,), generator=gen, dtype=torch.int64).pin_memory()
     prompt_dev = prompt.to(dev)
@@ -255,6 +260,33 @@ def main():
                "decode_tok_s": (new_tokens - 1) / max(1e-9, total - ttft),
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 8 + new_tokens * 8}
 
+    # ---------------------------------------------------------------- batched decode (B requests)
+    batch = None
+    if B > 1:
+        ids = []
+        toks = []
+        for b in range(B):
+            req[0] += 1
+            tok, _ = eng.prefill(req[0], prompt_dev, chunks, strategy, decode_horizon=new_tokens)
+            ids.append(req[0])
+            toks.append(tok.view(1))
+        cur = torch.cat(toks)
+        for _ in range(3):
+            cur = eng.decode_step(ids, cur)
+        barrier()
+        b0, b1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        n_dec = new_tokens - 4
+        b0.record()
+        for _ in range(n_dec):
+            cur = eng.decode_step(ids, cur)
+        b1.record()
+        barrier()
+        bms = max_over_ranks(b0.elapsed_time(b1) / n_dec, group)
+        for i in ids:
+            eng.release(i)
+        batch = {"batch": B, "context": Lp, "decode_ms_per_step": bms,
+                 "decode_tok_s": B * 1e3 / bms, "steps_timed": n_dec}
+
     clk = clocks.summary()
     value = Lp / (prefill_ms / 1e3)
     if rank == 0:
@@ -283,6 +315,8 @@ def main():
             "clocks": clk,
             "e2e": e2e,
         }
+        if batch is not None:
+            out["decode_batch"] = batch
         print(json.dumps(out), flush=True)
     eng.close()
     if world > 1:

@@ -67,6 +67,7 @@ struct KParams {
   int num_kv_tiles_total;
   unsigned long long wait_budget_ns;
   int* status;
+  int pingpong;         // 1: the two softmax warpgroups take turns (see the softmax loop)
 };
 
 // processing order: kv_start_tile .. n-1 ascending, then kv_start_tile-1 .. 0 descending
@@ -74,6 +75,94 @@ __device__ __forceinline__ int kv_tile_at(int j, int n, int start) {
   if (start >= n) start = 0;
   const int up = n - start;
   return j < up ? start + j : start - 1 - (j - up);
+}
+
+// One softmax step of a q-tile row over a 128-column score tile held in TMEM: row max (one batch
+// of TMEM loads, 3-input maxima), lazy rescale of the running max and of O (only when the max
+// grows by more than 2^8), then P = 2^(s * scale - m) packed to bf16 into the first 64 columns
+// of S and the row sum. MASK = true applies the causal / length bound (kv position > lim gives
+// -inf); tiles below every row's bound use MASK = false and carry no per-element compare.
+template <int D, int POLY, bool MASK>
+__device__ __forceinline__ void softmax_step(uint32_t s_addr, uint32_t o_addr, int kv0, int lim,
+                                             float scale_log2, bool o_live, float& m_ref,
+                                             float& l_sum) {
+  float tmax;
+  {
+    uint32_t r[128];
+    tmem_ld32(s_addr, r);
+    tmem_ld32(s_addr + 32, r + 32);
+    tmem_ld32(s_addr + 64, r + 64);
+    tmem_ld32(s_addr + 96, r + 96);
+    tmem_wait_ld();
+    if (MASK) {
+#pragma unroll
+      for (int e = 0; e < 128; ++e)
+        if (kv0 + e > lim) r[e] = __float_as_uint(-INFINITY);
+    }
+    float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+    for (int e = 0; e < 128; e += 8)
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        m4[k] = max3f(m4[k], __uint_as_float(r[e + 2 * k]), __uint_as_float(r[e + 2 * k + 1]));
+    tmax = max3f(m4[0], m4[1], fmaxf(m4[2], m4[3])) * scale_log2;
+  }
+  float alpha = 1.f;
+  bool resc = false;
+  if (tmax > m_ref + kRescaleThreshold || (m_ref == -INFINITY && tmax > -INFINITY)) {
+    alpha = (m_ref == -INFINITY) ? 0.f : fast_exp2(m_ref - tmax);
+    m_ref = tmax;
+    resc = true;
+  }
+  const float m_use = (m_ref == -INFINITY) ? 0.f : m_ref;
+  // PV_i(j-1) completed before S_i(j) did (same issuing thread, in-order commits): O_i is
+  // stable here and can be rescaled in place
+  if (o_live && __any_sync(0xffffffffu, resc)) {
+#pragma unroll 1
+    for (int c = 0; c < D / 32; ++c) {
+      uint32_t o[32];
+      tmem_ld32(o_addr + c * 32, o);
+      tmem_wait_ld();
+#pragma unroll
+      for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+      tmem_st32(o_addr + c * 32, o);
+    }
+  }
+  // P in two halves of 64 columns, packed to bf16 into the first 64 columns of S (half h lands
+  // on columns already consumed); packed f32x2 arithmetic; POLY of every 8 pairs take the
+  // FMA-pipe polynomial, the rest the MUFU
+  float2 rs0 = make_float2(0.f, 0.f), rs1 = make_float2(0.f, 0.f);
+  const float2 negm = make_float2(-m_use, -m_use);
+  const float2 sc2 = make_float2(scale_log2, scale_log2);
+#pragma unroll
+  for (int hh = 0; hh < 2; ++hh) {
+    uint32_t r[64];
+    tmem_ld32(s_addr + hh * 64, r);
+    tmem_ld32(s_addr + hh * 64 + 32, r + 32);
+    tmem_wait_ld();
+    uint32_t pk[32];
+#pragma unroll
+    for (int e = 0; e < 64; e += 2) {
+      float2 x = __ffma2_rn(make_float2(__uint_as_float(r[e]), __uint_as_float(r[e + 1])), sc2, negm);
+      if (MASK) {
+        if (kv0 + hh * 64 + e > lim) x.x = -INFINITY;
+        if (kv0 + hh * 64 + e + 1 > lim) x.y = -INFINITY;
+      }
+      float2 pp;
+      if (POLY > 0 && ((e >> 1) & 7) >= 8 - POLY) {
+        pp = poly_exp2_x2(x);
+      } else {
+        pp.x = fast_exp2(x.x);
+        pp.y = fast_exp2(x.y);
+      }
+      if ((e >> 1) & 1) rs1 = __fadd2_rn(rs1, pp);
+      else rs0 = __fadd2_rn(rs0, pp);
+      pk[e >> 1] = pack_bf16x2(pp.x, pp.y);
+    }
+    tmem_st32(s_addr + hh * 32, pk);
+  }
+  tmem_wait_st();
+  l_sum = l_sum * alpha + ((rs0.x + rs0.y) + (rs1.x + rs1.y));
 }
 
 // POLY: how many of every 8 exponential pairs use the FMA-pipe polynomial instead of the MUFU
@@ -157,6 +246,11 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int start = p.kv_start_tile < n_tiles ? p.kv_start_tile : 0;
   const bool tile1_live = (row0 + BQ) < p.T;
 
+  // register split: warpgroup 0 (TMA, MMA, TMEM allocator, idle warp) hands registers to the two
+  // softmax warpgroups: 128 x 88 + 256 x 208 = 384 x 168, the launch's total. Each warpgroup
+  // executes its setmaxnreg at one point, before its warps take their roles.
+  if (warp < 4) {
+  reg_dealloc<88>();
   if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer
     if (elect_one() && n_tiles > 0) {
@@ -268,7 +362,9 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
       }
     }
-  } else if (warp >= 4) {
+  }
+  } else {
+    reg_alloc<208>();
     // ------------------------------------------------------------------ softmax warpgroups
     const int q4 = warp % 4;
     const int row = q4 * 32 + lane;
@@ -276,105 +372,31 @@ __global__ void __launch_bounds__(THREADS, 1)
     const uint32_t lane_off = uint32_t(q4 * 32) << 16;
     const uint32_t s_addr = tmem_base + lane_off + uint32_t(tile * BKV);
     const uint32_t o_addr = tmem_base + lane_off + uint32_t(C::O_COL + tile * D);
-    const int qmin = s_qmin[tile];
     const bool live = (tile == 0) || tile1_live;
     float m_ref = -INFINITY;  // max used for exponentiation (log2 domain)
     float l_sum = 0.f;
     bool ok = true;
-    const float2 sc2 = make_float2(p.scale_log2, p.scale_log2);
     for (int j = 0; j < n_tiles; ++j) {
       const int t = kv_tile_at(j, n_tiles, start);
       // ping-pong: tile 1 runs its softmax for step j after tile 0 finished step j, tile 0 runs
       // step j after tile 1 finished step j - 1, so one warpgroup's exponentials overlap the
       // tensor core's work on the other tile
-      if (tile == 1) ok = mbar_wait(&turn[1], j & 1, p.status, 211);
-      else if (j > 0) ok = mbar_wait(&turn[0], (j - 1) & 1, p.status, 212);
+      if (p.pingpong) {
+        if (tile == 1) ok = mbar_wait(&turn[1], j & 1, p.status, 211);
+        else if (j > 0) ok = mbar_wait(&turn[0], (j - 1) & 1, p.status, 212);
+      }
       if (!ok || !mbar_wait(&s_full[tile], j & 1, p.status, 208)) {
         ok = false;
         break;
       }
       tc_fence_after();
       const int kv0 = t * BKV;
-      const bool need_mask = (p.causal && kv0 + BKV - 1 > qmin) || (kv0 + BKV > p.L) || my_pos < 0;
       const int lim = p.causal ? min(my_pos, p.L - 1) : p.L - 1;  // last visible kv position
-      // pass 1: the whole score row in one batch of TMEM loads, row max with 3-input maxima
-      float tmax;
-      {
-        uint32_t r[128];
-        tmem_ld32(s_addr, r);
-        tmem_ld32(s_addr + 32, r + 32);
-        tmem_ld32(s_addr + 64, r + 64);
-        tmem_ld32(s_addr + 96, r + 96);
-        tmem_wait_ld();
-        if (need_mask) {
-#pragma unroll
-          for (int e = 0; e < 128; ++e)
-            if (kv0 + e > lim) r[e] = __float_as_uint(-INFINITY);
-        }
-        float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-#pragma unroll
-        for (int e = 0; e < 128; e += 8)
-#pragma unroll
-          for (int k = 0; k < 4; ++k)
-            m4[k] = max3f(m4[k], __uint_as_float(r[e + 2 * k]), __uint_as_float(r[e + 2 * k + 1]));
-        tmax = max3f(m4[0], m4[1], fmaxf(m4[2], m4[3])) * p.scale_log2;
-      }
-      // lazy rescale: the reference max only moves when it grows by more than the threshold
-      float alpha = 1.f;
-      bool resc = false;
-      if (tmax > m_ref + kRescaleThreshold || (m_ref == -INFINITY && tmax > -INFINITY)) {
-        alpha = (m_ref == -INFINITY) ? 0.f : fast_exp2(m_ref - tmax);
-        m_ref = tmax;
-        resc = true;
-      }
-      const float m_use = (m_ref == -INFINITY) ? 0.f : m_ref;
-      // PV_i(j-1) completed before S_i(j) did (same issuing thread, in-order commits): O_i is
-      // stable here and can be rescaled in place
-      if (j > 0 && __any_sync(0xffffffffu, resc)) {
-#pragma unroll 1
-        for (int c = 0; c < D / 32; ++c) {
-          uint32_t o[32];
-          tmem_ld32(o_addr + c * 32, o);
-          tmem_wait_ld();
-#pragma unroll
-          for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
-          tmem_st32(o_addr + c * 32, o);
-        }
-      }
-      // pass 2: P = 2^(s * scale - m) in two halves of 64 columns, packed to bf16 into the first
-      // 64 columns of S_i (half h lands on columns already consumed). Packed f32x2 arithmetic;
-      // 3 of every 8 pairs take the FMA-pipe polynomial, the rest the MUFU.
-      float2 rs0 = make_float2(0.f, 0.f), rs1 = make_float2(0.f, 0.f);
-      const float2 negm = make_float2(-m_use, -m_use);
-#pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        uint32_t r[64];
-        tmem_ld32(s_addr + hh * 64, r);
-        tmem_ld32(s_addr + hh * 64 + 32, r + 32);
-        tmem_wait_ld();
-        uint32_t pk[32];
-#pragma unroll
-        for (int e = 0; e < 64; e += 2) {
-          float2 x = __ffma2_rn(make_float2(__uint_as_float(r[e]), __uint_as_float(r[e + 1])), sc2, negm);
-          if (need_mask) {
-            if (kv0 + hh * 64 + e > lim) x.x = -INFINITY;
-            if (kv0 + hh * 64 + e + 1 > lim) x.y = -INFINITY;
-          }
-          float2 pp;
-          if (POLY > 0 && ((e >> 1) & 7) >= 8 - POLY) {
-            pp = poly_exp2_x2(x);
-          } else {
-            pp.x = fast_exp2(x.x);
-            pp.y = fast_exp2(x.y);
-          }
-          if ((e >> 1) & 1) rs1 = __fadd2_rn(rs1, pp);
-          else rs0 = __fadd2_rn(rs0, pp);
-          pk[e >> 1] = pack_bf16x2(pp.x, pp.y);
-        }
-        tmem_st32(s_addr + hh * 32, pk);
-      }
-      tmem_wait_st();
-      l_sum = l_sum * alpha + ((rs0.x + rs0.y) + (rs1.x + rs1.y));
+      // the masked variant only for tiles that cross some row's bound (diagonal / tail tiles)
+      if (__any_sync(0xffffffffu, kv0 + BKV - 1 > lim))
+        softmax_step<D, POLY, true>(s_addr, o_addr, kv0, lim, p.scale_log2, j > 0, m_ref, l_sum);
+      else
+        softmax_step<D, POLY, false>(s_addr, o_addr, kv0, lim, p.scale_log2, j > 0, m_ref, l_sum);
       tc_fence_before();
       mbar_arrive(&p_full[tile]);
       mbar_arrive(&turn[tile ^ 1]);
@@ -434,6 +456,16 @@ static cudaError_t launch(const CUtensorMap& tq, const CUtensorMap& tk, const CU
 }
 
 // Polynomial share per head_dim (out of 8 exponential pairs); HCP_ATTN_POLY overrides it (0-3).
+// Softmax warpgroup turn-taking (HCP_ATTN_PINGPONG=0 lets both run freely).
+static int pingpong_enabled() {
+  static int env = -2;
+  if (env == -2) {
+    const char* s = getenv("HCP_ATTN_PINGPONG");
+    env = (s && *s) ? atoi(s) : 1;
+  }
+  return env != 0;
+}
+
 static int poly_share(int D) {
   static int env = -2;
   if (env == -2) {
@@ -494,6 +526,7 @@ const char* attn_fwd(const AttnArgs& a, cudaStream_t stream) {
   p.num_kv_tiles_total = (a.L + BKV - 1) / BKV;
   p.wait_budget_ns = a.wait_budget_ns;
   p.status = a.status;
+  p.pingpong = pingpong_enabled();
   cudaError_t e = a.D == 64 ? launch_d<64>(tq, tk, tv, p, stream) : launch_d<128>(tq, tk, tv, p, stream);
   return e == cudaSuccess ? nullptr : cudaGetErrorString(e);
 }

@@ -216,10 +216,21 @@ __device__ __forceinline__ float2 poly_exp2_x2(float2 x) {
                         make_float2(0.24260405145947925f, 0.24260405145947925f));
   p = __ffma2_rn(p, f, make_float2(0.6932762416819613f, 0.6932762416819613f));
   p = __ffma2_rn(p, f, make_float2(0.9999289403695117f, 0.9999289403695117f));
-  const int nx = __float_as_int(j.x) - 0x4B400000;
-  const int ny = __float_as_int(j.y) - 0x4B400000;
-  return make_float2(__int_as_float(__float_as_int(p.x) + (nx << 23)),
-                     __int_as_float(__float_as_int(p.y) + (ny << 23)));
+  // j's low mantissa bits hold n (j = 1.5 * 2^23 + n), and 0x4B400000 << 23 wraps to 0 in 32
+  // bits, so (bits(j) << 23) == n << 23: one shift-add scales p by 2^n
+  return make_float2(__uint_as_float(__float_as_uint(p.x) + (__float_as_uint(j.x) << 23)),
+                     __uint_as_float(__float_as_uint(p.y) + (__float_as_uint(j.y) << 23)));
+}
+
+// Warpgroup register reallocation (all four warps of a warpgroup execute the same one). The
+// increases and decreases of a block must add up to at most the registers it was launched with.
+template <int N>
+__device__ __forceinline__ void reg_alloc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <int N>
+__device__ __forceinline__ void reg_dealloc() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
 }
 
 __device__ __forceinline__ float max3f(float a, float b, float c) {

@@ -4,13 +4,17 @@
 // chunks 512/256/256 and blocks 128/64/64; Init -> Run -> Shutdown per domain). Here the three
 // domains are emulated on one GPU (every domain's push runs before any domain's attend, so no
 // launch waits on a later one), each runs one real ring-attention layer through the runtime, and
-// every domain's output rows are checked for finiteness. Without a GPU only the config checks run.
+// every domain's rotated Q rows and attention output are compared with a double-precision CPU
+// oracle (rotate-half RoPE on the bf16 inputs, then causal GQA softmax attention over all 1024
+// positions), the check the reference's ATen bridge makes in src/rust_bridge.cc:614-928.
+// Without a GPU only the config checks run.
 //
 //   hcp_runtime_smoke            exit 0 on success
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
 #include <cmath>
+#include <algorithm>
 #include <cstdio>
 #include <vector>
 
@@ -85,11 +89,31 @@ int main() {
   cudaMemcpy(dsin, hsin.data(), hsin.size() * 4, cudaMemcpyHostToDevice);
   std::vector<RingLayerArgs> args(N);
   std::vector<void*> bufs;
+  // host copy of every position's rotated q and k (bf16-rounded, as the kernel stores them) and v
+  std::vector<float> rq(size_t(L) * H * D), rk(size_t(L) * HKV * D), rv(size_t(L) * HKV * D);
+  auto rope_row = [&](const __nv_bfloat16* x, int p, float* out) {
+    for (int j = 0; j < half; ++j) {
+      const double a = __bfloat162float(x[j]), b = __bfloat162float(x[j + half]);
+      const double c = hcos[size_t(p) * half + j], sn = hsin[size_t(p) * half + j];
+      out[j] = __bfloat162float(__float2bfloat16(float(a * c - b * sn)));
+      out[j + half] = __bfloat162float(__float2bfloat16(float(b * c + a * sn)));
+    }
+  };
   int offset = 0;
   for (int r = 0; r < N; ++r) {
     const int T = int(cfg.domains[r].seq_chunk_len);
     std::vector<__nv_bfloat16> hq(size_t(T) * width);
     for (size_t i = 0; i < hq.size(); ++i) hq[i] = __float2bfloat16(float(std::sin(0.37 * double(i + offset * width))) * 0.5f);
+    for (int t = 0; t < T; ++t) {
+      const int p = offset + t;
+      const __nv_bfloat16* row = hq.data() + size_t(t) * width;
+      for (int h = 0; h < H; ++h) rope_row(row + h * D, p, rq.data() + (size_t(p) * H + h) * D);
+      for (int h = 0; h < HKV; ++h) {
+        rope_row(row + (H + h) * D, p, rk.data() + (size_t(p) * HKV + h) * D);
+        for (int d = 0; d < D; ++d)
+          rv[(size_t(p) * HKV + h) * D + d] = __bfloat162float(row[(H + HKV + h) * D + d]);
+      }
+    }
     std::vector<int> hpos(T), hpt(4);
     for (int t = 0; t < T; ++t) hpos[t] = offset + t;
     for (int i = 0; i < 4; ++i) hpt[i] = r * 2 + (i % 2);  // 2 pages (512 slots) per domain
@@ -131,20 +155,55 @@ int main() {
     if (!(st = rts[r].AttendLayer(args[r], 0)).ok()) return fail("AttendLayer", st);
   for (int r = 0; r < N; ++r)
     if (!(st = rts[r].CheckDevice(0)).ok()) return fail("CheckDevice", st);
+  const double scale = 1.0 / std::sqrt(double(D));
+  std::vector<double> sc(L), acc(D);
+  offset = 0;
   for (int r = 0; r < N; ++r) {
     const int T = args[r].T;
-    std::vector<__nv_bfloat16> ho(size_t(T) * H * D);
+    std::vector<__nv_bfloat16> ho(size_t(T) * H * D), hqo(size_t(T) * H * D);
     cudaMemcpy(ho.data(), args[r].o_out, ho.size() * 2, cudaMemcpyDeviceToHost);
-    double s = 0;
-    for (auto v : ho) {
-      const float f = __bfloat162float(v);
-      if (!std::isfinite(f)) {
-        std::fprintf(stderr, "[smoke] domain %d produced a non-finite output\n", r);
-        return 1;
+    cudaMemcpy(hqo.data(), args[r].q_out, hqo.size() * 2, cudaMemcpyDeviceToHost);
+    double q_err = 0, o_err = 0, s = 0;
+    for (int t = 0; t < T; ++t) {
+      const int p = offset + t;
+      for (int h = 0; h < H; ++h) {
+        const float* q = rq.data() + (size_t(p) * H + h) * D;
+        const int g = h / (H / HKV);
+        double m = -1e300, l = 0;
+        for (int j = 0; j <= p; ++j) {
+          const float* k = rk.data() + (size_t(j) * HKV + g) * D;
+          double dot = 0;
+          for (int d = 0; d < D; ++d) dot += double(q[d]) * k[d];
+          sc[j] = dot * scale;
+          m = std::max(m, sc[j]);
+        }
+        std::fill(acc.begin(), acc.end(), 0.0);
+        for (int j = 0; j <= p; ++j) {
+          const double e = std::exp(sc[j] - m);
+          l += e;
+          const float* v = rv.data() + (size_t(j) * HKV + g) * D;
+          for (int d = 0; d < D; ++d) acc[d] += e * v[d];
+        }
+        for (int d = 0; d < D; ++d) {
+          const size_t i = (size_t(t) * H + h) * D + d;
+          const float f = __bfloat162float(ho[i]);
+          if (!std::isfinite(f)) {
+            std::fprintf(stderr, "[smoke] domain %d produced a non-finite output\n", r);
+            return 1;
+          }
+          o_err = std::max(o_err, std::fabs(double(f) - acc[d] / l));
+          q_err = std::max(q_err, std::fabs(double(__bfloat162float(hqo[i])) - q[d]));
+          s += std::fabs(f);
+        }
       }
-      s += std::fabs(f);
     }
-    std::printf("[smoke] domain %d: %d rows, mean |o| = %.4f\n", r, T, s / double(ho.size()));
+    std::printf("[smoke] domain %d: %d rows, mean |o| = %.4f, max |q - oracle| = %.2e, "
+                "max |o - oracle| = %.2e\n", r, T, s / double(ho.size()), q_err, o_err);
+    if (q_err > 1e-2 || o_err > 2e-2) {
+      std::fprintf(stderr, "[smoke] domain %d differs from the CPU oracle\n", r);
+      return 1;
+    }
+    offset += T;
   }
   for (void* b : bufs) cudaFree(b);
   cudaFree(dcos);

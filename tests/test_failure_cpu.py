@@ -1,6 +1,6 @@
 """Failure detection on CPU ranks (gloo): nothing here faults, traps or hangs a GPU.
 
-Parity with the reference's failure handling (SURVEY 5.3): bounded control-plane timeouts
+Parity with the reference's failure handling: bounded control-plane timeouts
 (protocol.rs:348-353, HCP_QUIC_TIMEOUT_SECS), errors returned as `Error` responses without killing
 the worker (runtime.rs:275,310), reservation rollback on a failed prefill (coordinator.rs:855-871),
 rejection of truncated frames (tcp.rs partial-frame tests).
