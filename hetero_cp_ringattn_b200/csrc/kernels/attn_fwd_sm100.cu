@@ -455,7 +455,7 @@ static cudaError_t launch(const CUtensorMap& tq, const CUtensorMap& tk, const CU
   return cudaGetLastError();
 }
 
-// Polynomial share per head_dim (out of 8 exponential pairs); HCP_ATTN_POLY overrides it (0-3).
+// Polynomial share per head_dim (out of 8 exponential pairs); HCP_ATTN_POLY overrides it (0-4).
 // Softmax warpgroup turn-taking (HCP_ATTN_PINGPONG=0 lets both run freely).
 static int pingpong_enabled() {
   static int env = -2;
@@ -472,7 +472,7 @@ static int poly_share(int D) {
     const char* s = getenv("HCP_ATTN_POLY");
     env = (s && *s) ? atoi(s) : -1;
   }
-  if (env >= 0 && env <= 3) return env;
+  if (env >= 0 && env <= 4) return env;
   // measured on B200 (32k causal, 32/8 heads): 2 of 8 pairs is the best split for D=64 and 128
   return 2;
 }
@@ -484,6 +484,7 @@ static cudaError_t launch_d(const CUtensorMap& tq, const CUtensorMap& tk, const 
     case 1: return launch<D, 1>(tq, tk, tv, p, stream);
     case 2: return launch<D, 2>(tq, tk, tv, p, stream);
     case 3: return launch<D, 3>(tq, tk, tv, p, stream);
+    case 4: return launch<D, 4>(tq, tk, tv, p, stream);
     default: return launch<D, 0>(tq, tk, tv, p, stream);
   }
 }
