@@ -180,14 +180,14 @@ def bench_norm(args, dev, pk):
 
 
 def bench_decode(args, dev, pk):
-    """Decode step of the Llama-3.2-1B shape over a prefilled context (``--layers`` layers).
+    """Decode step of a model preset (``--model``) over a prefilled ``--seq`` context.
 
     The step is the captured CUDA graph the engine replays per token; ``--small`` uses 2 layers."""
     from hetero_cp_ringattn_b200.config import preset
     from hetero_cp_ringattn_b200.models.llama import LlamaCPEngine
     from hetero_cp_ringattn_b200.models.weights import PreparedWeights
-    cfg = preset("llama-3.2-1b")
-    cfg.num_layers = 2 if args.small else args.layers
+    cfg = preset(args.model)
+    cfg.num_layers = 2 if args.small else (args.layers or cfg.num_layers)
     ctx = args.seq
     w = PreparedWeights.random(cfg, seed=0, device=dev)
     eng = LlamaCPEngine(cfg, w, device=dev, max_context=ctx, max_batch=1, decode_reserve=args.iters + 16)
@@ -210,7 +210,7 @@ def bench_decode(args, dev, pk):
                    + cfg.num_heads * cfg.head_dim * cfg.hidden_size + 3 * cfg.hidden_size * cfg.intermediate_size) * 2
     kv = ctx * 2 * cfg.kv_heads * cfg.head_dim * 2
     byts = cfg.num_layers * (per_layer_w + kv) + cfg.vocab_size * cfg.hidden_size * 2
-    emit(kernel="decode_step", layers=cfg.num_layers, context=ctx, ms_per_token=round(ms, 4),
+    emit(kernel="decode_step", model=args.model, layers=cfg.num_layers, context=ctx, ms_per_token=round(ms, 4),
          tok_s=round(1e3 / ms, 1), gbs=round(byts / ms / 1e6, 1),
          frac_of_measured_hbm=round(byts / ms / 1e6 / pk["hbm_gbs"], 3), peaks=pk["source"])
     eng.release(1)
@@ -345,7 +345,8 @@ def main(argv=None):
     ap.add_argument("--tokens", type=int, default=32768)
     ap.add_argument("--seqs", type=lambda s: [int(x) for x in s.split(",")], default=[8192, 32768])
     ap.add_argument("--seq", type=int, default=32768)
-    ap.add_argument("--layers", type=int, default=16)
+    ap.add_argument("--layers", type=int, default=0, help="decode: layers (0 = the model's)")
+    ap.add_argument("--model", default="llama-3.2-1b", help="decode: model preset")
     ap.add_argument("--ratio", default="1:1")
     ap.add_argument("--strategy", default="zigzag")
     ap.add_argument("--heads", type=int, default=32)

@@ -194,6 +194,10 @@ void add_u64(torch::Tensor t, int64_t v) {
 
 int64_t num_sms(int64_t dev) { return sm_count(int(dev)); }
 
+int64_t decode_attn_ctas_per_sm(int64_t D, int64_t G) {
+  return hcp::dec::decode_attn_ctas_per_sm(int(D), int(G));
+}
+
 // ----------------------------------------------------------------------------- runtime
 class PyRuntime {
  public:
@@ -469,6 +473,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("tok64") = py::none());
   m.def("add_u64", &add_u64);
   m.def("num_sms", &num_sms);
+  m.def("decode_attn_ctas_per_sm", &decode_attn_ctas_per_sm);
   m.attr("EPI_STORE") = int(hcp::gemm::kEpiStore);
   m.attr("EPI_BIAS") = int(hcp::gemm::kEpiBias);
   m.attr("EPI_RESIDUAL") = int(hcp::gemm::kEpiResidual);

@@ -24,7 +24,9 @@
 // while the other tile's warpgroup runs its softmax. TMEM: S_i at column 128 i (P_i, packed
 // bf16, overwrites the first 64 columns of S_i in place), O_i at column 256 + D i.
 // Softmax: two passes over S (row max, then exponentials), tree reductions, lazy O rescale
-// (only when the running max grows by more than 2^8), half of the exponentials on the FMA pipe.
+// (only when the running max grows by more than 2^8), a share of the exponentials (POLY of every
+// 8 pairs) on the FMA pipe, a mask-free variant for tiles below every row's causal bound.
+// Registers: warpgroup 0 drops to 88 per thread so the softmax warpgroups can hold 208.
 #include <cstdlib>
 
 #include "attn_fwd_sm100.h"
@@ -378,9 +380,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     bool ok = true;
     for (int j = 0; j < n_tiles; ++j) {
       const int t = kv_tile_at(j, n_tiles, start);
-      // ping-pong: tile 1 runs its softmax for step j after tile 0 finished step j, tile 0 runs
-      // step j after tile 1 finished step j - 1, so one warpgroup's exponentials overlap the
-      // tensor core's work on the other tile
+      // optional turn-taking: tile 1 runs its softmax for step j after tile 0 finished step j,
+      // tile 0 runs step j after tile 1 finished step j - 1
       if (p.pingpong) {
         if (tile == 1) ok = mbar_wait(&turn[1], j & 1, p.status, 211);
         else if (j > 0) ok = mbar_wait(&turn[0], (j - 1) & 1, p.status, 212);
@@ -455,13 +456,15 @@ static cudaError_t launch(const CUtensorMap& tq, const CUtensorMap& tk, const CU
   return cudaGetLastError();
 }
 
-// Polynomial share per head_dim (out of 8 exponential pairs); HCP_ATTN_POLY overrides it (0-4).
-// Softmax warpgroup turn-taking (HCP_ATTN_PINGPONG=0 lets both run freely).
+// Polynomial share per head_dim (out of 8 exponential pairs); HCP_ATTN_POLY overrides it (0-6).
+// Softmax warpgroup turn-taking (HCP_ATTN_PINGPONG=1). Off by default: measured on B200 the two
+// warpgroups running freely is 10-25% faster (the softmax is issue-bound, so a second warp per
+// scheduler hides more latency than the turn-taking saves).
 static int pingpong_enabled() {
   static int env = -2;
   if (env == -2) {
     const char* s = getenv("HCP_ATTN_PINGPONG");
-    env = (s && *s) ? atoi(s) : 1;
+    env = (s && *s) ? atoi(s) : 0;
   }
   return env != 0;
 }
@@ -472,9 +475,10 @@ static int poly_share(int D) {
     const char* s = getenv("HCP_ATTN_POLY");
     env = (s && *s) ? atoi(s) : -1;
   }
-  if (env >= 0 && env <= 4) return env;
-  // measured on B200 (32k causal, 32/8 heads): 2 of 8 pairs is the best split for D=64 and 128
-  return 2;
+  if (env >= 0 && env <= 6) return env;
+  // measured on B200 (32k causal, 32/8 heads, no turn-taking): 4 of 8 pairs is the best split
+  // for D=64 and 128 (D=64: 702 / 707 / 728 TFLOP/s at 2 / 3 / 4)
+  return 4;
 }
 
 template <int D>
@@ -485,6 +489,8 @@ static cudaError_t launch_d(const CUtensorMap& tq, const CUtensorMap& tk, const 
     case 2: return launch<D, 2>(tq, tk, tv, p, stream);
     case 3: return launch<D, 3>(tq, tk, tv, p, stream);
     case 4: return launch<D, 4>(tq, tk, tv, p, stream);
+    case 5: return launch<D, 5>(tq, tk, tv, p, stream);
+    case 6: return launch<D, 6>(tq, tk, tv, p, stream);
     default: return launch<D, 0>(tq, tk, tv, p, stream);
   }
 }

@@ -52,25 +52,48 @@ __device__ __forceinline__ unsigned long long pack_argmax(float v, int idx) {
   return (static_cast<unsigned long long>(u) << 32) | (0xFFFFFFFFu - uint32_t(idx));
 }
 
-// One CTA (8 warps) computes R output rows (R gate/up pairs for SwiGLU) for all B inputs. The
-// whole CTA splits K: thread t reads uint4 columns t, t + 256, ... of each row, so every thread
-// issues its R row loads for several k steps back to back (no dependent-load chains), and the
-// partial dot products are reduced across the 8 warps through shared memory.
-// NORM: the input rows are RMS-normalised on the fly (statistics recomputed per CTA from the
-// 2-8 input rows, which is cheaper than a separate normalisation launch for decode).
+// Persistent decode GEMV, y[b, o] = epi(sum_k W[o, k] x[b, k]). The grid is one wave of CTAs
+// (8 warps each); every warp owns whole output rows (a gate/up row pair for SwiGLU) and walks
+// its (row, K-chunk) items with two register buffers: the loads of item i + 1 are issued before
+// item i is consumed, so each warp always has KC 16-byte streaming loads per lane in flight, and
+// the first item's loads are issued before the x prologue, hiding its latency. Lane l reads the
+// 16-byte columns l, l + 32, ... of a chunk; a row ends with one 5-step shuffle reduction and no
+// block barrier. x is staged once per CTA in shared memory; with NORM it is RMS-normalised
+// there first (the statistics of the 1-8 input rows cost far less than a separate launch).
 constexpr int GEMV_THREADS = 256;
 
-template <int EPI, int B, int R, bool NORM>
+template <int EPI, int B, bool NORM>
 __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(GemvArgs a) {
-  extern __shared__ uint4 xs[];                     // NORM: normalised x, [B][K/8]
-  __shared__ float red[GEMV_THREADS / 32][2 * R * B];
+  extern __shared__ uint4 xs[];                     // [B][K/8] (normalised when NORM)
+  __shared__ float red[GEMV_THREADS / 32][B];
   __shared__ float rstd[B];
+  constexpr int NWR = (EPI == kGemvSwiGLU) ? 2 : 1;  // weight rows per output row
+  constexpr int KC = 8 / NWR;                        // 16-byte columns per lane per chunk and row
   const int tid = threadIdx.x, lane = tid % 32, warp = tid / 32;
   const int kvec = a.K / 8;
   const int out_rows = (EPI == kGemvSwiGLU) ? a.N / 2 : a.N;
-  const int base = blockIdx.x * R;
+  const int nchunk = (kvec + 32 * KC - 1) / (32 * KC);
+  const int gw = blockIdx.x * (GEMV_THREADS / 32) + warp;
+  const int nwarps = gridDim.x * (GEMV_THREADS / 32);
+  const int my_rows = gw < out_rows ? (out_rows - 1 - gw) / nwarps + 1 : 0;
+  const int items = my_rows * nchunk;
+  auto load = [&](int item, uint4 (&buf)[NWR][KC]) {
+    const int o = gw + (item / nchunk) * nwarps;
+    const int c = item % nchunk;
+    const int w0 = (EPI == kGemvSwiGLU) ? (o / 128) * 256 + (o % 128) : o;
+#pragma unroll
+    for (int q = 0; q < NWR; ++q) {
+      const uint4* wp = reinterpret_cast<const uint4*>(a.W + (long)(w0 + q * 128) * a.K);
+#pragma unroll
+      for (int j = 0; j < KC; ++j) {
+        const int k = c * 32 * KC + j * 32 + lane;
+        buf[q][j] = k < kvec ? ld_stream(wp + k) : make_uint4(0u, 0u, 0u, 0u);
+      }
+    }
+  };
+  uint4 bufA[NWR][KC], bufB[NWR][KC];
+  if (items > 0) load(0, bufA);
   if (NORM) {
-    // sum of squares per input row, then the normalised bf16 row into shared memory
     float ss[B];
 #pragma unroll
     for (int b = 0; b < B; ++b) ss[b] = 0.f;
@@ -112,120 +135,104 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(GemvArgs a) {
         xs[b * kvec + k] = make_uint4(o[0], o[1], o[2], o[3]);
       }
     }
-    __syncthreads();
+  } else {
+    for (int k = tid; k < kvec; k += GEMV_THREADS)
+#pragma unroll
+      for (int b = 0; b < B; ++b) xs[b * kvec + k] = __ldg(reinterpret_cast<const uint4*>(a.x + (long)b * a.ldx) + k);
   }
-  int wrow[R], urow[R];
-#pragma unroll
-  for (int r = 0; r < R; ++r) {
-    int o = base + r;
-    if (o >= out_rows) o = out_rows - 1;
-    if (EPI == kGemvSwiGLU) {
-      wrow[r] = (o / 128) * 256 + (o % 128);
-      urow[r] = wrow[r] + 128;
-    } else {
-      wrow[r] = o;
-      urow[r] = o;
-    }
-  }
-  float acc[R][B], accu[R][B];
-#pragma unroll
-  for (int r = 0; r < R; ++r)
-#pragma unroll
-    for (int b = 0; b < B; ++b) acc[r][b] = accu[r][b] = 0.f;
-#pragma unroll 4
-  for (int k = tid; k < kvec; k += GEMV_THREADS) {
-    uint4 w[R], u[R];
-#pragma unroll
-    for (int r = 0; r < R; ++r) {
-      w[r] = ld_stream(reinterpret_cast<const uint4*>(a.W + (long)wrow[r] * a.K) + k);
-      if (EPI == kGemvSwiGLU) u[r] = ld_stream(reinterpret_cast<const uint4*>(a.W + (long)urow[r] * a.K) + k);
-    }
-#pragma unroll
-    for (int b = 0; b < B; ++b) {
-      const uint4 xv = NORM ? xs[b * kvec + k] : __ldg(reinterpret_cast<const uint4*>(a.x + (long)b * a.ldx) + k);
-#pragma unroll
-      for (int r = 0; r < R; ++r) {
-        dot8_acc(w[r], xv, acc[r][b]);
-        if (EPI == kGemvSwiGLU) dot8_acc(u[r], xv, accu[r][b]);
-      }
-    }
-  }
-  if (NORM) __syncthreads();  // `red` is reused below
-#pragma unroll
-  for (int r = 0; r < R; ++r)
-#pragma unroll
-    for (int b = 0; b < B; ++b) {
-      const float v = warp_sum(acc[r][b]);
-      if (lane == 0) red[warp][r * B + b] = v;
-      if (EPI == kGemvSwiGLU) {
-        const float vu = warp_sum(accu[r][b]);
-        if (lane == 0) red[warp][R * B + r * B + b] = vu;
-      }
-    }
   __syncthreads();
-  if (tid < R * B) {
-    const int r = tid / B, b = tid % B;
-    const int o = base + r;
-    float v = 0.f, vu = 0.f;
+
+  float acc[NWR][B];
+  unsigned long long best[B];
 #pragma unroll
-    for (int w = 0; w < GEMV_THREADS / 32; ++w) {
-      v += red[w][r * B + b];
-      if (EPI == kGemvSwiGLU) vu += red[w][R * B + r * B + b];
+  for (int b = 0; b < B; ++b) best[b] = 0ull;
+  auto consume = [&](int item, const uint4 (&buf)[NWR][KC]) {
+    const int o = gw + (item / nchunk) * nwarps;
+    const int c = item % nchunk;
+    if (c == 0) {
+#pragma unroll
+      for (int q = 0; q < NWR; ++q)
+#pragma unroll
+        for (int b = 0; b < B; ++b) acc[q][b] = 0.f;
     }
-    if (o < out_rows) {
+#pragma unroll
+    for (int j = 0; j < KC; ++j) {
+      const int k = c * 32 * KC + j * 32 + lane;
+      if (k < kvec) {
+#pragma unroll
+        for (int b = 0; b < B; ++b) {
+          const uint4 xv = xs[b * kvec + k];
+#pragma unroll
+          for (int q = 0; q < NWR; ++q) dot8_acc(buf[q][j], xv, acc[q][b]);
+        }
+      }
+    }
+    if (c != nchunk - 1) return;
+    // row complete: every lane gets every sum; lane b finishes input row b
+#pragma unroll
+    for (int q = 0; q < NWR; ++q)
+#pragma unroll
+      for (int b = 0; b < B; ++b) acc[q][b] = warp_sum(acc[q][b]);
+#pragma unroll
+    for (int b = 0; b < B; ++b) {
+      const float v = acc[0][b];
+      if (EPI == kGemvArgmax) {
+        const unsigned long long cnd = pack_argmax(v, o);
+        best[b] = cnd > best[b] ? cnd : best[b];
+      }
+      if (lane != b) continue;
       if (EPI == kGemvF32) {
-        if (a.bias) v += __bfloat162float(a.bias[o]);
-        a.y_f32[(long)b * a.ldy + o] = v;
+        a.y_f32[(long)b * a.ldy + o] = a.bias ? v + __bfloat162float(a.bias[o]) : v;
       } else if (EPI == kGemvResidual) {
         __nv_bfloat16* y = a.y_bf16 + (long)b * a.ldy + o;
         *y = __float2bfloat16(__bfloat162float(__float2bfloat16(v)) + __bfloat162float(*y));
       } else if (EPI == kGemvSwiGLU) {
         const float g = __bfloat162float(__float2bfloat16(v));
-        const float uu = __bfloat162float(__float2bfloat16(vu));
+        const float uu = __bfloat162float(__float2bfloat16(acc[NWR - 1][b]));
         const float sg = g / (1.f + fast_exp2(-g * kLog2e));
         a.y_bf16[(long)b * a.ldy + o] = __float2bfloat16(sg * uu);
       } else if (EPI == kGemvArgmax) {
         if (a.y_f32) a.y_f32[(long)b * a.ldy + o] = v;
-        red[0][2 * R * B - 1 - tid] = v;  // keep for the per-CTA argmax below (disjoint slots)
       }
+    }
+  };
+  for (int i = 0; i < items; i += 2) {
+    if (i + 1 < items) load(i + 1, bufB);
+    consume(i, bufA);
+    if (i + 1 < items) {
+      if (i + 2 < items) load(i + 2, bufA);
+      consume(i + 1, bufB);
     }
   }
-  if (EPI == kGemvArgmax) {
-    __syncthreads();
-    if (tid < B) {
-      unsigned long long best = 0;
+  if (EPI == kGemvArgmax && lane == 0) {
 #pragma unroll
-      for (int r = 0; r < R; ++r) {
-        const int o = base + r;
-        if (o < out_rows) {
-          const unsigned long long c = pack_argmax(red[0][2 * R * B - 1 - (r * B + tid)], o);
-          best = c > best ? c : best;
-        }
-      }
-      atomicMax(a.argmax + tid, best);
-    }
+    for (int b = 0; b < B; ++b)
+      if (best[b]) atomicMax(a.argmax + b, best[b]);
   }
 }
 
 template <int EPI, bool NORM>
 static cudaError_t gemv_launch(const GemvArgs& a, cudaStream_t s) {
-  constexpr int R = 4;  // output rows (gate/up pairs for SwiGLU) per CTA
-  const int out_rows = (EPI == kGemvSwiGLU) ? a.N / 2 : a.N;
-  const int grid = (out_rows + R - 1) / R;
-  const size_t smem = NORM ? size_t(a.B) * a.K * 2 : 0;
+  const size_t smem = size_t(a.B) * a.K * 2;
   auto go = [&](auto kernel) -> cudaError_t {
     if (smem > 48 * 1024) {
       cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
       if (e != cudaSuccess) return e;
     }
+    int occ = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kernel, GEMV_THREADS, smem) != cudaSuccess || occ < 1)
+      occ = 1;
+    const int out_rows = (EPI == kGemvSwiGLU) ? a.N / 2 : a.N;
+    const int need = (out_rows + GEMV_THREADS / 32 - 1) / (GEMV_THREADS / 32);
+    const int grid = need < occ * a.num_sms ? need : occ * a.num_sms;
     kernel<<<grid, GEMV_THREADS, smem, s>>>(a);
     return cudaGetLastError();
   };
   switch (a.B) {
-    case 1: return go(gemv_kernel<EPI, 1, R, NORM>);
-    case 2: return go(gemv_kernel<EPI, 2, R, NORM>);
-    case 4: return go(gemv_kernel<EPI, 4, R, NORM>);
-    case 8: return go(gemv_kernel<EPI, 8, R, NORM>);
+    case 1: return go(gemv_kernel<EPI, 1, NORM>);
+    case 2: return go(gemv_kernel<EPI, 2, NORM>);
+    case 4: return go(gemv_kernel<EPI, 4, NORM>);
+    case 8: return go(gemv_kernel<EPI, 8, NORM>);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -241,7 +248,7 @@ const char* gemv(const GemvArgs& a, cudaStream_t s) {
   if (a.epi == kGemvSwiGLU && a.N % 256) return "gemv: SwiGLU needs N % 256 == 0";
   if ((reinterpret_cast<uintptr_t>(a.W) | reinterpret_cast<uintptr_t>(a.x)) & 15)
     return "gemv: W/x must be 16-byte aligned";
-  if (a.norm_w && (size_t(a.B) * a.K * 2 > 200 * 1024)) return "gemv: fused norm needs B*K*2 <= 200 KB";
+  if (size_t(a.B) * a.K * 2 > 200 * 1024) return "gemv: needs B*K*2 <= 200 KB (x is staged in shared memory)";
   cudaError_t e;
   switch (a.epi) {
     case kGemvF32: e = gemv_dispatch<kGemvF32>(a, s); break;
@@ -254,111 +261,215 @@ const char* gemv(const GemvArgs& a, cudaStream_t s) {
 }
 
 // ----------------------------------------------------------------------------- K2 decode attention
-// grid (splits, Hkv, B), 128 threads. Each group of D/8 lanes handles one token at a time.
+// grid (splits, Hkv, B), 128 threads (4 warps). Each warp owns a contiguous, chunk-aligned token
+// range of its split and streams it through a private STAGES-deep shared-memory ring: lane 0
+// issues one bulk copy for the K rows and one for the V rows of a chunk (CT tokens, 2 KB each;
+// chunks never straddle a 256-row page) and the warp waits on the chunk's mbarrier (bounded).
+// A token's rows are spread over LPT lanes that each own DPL consecutive head dims (16, or 8
+// for 8-head GQA groups so q and the accumulators of all G heads fit in registers). Per chunk:
+// scores with packed f32x2 FMAs and an LPT-lane shuffle reduction, one warp-wide running-max
+// update per head (the accumulator rescale happens once per chunk, not per token), then
+// p = 2^(s - m) and O += p V with packed FMAs. The warp's token groups and the 4 warps are
+// merged at the end and the split's (O, LSE) partial is written.
+constexpr int kDecStages = 4;
+
+template <int D>
+struct DecChunk {
+  static constexpr int CT = 1024 / D;                  // tokens per chunk (2 KB of K rows)
+  static constexpr int BYTES = CT * D * 2;             // K (or V) bytes per chunk
+  static constexpr int WARP_SMEM = kDecStages * 2 * BYTES;
+  static constexpr int SMEM = 4 * WARP_SMEM;           // dynamic shared memory per CTA
+};
+
 template <int D, int G>
 __global__ void __launch_bounds__(128) decode_attn_kernel(DecodeAttnArgs a) {
-  constexpr int LPG = D / 8;        // lanes per token
-  constexpr int TPW = 32 / LPG;     // tokens per warp step
-  constexpr int GROUPS = 4 * TPW;   // token groups per CTA
+  constexpr int DPL = (G >= 8) ? 8 : 16;   // head dims per lane
+  constexpr int NV = DPL / 8;              // 16-byte vectors per lane per K (or V) row
+  constexpr int LPT = D / DPL;             // lanes per token
+  constexpr int TPW = 32 / LPT;            // tokens per warp step
+  constexpr int NW = 4;                    // warps per CTA
+  constexpr int CT = DecChunk<D>::CT;
+  constexpr int STEPS = CT / TPW;          // warp steps per chunk
+  constexpr int BYTES = DecChunk<D>::BYTES;
+  static_assert(LPT >= 1 && LPT <= 32 && 32 % LPT == 0 && CT % TPW == 0 && 256 % CT == 0, "tiling");
+  extern __shared__ __align__(128) uint8_t dsm[];
+  __shared__ __align__(8) uint64_t bars[NW][kDecStages];
   const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int lane = threadIdx.x % 32, warp = threadIdx.x / 32;
-  const int gl = lane % LPG;                  // lane within group
-  const int grp = warp * TPW + lane / LPG;    // group id within CTA
+  const int gl = lane % LPT;               // lane within the token group
   const int n = a.n_tokens[b];
-  const int per = (n + a.splits - 1) / a.splits;
+  // chunk-aligned ranges: split -> 4 warp ranges -> CT-token chunks
+  int per = (n + a.splits - 1) / a.splits;
+  per = (per + NW * CT - 1) / (NW * CT) * (NW * CT);
   const int s0 = split * per;
   const int s1 = min(n, s0 + per);
+  const int w0 = min(s1, s0 + warp * (per / NW));
+  const int w1 = min(s1, w0 + per / NW);
+  const int nc = (w1 - w0 + CT - 1) / CT;
   const int H = a.Hkv * G;
+  uint8_t* wsm = dsm + warp * DecChunk<D>::WARP_SMEM;  // [stage][K | V][CT][D] bf16
 
-  // q slice (pre-scaled into the log2 domain)
-  float q[G][8];
+  // zero the ring once (rows past the end of a range are then finite and get p = 0), init the
+  // barriers, make both visible to the async proxy
+  for (int i = threadIdx.x; i < DecChunk<D>::SMEM / 16; i += blockDim.x)
+    reinterpret_cast<uint4*>(dsm)[i] = make_uint4(0u, 0u, 0u, 0u);
+  if (lane == 0)
+    for (int st = 0; st < kDecStages; ++st) mbar_init(&bars[warp][st], 1);
+  fence_barrier_init();
+  fence_proxy_async_smem();
+  __syncthreads();
+
+  const int* pt = a.page_tables + (long)b * a.pt_stride;
+  auto issue = [&](int c) {
+    const int t0 = w0 + c * CT;
+    const int rows = min(CT, w1 - t0);
+    const int page = pt[t0 / a.geom.page];
+    const __nv_bfloat16* src = a.arena + a.geom.offset(a.layer, page, 0, h, t0 % a.geom.page);
+    uint8_t* dst = wsm + (c % kDecStages) * 2 * BYTES;
+    uint64_t* bar = &bars[warp][c % kDecStages];
+    const uint32_t bytes = uint32_t(rows) * D * 2;
+    mbar_arrive_expect_tx(bar, 2 * bytes);
+    bulk_load(dst, src, bytes, bar);
+    bulk_load(dst + BYTES, src + a.geom.kv_stride(), bytes, bar);
+  };
+  if (lane == 0)
+    for (int c = 0; c < kDecStages - 1 && c < nc; ++c) issue(c);
+
+  // q slice of every head of the group, pre-scaled into the log2 domain
+  float2 q[G][DPL / 2];
+  const float qs = a.scale * kLog2e;
 #pragma unroll
-  for (int g = 0; g < G; ++g) {
-    const uint4 v = *reinterpret_cast<const uint4*>(a.q + ((long)b * H + h * G + g) * D + gl * 8);
-    const uint32_t vv[4] = {v.x, v.y, v.z, v.w};
+  for (int g = 0; g < G; ++g)
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      q[g][2 * j] = bf16_lo(vv[j]) * a.scale * kLog2e;
-      q[g][2 * j + 1] = bf16_hi(vv[j]) * a.scale * kLog2e;
+    for (int v = 0; v < NV; ++v) {
+      const uint4 w = *reinterpret_cast<const uint4*>(a.q + ((long)b * H + h * G + g) * D + gl * DPL + v * 8);
+      const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) q[g][v * 4 + j] = make_float2(bf16_lo(ww[j]) * qs, bf16_hi(ww[j]) * qs);
     }
-  }
-  float m[G], l[G], acc[G][8];
+  float2 acc[G][DPL / 2];
+  float m[G], l[G];
 #pragma unroll
   for (int g = 0; g < G; ++g) {
     m[g] = -INFINITY;
     l[g] = 0.f;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) acc[g][j] = 0.f;
+    for (int i = 0; i < DPL / 2; ++i) acc[g][i] = make_float2(0.f, 0.f);
   }
-  const int* pt = a.page_tables + (long)b * a.pt_stride;
-  // The loop bound is warp-uniform (it depends on the warp, not the lane group) because the
-  // body reduces scores with full-warp shuffles; a lane group past the end of the split runs
-  // the step with `valid == false` and leaves its state untouched. UNR token steps are loaded
-  // before any is consumed, so each lane keeps 2 * UNR 16-byte loads in flight.
-  constexpr int UNR = 4;
-  for (int base = s0 + warp * TPW; base < s1; base += GROUPS * UNR) {
-    uint4 kvs[UNR], vvs[UNR];
-    bool valid[UNR];
-#pragma unroll
-    for (int u = 0; u < UNR; ++u) {
-      const int t = base + u * GROUPS + lane / LPG;
-      valid[u] = t < s1;
-      kvs[u] = make_uint4(0u, 0u, 0u, 0u);
-      vvs[u] = make_uint4(0u, 0u, 0u, 0u);
-      if (valid[u]) {
-        const int page = pt[t / a.geom.page];
-        const int row = t % a.geom.page;
-        const __nv_bfloat16* kp = a.arena + a.geom.offset(a.layer, page, 0, h, row) + gl * 8;
-        kvs[u] = *reinterpret_cast<const uint4*>(kp);
-        vvs[u] = *reinterpret_cast<const uint4*>(kp + a.geom.kv_stride());
-      }
+  int consumed = 0;
+  bool ok = true;
+  for (int c = 0; c < nc; ++c) {
+    if (lane == 0 && c + kDecStages - 1 < nc) {
+      fence_proxy_async_smem();  // the warp's reads of that stage (chunk c - 1) come first
+      issue(c + kDecStages - 1);
     }
+    ok = __all_sync(0xffffffffu, mbar_wait(&bars[warp][c % kDecStages], (c / kDecStages) & 1, a.status, 301));
+    if (!ok) break;
+    consumed = c + 1;
+    const __nv_bfloat16* sk = reinterpret_cast<const __nv_bfloat16*>(wsm + (c % kDecStages) * 2 * BYTES);
+    const __nv_bfloat16* sv = sk + CT * D;
+    const int t0 = w0 + c * CT;
+    float sc[STEPS][G];
 #pragma unroll
-    for (int u = 0; u < UNR; ++u) {
-      const uint32_t kw[4] = {kvs[u].x, kvs[u].y, kvs[u].z, kvs[u].w};
-      const uint32_t vw[4] = {vvs[u].x, vvs[u].y, vvs[u].z, vvs[u].w};
-      float vf[8];
+    for (int u = 0; u < STEPS; ++u) {
+      const int tt = u * TPW + lane / LPT;
+      const bool valid = t0 + tt < w1;
+      float2 kf[DPL / 2];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        vf[2 * j] = bf16_lo(vw[j]);
-        vf[2 * j + 1] = bf16_hi(vw[j]);
+      for (int v = 0; v < NV; ++v) {
+        const uint4 kw = *reinterpret_cast<const uint4*>(sk + tt * D + gl * DPL + v * 8);
+        const uint32_t ww[4] = {kw.x, kw.y, kw.z, kw.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) kf[v * 4 + j] = make_float2(bf16_lo(ww[j]), bf16_hi(ww[j]));
       }
 #pragma unroll
       for (int g = 0; g < G; ++g) {
-        float sc = 0.f;
+        float2 d2 = make_float2(0.f, 0.f);
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          sc = fmaf(q[g][2 * j], bf16_lo(kw[j]), sc);
-          sc = fmaf(q[g][2 * j + 1], bf16_hi(kw[j]), sc);
-        }
+        for (int i = 0; i < DPL / 2; ++i) d2 = __ffma2_rn(q[g][i], kf[i], d2);
+        float x = d2.x + d2.y;
 #pragma unroll
-        for (int o = LPG / 2; o > 0; o >>= 1) sc += __shfl_xor_sync(0xffffffffu, sc, o);
-        if (!valid[u]) continue;
-        const float mn = fmaxf(m[g], sc);
-        const float al = fast_exp2(m[g] - mn);
-        const float pp = fast_exp2(sc - mn);
-        l[g] = l[g] * al + pp;
+        for (int o = LPT / 2; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+        sc[u][g] = valid ? x : -INFINITY;
+      }
+    }
+    // one running-max update per head and chunk (warp-uniform)
 #pragma unroll
-        for (int j = 0; j < 8; ++j) acc[g][j] = fmaf(acc[g][j], al, pp * vf[j]);
-        m[g] = mn;
+    for (int g = 0; g < G; ++g) {
+      float cm = sc[0][g];
+#pragma unroll
+      for (int u = 1; u < STEPS; ++u) cm = fmaxf(cm, sc[u][g]);
+#pragma unroll
+      for (int o = LPT; o < 32; o <<= 1) cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, o));
+      if (cm > m[g]) {
+        const float al = fast_exp2(m[g] - cm);  // 0 while nothing has been accumulated
+        m[g] = cm;
+        l[g] *= al;
+        const float2 al2 = make_float2(al, al);
+#pragma unroll
+        for (int i = 0; i < DPL / 2; ++i) acc[g][i] = __fmul2_rn(acc[g][i], al2);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < STEPS; ++u) {
+      const int tt = u * TPW + lane / LPT;
+      float2 vf[DPL / 2];
+#pragma unroll
+      for (int v = 0; v < NV; ++v) {
+        const uint4 vw = *reinterpret_cast<const uint4*>(sv + tt * D + gl * DPL + v * 8);
+        const uint32_t ww[4] = {vw.x, vw.y, vw.z, vw.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) vf[v * 4 + j] = make_float2(bf16_lo(ww[j]), bf16_hi(ww[j]));
+      }
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        // m[g] is -inf only while every score so far was -inf; p is 0 then
+        const float pp = m[g] == -INFINITY ? 0.f : fast_exp2(sc[u][g] - m[g]);
+        l[g] += pp;
+        const float2 p2 = make_float2(pp, pp);
+#pragma unroll
+        for (int i = 0; i < DPL / 2; ++i) acc[g][i] = __ffma2_rn(p2, vf[i], acc[g][i]);
+      }
+    }
+    __syncwarp();
+  }
+  if (!ok && lane == 0) {
+    // a wait gave up: let the copies still in flight land (bounded) before the CTA exits
+    for (int c = consumed; c < nc && c < consumed + kDecStages; ++c)
+      mbar_wait(&bars[warp][c % kDecStages], (c / kDecStages) & 1, a.status, 302);
+  }
+  // merge the warp's token groups (same m in every lane of the warp): sum l and O over the lanes
+  // that own the same head dims
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+#pragma unroll
+    for (int o = LPT; o < 32; o <<= 1) {
+      l[g] += __shfl_xor_sync(0xffffffffu, l[g], o);
+#pragma unroll
+      for (int i = 0; i < DPL / 2; ++i) {
+        acc[g][i].x += __shfl_xor_sync(0xffffffffu, acc[g][i].x, o);
+        acc[g][i].y += __shfl_xor_sync(0xffffffffu, acc[g][i].y, o);
       }
     }
   }
-  // CTA reduction over the GROUPS token groups through shared memory
-  __shared__ float sm_m[GROUPS][G];
-  __shared__ float sm_l[GROUPS][G];
-  __shared__ float sm_acc[GROUPS][G][D];
-  if (gl == 0) {
+  // then the 4 warps through shared memory
+  __shared__ float sm_m[NW][G];
+  __shared__ float sm_l[NW][G];
+  __shared__ float sm_acc[NW][G][D];
+  if (lane < LPT) {
 #pragma unroll
     for (int g = 0; g < G; ++g) {
-      sm_m[grp][g] = m[g];
-      sm_l[grp][g] = l[g];
+      if (lane == 0) {
+        sm_m[warp][g] = m[g];
+        sm_l[warp][g] = l[g];
+      }
+#pragma unroll
+      for (int i = 0; i < DPL / 2; ++i) {
+        sm_acc[warp][g][gl * DPL + 2 * i] = acc[g][i].x;
+        sm_acc[warp][g][gl * DPL + 2 * i + 1] = acc[g][i].y;
+      }
     }
   }
-#pragma unroll
-  for (int g = 0; g < G; ++g)
-#pragma unroll
-    for (int j = 0; j < 8; ++j) sm_acc[grp][g][gl * 8 + j] = acc[g][j];
   __syncthreads();
   // each thread finalises (g, d) entries: G * D outputs over 128 threads
   float* po = a.part_o + ((long)(b * H + h * G) * a.splits + split) * D;   // [B,H,splits,D]
@@ -366,10 +477,12 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(DecodeAttnArgs a) {
   for (int i = threadIdx.x; i < G * D; i += blockDim.x) {
     const int g = i / D, d = i % D;
     float mx = -INFINITY;
-    for (int r = 0; r < GROUPS; ++r) mx = fmaxf(mx, sm_m[r][g]);
+#pragma unroll
+    for (int r = 0; r < NW; ++r) mx = fmaxf(mx, sm_m[r][g]);
     float ls = 0.f, o = 0.f;
     if (mx > -INFINITY) {
-      for (int r = 0; r < GROUPS; ++r) {
+#pragma unroll
+      for (int r = 0; r < NW; ++r) {
         const float w = fast_exp2(sm_m[r][g] - mx);
         ls += sm_l[r][g] * w;
         o += sm_acc[r][g][d] * w;
@@ -491,9 +604,21 @@ __global__ void decode_combine_kernel(DecodeCombineArgs a) {
 }
 
 template <int D, int G>
+static cudaError_t prepare_attn() {
+  static bool done = false;
+  if (done) return cudaSuccess;
+  cudaError_t e = cudaFuncSetAttribute(decode_attn_kernel<D, G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       DecChunk<D>::SMEM);
+  done = (e == cudaSuccess);
+  return e;
+}
+
+template <int D, int G>
 static cudaError_t launch_attn(const DecodeAttnArgs& a, cudaStream_t s) {
+  cudaError_t e = prepare_attn<D, G>();
+  if (e != cudaSuccess) return e;
   dim3 grid(a.splits, a.Hkv, a.B);
-  decode_attn_kernel<D, G><<<grid, 128, 0, s>>>(a);
+  decode_attn_kernel<D, G><<<grid, 128, DecChunk<D>::SMEM, s>>>(a);
   return cudaGetLastError();
 }
 
@@ -502,6 +627,9 @@ const char* decode_attn(const DecodeAttnArgs& a, cudaStream_t s) {
   if (a.H % a.Hkv) return "decode_attn: H % Hkv";
   if (a.n_ranks < 1 || a.n_ranks > kMaxRanks) return "decode_attn: bad n_ranks";
   if (a.splits < 1 || a.splits > kMaxDecodeSplits) return "decode_attn: splits must be in [1, 128]";
+  if ((a.D != 64 && a.D != 128) || a.geom.page % (1024 / a.D))
+    return "decode_attn: head_dim must be 64 or 128 and the page a multiple of 1024 / head_dim rows";
+  if (reinterpret_cast<uintptr_t>(a.arena) & 15) return "decode_attn: arena must be 16-byte aligned";
   cudaError_t e = cudaErrorInvalidValue;
 #define HCP_DEC_CASE(DD, GG) \
   if (a.D == DD && G == GG) e = launch_attn<DD, GG>(a, s);
@@ -510,6 +638,17 @@ const char* decode_attn(const DecodeAttnArgs& a, cudaStream_t s) {
 #undef HCP_DEC_CASE
   if (e == cudaErrorInvalidValue) return "decode_attn: unsupported (D, H/Hkv)";
   return e == cudaSuccess ? nullptr : cudaGetErrorString(e);
+}
+
+int decode_attn_ctas_per_sm(int D, int G) {
+  int n = 0;
+#define HCP_DEC_OCC(DD, GG)                                                                      \
+  if (D == DD && G == GG && prepare_attn<DD, GG>() == cudaSuccess)                                 \
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, decode_attn_kernel<DD, GG>, 128, DecChunk<DD>::SMEM);
+  HCP_DEC_OCC(64, 1) HCP_DEC_OCC(64, 2) HCP_DEC_OCC(64, 4) HCP_DEC_OCC(64, 8)
+  HCP_DEC_OCC(128, 1) HCP_DEC_OCC(128, 2) HCP_DEC_OCC(128, 4) HCP_DEC_OCC(128, 8)
+#undef HCP_DEC_OCC
+  return n;
 }
 
 const char* decode_combine(const DecodeCombineArgs& a, cudaStream_t s) {

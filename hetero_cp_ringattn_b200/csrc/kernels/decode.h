@@ -72,6 +72,9 @@ struct DecodeCombineArgs {
 
 const char* gemv(const GemvArgs& a, cudaStream_t s);
 const char* decode_attn(const DecodeAttnArgs& a, cudaStream_t s);
+// Resident decode_attn CTAs per SM for (head_dim, GQA group size); 0 when unsupported. Callers
+// size the split count so the grid fills the GPU in one wave.
+int decode_attn_ctas_per_sm(int D, int G);
 const char* decode_combine(const DecodeCombineArgs& a, cudaStream_t s);
 const char* fill_u64(unsigned long long* p, int n, unsigned long long v, cudaStream_t s);
 const char* argmax_finalize(const unsigned long long* packed, int B, int* tok, long long* tok64,

@@ -195,3 +195,22 @@ def test_gemv_fused_rmsnorm(dev, b):
     gg = (xn.float() @ g.float().t()).bfloat16().float()
     uu = (xn.float() @ u.float().t()).bfloat16().float()
     assert rel_err(out, torch.nn.functional.silu(gg) * uu) < 2e-2
+
+
+@pytest.mark.parametrize("kdim,n", [(8192, 2048), (11008, 1001), (1000, 37)])
+def test_gemv_k_chunks_and_row_tails(dev, kdim, n):
+    """K that spans several per-lane chunks or ends mid-chunk, and row counts that leave a
+    partial row group, against an fp32 reference."""
+    torch.manual_seed(8)
+    for b in (1, 4):
+        x = torch.randn(b, kdim, device=dev, dtype=torch.bfloat16)
+        w = torch.randn(n, kdim, device=dev, dtype=torch.bfloat16) / math.sqrt(kdim)
+        y = torch.empty(b, n, device=dev, dtype=torch.float32)
+        K.gemv(x, w, "f32", y_f32=y)
+        assert rel_err(y, x.float() @ w.float().t()) < 1e-3
+        am = torch.zeros(b, dtype=torch.int64, device=dev)
+        logits = torch.empty(b, n, device=dev, dtype=torch.float32)
+        K.gemv(x, w, "argmax", y_f32=logits, argmax=am)
+        tok = torch.empty(b, dtype=torch.int64, device=dev)
+        native().argmax_finalize(am, None, tok)
+        assert torch.equal(tok, logits.argmax(-1))
