@@ -189,7 +189,8 @@ PRESETS = {
     "llama-3-8b": dict(name="llama-3-8b", hidden_size=4096, num_layers=32, num_heads=32,
                        num_kv_heads=8, intermediate_size=14336, vocab_size=128256,
                        rope_theta=500000.0, rms_norm_eps=1e-5, tie_word_embeddings=False,
-                       max_position_embeddings=131072, torch_dtype="bfloat16",
+                       # the 128k-prompt benchmark decodes 256 tokens past position 131072
+                       max_position_embeddings=262144, torch_dtype="bfloat16",
                        architectures=["LlamaForCausalLM"], eos_token_id=[128001]),
     # Tiny shapes used by tests (the reference's synthetic model is hidden 32, 2 layers, GQA 4/1,
     # vocab 100: rust/src/model/model.rs:676-740).

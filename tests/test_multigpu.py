@@ -81,16 +81,18 @@ def _worker(rank, world, port, chunks, strategy, out):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("chunks,strategy", [([1536, 1536], "vanilla"), ([2048, 1024], "zigzag"),
-                                             ([1000, 1100], "striped")])
-def test_two_gpu_cp_matches_single_gpu(chunks, strategy):
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs two GPUs")
+def _launch(chunks, strategy):
+    world = len(chunks)
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     with tempfile.TemporaryDirectory() as d:
         out = os.path.join(d, "r.pt")
-        mp.start_processes(_worker, args=(2, free_port(), chunks, strategy, out), nprocs=2,
+        mp.start_processes(_worker, args=(world, free_port(), chunks, strategy, out), nprocs=world,
                            join=True, start_method="spawn")
-        r = torch.load(out)
+        return torch.load(out)
+
+
+def _check(r):
     cp_toks, cp_logits = r["cp"]
     one_toks, one_logits = r["single"]
     oracle = r["oracle"]
@@ -102,3 +104,20 @@ def test_two_gpu_cp_matches_single_gpu(chunks, strategy):
     assert (cp_logits - one_logits).abs().mean() < 1e-2
     assert int(torch.argmax(cp_logits)) == int(torch.argmax(oracle))
     assert cp_toks == one_toks
+
+
+@pytest.mark.parametrize("chunks,strategy", [([1536, 1536], "vanilla"), ([2048, 1024], "zigzag"),
+                                             ([1000, 1100], "striped")])
+def test_two_gpu_cp_matches_single_gpu(chunks, strategy):
+    _check(_launch(chunks, strategy))
+
+
+@pytest.mark.parametrize("chunks,strategy", [
+    ([1280, 1280, 256], "zigzag"),                                   # capacity ratio 5:5:1
+    ([768, 768, 768, 768], "striped"),
+    ([640, 640, 640, 640, 256, 256, 128, 128], "zigzag"),            # 5:5:5:5:2:2:1:1
+    ([500, 400, 300, 200, 600, 700, 100, 300], "vanilla"),
+])
+def test_many_gpu_uneven_cp_matches_single_gpu(chunks, strategy):
+    """3, 4 and 8 ranks with the capacity-weighted uneven splits (skipped below that many GPUs)."""
+    _check(_launch(chunks, strategy))
