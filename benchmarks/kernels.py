@@ -113,7 +113,7 @@ def causal_flops(Lq: int, Lk: int, H: int, D: int) -> float:
 def bench_attn(args, dev, pk):
     from hetero_cp_ringattn_b200.ops import kernels as K
     import torch.nn.functional as F
-    cases = [(8192, 128)] if args.small else [(s, d) for d in (64, 128) for s in args.seqs]
+    cases = [(8192, args.head_dim)] if args.small else [(s, d) for d in (64, 128) for s in args.seqs]
     H, Hkv = 32, 8
     for L, D in cases:
         q = torch.randn(L, H, D, device=dev, dtype=torch.bfloat16)

@@ -23,7 +23,7 @@
 // The MMA warp ping-pongs between the tiles, so the tensor core works on one tile's products
 // while the other tile's warpgroup runs its softmax. TMEM: S_i at column 128 i (P_i, packed
 // bf16, overwrites the first 64 columns of S_i in place), O_i at column 256 + D i.
-// Softmax: two passes over S (row max, then exponentials), tree reductions, lazy O rescale
+// Softmax: one TMEM read of S per row (row max, then exponentials from registers), lazy O rescale
 // (only when the running max grows by more than 2^8), a share of the exponentials (POLY of every
 // 8 pairs) on the FMA pipe, a mask-free variant for tiles below every row's causal bound.
 // Registers: warpgroup 0 drops to 88 per thread so the softmax warpgroups can hold 208.
@@ -79,28 +79,29 @@ __device__ __forceinline__ int kv_tile_at(int j, int n, int start) {
   return j < up ? start + j : start - 1 - (j - up);
 }
 
-// One softmax step of a q-tile row over a 128-column score tile held in TMEM: row max (one batch
-// of TMEM loads, 3-input maxima), lazy rescale of the running max and of O (only when the max
-// grows by more than 2^8), then P = 2^(s * scale - m) packed to bf16 into the first 64 columns
-// of S and the row sum. MASK = true applies the causal / length bound (kv position > lim gives
+// One softmax step of a q-tile row over a 128-column score tile held in TMEM: one batch of TMEM
+// loads brings the whole row into registers, row max with 3-input maxima, lazy rescale of the
+// running max and of O (only when the max grows by more than 2^8), then P = 2^(s * scale - m)
+// packed to bf16 into the first 64 columns of S and the row sum. MASK = true applies the causal / length bound (kv position > lim gives
 // -inf); tiles below every row's bound use MASK = false and carry no per-element compare.
 template <int D, int POLY, bool MASK>
 __device__ __forceinline__ void softmax_step(uint32_t s_addr, uint32_t o_addr, int kv0, int lim,
                                              float scale_log2, bool o_live, float& m_ref,
                                              float& l_sum) {
+  // the whole score row in one batch of TMEM loads; it stays in registers for both passes
+  uint32_t r[128];
+  tmem_ld32(s_addr, r);
+  tmem_ld32(s_addr + 32, r + 32);
+  tmem_ld32(s_addr + 64, r + 64);
+  tmem_ld32(s_addr + 96, r + 96);
+  tmem_wait_ld();
+  if (MASK) {
+#pragma unroll
+    for (int e = 0; e < 128; ++e)
+      if (kv0 + e > lim) r[e] = __float_as_uint(-INFINITY);
+  }
   float tmax;
   {
-    uint32_t r[128];
-    tmem_ld32(s_addr, r);
-    tmem_ld32(s_addr + 32, r + 32);
-    tmem_ld32(s_addr + 64, r + 64);
-    tmem_ld32(s_addr + 96, r + 96);
-    tmem_wait_ld();
-    if (MASK) {
-#pragma unroll
-      for (int e = 0; e < 128; ++e)
-        if (kv0 + e > lim) r[e] = __float_as_uint(-INFINITY);
-    }
     float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
     for (int e = 0; e < 128; e += 8)
@@ -117,39 +118,19 @@ __device__ __forceinline__ void softmax_step(uint32_t s_addr, uint32_t o_addr, i
     resc = true;
   }
   const float m_use = (m_ref == -INFINITY) ? 0.f : m_ref;
-  // PV_i(j-1) completed before S_i(j) did (same issuing thread, in-order commits): O_i is
-  // stable here and can be rescaled in place
-  if (o_live && __any_sync(0xffffffffu, resc)) {
-#pragma unroll 1
-    for (int c = 0; c < D / 32; ++c) {
-      uint32_t o[32];
-      tmem_ld32(o_addr + c * 32, o);
-      tmem_wait_ld();
-#pragma unroll
-      for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
-      tmem_st32(o_addr + c * 32, o);
-    }
-  }
-  // P in two halves of 64 columns, packed to bf16 into the first 64 columns of S (half h lands
-  // on columns already consumed); packed f32x2 arithmetic; POLY of every 8 pairs take the
-  // FMA-pipe polynomial, the rest the MUFU
+  // P in two halves of 64 columns, packed to bf16 into the first 64 columns of S (every score
+  // is already in registers); packed f32x2 arithmetic (masked entries are -inf already); POLY
+  // of every 8 pairs take the FMA-pipe polynomial, the rest the MUFU
   float2 rs0 = make_float2(0.f, 0.f), rs1 = make_float2(0.f, 0.f);
   const float2 negm = make_float2(-m_use, -m_use);
   const float2 sc2 = make_float2(scale_log2, scale_log2);
 #pragma unroll
   for (int hh = 0; hh < 2; ++hh) {
-    uint32_t r[64];
-    tmem_ld32(s_addr + hh * 64, r);
-    tmem_ld32(s_addr + hh * 64 + 32, r + 32);
-    tmem_wait_ld();
     uint32_t pk[32];
 #pragma unroll
     for (int e = 0; e < 64; e += 2) {
-      float2 x = __ffma2_rn(make_float2(__uint_as_float(r[e]), __uint_as_float(r[e + 1])), sc2, negm);
-      if (MASK) {
-        if (kv0 + hh * 64 + e > lim) x.x = -INFINITY;
-        if (kv0 + hh * 64 + e + 1 > lim) x.y = -INFINITY;
-      }
+      const float2 x = __ffma2_rn(make_float2(__uint_as_float(r[hh * 64 + e]), __uint_as_float(r[hh * 64 + e + 1])),
+                                  sc2, negm);
       float2 pp;
       if (POLY > 0 && ((e >> 1) & 7) >= 8 - POLY) {
         pp = poly_exp2_x2(x);
@@ -162,6 +143,20 @@ __device__ __forceinline__ void softmax_step(uint32_t s_addr, uint32_t o_addr, i
       pk[e >> 1] = pack_bf16x2(pp.x, pp.y);
     }
     tmem_st32(s_addr + hh * 32, pk);
+  }
+  // O rescale after the scores are dead (lower register peak). PV_i(j-1) completed before
+  // S_i(j) did (same issuing thread, in-order commits), so O_i is stable and PV_i(j) is only
+  // issued after this step arrives on p_full.
+  if (o_live && __any_sync(0xffffffffu, resc)) {
+#pragma unroll 1
+    for (int c = 0; c < D / 32; ++c) {
+      uint32_t o[32];
+      tmem_ld32(o_addr + c * 32, o);
+      tmem_wait_ld();
+#pragma unroll
+      for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+      tmem_st32(o_addr + c * 32, o);
+    }
   }
   tmem_wait_st();
   l_sum = l_sum * alpha + ((rs0.x + rs0.y) + (rs1.x + rs1.y));
@@ -197,10 +192,16 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
 
-  // heaviest tile pairs first (largest positions are last in local order): LPT-like balance
-  const int pair = p.num_pairs - 1 - int(blockIdx.x) / p.H;
-  const int head = int(blockIdx.x) % p.H;
-  const int kv_head = head / (p.H / p.Hkv);
+  // CTA order: KV-head major, so the CTAs resident at any time (one per SM) are the q heads of
+  // one GQA group over a run of q-tile pairs and stream the same K/V tiles in the same order
+  // (one KV head's K and V stay in L2 instead of every group's); within a group, heaviest tile
+  // pairs first (largest positions are last in local order), an LPT-like balance.
+  const int group = p.H / p.Hkv;
+  const int per_kv = p.num_pairs * group;
+  const int kv_head = int(blockIdx.x) / per_kv;
+  const int rem = int(blockIdx.x) % per_kv;
+  const int pair = p.num_pairs - 1 - rem / group;
+  const int head = kv_head * group + rem % group;
   const int row0 = pair * QT * BQ;
 
   if (threadIdx.x == 0) {
@@ -476,9 +477,9 @@ static int poly_share(int D) {
     env = (s && *s) ? atoi(s) : -1;
   }
   if (env >= 0 && env <= 6) return env;
-  // measured on B200 (32k causal, 32/8 heads, no turn-taking): 4 of 8 pairs is the best split
-  // for D=64 and 128 (D=64: 702 / 707 / 728 TFLOP/s at 2 / 3 / 4)
-  return 4;
+  // measured on B200 (32k causal, 32/8 heads, one TMEM read of S per step): 3 of 8 pairs is the
+  // best split for D=64 and 128 (748 / 1263 TFLOP/s; 4 of 8 gives 703 / 1152)
+  return 3;
 }
 
 template <int D>
