@@ -13,20 +13,21 @@
 // buffer over NVLink; the kernel's kv-tile order starts at `kv_start_tile` (this rank's own
 // chunk) and an optional per-tile ready-flag array lets the producer wait (bounded) for a tile.
 //
-// CTA layout (384 threads, one CTA per SM): two q tiles of 128 rows of one head share every K/V
-// tile.
+// CTA layout (one CTA per SM): two q tiles of 128 rows of one head share every K/V tile.
 //   warp 0      TMA producer (Q0, Q1 once; K/V tiles through a STAGES-deep ring)
-//   warp 1      MMA issuer: S_i = Q_i K^T (SS) and O_i += P_i V (TS: P read from TMEM)
+//   warp 1      MMA issuer: S_i = Q_i K^T (SS) and O += P V (TS: P read from TMEM)
 //   warp 2      TMEM allocator
-//   warps 4-7   softmax / correction / epilogue of q tile 0 (thread <-> row <-> TMEM lane)
-//   warps 8-11  the same for q tile 1
-// The MMA warp ping-pongs between the tiles, so the tensor core works on one tile's products
-// while the other tile's warpgroup runs its softmax. TMEM: S_i at column 128 i (P_i, packed
-// bf16, overwrites the first 64 columns of S_i in place), O_i at column 256 + D i.
+//   warpgroups 1..  softmax streams (thread <-> row <-> TMEM lane): head_dim 128 has one stream
+//               per q tile (384 threads); head_dim 64 splits each tile's 128 keys into two
+//               64-column streams with their own running max, row sum and O (640 threads), so
+//               four warpgroups share the exponentials, merged per row in the epilogue.
+// The MMA warp alternates between the tiles, so the tensor core works on one tile's products
+// while the other tile's streams run their softmax. TMEM: S_i at column 128 i (each stream's P,
+// packed bf16, overwrites the first half of its own S columns), O of stream st at 256 + D st.
 // Softmax: one TMEM read of S per row (row max, then exponentials from registers), lazy O rescale
 // (only when the running max grows by more than 2^8), a share of the exponentials (POLY of every
 // 8 pairs) on the FMA pipe, a mask-free variant for tiles below every row's causal bound.
-// Registers: warpgroup 0 drops to 88 per thread so the softmax warpgroups can hold 208.
+// Registers: warpgroup 0 hands registers to the softmax warpgroups with setmaxnreg.
 #include <cstdlib>
 
 #include "attn_fwd_sm100.h"
@@ -41,7 +42,6 @@ using namespace hcp::dev;
 constexpr int BQ = 128;      // q rows per tile
 constexpr int BKV = 128;     // kv rows per tile
 constexpr int QT = 2;        // q tiles per CTA
-constexpr int THREADS = 384;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 
 template <int D>
@@ -50,9 +50,15 @@ struct Cfg {
   static constexpr int Q_BYTES = BQ * D * 2;     // one q tile
   static constexpr int KV_BYTES = BKV * D * 2;
   static constexpr int STAGES = (D == 64) ? 3 : 2;
-  static constexpr int SMEM = 1024 + QT * Q_BYTES + 2 * STAGES * KV_BYTES + 1024;
+  static constexpr int SMEM = 1024 + QT * Q_BYTES + 2 * STAGES * KV_BYTES + 4096;
   static constexpr int TMEM_COLS = 512;
   static constexpr int O_COL = 256;
+  // threads: warpgroup 0 (TMA, MMA, TMEM allocator, idle) + one warpgroup per softmax stream
+  __host__ __device__ static constexpr int threads(int hv) { return 128 + QT * hv * 128; }
+  // register split (setmaxnreg): 128 x wg0 + (threads - 128) x sm must not exceed the launch's
+  // threads x registers (168 at 384 threads, 96 at 640)
+  __host__ __device__ static constexpr int wg0_regs(int hv) { return hv == 1 ? 88 : 80; }
+  __host__ __device__ static constexpr int sm_regs(int hv) { return hv == 1 ? 208 : 96; }
 };
 
 struct KParams {
@@ -69,7 +75,6 @@ struct KParams {
   int num_kv_tiles_total;
   unsigned long long wait_budget_ns;
   int* status;
-  int pingpong;         // 1: the two softmax warpgroups take turns (see the softmax loop)
 };
 
 // processing order: kv_start_tile .. n-1 ascending, then kv_start_tile-1 .. 0 descending
@@ -79,32 +84,30 @@ __device__ __forceinline__ int kv_tile_at(int j, int n, int start) {
   return j < up ? start + j : start - 1 - (j - up);
 }
 
-// One softmax step of a q-tile row over a 128-column score tile held in TMEM: one batch of TMEM
-// loads brings the whole row into registers, row max with 3-input maxima, lazy rescale of the
-// running max and of O (only when the max grows by more than 2^8), then P = 2^(s * scale - m)
-// packed to bf16 into the first 64 columns of S and the row sum. MASK = true applies the causal / length bound (kv position > lim gives
+// One softmax step of one stream (a q-tile row over CW key columns) held in TMEM: one batch of
+// TMEM loads brings the stream's scores into registers, row max with 3-input maxima, lazy
+// rescale of the running max and of the stream's O (only when the max grows by more than 2^8),
+// then P = 2^(s * scale - m) packed to bf16 into the first CW/2 columns of the stream's S range
+// and the row sum. MASK = true applies the causal / length bound (kv position > lim gives
 // -inf); tiles below every row's bound use MASK = false and carry no per-element compare.
-template <int D, int POLY, bool MASK>
+template <int D, int POLY, int CW, bool MASK>
 __device__ __forceinline__ void softmax_step(uint32_t s_addr, uint32_t o_addr, int kv0, int lim,
                                              float scale_log2, bool o_live, float& m_ref,
                                              float& l_sum) {
-  // the whole score row in one batch of TMEM loads; it stays in registers for both passes
-  uint32_t r[128];
-  tmem_ld32(s_addr, r);
-  tmem_ld32(s_addr + 32, r + 32);
-  tmem_ld32(s_addr + 64, r + 64);
-  tmem_ld32(s_addr + 96, r + 96);
+  uint32_t r[CW];
+#pragma unroll
+  for (int c = 0; c < CW / 32; ++c) tmem_ld32(s_addr + c * 32, r + c * 32);
   tmem_wait_ld();
   if (MASK) {
 #pragma unroll
-    for (int e = 0; e < 128; ++e)
+    for (int e = 0; e < CW; ++e)
       if (kv0 + e > lim) r[e] = __float_as_uint(-INFINITY);
   }
   float tmax;
   {
     float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-    for (int e = 0; e < 128; e += 8)
+    for (int e = 0; e < CW; e += 8)
 #pragma unroll
       for (int k = 0; k < 4; ++k)
         m4[k] = max3f(m4[k], __uint_as_float(r[e + 2 * k]), __uint_as_float(r[e + 2 * k + 1]));
@@ -118,18 +121,17 @@ __device__ __forceinline__ void softmax_step(uint32_t s_addr, uint32_t o_addr, i
     resc = true;
   }
   const float m_use = (m_ref == -INFINITY) ? 0.f : m_ref;
-  // P in two halves of 64 columns, packed to bf16 into the first 64 columns of S (every score
-  // is already in registers); packed f32x2 arithmetic (masked entries are -inf already); POLY
-  // of every 8 pairs take the FMA-pipe polynomial, the rest the MUFU
+  // P in chunks of 32 columns (16 packed TMEM columns each), written over scores already in
+  // registers; packed f32x2 arithmetic; POLY of every 8 pairs take the FMA-pipe polynomial
   float2 rs0 = make_float2(0.f, 0.f), rs1 = make_float2(0.f, 0.f);
   const float2 negm = make_float2(-m_use, -m_use);
   const float2 sc2 = make_float2(scale_log2, scale_log2);
 #pragma unroll
-  for (int hh = 0; hh < 2; ++hh) {
-    uint32_t pk[32];
+  for (int hh = 0; hh < CW / 32; ++hh) {
+    uint32_t pk[16];
 #pragma unroll
-    for (int e = 0; e < 64; e += 2) {
-      const float2 x = __ffma2_rn(make_float2(__uint_as_float(r[hh * 64 + e]), __uint_as_float(r[hh * 64 + e + 1])),
+    for (int e = 0; e < 32; e += 2) {
+      const float2 x = __ffma2_rn(make_float2(__uint_as_float(r[hh * 32 + e]), __uint_as_float(r[hh * 32 + e + 1])),
                                   sc2, negm);
       float2 pp;
       if (POLY > 0 && ((e >> 1) & 7) >= 8 - POLY) {
@@ -142,10 +144,10 @@ __device__ __forceinline__ void softmax_step(uint32_t s_addr, uint32_t o_addr, i
       else rs0 = __fadd2_rn(rs0, pp);
       pk[e >> 1] = pack_bf16x2(pp.x, pp.y);
     }
-    tmem_st32(s_addr + hh * 32, pk);
+    tmem_st16(s_addr + hh * 16, pk);
   }
-  // O rescale after the scores are dead (lower register peak). PV_i(j-1) completed before
-  // S_i(j) did (same issuing thread, in-order commits), so O_i is stable and PV_i(j) is only
+  // O rescale after the scores are dead (lower register peak). PV(j-1) of this stream completed
+  // before S(j) did (same issuing thread, in-order commits), so O is stable, and PV(j) is only
   // issued after this step arrives on p_full.
   if (o_live && __any_sync(0xffffffffu, resc)) {
 #pragma unroll 1
@@ -162,13 +164,19 @@ __device__ __forceinline__ void softmax_step(uint32_t s_addr, uint32_t o_addr, i
   l_sum = l_sum * alpha + ((rs0.x + rs0.y) + (rs1.x + rs1.y));
 }
 
-// POLY: how many of every 8 exponential pairs use the FMA-pipe polynomial instead of the MUFU
-// (trades MUFU throughput for issue slots; tuned per head_dim).
-template <int D, int POLY>
-__global__ void __launch_bounds__(THREADS, 1)
+// POLY: how many of every 8 exponential pairs use the FMA-pipe polynomial instead of the MUFU.
+// HV: softmax warpgroups per q tile. HV = 2 (head_dim 64) splits each 128-key tile into two
+// 64-column streams with their own running max, row sum and O accumulator (TMEM: S 2 x 128
+// columns, O 4 x 64), so four warpgroups share the softmax work, and merges the two streams of a
+// row in the epilogue. HV = 1 (head_dim 128) keeps one stream per q tile.
+template <int D, int POLY, int HV>
+__global__ void __launch_bounds__(Cfg<D>::threads(HV), 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, KParams p) {
   using C = Cfg<D>;
+  constexpr int CW = BKV / HV;               // key columns per stream
+  constexpr int NS = QT * HV;                // softmax streams per CTA
+  static_assert(C::O_COL + NS * D <= C::TMEM_COLS, "TMEM columns");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -182,15 +190,15 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint64_t* v_full = k_empty + C::STAGES;
   uint64_t* v_empty = v_full + C::STAGES;
   uint64_t* s_full = v_empty + C::STAGES;  // [QT]
-  uint64_t* p_full = s_full + QT;          // [QT]
-  uint64_t* o_done = p_full + QT;          // [QT]
-  uint64_t* turn = o_done + QT;            // [QT] softmax ping-pong between the two warpgroups
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(turn + QT);
+  uint64_t* p_full = s_full + QT;          // [NS]
+  uint64_t* o_done = p_full + NS;          // [QT]
+  uint64_t* merged = o_done + QT;          // [QT] HV = 2: both streams posted (m, l)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(merged + QT);
   int* s_qmin = reinterpret_cast<int*>(tmem_slot + 1);  // [QT]
   int* s_qmax = s_qmin + QT;                            // [QT]
+  float* s_ml = reinterpret_cast<float*>(s_qmax + QT);  // [QT][2][BQ] m, l of stream h = 1
 
   const int warp = threadIdx.x / 32;
-  const int lane = threadIdx.x % 32;
 
   // CTA order: KV-head major, so the CTAs resident at any time (one per SM) are the q heads of
   // one GQA group over a run of q-tile pairs and stream the same K/V tiles in the same order
@@ -214,12 +222,12 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     for (int i = 0; i < QT; ++i) {
       mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], 128);
       mbar_init(&o_done[i], 1);
-      mbar_init(&turn[i], 128);
+      mbar_init(&merged[i], BQ);
       s_qmin[i] = 0x7fffffff;
       s_qmax[i] = -1;
     }
+    for (int i = 0; i < NS; ++i) mbar_init(&p_full[i], 128);
     fence_barrier_init();
   }
   if (warp == 2) {
@@ -229,13 +237,16 @@ __global__ void __launch_bounds__(THREADS, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  // softmax warps own the rows: thread 128 + 128 i + r <-> row r of q tile i
-  const int tile = (warp >= 4) ? (warp - 4) / 4 : 0;
+  // softmax warps: warpgroup 1 + st handles stream st = tile * HV + half; thread <-> row <-> lane
+  const int st = (warp >= 4) ? (warp - 4) / 4 : 0;
+  const int tile = st / HV;
+  const int half = st % HV;
+  const int row = (warp >= 4) ? (int(threadIdx.x) - 128 - st * 128) : 0;
   int my_pos = -1;
   if (warp >= 4) {
-    const int r = row0 + tile * BQ + (int(threadIdx.x) - 128 - tile * 128);
+    const int r = row0 + tile * BQ + row;
     if (r < p.T) my_pos = p.q_pos[r];
-    if (my_pos >= 0) {
+    if (my_pos >= 0 && half == 0) {
       atomicMin(&s_qmin[tile], my_pos);
       atomicMax(&s_qmax[tile], my_pos);
     }
@@ -249,11 +260,11 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int start = p.kv_start_tile < n_tiles ? p.kv_start_tile : 0;
   const bool tile1_live = (row0 + BQ) < p.T;
 
-  // register split: warpgroup 0 (TMA, MMA, TMEM allocator, idle warp) hands registers to the two
-  // softmax warpgroups: 128 x 88 + 256 x 208 = 384 x 168, the launch's total. Each warpgroup
-  // executes its setmaxnreg at one point, before its warps take their roles.
+  // register split: warpgroup 0 (TMA, MMA, TMEM allocator, idle warp) hands registers to the
+  // softmax warpgroups; each warpgroup executes its setmaxnreg at one point, before its warps
+  // take their roles
   if (warp < 4) {
-  reg_dealloc<88>();
+  reg_dealloc<C::wg0_regs(HV)>();
   if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer
     if (elect_one() && n_tiles > 0) {
@@ -306,12 +317,13 @@ __global__ void __launch_bounds__(THREADS, 1)
                        sdesc_sw128(sk + offk, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
         }
       };
-      auto issue_pv = [&](int i, int s, bool acc) {
-        const uint32_t sv = smem_u32(sV + s * C::KV_BYTES);
+      // stream (i, h): O_ih += P_ih V[h * CW, (h + 1) * CW) with P from TMEM (16 keys = 8
+      // columns per step) and V rows from the MN-major smem tile (16 rows = 2048 bytes)
+      auto issue_pv = [&](int i, int h, int s, bool acc) {
+        const uint32_t sv = smem_u32(sV + s * C::KV_BYTES) + h * CW * 128;
 #pragma unroll
-        for (int kk = 0; kk < BKV / 16; ++kk) {
-          // A = P_i in TMEM (K = kv, 16 bf16 per step = 8 columns), B = V tile (MN-major)
-          umma_bf16_ts(tmem_base + C::O_COL + i * D, tmem_base + i * BKV + kk * 8,
+        for (int kk = 0; kk < CW / 16; ++kk) {
+          umma_bf16_ts(tmem_base + C::O_COL + (i * HV + h) * D, tmem_base + i * BKV + h * CW + kk * 8,
                        sdesc_sw128(sv + kk * 2048, BKV * 128, 1024), idesc_o,
                        (acc || kk > 0) ? 1u : 0u);
         }
@@ -329,105 +341,125 @@ __global__ void __launch_bounds__(THREADS, 1)
         const int s = j % C::STAGES;
         const int s1 = (j + 1) % C::STAGES;
         const bool more = j + 1 < n_tiles;
-        // q tile 0: O0 += P0 V_j, then S0 = Q0 K_{j+1}^T
-        if (!mbar_wait(&p_full[0], j & 1, p.status, 204) ||
-            !mbar_wait(&v_full[s], (j / C::STAGES) & 1, p.status, 205)) {
+        if (!mbar_wait(&v_full[s], (j / C::STAGES) & 1, p.status, 205)) {
           ok = false;
           break;
         }
-        tc_fence_after();
-        issue_pv(0, s, j > 0);
-        if (more) {
-          if (!mbar_wait(&k_full[s1], ((j + 1) / C::STAGES) & 1, p.status, 206)) {
-            ok = false;
-            break;
+        if (more && !mbar_wait(&k_full[s1], ((j + 1) / C::STAGES) & 1, p.status, 206)) {
+          ok = false;
+          break;
+        }
+#pragma unroll
+        for (int i = 0; i < QT; ++i) {
+          // tile i: O_ih += P_ih V_j for every stream, then S_i = Q_i K_{j+1}^T over the same
+          // TMEM columns (in-order issue: the PV reads of P come first)
+#pragma unroll
+          for (int h = 0; h < HV; ++h) {
+            if (!mbar_wait(&p_full[i * HV + h], j & 1, p.status, 204 + 3 * i)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            issue_pv(i, h, s, j > 0);
           }
-          tc_fence_after();
-          issue_qk(0, s1);
-          umma_commit(&s_full[0]);
-        } else {
-          umma_commit(&o_done[0]);
-        }
-        // q tile 1: O1 += P1 V_j, then S1 = Q1 K_{j+1}^T
-        if (!mbar_wait(&p_full[1], j & 1, p.status, 207)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        issue_pv(1, s, j > 0);
-        umma_commit(&v_empty[s]);
-        if (more) {
-          issue_qk(1, s1);
-          umma_commit(&s_full[1]);
-          umma_commit(&k_empty[s1]);
-        } else {
-          umma_commit(&o_done[1]);
+          if (!ok) break;
+          if (i == QT - 1) umma_commit(&v_empty[s]);
+          if (more) {
+            issue_qk(i, s1);
+            umma_commit(&s_full[i]);
+            if (i == QT - 1) umma_commit(&k_empty[s1]);
+          } else {
+            umma_commit(&o_done[i]);
+          }
         }
       }
     }
   }
   } else {
-    reg_alloc<208>();
-    // ------------------------------------------------------------------ softmax warpgroups
-    const int q4 = warp % 4;
-    const int row = q4 * 32 + lane;
+    reg_alloc<C::sm_regs(HV)>();
+    // ------------------------------------------------------------------ softmax streams
+    const uint32_t lane_off = uint32_t((warp % 4) * 32) << 16;
+    const uint32_t s_addr = tmem_base + lane_off + uint32_t(tile * BKV + half * CW);
+    const uint32_t o_addr = tmem_base + lane_off + uint32_t(C::O_COL + st * D);
     const int grow = row0 + tile * BQ + row;
-    const uint32_t lane_off = uint32_t(q4 * 32) << 16;
-    const uint32_t s_addr = tmem_base + lane_off + uint32_t(tile * BKV);
-    const uint32_t o_addr = tmem_base + lane_off + uint32_t(C::O_COL + tile * D);
     const bool live = (tile == 0) || tile1_live;
     float m_ref = -INFINITY;  // max used for exponentiation (log2 domain)
     float l_sum = 0.f;
     bool ok = true;
     for (int j = 0; j < n_tiles; ++j) {
       const int t = kv_tile_at(j, n_tiles, start);
-      // optional turn-taking: tile 1 runs its softmax for step j after tile 0 finished step j,
-      // tile 0 runs step j after tile 1 finished step j - 1
-      if (p.pingpong) {
-        if (tile == 1) ok = mbar_wait(&turn[1], j & 1, p.status, 211);
-        else if (j > 0) ok = mbar_wait(&turn[0], (j - 1) & 1, p.status, 212);
-      }
-      if (!ok || !mbar_wait(&s_full[tile], j & 1, p.status, 208)) {
+      if (!mbar_wait(&s_full[tile], j & 1, p.status, 208)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      const int kv0 = t * BKV;
+      const int kv0 = t * BKV + half * CW;
       const int lim = p.causal ? min(my_pos, p.L - 1) : p.L - 1;  // last visible kv position
       // the masked variant only for tiles that cross some row's bound (diagonal / tail tiles)
-      if (__any_sync(0xffffffffu, kv0 + BKV - 1 > lim))
-        softmax_step<D, POLY, true>(s_addr, o_addr, kv0, lim, p.scale_log2, j > 0, m_ref, l_sum);
+      if (__any_sync(0xffffffffu, kv0 + CW - 1 > lim))
+        softmax_step<D, POLY, CW, true>(s_addr, o_addr, kv0, lim, p.scale_log2, j > 0, m_ref, l_sum);
       else
-        softmax_step<D, POLY, false>(s_addr, o_addr, kv0, lim, p.scale_log2, j > 0, m_ref, l_sum);
+        softmax_step<D, POLY, CW, false>(s_addr, o_addr, kv0, lim, p.scale_log2, j > 0, m_ref, l_sum);
       tc_fence_before();
-      mbar_arrive(&p_full[tile]);
-      mbar_arrive(&turn[tile ^ 1]);
+      mbar_arrive(&p_full[st]);
     }
-    // epilogue: O / l and LSE
-    if (ok && n_tiles > 0 && mbar_wait(&o_done[tile], 0, p.status, 209)) {
-      tc_fence_after();
-      const float inv = l_sum > 0.f ? 1.f / l_sum : 0.f;
-      __nv_bfloat16* dst = p.O + ((long)grow * p.H + head) * D;
-#pragma unroll 1
-      for (int c = 0; c < D / 32; ++c) {
-        uint32_t o[32];
-        tmem_ld32(o_addr + c * 32, o);
-        tmem_wait_ld();
-        if (live && grow < p.T) {
-          uint4* d4 = reinterpret_cast<uint4*>(dst + c * 32);
-#pragma unroll
-          for (int i = 0; i < 4; ++i)
-            d4[i] = make_uint4(pack_bf16x2(__uint_as_float(o[8 * i]) * inv, __uint_as_float(o[8 * i + 1]) * inv),
-                               pack_bf16x2(__uint_as_float(o[8 * i + 2]) * inv, __uint_as_float(o[8 * i + 3]) * inv),
-                               pack_bf16x2(__uint_as_float(o[8 * i + 4]) * inv, __uint_as_float(o[8 * i + 5]) * inv),
-                               pack_bf16x2(__uint_as_float(o[8 * i + 6]) * inv, __uint_as_float(o[8 * i + 7]) * inv));
+    // epilogue: merge the HV streams of each row (half 1 posts its (m, l), half 0 combines and
+    // writes the row: both O accumulators sit in the same TMEM lanes), O / l and LSE
+    float m_tot = m_ref, l_tot = l_sum, a_own = 1.f, a_oth = 0.f;
+    if (HV == 2) {
+      float* ml = s_ml + tile * 2 * BQ;
+      if (half == 1) {
+        ml[row] = m_ref;
+        ml[BQ + row] = l_sum;
+        mbar_arrive(&merged[tile]);
+      } else if (ok) {
+        ok = mbar_wait(&merged[tile], 0, p.status, 213);
+        if (ok) {
+          const float m1 = ml[row], l1 = ml[BQ + row];
+          m_tot = fmaxf(m_ref, m1);
+          a_own = m_tot == -INFINITY ? 0.f : fast_exp2(m_ref - m_tot);
+          a_oth = m_tot == -INFINITY ? 0.f : fast_exp2(m1 - m_tot);
+          l_tot = l_sum * a_own + l1 * a_oth;
         }
       }
-      if (live && grow < p.T && p.lse != nullptr) {
-        p.lse[(long)head * p.T + grow] =
-            l_sum > 0.f ? (m_ref + __log2f(l_sum)) * 0.6931471805599453f : -INFINITY;
+    }
+    // HV = 2: half 0 finishes the row (both O accumulators are in the same TMEM lanes)
+    const bool writer = (HV == 1) || (half == 0);
+    if (ok && n_tiles > 0 && mbar_wait(&o_done[tile], 0, p.status, 209)) {
+      tc_fence_after();
+      if (writer) {
+        const float inv = l_tot > 0.f ? 1.f / l_tot : 0.f;
+        __nv_bfloat16* dst = p.O + ((long)grow * p.H + head) * D;
+#pragma unroll 1
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t o[32];
+          tmem_ld32(o_addr + c * 32, o);
+          if (HV == 2) {
+            uint32_t o2[32];
+            tmem_ld32(o_addr + D + c * 32, o2);
+            tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 32; ++e)
+              o[e] = __float_as_uint(__uint_as_float(o[e]) * a_own + __uint_as_float(o2[e]) * a_oth);
+          } else {
+            tmem_wait_ld();
+          }
+          if (live && grow < p.T) {
+            uint4* d4 = reinterpret_cast<uint4*>(dst + c * 32);
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              d4[i] = make_uint4(pack_bf16x2(__uint_as_float(o[8 * i]) * inv, __uint_as_float(o[8 * i + 1]) * inv),
+                                 pack_bf16x2(__uint_as_float(o[8 * i + 2]) * inv, __uint_as_float(o[8 * i + 3]) * inv),
+                                 pack_bf16x2(__uint_as_float(o[8 * i + 4]) * inv, __uint_as_float(o[8 * i + 5]) * inv),
+                                 pack_bf16x2(__uint_as_float(o[8 * i + 6]) * inv, __uint_as_float(o[8 * i + 7]) * inv));
+          }
+        }
+        if (live && grow < p.T && p.lse != nullptr) {
+          p.lse[(long)head * p.T + grow] =
+              l_tot > 0.f ? (m_tot + __log2f(l_tot)) * 0.6931471805599453f : -INFINITY;
+        }
       }
-    } else if (n_tiles == 0 && live && grow < p.T) {
+    } else if (n_tiles == 0 && writer && live && grow < p.T) {
       // no visible key (padding rows / empty KV): O = 0, LSE = -inf
       __nv_bfloat16* dst = p.O + ((long)grow * p.H + head) * D;
       for (int i = 0; i < D; ++i) dst[i] = __float2bfloat16(0.f);
@@ -442,58 +474,65 @@ __global__ void __launch_bounds__(THREADS, 1)
   }
 }
 
-template <int D, int POLY>
+template <int D, int POLY, int HV>
 static cudaError_t launch(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                           const KParams& p, cudaStream_t stream) {
+  static_assert(Cfg<D>::threads(HV) <= 1024, "threads");
+  static_assert(128 * Cfg<D>::wg0_regs(HV) + (Cfg<D>::threads(HV) - 128) * Cfg<D>::sm_regs(HV) <=
+                    Cfg<D>::threads(HV) * ((65536 / Cfg<D>::threads(HV)) / 8 * 8),
+                "register split exceeds the launch's registers");
   static bool attr = false;
   if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(attn_fwd_kernel<D, POLY>,
+    cudaError_t e = cudaFuncSetAttribute(attn_fwd_kernel<D, POLY, HV>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<D>::SMEM);
     if (e != cudaSuccess) return e;
     attr = true;
   }
   const int grid = p.num_pairs * p.H;
-  attn_fwd_kernel<D, POLY><<<grid, THREADS, Cfg<D>::SMEM, stream>>>(tq, tk, tv, p);
+  attn_fwd_kernel<D, POLY, HV><<<grid, Cfg<D>::threads(HV), Cfg<D>::SMEM, stream>>>(tq, tk, tv, p);
   return cudaGetLastError();
 }
 
-// Polynomial share per head_dim (out of 8 exponential pairs); HCP_ATTN_POLY overrides it (0-6).
-// Softmax warpgroup turn-taking (HCP_ATTN_PINGPONG=1). Off by default: measured on B200 the two
-// warpgroups running freely is 10-25% faster (the softmax is issue-bound, so a second warp per
-// scheduler hides more latency than the turn-taking saves).
-static int pingpong_enabled() {
+// Softmax streams per q tile for head_dim 64 (HCP_ATTN_HV=1 keeps one stream per tile).
+static int hv64() {
   static int env = -2;
   if (env == -2) {
-    const char* s = getenv("HCP_ATTN_PINGPONG");
-    env = (s && *s) ? atoi(s) : 0;
+    const char* s = getenv("HCP_ATTN_HV");
+    env = (s && *s) ? atoi(s) : 2;
   }
-  return env != 0;
+  return env == 1 ? 1 : 2;
 }
 
+// Polynomial share per head_dim (out of 8 exponential pairs); HCP_ATTN_POLY overrides it (0, 2,
+// 3 or 4).
 static int poly_share(int D) {
   static int env = -2;
   if (env == -2) {
     const char* s = getenv("HCP_ATTN_POLY");
     env = (s && *s) ? atoi(s) : -1;
   }
-  if (env >= 0 && env <= 6) return env;
+  if (env == 0 || (env >= 2 && env <= 4)) return env;
   // measured on B200 (32k causal, 32/8 heads, one TMEM read of S per step): 3 of 8 pairs is the
   // best split for D=64 and 128 (748 / 1263 TFLOP/s; 4 of 8 gives 703 / 1152)
   return 3;
 }
 
+template <int D, int HV>
+static cudaError_t launch_hv(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
+                             const KParams& p, cudaStream_t stream) {
+  switch (poly_share(D)) {
+    case 2: return launch<D, 2, HV>(tq, tk, tv, p, stream);
+    case 3: return launch<D, 3, HV>(tq, tk, tv, p, stream);
+    case 4: return launch<D, 4, HV>(tq, tk, tv, p, stream);
+    default: return launch<D, 0, HV>(tq, tk, tv, p, stream);
+  }
+}
+
 template <int D>
 static cudaError_t launch_d(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                             const KParams& p, cudaStream_t stream) {
-  switch (poly_share(D)) {
-    case 1: return launch<D, 1>(tq, tk, tv, p, stream);
-    case 2: return launch<D, 2>(tq, tk, tv, p, stream);
-    case 3: return launch<D, 3>(tq, tk, tv, p, stream);
-    case 4: return launch<D, 4>(tq, tk, tv, p, stream);
-    case 5: return launch<D, 5>(tq, tk, tv, p, stream);
-    case 6: return launch<D, 6>(tq, tk, tv, p, stream);
-    default: return launch<D, 0>(tq, tk, tv, p, stream);
-  }
+  if (D == 64 && hv64() == 2) return launch_hv<64, 2>(tq, tk, tv, p, stream);
+  return launch_hv<D, 1>(tq, tk, tv, p, stream);
 }
 
 const char* attn_fwd(const AttnArgs& a, cudaStream_t stream) {
@@ -534,7 +573,6 @@ const char* attn_fwd(const AttnArgs& a, cudaStream_t stream) {
   p.num_kv_tiles_total = (a.L + BKV - 1) / BKV;
   p.wait_budget_ns = a.wait_budget_ns;
   p.status = a.status;
-  p.pingpong = pingpong_enabled();
   cudaError_t e = a.D == 64 ? launch_d<64>(tq, tk, tv, p, stream) : launch_d<128>(tq, tk, tv, p, stream);
   return e == cudaSuccess ? nullptr : cudaGetErrorString(e);
 }
