@@ -247,7 +247,7 @@ class PyRuntime {
                                 int64_t L, int64_t kv_start_tile, double scale, bool causal,
                                 torch::Tensor q_out, torch::Tensor o_out,
                                 c10::optional<torch::Tensor> lse_out, int64_t epoch,
-                                c10::optional<torch::Tensor> existing_slot_pos) {
+                                c10::optional<torch::Tensor> existing_slot_pos, bool has_qkv = true) {
     check_cuda_bf16(qkv, "qkv");
     check_cuda_bf16(q_out, "q_out");
     check_cuda_bf16(o_out, "o_out");
@@ -263,7 +263,11 @@ class PyRuntime {
     a.max_pos = int(cos_t.size(0));
     a.T = int(qkv.size(0));
     a.H = int(q_out.size(1));
-    TORCH_CHECK(qkv.size(1) >= (a.H + 2 * c.geom.hkv) * c.geom.d, "qkv too narrow");
+    if (has_qkv) {
+      TORCH_CHECK(qkv.size(1) >= (a.H + 2 * c.geom.hkv) * c.geom.d, "qkv too narrow");
+    } else {
+      a.qkv = nullptr;
+    }
     a.layer = int(layer);
     if (page_table.has_value() && page_table->defined()) {
       TORCH_CHECK(page_table->scalar_type() == torch::kInt32, "page table int32");
@@ -300,14 +304,44 @@ class PyRuntime {
     TORCH_CHECK(st.ok(), "push_layer: ", st.ToString());
   }
 
+  // Fused projection + push: x [T, hidden] (normalised layer input), w_qkv [(H + 2 Hkv) D, hidden]
+  // and optional bias; the projection output is never stored.
+  void push_layer_fused(torch::Tensor x, torch::Tensor w_qkv, c10::optional<torch::Tensor> b_qkv,
+                        torch::Tensor pos, torch::Tensor cos_t, torch::Tensor sin_t, int64_t layer,
+                        c10::optional<torch::Tensor> page_table, int64_t slot_base, int64_t L,
+                        int64_t kv_start_tile, double scale, bool causal, torch::Tensor q_out,
+                        torch::Tensor o_out, c10::optional<torch::Tensor> lse_out, int64_t epoch,
+                        c10::optional<torch::Tensor> existing_slot_pos) {
+    check_cuda_bf16(x, "x");
+    check_cuda_bf16(w_qkv, "w_qkv");
+    TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1 && w_qkv.is_contiguous() && x.size(1) == w_qkv.size(1),
+                "x [T, hidden] row-major and w_qkv [N, hidden] contiguous");
+    const c10::cuda::CUDAGuard g(x.device());
+    auto a = layer_args(x, pos, cos_t, sin_t, layer, page_table, slot_base, L, kv_start_tile, scale,
+                        causal, q_out, o_out, lse_out, epoch, existing_slot_pos, /*has_qkv=*/false);
+    a.x = x.data_ptr();
+    a.ldx = x.stride(0);
+    a.w_qkv = w_qkv.data_ptr();
+    a.hidden = int(x.size(1));
+    if (b_qkv.has_value() && b_qkv->defined()) {
+      check_cuda_bf16(*b_qkv, "b_qkv");
+      TORCH_CHECK(b_qkv->numel() == w_qkv.size(0), "b_qkv size");
+      a.b_qkv = b_qkv->data_ptr();
+    }
+    TORCH_CHECK(w_qkv.size(0) == (a.H + 2 * rt_.config().geom.hkv) * rt_.config().geom.d, "w_qkv rows");
+    auto st = rt_.PushLayer(a, cur_stream());
+    TORCH_CHECK(st.ok(), "push_layer_fused: ", st.ToString());
+  }
+
   void attend_layer(torch::Tensor qkv, torch::Tensor pos, torch::Tensor cos_t, torch::Tensor sin_t,
                     int64_t layer, c10::optional<torch::Tensor> page_table, int64_t slot_base,
                     int64_t L, int64_t kv_start_tile, double scale, bool causal,
                     torch::Tensor q_out, torch::Tensor o_out, c10::optional<torch::Tensor> lse_out,
                     int64_t epoch, c10::optional<torch::Tensor> existing_slot_pos) {
+    // `qkv` only gives the row count here (the projection output or the layer input)
     const c10::cuda::CUDAGuard g(qkv.device());
     auto a = layer_args(qkv, pos, cos_t, sin_t, layer, page_table, slot_base, L, kv_start_tile,
-                        scale, causal, q_out, o_out, lse_out, epoch, existing_slot_pos);
+                        scale, causal, q_out, o_out, lse_out, epoch, existing_slot_pos, false);
     auto st = rt_.AttendLayer(a, cur_stream());
     TORCH_CHECK(st.ok(), "attend_layer: ", st.ToString());
   }
@@ -496,6 +530,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
            py::arg("sin_t"), py::arg("layer"), py::arg("page_table"), py::arg("slot_base"), py::arg("L"),
            py::arg("kv_start_tile"), py::arg("scale"), py::arg("causal"), py::arg("q_out"),
            py::arg("o_out"), py::arg("lse_out"), py::arg("epoch"), py::arg("existing_slot_pos") = py::none())
+      .def("push_layer_fused", &PyRuntime::push_layer_fused, py::arg("x"), py::arg("w_qkv"),
+           py::arg("b_qkv"), py::arg("pos"), py::arg("cos_t"), py::arg("sin_t"), py::arg("layer"),
+           py::arg("page_table"), py::arg("slot_base"), py::arg("L"), py::arg("kv_start_tile"),
+           py::arg("scale"), py::arg("causal"), py::arg("q_out"), py::arg("o_out"),
+           py::arg("lse_out"), py::arg("epoch"), py::arg("existing_slot_pos") = py::none())
       .def("attend_layer", &PyRuntime::attend_layer, py::arg("qkv"), py::arg("pos"), py::arg("cos_t"),
            py::arg("sin_t"), py::arg("layer"), py::arg("page_table"), py::arg("slot_base"), py::arg("L"),
            py::arg("kv_start_tile"), py::arg("scale"), py::arg("causal"), py::arg("q_out"),

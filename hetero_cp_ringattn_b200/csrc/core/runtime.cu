@@ -6,6 +6,7 @@
 
 #include "../kernels/attn_fwd_sm100.h"
 #include "../kernels/elementwise.h"
+#include "../kernels/gemm_sm100.h"
 
 namespace hcp {
 
@@ -31,6 +32,9 @@ Status DomainRuntime::Init(const RuntimeConfig& cfg) {
   if (cfg.num_heads <= 0 || cfg.num_heads % cfg.geom.hkv) return Status::InvalidArgument("num_heads % hkv");
   cfg_ = cfg;
   auto st = cuda_status(cudaSetDevice(cfg.device), "cudaSetDevice");
+  if (!st.ok()) return st;
+  st = cuda_status(cudaDeviceGetAttribute(&num_sms_, cudaDevAttrMultiProcessorCount, cfg.device),
+                   "cudaDeviceGetAttribute");
   if (!st.ok()) return st;
   off_flags_ = 0;
   size_t flags_bytes = size_t(kFlagWords) * sizeof(unsigned long long);
@@ -171,7 +175,45 @@ Status DomainRuntime::PushLayer(const RingLayerArgs& a, cudaStream_t stream) {
     const char* e = ew::stage_push(sp, stream);
     if (e) return Status::Internal(e);
   }
-  // 2. RoPE + Q write + arena write + push K/V to every rank's staging buffer, then kv_ready
+  // 2. RoPE + Q write + arena write + push K/V to every rank's staging buffer, then kv_ready;
+  //    fused into the projection GEMM's epilogue when the layer input is given
+  if (a.x != nullptr && a.T > 0) {
+    gemm::GemmArgs g{};
+    g.A = static_cast<const __nv_bfloat16*>(a.x);
+    g.lda = a.ldx;
+    g.B = static_cast<const __nv_bfloat16*>(a.w_qkv);
+    g.ldb = a.hidden;
+    g.M = a.T;
+    g.N = (a.H + 2 * cfg_.geom.hkv) * cfg_.geom.d;
+    g.K = a.hidden;
+    g.bias = static_cast<const __nv_bfloat16*>(a.b_qkv);
+    g.status = status_;
+    g.num_sms = num_sms_;
+    gemm::QkvPushArgs q{};
+    q.pos = a.pos;
+    q.cos_t = a.cos_t;
+    q.sin_t = a.sin_t;
+    q.max_pos = a.max_pos;
+    q.H = a.H;
+    q.Hkv = cfg_.geom.hkv;
+    q.D = cfg_.geom.d;
+    q.q_out = static_cast<__nv_bfloat16*>(a.q_out);
+    q.arena = a.page_table ? static_cast<__nv_bfloat16*>(arena()) : nullptr;
+    q.geom = cfg_.geom;
+    q.layer = a.layer;
+    q.page_table = a.page_table;
+    q.slot_base = a.slot_base;
+    q.slot_cap = a.slot_cap;
+    q.stage_ptrs = stage_tab_[parity];
+    q.n_stage = n;
+    q.stage_cap = cfg_.stage_cap;
+    q.done_counter = n > 1 ? counters_ : nullptr;
+    q.ready_ptrs = kv_ready_tab_;
+    q.epoch = a.epoch;
+    const char* e = gemm::gemm_qkv_push(g, q, stream);
+    if (e) return Status::Internal(e);
+    return Status::Ok();
+  }
   ew::QkvPrefillArgs q{};
   q.qkv = static_cast<const __nv_bfloat16*>(a.qkv);
   q.ld_qkv = a.ld_qkv;

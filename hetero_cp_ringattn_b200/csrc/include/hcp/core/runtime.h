@@ -62,6 +62,14 @@ struct RingLayerArgs {
   // session continuation: already-stored slots [0, existing_n) of this layer to re-push
   const int* existing_slot_pos = nullptr;
   int existing_n = 0;
+  // fused projection (optional): with x set, PushLayer computes the projection x w_qkv^T
+  // (+ b_qkv) with the tcgen05 GEMM whose epilogue rotates, writes Q and pushes K/V, and `qkv`
+  // is not read
+  const void* x = nullptr;          // [T, hidden] bf16, the normalised layer input
+  long ldx = 0;
+  const void* w_qkv = nullptr;      // [(H + 2 Hkv) D, hidden] bf16
+  const void* b_qkv = nullptr;      // optional [(H + 2 Hkv) D] bias
+  int hidden = 0;
 };
 
 class DomainRuntime {
@@ -122,6 +130,7 @@ class DomainRuntime {
   size_t xslot_bytes_ = 0, stage_parity_bytes_ = 0, arena_bytes_ = 0;
   int* status_ = nullptr;            // kStatusWords int32
   unsigned int* counters_ = nullptr; // 64 uint32 (last-CTA-done counters)
+  int num_sms_ = 0;
   void** stage_tab_[2] = {nullptr, nullptr};
   unsigned long long** kv_ready_tab_ = nullptr;
   unsigned long long** consumed_tab_ = nullptr;

@@ -42,6 +42,7 @@ struct Params {
   const __nv_bfloat16* R;
   long ldr;
   int* status;
+  QkvPushArgs qkv;  // kEpiQkvPush only
 };
 
 __device__ __forceinline__ void tile_coords(int tile, const Params& p, int& mb, int& nb) {
@@ -56,7 +57,94 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, uint32_t tacc, in
   const int m = mb * BM + row_in_tile;
   const bool row_ok = m < p.M;
   uint32_t r[32];
-  if constexpr (EPI == kEpiSwiGLU) {
+  if constexpr (EPI == kEpiQkvPush) {
+    // heads never straddle a 32-column chunk (D is 64 or 128); a head's rotation pairs column j
+    // with j + D/2, both in this thread's accumulator row
+    const QkvPushArgs& q = p.qkv;
+    const int D = q.D, half = D / 2;
+    const int pos = row_ok ? q.pos[m] : -1;
+    const bool pos_ok = pos >= 0 && pos < q.max_pos;
+    if (row_ok && !pos_ok) report_error(p.status, int(StatusCode::kOutOfBounds), 111, pos, m);
+    const int slot = q.slot_base + m;
+    int page = -1;
+    if (row_ok && q.arena != nullptr) {
+      if (slot >= 0 && slot < q.slot_cap) page = q.page_table[slot / q.geom.page];
+      else report_error(p.status, int(StatusCode::kOutOfBounds), 112, slot, m);
+    }
+    const bool stage_ok = pos_ok && pos < q.stage_cap;
+#pragma unroll 1
+    for (int hb = 0; hb < BN; hb += D) {
+      const int col0 = nb * BN + hb;
+      if (col0 >= p.N) break;
+      const int gh = col0 / D;                           // head index in the q | k | v row
+      const int kind = gh < q.H ? 0 : (gh < q.H + q.Hkv ? 1 : 2);
+#pragma unroll 1
+      for (int jc = 0; jc < half; jc += 32) {
+        uint32_t u[32];
+        tmem_ld32(tacc + hb + jc, r);
+        tmem_ld32(tacc + hb + half + jc, u);
+        tmem_wait_ld();
+        if (!row_ok) continue;
+        float lo[32], hi[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          lo[i] = __uint_as_float(r[i]);
+          hi[i] = __uint_as_float(u[i]);
+        }
+        if (p.bias != nullptr) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            lo[i] += __bfloat162float(p.bias[col0 + jc + i]);
+            hi[i] += __bfloat162float(p.bias[col0 + half + jc + i]);
+          }
+        }
+        if (kind < 2 && pos_ok) {
+          const float4* c4 = reinterpret_cast<const float4*>(q.cos_t + (long)pos * half + jc);
+          const float4* s4 = reinterpret_cast<const float4*>(q.sin_t + (long)pos * half + jc);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const float4 c = c4[i], sn = s4[i];
+            const float cc[4] = {c.x, c.y, c.z, c.w}, ss[4] = {sn.x, sn.y, sn.z, sn.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float x1 = lo[4 * i + e], x2 = hi[4 * i + e];
+              lo[4 * i + e] = x1 * cc[e] - x2 * ss[e];
+              hi[4 * i + e] = x2 * cc[e] + x1 * ss[e];
+            }
+          }
+        }
+        uint4 vlo[4], vhi[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          vlo[i] = make_uint4(pack_bf16x2(lo[8 * i], lo[8 * i + 1]), pack_bf16x2(lo[8 * i + 2], lo[8 * i + 3]),
+                              pack_bf16x2(lo[8 * i + 4], lo[8 * i + 5]), pack_bf16x2(lo[8 * i + 6], lo[8 * i + 7]));
+          vhi[i] = make_uint4(pack_bf16x2(hi[8 * i], hi[8 * i + 1]), pack_bf16x2(hi[8 * i + 2], hi[8 * i + 3]),
+                              pack_bf16x2(hi[8 * i + 4], hi[8 * i + 5]), pack_bf16x2(hi[8 * i + 6], hi[8 * i + 7]));
+        }
+        auto put = [&](__nv_bfloat16* base) {
+          uint4* d0 = reinterpret_cast<uint4*>(base + jc);
+          uint4* d1 = reinterpret_cast<uint4*>(base + half + jc);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            d0[i] = vlo[i];
+            d1[i] = vhi[i];
+          }
+        };
+        if (kind == 0) {
+          put(q.q_out + ((long)m * q.H + gh) * D);
+        } else {
+          const int kv = kind - 1;
+          const int h = gh - q.H - kv * q.Hkv;
+          if (page >= 0) put(q.arena + q.geom.offset(q.layer, page, kv, h, slot % q.geom.page));
+          if (stage_ok) {
+            const long soff = ((long)(kv * q.Hkv + h) * q.stage_cap + pos) * D;
+            for (int rk = 0; rk < q.n_stage; ++rk)
+              put(reinterpret_cast<__nv_bfloat16*>(q.stage_ptrs[rk]) + soff);
+          }
+        }
+      }
+    }
+  } else if constexpr (EPI == kEpiSwiGLU) {
     // tile columns [0,128) are gate rows, [128,256) the matching up rows
     const int out_n0 = nb * (BN / 2);
 #pragma unroll 1
@@ -291,11 +379,28 @@ __global__ void __launch_bounds__(256, 1)
     }
   }
 
+  if constexpr (EPI == kEpiQkvPush) {
+    // this thread's peer stores are ordered before the CTA's completion count below
+    if (warp >= 4) __threadfence_system();
+  }
   tc_fence_before();
   __syncthreads();
   if (warp == 2) {
     tc_fence_after();
     tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+  if constexpr (EPI == kEpiQkvPush) {
+    // last CTA done: every CTA's K/V rows are visible system-wide, publish the epoch to every
+    // rank's kv_ready slot for this rank
+    if (threadIdx.x == 0 && p.qkv.done_counter != nullptr) {
+      __threadfence_system();
+      const unsigned prev = atomicAdd(p.qkv.done_counter, 1u);
+      if (prev == gridDim.x - 1) {
+        __threadfence_system();
+        for (int rk = 0; rk < p.qkv.n_stage; ++rk) st_release_sys(p.qkv.ready_ptrs[rk], p.qkv.epoch);
+        *p.qkv.done_counter = 0;
+      }
+    }
   }
 }
 
@@ -395,6 +500,39 @@ const char* gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
     case kEpiSwiGLU: e = launch<kEpiSwiGLU>(ta, tb, p, grid, stream); break;
     default: return "gemm: unknown epilogue";
   }
+  return e == cudaSuccess ? nullptr : cudaGetErrorString(e);
+}
+
+const char* gemm_qkv_push(const GemmArgs& a, const QkvPushArgs& q, cudaStream_t stream) {
+  if (a.M <= 0 || a.N <= 0 || a.K <= 0) return "gemm_qkv_push: empty problem";
+  if ((a.lda * 2) % 16 || (a.ldb * 2) % 16) return "gemm_qkv_push: lda/ldb must be multiples of 8";
+  if ((reinterpret_cast<uintptr_t>(a.A) | reinterpret_cast<uintptr_t>(a.B)) & 15)
+    return "gemm_qkv_push: A/B base must be 16-byte aligned";
+  if ((q.D != 64 && q.D != 128) || BN % q.D) return "gemm_qkv_push: head_dim must be 64 or 128";
+  if (a.N != (q.H + 2 * q.Hkv) * q.D) return "gemm_qkv_push: N must be (H + 2 Hkv) * D";
+  if (q.pos == nullptr || q.cos_t == nullptr || q.sin_t == nullptr || q.q_out == nullptr)
+    return "gemm_qkv_push: positions, RoPE tables and q_out are required";
+  if ((reinterpret_cast<uintptr_t>(q.q_out) | reinterpret_cast<uintptr_t>(q.cos_t) |
+       reinterpret_cast<uintptr_t>(q.sin_t)) & 15)
+    return "gemm_qkv_push: q_out and the RoPE tables must be 16-byte aligned";
+  if (q.n_stage > 0 && q.stage_ptrs == nullptr) return "gemm_qkv_push: staging pointers missing";
+  CUtensorMap ta, tb;
+  if (!make_tma_2d_bf16(&ta, a.A, a.K, a.M, uint64_t(a.lda) * 2, BK, BM))
+    return "gemm_qkv_push: TMA descriptor for A failed";
+  if (!make_tma_2d_bf16(&tb, a.B, a.K, a.N, uint64_t(a.ldb) * 2, BK, BN))
+    return "gemm_qkv_push: TMA descriptor for B failed";
+  Params p{};
+  p.M = a.M;
+  p.N = a.N;
+  p.K = a.K;
+  p.num_m_tiles = (a.M + BM - 1) / BM;
+  p.num_n_tiles = (a.N + BN - 1) / BN;
+  p.bias = a.bias;
+  p.status = a.status;
+  p.qkv = q;
+  const int tiles = p.num_m_tiles * p.num_n_tiles;
+  const int grid = tiles < a.num_sms ? tiles : a.num_sms;
+  cudaError_t e = launch<kEpiQkvPush>(ta, tb, p, grid, stream);
   return e == cudaSuccess ? nullptr : cudaGetErrorString(e);
 }
 

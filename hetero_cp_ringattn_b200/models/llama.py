@@ -199,20 +199,24 @@ class LlamaCPEngine:
                 ev = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
                 ev[0].record()
             K.rmsnorm(x, lw.in_norm, self.cfg.rms_norm_eps, out=xn)
-            qkv = K.gemm(xn, lw.wqkv, "bias" if lw.bqkv is not None else "store", bias=lw.bqkv)
             self.prefill_epoch += 1
-            args = (qkv, pos, self.cos, self.sin, li, st.kv.pt_device, 0, Lp, start_tile,
+            tail = (pos, self.cos, self.sin, li, st.kv.pt_device, 0, Lp, start_tile,
                     self.scale, True, q_buf, o_buf, None, self.prefill_epoch)
             if trace:
                 ev[1].record()
-            self.rt.push_layer(*args)
+            if self.env.fused_qkv:
+                # one kernel: QKV GEMM whose epilogue rotates, writes Q and pushes K/V to every rank
+                self.rt.push_layer_fused(xn, lw.wqkv, lw.bqkv, *tail)
+            else:
+                qkv = K.gemm(xn, lw.wqkv, "bias" if lw.bqkv is not None else "store", bias=lw.bqkv)
+                self.rt.push_layer(qkv, *tail)
+                del qkv
             if trace:
                 ev[2].record()
-            self.rt.attend_layer(*args)
+            self.rt.attend_layer(xn, *tail)
             if trace:
                 ev[3].record()
             launches.count(2 + (3 if self.world > 1 else 0) - (1 if self.world > 1 and self.prefill_epoch <= 2 else 0))
-            del qkv
             K.gemm(o_buf.view(T, self.H * self.D), lw.wo, "residual", residual=x)
             K.rmsnorm(x, lw.post_norm, self.cfg.rms_norm_eps, out=xn)
             g = K.gemm(xn, lw.wgu, "swiglu")
@@ -495,16 +499,19 @@ class LlamaCPEngine:
         for li, lw in enumerate(w.layers):
             c = int(kv.layer_counts[li])
             existing = torch.from_numpy(kv.slot_pos[li, :c].astype(np.int32)).to(dev)
+            self.prefill_epoch += 1
+            tail = (pos, self.cos, self.sin, li, kv.pt_device, c, Ltot, start_tile, self.scale,
+                    True, q_buf, o_buf, None, self.prefill_epoch, existing)
             if T:
                 K.rmsnorm(x, lw.in_norm, self.cfg.rms_norm_eps, out=xn)
-                qkv = K.gemm(xn, lw.wqkv, "bias" if lw.bqkv is not None else "store", bias=lw.bqkv)
+            if T and self.env.fused_qkv:
+                self.rt.push_layer_fused(xn, lw.wqkv, lw.bqkv, *tail)
+                self.rt.attend_layer(xn, *tail)
             else:
-                qkv = empty_qkv
-            self.prefill_epoch += 1
-            args = (qkv, pos, self.cos, self.sin, li, kv.pt_device, c, Ltot, start_tile, self.scale,
-                    True, q_buf, o_buf, None, self.prefill_epoch, existing)
-            self.rt.push_layer(*args)
-            self.rt.attend_layer(*args)
+                qkv = K.gemm(xn, lw.wqkv, "bias" if lw.bqkv is not None else "store",
+                             bias=lw.bqkv) if T else empty_qkv
+                self.rt.push_layer(qkv, *tail)
+                self.rt.attend_layer(qkv, *tail)
             if T:
                 K.gemm(o_buf.view(T, self.H * self.D), lw.wo, "residual", residual=x)
                 K.rmsnorm(x, lw.post_norm, self.cfg.rms_norm_eps, out=xn)

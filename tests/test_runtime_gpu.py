@@ -148,3 +148,63 @@ def test_decode_exchange(dev, world, b):
             assert (outs[r][bb].view(H, D).float() - ro[0]).abs().max() < 2e-2
     for r in range(1, world):
         assert torch.equal(outs[r], outs[0]), "ranks must produce bit-identical combined outputs"
+
+
+@pytest.mark.parametrize("d,chunks,strategy", [(64, [700], "vanilla"), (128, [333, 400], "zigzag"),
+                                               (64, [300, 200, 257], "striped")])
+def test_fused_projection_push(dev, d, chunks, strategy):
+    """QKV GEMM whose epilogue adds the bias, rotates, writes Q and pushes K/V to every rank's
+    staging buffer and arena (no projection output in memory), then ring attention; against an
+    fp32 reference of projection + RoPE + causal attention."""
+    torch.manual_seed(11)
+    hid, n, L = 320, len(chunks), sum(chunks)
+    nq = (H + 2 * HKV) * d
+    rts = [native().Runtime(r, n, 0, 1, 16, PAGE, HKV, d, H, 2048, 8, 2000) for r in range(n)]
+    if n > 1:
+        for rt in rts:
+            rt.open_peers_local(rts)
+    x_all = (torch.randn(L, hid, device=dev) * 0.5).bfloat16()
+    w = (torch.randn(nq, hid, device=dev) / math.sqrt(hid)).bfloat16()
+    bias = (torch.randn(nq, device=dev) * 0.1).bfloat16()
+    qkv_all = x_all.float() @ w.float().t() + bias.float()
+    pos_all = torch.arange(L, device=dev)
+    cos, sin = ref.rope_cos_sin(torch.arange(4096, device=dev), d, 10000.0)
+    cos, sin = cos.contiguous(), sin.contiguous()
+    positions = [torch.as_tensor(p, device=dev) for p in layout_positions(chunks, strategy)]
+    runs = []
+    for r in range(n):
+        p = positions[r]
+        x = x_all[p].contiguous()
+        pt = torch.arange(r * 4, r * 4 + 4, dtype=torch.int32, device=dev)
+        q_out = torch.empty(len(p), H, d, device=dev, dtype=torch.bfloat16)
+        o_out = torch.empty_like(q_out)
+        lse = torch.empty(H, len(p), device=dev, dtype=torch.float32)
+        start = int(p[0]) // 128 if strategy == "vanilla" else 0
+        tail = (p.int().contiguous(), cos, sin, 0, pt, 0, L, start, 1.0 / math.sqrt(d), True,
+                q_out, o_out, lse, 1)
+        runs.append((x, tail, q_out, o_out, lse))
+    for r in range(n):
+        rts[r].push_layer_fused(runs[r][0], w, bias, *runs[r][1])
+    for r in range(n):
+        rts[r].attend_layer(runs[r][0], *runs[r][1])
+    torch.cuda.synchronize()
+    for rt in rts:
+        rt.check()
+    q = ref.apply_rope(qkv_all[:, : H * d].view(-1, H, d), pos_all, 10000.0)
+    k = ref.apply_rope(qkv_all[:, H * d:(H + HKV) * d].view(-1, HKV, d), pos_all, 10000.0)
+    v = qkv_all[:, (H + HKV) * d:].view(-1, HKV, d)
+    o_ref, lse_ref = ref.full_attention(q, k, v, pos_all, pos_all, causal=True)
+    for r in range(n):
+        p = positions[r]
+        _, _, q_out, o_out, lse = runs[r]
+        assert (q_out.float() - q[p]).abs().max() < 3e-2, f"rank {r} q"
+        assert (o_out.float() - o_ref[p]).abs().max() < 3e-2, f"rank {r} o"
+        assert (lse - lse_ref[:, p]).abs().max() < 3e-2
+        arena = rts[r].arena()
+        pages = torch.arange(r * 4, r * 4 + 4, device=dev)
+        kk = arena[0, pages, 0].permute(1, 0, 2, 3).reshape(HKV, -1, d)[:, : len(p)]
+        vv = arena[0, pages, 1].permute(1, 0, 2, 3).reshape(HKV, -1, d)[:, : len(p)]
+        assert (kk.float().transpose(0, 1) - k[p]).abs().max() < 3e-2
+        assert (vv.float().transpose(0, 1) - v[p]).abs().max() < 3e-2
+    for rt in rts:
+        rt.shutdown()
