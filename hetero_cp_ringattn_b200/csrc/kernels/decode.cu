@@ -18,6 +18,7 @@
 // exchange O(B*H*D) bytes once per layer instead of N-1 serial network hops.
 #include "common.cuh"
 #include "decode.h"
+#include "gemm_sm100.h"
 #include "kv_layout.h"
 
 namespace hcp {
@@ -263,40 +264,66 @@ const char* gemv(const GemvArgs& a, cudaStream_t s) {
 // ----------------------------------------------------------------------------- K2 decode attention
 // grid (splits, Hkv, B), 128 threads (4 warps). Each warp owns a contiguous, chunk-aligned token
 // range of its split and streams it through a private STAGES-deep shared-memory ring: lane 0
-// issues one bulk copy for the K rows and one for the V rows of a chunk (CT tokens, 2 KB each;
-// chunks never straddle a 256-row page) and the warp waits on the chunk's mbarrier (bounded).
-// A token's rows are spread over LPT lanes that each own DPL consecutive head dims (16, or 8
-// for 8-head GQA groups so q and the accumulators of all G heads fit in registers). Per chunk:
-// scores with packed f32x2 FMAs and an LPT-lane shuffle reduction, one warp-wide running-max
-// update per head (the accumulator rescale happens once per chunk, not per token), then
-// p = 2^(s - m) and O += p V with packed FMAs. The warp's token groups and the 4 warps are
-// merged at the end and the split's (O, LSE) partial is written.
-constexpr int kDecStages = 4;
+// issues TMA tile loads (128-byte swizzle, 16 rows x 64 head dims per box) of the chunk's K and V
+// rows straight from the paged arena (a chunk never straddles a 256-row page) and the warp waits
+// on the chunk's mbarrier (bounded).
+//
+// The math runs on the tensor cores with warp-level m16n8k16 bf16 MMAs (the GQA group has at most
+// 8 query rows, below the 64-row minimum of tcgen05, and the loop is memory-bound, so the MMAs are
+// only there to cut the instruction count per token):
+//   S = Q K^T   A = the group's q rows (16 rows, G used), B = K^T of 8 tokens. The head-dim
+//               order inside the dot product is permuted so lane t's B operand is one contiguous
+//               run of D/4 dims of a K row (two or four conflict-free 16-byte shared loads); the
+//               q fragments use the same permutation.
+//   O += P V    A = P straight from S's accumulator fragments (packed to bf16), B = V through
+//               ldmatrix.trans (the swizzle makes the 8 row addresses conflict-free).
+// One running-max update per head and chunk; the row sums are per-lane partials reduced at the
+// end; the 4 warps are merged through shared memory and the split's (O, LSE) partial is written.
+constexpr int kDecCT = 16;  // tokens per chunk (two 8-token MMA n-tiles)
 
 template <int D>
-struct DecChunk {
-  static constexpr int CT = 1024 / D;                  // tokens per chunk (2 KB of K rows)
-  static constexpr int BYTES = CT * D * 2;             // K (or V) bytes per chunk
-  static constexpr int WARP_SMEM = kDecStages * 2 * BYTES;
-  static constexpr int SMEM = 4 * WARP_SMEM;           // dynamic shared memory per CTA
+struct DecCfg {
+  static constexpr int NH = D / 64;                      // 64-dim swizzled sub-tiles per row
+  static constexpr int SUB = kDecCT * 128;               // bytes of one sub-tile (16 rows x 128 B)
+  static constexpr int STAGE = 2 * NH * SUB;             // K then V sub-tiles
+  static constexpr int STAGES = (D == 64) ? 3 : 2;         // 2-3 CTAs per SM
+  static constexpr int WARP_SMEM = STAGES * STAGE;
+  static constexpr int SMEM = 1024 + 4 * WARP_SMEM;      // + alignment slack
 };
 
+__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+
+// byte offset of 16-byte chunk c of row r inside a 128-byte-swizzled tile (TMA SWIZZLE_128B)
+__device__ __forceinline__ uint32_t swz(int r, int c) { return uint32_t(r * 128 + ((c ^ (r & 7)) << 4)); }
+
 template <int D, int G>
-__global__ void __launch_bounds__(128) decode_attn_kernel(DecodeAttnArgs a) {
-  constexpr int DPL = (G >= 8) ? 8 : 16;   // head dims per lane
-  constexpr int NV = DPL / 8;              // 16-byte vectors per lane per K (or V) row
-  constexpr int LPT = D / DPL;             // lanes per token
-  constexpr int TPW = 32 / LPT;            // tokens per warp step
+__global__ void __launch_bounds__(128) decode_attn_kernel(const __grid_constant__ CUtensorMap tm_kv,
+                                                          DecodeAttnArgs a) {
+  using C = DecCfg<D>;
   constexpr int NW = 4;                    // warps per CTA
-  constexpr int CT = DecChunk<D>::CT;
-  constexpr int STEPS = CT / TPW;          // warp steps per chunk
-  constexpr int BYTES = DecChunk<D>::BYTES;
-  static_assert(LPT >= 1 && LPT <= 32 && 32 % LPT == 0 && CT % TPW == 0 && 256 % CT == 0, "tiling");
-  extern __shared__ __align__(128) uint8_t dsm[];
-  __shared__ __align__(8) uint64_t bars[NW][kDecStages];
+  constexpr int CT = kDecCT;
+  constexpr int DQ = D / 4;                // contiguous dims of a K row per lane in S = Q K^T
+  constexpr int KS = D / 16;               // MMA k-steps over the head dim
+  constexpr int NT = D / 8;                // 8-dim n-tiles of O
+  static_assert(G >= 1 && G <= 8, "GQA group of at most 8 query heads");
+  extern __shared__ uint8_t dsm_raw[];
+  uint8_t* dsm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dsm_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ __align__(8) uint64_t bars[NW][C::STAGES];
   const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int lane = threadIdx.x % 32, warp = threadIdx.x / 32;
-  const int gl = lane % LPT;               // lane within the token group
+  const int g = lane / 4, t = lane % 4;    // MMA fragment row group / column pair
   const int n = a.n_tokens[b];
   // chunk-aligned ranges: split -> 4 warp ranges -> CT-token chunks
   int per = (n + a.splits - 1) / a.splits;
@@ -307,189 +334,191 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(DecodeAttnArgs a) {
   const int w1 = min(s1, w0 + per / NW);
   const int nc = (w1 - w0 + CT - 1) / CT;
   const int H = a.Hkv * G;
-  uint8_t* wsm = dsm + warp * DecChunk<D>::WARP_SMEM;  // [stage][K | V][CT][D] bf16
+  uint8_t* wsm = dsm + warp * C::WARP_SMEM;  // [stage][K sub-tiles | V sub-tiles]
 
-  // zero the ring once (rows past the end of a range are then finite and get p = 0), init the
-  // barriers, make both visible to the async proxy
-  for (int i = threadIdx.x; i < DecChunk<D>::SMEM / 16; i += blockDim.x)
-    reinterpret_cast<uint4*>(dsm)[i] = make_uint4(0u, 0u, 0u, 0u);
   if (lane == 0)
-    for (int st = 0; st < kDecStages; ++st) mbar_init(&bars[warp][st], 1);
+    for (int st = 0; st < C::STAGES; ++st) mbar_init(&bars[warp][st], 1);
   fence_barrier_init();
-  fence_proxy_async_smem();
-  __syncthreads();
+  __syncwarp();
 
   const int* pt = a.page_tables + (long)b * a.pt_stride;
+  const long rows_per_layer = (long)a.geom.pages * 2 * a.geom.hkv * a.geom.page;
   auto issue = [&](int c) {
     const int t0 = w0 + c * CT;
-    const int rows = min(CT, w1 - t0);
     const int page = pt[t0 / a.geom.page];
-    const __nv_bfloat16* src = a.arena + a.geom.offset(a.layer, page, 0, h, t0 % a.geom.page);
-    uint8_t* dst = wsm + (c % kDecStages) * 2 * BYTES;
-    uint64_t* bar = &bars[warp][c % kDecStages];
-    const uint32_t bytes = uint32_t(rows) * D * 2;
-    mbar_arrive_expect_tx(bar, 2 * bytes);
-    bulk_load(dst, src, bytes, bar);
-    bulk_load(dst + BYTES, src + a.geom.kv_stride(), bytes, bar);
-  };
-  if (lane == 0)
-    for (int c = 0; c < kDecStages - 1 && c < nc; ++c) issue(c);
-
-  // q slice of every head of the group, pre-scaled into the log2 domain
-  float2 q[G][DPL / 2];
-  const float qs = a.scale * kLog2e;
+    const long krow = (long)a.layer * rows_per_layer +
+                      ((long)(page * 2 + 0) * a.geom.hkv + h) * a.geom.page + (t0 % a.geom.page);
+    const long vrow = krow + (long)a.geom.hkv * a.geom.page;
+    uint8_t* dst = wsm + (c % C::STAGES) * C::STAGE;
+    uint64_t* bar = &bars[warp][c % C::STAGES];
+    mbar_arrive_expect_tx(bar, C::STAGE);
 #pragma unroll
-  for (int g = 0; g < G; ++g)
-#pragma unroll
-    for (int v = 0; v < NV; ++v) {
-      const uint4 w = *reinterpret_cast<const uint4*>(a.q + ((long)b * H + h * G + g) * D + gl * DPL + v * 8);
-      const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-      for (int j = 0; j < 4; ++j) q[g][v * 4 + j] = make_float2(bf16_lo(ww[j]) * qs, bf16_hi(ww[j]) * qs);
+    for (int j = 0; j < C::NH; ++j) {
+      tma_load_2d(dst + j * C::SUB, &tm_kv, bar, j * 64, int(krow));
+      tma_load_2d(dst + (C::NH + j) * C::SUB, &tm_kv, bar, j * 64, int(vrow));
     }
-  float2 acc[G][DPL / 2];
-  float m[G], l[G];
-#pragma unroll
-  for (int g = 0; g < G; ++g) {
-    m[g] = -INFINITY;
-    l[g] = 0.f;
-#pragma unroll
-    for (int i = 0; i < DPL / 2; ++i) acc[g][i] = make_float2(0.f, 0.f);
+  };
+  if (lane == 0) {
+    tma_prefetch_desc(&tm_kv);
+    for (int c = 0; c < C::STAGES - 1 && c < nc; ++c) issue(c);
   }
+
+  // q fragments (A of S = Q K^T): row g = head g of the group, pre-scaled into the log2 domain;
+  // k-step ks, lane t covers dims t * DQ + 4 ks + {0, 1} (a0) and + {2, 3} (a2)
+  uint32_t qa[KS][2];
+  {
+    const float qs = a.scale * kLog2e;
+    float qf[DQ];
+    if (g < G) {
+      const __nv_bfloat16* qp = a.q + ((long)b * H + h * G + g) * D + t * DQ;
+#pragma unroll
+      for (int v = 0; v < DQ / 8; ++v) {
+        const uint4 w = *reinterpret_cast<const uint4*>(qp + v * 8);
+        const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          qf[v * 8 + 2 * j] = bf16_lo(ww[j]) * qs;
+          qf[v * 8 + 2 * j + 1] = bf16_hi(ww[j]) * qs;
+        }
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < DQ; ++i) qf[i] = 0.f;
+    }
+#pragma unroll
+    for (int ks = 0; ks < KS; ++ks) {
+      qa[ks][0] = pack_bf16x2(qf[4 * ks], qf[4 * ks + 1]);
+      qa[ks][1] = pack_bf16x2(qf[4 * ks + 2], qf[4 * ks + 3]);
+    }
+  }
+  float acc[NT][4];
+#pragma unroll
+  for (int i = 0; i < NT; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+  float m = -INFINITY, l = 0.f;  // head g's running max (log2 domain) and this lane's row-sum part
   int consumed = 0;
   bool ok = true;
   for (int c = 0; c < nc; ++c) {
-    if (lane == 0 && c + kDecStages - 1 < nc) {
+    if (lane == 0 && c + C::STAGES - 1 < nc) {
       fence_proxy_async_smem();  // the warp's reads of that stage (chunk c - 1) come first
-      issue(c + kDecStages - 1);
+      issue(c + C::STAGES - 1);
     }
-    ok = __all_sync(0xffffffffu, mbar_wait(&bars[warp][c % kDecStages], (c / kDecStages) & 1, a.status, 301));
+    ok = __all_sync(0xffffffffu, mbar_wait(&bars[warp][c % C::STAGES], (c / C::STAGES) & 1, a.status, 301));
     if (!ok) break;
     consumed = c + 1;
-    const __nv_bfloat16* sk = reinterpret_cast<const __nv_bfloat16*>(wsm + (c % kDecStages) * 2 * BYTES);
-    const __nv_bfloat16* sv = sk + CT * D;
+    uint8_t* sk = wsm + (c % C::STAGES) * C::STAGE;
+    uint8_t* sv = sk + C::NH * C::SUB;
     const int t0 = w0 + c * CT;
-    float sc[STEPS][G];
+    const int valid = min(CT, w1 - t0);
+    if (valid < CT) {
+      // rows past the range hold whatever the page had: zero V there (p is 0 for them, and
+      // 0 * a non-finite value would not be)
+      for (int i = lane; i < (CT - valid) * C::NH * 8; i += 32) {
+        const int r = valid + i / (C::NH * 8), rem = i % (C::NH * 8);
+        *reinterpret_cast<uint4*>(sv + (rem / 8) * C::SUB + r * 128 + (rem % 8) * 16) = make_uint4(0u, 0u, 0u, 0u);
+      }
+      __syncwarp();
+    }
+    // S = Q K^T for the two 8-token n-tiles
+    float s[2][4];
 #pragma unroll
-    for (int u = 0; u < STEPS; ++u) {
-      const int tt = u * TPW + lane / LPT;
-      const bool valid = t0 + tt < w1;
-      float2 kf[DPL / 2];
+    for (int nt = 0; nt < 2; ++nt) {
+      s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
+      const int r = nt * 8 + g;
+      uint32_t kw[DQ / 2];
 #pragma unroll
-      for (int v = 0; v < NV; ++v) {
-        const uint4 kw = *reinterpret_cast<const uint4*>(sk + tt * D + gl * DPL + v * 8);
-        const uint32_t ww[4] = {kw.x, kw.y, kw.z, kw.w};
-#pragma unroll
-        for (int j = 0; j < 4; ++j) kf[v * 4 + j] = make_float2(bf16_lo(ww[j]), bf16_hi(ww[j]));
+      for (int v = 0; v < DQ / 8; ++v) {
+        const int dim = t * DQ + v * 8;
+        const uint4 w = *reinterpret_cast<const uint4*>(sk + (dim / 64) * C::SUB + swz(r, (dim % 64) / 8));
+        kw[4 * v] = w.x;
+        kw[4 * v + 1] = w.y;
+        kw[4 * v + 2] = w.z;
+        kw[4 * v + 3] = w.w;
       }
 #pragma unroll
-      for (int g = 0; g < G; ++g) {
-        float2 d2 = make_float2(0.f, 0.f);
-#pragma unroll
-        for (int i = 0; i < DPL / 2; ++i) d2 = __ffma2_rn(q[g][i], kf[i], d2);
-        float x = d2.x + d2.y;
-#pragma unroll
-        for (int o = LPT / 2; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
-        sc[u][g] = valid ? x : -INFINITY;
+      for (int ks = 0; ks < KS; ++ks) {
+        const uint32_t af[4] = {qa[ks][0], 0u, qa[ks][1], 0u};
+        mma16816(s[nt], af, kw[2 * ks], kw[2 * ks + 1]);
       }
     }
-    // one running-max update per head and chunk (warp-uniform)
+    // head g's scores: tokens 2t, 2t + 1 (n-tile 0) and 8 + 2t, 9 + 2t (n-tile 1)
+    float sc[4] = {s[0][0], s[0][1], s[1][0], s[1][1]};
 #pragma unroll
-    for (int g = 0; g < G; ++g) {
-      float cm = sc[0][g];
+    for (int e = 0; e < 4; ++e) {
+      const int tok = (e >> 1) * 8 + 2 * t + (e & 1);
+      if (tok >= valid) sc[e] = -INFINITY;
+    }
+    float cm = fmaxf(fmaxf(sc[0], sc[1]), fmaxf(sc[2], sc[3]));
+    cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 1));
+    cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 2));
+    if (cm > m) {
+      const float al = fast_exp2(m - cm);  // 0 while nothing has been accumulated
+      m = cm;
+      l *= al;
 #pragma unroll
-      for (int u = 1; u < STEPS; ++u) cm = fmaxf(cm, sc[u][g]);
-#pragma unroll
-      for (int o = LPT; o < 32; o <<= 1) cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, o));
-      if (cm > m[g]) {
-        const float al = fast_exp2(m[g] - cm);  // 0 while nothing has been accumulated
-        m[g] = cm;
-        l[g] *= al;
-        const float2 al2 = make_float2(al, al);
-#pragma unroll
-        for (int i = 0; i < DPL / 2; ++i) acc[g][i] = __fmul2_rn(acc[g][i], al2);
+      for (int i = 0; i < NT; ++i) {
+        acc[i][0] *= al;
+        acc[i][1] *= al;
       }
     }
+    float pe[4];
 #pragma unroll
-    for (int u = 0; u < STEPS; ++u) {
-      const int tt = u * TPW + lane / LPT;
-      float2 vf[DPL / 2];
+    for (int e = 0; e < 4; ++e) pe[e] = (m == -INFINITY) ? 0.f : fast_exp2(sc[e] - m);
+    l += (pe[0] + pe[1]) + (pe[2] + pe[3]);
+    const uint32_t pa[4] = {pack_bf16x2(pe[0], pe[1]), 0u, pack_bf16x2(pe[2], pe[3]), 0u};
+    // O += P V: ldmatrix.trans gives the V fragments of two 8-dim n-tiles per call
+    const int lr = (lane & 7) + ((lane >> 3) & 1) * 8;  // token row this lane addresses
+    const int lc = lane >> 4;                            // +0 / +1 chunk (second n-tile)
 #pragma unroll
-      for (int v = 0; v < NV; ++v) {
-        const uint4 vw = *reinterpret_cast<const uint4*>(sv + tt * D + gl * DPL + v * 8);
-        const uint32_t ww[4] = {vw.x, vw.y, vw.z, vw.w};
-#pragma unroll
-        for (int j = 0; j < 4; ++j) vf[v * 4 + j] = make_float2(bf16_lo(ww[j]), bf16_hi(ww[j]));
-      }
-#pragma unroll
-      for (int g = 0; g < G; ++g) {
-        // m[g] is -inf only while every score so far was -inf; p is 0 then
-        const float pp = m[g] == -INFINITY ? 0.f : fast_exp2(sc[u][g] - m[g]);
-        l[g] += pp;
-        const float2 p2 = make_float2(pp, pp);
-#pragma unroll
-        for (int i = 0; i < DPL / 2; ++i) acc[g][i] = __ffma2_rn(p2, vf[i], acc[g][i]);
-      }
+    for (int j = 0; j < NT / 2; ++j) {
+      const int dim = j * 16;
+      uint32_t vb[4];
+      ldsm_x4_trans(vb, smem_u32(sv + (dim / 64) * C::SUB + swz(lr, (dim % 64) / 8 + lc)));
+      mma16816(acc[2 * j], pa, vb[0], vb[1]);
+      mma16816(acc[2 * j + 1], pa, vb[2], vb[3]);
     }
     __syncwarp();
   }
   if (!ok && lane == 0) {
     // a wait gave up: let the copies still in flight land (bounded) before the CTA exits
-    for (int c = consumed; c < nc && c < consumed + kDecStages; ++c)
-      mbar_wait(&bars[warp][c % kDecStages], (c / kDecStages) & 1, a.status, 302);
+    for (int c = consumed; c < nc && c < consumed + C::STAGES; ++c)
+      mbar_wait(&bars[warp][c % C::STAGES], (c / C::STAGES) & 1, a.status, 302);
   }
-  // merge the warp's token groups (same m in every lane of the warp): sum l and O over the lanes
-  // that own the same head dims
-#pragma unroll
-  for (int g = 0; g < G; ++g) {
-#pragma unroll
-    for (int o = LPT; o < 32; o <<= 1) {
-      l[g] += __shfl_xor_sync(0xffffffffu, l[g], o);
-#pragma unroll
-      for (int i = 0; i < DPL / 2; ++i) {
-        acc[g][i].x += __shfl_xor_sync(0xffffffffu, acc[g][i].x, o);
-        acc[g][i].y += __shfl_xor_sync(0xffffffffu, acc[g][i].y, o);
-      }
-    }
+  // the 4 lanes of a row group hold parts of head g's row sum
+  l += __shfl_xor_sync(0xffffffffu, l, 1);
+  l += __shfl_xor_sync(0xffffffffu, l, 2);
+  // merge the 4 warps through shared memory
+  __shared__ float sm_m[NW][8];
+  __shared__ float sm_l[NW][8];
+  __shared__ float sm_acc[NW][8][D];
+  if (t == 0) {
+    sm_m[warp][g] = m;
+    sm_l[warp][g] = l;
   }
-  // then the 4 warps through shared memory
-  __shared__ float sm_m[NW][G];
-  __shared__ float sm_l[NW][G];
-  __shared__ float sm_acc[NW][G][D];
-  if (lane < LPT) {
 #pragma unroll
-    for (int g = 0; g < G; ++g) {
-      if (lane == 0) {
-        sm_m[warp][g] = m[g];
-        sm_l[warp][g] = l[g];
-      }
-#pragma unroll
-      for (int i = 0; i < DPL / 2; ++i) {
-        sm_acc[warp][g][gl * DPL + 2 * i] = acc[g][i].x;
-        sm_acc[warp][g][gl * DPL + 2 * i + 1] = acc[g][i].y;
-      }
-    }
+  for (int i = 0; i < NT; ++i) {
+    sm_acc[warp][g][i * 8 + 2 * t] = acc[i][0];
+    sm_acc[warp][g][i * 8 + 2 * t + 1] = acc[i][1];
   }
   __syncthreads();
   // each thread finalises (g, d) entries: G * D outputs over 128 threads
   float* po = a.part_o + ((long)(b * H + h * G) * a.splits + split) * D;   // [B,H,splits,D]
   float* pml = a.part_lse + (long)(b * H + h * G) * a.splits + split;      // [B,H,splits]
   for (int i = threadIdx.x; i < G * D; i += blockDim.x) {
-    const int g = i / D, d = i % D;
+    const int gg = i / D, d = i % D;
     float mx = -INFINITY;
 #pragma unroll
-    for (int r = 0; r < NW; ++r) mx = fmaxf(mx, sm_m[r][g]);
+    for (int r = 0; r < NW; ++r) mx = fmaxf(mx, sm_m[r][gg]);
     float ls = 0.f, o = 0.f;
     if (mx > -INFINITY) {
 #pragma unroll
       for (int r = 0; r < NW; ++r) {
-        const float w = fast_exp2(sm_m[r][g] - mx);
-        ls += sm_l[r][g] * w;
-        o += sm_acc[r][g][d] * w;
+        const float w = fast_exp2(sm_m[r][gg] - mx);
+        ls += sm_l[r][gg] * w;
+        o += sm_acc[r][gg][d] * w;
       }
     }
-    po[(long)g * a.splits * D + d] = ls > 0.f ? o / ls : 0.f;
-    if (d == 0) pml[(long)g * a.splits] = ls > 0.f ? mx + __log2f(ls) : -INFINITY;
+    po[(long)gg * a.splits * D + d] = ls > 0.f ? o / ls : 0.f;
+    if (d == 0) pml[(long)gg * a.splits] = ls > 0.f ? mx + __log2f(ls) : -INFINITY;
   }
   // last CTA of this (b, h) combines the splits and publishes the rank partial
   __shared__ bool is_last;
@@ -608,17 +637,17 @@ static cudaError_t prepare_attn() {
   static bool done = false;
   if (done) return cudaSuccess;
   cudaError_t e = cudaFuncSetAttribute(decode_attn_kernel<D, G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       DecChunk<D>::SMEM);
+                                       DecCfg<D>::SMEM);
   done = (e == cudaSuccess);
   return e;
 }
 
 template <int D, int G>
-static cudaError_t launch_attn(const DecodeAttnArgs& a, cudaStream_t s) {
+static cudaError_t launch_attn(const CUtensorMap& tm, const DecodeAttnArgs& a, cudaStream_t s) {
   cudaError_t e = prepare_attn<D, G>();
   if (e != cudaSuccess) return e;
   dim3 grid(a.splits, a.Hkv, a.B);
-  decode_attn_kernel<D, G><<<grid, 128, DecChunk<D>::SMEM, s>>>(a);
+  decode_attn_kernel<D, G><<<grid, 128, DecCfg<D>::SMEM, s>>>(tm, a);
   return cudaGetLastError();
 }
 
@@ -627,12 +656,20 @@ const char* decode_attn(const DecodeAttnArgs& a, cudaStream_t s) {
   if (a.H % a.Hkv) return "decode_attn: H % Hkv";
   if (a.n_ranks < 1 || a.n_ranks > kMaxRanks) return "decode_attn: bad n_ranks";
   if (a.splits < 1 || a.splits > kMaxDecodeSplits) return "decode_attn: splits must be in [1, 128]";
-  if ((a.D != 64 && a.D != 128) || a.geom.page % (1024 / a.D))
-    return "decode_attn: head_dim must be 64 or 128 and the page a multiple of 1024 / head_dim rows";
+  if ((a.D != 64 && a.D != 128) || a.geom.page % kDecCT)
+    return "decode_attn: head_dim must be 64 or 128 and the page a multiple of 16 rows";
+  if (G > 8) return "decode_attn: at most 8 query heads per KV head";
   if (reinterpret_cast<uintptr_t>(a.arena) & 15) return "decode_attn: arena must be 16-byte aligned";
+  // the whole arena as one [rows, D] bf16 matrix; boxes of 16 rows x 64 dims, 128-byte swizzle
+  const unsigned long long rows =
+      (unsigned long long)a.geom.layers * a.geom.pages * 2 * a.geom.hkv * a.geom.page;
+  if (rows >= (1ull << 31)) return "decode_attn: arena has too many rows for 32-bit TMA coordinates";
+  CUtensorMap tm;
+  if (!gemm::make_tma_2d_bf16(&tm, a.arena, uint64_t(a.D), rows, uint64_t(a.D) * 2, 64, kDecCT))
+    return "decode_attn: TMA descriptor for the arena failed";
   cudaError_t e = cudaErrorInvalidValue;
 #define HCP_DEC_CASE(DD, GG) \
-  if (a.D == DD && G == GG) e = launch_attn<DD, GG>(a, s);
+  if (a.D == DD && G == GG) e = launch_attn<DD, GG>(tm, a, s);
   HCP_DEC_CASE(64, 1) HCP_DEC_CASE(64, 2) HCP_DEC_CASE(64, 4) HCP_DEC_CASE(64, 8)
   HCP_DEC_CASE(128, 1) HCP_DEC_CASE(128, 2) HCP_DEC_CASE(128, 4) HCP_DEC_CASE(128, 8)
 #undef HCP_DEC_CASE
@@ -644,7 +681,7 @@ int decode_attn_ctas_per_sm(int D, int G) {
   int n = 0;
 #define HCP_DEC_OCC(DD, GG)                                                                      \
   if (D == DD && G == GG && prepare_attn<DD, GG>() == cudaSuccess)                                 \
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, decode_attn_kernel<DD, GG>, 128, DecChunk<DD>::SMEM);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, decode_attn_kernel<DD, GG>, 128, DecCfg<DD>::SMEM);
   HCP_DEC_OCC(64, 1) HCP_DEC_OCC(64, 2) HCP_DEC_OCC(64, 4) HCP_DEC_OCC(64, 8)
   HCP_DEC_OCC(128, 1) HCP_DEC_OCC(128, 2) HCP_DEC_OCC(128, 4) HCP_DEC_OCC(128, 8)
 #undef HCP_DEC_OCC
