@@ -383,7 +383,7 @@ class PyRuntime {
   void decode_attn(torch::Tensor q, int64_t layer, torch::Tensor page_tables, torch::Tensor n_tokens,
                    double scale, int64_t splits, torch::Tensor part_o, torch::Tensor part_lse,
                    torch::Tensor counters, c10::optional<torch::Tensor> epoch_src,
-                   int64_t epoch_mul, int64_t epoch_add) {
+                   int64_t epoch_mul, int64_t epoch_add, c10::optional<torch::Tensor> final_out) {
     check_cuda_bf16(q, "q");
     const c10::cuda::CUDAGuard g(q.device());
     const auto& c = rt_.config();
@@ -420,7 +420,61 @@ class PyRuntime {
     a.epoch_mul = uint64_t(epoch_mul);
     a.epoch_add = uint64_t(epoch_add);
     a.status = rt_.status();
+    if (final_out.has_value() && final_out->defined()) {
+      check_cuda_bf16(*final_out, "final_out");
+      TORCH_CHECK(c.world == 1, "final_out: the exchange is skipped only on a single rank");
+      TORCH_CHECK(final_out->numel() >= int64_t(a.B) * a.H * a.D, "final_out too small");
+      a.final_out = reinterpret_cast<__nv_bfloat16*>(final_out->data_ptr());
+    }
     HCP_CHECK_OK(hcp::dec::decode_attn(a, cur_stream()));
+  }
+
+  // Decode QKV projection with the RoPE + KV-append epilogue (replaces gemv f32 + qkv_decode).
+  void qkv_gemv_rope(torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> bias,
+                     c10::optional<torch::Tensor> norm_w, double eps, torch::Tensor pos,
+                     torch::Tensor cos_t, torch::Tensor sin_t, int64_t layer,
+                     torch::Tensor page_tables, torch::Tensor owner, torch::Tensor slot,
+                     torch::Tensor q_out) {
+    check_cuda_bf16(x, "x");
+    check_cuda_bf16(w, "w");
+    check_cuda_bf16(q_out, "q_out");
+    TORCH_CHECK(owner.scalar_type() == torch::kInt32 && slot.scalar_type() == torch::kInt32, "owner/slot int32");
+    TORCH_CHECK(owner.dim() == 2 && owner.is_contiguous() && slot.sizes() == owner.sizes(), "owner/slot [B, layers]");
+    const c10::cuda::CUDAGuard g(x.device());
+    const auto& c = rt_.config();
+    hcp::dec::GemvArgs a{};
+    a.x = reinterpret_cast<const __nv_bfloat16*>(x.data_ptr());
+    a.ldx = x.stride(0);
+    a.W = reinterpret_cast<const __nv_bfloat16*>(w.data_ptr());
+    a.B = int(x.size(0));
+    a.N = int(w.size(0));
+    a.K = int(w.size(1));
+    TORCH_CHECK(x.size(1) == a.K, "qkv_gemv_rope K mismatch");
+    a.epi = hcp::dec::kGemvQkvRope;
+    a.bias = ptr_or_null<const __nv_bfloat16>(bias);
+    a.num_sms = sm_count(x.get_device());
+    a.norm_w = ptr_or_null<const __nv_bfloat16>(norm_w);
+    a.eps = float(eps);
+    auto& r = a.rope;
+    r.pos = pos.data_ptr<int>();
+    r.cos_t = cos_t.data_ptr<float>();
+    r.sin_t = sin_t.data_ptr<float>();
+    r.max_pos = int(cos_t.size(0));
+    r.H = int(q_out.size(1));
+    r.Hkv = c.geom.hkv;
+    r.D = c.geom.d;
+    r.q_out = reinterpret_cast<__nv_bfloat16*>(q_out.data_ptr());
+    r.arena = static_cast<__nv_bfloat16*>(rt_.arena());
+    r.geom = c.geom;
+    r.layer = int(layer);
+    r.page_tables = page_tables.data_ptr<int>();
+    r.pt_stride = int(page_tables.stride(0));
+    r.slot_cap = int(page_tables.size(1)) * c.geom.page;
+    r.owner = owner.data_ptr<int>();
+    r.slot = slot.data_ptr<int>();
+    r.owner_stride = int(owner.size(1));
+    r.status = rt_.status();
+    HCP_CHECK_OK(hcp::dec::gemv(a, cur_stream()));
   }
 
   void decode_combine(torch::Tensor out, int64_t B, int64_t H, c10::optional<torch::Tensor> epoch_src,
@@ -540,7 +594,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
            py::arg("kv_start_tile"), py::arg("scale"), py::arg("causal"), py::arg("q_out"),
            py::arg("o_out"), py::arg("lse_out"), py::arg("epoch"), py::arg("existing_slot_pos") = py::none())
       .def("qkv_decode", &PyRuntime::qkv_decode)
-      .def("decode_attn", &PyRuntime::decode_attn)
+      .def("decode_attn", &PyRuntime::decode_attn, py::arg("q"), py::arg("layer"), py::arg("page_tables"),
+           py::arg("n_tokens"), py::arg("scale"), py::arg("splits"), py::arg("part_o"),
+           py::arg("part_lse"), py::arg("counters"), py::arg("epoch_src"), py::arg("epoch_mul"),
+           py::arg("epoch_add"), py::arg("final_out") = py::none())
+      .def("qkv_gemv_rope", &PyRuntime::qkv_gemv_rope)
       .def("decode_combine", &PyRuntime::decode_combine)
       .def("wait_flags", &PyRuntime::wait_flags)
       .def("arena", &PyRuntime::arena)

@@ -68,11 +68,13 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(GemvArgs a) {
   extern __shared__ uint4 xs[];                     // [B][K/8] (normalised when NORM)
   __shared__ float red[GEMV_THREADS / 32][B];
   __shared__ float rstd[B];
-  constexpr int NWR = (EPI == kGemvSwiGLU) ? 2 : 1;  // weight rows per output row
-  constexpr int KC = 8 / NWR;                        // 16-byte columns per lane per chunk and row
+  constexpr bool PAIRED = (EPI == kGemvSwiGLU) || (EPI == kGemvQkvRope);
+  constexpr int NWR = PAIRED ? 2 : 1;  // weight rows per output item (gate/up, rotation pair)
+  constexpr int KC = 8 / NWR;          // 16-byte columns per lane per chunk and row
   const int tid = threadIdx.x, lane = tid % 32, warp = tid / 32;
   const int kvec = a.K / 8;
-  const int out_rows = (EPI == kGemvSwiGLU) ? a.N / 2 : a.N;
+  const int out_rows = PAIRED ? a.N / 2 : a.N;
+  const int half = (EPI == kGemvQkvRope) ? a.rope.D / 2 : 128;  // offset of the item's second row
   const int nchunk = (kvec + 32 * KC - 1) / (32 * KC);
   const int gw = blockIdx.x * (GEMV_THREADS / 32) + warp;
   const int nwarps = gridDim.x * (GEMV_THREADS / 32);
@@ -81,10 +83,10 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(GemvArgs a) {
   auto load = [&](int item, uint4 (&buf)[NWR][KC]) {
     const int o = gw + (item / nchunk) * nwarps;
     const int c = item % nchunk;
-    const int w0 = (EPI == kGemvSwiGLU) ? (o / 128) * 256 + (o % 128) : o;
+    const int w0 = PAIRED ? (o / half) * 2 * half + (o % half) : o;
 #pragma unroll
     for (int q = 0; q < NWR; ++q) {
-      const uint4* wp = reinterpret_cast<const uint4*>(a.W + (long)(w0 + q * 128) * a.K);
+      const uint4* wp = reinterpret_cast<const uint4*>(a.W + (long)(w0 + q * half) * a.K);
 #pragma unroll
       for (int j = 0; j < KC; ++j) {
         const int k = c * 32 * KC + j * 32 + lane;
@@ -194,6 +196,46 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(GemvArgs a) {
         a.y_bf16[(long)b * a.ldy + o] = __float2bfloat16(sg * uu);
       } else if (EPI == kGemvArgmax) {
         if (a.y_f32) a.y_f32[(long)b * a.ldy + o] = v;
+      } else if (EPI == kGemvQkvRope) {
+        const GemvRopeArgs& rp = a.rope;
+        const int r0 = (o / half) * 2 * half + (o % half);  // row j of head hh; its pair is j + half
+        const int hh = r0 / rp.D, j = r0 % rp.D;
+        float y1 = v, y2 = acc[1][b];
+        if (a.bias) {
+          y1 += __bfloat162float(a.bias[r0]);
+          y2 += __bfloat162float(a.bias[r0 + half]);
+        }
+        // the bf16 linear output, then the rotation
+        y1 = __bfloat162float(__float2bfloat16(y1));
+        y2 = __bfloat162float(__float2bfloat16(y2));
+        const int pos = rp.pos[b];
+        float o1 = y1, o2 = y2;
+        if (hh < rp.H + rp.Hkv) {
+          if (pos >= 0 && pos < rp.max_pos) {
+            const float c = rp.cos_t[(long)pos * half + j], sn = rp.sin_t[(long)pos * half + j];
+            o1 = y1 * c - y2 * sn;
+            o2 = y2 * c + y1 * sn;
+          } else if (j == 0 && hh == 0) {
+            report_error(rp.status, int(StatusCode::kOutOfBounds), 332, pos, b);
+          }
+        }
+        if (hh < rp.H) {
+          __nv_bfloat16* dst = rp.q_out + ((long)b * rp.H + hh) * rp.D;
+          dst[j] = __float2bfloat16(o1);
+          dst[j + half] = __float2bfloat16(o2);
+        } else if (rp.owner[b * rp.owner_stride + rp.layer]) {
+          const int slot = rp.slot[b * rp.owner_stride + rp.layer];
+          if (slot >= 0 && slot < rp.slot_cap) {
+            const int page = rp.page_tables[(long)b * rp.pt_stride + slot / rp.geom.page];
+            const int kv = hh < rp.H + rp.Hkv ? 0 : 1;
+            const int kh = hh - rp.H - kv * rp.Hkv;
+            __nv_bfloat16* dst = rp.arena + rp.geom.offset(rp.layer, page, kv, kh, slot % rp.geom.page);
+            dst[j] = __float2bfloat16(o1);
+            dst[j + half] = __float2bfloat16(o2);
+          } else if (j == 0) {
+            report_error(rp.status, int(StatusCode::kOutOfBounds), 331, slot, b);
+          }
+        }
       }
     }
   };
@@ -223,7 +265,7 @@ static cudaError_t gemv_launch(const GemvArgs& a, cudaStream_t s) {
     int occ = 0;
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kernel, GEMV_THREADS, smem) != cudaSuccess || occ < 1)
       occ = 1;
-    const int out_rows = (EPI == kGemvSwiGLU) ? a.N / 2 : a.N;
+    const int out_rows = (EPI == kGemvSwiGLU || EPI == kGemvQkvRope) ? a.N / 2 : a.N;
     const int need = (out_rows + GEMV_THREADS / 32 - 1) / (GEMV_THREADS / 32);
     const int grid = need < occ * a.num_sms ? need : occ * a.num_sms;
     kernel<<<grid, GEMV_THREADS, smem, s>>>(a);
@@ -247,6 +289,9 @@ const char* gemv(const GemvArgs& a, cudaStream_t s) {
   if (a.K % 8 || a.ldx % 8) return "gemv: K and ldx must be multiples of 8";
   if (a.B != 1 && a.B != 2 && a.B != 4 && a.B != 8) return "gemv: B must be 1, 2, 4 or 8";
   if (a.epi == kGemvSwiGLU && a.N % 256) return "gemv: SwiGLU needs N % 256 == 0";
+  if (a.epi == kGemvQkvRope &&
+      (a.rope.q_out == nullptr || a.rope.D % 2 || a.N != (a.rope.H + 2 * a.rope.Hkv) * a.rope.D))
+    return "gemv: QKV rope epilogue needs q_out and N = (H + 2 Hkv) D";
   if ((reinterpret_cast<uintptr_t>(a.W) | reinterpret_cast<uintptr_t>(a.x)) & 15)
     return "gemv: W/x must be 16-byte aligned";
   if (size_t(a.B) * a.K * 2 > 200 * 1024) return "gemv: needs B*K*2 <= 200 KB (x is staged in shared memory)";
@@ -256,6 +301,7 @@ const char* gemv(const GemvArgs& a, cudaStream_t s) {
     case kGemvResidual: e = gemv_dispatch<kGemvResidual>(a, s); break;
     case kGemvSwiGLU: e = gemv_dispatch<kGemvSwiGLU>(a, s); break;
     case kGemvArgmax: e = gemv_dispatch<kGemvArgmax>(a, s); break;
+    case kGemvQkvRope: e = gemv_dispatch<kGemvQkvRope>(a, s); break;
     default: return "gemv: unknown epilogue";
   }
   return e == cudaSuccess ? nullptr : cudaGetErrorString(e);
@@ -580,6 +626,11 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(const __grid_constant_
       for (; s < a.splits; ++s) o0 = fmaf(s_w[g][s], __ldcg(pof + (long)s * D), o0);
       val = ((o0 + o1) + (o2 + o3)) / s_ws[g];
     }
+    if (a.final_out != nullptr) {
+      // single rank: this is the layer's attention output
+      if (d < D) a.final_out[((long)b * H + h * G + g) * D + d] = __float2bfloat16(val);
+      continue;
+    }
     // exchange slot layout: [2 parity][N src][B][H][D+1] fp32
     const long off = (((long)parity * a.n_ranks + a.my_rank) * a.B * H + (long)b * H + h * G + g) * (D + 1) + d;
     for (int r = 0; r < a.n_ranks; ++r) a.xslot_ptrs[r][off] = val;
@@ -655,6 +706,7 @@ const char* decode_attn(const DecodeAttnArgs& a, cudaStream_t s) {
   const int G = a.H / a.Hkv;
   if (a.H % a.Hkv) return "decode_attn: H % Hkv";
   if (a.n_ranks < 1 || a.n_ranks > kMaxRanks) return "decode_attn: bad n_ranks";
+  if (a.final_out != nullptr && a.n_ranks != 1) return "decode_attn: final_out is for a single rank";
   if (a.splits < 1 || a.splits > kMaxDecodeSplits) return "decode_attn: splits must be in [1, 128]";
   if ((a.D != 64 && a.D != 128) || a.geom.page % kDecCT)
     return "decode_attn: head_dim must be 64 or 128 and the page a multiple of 16 rows";

@@ -14,6 +14,30 @@ enum GemvEpilogue : int {
   kGemvResidual = 1,  // y_bf16 += bf16(x W^T)     (in place)
   kGemvSwiGLU = 2,    // y_bf16[:, j] = silu(g_j) * u_j, W rows interleaved [128 gate | 128 up]
   kGemvArgmax = 3,    // optional y_f32 logits + packed argmax per row into `argmax`
+  kGemvQkvRope = 4,   // QKV projection + bias + RoPE, q -> rope.q_out, k/v appended (GemvRopeArgs)
+};
+
+// kGemvQkvRope epilogue: the projection rows of a head are computed in rotation pairs (j, j + D/2),
+// rounded to bf16 (the bf16 linear output), rotated at pos[b] (q and k heads); q goes to q_out
+// [B, H, D], k and v to the arena slot slot[b, layer] when this rank stores the row
+// (owner[b, layer] != 0).
+struct GemvRopeArgs {
+  const int* pos;
+  const float* cos_t;
+  const float* sin_t;
+  int max_pos;
+  int H, Hkv, D;
+  __nv_bfloat16* q_out;
+  __nv_bfloat16* arena;
+  ArenaGeom geom;
+  int layer;
+  const int* page_tables;  // [B, pt_stride]
+  int pt_stride;
+  int slot_cap;
+  const int* owner;        // [B, owner_stride]
+  const int* slot;
+  int owner_stride;
+  int* status;
 };
 
 struct GemvArgs {
@@ -30,6 +54,7 @@ struct GemvArgs {
   int num_sms;
   const __nv_bfloat16* norm_w; // optional fused input RMSNorm weight [K]
   float eps;
+  GemvRopeArgs rope;           // kGemvQkvRope only
 };
 
 struct DecodeAttnArgs {
@@ -52,6 +77,7 @@ struct DecodeAttnArgs {
   int n_ranks;
   int my_rank;
   unsigned long long* const* ready_ptrs;  // device array [n_ranks]: &dec_ready[my_rank] on rank r
+  __nv_bfloat16* final_out;    // single rank: the last CTA writes O [B, H*D] here (no exchange)
   const unsigned long long* epoch_parity_src;  // device step counter (may be null)
   unsigned long long epoch_mul;  // epoch = (*src) * mul + add
   unsigned long long epoch_add;

@@ -641,7 +641,6 @@ class DecodeGraph:
         self.h_pt = torch.zeros(B, self.max_pages, dtype=torch.int32, **pin)
         self.x = torch.zeros(B, cfg.hidden_size, dtype=torch.bfloat16, device=dev)
         self.xn = torch.zeros_like(self.x)
-        self.qkv = torch.zeros(B, cfg.qkv_size, dtype=torch.float32, device=dev)
         self.q = torch.zeros(B, eng.H, eng.D, dtype=torch.bfloat16, device=dev)
         self.o = torch.zeros(B, eng.H * eng.D, dtype=torch.bfloat16, device=dev)
         self.g = torch.zeros(B, eng.w.intermediate_padded, dtype=torch.bfloat16, device=dev)
@@ -664,13 +663,19 @@ class DecodeGraph:
         launches.count()
         K.embedding(self.tokens, w.embed, out=self.x)
         eps = cfg.rms_norm_eps
+        single = e.world == 1
         for li, lw in enumerate(w.layers):
-            K.gemv(self.x, lw.wqkv, "f32", bias=lw.bqkv, y_f32=self.qkv, norm_w=lw.in_norm, eps=eps)
-            rt.qkv_decode(self.qkv, self.pos, e.cos, e.sin, li, self.pt, self.owner, self.slot, self.q)
+            # RMSNorm + QKV GEMV whose epilogue applies RoPE, writes q and appends k/v on the owner
+            rt.qkv_gemv_rope(self.x, lw.wqkv, lw.bqkv, lw.in_norm, eps, self.pos, e.cos, e.sin, li,
+                             self.pt, self.owner, self.slot, self.q)
+            # split-KV attention; on one rank its last CTA writes the layer output directly,
+            # otherwise the (O, LSE) partials go to every rank and are combined in rank order
             rt.decode_attn(self.q, li, self.pt, self.ntok[li], e.scale, self.splits, self.part_o,
-                           self.part_l, self.counters, e.dec_step, e.L, li + 1)
-            rt.decode_combine(self.o, self.B, e.H, e.dec_step, e.L, li + 1)
-            launches.count(3)
+                           self.part_l, self.counters, e.dec_step, e.L, li + 1,
+                           self.o if single else None)
+            if not single:
+                rt.decode_combine(self.o, self.B, e.H, e.dec_step, e.L, li + 1)
+            launches.count(2 if single else 3)
             K.gemv(self.o, lw.wo, "residual", y_bf16=self.x)
             K.gemv(self.x, lw.wgu, "swiglu", y_bf16=self.g, norm_w=lw.post_norm, eps=eps)
             K.gemv(self.g, lw.wd, "residual", y_bf16=self.x)

@@ -208,3 +208,39 @@ def test_fused_projection_push(dev, d, chunks, strategy):
         assert (vv.float().transpose(0, 1) - v[p]).abs().max() < 3e-2
     for rt in rts:
         rt.shutdown()
+
+
+@pytest.mark.parametrize("b,d", [(1, 64), (4, 128)])
+def test_qkv_gemv_rope_matches_two_kernel_path(dev, b, d):
+    """Decode QKV GEMV with the RoPE + KV-append epilogue against GEMV (fp32 out) + qkv_decode."""
+    from hetero_cp_ringattn_b200.ops import kernels as K
+    torch.manual_seed(13)
+    hid, layers = 512, 2
+    nq = (H + 2 * HKV) * d
+    rt = native().Runtime(0, 1, 0, layers, 8, PAGE, HKV, d, H, 1024, 8, 2000)
+    x = torch.randn(b, hid, device=dev).bfloat16()
+    w = (torch.randn(nq, hid, device=dev) / math.sqrt(hid)).bfloat16()
+    bias = (torch.randn(nq, device=dev) * 0.1).bfloat16()
+    nw = (torch.rand(hid, device=dev) + 0.5).bfloat16()
+    cos, sin = ref.rope_cos_sin(torch.arange(2048, device=dev), d, 10000.0)
+    cos, sin = cos.contiguous(), sin.contiguous()
+    pos = torch.tensor([5, 700, 1000, 33][:b], dtype=torch.int32, device=dev)
+    pt = torch.tensor([[1, 2, 3]] * b, dtype=torch.int32, device=dev)
+    owner = torch.tensor([[1, 1], [0, 1], [1, 0], [1, 1]][:b], dtype=torch.int32, device=dev)
+    slot = torch.tensor([[3, 3], [300, 301], [600, 7], [17, 18]][:b], dtype=torch.int32, device=dev)
+    layer = 1
+    qa = torch.empty(b, H, d, device=dev, dtype=torch.bfloat16)
+    rt.qkv_gemv_rope(x, w, bias, nw, 1e-5, pos, cos, sin, layer, pt, owner, slot, qa)
+    torch.cuda.synchronize()
+    arena_a = rt.arena().clone()
+    rt.arena().zero_()
+    qkv = torch.empty(b, nq, device=dev, dtype=torch.float32)
+    K.gemv(x, w, "f32", bias=bias, y_f32=qkv, norm_w=nw, eps=1e-5)
+    qb = torch.empty_like(qa)
+    rt.qkv_decode(qkv, pos, cos, sin, layer, pt, owner, slot, qb)
+    torch.cuda.synchronize()
+    rt.check()
+    assert (qa.float() - qb.float()).abs().max() < 2e-2
+    assert (arena_a.float() - rt.arena().float()).abs().max() < 2e-2
+    assert arena_a.abs().sum() > 0
+    rt.shutdown()
