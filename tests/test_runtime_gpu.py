@@ -230,6 +230,7 @@ def test_qkv_gemv_rope_matches_two_kernel_path(dev, b, d):
     slot = torch.tensor([[3, 3], [300, 301], [600, 7], [17, 18]][:b], dtype=torch.int32, device=dev)
     layer = 1
     qa = torch.empty(b, H, d, device=dev, dtype=torch.bfloat16)
+    rt.arena().zero_()
     rt.qkv_gemv_rope(x, w, bias, nw, 1e-5, pos, cos, sin, layer, pt, owner, slot, qa)
     torch.cuda.synchronize()
     arena_a = rt.arena().clone()
