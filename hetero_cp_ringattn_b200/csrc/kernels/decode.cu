@@ -308,11 +308,12 @@ const char* gemv(const GemvArgs& a, cudaStream_t s) {
 }
 
 // ----------------------------------------------------------------------------- K2 decode attention
-// grid (splits, Hkv, B), 128 threads (4 warps). Each warp owns a contiguous, chunk-aligned token
-// range of its split and streams it through a private STAGES-deep shared-memory ring: lane 0
-// issues TMA tile loads (128-byte swizzle, 16 rows x 64 head dims per box) of the chunk's K and V
-// rows straight from the paged arena (a chunk never straddles a 256-row page) and the warp waits
-// on the chunk's mbarrier (bounded).
+// grid (splits, Hkv, B), 128 threads (4 warps). A CTA streams its split's token range through a
+// STAGES-deep shared-memory ring of 64-token chunks: one thread issues TMA tile loads (128-byte
+// swizzle, 64 rows x 64 head dims per box, so each box moves 8 KB) of the chunk's K and V rows
+// straight from the paged arena (a chunk never straddles a 256-row page); every warp waits on the
+// chunk's mbarrier (bounded), works on its own 16 rows of the chunk and arrives on the stage's
+// "empty" barrier, which gates the reuse of that stage.
 //
 // The math runs on the tensor cores with warp-level m16n8k16 bf16 MMAs (the GQA group has at most
 // 8 query rows, below the 64-row minimum of tcgen05, and the loop is memory-bound, so the MMAs are
@@ -323,18 +324,18 @@ const char* gemv(const GemvArgs& a, cudaStream_t s) {
 //               q fragments use the same permutation.
 //   O += P V    A = P straight from S's accumulator fragments (packed to bf16), B = V through
 //               ldmatrix.trans (the swizzle makes the 8 row addresses conflict-free).
-// One running-max update per head and chunk; the row sums are per-lane partials reduced at the
-// end; the 4 warps are merged through shared memory and the split's (O, LSE) partial is written.
-constexpr int kDecCT = 16;  // tokens per chunk (two 8-token MMA n-tiles)
+// One running-max update per head and 16-row slice; the row sums are per-lane partials reduced at
+// the end; the 4 warps are merged through shared memory and the split's (O, LSE) partial written.
+constexpr int kDecCC = 64;   // tokens per chunk (one TMA box of rows)
+constexpr int kDecWR = 16;   // rows of a chunk per warp (two 8-token MMA n-tiles)
 
 template <int D>
 struct DecCfg {
   static constexpr int NH = D / 64;                      // 64-dim swizzled sub-tiles per row
-  static constexpr int SUB = kDecCT * 128;               // bytes of one sub-tile (16 rows x 128 B)
+  static constexpr int SUB = kDecCC * 128;               // bytes of one sub-tile (64 rows x 128 B)
   static constexpr int STAGE = 2 * NH * SUB;             // K then V sub-tiles
-  static constexpr int STAGES = (D == 64) ? 3 : 2;         // 2-3 CTAs per SM
-  static constexpr int WARP_SMEM = STAGES * STAGE;
-  static constexpr int SMEM = 1024 + 4 * WARP_SMEM;      // + alignment slack
+  static constexpr int STAGES = (D == 64) ? 3 : 2;      // 4 / 3 CTAs per SM
+  static constexpr int SMEM = 1024 + STAGES * STAGE;     // + alignment slack
 };
 
 __device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
@@ -359,44 +360,47 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(const __grid_constant_
                                                           DecodeAttnArgs a) {
   using C = DecCfg<D>;
   constexpr int NW = 4;                    // warps per CTA
-  constexpr int CT = kDecCT;
+  constexpr int CC = kDecCC;
   constexpr int DQ = D / 4;                // contiguous dims of a K row per lane in S = Q K^T
   constexpr int KS = D / 16;               // MMA k-steps over the head dim
   constexpr int NT = D / 8;                // 8-dim n-tiles of O
   static_assert(G >= 1 && G <= 8, "GQA group of at most 8 query heads");
+  static_assert(NW * kDecWR == CC, "warps x rows per warp = chunk");
   extern __shared__ uint8_t dsm_raw[];
   uint8_t* dsm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dsm_raw) + 1023) & ~uintptr_t(1023));
-  __shared__ __align__(8) uint64_t bars[NW][C::STAGES];
+  __shared__ __align__(8) uint64_t full[C::STAGES];
+  __shared__ __align__(8) uint64_t empty[C::STAGES];
   const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int lane = threadIdx.x % 32, warp = threadIdx.x / 32;
   const int g = lane / 4, t = lane % 4;    // MMA fragment row group / column pair
   const int n = a.n_tokens[b];
-  // chunk-aligned ranges: split -> 4 warp ranges -> CT-token chunks
+  // chunk-aligned split ranges
   int per = (n + a.splits - 1) / a.splits;
-  per = (per + NW * CT - 1) / (NW * CT) * (NW * CT);
-  const int s0 = split * per;
+  per = (per + CC - 1) / CC * CC;
+  const int s0 = min(n, split * per);
   const int s1 = min(n, s0 + per);
-  const int w0 = min(s1, s0 + warp * (per / NW));
-  const int w1 = min(s1, w0 + per / NW);
-  const int nc = (w1 - w0 + CT - 1) / CT;
+  const int nc = (s1 - s0 + CC - 1) / CC;
   const int H = a.Hkv * G;
-  uint8_t* wsm = dsm + warp * C::WARP_SMEM;  // [stage][K sub-tiles | V sub-tiles]
 
-  if (lane == 0)
-    for (int st = 0; st < C::STAGES; ++st) mbar_init(&bars[warp][st], 1);
-  fence_barrier_init();
-  __syncwarp();
+  if (threadIdx.x == 0) {
+    for (int st = 0; st < C::STAGES; ++st) {
+      mbar_init(&full[st], 1);
+      mbar_init(&empty[st], NW);
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
 
   const int* pt = a.page_tables + (long)b * a.pt_stride;
   const long rows_per_layer = (long)a.geom.pages * 2 * a.geom.hkv * a.geom.page;
   auto issue = [&](int c) {
-    const int t0 = w0 + c * CT;
+    const int t0 = s0 + c * CC;
     const int page = pt[t0 / a.geom.page];
     const long krow = (long)a.layer * rows_per_layer +
                       ((long)(page * 2 + 0) * a.geom.hkv + h) * a.geom.page + (t0 % a.geom.page);
     const long vrow = krow + (long)a.geom.hkv * a.geom.page;
-    uint8_t* dst = wsm + (c % C::STAGES) * C::STAGE;
-    uint64_t* bar = &bars[warp][c % C::STAGES];
+    uint8_t* dst = dsm + (c % C::STAGES) * C::STAGE;
+    uint64_t* bar = &full[c % C::STAGES];
     mbar_arrive_expect_tx(bar, C::STAGE);
 #pragma unroll
     for (int j = 0; j < C::NH; ++j) {
@@ -404,7 +408,8 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(const __grid_constant_
       tma_load_2d(dst + (C::NH + j) * C::SUB, &tm_kv, bar, j * 64, int(vrow));
     }
   };
-  if (lane == 0) {
+  const bool producer = threadIdx.x == 0;
+  if (producer) {
     tma_prefetch_desc(&tm_kv);
     for (int c = 0; c < C::STAGES - 1 && c < nc; ++c) issue(c);
   }
@@ -441,101 +446,114 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(const __grid_constant_
 #pragma unroll
   for (int i = 0; i < NT; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
   float m = -INFINITY, l = 0.f;  // head g's running max (log2 domain) and this lane's row-sum part
-  int consumed = 0;
+  int issued = min(nc, C::STAGES - 1);
   bool ok = true;
+  const int wr0 = warp * kDecWR;           // this warp's rows inside a chunk
   for (int c = 0; c < nc; ++c) {
-    if (lane == 0 && c + C::STAGES - 1 < nc) {
-      fence_proxy_async_smem();  // the warp's reads of that stage (chunk c - 1) come first
-      issue(c + C::STAGES - 1);
+    if (producer && c + C::STAGES - 1 < nc) {
+      // stage (c - 1) % STAGES is reused once every warp has released chunk c - 1
+      const int k = c + C::STAGES - 1;
+      if (k >= C::STAGES && !mbar_wait(&empty[k % C::STAGES], ((k / C::STAGES) - 1) & 1, a.status, 303)) {
+        ok = false;
+      } else {
+        fence_proxy_async_smem();
+        issue(k);
+        issued = k + 1;
+      }
     }
-    ok = __all_sync(0xffffffffu, mbar_wait(&bars[warp][c % C::STAGES], (c / C::STAGES) & 1, a.status, 301));
+    ok = __all_sync(0xffffffffu, ok && mbar_wait(&full[c % C::STAGES], (c / C::STAGES) & 1, a.status, 301));
     if (!ok) break;
-    consumed = c + 1;
-    uint8_t* sk = wsm + (c % C::STAGES) * C::STAGE;
+    uint8_t* sk = dsm + (c % C::STAGES) * C::STAGE;
     uint8_t* sv = sk + C::NH * C::SUB;
-    const int t0 = w0 + c * CT;
-    const int valid = min(CT, w1 - t0);
-    if (valid < CT) {
+    const int t0 = s0 + c * CC + wr0;      // first token of this warp's 16 rows
+    const int valid = max(0, min(kDecWR, s1 - t0));
+    if (valid < kDecWR) {
       // rows past the range hold whatever the page had: zero V there (p is 0 for them, and
       // 0 * a non-finite value would not be)
-      for (int i = lane; i < (CT - valid) * C::NH * 8; i += 32) {
-        const int r = valid + i / (C::NH * 8), rem = i % (C::NH * 8);
+      for (int i = lane; i < (kDecWR - valid) * C::NH * 8; i += 32) {
+        const int r = wr0 + valid + i / (C::NH * 8), rem = i % (C::NH * 8);
         *reinterpret_cast<uint4*>(sv + (rem / 8) * C::SUB + r * 128 + (rem % 8) * 16) = make_uint4(0u, 0u, 0u, 0u);
       }
       __syncwarp();
     }
-    // S = Q K^T for the two 8-token n-tiles
-    float s[2][4];
+    if (valid > 0) {
+      // S = Q K^T for the two 8-token n-tiles
+      float s[2][4];
 #pragma unroll
-    for (int nt = 0; nt < 2; ++nt) {
-      s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
-      const int r = nt * 8 + g;
-      uint32_t kw[DQ / 2];
+      for (int nt = 0; nt < 2; ++nt) {
+        s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
+        const int r = wr0 + nt * 8 + g;
+        uint32_t kw[DQ / 2];
 #pragma unroll
-      for (int v = 0; v < DQ / 8; ++v) {
-        const int dim = t * DQ + v * 8;
-        const uint4 w = *reinterpret_cast<const uint4*>(sk + (dim / 64) * C::SUB + swz(r, (dim % 64) / 8));
-        kw[4 * v] = w.x;
-        kw[4 * v + 1] = w.y;
-        kw[4 * v + 2] = w.z;
-        kw[4 * v + 3] = w.w;
+        for (int v = 0; v < DQ / 8; ++v) {
+          const int dim = t * DQ + v * 8;
+          const uint4 w = *reinterpret_cast<const uint4*>(sk + (dim / 64) * C::SUB + swz(r, (dim % 64) / 8));
+          kw[4 * v] = w.x;
+          kw[4 * v + 1] = w.y;
+          kw[4 * v + 2] = w.z;
+          kw[4 * v + 3] = w.w;
+        }
+#pragma unroll
+        for (int ks = 0; ks < KS; ++ks) {
+          const uint32_t af[4] = {qa[ks][0], 0u, qa[ks][1], 0u};
+          mma16816(s[nt], af, kw[2 * ks], kw[2 * ks + 1]);
+        }
       }
+      // head g's scores: tokens 2t, 2t + 1 (n-tile 0) and 8 + 2t, 9 + 2t (n-tile 1)
+      float sc[4] = {s[0][0], s[0][1], s[1][0], s[1][1]};
 #pragma unroll
-      for (int ks = 0; ks < KS; ++ks) {
-        const uint32_t af[4] = {qa[ks][0], 0u, qa[ks][1], 0u};
-        mma16816(s[nt], af, kw[2 * ks], kw[2 * ks + 1]);
+      for (int e = 0; e < 4; ++e) {
+        const int tok = (e >> 1) * 8 + 2 * t + (e & 1);
+        if (tok >= valid) sc[e] = -INFINITY;
       }
-    }
-    // head g's scores: tokens 2t, 2t + 1 (n-tile 0) and 8 + 2t, 9 + 2t (n-tile 1)
-    float sc[4] = {s[0][0], s[0][1], s[1][0], s[1][1]};
+      float cm = fmaxf(fmaxf(sc[0], sc[1]), fmaxf(sc[2], sc[3]));
+      cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 1));
+      cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 2));
+      if (cm > m) {
+        const float al = fast_exp2(m - cm);  // 0 while nothing has been accumulated
+        m = cm;
+        l *= al;
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const int tok = (e >> 1) * 8 + 2 * t + (e & 1);
-      if (tok >= valid) sc[e] = -INFINITY;
-    }
-    float cm = fmaxf(fmaxf(sc[0], sc[1]), fmaxf(sc[2], sc[3]));
-    cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 1));
-    cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 2));
-    if (cm > m) {
-      const float al = fast_exp2(m - cm);  // 0 while nothing has been accumulated
-      m = cm;
-      l *= al;
-#pragma unroll
-      for (int i = 0; i < NT; ++i) {
-        acc[i][0] *= al;
-        acc[i][1] *= al;
+        for (int i = 0; i < NT; ++i) {
+          acc[i][0] *= al;
+          acc[i][1] *= al;
+        }
       }
-    }
-    float pe[4];
+      float pe[4];
 #pragma unroll
-    for (int e = 0; e < 4; ++e) pe[e] = (m == -INFINITY) ? 0.f : fast_exp2(sc[e] - m);
-    l += (pe[0] + pe[1]) + (pe[2] + pe[3]);
-    const uint32_t pa[4] = {pack_bf16x2(pe[0], pe[1]), 0u, pack_bf16x2(pe[2], pe[3]), 0u};
-    // O += P V: ldmatrix.trans gives the V fragments of two 8-dim n-tiles per call
-    const int lr = (lane & 7) + ((lane >> 3) & 1) * 8;  // token row this lane addresses
-    const int lc = lane >> 4;                            // +0 / +1 chunk (second n-tile)
+      for (int e = 0; e < 4; ++e) pe[e] = (m == -INFINITY) ? 0.f : fast_exp2(sc[e] - m);
+      l += (pe[0] + pe[1]) + (pe[2] + pe[3]);
+      const uint32_t pa[4] = {pack_bf16x2(pe[0], pe[1]), 0u, pack_bf16x2(pe[2], pe[3]), 0u};
+      // O += P V: ldmatrix.trans gives the V fragments of two 8-dim n-tiles per call
+      const int lr = wr0 + (lane & 7) + ((lane >> 3) & 1) * 8;  // token row this lane addresses
+      const int lc = lane >> 4;                                  // +0 / +1 chunk (second n-tile)
 #pragma unroll
-    for (int j = 0; j < NT / 2; ++j) {
-      const int dim = j * 16;
-      uint32_t vb[4];
-      ldsm_x4_trans(vb, smem_u32(sv + (dim / 64) * C::SUB + swz(lr, (dim % 64) / 8 + lc)));
-      mma16816(acc[2 * j], pa, vb[0], vb[1]);
-      mma16816(acc[2 * j + 1], pa, vb[2], vb[3]);
+      for (int j = 0; j < NT / 2; ++j) {
+        const int dim = j * 16;
+        uint32_t vb[4];
+        ldsm_x4_trans(vb, smem_u32(sv + (dim / 64) * C::SUB + swz(lr, (dim % 64) / 8 + lc)));
+        mma16816(acc[2 * j], pa, vb[0], vb[1]);
+        mma16816(acc[2 * j + 1], pa, vb[2], vb[3]);
+      }
     }
     __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[c % C::STAGES]);
   }
-  if (!ok && lane == 0) {
+  if (!ok && producer) {
     // a wait gave up: let the copies still in flight land (bounded) before the CTA exits
-    for (int c = consumed; c < nc && c < consumed + C::STAGES; ++c)
-      mbar_wait(&bars[warp][c % C::STAGES], (c / C::STAGES) & 1, a.status, 302);
+    for (int c = 0; c < issued; ++c)
+      mbar_wait(&full[c % C::STAGES], (c / C::STAGES) & 1, a.status, 302);
   }
   // the 4 lanes of a row group hold parts of head g's row sum
   l += __shfl_xor_sync(0xffffffffu, l, 1);
   l += __shfl_xor_sync(0xffffffffu, l, 2);
-  // merge the 4 warps through shared memory
-  __shared__ float sm_m[NW][8];
-  __shared__ float sm_l[NW][8];
-  __shared__ float sm_acc[NW][8][D];
+  // merge the 4 warps through shared memory, reusing the ring (every warp is past its last read
+  // of it and every issued copy has landed: each was waited on)
+  static_assert(NW * 8 * (D + 2) * 4 <= C::STAGES * C::STAGE, "merge buffers fit in the ring");
+  __syncthreads();
+  float (*sm_acc)[8][D] = reinterpret_cast<float (*)[8][D]>(dsm);
+  float (*sm_m)[8] = reinterpret_cast<float (*)[8]>(dsm + NW * 8 * D * 4);
+  float (*sm_l)[8] = reinterpret_cast<float (*)[8]>(dsm + NW * 8 * D * 4 + NW * 8 * 4);
   if (t == 0) {
     sm_m[warp][g] = m;
     sm_l[warp][g] = l;
@@ -708,16 +726,16 @@ const char* decode_attn(const DecodeAttnArgs& a, cudaStream_t s) {
   if (a.n_ranks < 1 || a.n_ranks > kMaxRanks) return "decode_attn: bad n_ranks";
   if (a.final_out != nullptr && a.n_ranks != 1) return "decode_attn: final_out is for a single rank";
   if (a.splits < 1 || a.splits > kMaxDecodeSplits) return "decode_attn: splits must be in [1, 128]";
-  if ((a.D != 64 && a.D != 128) || a.geom.page % kDecCT)
-    return "decode_attn: head_dim must be 64 or 128 and the page a multiple of 16 rows";
+  if ((a.D != 64 && a.D != 128) || a.geom.page % kDecCC)
+    return "decode_attn: head_dim must be 64 or 128 and the page a multiple of 64 rows";
   if (G > 8) return "decode_attn: at most 8 query heads per KV head";
   if (reinterpret_cast<uintptr_t>(a.arena) & 15) return "decode_attn: arena must be 16-byte aligned";
-  // the whole arena as one [rows, D] bf16 matrix; boxes of 16 rows x 64 dims, 128-byte swizzle
+  // the whole arena as one [rows, D] bf16 matrix; boxes of 64 rows x 64 dims, 128-byte swizzle
   const unsigned long long rows =
       (unsigned long long)a.geom.layers * a.geom.pages * 2 * a.geom.hkv * a.geom.page;
   if (rows >= (1ull << 31)) return "decode_attn: arena has too many rows for 32-bit TMA coordinates";
   CUtensorMap tm;
-  if (!gemm::make_tma_2d_bf16(&tm, a.arena, uint64_t(a.D), rows, uint64_t(a.D) * 2, 64, kDecCT))
+  if (!gemm::make_tma_2d_bf16(&tm, a.arena, uint64_t(a.D), rows, uint64_t(a.D) * 2, 64, kDecCC))
     return "decode_attn: TMA descriptor for the arena failed";
   cudaError_t e = cudaErrorInvalidValue;
 #define HCP_DEC_CASE(DD, GG) \
