@@ -118,6 +118,14 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
+// ------------------------------------------------------------------------------- dependent launch
+// Programmatic dependent launch: a kernel launched with the programmatic-serialization attribute
+// may start while its predecessor is still running. pdl_wait() blocks until the predecessor has
+// completed and its memory is visible (a no-op without the attribute); anything before it may
+// only touch data no kernel in flight writes (weights). pdl_trigger() lets the successor launch.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ------------------------------------------------------------------------------- bulk copies
 // Untiled bulk copy global -> this CTA's shared memory; completes on `bar` as a transaction
 // count. Both addresses 16-byte aligned, `bytes` a multiple of 16.

@@ -20,6 +20,7 @@
 #include "decode.h"
 #include "gemm_sm100.h"
 #include "kv_layout.h"
+#include "launch.h"
 
 namespace hcp {
 namespace dec {
@@ -95,7 +96,9 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(GemvArgs a) {
     }
   };
   uint4 bufA[NWR][KC], bufB[NWR][KC];
-  if (items > 0) load(0, bufA);
+  pdl_trigger();
+  if (items > 0) load(0, bufA);  // weights: nothing in flight writes them
+  pdl_wait();                    // x, residual rows, positions, ... come from predecessors
   if (NORM) {
     float ss[B];
 #pragma unroll
@@ -258,6 +261,13 @@ template <int EPI, bool NORM>
 static cudaError_t gemv_launch(const GemvArgs& a, cudaStream_t s) {
   const size_t smem = size_t(a.B) * a.K * 2;
   auto go = [&](auto kernel) -> cudaError_t {
+    static bool carveout = false;
+    if (!carveout) {
+      // the whole decode chain runs with the maximum shared-memory carveout, so consecutive
+      // (overlapping) kernels never need the SM's L1 / shared split reconfigured
+      cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
+      carveout = true;
+    }
     if (smem > 48 * 1024) {
       cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
       if (e != cudaSuccess) return e;
@@ -268,8 +278,7 @@ static cudaError_t gemv_launch(const GemvArgs& a, cudaStream_t s) {
     const int out_rows = (EPI == kGemvSwiGLU || EPI == kGemvQkvRope) ? a.N / 2 : a.N;
     const int need = (out_rows + GEMV_THREADS / 32 - 1) / (GEMV_THREADS / 32);
     const int grid = need < occ * a.num_sms ? need : occ * a.num_sms;
-    kernel<<<grid, GEMV_THREADS, smem, s>>>(a);
-    return cudaGetLastError();
+    return launch_pdl(kernel, dim3(grid), dim3(GEMV_THREADS), smem, s, a);
   };
   switch (a.B) {
     case 1: return go(gemv_kernel<EPI, 1, NORM>);
@@ -359,6 +368,8 @@ template <int D, int G>
 __global__ void __launch_bounds__(128) decode_attn_kernel(const __grid_constant__ CUtensorMap tm_kv,
                                                           DecodeAttnArgs a) {
   using C = DecCfg<D>;
+  pdl_trigger();
+  pdl_wait();
   constexpr int NW = 4;                    // warps per CTA
   constexpr int CC = kDecCC;
   constexpr int DQ = D / 4;                // contiguous dims of a K row per lane in S = Q K^T
@@ -632,17 +643,19 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(const __grid_constant_
     } else if (d == D) {
       val = s_mx[g] + __log2f(s_ws[g]);
     } else {
+      // 16 independent L2 loads in flight per round (this tail runs after every split of the
+      // group is done, so its latency adds to the kernel's)
       const float* pof = a.part_o + (long)(b * H + h * G + g) * a.splits * D + d;
-      float o0 = 0.f, o1 = 0.f, o2 = 0.f, o3 = 0.f;
-      int s = 0;
-      for (; s + 4 <= a.splits; s += 4) {
-        o0 = fmaf(s_w[g][s], __ldcg(pof + (long)s * D), o0);
-        o1 = fmaf(s_w[g][s + 1], __ldcg(pof + (long)(s + 1) * D), o1);
-        o2 = fmaf(s_w[g][s + 2], __ldcg(pof + (long)(s + 2) * D), o2);
-        o3 = fmaf(s_w[g][s + 3], __ldcg(pof + (long)(s + 3) * D), o3);
+      float o = 0.f;
+      for (int s0 = 0; s0 < a.splits; s0 += 16) {
+        float v[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) v[j] = (s0 + j < a.splits) ? __ldcg(pof + (long)(s0 + j) * D) : 0.f;
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+          if (s0 + j < a.splits) o = fmaf(s_w[g][s0 + j], v[j], o);
       }
-      for (; s < a.splits; ++s) o0 = fmaf(s_w[g][s], __ldcg(pof + (long)s * D), o0);
-      val = ((o0 + o1) + (o2 + o3)) / s_ws[g];
+      val = o / s_ws[g];
     }
     if (a.final_out != nullptr) {
       // single rank: this is the layer's attention output
@@ -654,6 +667,7 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(const __grid_constant_
     for (int r = 0; r < a.n_ranks; ++r) a.xslot_ptrs[r][off] = val;
   }
   if (threadIdx.x == 0) a.split_counter[b * a.Hkv + h] = 0;
+  if (a.final_out != nullptr) return;  // single rank: nothing to signal
   // grid-wide last CTA signals every rank that this rank's partial has landed
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -670,6 +684,8 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(const __grid_constant_
 // grid (B, H), block D: wait for every rank's partial (bounded), then LSE-combine in rank
 // order (the same order on every rank, so every rank produces bit-identical outputs).
 __global__ void decode_combine_kernel(DecodeCombineArgs a) {
+  pdl_trigger();
+  pdl_wait();
   const int b = blockIdx.x, hh = blockIdx.y, d = threadIdx.x;
   const unsigned long long e = a.epoch_src ? (*a.epoch_src * a.epoch_mul + a.epoch_add) : a.epoch_add;
   const int parity = int(e & 1ull);
@@ -707,6 +723,9 @@ static cudaError_t prepare_attn() {
   if (done) return cudaSuccess;
   cudaError_t e = cudaFuncSetAttribute(decode_attn_kernel<D, G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        DecCfg<D>::SMEM);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(decode_attn_kernel<D, G>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                             cudaSharedmemCarveoutMaxShared);
   done = (e == cudaSuccess);
   return e;
 }
@@ -716,8 +735,7 @@ static cudaError_t launch_attn(const CUtensorMap& tm, const DecodeAttnArgs& a, c
   cudaError_t e = prepare_attn<D, G>();
   if (e != cudaSuccess) return e;
   dim3 grid(a.splits, a.Hkv, a.B);
-  decode_attn_kernel<D, G><<<grid, 128, DecCfg<D>::SMEM, s>>>(tm, a);
-  return cudaGetLastError();
+  return launch_pdl(decode_attn_kernel<D, G>, grid, dim3(128), size_t(DecCfg<D>::SMEM), s, tm, a);
 }
 
 const char* decode_attn(const DecodeAttnArgs& a, cudaStream_t s) {
@@ -760,18 +778,23 @@ int decode_attn_ctas_per_sm(int D, int G) {
 
 const char* decode_combine(const DecodeCombineArgs& a, cudaStream_t s) {
   if (a.n_ranks > a.D) return "decode_combine: more ranks than head_dim threads";
-  decode_combine_kernel<<<dim3(a.B, a.H), a.D, 0, s>>>(a);
-  return cudaGetLastError() == cudaSuccess ? nullptr : "decode_combine: launch failed";
+  return launch_pdl(decode_combine_kernel, dim3(a.B, a.H), dim3(a.D), 0, s, a) == cudaSuccess
+             ? nullptr
+             : "decode_combine: launch failed";
 }
 
 // ----------------------------------------------------------------------------- small helpers
 __global__ void fill_u64_kernel(unsigned long long* p, int n, unsigned long long v) {
+  pdl_trigger();
+  pdl_wait();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i < n) p[i] = v;
 }
 
 __global__ void argmax_finalize_kernel(const unsigned long long* packed, int B, int* tokens_out,
                                        long long* tokens_out64) {
+  pdl_trigger();
+  pdl_wait();
   const int b = threadIdx.x;
   if (b < B) {
     const int idx = int(0xFFFFFFFFu - uint32_t(packed[b] & 0xFFFFFFFFull));
@@ -780,23 +803,24 @@ __global__ void argmax_finalize_kernel(const unsigned long long* packed, int B, 
   }
 }
 
-__global__ void add_u64_kernel(unsigned long long* p, unsigned long long v) { *p += v; }
+__global__ void add_u64_kernel(unsigned long long* p, unsigned long long v) {
+  pdl_trigger();
+  pdl_wait();
+  *p += v;
+}
 
 const char* fill_u64(unsigned long long* p, int n, unsigned long long v, cudaStream_t s) {
   if (n == 0) return nullptr;
-  fill_u64_kernel<<<(n + 255) / 256, 256, 0, s>>>(p, n, v);
-  return cudaGetLastError() == cudaSuccess ? nullptr : "fill_u64: launch failed";
+  return launch_pdl(fill_u64_kernel, dim3((n + 255) / 256), dim3(256), 0, s, p, n, v) == cudaSuccess ? nullptr : "fill_u64: launch failed";
 }
 
 const char* argmax_finalize(const unsigned long long* packed, int B, int* tok, long long* tok64,
                             cudaStream_t s) {
-  argmax_finalize_kernel<<<1, 32, 0, s>>>(packed, B, tok, tok64);
-  return cudaGetLastError() == cudaSuccess ? nullptr : "argmax_finalize: launch failed";
+  return launch_pdl(argmax_finalize_kernel, dim3(1), dim3(32), 0, s, packed, B, tok, tok64) == cudaSuccess ? nullptr : "argmax_finalize: launch failed";
 }
 
 const char* add_u64(unsigned long long* p, unsigned long long v, cudaStream_t s) {
-  add_u64_kernel<<<1, 1, 0, s>>>(p, v);
-  return cudaGetLastError() == cudaSuccess ? nullptr : "add_u64: launch failed";
+  return launch_pdl(add_u64_kernel, dim3(1), dim3(1), 0, s, p, v) == cudaSuccess ? nullptr : "add_u64: launch failed";
 }
 
 }  // namespace dec

@@ -15,6 +15,7 @@
 //     release flag per peer (last-CTA-done), instead of host-staged f32 QUIC frames.
 #include "common.cuh"
 #include "elementwise.h"
+#include "launch.h"
 #include "kv_layout.h"
 
 namespace hcp {
@@ -26,6 +27,8 @@ using namespace hcp::dev;
 __global__ void embedding_kernel(const int* __restrict__ ids, const __nv_bfloat16* __restrict__ W,
                                  __nv_bfloat16* __restrict__ out, int T, int hidden, int vocab,
                                  int* status) {
+  pdl_trigger();
+  pdl_wait();
   const int t = blockIdx.x;
   if (t >= T) return;
   int id = ids[t];
@@ -252,8 +255,7 @@ const char* embedding(const int* ids, const __nv_bfloat16* W, __nv_bfloat16* out
                       int vocab, int* status, cudaStream_t s) {
   if (hidden % 8) return "embedding: hidden must be a multiple of 8";
   if (T == 0) return nullptr;
-  embedding_kernel<<<T, 128, 0, s>>>(ids, W, out, T, hidden, vocab, status);
-  return cudaGetLastError() == cudaSuccess ? nullptr : "embedding: launch failed";
+  return launch_pdl(embedding_kernel, dim3(T), dim3(128), 0, s, ids, W, out, T, hidden, vocab, status) == cudaSuccess ? nullptr : "embedding: launch failed";
 }
 
 const char* rmsnorm(const __nv_bfloat16* x, const __nv_bfloat16* w, __nv_bfloat16* y, int T,
