@@ -635,36 +635,54 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(const __grid_constant_
     }
   }
   __syncthreads();
-  for (int i = threadIdx.x; i < G * (D + 1); i += blockDim.x) {
-    const int g = i / (D + 1), d = i % (D + 1);
-    float val;
-    if (s_mx[g] == -INFINITY) {
-      val = (d < D) ? 0.f : -INFINITY;
-    } else if (d == D) {
-      val = s_mx[g] + __log2f(s_ws[g]);
-    } else {
-      // 16 independent L2 loads in flight per round (this tail runs after every split of the
-      // group is done, so its latency adds to the kernel's)
-      const float* pof = a.part_o + (long)(b * H + h * G + g) * a.splits * D + d;
-      float o = 0.f;
+  // each thread owns 4 consecutive dims of one head; 16-byte L2 loads, 16 splits per round in
+  // flight (this tail runs after every split of the group is done, so its latency adds to the
+  // kernel's)
+  for (int c = threadIdx.x; c < G * (D / 4); c += blockDim.x) {
+    const int g = c / (D / 4), d4 = c % (D / 4);
+    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (s_mx[g] != -INFINITY) {
+      const float4* pof = reinterpret_cast<const float4*>(a.part_o + (long)(b * H + h * G + g) * a.splits * D) + d4;
       for (int s0 = 0; s0 < a.splits; s0 += 16) {
-        float v[16];
-#pragma unroll
-        for (int j = 0; j < 16; ++j) v[j] = (s0 + j < a.splits) ? __ldcg(pof + (long)(s0 + j) * D) : 0.f;
+        float4 v[16];
 #pragma unroll
         for (int j = 0; j < 16; ++j)
-          if (s0 + j < a.splits) o = fmaf(s_w[g][s0 + j], v[j], o);
+          v[j] = (s0 + j < a.splits) ? __ldcg(pof + (long)(s0 + j) * (D / 4)) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          if (s0 + j < a.splits) {
+            const float w = s_w[g][s0 + j];
+            o.x = fmaf(w, v[j].x, o.x);
+            o.y = fmaf(w, v[j].y, o.y);
+            o.z = fmaf(w, v[j].z, o.z);
+            o.w = fmaf(w, v[j].w, o.w);
+          }
+        }
       }
-      val = o / s_ws[g];
+      const float inv = 1.f / s_ws[g];
+      o = make_float4(o.x * inv, o.y * inv, o.z * inv, o.w * inv);
     }
     if (a.final_out != nullptr) {
       // single rank: this is the layer's attention output
-      if (d < D) a.final_out[((long)b * H + h * G + g) * D + d] = __float2bfloat16(val);
+      __nv_bfloat16* dst = a.final_out + ((long)b * H + h * G + g) * D + d4 * 4;
+      *reinterpret_cast<uint2*>(dst) = make_uint2(pack_bf16x2(o.x, o.y), pack_bf16x2(o.z, o.w));
       continue;
     }
     // exchange slot layout: [2 parity][N src][B][H][D+1] fp32
-    const long off = (((long)parity * a.n_ranks + a.my_rank) * a.B * H + (long)b * H + h * G + g) * (D + 1) + d;
-    for (int r = 0; r < a.n_ranks; ++r) a.xslot_ptrs[r][off] = val;
+    const long off = (((long)parity * a.n_ranks + a.my_rank) * a.B * H + (long)b * H + h * G + g) * (D + 1) + d4 * 4;
+    for (int r = 0; r < a.n_ranks; ++r) {
+      float* x = a.xslot_ptrs[r] + off;
+      x[0] = o.x;
+      x[1] = o.y;
+      x[2] = o.z;
+      x[3] = o.w;
+    }
+  }
+  if (a.final_out == nullptr && threadIdx.x < G) {
+    const int g = threadIdx.x;
+    const float lse = s_mx[g] == -INFINITY ? -INFINITY : s_mx[g] + __log2f(s_ws[g]);
+    const long off = (((long)parity * a.n_ranks + a.my_rank) * a.B * H + (long)b * H + h * G + g) * (D + 1) + D;
+    for (int r = 0; r < a.n_ranks; ++r) a.xslot_ptrs[r][off] = lse;
   }
   if (threadIdx.x == 0) a.split_counter[b * a.Hkv + h] = 0;
   if (a.final_out != nullptr) return;  // single rank: nothing to signal
