@@ -96,10 +96,40 @@ def read_logits(path: str):
     return vocab, steps, data
 
 
+def _debug_exports(args, dev, ids) -> int:
+    """--export-hidden-states / --prefill-debug: float32 oracle intermediates on the same weights."""
+    from .config import ModelConfig, preset
+    from .debug_export import export_hidden_states, prefill_debug_layer0
+    from .models.weights import ModelWeights
+    if args.model_dir:
+        cfg = ModelConfig.from_file(os.path.join(args.model_dir, "config.json"))
+        w = ModelWeights.from_dir(args.model_dir, device=dev, dtype=torch.float32, cfg=cfg)
+    else:
+        cfg = preset(args.model_preset)
+        w = ModelWeights.random_init(cfg, seed=args.seed, dtype=torch.float32, device=dev)
+    ids = ids.to(dev)
+    out = {"prompt_tokens": ids.numel()}
+    if args.prefill_debug:
+        prefill_debug_layer0(w, ids, args.prefill_debug, args.qk_inject)
+        out["prefill_debug"] = args.prefill_debug
+    if args.export_hidden_states:
+        out["first_token"] = export_hidden_states(w, ids, args.export_hidden_states)
+        out["export_hidden_states"] = args.export_hidden_states
+    print(json.dumps(out))
+    return 0
+
+
 def cmd_infer(args) -> int:
     from .models.llama import LlamaCPEngine
     from .serve.tokenizer import load_tokenizer
     dev = _device(args)
+    if args.export_hidden_states or args.prefill_debug:
+        from .config import ModelConfig, preset
+        cfg0 = (ModelConfig.from_file(os.path.join(args.model_dir, "config.json")) if args.model_dir
+                else preset(args.model_preset))
+        tok0 = load_tokenizer(args.model_dir, cfg0.vocab_size)
+        text = open(args.prompt_file).read() if args.prompt_file else (args.prompt or "hello")
+        return _debug_exports(args, dev, torch.tensor(tok0.encode(text), dtype=torch.int64))
     cfg, w = _load_model(args, dev)
     tok = load_tokenizer(args.model_dir, cfg.vocab_size)
     prompt = args.prompt
@@ -254,6 +284,12 @@ def main(argv: Optional[List[str]] = None) -> int:
     i.add_argument("--prompt-file", default=None)
     i.add_argument("--max-tokens", type=int, default=10)
     i.add_argument("--export-logits", default=None)
+    i.add_argument("--export-hidden-states", default=None, metavar="DIR",
+                   help="per-layer K/V after prefill + first decode step hidden states (f32 oracle)")
+    i.add_argument("--prefill-debug", default=None, metavar="DIR",
+                   help="layer-0 prefill intermediates + every layer's K/V (f32 oracle)")
+    i.add_argument("--qk-inject", default=None, metavar="DIR",
+                   help="with --prefill-debug: read layer 0's q/k projections from DIR")
     i.set_defaults(fn=cmd_infer)
     s = sub.add_parser("serve", aliases=["coordinator", "worker"])
     _add_model_args(s)
