@@ -717,9 +717,10 @@ class DecodeGraph:
             self.body()
         else:
             if self.graph is None:
-                # every kernel of the body writes into preallocated buffers and sets no function
-                # attributes, so the graph is captured directly (no eager warm-up step, which
-                # would advance the cross-rank exchange epochs and overwrite `tokens`)
+                # every kernel of the body writes into preallocated buffers (function attributes
+                # and TMA descriptors are host-side calls, legal during capture), so the graph is
+                # captured directly (no eager warm-up step, which would advance the cross-rank
+                # exchange epochs and overwrite `tokens`)
                 self.graph = torch.cuda.CUDAGraph()
                 with launches.capture() as cap:
                     with torch.cuda.graph(self.graph):
