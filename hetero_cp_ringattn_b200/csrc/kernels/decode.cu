@@ -303,7 +303,26 @@ const char* gemv(const GemvArgs& a, cudaStream_t s) {
     return "gemv: QKV rope epilogue needs q_out and N = (H + 2 Hkv) D";
   if ((reinterpret_cast<uintptr_t>(a.W) | reinterpret_cast<uintptr_t>(a.x)) & 15)
     return "gemv: W/x must be 16-byte aligned";
-  if (size_t(a.B) * a.K * 2 > 200 * 1024) return "gemv: needs B*K*2 <= 200 KB (x is staged in shared memory)";
+  if (size_t(a.K) * 2 > 200 * 1024) return "gemv: needs K*2 <= 200 KB (x is staged in shared memory)";
+  if (size_t(a.B) * a.K * 2 > 200 * 1024) {
+    // x rows are staged in shared memory: run the batch in halves (their rows are independent)
+    GemvArgs lo = a, hi = a;
+    lo.B = hi.B = a.B / 2;
+    const int o = a.B / 2;
+    hi.x = a.x + (long)o * a.ldx;
+    if (a.y_f32) hi.y_f32 = a.y_f32 + (long)o * a.ldy;
+    if (a.y_bf16) hi.y_bf16 = a.y_bf16 + (long)o * a.ldy;
+    if (a.argmax) hi.argmax = a.argmax + o;
+    if (a.epi == kGemvQkvRope) {
+      hi.rope.pos = a.rope.pos + o;
+      hi.rope.q_out = a.rope.q_out + (long)o * a.rope.H * a.rope.D;
+      hi.rope.page_tables = a.rope.page_tables + (long)o * a.rope.pt_stride;
+      hi.rope.owner = a.rope.owner + (long)o * a.rope.owner_stride;
+      hi.rope.slot = a.rope.slot + (long)o * a.rope.owner_stride;
+    }
+    const char* err = gemv(lo, s);
+    return err ? err : gemv(hi, s);
+  }
   cudaError_t e;
   switch (a.epi) {
     case kGemvF32: e = gemv_dispatch<kGemvF32>(a, s); break;

@@ -86,6 +86,10 @@ class LlamaCPEngine:
         self.scale = 1.0 / math.sqrt(self.D)
         self.use_graphs = use_graphs and self.cuda
         self.perf = perf_log or PerfLog.from_env(self.env)
+        # fused QKV projection + K/V push: measured faster on one rank (+2% prefill), slower at
+        # CP=8 (the GEMM epilogue's 4 warps per SM then carry every peer store); an explicit
+        # HCP_FUSED_QKV overrides
+        self.fused_qkv = self.env.fused_qkv if self.env.fused_qkv is not None else (world == 1)
         if kv_pages is None:
             kv_pages = -(-self.max_context // self.page_size) + \
                 max_batch * -(-decode_reserve // self.page_size) + 2
@@ -204,7 +208,7 @@ class LlamaCPEngine:
                     self.scale, True, q_buf, o_buf, None, self.prefill_epoch)
             if trace:
                 ev[1].record()
-            if self.env.fused_qkv:
+            if self.fused_qkv:
                 # one kernel: QKV GEMM whose epilogue rotates, writes Q and pushes K/V to every rank
                 self.rt.push_layer_fused(xn, lw.wqkv, lw.bqkv, *tail)
             else:
@@ -504,7 +508,7 @@ class LlamaCPEngine:
                     True, q_buf, o_buf, None, self.prefill_epoch, existing)
             if T:
                 K.rmsnorm(x, lw.in_norm, self.cfg.rms_norm_eps, out=xn)
-            if T and self.env.fused_qkv:
+            if T and self.fused_qkv:
                 self.rt.push_layer_fused(xn, lw.wqkv, lw.bqkv, *tail)
                 self.rt.attend_layer(xn, *tail)
             else:

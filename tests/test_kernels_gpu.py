@@ -214,3 +214,16 @@ def test_gemv_k_chunks_and_row_tails(dev, kdim, n):
         tok = torch.empty(b, dtype=torch.int64, device=dev)
         native().argmax_finalize(am, None, tok)
         assert torch.equal(tok, logits.argmax(-1))
+
+
+def test_gemv_batch_larger_than_staging(dev):
+    """B x K too large for one shared-memory x stage (8 rows x 14336, the Llama-3-8B down
+    projection at batch 8): the batch is run in halves; same result as per-row GEMVs."""
+    torch.manual_seed(9)
+    b, kdim, n = 8, 14336, 256
+    x = torch.randn(b, kdim, device=dev, dtype=torch.bfloat16)
+    w = torch.randn(n, kdim, device=dev, dtype=torch.bfloat16) / math.sqrt(kdim)
+    res = torch.randn(b, n, device=dev, dtype=torch.bfloat16)
+    expect = (x.float() @ w.float().t()).bfloat16().float() + res.float()
+    K.gemv(x, w, "residual", y_bf16=res)
+    assert rel_err(res, expect) < 1e-2
