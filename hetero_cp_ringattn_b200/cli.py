@@ -241,6 +241,31 @@ def cmd_compare_logits(args) -> int:
     return 0 if ok else 1
 
 
+def cmd_compare_hidden(args) -> int:
+    """Compare two tensor-dump directories (--export-hidden-states / --prefill-debug outputs, or
+    the reference's dumps; the reference's scripts/compare_hidden_states.py): every file name
+    present in both, shape check, max / mean absolute and max relative difference."""
+    from .debug_export import read_tensor_bin
+    names = sorted(set(f for f in os.listdir(args.a) if f.endswith(".bin") and f != "logits.bin") &
+                   set(f for f in os.listdir(args.b) if f.endswith(".bin")))
+    rows, ok = [], True
+    for n in names:
+        ta = read_tensor_bin(os.path.join(args.a, n)).double()
+        tb = read_tensor_bin(os.path.join(args.b, n)).double()
+        if ta.shape != tb.shape:
+            rows.append({"file": n, "error": f"shape {tuple(ta.shape)} vs {tuple(tb.shape)}"})
+            ok = False
+            continue
+        d = (ta - tb).abs()
+        rel = float((d / tb.abs().clamp_min(1e-6)).max()) if d.numel() else 0.0
+        r = {"file": n, "max_abs": float(d.max()) if d.numel() else 0.0,
+             "mean_abs": float(d.mean()) if d.numel() else 0.0, "max_rel": rel}
+        ok = ok and r["max_abs"] <= args.tolerance
+        rows.append(r)
+    print(json.dumps({"files": len(names), "passed": ok and bool(names), "per_file": rows}))
+    return 0 if ok and names else 1
+
+
 def cmd_perf_summary(args) -> int:
     """Aggregate an HCP_PERF_LOG JSONL file per event (the reference's parse_worker_perf.py)."""
     import collections
@@ -307,6 +332,11 @@ def main(argv: Optional[List[str]] = None) -> int:
     s.add_argument("--session-continuation-tokens", type=int, default=64)
     s.add_argument("--http-addr", default=None)
     s.set_defaults(fn=cmd_serve)
+    ch = sub.add_parser("compare-hidden")
+    ch.add_argument("a")
+    ch.add_argument("b")
+    ch.add_argument("--tolerance", type=float, default=2e-2)
+    ch.set_defaults(fn=cmd_compare_hidden)
     cl = sub.add_parser("compare-logits")
     cl.add_argument("a")
     cl.add_argument("b")

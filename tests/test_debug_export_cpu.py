@@ -82,3 +82,27 @@ def test_prefill_debug_and_qk_injection(tmp_path):
     a = read_tensor_bin(os.path.join(d1, "layer_0_post_attn.bin"))
     c = read_tensor_bin(os.path.join(d3, "layer_0_post_attn.bin"))
     assert not torch.allclose(a, c)
+
+
+def test_compare_hidden_cli(tmp_path):
+    import json
+    import subprocess
+    import sys
+    cfg, w = _model()
+    ids = torch.randint(0, cfg.vocab_size, (9,), generator=torch.Generator().manual_seed(4))
+    a, b = str(tmp_path / "a"), str(tmp_path / "b")
+    prefill_debug_layer0(w, ids, a)
+    prefill_debug_layer0(w, ids, b)
+    r = subprocess.run([sys.executable, "-m", "hetero_cp_ringattn_b200", "compare-hidden", a, b],
+                       capture_output=True, text=True, timeout=120)
+    out = json.loads(r.stdout.strip().splitlines()[-1])
+    assert r.returncode == 0 and out["passed"] and out["files"] >= 7
+    # perturb one file: the comparison fails and names it
+    t = read_tensor_bin(os.path.join(b, "layer_0_post_attn.bin"))
+    write_tensor_bin(t + 1.0, os.path.join(b, "layer_0_post_attn.bin"))
+    r = subprocess.run([sys.executable, "-m", "hetero_cp_ringattn_b200", "compare-hidden", a, b],
+                       capture_output=True, text=True, timeout=120)
+    out = json.loads(r.stdout.strip().splitlines()[-1])
+    assert r.returncode == 1 and not out["passed"]
+    bad = [x for x in out["per_file"] if x["max_abs"] > 0.5]
+    assert [x["file"] for x in bad] == ["layer_0_post_attn.bin"]
