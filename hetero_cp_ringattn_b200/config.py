@@ -305,6 +305,7 @@ class EnvConfig:
     control_timeout_s: int = 600            # HCP_QUIC_TIMEOUT_SECS (control-plane timeout)
     p2p_spin_budget_ms: int = 5000          # HCP_P2P_SPIN_BUDGET_MS: device-side peer-wait limit
     device: Optional[str] = None            # HCP_TORCH_DEVICE / HCP_TCH_DEVICE
+    nvtx: bool = False                      # HCP_NVTX: NVTX ranges per prefill layer / decode step
     fused_qkv: Optional[bool] = None        # HCP_FUSED_QKV: projection GEMM epilogue pushes K/V
                                             # (default: on a single rank only, see the engine)
 
@@ -321,6 +322,7 @@ class EnvConfig:
             control_timeout_s=_env_int("HCP_QUIC_TIMEOUT_SECS", 600),
             p2p_spin_budget_ms=_env_int("HCP_P2P_SPIN_BUDGET_MS", 5000),
             device=os.environ.get("HCP_TORCH_DEVICE") or os.environ.get("HCP_TCH_DEVICE") or None,
+            nvtx=_env_bool("HCP_NVTX", False),
             fused_qkv=(_env_bool("HCP_FUSED_QKV", True) if os.environ.get("HCP_FUSED_QKV") else None),
         )
 

@@ -198,7 +198,10 @@ class LlamaCPEngine:
         o_buf = torch.empty_like(q_buf)
         start_tile = int(st.positions[0]) // 128 if st.strategy is RingStrategy.VANILLA else 0
         trace = self.perf.enabled
+        nvtx = self.env.nvtx
         for li, lw in enumerate(w.layers):
+            if nvtx:
+                torch.cuda.nvtx.range_push(f"prefill layer {li}")
             if trace:
                 ev = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
                 ev[0].record()
@@ -229,6 +232,8 @@ class LlamaCPEngine:
             if trace:
                 ev[4].record()
                 self._emit_layer(st, li, T, Lp, ev)
+            if nvtx:
+                torch.cuda.nvtx.range_pop()
         return self._first_token_cuda(st, x, return_logits)
 
     def _emit_layer(self, st: RequestState, layer: int, T: int, Lp: int, ev) -> None:
@@ -247,6 +252,7 @@ class LlamaCPEngine:
                        mlp_ms=ev[3].elapsed_time(ev[4]), kv_sent_bytes=sent, kv_recv_bytes=recv,
                        wire_sent_bytes=sent, wire_recv_bytes=recv, micro_blocks=-(-Lp // 128),
                        num_domains=self.world, seq_len=T, overlap=True,
+                       nvlink_gbps=sent / max(ev[1].elapsed_time(ev[2]), 1e-6) / 1e6,
                        attn_tflops=4.0 * self.H * self.D * float(np.sum(st.positions + 1)) /
                        max(attn_ms, 1e-6) / 1e9)
 
@@ -730,6 +736,10 @@ class DecodeGraph:
                     with torch.cuda.graph(self.graph):
                         self.body()
                 self.graph_launches = cap.launches
+            if self.e.env.nvtx:
+                torch.cuda.nvtx.range_push(f"decode step B={self.B}")
             self.graph.replay()
+            if self.e.env.nvtx:
+                torch.cuda.nvtx.range_pop()
             launches.count(self.graph_launches)
         return self.out_tok[:n].clone()

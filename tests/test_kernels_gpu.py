@@ -227,3 +227,24 @@ def test_gemv_batch_larger_than_staging(dev):
     expect = (x.float() @ w.float().t()).bfloat16().float() + res.float()
     K.gemv(x, w, "residual", y_bf16=res)
     assert rel_err(res, expect) < 1e-2
+
+
+@pytest.mark.parametrize("L,T,h,hkv,d", [(1, 1, 4, 1, 64), (129, 1, 4, 1, 128), (300, 300, 16, 2, 128),
+                                         (257, 2, 8, 8, 64), (1000, 130, 16, 2, 64)])
+def test_attention_edge_shapes(dev, L, T, h, hkv, d):
+    """A single key, a single query, MQA (one KV head), 8-head GQA groups, no GQA, a query block
+    one row past a tile: the queries are the last T positions of an L-token context."""
+    torch.manual_seed(12)
+    q_all = torch.randn(L, h, d, device=dev, dtype=torch.bfloat16)
+    k_all = torch.randn(L, hkv, d, device=dev, dtype=torch.bfloat16)
+    v_all = torch.randn(L, hkv, d, device=dev, dtype=torch.bfloat16)
+    pos = torch.arange(L - T, L, device=dev)
+    ks, vs = _stage(k_all, v_all, cap=max(128, L))
+    st = status_tensor(dev)
+    o, lse = K.attention(q_all[pos].contiguous(), ks, vs, pos.int(), L, causal=True,
+                         kv_start_tile=(L - T) // 128, status=st)
+    assert_status_clean(st)
+    ro, rl = ref.full_attention(q_all[pos].float(), k_all.float(), v_all.float(), pos,
+                                torch.arange(L, device=dev), causal=True)
+    assert (o.float() - ro).abs().max() < 2e-2
+    assert (lse - rl).abs().max() < 2e-2

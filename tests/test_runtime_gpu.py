@@ -245,3 +245,35 @@ def test_qkv_gemv_rope_matches_two_kernel_path(dev, b, d):
     assert (arena_a.float() - rt.arena().float()).abs().max() < 2e-2
     assert arena_a.abs().sum() > 0
     rt.shutdown()
+
+
+@pytest.mark.parametrize("h,hkv,d,n", [(16, 2, 128, 5000), (4, 4, 64, 70), (8, 1, 64, 1)])
+def test_decode_attention_group_shapes(dev, h, hkv, d, n):
+    """Tensor-core split-KV decode attention for 8-head GQA groups at head_dim 128 (the Qwen2.5
+    shape), no GQA, and MQA with a single cached token, against an fp32 reference."""
+    torch.manual_seed(14)
+    pages_n = -(-n // PAGE) + 1
+    rt = native().Runtime(0, 1, 0, 1, pages_n + 1, PAGE, hkv, d, h, 1024, 8, 2000)
+    arena = rt.arena()
+    arena.zero_()
+    k = torch.randn(n, hkv, d, device=dev, dtype=torch.bfloat16)
+    v = torch.randn(n, hkv, d, device=dev, dtype=torch.bfloat16)
+    page_ids = list(range(pages_n, 0, -1))  # reversed page order
+    for i in range(n):
+        arena[0, page_ids[i // PAGE], 0, :, i % PAGE] = k[i]
+        arena[0, page_ids[i // PAGE], 1, :, i % PAGE] = v[i]
+    pt = torch.tensor([page_ids], dtype=torch.int32, device=dev)
+    q = torch.randn(1, h, d, device=dev, dtype=torch.bfloat16)
+    ntok = torch.tensor([n], dtype=torch.int32, device=dev)
+    splits = 7
+    part_o = torch.empty(h * splits * d, device=dev)
+    part_l = torch.empty(h * splits, device=dev)
+    cnt = torch.zeros(hkv + 1, dtype=torch.int32, device=dev)
+    out = torch.empty(1, h * d, device=dev, dtype=torch.bfloat16)
+    rt.decode_attn(q, 0, pt, ntok, 1.0 / math.sqrt(d), splits, part_o, part_l, cnt, None, 1, 5, out)
+    torch.cuda.synchronize()
+    rt.check()
+    ro, _ = ref.full_attention(q[0][None].float(), k.float(), v.float(), torch.tensor([n - 1], device=dev),
+                               torch.arange(n, device=dev), causal=True)
+    assert (out.view(h, d).float() - ro[0]).abs().max() < 2e-2
+    rt.shutdown()
