@@ -64,10 +64,13 @@ def _device(args) -> torch.device:
 
 
 def cmd_correctness(args) -> int:
-    from .correctness import run_suite, write_report
+    from .config import RingAttnConfig
+    from .correctness import case_from_ring_config, run_suite, write_report
     from .errors import ToleranceTier
     tier = ToleranceTier.parse(args.tolerance_tier)
-    rep = run_suite(tier, stress_seeds=args.stress_test)
+    extra = [(os.path.basename(p), case_from_ring_config(RingAttnConfig.from_file(p)))
+             for p in (args.config or [])]
+    rep = run_suite(tier, stress_seeds=args.stress_test, extra_cases=extra)
     for c in rep["cases"]:
         w = c["worst_seed"]
         print(f"[{'PASS' if c['passed'] else 'FAIL'}] {c['name']}: out max_abs={w['output']['max_abs_err']:.3e} "
@@ -302,6 +305,8 @@ def main(argv: Optional[List[str]] = None) -> int:
     c.add_argument("--report-path", default=None)
     c.add_argument("--tolerance-tier", default="strict")
     c.add_argument("--stress-test", type=int, default=5)
+    c.add_argument("--config", action="append", default=None,
+                   help="domain layout JSON (global_seq_len, heads, domains[seq_chunk_len, block_size])")
     c.set_defaults(fn=cmd_correctness)
     i = sub.add_parser("infer")
     _add_model_args(i)

@@ -126,10 +126,16 @@ def run_case(name: str, cfg: CaseConfig, seeds: Sequence[int], tier: ToleranceTi
             "worst_seed": worst, "passed": passed, "tolerance_tier": tier.value}
 
 
+def case_from_ring_config(cfg) -> CaseConfig:
+    """A domain layout file (config.RingAttnConfig: chunks, block sizes, heads) as a causal case."""
+    return CaseConfig(cfg.chunks, cfg.block_sizes, cfg.num_heads, cfg.head_dim,
+                      num_kv_heads=cfg.num_kv_heads, causal=True)
+
+
 def run_suite(tier: ToleranceTier = ToleranceTier.STRICT, stress_seeds: int = 5,
-              include_extended: bool = True, dtype=torch.float64) -> dict:
+              include_extended: bool = True, dtype=torch.float64, extra_cases=()) -> dict:
     t0 = time.time()
-    cases = default_cases() + (extended_cases() if include_extended else [])
+    cases = default_cases() + (extended_cases() if include_extended else []) + list(extra_cases)
     reports = []
     for name, cfg in cases:
         small = cfg.global_seq_len <= 256

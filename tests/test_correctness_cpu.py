@@ -47,3 +47,29 @@ def test_cli_correctness_report(tmp_path):
     assert cli_main(["correctness", "--report-path", str(path), "--stress-test", "1"]) == 0
     rep = json.loads(path.read_text())
     assert rep["passed"] and len(rep["cases"]) == 10
+
+
+def test_domain_layout_files_run_as_cases(tmp_path):
+    """The shipped domain layout files (configs/*.json) parse, validate and pass as causal ring
+    cases; the CLI takes them with --config."""
+    import glob
+    import json
+    import os
+    import subprocess
+    import sys
+    from hetero_cp_ringattn_b200.config import RingAttnConfig
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    files = sorted(glob.glob(os.path.join(root, "configs", "*.json")))
+    assert files
+    for p in files:
+        cfg = RingAttnConfig.from_file(p)
+        rep = C.run_case(os.path.basename(p), C.case_from_ring_config(cfg), seeds=[0],
+                         tier=ToleranceTier.STRICT)
+        assert rep["passed"], rep["worst_seed"]
+    out = tmp_path / "r.json"
+    r = subprocess.run([sys.executable, "-m", "hetero_cp_ringattn_b200", "correctness", "--stress-test", "1",
+                        "--config", files[0], "--report-path", str(out)],
+                       capture_output=True, text=True, timeout=600, cwd=root)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
+    names = [c["name"] for c in json.load(open(out))["cases"]]
+    assert os.path.basename(files[0]) in names
