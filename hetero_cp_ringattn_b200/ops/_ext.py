@@ -20,6 +20,7 @@ def _load():
     if _mod is not None or _err is not None:
         return _mod
     try:
+        import torch  # noqa: F401  (loads libc10 / libtorch that the extension links against)
         _mod = importlib.import_module("hetero_cp_ringattn_b200._C")
     except Exception as e:  # pragma: no cover - exercised only when the build is missing
         _err = e
