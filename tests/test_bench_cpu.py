@@ -1,0 +1,39 @@
+"""Host-side pieces of the benchmark entry points (no GPU): the configs name existing model shapes
+of the benchmark table, `--impl reference` prints its one-line JSON and exits 0, and the kernel
+bench's ratio / FLOP helpers."""
+
+import json
+import os
+import subprocess
+import sys
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path.insert(0, ROOT)
+
+
+def test_bench_configs_are_known_shapes():
+    import bench
+    from hetero_cp_ringattn_b200.config import preset
+    assert bench.CONFIGS["llama-3.2-1b-32k"]["prompt"] == 32768
+    for name, spec in bench.CONFIGS.items():
+        cfg = preset(spec["model"])
+        assert cfg.max_position_embeddings >= spec["prompt"] + spec["new_tokens"], name
+
+
+def test_reference_arm_reports_unavailable():
+    r = subprocess.run([sys.executable, "bench.py", "--impl", "reference"], cwd=ROOT,
+                       capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0
+    line = json.loads(r.stdout.strip().splitlines()[-1])
+    assert line["impl"] == "reference" and "unavailable" in line
+
+
+def test_kernel_bench_helpers():
+    from benchmarks import kernels as kb
+    assert kb.parse_ratio("1:1", 2) == [1, 1]
+    assert kb.parse_ratio("4:1", 8) == [4, 4, 4, 4, 1, 1, 1, 1]
+    assert kb.parse_ratio("5:5:1", 3) == [5, 5, 1]
+    # causal FLOPs of an L-token prefill: 4 * H * D * L (L + 1) / 2
+    assert kb.causal_flops(8, 8, 2, 4) == 4.0 * 2 * 4 * 36
+    p = kb.peaks()
+    assert p["hbm_gbs"] > 0 and p["tflops"] > 0
