@@ -172,7 +172,8 @@ def cmd_serve(args) -> int:
     dev = _device(args)
     group = None
     from datetime import timedelta
-    timeout = timedelta(seconds=int(os.environ.get("HCP_QUIC_TIMEOUT_SECS", "600")))
+    from .config import EnvConfig
+    timeout = timedelta(seconds=EnvConfig.from_env().control_timeout_s)  # HCP_QUIC_TIMEOUT_SECS
     if world > 1:
         if dev.type == "cuda":
             torch.cuda.set_device(dev)

@@ -296,13 +296,18 @@ def _env_int(name: str, default: int) -> int:
 @dataclasses.dataclass
 class EnvConfig:
     perf_log: Optional[str] = None          # HCP_PERF_LOG: JSONL perf events
-    micro_kv_block_size: int = 0            # HCP_MICRO_KV_BLOCK_SIZE (0 -> kernel default tile)
-    disable_overlap: bool = False           # HCP_DISABLE_OVERLAP: stage all peer KV first
-    decode_ring: bool = True                # HCP_RING_DECODE_RING
-    decode_sd: bool = True                  # HCP_RING_DECODE_SD: capacity-scheduled KV growth
+    micro_kv_block_size: int = 0            # HCP_MICRO_KV_BLOCK_SIZE: host-path ring fold block
+                                            # (0 -> 128, the CUDA kernels' fixed KV tile)
+    disable_overlap: bool = False           # HCP_DISABLE_OVERLAP: accepted; both paths already
+                                            # stage every rank's KV before the attention reads it
+    decode_ring: bool = True                # HCP_RING_DECODE_RING=0: legacy KV re-send decode
+                                            # (host path; CUDA ranks warn and keep the exchange)
+    decode_sd: bool = True                  # HCP_RING_DECODE_SD: capacity-scheduled KV growth;
+                                            # 0 -> Q-ring placement, position % N
     kv_block_table: bool = True             # HCP_KV_CACHE_BLOCK_TABLE (paged arena is always used)
-    kv_block_size: int = 256                # HCP_KV_CACHE_BLOCK_SIZE (tokens per page)
-    control_timeout_s: int = 600            # HCP_QUIC_TIMEOUT_SECS (control-plane timeout)
+    kv_block_size: int = 256                # HCP_KV_CACHE_BLOCK_SIZE: tokens per KV page
+                                            # (engine default; CUDA needs a multiple of 128)
+    control_timeout_s: int = 600            # HCP_QUIC_TIMEOUT_SECS: process-group timeout of serve
     p2p_spin_budget_ms: int = 5000          # HCP_P2P_SPIN_BUDGET_MS: device-side peer-wait limit
     device: Optional[str] = None            # HCP_TORCH_DEVICE / HCP_TCH_DEVICE
     nvtx: bool = False                      # HCP_NVTX: NVTX ranges per prefill layer / decode step

@@ -7,8 +7,12 @@ Parity (reference call stacks):
     final position);
   * decode: the Q-ring / self-driving routes (ring.rs:682-818, self_driving.rs:333-675,
     tch_backend.rs:634-904) with KV growth placed by `FrozenKvAssigneeSchedule`
-    (self_driving.rs:12-120); here every rank computes the token's layer in parallel, attends
+    (self_driving.rs:12-120), or by global position % N (ring.rs:1934) when
+    HCP_RING_DECODE_SD=0; here every rank computes the token's layer in parallel, attends
     over its own shard and combines (O, LSE) with the other ranks inside the decode kernels;
+  * HCP_RING_DECODE_RING=0 selects the legacy route (ring.rs:982-997): every rank keeps every
+    decoded row and the prefill partitions are re-sent each step. It is a correctness fallback
+    of the host path only; CUDA ranks keep the (O, LSE) exchange;
   * release: tch_backend.rs:1077 (`release_request`).
 
 Hot path (CUDA): embedding, RMSNorm, tcgen05 GEMMs with fused bias / residual / SwiGLU epilogues,
@@ -26,6 +30,7 @@ from __future__ import annotations
 import dataclasses
 import math
 import time
+import warnings
 from typing import Dict, List, Optional, Sequence
 
 import numpy as np
@@ -58,7 +63,9 @@ class RequestState:
     decode_offset: int = 0
     context_len: int = 0             # tokens with KV (prompt + decoded)
     kv: Optional[RequestKv] = None
-    host_kv: Optional[list] = None   # CPU path: per layer (k [n,Hkv,D], v, pos [n])
+    host_kv: Optional[list] = None   # CPU path: per layer [k [n,Hkv,D], v, pos [n], shared [n]]
+                                     # shared: the row lives on this rank only (prompt / segment /
+                                     # owned growth); False: a replicated legacy-decode row
     keep_kv: bool = False
 
 
@@ -66,7 +73,7 @@ class LlamaCPEngine:
     def __init__(self, cfg: ModelConfig, weights: PreparedWeights, *, rank: int = 0,
                  world: int = 1, device: Optional[torch.device] = None,
                  group: Optional["dist.ProcessGroup"] = None, max_context: int = 8192,
-                 max_batch: int = 8, page_size: int = 256, kv_pages: Optional[int] = None,
+                 max_batch: int = 8, page_size: Optional[int] = None, kv_pages: Optional[int] = None,
                  decode_reserve: int = 512, env: Optional[EnvConfig] = None,
                  use_graphs: bool = True, perf_log: Optional[PerfLog] = None):
         cfg.validate()
@@ -80,7 +87,21 @@ class LlamaCPEngine:
         self.cuda = self.device.type == "cuda"
         self.max_context = int(max_context)
         self.max_batch = int(max_batch)
-        self.page_size = int(page_size)
+        # tokens per KV page: HCP_KV_CACHE_BLOCK_SIZE unless given; the arena is always paged
+        # (HCP_KV_CACHE_BLOCK_TABLE has nothing to switch off)
+        self.page_size = int(page_size if page_size is not None else self.env.kv_block_size)
+        if self.page_size <= 0 or (self.cuda and self.page_size % 128):
+            raise CapacityError(f"KV page size {self.page_size} must be a positive multiple of 128 "
+                                f"tokens on CUDA (the attention kernels read 128-token tiles)")
+        # host-path ring fold granularity (HCP_MICRO_KV_BLOCK_SIZE; 0 -> the CUDA tile, 128).
+        # The CUDA kernels always stream 128-token KV tiles.
+        self.micro_kv = int(self.env.micro_kv_block_size) or 128
+        self.legacy_decode = not self.env.decode_ring
+        if self.legacy_decode and self.cuda:
+            warnings.warn("HCP_RING_DECODE_RING=0 (legacy KV re-send decode) is a host-path "
+                          "correctness fallback; CUDA ranks decode with the (O, LSE) exchange",
+                          RuntimeWarning, stacklevel=2)
+            self.legacy_decode = False
         self.H, self.Hkv, self.D = cfg.num_heads, cfg.kv_heads, cfg.head_dim
         self.L = cfg.num_layers
         self.scale = 1.0 / math.sqrt(self.D)
@@ -132,9 +153,17 @@ class LlamaCPEngine:
         positions = build_domain_positions(assignment, len(chunks))
         return assignment, positions
 
-    def _schedule(self, req_id: int, tickets: Sequence[int], horizon: int) -> np.ndarray:
+    def _schedule(self, req_id: int, tickets: Sequence[int], horizon: int,
+                  first_t: int = 0, first_pos: int = 0) -> np.ndarray:
+        """[horizon, layers]: the rank that stores each decoded (token, layer) KV row. Row t is
+        the request's t-th decoded token; rows before `first_t` are already consumed and the
+        token of row `first_t` sits at global position `first_pos`."""
         if horizon <= 0:
             return np.zeros((0, self.L), dtype=np.int64)
+        if not self.env.decode_sd:
+            # Q-ring placement (ring.rs:1934): position p is kept by rank p % N on every layer
+            owners = (first_pos + np.arange(horizon, dtype=np.int64) - first_t) % self.world
+            return np.repeat(owners[:, None], self.L, axis=1)
         sched = FrozenKvAssigneeSchedule(tickets, req_id, horizon * self.L)
         seq = np.asarray(sched.sequence, dtype=np.int64)
         ordinals = (sched.phase + np.arange(horizon * self.L)) % len(seq)
@@ -167,7 +196,7 @@ class LlamaCPEngine:
         my_pos = positions[self.rank]
         T = len(my_pos)
         tickets = list(tickets) if tickets is not None else list(chunks)
-        assignee = self._schedule(req_id, tickets, decode_horizon)
+        assignee = self._schedule(req_id, tickets, decode_horizon, 0, Lp)
         growth = int((assignee == self.rank).sum(0).max()) if decode_horizon else 0
         st = RequestState(req_id=req_id, prompt_len=Lp, chunks=chunks, strategy=strategy,
                           positions=my_pos, owner_of_last=int(assignment[Lp - 1]),
@@ -291,6 +320,24 @@ class LlamaCPEngine:
         dist.all_gather(bufs, pad, group=self.group)
         return [b[: int(s)] for b, s in zip(bufs, sizes)]
 
+    def _ring_fold(self, q, q_pos, ks, vs, ps) -> torch.Tensor:
+        """Host ring attention: fold the sources in ring arrival order (own chunk first, then
+        the predecessor's, ...), each cut into micro blocks of `micro_kv` rows, with the online
+        softmax and the fully-future block skip (ring.rs:861-1399)."""
+        Tq = q.shape[0]
+        m = torch.full((self.H, Tq), ref.NEG_INIT, dtype=q.dtype)
+        l = torch.zeros(self.H, Tq, dtype=q.dtype)
+        acc = torch.zeros_like(q)
+        for step in range(self.world):
+            src = (self.rank - step) % self.world
+            k, v, kp = ks[src], vs[src], ps[src]
+            for b0 in range(0, k.shape[0], self.micro_kv):
+                b1 = min(b0 + self.micro_kv, k.shape[0])
+                m, l, acc = ref.online_update_block(m, l, acc, q, k[b0:b1].to(q.dtype),
+                                                    v[b0:b1].to(q.dtype), q_pos, kp[b0:b1],
+                                                    True, self.scale)
+        return ref.finalize_state(m, l, acc)[0]
+
     def _prefill_host(self, st: RequestState, ids: torch.Tensor, Lp: int, return_logits: bool):
         w, cfg = self.w, self.cfg
         T = ids.numel()
@@ -304,16 +351,9 @@ class LlamaCPEngine:
             k = ref.apply_rope(qkv[:, self.H * self.D:(self.H + self.Hkv) * self.D].view(T, self.Hkv, self.D),
                                pos, cfg.rope_theta)
             v = qkv[:, (self.H + self.Hkv) * self.D:].reshape(T, self.Hkv, self.D)
-            st.host_kv.append([k.clone(), v.clone(), pos.clone()])
-            ks = self._gather_rows(k)
-            vs = self._gather_rows(v)
-            ps = self._gather_rows(pos)
-            kk = torch.zeros(Lp, self.Hkv, self.D, dtype=k.dtype)
-            vv = torch.zeros_like(kk)
-            for a, b, p in zip(ks, vs, ps):
-                kk[p] = a
-                vv[p] = b
-            o, _ = ref.full_attention(q, kk, vv, pos, torch.arange(Lp), causal=True)
+            st.host_kv.append([k.clone(), v.clone(), pos.clone(), torch.ones(T, dtype=torch.bool)])
+            o = self._ring_fold(q, pos, self._gather_rows(k), self._gather_rows(v),
+                                self._gather_rows(pos))
             x = x + ref.linear(o.reshape(T, self.H * self.D), lw.wo)
             h = ref.rmsnorm(x, lw.post_norm, cfg.rms_norm_eps)
             x = x + ref.linear(K.swiglu_from_interleaved(ref.linear(h, lw.wgu)), lw.wd)
@@ -352,7 +392,8 @@ class LlamaCPEngine:
                 slot[b] = counts
                 ntok[:, b] = counts + own
             else:
-                owner[b] = own
+                # legacy route: every rank keeps every decoded row
+                owner[b] = 1 if self.legacy_decode else own
         return pos, owner, slot, ntok
 
     def _advance(self, req_ids: Sequence[int], owner: np.ndarray, pos: np.ndarray) -> None:
@@ -416,6 +457,16 @@ class LlamaCPEngine:
                     kv[0] = torch.cat([kv[0], k[b:b + 1]])
                     kv[1] = torch.cat([kv[1], v[b:b + 1]])
                     kv[2] = torch.cat([kv[2], posn[b:b + 1]])
+                    kv[3] = torch.cat([kv[3], torch.tensor([not self.legacy_decode])])
+                if self.legacy_decode:
+                    # re-send every rank's partition rows (ring.rs:982-997), attend over them
+                    # plus the replicated decoded rows; every rank gets the whole answer
+                    sh = kv[3]
+                    kk = torch.cat(self._gather_rows(kv[0][sh]) + [kv[0][~sh]])
+                    vv = torch.cat(self._gather_rows(kv[1][sh]) + [kv[1][~sh]])
+                    o, _ = ref.full_attention(q[b:b + 1], kk, vv, causal=False)
+                    outs.append(o)
+                    continue
                 if kv[0].shape[0]:
                     o, lse = ref.full_attention(q[b:b + 1], kv[0], kv[1], causal=False)
                 else:
@@ -475,7 +526,7 @@ class LlamaCPEngine:
         my_pos = np.arange(L0 + off, L0 + off + T, dtype=np.int64)
         last_owner = max(r for r in range(self.world) if seg[r] > 0)
         new_horizon = st.decode_offset + extra_horizon
-        sched_tab = self._schedule(req_id, tickets, new_horizon)
+        sched_tab = self._schedule(req_id, tickets, new_horizon, st.decode_offset, L0 + S)
         if self.cuda:
             kv = st.kv
             growth = int((sched_tab[st.decode_offset:] == self.rank).sum(0).max()) if extra_horizon else 0
@@ -547,13 +598,19 @@ class LlamaCPEngine:
                 kv[0] = torch.cat([kv[0], k])
                 kv[1] = torch.cat([kv[1], v])
                 kv[2] = torch.cat([kv[2], pos])
-            ks, vs, ps = self._gather_rows(kv[0]), self._gather_rows(kv[1]), self._gather_rows(kv[2])
+                kv[3] = torch.cat([kv[3], torch.ones(T, dtype=torch.bool)])
+            sh = kv[3]
+            ks, vs, ps = (self._gather_rows(kv[0][sh]), self._gather_rows(kv[1][sh]),
+                          self._gather_rows(kv[2][sh]))
             if T:
                 kk = torch.zeros(Ltot, self.Hkv, self.D, dtype=torch.float32)
                 vv = torch.zeros_like(kk)
                 for a, b, p in zip(ks, vs, ps):
                     kk[p] = a.float()
                     vv[p] = b.float()
+                # replicated legacy-decode rows (identical on every rank): once, from here
+                kk[kv[2][~sh]] = kv[0][~sh].float()
+                vv[kv[2][~sh]] = kv[1][~sh].float()
                 o, _ = ref.full_attention(q, kk, vv, pos, torch.arange(Ltot), causal=True)
                 x = x + ref.linear(o.reshape(T, self.H * self.D), lw.wo)
                 h = ref.rmsnorm(x, lw.post_norm, cfg.rms_norm_eps)

@@ -164,3 +164,84 @@ def test_session_append_matches_reference(world):
     full = torch.cat([r["a"], torch.tensor(r["toks"]), r["b"]])
     ref_more, _ = reference_model.greedy_generate(w, full, 3)
     assert r["more"] == ref_more
+
+
+def _route_worker(rank, world, port, out_dir, env_kwargs):
+    from hetero_cp_ringattn_b200.config import EnvConfig
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        cfg, w = tiny_weights()
+        pw = PreparedWeights.from_weights(w, dtype=torch.float32)
+        eng = LlamaCPEngine(cfg, pw, rank=rank, world=world, device=torch.device("cpu"),
+                            max_context=256, env=EnvConfig(**env_kwargs))
+        g = torch.Generator().manual_seed(11)
+        a = torch.randint(0, cfg.vocab_size, (29,), generator=g)
+        b = torch.randint(0, cfg.vocab_size, (7,), generator=g)
+        chunks = [12, 11, 6][:world]
+        tok, _ = eng.prefill(4, a, chunks, "zigzag", decode_horizon=5, keep_kv=True,
+                             tickets=[2, 2, 1][:world])
+        toks = [int(tok)]
+        cur = tok
+        for _ in range(4):
+            cur = eng.decode_step([4], cur)
+            toks.append(int(cur))
+        # rows stored on this rank after decoding: (own rows, replicated rows, decoded positions)
+        kv0 = eng.reqs[4].host_kv[0]
+        mine = [int(p) for p, s in zip(kv0[2], kv0[3]) if s and int(p) >= 29]
+        replicated = [int(p) for p, s in zip(kv0[2], kv0[3]) if not s]
+        seg = torch.tensor([toks[-1]] + b.tolist())
+        L0 = eng.reqs[4].context_len
+        tok2, _ = eng.append(4, seg, list(range(L0, L0 + seg.numel())), [1] * world)
+        more = [int(tok2)]
+        cur = tok2
+        for _ in range(3):
+            cur = eng.decode_step([4], cur)
+            more.append(int(cur))
+        torch.save({"a": a, "b": b, "toks": toks, "more": more, "mine": mine,
+                    "replicated": replicated}, os.path.join(out_dir, f"r{rank}.pt"))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("env_kwargs", [
+    {"decode_sd": False, "micro_kv_block_size": 7},   # Q-ring placement: position % N
+    {"decode_ring": False},                           # legacy KV re-send decode
+])
+def test_decode_routes_match_reference(env_kwargs):
+    """The reference's selectable decode routes (HCP_RING_DECODE_SD=0, HCP_RING_DECODE_RING=0;
+    ring.rs:682-818, :982-997, :1934) give the single-device tokens, before and after a session
+    continuation, with their own KV placement."""
+    world = 3
+    with tempfile.TemporaryDirectory() as d:
+        mp.start_processes(_route_worker, args=(world, free_port(), d, env_kwargs), nprocs=world,
+                           join=True, start_method="spawn")
+        res = [torch.load(os.path.join(d, f"r{r}.pt")) for r in range(world)]
+    cfg, w = tiny_weights()
+    r0 = res[0]
+    ref_first, _ = reference_model.greedy_generate(w, r0["a"], 4)
+    full = torch.cat([r0["a"], torch.tensor(r0["toks"]), r0["b"]])
+    ref_more, _ = reference_model.greedy_generate(w, full, 3)
+    decoded = list(range(29, 33))  # positions of the 4 decoded tokens with KV before the append
+    for r, out in enumerate(res):
+        assert out["toks"] == ref_first and out["more"] == ref_more
+        if env_kwargs.get("decode_ring") is False:
+            assert out["mine"] == [] and out["replicated"] == decoded
+        else:
+            assert out["replicated"] == [] and out["mine"] == [p for p in decoded if p % world == r]
+
+
+def test_page_size_from_environment():
+    from hetero_cp_ringattn_b200.config import EnvConfig
+    from hetero_cp_ringattn_b200.errors import CapacityError
+    cfg, w = tiny_weights()
+    pw = PreparedWeights.from_weights(w, dtype=torch.float32)
+    eng = LlamaCPEngine(cfg, pw, device=torch.device("cpu"), max_context=256,
+                        env=EnvConfig(kv_block_size=384))
+    assert eng.page_size == 384 and eng.kv.page_size == 384
+    assert LlamaCPEngine(cfg, pw, device=torch.device("cpu"), max_context=256, page_size=128,
+                         env=EnvConfig(kv_block_size=384)).page_size == 128
+    with pytest.raises(CapacityError):
+        LlamaCPEngine(cfg, pw, device=torch.device("cpu"), env=EnvConfig(kv_block_size=0))
