@@ -23,6 +23,7 @@ import argparse
 import json
 import logging
 import os
+import signal
 import struct
 import sys
 from typing import List, Optional
@@ -158,6 +159,10 @@ def cmd_infer(args) -> int:
     return 0
 
 
+def _raise_interrupt(signum, frame):
+    raise KeyboardInterrupt
+
+
 def cmd_serve(args) -> int:
     import torch.distributed as dist
     from .models.llama import LlamaCPEngine
@@ -187,8 +192,14 @@ def cmd_serve(args) -> int:
     control = P.ControlPlane(group, rank, world)
     worker = Worker(eng, control)
     caps = control.all_gather(query_device_capacity_mb(str(dev)))  # the handshake
+    # torchrun forwards SIGINT / SIGTERM to every rank: both end the serve loop the same way
+    signal.signal(signal.SIGTERM, _raise_interrupt)
     if rank != 0:
-        worker.loop()
+        try:
+            worker.loop()
+        except KeyboardInterrupt:
+            eng.close(sync=False)  # the other ranks are stopping too: no barrier
+            return 0
         eng.close()
         return 0
     tok = load_tokenizer(args.model_dir, cfg.vocab_size)
@@ -219,8 +230,9 @@ def cmd_serve(args) -> int:
     except KeyboardInterrupt:
         pass
     finally:
-        coord.shutdown()
-        eng.close()
+        # the workers reached Shutdown: they close after a barrier, so close with one too
+        workers_stopped_cleanly = coord.shutdown()
+    eng.close(sync=workers_stopped_cleanly)
     return 0
 
 

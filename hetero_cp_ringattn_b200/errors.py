@@ -39,6 +39,11 @@ class CapacityError(RingError):
     """KV byte admission / reservation failure."""
 
 
+class AdmissionError(RingError):
+    """The coordinator rejected a request before any rank ran it (e.g. a prompt shorter than
+    the number of ranks). The HTTP API answers 400, as for a `CapacityError`."""
+
+
 class KernelError(RingError):
     """A device kernel reported a failure through the runtime status word."""
 

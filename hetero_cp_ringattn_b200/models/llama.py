@@ -136,10 +136,12 @@ class LlamaCPEngine:
             self.num_sms = native().num_sms(self.device.index or 0)
 
     # ------------------------------------------------------------------ helpers
-    def close(self) -> None:
+    def close(self, sync: bool = True) -> None:
+        """Free the graphs and the runtime. `sync` waits for every rank first (peers may still
+        read this rank's region); pass False when the other ranks are stopping as well."""
         self._graphs = {} if self.cuda else None
         if self.rt is not None:
-            if self.world > 1 and dist.is_initialized():
+            if sync and self.world > 1 and dist.is_initialized():
                 dist.barrier(group=self.group)
             self.rt.shutdown()
             self.rt = None

@@ -24,7 +24,7 @@ import threading
 import time
 from typing import Dict, List, Optional, Sequence
 
-from ..errors import CapacityError, ProtocolError
+from ..errors import AdmissionError, CapacityError, ProtocolError, RingError
 from ..models.sampling import sample_token
 from ..parallel.capacity import (DEFAULT_ACTIVATION_RESERVE_MB, KvLedger, UNKNOWN_CAPACITY,
                                  chunk_sizes)
@@ -131,10 +131,18 @@ class Coordinator:
             raise ProtocolError("; ".join(f"rank error: {e.message}" for e in errs))
         return resp
 
-    def shutdown(self) -> None:
+    def shutdown(self) -> bool:
+        """Stop the loop and tell the worker ranks to exit. Returns False when the ranks were
+        already gone (an interrupt that reached every rank makes the broadcast fail; that is not
+        an error here)."""
         self._stop.set()
         with self.lock:
-            self.control.broadcast(P.Shutdown())
+            try:
+                self.control.broadcast(P.Shutdown())
+            except (RuntimeError, OSError) as e:
+                self.trace.emit("shutdown_broadcast_failed", error=str(e))
+                return False
+        return True
 
     # ------------------------------------------------------------------ admission
     def _chunks(self, n: int) -> List[int]:
@@ -162,9 +170,12 @@ class Coordinator:
         rid = job.request_id
         if job.append:
             return self._append(job)
-        chunks = self._chunks(len(job.prompt_ids))
         horizon = max(1, job.max_tokens) + (self.args.session_continuation_tokens if job.keep_kv else 0)
-        self._reserve(rid, chunks, horizon)
+        try:
+            chunks = self._chunks(len(job.prompt_ids))
+        except RingError as e:
+            raise AdmissionError(str(e)) from e
+        self._reserve(rid, chunks, horizon)  # CapacityError: requeued while others hold KV
         try:
             resp = self.run_command(P.Prefill(rid, list(job.prompt_ids), chunks, self.args.strategy,
                                               horizon, self._tickets(chunks), job.keep_kv))
@@ -240,7 +251,8 @@ class Coordinator:
             self.ledger.release(job.request_id)
         self.trace.emit("failed", request=job.request_id, error=str(err))
         if job.done:
-            job.done({"request_id": job.request_id, "error": str(err)})
+            job.done({"request_id": job.request_id, "error": str(err),
+                      "status": 400 if isinstance(err, (AdmissionError, CapacityError)) else 500})
 
     # ------------------------------------------------------------------ iteration
     def iteration(self) -> bool:

@@ -119,7 +119,7 @@ def make_handler(state: ApiState):
                     res = a
                     break
             if "error" in res:
-                return self._text(500, res["error"])
+                return self._text(int(res.get("status", 500)), res["error"])
             text = state.tok.decode(res["tokens"])
             pt, ct = res["prompt_tokens"], len(res["tokens"])
             return self._json(200, {

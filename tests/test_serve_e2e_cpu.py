@@ -1,0 +1,144 @@
+"""Local multi-process serving end to end: `serve` under torchrun with two CPU (gloo) ranks, an HF
+directory of random weights, an uneven 3:1 capacity ratio and the zigzag layout; completions over
+HTTP, concurrent requests, health and metrics, then a shutdown on SIGINT without rank tracebacks.
+
+Parity: the reference's local multi-process drivers (scripts/test_http_api_local.sh,
+test_http_api_concurrent_local.sh: coordinator + 2 workers on one host, curl /v1/completions,
+/health, /metrics).
+"""
+
+import json
+import os
+import signal
+import socket
+import subprocess
+import sys
+import threading
+import time
+import urllib.error
+import urllib.request
+
+import pytest
+import torch
+
+from hetero_cp_ringattn_b200.config import preset
+from hetero_cp_ringattn_b200.models import reference_model
+from hetero_cp_ringattn_b200.models.weights import ModelWeights
+from hetero_cp_ringattn_b200.serve.tokenizer import ByteTokenizer
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _get(port, path):
+    with urllib.request.urlopen(f"http://127.0.0.1:{port}{path}", timeout=30) as r:
+        return json.loads(r.read())
+
+
+def _complete(port, prompt, n):
+    req = urllib.request.Request(f"http://127.0.0.1:{port}/v1/completions",
+                                 data=json.dumps({"prompt": prompt, "max_tokens": n}).encode(),
+                                 headers={"Content-Type": "application/json"})
+    with urllib.request.urlopen(req, timeout=120) as r:
+        return json.loads(r.read())
+
+
+@pytest.fixture(scope="module")
+def server(tmp_path_factory):
+    cfg = preset("tiny")
+    w = ModelWeights.random_init(cfg, seed=5, dtype=torch.float32, std=0.2)
+    mdir = tmp_path_factory.mktemp("model")
+    w.save(str(mdir))
+    http = _port()
+    env = dict(os.environ, HCP_QUIC_TIMEOUT_SECS="60", PYTHONPATH=REPO, OMP_NUM_THREADS="2")
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2",
+           "--master-addr", "127.0.0.1", "--master-port", str(_port()),
+           "-m", "hetero_cp_ringattn_b200", "serve", "--model-dir", str(mdir), "--device", "cpu",
+           "--max-context", "512", "--ratio", "3:1", "--ring-strategy", "zigzag",
+           "--http-addr", f"127.0.0.1:{http}"]
+    log = open(mdir / "serve.log", "w")
+    proc = subprocess.Popen(cmd, cwd=REPO, env=env, stdout=log, stderr=subprocess.STDOUT,
+                            start_new_session=True)
+    try:
+        deadline = time.time() + 180
+        while True:
+            try:
+                health = _get(http, "/health")
+                break
+            except OSError:
+                if proc.poll() is not None or time.time() > deadline:
+                    log.flush()
+                    raise RuntimeError("serve did not come up:\n" + (mdir / "serve.log").read_text()[-3000:])
+                time.sleep(0.5)
+        yield w, http, health, proc, mdir / "serve.log"
+    finally:
+        if proc.poll() is None:
+            proc.send_signal(signal.SIGINT)
+            try:
+                proc.wait(timeout=60)
+            except subprocess.TimeoutExpired:
+                os.killpg(proc.pid, signal.SIGKILL)  # the group this fixture started
+                proc.wait(timeout=30)
+        log.close()
+
+
+def _expected(w, prompt, n):
+    tok = ByteTokenizer(w.cfg.vocab_size)
+    ids = tok.encode(prompt)
+    ref, _ = reference_model.greedy_generate(w, torch.tensor(ids), n - 1)
+    return tok.decode(ref), len(ids)
+
+
+def test_two_rank_server_health_and_completion(server):
+    w, port, health, _, _ = server
+    assert health == {"status": "ok", "workers_connected": 2, "num_domains": 2}
+    text, n_prompt = _expected(w, "heterogeneous context parallel ring", 6)
+    res = _complete(port, "heterogeneous context parallel ring", 6)
+    assert res["choices"][0]["text"] == text
+    assert res["usage"] == {"prompt_tokens": n_prompt, "completion_tokens": 6,
+                            "total_tokens": n_prompt + 6}
+
+
+def test_two_rank_server_concurrent_requests(server):
+    w, port, _, _, _ = server
+    prompts = ["ab", "two ranks share one prompt", "zigzag layout, uneven 3:1 split", "xyz"]
+    out = {}
+
+    def go(i, p):
+        out[i] = _complete(port, p, 4)
+
+    ts = [threading.Thread(target=go, args=(i, p)) for i, p in enumerate(prompts)]
+    for t in ts:
+        t.start()
+    for t in ts:
+        t.join(timeout=180)
+    for i, p in enumerate(prompts):
+        assert out[i]["choices"][0]["text"] == _expected(w, p, 4)[0]
+    m = _get(port, "/metrics")
+    assert m["completed_requests"] >= len(prompts) + 1
+    assert m["active_requests"] == 0 and m["failed_requests"] == 0
+
+
+def test_two_rank_server_rejects_prompt_shorter_than_ranks(server):
+    _, port, _, _, _ = server
+    with pytest.raises(urllib.error.HTTPError) as ei:
+        _complete(port, "a", 2)
+    assert ei.value.code == 400
+    assert "must be >= num_domains (2)" in ei.value.read().decode()
+
+
+def test_two_rank_server_exits_on_interrupt(server):
+    """Ctrl-C reaches every rank through torchrun; each rank leaves its loop without a
+    traceback (torchrun itself still reports the signal in its own exit status)."""
+    _, _, _, proc, log = server
+    proc.send_signal(signal.SIGINT)
+    proc.wait(timeout=60)
+    text = log.read_text()
+    assert "[rank0]: Traceback" not in text and "[rank1]: Traceback" not in text, text[-3000:]
