@@ -1,0 +1,100 @@
+"""KV arena bookkeeping and token sampling on CPU.
+
+Parity: the reference's cache tests (rust/src/model/cache.rs:447-625: block table capacity,
+sharded growth) and reserved-slab capacity errors (self_driving.rs:146-331), and its sampling
+rules (rust/src/model/sampling.rs:8-119: greedy at temperature 0, top-p keeps the most likely
+token).
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from hetero_cp_ringattn_b200.errors import CapacityError
+from hetero_cp_ringattn_b200.kv.arena import KvArenaManager, PageAllocator
+from hetero_cp_ringattn_b200.models.sampling import sample_token
+
+
+def test_page_allocator_exhaustion_and_reuse():
+    a = PageAllocator(4, 128)
+    p = a.alloc(3, req_id=1)
+    assert len(set(p)) == 3 and a.free_pages == 1
+    assert all(a.owner[x] == 1 for x in p)
+    with pytest.raises(CapacityError):
+        a.alloc(2, req_id=2)
+    a.free(p[:2])
+    q = a.alloc(3, req_id=2)
+    assert set(p[:2]) <= set(q) and a.free_pages == 0
+
+
+def test_arena_reserve_extend_release():
+    m = KvArenaManager(num_pages=8, page_size=128, num_layers=3)
+    pos = np.arange(10, 110)
+    rk = m.reserve(7, n_prefill=100, capacity_slots=200, positions=pos)
+    assert len(rk.pages) == 2 and rk.capacity == 256
+    assert (rk.layer_counts == 100).all()
+    assert (rk.slot_pos[:, :100] == pos[None]).all() and (rk.slot_pos[:, 100:] == -1).all()
+    with pytest.raises(CapacityError):
+        m.reserve(7, 1, 1)
+    # growth on one layer only (a sharded decode row), then a session extension
+    rk.slot_pos[1, 100] = 500
+    rk.layer_counts[1] += 1
+    m.extend(7, 300)
+    assert len(rk.pages) == 4 and rk.slot_pos.shape == (3, 512)
+    assert rk.slot_pos[1, 100] == 500 and (rk.slot_pos[:, :100] == pos[None]).all()
+    assert m.alloc.free_pages == 4
+    assert m.release(7) and not m.release(7)
+    assert m.alloc.free_pages == 8
+    with pytest.raises(CapacityError):
+        m.get(7)
+
+
+def test_reserved_slab_full_raises():
+    m = KvArenaManager(num_pages=2, page_size=128, num_layers=2)
+    rk = m.reserve(1, n_prefill=127, capacity_slots=128)
+    rk.check_room(0)                 # one slot left
+    rk.layer_counts[0] += 1
+    with pytest.raises(CapacityError):
+        rk.check_room(0)
+    rk.check_room(1)
+
+
+def test_decode_past_horizon_raises():
+    from hetero_cp_ringattn_b200.config import preset
+    from hetero_cp_ringattn_b200.models.llama import LlamaCPEngine
+    from hetero_cp_ringattn_b200.models.weights import ModelWeights, PreparedWeights
+    cfg = preset("tiny")
+    w = ModelWeights.random_init(cfg, seed=0, dtype=torch.float32, std=0.2)
+    eng = LlamaCPEngine(cfg, PreparedWeights.from_weights(w, dtype=torch.float32),
+                        device=torch.device("cpu"), max_context=128)
+    tok, _ = eng.prefill(1, torch.arange(9), [9], decode_horizon=2)
+    tok = eng.decode_step([1], tok)
+    tok = eng.decode_step([1], tok)
+    with pytest.raises(CapacityError):
+        eng.decode_step([1], tok)
+
+
+def test_greedy_and_degenerate_top_p_pick_argmax():
+    logits = torch.tensor([0.1, 3.0, -1.0, 2.9])
+    assert sample_token(logits) == 1
+    g = torch.Generator().manual_seed(0)
+    assert all(sample_token(logits, 1.0, 1e-6, generator=g) == 1 for _ in range(50))
+
+
+def test_temperature_sampling_follows_softmax():
+    logits = torch.tensor([0.0, 1.0, 2.0, -0.5])
+    g = torch.Generator().manual_seed(1)
+    n = 20000
+    counts = np.bincount([sample_token(logits, 1.0, generator=g) for _ in range(n)], minlength=4)
+    p = torch.softmax(logits, -1).numpy()
+    assert np.abs(counts / n - p).max() < 0.015
+
+
+def test_top_p_samples_only_the_nucleus():
+    # probabilities ~ [0.64, 0.24, 0.09, 0.03]: top_p 0.8 keeps the first two
+    logits = torch.log(torch.tensor([0.64, 0.24, 0.09, 0.03]))
+    g = torch.Generator().manual_seed(2)
+    draws = [sample_token(logits, 1.0, 0.8, generator=g) for _ in range(4000)]
+    assert set(draws) == {0, 1}
+    frac0 = draws.count(0) / len(draws)
+    assert abs(frac0 - 0.64 / 0.88) < 0.03
