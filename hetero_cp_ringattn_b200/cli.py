@@ -165,6 +165,7 @@ def _raise_interrupt(signum, frame):
 
 def cmd_serve(args) -> int:
     import torch.distributed as dist
+    from .errors import RingError
     from .models.llama import LlamaCPEngine
     from .parallel.capacity import query_device_capacity_mb
     from .serve import protocol as P
@@ -174,6 +175,9 @@ def cmd_serve(args) -> int:
     from .serve.worker import Worker
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
+    if args.num_domains is not None and args.num_domains != world:
+        raise SystemExit(f"--num-domains {args.num_domains} but WORLD_SIZE is {world} "
+                         f"(launch one process per domain with torchrun)")
     dev = _device(args)
     group = None
     from datetime import timedelta
@@ -210,15 +214,36 @@ def cmd_serve(args) -> int:
                          max_batch_size=args.max_batch_size,
                          activation_reserve_mb=args.activation_reserve_mb,
                          session_continuation_tokens=args.session_continuation_tokens,
-                         trace_jsonl=args.trace_jsonl, eos_ids=cfg.eos_token_id)
+                         trace_jsonl=args.trace_jsonl, eos_ids=cfg.eos_token_id,
+                         export_logits_dir=args.export_logits)
     coord = Coordinator(worker, control, tok, cfg, ca, capacities_mb=caps)
     prompts = []
     if args.prompt:
         prompts.append(args.prompt)
+    if args.prompt_file:
+        prompts.append(open(args.prompt_file).read())
     if args.prompts_file:
         prompts += [ln.rstrip("\n") for ln in open(args.prompts_file) if ln.strip()]
+    ints = (lambda v: [int(x) for x in v.split(",") if x.strip()] if v else None)
+    status = 0
     try:
-        if prompts and not args.http_addr:
+        if args.continuation_segment:
+            ids = ints(args.prompt_token_ids) or tok.encode(prompts[0] if prompts else "hello")
+            try:
+                meta = coord.continuation_e2e(args.continuation_request_id, ids,
+                                              ints(args.continuation_segment), args.max_tokens,
+                                              ints(args.continuation_capacity_tickets))
+            except RingError as e:
+                print(json.dumps({"continuation_e2e_failed": str(e)}), flush=True)
+                status = 1
+            else:
+                print(json.dumps({"continuation_e2e": meta}), flush=True)
+        elif args.prompt_token_ids and not args.http_addr:
+            r = coord.generate(ints(args.prompt_token_ids), args.max_tokens, args.temperature,
+                               args.top_p)
+            print(json.dumps({"prompt_token_ids": ints(args.prompt_token_ids),
+                              "text": tok.decode(r.get("tokens", [])), **r}), flush=True)
+        elif prompts and not args.http_addr:
             for p in prompts:
                 r = coord.generate(tok.encode(p), args.max_tokens, args.temperature, args.top_p)
                 print(json.dumps({"prompt": p, "text": tok.decode(r.get("tokens", [])), **r}), flush=True)
@@ -233,7 +258,7 @@ def cmd_serve(args) -> int:
         # the workers reached Shutdown: they close after a barrier, so close with one too
         workers_stopped_cleanly = coord.shutdown()
     eng.close(sync=workers_stopped_cleanly)
-    return 0
+    return status
 
 
 def cmd_compare_logits(args) -> int:
@@ -349,6 +374,17 @@ def main(argv: Optional[List[str]] = None) -> int:
     s.add_argument("--activation-reserve-mb", type=int, default=1536)
     s.add_argument("--session-continuation-tokens", type=int, default=64)
     s.add_argument("--http-addr", default=None)
+    s.add_argument("--prompt-file", default=None, help="one prompt: the whole file")
+    s.add_argument("--num-domains", type=int, default=None,
+                   help="expected number of ranks (checked against WORLD_SIZE)")
+    s.add_argument("--export-logits", default=None, metavar="DIR",
+                   help="per-request logits dumps: DIR/request_<id>/<name>.f32le + meta.json")
+    s.add_argument("--prompt-token-ids", default=None, help="comma-separated prompt token ids")
+    s.add_argument("--continuation-segment", default=None,
+                   help="comma-separated token ids: run the continuation end-to-end check")
+    s.add_argument("--continuation-request-id", type=int, default=1)
+    s.add_argument("--continuation-capacity-tickets", default=None,
+                   help="comma-separated tickets per rank (default: the handshake capacities)")
     s.set_defaults(fn=cmd_serve)
     ch = sub.add_parser("compare-hidden")
     ch.add_argument("a")

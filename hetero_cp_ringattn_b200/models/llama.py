@@ -498,14 +498,8 @@ class LlamaCPEngine:
 
     # ------------------------------------------------------------------ continuation (sessions)
     def _segment_chunks(self, S: int, tickets: Sequence[int]) -> List[int]:
-        from ..parallel.capacity import allocate_by_capacity
-        if S >= self.world:
-            return allocate_by_capacity(S, list(tickets))
-        order = sorted(range(self.world), key=lambda r: (-int(tickets[r]), r))
-        out = [0] * self.world
-        for r in order[:S]:
-            out[r] = 1
-        return out
+        from ..parallel.capacity import continuation_split
+        return continuation_split(S, tickets)
 
     @torch.no_grad()
     def append(self, req_id: int, tokens: torch.Tensor, position_ids: Sequence[int],

@@ -19,7 +19,7 @@ from __future__ import annotations
 
 import dataclasses
 import os
-from typing import Optional, Sequence
+from typing import List, Optional, Sequence
 
 from ..errors import CapacityError, RingError
 
@@ -260,3 +260,18 @@ def _available_ram_mb() -> int:
         return (os.sysconf("SC_PAGE_SIZE") * os.sysconf("SC_AVPHYS_PAGES")) // (1024 * 1024)
     except (ValueError, OSError):
         return 0
+
+
+def continuation_split(segment_len: int, tickets: Sequence[int]) -> List[int]:
+    """Tokens of a continuation segment per rank, in rank order (the segment is cut into
+    contiguous pieces, so each rank's new rows stay position-ordered). Long segments follow the
+    capacity tickets (largest remainder); a segment shorter than the number of ranks gives one
+    token each to the ranks with the most tickets (ties: lower rank)."""
+    n = len(tickets)
+    if segment_len >= n:
+        return allocate_by_capacity(segment_len, list(tickets))
+    order = sorted(range(n), key=lambda r: (-int(tickets[r]), r))
+    out = [0] * n
+    for r in order[:segment_len]:
+        out[r] = 1
+    return out

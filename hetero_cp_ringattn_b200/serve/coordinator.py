@@ -27,8 +27,9 @@ from typing import Dict, List, Optional, Sequence
 from ..errors import AdmissionError, CapacityError, ProtocolError, RingError
 from ..models.sampling import sample_token
 from ..parallel.capacity import (DEFAULT_ACTIVATION_RESERVE_MB, KvLedger, UNKNOWN_CAPACITY,
-                                 chunk_sizes)
+                                 chunk_sizes, continuation_split)
 from . import protocol as P
+from .logits_dump import export_logits_dump
 from .scheduler import ActiveRequest, BatchScheduler, Job
 
 log = logging.getLogger("hcp.coordinator")
@@ -45,6 +46,7 @@ class CoordinatorArgs:
     session_continuation_tokens: int = 64
     trace_jsonl: Optional[str] = None
     eos_ids: Optional[List[int]] = None
+    export_logits_dir: Optional[str] = None  # per-request logits dumps (coordinator.rs:1170)
 
 
 class TraceSink:
@@ -184,6 +186,12 @@ class Coordinator:
             raise
         self.trace.emit("prefill_accepted", request=rid, chunks=chunks,
                         hops_per_prefill=self.cfg.num_layers * max(0, self.world - 1))
+        if self.args.export_logits_dir and self.worker.last_logits is not None:
+            export_logits_dump(self._dump_dir(rid), {"prefill_last_logits": self.worker.last_logits}, {
+                "mode": "service", "device": "distributed-workers", "request_id": rid,
+                "session_id": job.session_id, "keep_kv": job.keep_kv, "domains": self.world,
+                "layers": self.cfg.num_layers, "prompt_tokens": len(job.prompt_ids),
+                "prefill_argmax": int(resp.token)})
         req = ActiveRequest(job=job, chunks=chunks, next_position=len(job.prompt_ids))
         self._emit_token(req, resp.token)
 
@@ -195,11 +203,102 @@ class Coordinator:
         seg = [sess.last_token] + list(job.prompt_ids)
         n = len(seg)
         positions = list(range(sess.context_len, sess.context_len + n))
-        resp = self.run_command(P.StationaryContinuation(rid, seg, positions,
-                                                         self._tickets(sess.chunks), 0))
+        tickets = self._tickets(sess.chunks)
+        resp = self.run_command(P.StationaryContinuation(rid, seg, positions, tickets, 0))
+        if self.args.export_logits_dir and self.worker.last_logits is not None:
+            export_logits_dump(self._dump_dir(rid), {"continuation_last_logits": self.worker.last_logits}, {
+                "mode": "service", "device": "distributed-workers", "request_id": rid,
+                "append_request_id": job.request_id, "session_id": job.session_id,
+                "domains": self.world, "layers": self.cfg.num_layers, "tickets": tickets,
+                "capacity_tickets": tickets, "starter_domain": 0,
+                "continuation_offsets_by_domain": self._offsets_by_domain(n, tickets),
+                "continuation_base_position": sess.context_len, "continuation_tokens": n,
+                "continuation_argmax": int(resp.token)})
         job.request_id = rid
         req = ActiveRequest(job=job, chunks=sess.chunks, next_position=sess.context_len + n)
         self._emit_token(req, resp.token)
+
+    def _dump_dir(self, request_id: int) -> str:
+        import os
+        return os.path.join(self.args.export_logits_dir, f"request_{request_id}")
+
+    def _snapshot_logits(self):
+        lg = self.worker.last_logits
+        return None if lg is None else lg.detach().float().reshape(-1).cpu().clone()
+
+    def _offsets_by_domain(self, n: int, tickets: Sequence[int]) -> List[List[int]]:
+        """Segment offsets stored by each rank (the engine's contiguous continuation split)."""
+        out, o = [], 0
+        for c in continuation_split(n, tickets):
+            out.append(list(range(o, o + c)))
+            o += c
+        return out
+
+    def continuation_e2e(self, request_id: int, prompt_ids: Sequence[int], segment: Sequence[int],
+                         max_tokens: int, tickets: Optional[Sequence[int]] = None) -> dict:
+        """The reference's experimental continuation run (coordinator.rs:1973-2245, CLI
+        `--continuation-segment`): prefill the prompt (vanilla layout, `--chunk-sizes` or an even
+        split), decode its first token, prefill `segment` as a continuation right after it,
+        then greedy-decode `max_tokens - 2` more. Logits of the prefill, of the decode step and
+        of the continuation go to `export_logits_dir` when it is set."""
+        if max_tokens < 2:
+            raise AdmissionError("continuation E2E needs --max-tokens >= 2")
+        if not segment:
+            raise AdmissionError("continuation E2E needs a non-empty segment")
+        if self.args.strategy != "vanilla":
+            raise AdmissionError("--continuation-segment requires the vanilla ring strategy")
+        L, n, N = len(prompt_ids), len(segment), self.world
+        if self.args.chunk_sizes:
+            chunks = list(self.args.chunk_sizes)
+            if len(chunks) != N or sum(chunks) != L:
+                raise AdmissionError(f"--chunk-sizes {chunks} must match domains {N} and prompt "
+                                     f"length {L}")
+        else:
+            c = max(1, -(-L // N))
+            chunks = [max(0, min(L, (i + 1) * c) - min(L, i * c)) for i in range(N)]
+            chunks[-1] = L - sum(chunks[:-1])
+        if 0 in chunks:
+            raise AdmissionError("continuation E2E requires a non-zero chunk per domain")
+        if not tickets:
+            known = [int(c) for c in self.capacities_mb if c != UNKNOWN_CAPACITY]
+            tickets = [max(1, int(c)) for c in self.capacities_mb] if len(known) == N else [1] * N
+        if len(tickets) != N:
+            raise AdmissionError(f"{len(tickets)} capacity tickets for {N} domains")
+        tickets = [int(t) for t in tickets]
+        rid = int(request_id)
+        horizon = max_tokens + self.args.session_continuation_tokens
+        resp = self.run_command(P.Prefill(rid, list(prompt_ids), chunks, "vanilla", horizon,
+                                          tickets, True))
+        prefill_logits = self._snapshot_logits()
+        decode_token = int(resp.token)
+        generated = [decode_token]
+        try:
+            d = self.run_command(P.Decode(rid, decode_token))
+            decode_logits = self._snapshot_logits()  # the decode graph reuses its buffer
+            decode_argmax = int(d.token)
+            positions = list(range(L + 1, L + 1 + n))
+            c = self.run_command(P.StationaryContinuation(rid, list(segment), positions, tickets, 0))
+            cont_logits = self._snapshot_logits()
+            nxt = int(c.token)
+            generated.append(nxt)
+            for _ in range(max_tokens - 2):
+                nxt = int(self.run_command(P.Decode(rid, nxt)).token)
+                generated.append(nxt)
+        finally:
+            self.run_command(P.ReleaseRequest(rid))
+        meta = {"mode": "production-nvlink", "device": "distributed-workers", "request_id": rid,
+                "domains": N, "layers": self.cfg.num_layers, "tickets": tickets,
+                "capacity_tickets": tickets, "prefix_splits": chunks, "starter_domain": 0,
+                "continuation_offsets_by_domain": self._offsets_by_domain(n, tickets),
+                "decode_token": decode_token, "prefill_argmax": decode_token,
+                "decode_argmax": decode_argmax, "continuation_argmax": generated[1],
+                "generated_ids": generated}
+        if self.args.export_logits_dir:
+            arts = {k: v for k, v in (("prefill_last_logits", prefill_logits),
+                                      ("decode_logits", decode_logits),
+                                      ("continuation_last_logits", cont_logits)) if v is not None}
+            export_logits_dump(self.args.export_logits_dir, arts, meta)
+        return meta
 
     def _emit_token(self, req: ActiveRequest, argmax_token: int) -> None:
         job = req.job

@@ -165,3 +165,37 @@ def test_http_api(stack):
         srv.stop()
         stop.set()
         loop.join(timeout=5)
+
+
+def test_continuation_e2e_and_logits_dumps(stack, tmp_path):
+    """The reference's experimental continuation run (coordinator.rs:1973-2245) on one rank:
+    prefill, one decode, a continuation segment right after it, greedy decode; the three logits
+    dumps equal the dense oracle's last-row logits of the matching prefixes."""
+    from hetero_cp_ringattn_b200.serve.logits_dump import read_raw_logits
+    cfg, w, eng, coord, tok = stack
+    coord.args.export_logits_dir = str(tmp_path / "cont")
+    try:
+        prompt = tok.encode("stationary continuation")
+        seg = tok.encode(" and more")
+        meta = coord.continuation_e2e(77, prompt, seg, max_tokens=4, tickets=[1])
+        t0 = meta["decode_token"]
+        ref_more, _ = reference_model.greedy_generate(w, torch.tensor(prompt + [t0] + seg), 2)
+        assert meta["generated_ids"] == [t0] + ref_more
+        d = tmp_path / "cont"
+        for name, ids in (("prefill_last_logits", prompt), ("decode_logits", prompt + [t0]),
+                          ("continuation_last_logits", prompt + [t0] + seg)):
+            got = read_raw_logits(str(d / f"{name}.f32le"))
+            ref = reference_model.forward(w, torch.tensor(ids), last_only=True)[0]
+            assert got.shape == (cfg.vocab_size,)
+            assert abs(got - ref.numpy()).max() < 1e-3, name
+        m = json.loads((d / "meta.json").read_text())
+        assert m["generated_ids"] == meta["generated_ids"] and m["prefix_splits"] == [len(prompt)]
+        assert m["continuation_offsets_by_domain"] == [list(range(len(seg)))]
+        assert 77 not in eng.reqs  # released
+        # the service path dumps per request
+        res = coord.generate(prompt, max_tokens=2)
+        pd = tmp_path / "cont" / f"request_{res['request_id']}"
+        assert (pd / "prefill_last_logits.f32le").exists()
+        assert json.loads((pd / "meta.json").read_text())["prefill_argmax"] == res["tokens"][0]
+    finally:
+        coord.args.export_logits_dir = None

@@ -142,3 +142,39 @@ def test_two_rank_server_exits_on_interrupt(server):
     proc.wait(timeout=60)
     text = log.read_text()
     assert "[rank0]: Traceback" not in text and "[rank1]: Traceback" not in text, text[-3000:]
+
+
+def test_two_rank_continuation_e2e_cli(tmp_path):
+    """`serve --continuation-segment` under torchrun with two ranks and uneven tickets: the
+    generated ids and the three logits dumps match the dense oracle."""
+    import numpy as np
+    cfg = preset("tiny")
+    w = ModelWeights.random_init(cfg, seed=6, dtype=torch.float32, std=0.2)
+    mdir = tmp_path / "model"
+    w.save(str(mdir))
+    dump = tmp_path / "dump"
+    prompt = list(range(3, 24))
+    seg = [40, 41, 42, 43, 44]
+    env = dict(os.environ, HCP_QUIC_TIMEOUT_SECS="60", PYTHONPATH=REPO, OMP_NUM_THREADS="2")
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2",
+           "--master-addr", "127.0.0.1", "--master-port", str(_port()),
+           "-m", "hetero_cp_ringattn_b200", "serve", "--model-dir", str(mdir), "--device", "cpu",
+           "--max-context", "256", "--num-domains", "2", "--max-tokens", "4",
+           "--prompt-token-ids", ",".join(map(str, prompt)),
+           "--continuation-segment", ",".join(map(str, seg)),
+           "--continuation-request-id", "9", "--continuation-capacity-tickets", "3,1",
+           "--export-logits", str(dump)]
+    out = subprocess.run(cmd, cwd=REPO, env=env, capture_output=True, text=True, timeout=300)
+    assert out.returncode == 0, out.stdout[-2000:] + out.stderr[-3000:]
+    line = [ln for ln in out.stdout.splitlines() if ln.startswith('{"continuation_e2e"')][0]
+    meta = json.loads(line)["continuation_e2e"]
+    t0 = meta["decode_token"]
+    ref_more, _ = reference_model.greedy_generate(w, torch.tensor(prompt + [t0] + seg), 2)
+    assert meta["generated_ids"] == [t0] + ref_more
+    assert meta["prefix_splits"] == [11, 10] and meta["capacity_tickets"] == [3, 1]
+    assert meta["continuation_offsets_by_domain"] == [[0, 1, 2, 3], [4]]
+    for name, ids in (("prefill_last_logits", prompt), ("decode_logits", prompt + [t0]),
+                      ("continuation_last_logits", prompt + [t0] + seg)):
+        got = np.fromfile(str(dump / f"{name}.f32le"), dtype="<f4")
+        ref = reference_model.forward(w, torch.tensor(ids), last_only=True)[0].numpy()
+        assert np.abs(got - ref).max() < 1e-3, name
