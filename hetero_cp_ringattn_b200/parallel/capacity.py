@@ -242,8 +242,9 @@ def query_device_capacity_mb(device: str = "cuda") -> int:
                 idx = torch.device(device).index
                 free, _ = torch.cuda.mem_get_info(idx if idx is not None else torch.cuda.current_device())
                 return int(free // (1024 * 1024))
-        except Exception:
-            pass
+        except (RuntimeError, ValueError) as e:  # no usable device: capacity unknown
+            import logging
+            logging.getLogger("hcp.capacity").warning("capacity probe of %s failed: %s", device, e)
         return UNKNOWN_CAPACITY
     return _available_ram_mb() // 4
 

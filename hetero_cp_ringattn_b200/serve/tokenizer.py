@@ -8,6 +8,7 @@ with them.
 
 from __future__ import annotations
 
+import logging
 import os
 from typing import List, Optional
 
@@ -45,6 +46,8 @@ def load_tokenizer(model_dir: Optional[str], vocab_size: int):
         if os.path.exists(p):
             try:
                 return HfTokenizer(p)
-            except Exception:
-                pass
+            except Exception as e:  # any parse / import failure: say so, then fall back
+                logging.getLogger("hcp.tokenizer").warning(
+                    "could not load %s (%s: %s); using the byte tokenizer", p,
+                    type(e).__name__, e)
     return ByteTokenizer(vocab_size)
