@@ -134,29 +134,81 @@ def cmd_infer(args) -> int:
         tok0 = load_tokenizer(args.model_dir, cfg0.vocab_size)
         text = open(args.prompt_file).read() if args.prompt_file else (args.prompt or "hello")
         return _debug_exports(args, dev, torch.tensor(tok0.encode(text), dtype=torch.int64))
+    import torch.distributed as dist
+    from .models.sampling import sample_token
+    from .parallel.capacity import chunk_sizes
+    rank, world, group = _init_ranks(dev, args.num_domains)
     cfg, w = _load_model(args, dev)
     tok = load_tokenizer(args.model_dir, cfg.vocab_size)
     prompt = args.prompt
     if args.prompt_file:
         prompt = open(args.prompt_file).read()
     ids = torch.tensor(tok.encode(prompt or "hello"), dtype=torch.int64)
-    eng = LlamaCPEngine(cfg, w, device=dev, max_context=max(args.max_context, ids.numel()),
-                        max_batch=1, decode_reserve=args.max_tokens + 8)
-    first, logits = eng.prefill(1, ids, [ids.numel()], decode_horizon=max(1, args.max_tokens),
-                                return_logits=True)
-    rows = [logits.float().cpu()]
-    out = [int(first)]
-    cur = first
-    for _ in range(args.max_tokens - 1):
-        cur = eng.decode_step([1], cur)
-        out.append(int(cur.view(-1)[0]))
-        if args.export_logits:
-            rows.append(eng.last_logits(1)[0].float().cpu())
-    if args.export_logits:
-        write_logits(args.export_logits, rows)
-    print(json.dumps({"prompt_tokens": ids.numel(), "tokens": out, "text": tok.decode(out)}))
-    eng.close()
+    ratio = [int(x) for x in args.ratio.split(":")] if args.ratio else None
+    chunks = chunk_sizes(ids.numel(), world, ratio=ratio,
+                         explicit=[int(x) for x in args.chunk_sizes.split(",")] if args.chunk_sizes else None)
+    eng = LlamaCPEngine(cfg, w, rank=rank, world=world, device=dev, group=group,
+                        max_context=max(args.max_context, ids.numel()), max_batch=1,
+                        decode_reserve=args.max_tokens + 8)
+    gen = torch.Generator().manual_seed(args.seed)
+
+    def pick(argmax_tok, logits):
+        """Greedy uses the engine's (identical on every rank) argmax; sampling happens on rank 0
+        and the token is broadcast so every rank feeds the same one."""
+        if args.temperature <= 0:
+            return int(argmax_tok)
+        t = torch.tensor([sample_token(logits.float().cpu(), args.temperature, args.top_p, gen)
+                          if rank == 0 else 0])
+        if world > 1:
+            dist.broadcast(t, src=0, group=group)
+        return int(t[0])
+
+    try:
+        first, logits = eng.prefill(1, ids, chunks, args.ring_strategy,
+                                    decode_horizon=max(1, args.max_tokens), return_logits=True,
+                                    tickets=ratio)
+        rows = [logits.float().cpu()]
+        out = [pick(first, logits)]
+        for _ in range(args.max_tokens - 1):
+            cur = torch.tensor([out[-1]], dtype=torch.int64, device=dev)
+            nxt = eng.decode_step([1], cur)
+            lg = eng.last_logits(1)[0]
+            if args.export_logits:
+                rows.append(lg.float().cpu())
+            out.append(pick(nxt.view(-1)[0], lg))
+        if rank == 0:
+            if args.export_logits:
+                write_logits(args.export_logits, rows)
+            print(json.dumps({"prompt_tokens": ids.numel(), "tokens": out, "text": tok.decode(out),
+                              "chunks": chunks, "world": world}))
+    finally:
+        eng.close()
+        if world > 1:
+            dist.destroy_process_group()
     return 0
+
+
+def _init_ranks(dev: torch.device, num_domains: Optional[int] = None):
+    """(rank, world, gloo control group or None) from the torchrun environment. Multi-rank runs
+    get an NCCL (GPU) or gloo (CPU) default group plus a gloo group for host control messages,
+    with HCP_QUIC_TIMEOUT_SECS as the timeout of both."""
+    import torch.distributed as dist
+    from datetime import timedelta
+    from .config import EnvConfig
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if num_domains is not None and num_domains != world:
+        raise SystemExit(f"--num-domains {num_domains} but WORLD_SIZE is {world} "
+                         f"(launch one process per domain with torchrun)")
+    if world == 1:
+        return rank, world, None
+    timeout = timedelta(seconds=EnvConfig.from_env().control_timeout_s)
+    if dev.type == "cuda":
+        torch.cuda.set_device(dev)
+        dist.init_process_group("nccl", device_id=dev, timeout=timeout)
+    else:
+        dist.init_process_group("gloo", timeout=timeout)
+    return rank, world, dist.new_group(backend="gloo", timeout=timeout)
 
 
 def _raise_interrupt(signum, frame):
@@ -164,7 +216,6 @@ def _raise_interrupt(signum, frame):
 
 
 def cmd_serve(args) -> int:
-    import torch.distributed as dist
     from .errors import RingError
     from .models.llama import LlamaCPEngine
     from .parallel.capacity import query_device_capacity_mb
@@ -173,23 +224,8 @@ def cmd_serve(args) -> int:
     from .serve.http_server import ApiServer, ApiState
     from .serve.tokenizer import load_tokenizer
     from .serve.worker import Worker
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    if args.num_domains is not None and args.num_domains != world:
-        raise SystemExit(f"--num-domains {args.num_domains} but WORLD_SIZE is {world} "
-                         f"(launch one process per domain with torchrun)")
     dev = _device(args)
-    group = None
-    from datetime import timedelta
-    from .config import EnvConfig
-    timeout = timedelta(seconds=EnvConfig.from_env().control_timeout_s)  # HCP_QUIC_TIMEOUT_SECS
-    if world > 1:
-        if dev.type == "cuda":
-            torch.cuda.set_device(dev)
-            dist.init_process_group("nccl", device_id=dev, timeout=timeout)
-        else:
-            dist.init_process_group("gloo", timeout=timeout)
-        group = dist.new_group(backend="gloo", timeout=timeout)
+    rank, world, group = _init_ranks(dev, args.num_domains)
     cfg, w = _load_model(args, dev)
     eng = LlamaCPEngine(cfg, w, rank=rank, world=world, device=dev, group=group,
                         max_context=args.max_context, max_batch=args.max_batch_size)
@@ -352,6 +388,13 @@ def main(argv: Optional[List[str]] = None) -> int:
     i.add_argument("--prompt-file", default=None)
     i.add_argument("--max-tokens", type=int, default=10)
     i.add_argument("--export-logits", default=None)
+    i.add_argument("--temperature", type=float, default=0.0)
+    i.add_argument("--top-p", type=float, default=1.0)
+    i.add_argument("--num-domains", type=int, default=None,
+                   help="expected number of ranks (checked against WORLD_SIZE)")
+    i.add_argument("--chunk-sizes", default=None)
+    i.add_argument("--ratio", default=None, help="capacity ratio, e.g. 5:5:1")
+    i.add_argument("--ring-strategy", default="vanilla", choices=["vanilla", "striped", "zigzag"])
     i.add_argument("--export-hidden-states", default=None, metavar="DIR",
                    help="per-layer K/V after prefill + first decode step hidden states (f32 oracle)")
     i.add_argument("--prefill-debug", default=None, metavar="DIR",

@@ -76,3 +76,20 @@ def test_generate_batch_matches_single_requests():
         ref, _ = reference_model.greedy_generate(w, p, 4)
         assert o.tolist() == ref
     assert not eng.reqs
+
+
+def test_infer_sampling_is_seeded(tmp_path, capsys):
+    cfg = preset("tiny")
+    w = ModelWeights.random_init(cfg, seed=4, dtype=torch.float32, std=0.2)
+    mdir = tmp_path / "model"
+    w.save(str(mdir))
+    args = ["infer", "--model-dir", str(mdir), "--device", "cpu", "--prompt", "sampling",
+            "--max-tokens", "6", "--temperature", "1.5", "--top-p", "0.9", "--seed", "3"]
+    outs = []
+    for _ in range(2):
+        assert main(args) == 0
+        outs.append(json.loads(capsys.readouterr().out.strip().splitlines()[-1])["tokens"])
+    assert outs[0] == outs[1] and len(outs[0]) == 6
+    assert main(args[:-1] + ["4"]) == 0
+    other = json.loads(capsys.readouterr().out.strip().splitlines()[-1])["tokens"]
+    assert len(other) == 6

@@ -178,3 +178,33 @@ def test_two_rank_continuation_e2e_cli(tmp_path):
         got = np.fromfile(str(dump / f"{name}.f32le"), dtype="<f4")
         ref = reference_model.forward(w, torch.tensor(ids), last_only=True)[0].numpy()
         assert np.abs(got - ref).max() < 1e-3, name
+
+
+def test_infer_under_torchrun_matches_single_process(tmp_path):
+    """`infer` on two ranks (zigzag, 3:1) exports the same logits and tokens as on one rank, so
+    `compare-logits` passes between a distributed and a single-device run."""
+    cfg = preset("tiny")
+    w = ModelWeights.random_init(cfg, seed=8, dtype=torch.float32, std=0.2)
+    mdir = tmp_path / "model"
+    w.save(str(mdir))
+    env = dict(os.environ, PYTHONPATH=REPO, OMP_NUM_THREADS="2")
+    base = ["-m", "hetero_cp_ringattn_b200", "infer", "--model-dir", str(mdir), "--device", "cpu",
+            "--prompt", "distributed logits export check", "--max-tokens", "5"]
+    one = subprocess.run([sys.executable] + base + ["--export-logits", str(tmp_path / "a.bin")],
+                         cwd=REPO, env=env, capture_output=True, text=True, timeout=300)
+    assert one.returncode == 0, one.stderr[-3000:]
+    two = subprocess.run([sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+                          "--nproc-per-node", "2", "--master-addr", "127.0.0.1",
+                          "--master-port", str(_port())] + base +
+                         ["--export-logits", str(tmp_path / "b.bin"), "--ratio", "3:1",
+                          "--ring-strategy", "zigzag", "--num-domains", "2"],
+                         cwd=REPO, env=env, capture_output=True, text=True, timeout=300)
+    assert two.returncode == 0, two.stdout[-2000:] + two.stderr[-3000:]
+    r1 = json.loads(one.stdout.strip().splitlines()[-1])
+    r2 = json.loads([ln for ln in two.stdout.splitlines() if ln.startswith("{")][-1])
+    assert r2["world"] == 2 and r2["chunks"][0] > r2["chunks"][1]
+    assert r1["tokens"] == r2["tokens"]
+    cmp_ = subprocess.run([sys.executable, "-m", "hetero_cp_ringattn_b200", "compare-logits",
+                           str(tmp_path / "a.bin"), str(tmp_path / "b.bin"), "--tolerance", "1e-3"],
+                          cwd=REPO, env=env, capture_output=True, text=True, timeout=120)
+    assert cmp_.returncode == 0 and json.loads(cmp_.stdout)["passed"], cmp_.stdout
