@@ -46,7 +46,7 @@ from ..ops._ext import native
 from ..parallel.schedule import FrozenKvAssigneeSchedule
 from ..parallel.strategy import RingStrategy, build_assignment, build_domain_positions
 from ..utils import launches
-from ..utils.perf import PerfLog
+from ..utils.perf import PerfLog, peak_bf16_tflops
 from .weights import PreparedWeights
 
 
@@ -276,6 +276,7 @@ class LlamaCPEngine:
         sent = T * row_bytes * (self.world - 1)
         recv = (Lp - T) * row_bytes
         attn_ms = ev[2].elapsed_time(ev[3])
+        tflops = 4.0 * self.H * self.D * float(np.sum(st.positions + 1)) / max(attn_ms, 1e-6) / 1e9
         self.perf.emit("ring_attention", domain=self.rank, layer=layer, request=st.req_id,
                        total_ms=ev[0].elapsed_time(ev[4]), qkv_ms=ev[0].elapsed_time(ev[1]),
                        send_ms=ev[1].elapsed_time(ev[2]), local_compute_ms=attn_ms,
@@ -284,8 +285,7 @@ class LlamaCPEngine:
                        wire_sent_bytes=sent, wire_recv_bytes=recv, micro_blocks=-(-Lp // 128),
                        num_domains=self.world, seq_len=T, overlap=True,
                        nvlink_gbps=sent / max(ev[1].elapsed_time(ev[2]), 1e-6) / 1e6,
-                       attn_tflops=4.0 * self.H * self.D * float(np.sum(st.positions + 1)) /
-                       max(attn_ms, 1e-6) / 1e9)
+                       attn_tflops=tflops, roofline_frac=tflops / peak_bf16_tflops())
 
     def _first_token_cuda(self, st: RequestState, x: torch.Tensor, return_logits: bool):
         dev = self.device
@@ -416,12 +416,53 @@ class LlamaCPEngine:
         if B == 0:
             return tokens
         pos, owner, slot, ntok = self._decode_meta(req_ids)
+        timing = self.perf.enabled
+        if timing:
+            t0 = time.perf_counter()
+            if self.cuda:
+                ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                ev[0].record()
         if self.cuda:
             out = self._decode_cuda(req_ids, tokens, pos, owner, slot, ntok)
         else:
             out = self._decode_host(req_ids, tokens, pos, owner)
+        if timing:
+            if self.cuda:
+                ev[1].record()
+                ev[1].synchronize()
+                ms = ev[0].elapsed_time(ev[1])
+            else:
+                ms = (time.perf_counter() - t0) * 1e3
+            self._emit_decode(req_ids, tokens, pos, owner, ms)
         self._advance(req_ids, owner, pos)
         return out
+
+    def _emit_decode(self, req_ids, tokens, pos, owner, ms: float) -> None:
+        """`stationary_decode` perf event per row (the reference's schema,
+        worker_sdk/tch_backend.rs:859-880). On the (O, LSE) exchange route every layer stores
+        this rank's partial, H x (D + 1) float32 per row, into each other rank's slot: one hop,
+        not N - 1. The whole batch step is one device-timed interval."""
+        peers = self.world - 1
+        part = self.H * (self.D + 1) * 4
+        toks = tokens.view(-1).tolist()
+        for b, rid in enumerate(req_ids):
+            st = self.reqs[rid]
+            n_msg = self.L * peers
+            sent = recv = n_msg * part
+            if self.legacy_decode:
+                # this rank's partition rows (float32 K and V) go to every peer, every layer;
+                # what arrives depends on the peers' partitions
+                rows = sum(int(kv[3].sum()) for kv in st.host_kv)
+                sent, recv = rows * 2 * self.Hkv * self.D * 4 * peers, -1
+            self.perf.emit("stationary_decode", domain=self.rank, request_id=int(rid),
+                           token=int(toks[b]), position=int(pos[b]), layers=self.L,
+                           domains=self.world, token_offset=int(st.decode_offset),
+                           decode_horizon=int(st.horizon), sends=n_msg, recvs=n_msg,
+                           wire_sent_bytes=sent, wire_recv_bytes=recv,
+                           hops_per_layer=1 if peers else 0,
+                           kv_rows_appended=int(np.sum(owner[b])), batch=len(req_ids),
+                           route="legacy_kv_resend" if self.legacy_decode else "o_lse_exchange",
+                           recv_wait_ms=0.0, process_ms=ms, send_ms=0.0, total_ms=ms)
 
     def _graph_for(self, B: int) -> "DecodeGraph":
         g = self._graphs.get(B)

@@ -41,6 +41,31 @@ class PerfLog:
                 f.write(line + "\n")
 
 
+_PEAK = None
+
+
+def peak_bf16_tflops() -> float:
+    """bf16 tensor throughput that perf events report roofline fractions against: the
+    HCP_PEAK_BF16_TFLOPS override, else the sustained cuBLAS bf16 figure of a MEASURED_PEAKS.json
+    beside the package (written by the benchmark driver on the target GPUs), else 1400 (a B200
+    under its 1 kW power cap)."""
+    global _PEAK
+    if _PEAK is None:
+        env = os.environ.get("HCP_PEAK_BF16_TFLOPS")
+        if env:
+            _PEAK = float(env)
+        else:
+            path = os.path.join(os.path.dirname(os.path.dirname(os.path.dirname(
+                os.path.abspath(__file__)))), "MEASURED_PEAKS.json")
+            try:
+                with open(path) as f:
+                    p = json.load(f)
+                _PEAK = float(p.get("bf16_tflops_sustained", p["bf16_tflops"]))
+            except (OSError, KeyError, ValueError):
+                _PEAK = 1400.0
+    return _PEAK
+
+
 class CudaTimer:
     """Device time between two points of the current stream (milliseconds)."""
 

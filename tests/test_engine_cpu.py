@@ -245,3 +245,47 @@ def test_page_size_from_environment():
                          env=EnvConfig(kv_block_size=384)).page_size == 128
     with pytest.raises(CapacityError):
         LlamaCPEngine(cfg, pw, device=torch.device("cpu"), env=EnvConfig(kv_block_size=0))
+
+
+def _perf_worker(rank, world, port, out_dir):
+    from hetero_cp_ringattn_b200.utils.perf import PerfLog
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        cfg, w = tiny_weights()
+        pw = PreparedWeights.from_weights(w, dtype=torch.float32)
+        eng = LlamaCPEngine(cfg, pw, rank=rank, world=world, device=torch.device("cpu"),
+                            max_context=256,
+                            perf_log=PerfLog(os.path.join(out_dir, f"perf{rank}.jsonl")))
+        tok, _ = eng.prefill(2, torch.arange(3, 30), [14, 13], decode_horizon=4)
+        for _ in range(3):
+            tok = eng.decode_step([2], tok)
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_decode_perf_events_two_ranks(tmp_path):
+    """HCP_PERF_LOG decode events in the reference's `stationary_decode` shape: one per step and
+    rank, with the (O, LSE) exchange's message count and bytes."""
+    import json
+    world = 2
+    mp.start_processes(_perf_worker, args=(world, free_port(), str(tmp_path)), nprocs=world,
+                       join=True, start_method="spawn")
+    cfg = preset("tiny")
+    part = cfg.num_heads * (cfg.head_dim + 1) * 4
+    for r in range(world):
+        evs = [json.loads(l) for l in open(tmp_path / f"perf{r}.jsonl")]
+        dec = [e for e in evs if e["event"] == "stationary_decode"]
+        assert [e["position"] for e in dec] == [27, 28, 29]
+        assert [e["token_offset"] for e in dec] == [0, 1, 2]
+        for e in dec:
+            assert e["domain"] == r and e["domains"] == 2 and e["route"] == "o_lse_exchange"
+            assert e["sends"] == cfg.num_layers and e["wire_sent_bytes"] == cfg.num_layers * part
+            assert e["total_ms"] > 0 and e["decode_horizon"] == 4
+        assert sum(1 for e in evs if e["event"] == "prefill") == 1
+    # across ranks, every (token, layer) KV row is appended exactly once
+    rows = [sum(e["kv_rows_appended"] for e in map(json.loads, open(tmp_path / f"perf{r}.jsonl"))
+                if e["event"] == "stationary_decode") for r in range(world)]
+    assert sum(rows) == 3 * cfg.num_layers
