@@ -1,0 +1,140 @@
+// Python module `hetero_cp_ringattn_b200._host`: bindings of the host runtime library.
+// C++ RingError / CapacityError surface as the package's own exception classes.
+#include <algorithm>
+#include <cstring>
+
+#include <pybind11/numpy.h>
+#include <pybind11/pybind11.h>
+#include <pybind11/stl.h>
+
+#include "hcp_host.h"
+
+namespace py = pybind11;
+using namespace hcp::host;
+
+namespace {
+
+py::array_t<int64_t> ToArray(const std::vector<int64_t>& v) {
+  py::array_t<int64_t> a(py::ssize_t(v.size()));
+  if (!v.empty()) std::memcpy(a.mutable_data(), v.data(), v.size() * sizeof(int64_t));
+  return a;
+}
+
+std::vector<int64_t> FromArray(const py::array_t<int64_t, py::array::c_style | py::array::forcecast>& a) {
+  return std::vector<int64_t>(a.data(), a.data() + a.size());
+}
+
+void RaiseAs(const char* cls_name, const char* what) {
+  py::object cls = py::module_::import("hetero_cp_ringattn_b200.errors").attr(cls_name);
+  PyErr_SetString(cls.ptr(), what);
+}
+
+}  // namespace
+
+PYBIND11_MODULE(_host, m) {
+  m.doc() = "host runtime: ring layouts, capacity chunking and admission, KV growth schedule, "
+            "page allocator, batch scheduler core";
+  py::register_exception_translator([](std::exception_ptr p) {
+    try {
+      if (p) std::rethrow_exception(p);
+    } catch (const CapacityError& e) {
+      RaiseAs("CapacityError", e.what());
+    } catch (const RingError& e) {
+      RaiseAs("RingError", e.what());
+    }
+  });
+  m.attr("UNKNOWN_CAPACITY") = py::int_(kUnknownCapacity);
+
+  // layouts
+  m.def("build_assignment", [](const std::vector<int64_t>& chunks, const std::string& strategy) {
+    return ToArray(BuildAssignment(chunks, ParseStrategy(strategy)));
+  }, py::arg("chunks"), py::arg("strategy"));
+  m.def("build_domain_positions",
+        [](const py::array_t<int64_t, py::array::c_style | py::array::forcecast>& a, int64_t n) {
+          py::list out;
+          for (const auto& v : BuildDomainPositions(FromArray(a), n)) out.append(ToArray(v));
+          return out;
+        }, py::arg("assignment"), py::arg("num_domains") = -1);
+  m.def("build_inverse_perm",
+        [](const py::array_t<int64_t, py::array::c_style | py::array::forcecast>& a) {
+          return ToArray(BuildInversePerm(FromArray(a)));
+        }, py::arg("assignment"));
+
+  // capacity
+  m.def("allocate_by_capacity", &AllocateByCapacity, py::arg("prompt_len"), py::arg("capacities"));
+  m.def("equal_chunks", &EqualChunks, py::arg("prompt_len"), py::arg("n"));
+  m.def("chunk_sizes", &ChunkSizes, py::arg("prompt_len"), py::arg("num_domains"),
+        py::arg("explicit_sizes"), py::arg("capacities_mb"), py::arg("capacity_aware"),
+        py::arg("ratio"), py::arg("activation_reserve_mb"));
+  m.def("continuation_split", &ContinuationSplit, py::arg("segment_len"), py::arg("tickets"));
+  m.def("capacity_mb_to_bytes", &CapacityMbToBytes, py::arg("capacity_mb"));
+  m.def("admit_reserved_kv_bytes",
+        [](const std::vector<std::vector<uint64_t>>& caps, const std::vector<uint64_t>& budgets,
+           uint64_t hkv, uint64_t d, uint64_t elem) {
+          auto a = AdmitReservedKvBytes(caps, budgets, hkv, d, elem);
+          return py::make_tuple(a.bytes_per_token_per_layer, a.required_bytes_per_domain);
+        });
+  py::class_<KvLedger>(m, "KvLedger")
+      .def(py::init<std::vector<uint64_t>>(), py::arg("budgets"))
+      .def("try_reserve", &KvLedger::TryReserve, py::arg("request_id"), py::arg("bytes_per_domain"))
+      .def("release", &KvLedger::Release, py::arg("request_id"))
+      .def("free_bytes", &KvLedger::FreeBytes)
+      .def("holds", &KvLedger::Holds)
+      .def_property_readonly("used", &KvLedger::Used)
+      .def_property_readonly("budgets", &KvLedger::Budgets);
+
+  // schedule
+  py::class_<FrozenKvAssigneeSchedule>(m, "FrozenKvAssigneeSchedule")
+      .def(py::init<const std::vector<uint64_t>&, uint64_t, uint64_t>(), py::arg("tickets"),
+           py::arg("request_id"), py::arg("total_units"))
+      .def("assignee_for",
+           [](const FrozenKvAssigneeSchedule& s, int64_t t, int64_t l, int64_t n) -> py::object {
+             const int64_t a = s.AssigneeFor(t, l, n);
+             return a < 0 ? py::none() : py::object(py::int_(a));
+           })
+      .def("per_rank_units", &FrozenKvAssigneeSchedule::PerRankUnits)
+      .def_property_readonly("sequence", &FrozenKvAssigneeSchedule::Sequence)
+      .def_property_readonly("counts", &FrozenKvAssigneeSchedule::Counts)
+      .def_property_readonly("phase", &FrozenKvAssigneeSchedule::Phase)
+      .def("total_units", [](const FrozenKvAssigneeSchedule& s) { return s.Sequence().size(); });
+  m.def("assignee_table",
+        [](const std::vector<uint64_t>& tickets, uint64_t rid, int64_t horizon, int64_t layers) {
+          auto v = AssigneeTable(tickets, rid, horizon, layers);
+          py::array_t<int64_t> a({py::ssize_t(std::max<int64_t>(horizon, 0)),
+                                  py::ssize_t(std::max<int64_t>(layers, 0))});
+          if (!v.empty()) std::memcpy(a.mutable_data(), v.data(), v.size() * sizeof(int64_t));
+          return a;
+        }, py::arg("tickets"), py::arg("request_id"), py::arg("horizon"), py::arg("layers"));
+  m.def("stationary_layer_starters", &StationaryLayerStarters, py::arg("initial_starter"),
+        py::arg("layers"), py::arg("domains"));
+
+  // pages
+  py::class_<PageAllocator>(m, "PageAllocator")
+      .def(py::init<int64_t, int64_t>(), py::arg("num_pages"), py::arg("page_size"))
+      .def("alloc", &PageAllocator::Alloc, py::arg("n"), py::arg("request_id"))
+      .def("free", &PageAllocator::Free, py::arg("pages"))
+      .def("owner_of", &PageAllocator::OwnerOf)
+      .def_property_readonly("free_pages", &PageAllocator::FreePages)
+      .def_property_readonly("num_pages", &PageAllocator::NumPages)
+      .def_property_readonly("page_size", &PageAllocator::PageSize);
+
+  // scheduler core
+  py::class_<BatchSchedulerCore>(m, "BatchSchedulerCore")
+      .def(py::init<int64_t>(), py::arg("max_batch_size"))
+      .def("enqueue", &BatchSchedulerCore::Enqueue)
+      .def("pop_pending",
+           [](BatchSchedulerCore& s) -> py::object {
+             auto v = s.PopPending();
+             return v ? py::object(py::int_(*v)) : py::none();
+           })
+      .def("requeue_front", &BatchSchedulerCore::RequeueFront)
+      .def("activate", &BatchSchedulerCore::Activate)
+      .def("complete", &BatchSchedulerCore::Complete)
+      .def("has_capacity", &BatchSchedulerCore::HasCapacity)
+      .def("active", &BatchSchedulerCore::Active)
+      .def_property_readonly("queued", &BatchSchedulerCore::Queued)
+      .def_property_readonly("num_active", &BatchSchedulerCore::NumActive)
+      .def_property_readonly("max_batch_size", &BatchSchedulerCore::MaxBatchSize)
+      .def("wait_for_work", &BatchSchedulerCore::WaitForWork, py::arg("timeout_s"),
+           py::call_guard<py::gil_scoped_release>());
+}

@@ -17,32 +17,31 @@ from typing import Dict, List, Optional
 import numpy as np
 
 from ..errors import CapacityError
+from ..host import lib
 
 
 class PageAllocator:
+    """Page ids of this rank's arena, handed out and taken back by the native allocator
+    (`csrc/host/pages.cpp`)."""
+
     def __init__(self, num_pages: int, page_size: int):
+        self._a = lib().PageAllocator(int(num_pages), int(page_size))
         self.num_pages = int(num_pages)
         self.page_size = int(page_size)
-        self._free: List[int] = list(range(self.num_pages - 1, -1, -1))
-        self.owner: Dict[int, int] = {}
 
     @property
     def free_pages(self) -> int:
-        return len(self._free)
+        return self._a.free_pages
 
     def alloc(self, n: int, req_id: int) -> List[int]:
-        if n > len(self._free):
-            raise CapacityError(f"KV arena out of pages: need {n}, {len(self._free)} free of "
-                                f"{self.num_pages}")
-        out = [self._free.pop() for _ in range(n)]
-        for p in out:
-            self.owner[p] = req_id
-        return out
+        return list(self._a.alloc(int(n), int(req_id)))
 
     def free(self, pages: List[int]) -> None:
-        for p in pages:
-            self.owner.pop(p, None)
-            self._free.append(p)
+        self._a.free([int(p) for p in pages])
+
+    def owner_of(self, page: int) -> Optional[int]:
+        o = self._a.owner_of(int(page))
+        return None if o < 0 else o
 
 
 @dataclasses.dataclass

@@ -43,7 +43,7 @@ from ..kv.arena import KvArenaManager, RequestKv
 from ..ops import kernels as K
 from ..ops import reference as ref
 from ..ops._ext import native
-from ..parallel.schedule import FrozenKvAssigneeSchedule
+from ..parallel.schedule import assignee_table
 from ..parallel.strategy import RingStrategy, build_assignment, build_domain_positions
 from ..utils import launches
 from ..utils.perf import PerfLog, peak_bf16_tflops
@@ -166,10 +166,7 @@ class LlamaCPEngine:
             # Q-ring placement (ring.rs:1934): position p is kept by rank p % N on every layer
             owners = (first_pos + np.arange(horizon, dtype=np.int64) - first_t) % self.world
             return np.repeat(owners[:, None], self.L, axis=1)
-        sched = FrozenKvAssigneeSchedule(tickets, req_id, horizon * self.L)
-        seq = np.asarray(sched.sequence, dtype=np.int64)
-        ordinals = (sched.phase + np.arange(horizon * self.L)) % len(seq)
-        return seq[ordinals].reshape(horizon, self.L)
+        return assignee_table(tickets, req_id, horizon, self.L)
 
     # ------------------------------------------------------------------ prefill
     @torch.no_grad()

@@ -10,80 +10,60 @@ for every unit without talking to each other.
 On B200 the reference's serial hop-by-hop packet walk is replaced by parallel per-rank partial
 attention plus an (O, LSE) combine, so "starter"/"finisher" no longer route compute; the starter
 sequence is still derived (and validated) for protocol parity.
+
+The schedule is computed by the native host library (`csrc/host/schedule.cpp`).
 """
 
 from __future__ import annotations
 
 from typing import Optional, Sequence
 
-from ..errors import RingError
+import numpy as np
+
+from ..host import lib
 
 
 class FrozenKvAssigneeSchedule:
     def __init__(self, capacity_tickets: Sequence[int], request_id: int, total_kv_units: int):
-        if len(capacity_tickets) == 0:
-            raise RingError("KV assignee schedule requires at least one worker")
-        if total_kv_units == 0:
-            raise RingError("KV assignee schedule requires at least one KV unit")
-        cap_sum = sum(int(t) for t in capacity_tickets)
-        if cap_sum == 0:
-            raise RingError("KV assignee schedule requires non-zero capacity")
-        total = int(total_kv_units)
-        counts = []
-        remainders = []
-        for d, t in enumerate(capacity_tickets):
-            num = total * int(t)
-            counts.append(num // cap_sum)
-            remainders.append((d, num % cap_sum))
-        remainders.sort(key=lambda x: (-x[1], x[0]))
-        remaining = total - sum(counts)
-        for d, _ in remainders[:remaining]:
-            counts[d] += 1
-        scores = [0] * len(counts)
-        seq = []
-        for _ in range(total):
-            for i, c in enumerate(counts):
-                scores[i] += c
-            # max score, ties broken toward the lowest rank index
-            best = max(range(len(scores)), key=lambda i: (scores[i], -i))
-            scores[best] -= total
-            seq.append(best)
-        self.sequence = seq
-        self.counts = counts
-        self.phase = int(request_id) % total
+        self._s = lib().FrozenKvAssigneeSchedule([int(t) for t in capacity_tickets],
+                                                 int(request_id), int(total_kv_units))
+
+    @property
+    def sequence(self) -> list:
+        return list(self._s.sequence)
+
+    @property
+    def counts(self) -> list:
+        return list(self._s.counts)
+
+    @property
+    def phase(self) -> int:
+        return int(self._s.phase)
 
     def total_units(self) -> int:
-        return len(self.sequence)
+        return int(self._s.total_units())
 
     def assignee_for(self, token_offset: int, layer_idx: int, num_layers: int) -> Optional[int]:
-        if num_layers == 0 or layer_idx >= num_layers or layer_idx < 0 or token_offset < 0:
-            return None
-        ordinal = token_offset * num_layers + layer_idx
-        if ordinal >= len(self.sequence):
-            return None
-        return self.sequence[(self.phase + ordinal) % len(self.sequence)]
+        return self._s.assignee_for(int(token_offset), int(layer_idx), int(num_layers))
 
     def per_rank_units(self, num_ranks: int, token_offsets: range, num_layers: int) -> list:
-        out = [0] * num_ranks
-        for t in token_offsets:
-            for layer in range(num_layers):
-                a = self.assignee_for(t, layer, num_layers)
-                if a is not None:
-                    out[a] += 1
-        return out
+        if token_offsets.step != 1:
+            return [sum(1 for t in token_offsets for l in range(num_layers)
+                        if self.assignee_for(t, l, num_layers) == r) for r in range(num_ranks)]
+        return list(self._s.per_rank_units(int(num_ranks), token_offsets.start, token_offsets.stop,
+                                           int(num_layers)))
+
+
+def assignee_table(capacity_tickets: Sequence[int], request_id: int, horizon: int,
+                   num_layers: int) -> np.ndarray:
+    """[horizon, layers] rank that stores each decoded (token, layer) KV row: the frozen schedule
+    over horizon * layers units read from the request's phase."""
+    return lib().assignee_table([int(t) for t in capacity_tickets], int(request_id), int(horizon),
+                                int(num_layers))
 
 
 def stationary_layer_starters(initial_starter: int, layers: int, domains: int) -> list:
-    if domains == 0:
-        raise RingError("stationary ring requires at least one domain")
-    if initial_starter >= domains or initial_starter < 0:
-        raise RingError(f"stationary ring starter {initial_starter} out of {domains} domains")
-    out = []
-    s = initial_starter
-    for _ in range(layers):
-        out.append(s)
-        s = (s + domains - 1) % domains
-    return out
+    return list(lib().stationary_layer_starters(int(initial_starter), int(layers), int(domains)))
 
 
 def layer_finisher(starter: int, domains: int) -> int:

@@ -11,6 +11,7 @@ the attention kernels' causal skip all derive from the same assignment:
              suffix segment of floor(c_i/2) tokens (suffixes in reverse rank order).
 
 Every layout preserves exact attention; the kernels only ever see per-token global positions.
+The layouts are computed by the native host library (`csrc/host/layout.cpp`).
 """
 
 from __future__ import annotations
@@ -19,6 +20,8 @@ import enum
 from typing import Sequence
 
 import numpy as np
+
+from ..host import lib
 
 
 class RingStrategy(enum.Enum):
@@ -43,53 +46,18 @@ class RingStrategy(enum.Enum):
 def build_assignment(chunks: Sequence[int], strategy: "RingStrategy | str") -> np.ndarray:
     """Return `a` with a[p] = rank owning global position p; rank i owns chunks[i] positions."""
     strategy = RingStrategy.parse(strategy)
-    chunks = [int(c) for c in chunks]
-    seq_len = sum(chunks)
-    n = len(chunks)
-    if strategy is RingStrategy.VANILLA:
-        return np.repeat(np.arange(n, dtype=np.int64), chunks)
-    if strategy is RingStrategy.STRIPED:
-        remaining = list(chunks)
-        sched = []
-        while any(c > 0 for c in remaining):
-            for d in range(n):
-                if remaining[d] > 0:
-                    sched.append(d)
-                    remaining[d] -= 1
-        sched = np.asarray(sched, dtype=np.int64)
-        if seq_len == 0:
-            return sched
-        return sched[np.arange(seq_len) % len(sched)]
-    # zigzag
-    prefix = [c - c // 2 for c in chunks]
-    suffix = [c // 2 for c in chunks]
-    out = np.empty(seq_len, dtype=np.int64)
-    pos = 0
-    for d in range(n):
-        out[pos:pos + prefix[d]] = d
-        pos += prefix[d]
-    for d in reversed(range(n)):
-        out[pos:pos + suffix[d]] = d
-        pos += suffix[d]
-    return out
+    return lib().build_assignment([int(c) for c in chunks], strategy.value)
 
 
 def build_domain_positions(assignment: np.ndarray, num_domains: int | None = None) -> list:
     """Ordered global positions owned by each rank (local storage order)."""
-    assignment = np.asarray(assignment)
-    n = int(assignment.max()) + 1 if num_domains is None and assignment.size else (num_domains or 0)
-    return [np.nonzero(assignment == d)[0].astype(np.int64) for d in range(n)]
+    return list(lib().build_domain_positions(np.asarray(assignment, dtype=np.int64),
+                                             -1 if num_domains is None else int(num_domains)))
 
 
 def build_inverse_perm(assignment: np.ndarray) -> np.ndarray:
     """inverse[p] = index of global position p inside concat(rank0 tokens, rank1 tokens, ...)."""
-    positions = build_domain_positions(assignment)
-    inverse = np.empty(len(assignment), dtype=np.int64)
-    off = 0
-    for pos in positions:
-        inverse[pos] = np.arange(off, off + len(pos), dtype=np.int64)
-        off += len(pos)
-    return inverse
+    return lib().build_inverse_perm(np.asarray(assignment, dtype=np.int64))
 
 
 def layout_positions(chunks: Sequence[int], strategy: "RingStrategy | str") -> list:

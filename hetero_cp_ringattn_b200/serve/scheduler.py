@@ -3,16 +3,17 @@
 Parity: rust/src/distributed/scheduler.rs:18-160 (`ActiveRequest`, `BatchScheduler` with
 `enqueue`, admission up to `max_batch_size` (default 4), removal on completion) and the
 coordinator's iteration order (coordinator.rs:2563-2916: pending -> prefill (serial) -> active;
-each iteration runs one decode step for the active requests).
+each iteration runs one decode step for the active requests). The queue and the active set
+live in the native host library.
 """
 
 from __future__ import annotations
 
-import collections
 import dataclasses
-import threading
 import time
-from typing import Any, Callable, Deque, Dict, List, Optional
+from typing import Callable, Dict, List, Optional
+
+from ..host import lib
 
 
 @dataclasses.dataclass
@@ -43,50 +44,44 @@ class ActiveRequest:
 
 
 class BatchScheduler:
+    """Admission order and the active set are kept by the native scheduler core
+    (`csrc/host/scheduler.cpp`, thread safe); this wrapper holds the request objects by id."""
+
     def __init__(self, max_batch_size: int = 4):
-        if max_batch_size < 1:
-            raise ValueError("max_batch_size must be >= 1")
-        self.max_batch_size = max_batch_size
-        self.pending: Deque[Job] = collections.deque()
+        self._core = lib().BatchSchedulerCore(int(max_batch_size))
+        self.max_batch_size = int(max_batch_size)
+        self._pending: Dict[int, Job] = {}
         self.active: Dict[int, ActiveRequest] = {}
-        self.lock = threading.Lock()
-        self.cv = threading.Condition(self.lock)
 
     def enqueue(self, job: Job) -> None:
-        with self.cv:
-            self.pending.append(job)
-            self.cv.notify_all()
+        self._pending[job.request_id] = job
+        self._core.enqueue(job.request_id)
 
     def has_capacity(self) -> bool:
-        return len(self.active) < self.max_batch_size
+        return self._core.has_capacity()
 
     def pop_pending(self) -> Optional[Job]:
-        with self.lock:
-            if self.pending and self.has_capacity():
-                return self.pending.popleft()
-            return None
+        rid = self._core.pop_pending()
+        return None if rid is None else self._pending.pop(rid)
 
     def requeue_front(self, job: Job) -> None:
-        with self.lock:
-            self.pending.appendleft(job)
+        self._pending[job.request_id] = job
+        self._core.requeue_front(job.request_id)
 
     def activate(self, req: ActiveRequest) -> None:
-        with self.lock:
-            self.active[req.job.request_id] = req
+        self.active[req.job.request_id] = req
+        self._core.activate(req.job.request_id)
 
     def complete(self, request_id: int) -> Optional[ActiveRequest]:
-        with self.lock:
-            return self.active.pop(request_id, None)
+        self._core.complete(request_id)
+        return self.active.pop(request_id, None)
 
     def active_list(self) -> List[ActiveRequest]:
-        with self.lock:
-            return list(self.active.values())
+        return [self.active[i] for i in self._core.active() if i in self.active]
 
     def wait_for_work(self, timeout: float = 0.05) -> None:
-        with self.cv:
-            if not self.pending and not self.active:
-                self.cv.wait(timeout)
+        self._core.wait_for_work(float(timeout))
 
     @property
     def queued(self) -> int:
-        return len(self.pending)
+        return self._core.queued

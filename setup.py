@@ -1,4 +1,6 @@
-"""Build the sm_100a extension in-tree:  python setup.py build_ext --inplace
+"""Build the extensions in-tree:  python setup.py build_ext --inplace
+
+`_C`: the sm_100a kernels and the domain runtime; `_host`: the CPU-side runtime library.
 
 Only sm_100a code is generated (`-gencode arch=compute_100a,code=sm_100a`); torch's own
 TORCH_CUDA_ARCH_LIST is bypassed by passing the arch flags explicitly.
@@ -7,7 +9,8 @@ TORCH_CUDA_ARCH_LIST is bypassed by passing the arch flags explicitly.
 import os
 from pathlib import Path
 
-from setuptools import setup
+import pybind11
+from setuptools import Extension, setup
 from torch.utils.cpp_extension import BuildExtension, CUDAExtension
 
 ROOT = Path(__file__).resolve().parent
@@ -31,6 +34,10 @@ SOURCES = [
     "kernels/decode.cu",
 ]
 
+# host runtime library (no CUDA, no libtorch): layouts, capacity, schedule, pages, scheduler
+HOST_SOURCES = ["layout.cpp", "capacity.cpp", "schedule.cpp", "pages.cpp", "scheduler.cpp",
+                "host_bindings.cpp"]
+
 setup(
     name=PKG,
     version="0.1.0",
@@ -41,7 +48,14 @@ setup(
             sources=[str(CSRC / s) for s in SOURCES],
             include_dirs=[str(CSRC / "include"), str(CSRC)],
             extra_compile_args={"cxx": ["-O3", "-std=c++17"], "nvcc": NVCC_FLAGS},
-        )
+        ),
+        Extension(
+            name=f"{PKG}._host",
+            sources=[str(CSRC / "host" / s) for s in HOST_SOURCES],
+            include_dirs=[str(CSRC / "host"), pybind11.get_include()],
+            extra_compile_args=["-O3", "-std=c++17", "-fvisibility=hidden", "-Wall"],
+            language="c++",
+        ),
     ],
     cmdclass={"build_ext": BuildExtension.with_options(use_ninja=True)},
 )

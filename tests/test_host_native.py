@@ -1,0 +1,26 @@
+"""The host runtime library's own C++ test (`csrc/tests/host_test.cpp`), built with g++ and run
+on the CPU: reference golden vectors for layouts, capacity allocation, admission and the KV-growth
+schedule, the page allocator, and the batch scheduler core under concurrent producers."""
+
+import os
+import shutil
+import subprocess
+
+import pytest
+
+CSRC = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))),
+                    "hetero_cp_ringattn_b200", "csrc")
+SOURCES = ["tests/host_test.cpp"] + [f"host/{f}" for f in ("layout.cpp", "capacity.cpp",
+                                                         "schedule.cpp", "pages.cpp",
+                                                         "scheduler.cpp")]
+
+
+@pytest.mark.skipif(shutil.which("g++") is None, reason="no C++ compiler")
+def test_host_library_native_tests(tmp_path):
+    exe = str(tmp_path / "host_test")
+    cc = subprocess.run(["g++", "-O2", "-std=c++17", "-Wall", "-Werror", "-pthread", "-o", exe] +
+                        [os.path.join(CSRC, s) for s in SOURCES], capture_output=True, text=True,
+                        timeout=300)
+    assert cc.returncode == 0, cc.stderr[-4000:]
+    run = subprocess.run([exe], capture_output=True, text=True, timeout=120)
+    assert run.returncode == 0 and "host_test ok" in run.stdout, run.stdout + run.stderr

@@ -19,7 +19,7 @@ def test_page_allocator_exhaustion_and_reuse():
     a = PageAllocator(4, 128)
     p = a.alloc(3, req_id=1)
     assert len(set(p)) == 3 and a.free_pages == 1
-    assert all(a.owner[x] == 1 for x in p)
+    assert all(a.owner_of(x) == 1 for x in p) and a.owner_of(3) is None
     with pytest.raises(CapacityError):
         a.alloc(2, req_id=2)
     a.free(p[:2])

@@ -82,8 +82,6 @@ def test_chunk_sizes_tiers_and_ratios():
     assert C.chunk_sizes(10, 3) == [4, 4, 2]
     assert C.chunk_sizes(12, 2, capacities_mb=[1536 + 100, 1536 + 300], capacity_aware=True) == [3, 9]
     assert C.equal_chunks(32768, 8) == [4096] * 8
-    rc = C.round_chunks_to_tile([300, 300, 37], 128)
-    assert sum(rc) == 637 and rc[0] % 128 == 0
 
 
 def test_kv_admission_and_ledger():
