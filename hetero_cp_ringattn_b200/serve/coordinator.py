@@ -94,6 +94,7 @@ class Coordinator:
         self.trace = TraceSink(args.trace_jsonl)
         self.metrics = Metrics()
         self.sessions: Dict[str, Session] = {}
+        self._busy: set = set()   # session ids with a keep_kv / append request in flight
         self._ids = itertools.count(1)
         caps = list(capacities_mb) if capacities_mb else [UNKNOWN_CAPACITY] * self.world
         self.capacities_mb = caps
@@ -119,6 +120,8 @@ class Coordinator:
                 raise ProtocolError(("append" if job.append else "keep_kv") + "=true requires session_id")
         if job.append and job.session_id not in self.sessions:
             raise ProtocolError(f"unknown or expired session {job.session_id!r}")
+        if job.keep_kv and not job.append and job.session_id in self.sessions:
+            raise ProtocolError(f"session_id {job.session_id!r} already has resident KV")
         self.trace.emit("enqueue", request=job.request_id, prompt_tokens=len(job.prompt_ids))
         self.sched.enqueue(job)
 
@@ -173,6 +176,11 @@ class Coordinator:
         if job.append:
             return self._append(job)
         horizon = max(1, job.max_tokens) + (self.args.session_continuation_tokens if job.keep_kv else 0)
+        if job.keep_kv:
+            if job.session_id in self.sessions or job.session_id in self._busy:
+                raise AdmissionError(f"session_id {job.session_id!r} already has resident KV")
+            self._busy.add(job.session_id)
+            job.holds_session = True
         try:
             chunks = self._chunks(len(job.prompt_ids))
         except RingError as e:
@@ -196,14 +204,26 @@ class Coordinator:
         self._emit_token(req, resp.token)
 
     def _append(self, job: Job) -> None:
-        sess = self.sessions[job.session_id]
+        sess = self.sessions.get(job.session_id)
+        if sess is None:
+            raise AdmissionError(f"unknown or expired session {job.session_id!r}")
+        if job.session_id in self._busy:
+            raise AdmissionError(f"session {job.session_id!r} already has a request in flight")
+        self._busy.add(job.session_id)
+        job.holds_session = True
         rid = sess.request_id
         # the session's last generated token was never fed back, so it has no KV yet: it leads
-        # the continuation segment
+        # the continuation segment (the context is exactly the text the client has seen)
         seg = [sess.last_token] + list(job.prompt_ids)
         n = len(seg)
         positions = list(range(sess.context_len, sess.context_len + n))
         tickets = self._tickets(sess.chunks)
+        # KV bytes of the segment and its decode growth join the session's ledger entry
+        tot = sum(tickets)
+        per = [(c + -(-max(1, job.max_tokens) * t // tot) + 1) * self.cfg.num_layers *
+               self.bytes_per_token_layer for c, t in zip(continuation_split(n, tickets), tickets)]
+        self.ledger.try_reserve(rid, per)
+        self.trace.emit("kv_reserved", request=rid, bytes=per)
         resp = self.run_command(P.StationaryContinuation(rid, seg, positions, tickets, 0))
         if self.args.export_logits_dir and self.worker.last_logits is not None:
             export_logits_dump(self._dump_dir(rid), {"continuation_last_logits": self.worker.last_logits}, {
@@ -325,13 +345,21 @@ class Coordinator:
             self.sched.activate(req)
 
     def _finish(self, req: ActiveRequest) -> None:
+        """Session rules (coordinator.rs:1743-1810, 2770-2830): a keep_kv request registers or
+        advances its session and keeps the KV; an append without keep_kv ends the session it
+        rode on; any other request releases its KV."""
         job = req.job
         self.sched.complete(job.request_id)
-        if job.keep_kv or job.append:
+        if job.holds_session:
+            self._busy.discard(job.session_id)
+            job.holds_session = False
+        if job.keep_kv:
             ctx = req.next_position + len(req.generated) - 1
             self.sessions[job.session_id] = Session(job.request_id, ctx, req.chunks, req.next_token)
             # the last generated token has no KV yet: the next append starts with it
         else:
+            if job.append:
+                self.sessions.pop(job.session_id, None)
             self.run_command(P.ReleaseRequest(job.request_id))
             released = self.ledger.release(job.request_id)
             self.trace.emit("kv_released", request=job.request_id, bytes=released)
@@ -344,10 +372,24 @@ class Coordinator:
                       "prompt_tokens": len(job.prompt_ids), "finish_reason": req.finish_reason})
 
     def _fail(self, job: Job, err: Exception) -> None:
+        """A failed request leaves no half-live KV: its rows on the workers and its ledger bytes
+        are released, and a failed append drops the session it rode on
+        (coordinator.rs:2636-2652). A request rejected before it owned its session (unknown or
+        busy session, a keep_kv id that already holds KV) touches no session."""
         self.metrics.bump("failed")
         self.sched.complete(job.request_id)
-        if not job.append:
-            self.ledger.release(job.request_id)
+        rid = job.request_id
+        if job.holds_session:
+            self._busy.discard(job.session_id)
+            job.holds_session = False
+            if job.append:
+                sess = self.sessions.pop(job.session_id, None)
+                rid = sess.request_id if sess is not None else rid
+        try:
+            self.run_command(P.ReleaseRequest(rid))
+        except (ProtocolError, RuntimeError, OSError) as e:  # a rank is gone: nothing to free
+            self.trace.emit("release_failed", request=rid, error=str(e))
+        self.ledger.release(rid)
         self.trace.emit("failed", request=job.request_id, error=str(err))
         if job.done:
             job.done({"request_id": job.request_id, "error": str(err),

@@ -30,6 +30,7 @@ class Job:
     on_token: Optional[Callable[[int, Optional[str]], None]] = None   # (token, finish_reason)
     done: Optional[Callable[[dict], None]] = None
     enqueued_at: float = dataclasses.field(default_factory=time.time)
+    holds_session: bool = False   # set by the coordinator while this job owns its session
 
 
 @dataclasses.dataclass

@@ -199,3 +199,37 @@ def test_continuation_e2e_and_logits_dumps(stack, tmp_path):
         assert json.loads((pd / "meta.json").read_text())["prefill_argmax"] == res["tokens"][0]
     finally:
         coord.args.export_logits_dir = None
+
+
+def test_session_lifecycle_matches_reference_rules(stack):
+    """keep_kv registers a session; append (+keep_kv) continues and advances it; an append
+    without keep_kv ends it and frees its KV; a keep_kv id that already holds KV and an unknown
+    session are rejected; a failed append drops its session (coordinator.rs:1743-1810,
+    2630-2830). Every phase's tokens equal the dense oracle on the whole context."""
+    cfg, w, eng, coord, tok = stack
+    free0 = coord.ledger.free_bytes()
+    prompt = tok.encode("session prompt")
+    r1 = coord.generate(prompt, max_tokens=3, session_id="s", keep_kv=True)
+    ref1, _ = reference_model.greedy_generate(w, torch.tensor(prompt), 2)
+    assert r1["tokens"] == ref1 and "s" in coord.sessions
+    with pytest.raises(P.ProtocolError):
+        coord.submit(Job(request_id=coord.next_request_id(), prompt_ids=[1, 2], session_id="s",
+                         keep_kv=True))
+    with pytest.raises(P.ProtocolError):
+        coord.submit(Job(request_id=coord.next_request_id(), prompt_ids=[1, 2], session_id="nope",
+                         append=True))
+    seg1 = tok.encode(" more")
+    r2 = coord.generate(seg1, max_tokens=3, session_id="s", append=True, keep_kv=True)
+    ctx = prompt + ref1 + seg1
+    ref2, _ = reference_model.greedy_generate(w, torch.tensor(ctx), 2)
+    assert r2["tokens"] == ref2
+    seg2 = tok.encode(" end")
+    r3 = coord.generate(seg2, max_tokens=2, session_id="s", append=True)
+    ref3, _ = reference_model.greedy_generate(w, torch.tensor(ctx + ref2 + seg2), 1)
+    assert r3["tokens"] == ref3
+    assert "s" not in coord.sessions and not eng.reqs and coord.ledger.free_bytes() == free0
+    # a failed append (segment past the engine's context) drops the session and its KV
+    coord.generate(prompt, max_tokens=2, session_id="t", keep_kv=True)
+    bad = coord.generate([5] * 600, max_tokens=2, session_id="t", append=True)
+    assert "error" in bad and "t" not in coord.sessions and not eng.reqs
+    assert coord.ledger.free_bytes() == free0

@@ -126,6 +126,32 @@ def test_two_rank_server_concurrent_requests(server):
     assert m["active_requests"] == 0 and m["failed_requests"] == 0
 
 
+def _post(port, body):
+    req = urllib.request.Request(f"http://127.0.0.1:{port}/v1/completions",
+                                 data=json.dumps(body).encode(),
+                                 headers={"Content-Type": "application/json"})
+    with urllib.request.urlopen(req, timeout=120) as r:
+        return json.loads(r.read())
+
+
+def test_two_rank_server_session_keep_kv_then_append(server):
+    """A keep_kv request leaves its KV sharded over both ranks; the append continues it; the
+    texts equal the dense oracle on the whole context."""
+    w, port, _, _, _ = server
+    tok = ByteTokenizer(w.cfg.vocab_size)
+    p1, p2 = "first turn of a session", " and the second turn"
+    r1 = _post(port, {"prompt": p1, "max_tokens": 4, "session_id": "conv", "keep_kv": True})
+    ids1 = tok.encode(p1)
+    g1, _ = reference_model.greedy_generate(w, torch.tensor(ids1), 3)
+    assert r1["choices"][0]["text"] == tok.decode(g1)
+    r2 = _post(port, {"prompt": p2, "max_tokens": 3, "session_id": "conv", "append": True})
+    g2, _ = reference_model.greedy_generate(w, torch.tensor(ids1 + g1 + tok.encode(p2)), 2)
+    assert r2["choices"][0]["text"] == tok.decode(g2)
+    with pytest.raises(urllib.error.HTTPError) as ei:   # the append without keep_kv ended it
+        _post(port, {"prompt": "x y", "max_tokens": 1, "session_id": "conv", "append": True})
+    assert ei.value.code == 400
+
+
 def test_two_rank_server_rejects_prompt_shorter_than_ranks(server):
     _, port, _, _, _ = server
     with pytest.raises(urllib.error.HTTPError) as ei:
