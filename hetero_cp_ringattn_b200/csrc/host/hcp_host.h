@@ -11,7 +11,9 @@
 //     (rust/src/model/self_driving.rs:12-144);
 //   * the paged KV arena's page allocator (rust/src/model/cache.rs block tables,
 //     self_driving.rs:146-331 reserved slabs);
-//   * the iterative batch scheduler's queue / active-set core (rust/src/distributed/scheduler.rs).
+//   * the iterative batch scheduler's queue / active-set core (rust/src/distributed/scheduler.rs);
+//   * the binary frames of the coordinator <-> rank control protocol
+//     (rust/src/distributed/protocol.rs:14-192 message set).
 #pragma once
 
 #include <condition_variable>
@@ -157,6 +159,45 @@ class BatchSchedulerCore {
   std::condition_variable cv_;
   std::deque<uint64_t> pending_;
   std::vector<uint64_t> active_;
+};
+
+// ----------------------------------------------------------------------------- control protocol
+// Binary frames of the coordinator <-> rank control messages:
+//   [u32 payload bytes][u8 version][u8 message type][fields ...], all little endian.
+// Each message type has a fixed field list (kinds below); arrays carry a u64 count, strings a u32
+// byte count, optionals a u8 presence flag. Token arrays travel as raw int64, so a 128k-token
+// prompt costs one memcpy instead of a text encoding.
+enum class FieldKind : char {
+  kI64 = 'i',        // int64
+  kF64 = 'f',        // double
+  kBool = 'b',       // u8 0/1
+  kStr = 's',        // u32 length + utf-8 bytes
+  kI64Array = 'A',   // u64 count + int64[count]
+  kPairs = 'P',      // u64 count + int64[2 * count] (rows of two)
+  kOptI64 = 'o',     // u8 present + int64
+  kOptI64Array = 'O',// u8 present + array
+  kOptF32Array = 'G',// u8 present + u64 count + float[count]
+};
+
+struct Field {
+  FieldKind kind = FieldKind::kI64;
+  bool present = true;             // optionals
+  int64_t i = 0;
+  double f = 0.0;
+  std::string s;
+  std::vector<int64_t> a;          // arrays and pairs (row-major)
+  std::vector<float> fa;
+};
+
+constexpr uint8_t kProtocolVersion = 1;
+// Field kinds of a message type ("" if unknown).
+const char* MessageSchema(int type);
+std::string EncodeFrame(int type, const std::vector<Field>& fields);
+// Throws ProtocolError on a short, partial, oversized, unknown-type or wrong-version frame.
+std::vector<Field> DecodeFrame(const std::string& frame, int* type);
+
+struct ProtocolError : RingError {
+  using RingError::RingError;
 };
 
 }  // namespace hcp::host

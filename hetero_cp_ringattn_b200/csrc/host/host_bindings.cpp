@@ -24,6 +24,74 @@ std::vector<int64_t> FromArray(const py::array_t<int64_t, py::array::c_style | p
   return std::vector<int64_t>(a.data(), a.data() + a.size());
 }
 
+using I64Arr = py::array_t<int64_t, py::array::c_style | py::array::forcecast>;
+using F32Arr = py::array_t<float, py::array::c_style | py::array::forcecast>;
+
+std::vector<int64_t> ToVec(const py::handle& obj) {
+  I64Arr a = I64Arr::ensure(obj);
+  if (!a) throw ProtocolError("expected an integer array");
+  return std::vector<int64_t>(a.data(), a.data() + a.size());
+}
+
+Field ToField(FieldKind k, const py::handle& v) {
+  Field f;
+  f.kind = k;
+  const bool none = v.is_none();
+  switch (k) {
+    case FieldKind::kI64: f.i = py::cast<int64_t>(v); break;
+    case FieldKind::kF64: f.f = py::cast<double>(v); break;
+    case FieldKind::kBool: f.i = py::cast<bool>(v) ? 1 : 0; break;
+    case FieldKind::kStr: f.s = py::cast<std::string>(v); break;
+    case FieldKind::kI64Array: f.a = ToVec(v); break;
+    case FieldKind::kPairs:
+      f.a = ToVec(v);
+      if (f.a.size() % 2) throw ProtocolError("pairs field needs rows of two integers");
+      break;
+    case FieldKind::kOptI64:
+      f.present = !none;
+      if (!none) f.i = py::cast<int64_t>(v);
+      break;
+    case FieldKind::kOptI64Array:
+      f.present = !none;
+      if (!none) f.a = ToVec(v);
+      break;
+    case FieldKind::kOptF32Array:
+      f.present = !none;
+      if (!none) {
+        F32Arr a = F32Arr::ensure(v);
+        if (!a) throw ProtocolError("expected a float array");
+        f.fa.assign(a.data(), a.data() + a.size());
+      }
+      break;
+  }
+  return f;
+}
+
+py::object FromField(const Field& f) {
+  auto arr = [](const std::vector<int64_t>& v) { return py::object(ToArray(v)); };
+  switch (f.kind) {
+    case FieldKind::kI64: return py::int_(f.i);
+    case FieldKind::kF64: return py::float_(f.f);
+    case FieldKind::kBool: return py::bool_(f.i != 0);
+    case FieldKind::kStr: return py::str(f.s);
+    case FieldKind::kI64Array: return arr(f.a);
+    case FieldKind::kPairs: {
+      py::array_t<int64_t> a({py::ssize_t(f.a.size() / 2), py::ssize_t(2)});
+      if (!f.a.empty()) std::memcpy(a.mutable_data(), f.a.data(), f.a.size() * sizeof(int64_t));
+      return a;
+    }
+    case FieldKind::kOptI64: return f.present ? py::object(py::int_(f.i)) : py::none();
+    case FieldKind::kOptI64Array: return f.present ? arr(f.a) : py::none();
+    case FieldKind::kOptF32Array: {
+      if (!f.present) return py::none();
+      py::array_t<float> a(py::ssize_t(f.fa.size()));
+      if (!f.fa.empty()) std::memcpy(a.mutable_data(), f.fa.data(), f.fa.size() * sizeof(float));
+      return a;
+    }
+  }
+  return py::none();
+}
+
 void RaiseAs(const char* cls_name, const char* what) {
   py::object cls = py::module_::import("hetero_cp_ringattn_b200.errors").attr(cls_name);
   PyErr_SetString(cls.ptr(), what);
@@ -37,6 +105,8 @@ PYBIND11_MODULE(_host, m) {
   py::register_exception_translator([](std::exception_ptr p) {
     try {
       if (p) std::rethrow_exception(p);
+    } catch (const ProtocolError& e) {
+      RaiseAs("ProtocolError", e.what());
     } catch (const CapacityError& e) {
       RaiseAs("CapacityError", e.what());
     } catch (const RingError& e) {
@@ -117,6 +187,27 @@ PYBIND11_MODULE(_host, m) {
       .def_property_readonly("free_pages", &PageAllocator::FreePages)
       .def_property_readonly("num_pages", &PageAllocator::NumPages)
       .def_property_readonly("page_size", &PageAllocator::PageSize);
+
+  // control protocol frames
+  m.attr("PROTOCOL_VERSION") = py::int_(kProtocolVersion);
+  m.def("message_schema", [](int type) { return std::string(MessageSchema(type)); });
+  m.def("encode_frame", [](int type, const py::sequence& values) {
+    const std::string kinds = MessageSchema(type);
+    if (kinds.empty() && type != 8) throw ProtocolError("not a protocol message type");
+    if (size_t(py::len(values)) != kinds.size())
+      throw ProtocolError("message type " + std::to_string(type) + " takes " +
+                          std::to_string(kinds.size()) + " fields");
+    std::vector<Field> fields;
+    for (size_t k = 0; k < kinds.size(); ++k) fields.push_back(ToField(FieldKind(kinds[k]), values[k]));
+    return py::bytes(EncodeFrame(type, fields));
+  }, py::arg("type"), py::arg("values"));
+  m.def("decode_frame", [](const py::bytes& frame) {
+    int type = 0;
+    const auto fields = DecodeFrame(std::string(frame), &type);
+    py::list out;
+    for (const auto& f : fields) out.append(FromField(f));
+    return py::make_tuple(type, out);
+  }, py::arg("frame"));
 
   // scheduler core
   py::class_<BatchSchedulerCore>(m, "BatchSchedulerCore")

@@ -4,6 +4,7 @@
 // Exit status 0 and "host_test ok" on success; the first failed check prints its line.
 #include <cstdio>
 #include <cstdlib>
+#include <cstring>
 #include <thread>
 
 #include "../host/hcp_host.h"
@@ -160,12 +161,69 @@ static void Scheduler() {
   CHECK(s.PopPending().value() == 8);
 }
 
+static Field I(int64_t v) {
+  Field f;
+  f.i = v;
+  return f;
+}
+static Field Arr(V v) {
+  Field f;
+  f.a = std::move(v);
+  return f;
+}
+
+static void Protocol() {
+  // Prefill: request_id, prompt, chunks, strategy, horizon, tickets?, keep_kv
+  Field strat;
+  strat.s = "zigzag";
+  Field none;
+  none.present = false;
+  std::vector<Field> prefill{I(5), Arr({9, 8, 7, 6}), Arr({3, 1}), strat, I(16), none, I(1)};
+  const std::string fr = EncodeFrame(1, prefill);
+  uint32_t payload;
+  std::memcpy(&payload, fr.data(), 4);
+  CHECK(payload == fr.size() - 4 && uint8_t(fr[4]) == kProtocolVersion && uint8_t(fr[5]) == 1);
+  int type = 0;
+  auto back = DecodeFrame(fr, &type);
+  CHECK(type == 1 && back.size() == 7 && back[0].i == 5 && (back[1].a == V{9, 8, 7, 6}));
+  CHECK(back[3].s == "zigzag" && !back[5].present && back[6].i == 1);
+  // every truncation and any trailing byte is rejected
+  for (size_t n = 0; n < fr.size(); ++n)
+    CHECK(Throws<ProtocolError>([&] { DecodeFrame(fr.substr(0, n), &type); }));
+  CHECK(Throws<ProtocolError>([&] { DecodeFrame(fr + "x", &type); }));
+  std::string bad = fr;
+  bad[4] = 2;
+  CHECK(Throws<ProtocolError>([&] { DecodeFrame(bad, &type); }));
+  bad[4] = char(kProtocolVersion);
+  bad[5] = 42;
+  CHECK(Throws<ProtocolError>([&] { DecodeFrame(bad, &type); }));
+  // a count that points past the frame
+  std::string lie = fr;
+  const uint64_t huge = 1ull << 40;
+  std::memcpy(&lie[6 + 8], &huge, 8);
+  CHECK(Throws<ProtocolError>([&] { DecodeFrame(lie, &type); }));
+  // pairs, optional token, error string, empty message
+  back = DecodeFrame(EncodeFrame(66, {Arr({1, 10, 2, 20})}), &type);
+  CHECK(type == 66 && (back[0].a == V{1, 10, 2, 20}));
+  back = DecodeFrame(EncodeFrame(67, {I(3), none}), &type);
+  CHECK(type == 67 && !back[1].present);
+  Field msg;
+  msg.s = "rank error";
+  back = DecodeFrame(EncodeFrame(69, {I(4), msg}), &type);
+  CHECK(back[1].s == "rank error");
+  CHECK(DecodeFrame(EncodeFrame(8, {}), &type).empty() && type == 8);
+  CHECK(Throws<ProtocolError>([&] { EncodeFrame(2, {I(1)}); }));
+  CHECK(Throws<ProtocolError>([&] { EncodeFrame(99, {}); }));
+  CHECK(Throws<ProtocolError>([&] { EncodeFrame(3, {Arr({1, 2, 3})}); }));
+}
+
 int main() {
   Layouts();
   Capacity();
   Schedule();
   Pages();
   Scheduler();
+  Protocol();
   std::printf("host_test ok (%d checks)\n", g_checks);
   return 0;
 }

@@ -9,19 +9,21 @@ is mapped once at start-up through CUDA IPC, see the domain runtime).
 Transport: the reference frames bincode messages over QUIC streams (protocol.rs:194-553). Here all
 ranks live in one torchrun job, so the control plane is torch.distributed on a gloo group: rank 0
 (the coordinator) broadcasts each command to every rank, every rank executes it SPMD, and rank 0
-gathers the responses. Messages are dataclasses; `encode`/`decode` give a stable JSON form (used by
-the tests and by the wire-compat check).
+gathers the responses. Messages are dataclasses; `encode`/`decode` turn them into the native
+codec's binary frames (csrc/host/protocol.cpp), which is what the control group carries.
 """
 
 from __future__ import annotations
 
 import dataclasses
-import json
 import struct
 from datetime import timedelta
 from typing import Any, List, Optional, Sequence
 
+import numpy as np
+
 from ..errors import ProtocolError
+from ..host import lib
 
 
 # --------------------------------------------------------------------------- commands
@@ -124,27 +126,51 @@ COMMANDS = {c.__name__: c for c in (Prefill, Decode, DecodeBatch, StationaryCont
                                      StationaryDecode, SyncGlobalSeqLen, ReleaseRequest, Shutdown)}
 RESPONSES = {c.__name__: c for c in (PrefillDone, DecodeDone, DecodeBatchDone,
                                       StationaryContinuationDone, Ack, Error)}
+# wire type ids of the native codec (csrc/host/protocol.cpp): commands 1-8, responses 64-69
+TYPE_IDS = {Prefill: 1, Decode: 2, DecodeBatch: 3, StationaryContinuation: 4, StationaryDecode: 5,
+            SyncGlobalSeqLen: 6, ReleaseRequest: 7, Shutdown: 8, PrefillDone: 64, DecodeDone: 65,
+            DecodeBatchDone: 66, StationaryContinuationDone: 67, Ack: 68, Error: 69}
+_BY_ID = {v: k for k, v in TYPE_IDS.items()}
+# array fields that stay numpy int64 arrays after decoding (prompt-sized); the other arrays
+# become lists
+_BULK = {(Prefill, "prompt"), (StationaryContinuation, "tokens"),
+         (StationaryContinuation, "position_ids")}
 
 
 def encode(msg) -> bytes:
-    name = type(msg).__name__
-    if name not in COMMANDS and name not in RESPONSES:
-        raise ProtocolError(f"not a protocol message: {name}")
-    body = json.dumps({"type": name, "body": dataclasses.asdict(msg)}).encode()
-    return struct.pack(">I", len(body)) + body
+    """One binary frame: [u32 payload bytes][u8 version][u8 type][fields], little endian, built
+    by the native codec; token arrays travel as raw int64."""
+    tid = TYPE_IDS.get(type(msg))
+    if tid is None:
+        raise ProtocolError(f"not a protocol message: {type(msg).__name__}")
+    return lib().encode_frame(tid, [getattr(msg, f.name) for f in dataclasses.fields(msg)])
 
 
 def decode(frame: bytes):
-    if len(frame) < 4:
-        raise ProtocolError("short frame")
-    (n,) = struct.unpack(">I", frame[:4])
-    if len(frame) - 4 < n:
-        raise ProtocolError(f"partial frame: need {n} bytes, have {len(frame) - 4}")
-    obj = json.loads(frame[4:4 + n].decode())
-    cls = COMMANDS.get(obj.get("type")) or RESPONSES.get(obj.get("type"))
-    if cls is None:
-        raise ProtocolError(f"unknown message type {obj.get('type')!r}")
-    return cls(**obj["body"])
+    """Inverse of `encode`; a short, partial, trailing-byte, wrong-version or unknown-type frame
+    raises ProtocolError."""
+    tid, values = lib().decode_frame(bytes(frame))
+    cls = _BY_ID[tid]
+    out = []
+    for f, v in zip(dataclasses.fields(cls), values):
+        if isinstance(v, np.ndarray) and (cls, f.name) not in _BULK:
+            v = v.tolist()
+        out.append(v)
+    return cls(*out)
+
+
+def as_plain(msg) -> dict:
+    """The message's fields with arrays as lists (for comparisons and logs)."""
+    return {f.name: (v.tolist() if isinstance(v, np.ndarray) else v)
+            for f in dataclasses.fields(msg) for v in [getattr(msg, f.name)]}
+
+
+def _check_schemas() -> None:
+    for cls, tid in TYPE_IDS.items():
+        kinds = lib().message_schema(tid)
+        if len(kinds) != len(dataclasses.fields(cls)):
+            raise ProtocolError(f"{cls.__name__}: {len(dataclasses.fields(cls))} fields, native "
+                                f"schema {kinds!r}")
 
 
 # --------------------------------------------------------------------------- validators

@@ -46,7 +46,7 @@ class Worker:
         e = self.engine
         try:
             if isinstance(cmd, P.Prefill):
-                prompt = torch.tensor(cmd.prompt, dtype=torch.int64)
+                prompt = torch.as_tensor(cmd.prompt, dtype=torch.int64)  # no copy from the frame
                 tok, logits = e.prefill(cmd.request_id, prompt, cmd.chunks, cmd.strategy,
                                         decode_horizon=cmd.decode_horizon,
                                         tickets=cmd.capacity_tickets, return_logits=True,
@@ -80,7 +80,7 @@ class Worker:
             if isinstance(cmd, P.StationaryContinuation):
                 P.validate_stationary_continuation(e.world, cmd.tokens, cmd.position_ids,
                                                    cmd.capacity_tickets, cmd.starter_domain)
-                tok, logits = e.append(cmd.request_id, torch.tensor(cmd.tokens, dtype=torch.int64),
+                tok, logits = e.append(cmd.request_id, torch.as_tensor(cmd.tokens, dtype=torch.int64),
                                        cmd.position_ids, cmd.capacity_tickets, return_logits=True)
                 self.last_logits = logits
                 return P.StationaryContinuationDone(cmd.request_id, int(tok))

@@ -1,6 +1,7 @@
 """The host runtime library's own C++ test (`csrc/tests/host_test.cpp`), built with g++ and run
 on the CPU: reference golden vectors for layouts, capacity allocation, admission and the KV-growth
-schedule, the page allocator, and the batch scheduler core under concurrent producers."""
+schedule, the page allocator, the batch scheduler core under concurrent producers, and the control
+protocol's binary frames (round trips, every truncation, versions, lying counts)."""
 
 import os
 import shutil
@@ -12,7 +13,7 @@ CSRC = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))),
                     "hetero_cp_ringattn_b200", "csrc")
 SOURCES = ["tests/host_test.cpp"] + [f"host/{f}" for f in ("layout.cpp", "capacity.cpp",
                                                          "schedule.cpp", "pages.cpp",
-                                                         "scheduler.cpp")]
+                                                         "scheduler.cpp", "protocol.cpp")]
 
 
 @pytest.mark.skipif(shutil.which("g++") is None, reason="no C++ compiler")

@@ -31,11 +31,26 @@ def test_protocol_roundtrip_and_partial_frames():
                 P.DecodeBatch([[1, 2], [3, 4]]), P.StationaryDecode(1, 2, 3, [1, 1], 0, 0, 4),
                 P.ReleaseRequest(9), P.Shutdown(), P.PrefillDone(1, 5, 3), P.Error(1, "x")]:
         frame = P.encode(msg)
-        assert P.decode(frame) == msg
+        assert P.as_plain(P.decode(frame)) == P.as_plain(msg)
         with pytest.raises(ProtocolError):
             P.decode(frame[:-1])
+        with pytest.raises(ProtocolError):
+            P.decode(frame + b"\x00")
     with pytest.raises(ProtocolError):
         P.decode(b"\x00\x00\x00\x05{\"ty")
+    # the wire layout: [u32 payload][u8 version][u8 type][fields], token arrays as raw int64
+    f = P.encode(P.Prefill(7, [1, 2, 3], [3], "vanilla", 4, None, False))
+    assert f[4] == 1 and f[5] == 1 and int.from_bytes(f[:4], "little") == len(f) - 4
+    bad = bytearray(f)
+    bad[4] = 9
+    with pytest.raises(ProtocolError, match="version"):
+        P.decode(bytes(bad))
+    bad[4], bad[5] = 1, 200
+    with pytest.raises(ProtocolError, match="unknown message type"):
+        P.decode(bytes(bad))
+    big = P.decode(P.encode(P.Prefill(1, list(range(70000)), [70000], "zigzag", 4, [1], True)))
+    assert big.prompt.dtype.name == "int64" and int(big.prompt[-1]) == 69999
+    assert big.chunks == [70000] and big.capacity_tickets == [1] and big.keep_kv is True
     hs = P.pack_handshake(3, 4096)
     assert len(hs) == 16 and P.unpack_handshake(hs) == (3, 4096)
 
