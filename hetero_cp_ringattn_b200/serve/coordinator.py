@@ -320,6 +320,13 @@ class Coordinator:
             export_logits_dump(self.args.export_logits_dir, arts, meta)
         return meta
 
+    def _eos(self, job: Job) -> set:
+        """Tokens that end a request: its stop ids, else the model's EOS ids; none with
+        ignore_eos."""
+        if job.ignore_eos:
+            return set()
+        return set(job.stop_ids or self.args.eos_ids or [])
+
     def _emit_token(self, req: ActiveRequest, argmax_token: int) -> None:
         job = req.job
         tok = argmax_token
@@ -332,7 +339,7 @@ class Coordinator:
             req.first_token_at = time.time()
             self.trace.emit("first_token", request=job.request_id,
                             ttft_s=req.first_token_at - job.enqueued_at)
-        eos = set(job.stop_ids or self.args.eos_ids or [])
+        eos = self._eos(job)
         if tok in eos:
             req.finish_reason = "stop"
         elif len(req.generated) >= job.max_tokens:
@@ -428,7 +435,7 @@ class Coordinator:
                     tok = sample_token(logits[i], a.job.temperature, a.job.top_p)
                 a.generated.append(tok)
                 a.next_token = tok
-                eos = set(a.job.stop_ids or self.args.eos_ids or [])
+                eos = self._eos(a.job)
                 if tok in eos:
                     a.finish_reason = "stop"
                 elif len(a.generated) >= a.job.max_tokens:

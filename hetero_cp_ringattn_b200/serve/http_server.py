@@ -102,7 +102,7 @@ def make_handler(state: ApiState):
                       temperature=float(body.get("temperature", 0.0)),
                       top_p=float(body.get("top_p", 1.0)), session_id=body.get("session_id"),
                       keep_kv=bool(body.get("keep_kv", False)), append=bool(body.get("append", False)),
-                      stop_ids=stop_ids,
+                      stop_ids=stop_ids, ignore_eos=bool(body.get("ignore_eos", False)),
                       on_token=lambda t, fr: events.put(("tok", t, fr)),
                       done=lambda r: events.put(("done", r, None)))
             try:

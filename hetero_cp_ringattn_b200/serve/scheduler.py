@@ -27,6 +27,7 @@ class Job:
     keep_kv: bool = False
     append: bool = False
     stop_ids: Optional[List[int]] = None
+    ignore_eos: bool = False      # generate exactly max_tokens (benchmarks)
     on_token: Optional[Callable[[int, Optional[str]], None]] = None   # (token, finish_reason)
     done: Optional[Callable[[dict], None]] = None
     enqueued_at: float = dataclasses.field(default_factory=time.time)

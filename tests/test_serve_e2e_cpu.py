@@ -160,16 +160,6 @@ def test_two_rank_server_rejects_prompt_shorter_than_ranks(server):
     assert "must be >= num_domains (2)" in ei.value.read().decode()
 
 
-def test_two_rank_server_exits_on_interrupt(server):
-    """Ctrl-C reaches every rank through torchrun; each rank leaves its loop without a
-    traceback (torchrun itself still reports the signal in its own exit status)."""
-    _, _, _, proc, log = server
-    proc.send_signal(signal.SIGINT)
-    proc.wait(timeout=60)
-    text = log.read_text()
-    assert "[rank0]: Traceback" not in text and "[rank1]: Traceback" not in text, text[-3000:]
-
-
 def test_two_rank_continuation_e2e_cli(tmp_path):
     """`serve --continuation-segment` under torchrun with two ranks and uneven tickets: the
     generated ids and the three logits dumps match the dense oracle."""
@@ -234,3 +224,31 @@ def test_infer_under_torchrun_matches_single_process(tmp_path):
                            str(tmp_path / "a.bin"), str(tmp_path / "b.bin"), "--tolerance", "1e-3"],
                           cwd=REPO, env=env, capture_output=True, text=True, timeout=120)
     assert cmp_.returncode == 0 and json.loads(cmp_.stdout)["passed"], cmp_.stdout
+
+
+def test_serve_bench_client_against_two_ranks(server):
+    """benchmarks/serve_bench.py (the reference's serving baseline shape: random prompts,
+    fixed output length with EOS ignored, closed-loop concurrency) completes every request and
+    reports TTFT / TPOT / throughput."""
+    sys.path.insert(0, os.path.join(REPO, "benchmarks"))
+    try:
+        import serve_bench
+    finally:
+        sys.path.pop(0)
+    _, port, _, _, _ = server
+    res = serve_bench.run(f"http://127.0.0.1:{port}", num_prompts=6, input_len=12, output_len=5,
+                          max_concurrency=2, seed=1)
+    assert res["completed"] == 6 and res["failed"] == 0
+    assert res["output_throughput"] > 0 and res["mean_ttft_ms"] > 0 and res["mean_tpot_ms"] > 0
+    assert res["median_ttft_ms"] <= res["p99_ttft_ms"]
+
+
+# stops the module's server: keep it the last test that uses the fixture
+def test_two_rank_server_exits_on_interrupt(server):
+    """Ctrl-C reaches every rank through torchrun; each rank leaves its loop without a
+    traceback (torchrun itself still reports the signal in its own exit status)."""
+    _, _, _, proc, log = server
+    proc.send_signal(signal.SIGINT)
+    proc.wait(timeout=60)
+    text = log.read_text()
+    assert "[rank0]: Traceback" not in text and "[rank1]: Traceback" not in text, text[-3000:]
