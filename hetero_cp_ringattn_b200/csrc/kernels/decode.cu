@@ -795,8 +795,12 @@ const char* decode_attn(const DecodeAttnArgs& a, cudaStream_t s) {
   cudaError_t e = cudaErrorInvalidValue;
 #define HCP_DEC_CASE(DD, GG) \
   if (a.D == DD && G == GG) e = launch_attn<DD, GG>(tm, a, s);
-  HCP_DEC_CASE(64, 1) HCP_DEC_CASE(64, 2) HCP_DEC_CASE(64, 4) HCP_DEC_CASE(64, 8)
-  HCP_DEC_CASE(128, 1) HCP_DEC_CASE(128, 2) HCP_DEC_CASE(128, 4) HCP_DEC_CASE(128, 8)
+  // every GQA group size up to 8 query heads per KV head: 1, 2, 4, 8 (Llama 3, Qwen2.5-3B),
+  // 3 (Llama-3.2-3B), 5 (Qwen2.5-14B), 6 (Qwen2.5-1.5B), 7 (Qwen2-0.5B, Qwen2.5-7B)
+  HCP_DEC_CASE(64, 1) HCP_DEC_CASE(64, 2) HCP_DEC_CASE(64, 3) HCP_DEC_CASE(64, 4)
+  HCP_DEC_CASE(64, 5) HCP_DEC_CASE(64, 6) HCP_DEC_CASE(64, 7) HCP_DEC_CASE(64, 8)
+  HCP_DEC_CASE(128, 1) HCP_DEC_CASE(128, 2) HCP_DEC_CASE(128, 3) HCP_DEC_CASE(128, 4)
+  HCP_DEC_CASE(128, 5) HCP_DEC_CASE(128, 6) HCP_DEC_CASE(128, 7) HCP_DEC_CASE(128, 8)
 #undef HCP_DEC_CASE
   if (e == cudaErrorInvalidValue) return "decode_attn: unsupported (D, H/Hkv)";
   return e == cudaSuccess ? nullptr : cudaGetErrorString(e);
@@ -807,8 +811,10 @@ int decode_attn_ctas_per_sm(int D, int G) {
 #define HCP_DEC_OCC(DD, GG)                                                                      \
   if (D == DD && G == GG && prepare_attn<DD, GG>() == cudaSuccess)                                 \
     cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, decode_attn_kernel<DD, GG>, 128, DecCfg<DD>::SMEM);
-  HCP_DEC_OCC(64, 1) HCP_DEC_OCC(64, 2) HCP_DEC_OCC(64, 4) HCP_DEC_OCC(64, 8)
-  HCP_DEC_OCC(128, 1) HCP_DEC_OCC(128, 2) HCP_DEC_OCC(128, 4) HCP_DEC_OCC(128, 8)
+  HCP_DEC_OCC(64, 1) HCP_DEC_OCC(64, 2) HCP_DEC_OCC(64, 3) HCP_DEC_OCC(64, 4)
+  HCP_DEC_OCC(64, 5) HCP_DEC_OCC(64, 6) HCP_DEC_OCC(64, 7) HCP_DEC_OCC(64, 8)
+  HCP_DEC_OCC(128, 1) HCP_DEC_OCC(128, 2) HCP_DEC_OCC(128, 3) HCP_DEC_OCC(128, 4)
+  HCP_DEC_OCC(128, 5) HCP_DEC_OCC(128, 6) HCP_DEC_OCC(128, 7) HCP_DEC_OCC(128, 8)
 #undef HCP_DEC_OCC
   return n;
 }
@@ -957,8 +963,8 @@ extern "C" int hcp_decode_attention_noalloc(const void* q, const void* arena, in
   if (d != 64 && d != 128) return noalloc_fail(-4, "hcp_decode_attention_noalloc: head_dim must be 64 or 128");
   if (heads % hkv) return noalloc_fail(-5, "hcp_decode_attention_noalloc: heads % kv_heads != 0");
   const int G = heads / hkv;
-  if (G != 1 && G != 2 && G != 4 && G != 8)
-    return noalloc_fail(-6, "hcp_decode_attention_noalloc: heads / kv_heads must be 1, 2, 4 or 8");
+  if (G < 1 || G > 8)
+    return noalloc_fail(-6, "hcp_decode_attention_noalloc: heads / kv_heads must be 1 to 8");
   const NoAllocLayout lay = noalloc_layout(batch, heads, hkv, d, splits);
   if (lay.total > kNoAllocBytes)
     return noalloc_fail(-7, "hcp_decode_attention_noalloc: problem needs " + std::to_string(lay.total) +

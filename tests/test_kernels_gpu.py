@@ -230,10 +230,12 @@ def test_gemv_batch_larger_than_staging(dev):
 
 
 @pytest.mark.parametrize("L,T,h,hkv,d", [(1, 1, 4, 1, 64), (129, 1, 4, 1, 128), (300, 300, 16, 2, 128),
-                                         (257, 2, 8, 8, 64), (1000, 130, 16, 2, 64)])
+                                         (257, 2, 8, 8, 64), (1000, 130, 16, 2, 64),
+                                         (500, 200, 14, 2, 64), (300, 300, 24, 8, 128)])
 def test_attention_edge_shapes(dev, L, T, h, hkv, d):
     """A single key, a single query, MQA (one KV head), 8-head GQA groups, no GQA, a query block
-    one row past a tile: the queries are the last T positions of an L-token context."""
+    one row past a tile, groups of 7 and 3 query heads: the queries are the last T positions of
+    an L-token context."""
     torch.manual_seed(12)
     q_all = torch.randn(L, h, d, device=dev, dtype=torch.bfloat16)
     k_all = torch.randn(L, hkv, d, device=dev, dtype=torch.bfloat16)
