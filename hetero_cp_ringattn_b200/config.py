@@ -45,6 +45,7 @@ class ModelConfig:
     sliding_window: Optional[int] = None  # parsed, unused (as in the reference)
     use_sliding_window: Optional[bool] = None
     partial_rotary_factor: float = 1.0    # parsed, unused
+    rope_scaling: Optional[dict] = None   # HF rope_scaling: linear / llama3 / yarn frequencies
     name: str = "custom"
 
     # ------------------------------------------------------------------ derived
@@ -93,6 +94,11 @@ class ModelConfig:
             raise RingError("head_dim must be even for rotate-half RoPE")
         if self.hidden_act not in ("silu", "swish"):
             raise RingError(f"unsupported hidden_act {self.hidden_act}")
+        if self.rope_scaling:
+            kind = self.rope_scaling.get("rope_type", self.rope_scaling.get("type", "default"))
+            if kind not in ("default", "linear", "llama3", "yarn"):
+                raise RingError(f"unsupported rope_scaling type {kind!r} (default, linear, llama3, "
+                                "yarn)")
 
     # ------------------------------------------------------------------ io
     @classmethod
@@ -129,6 +135,7 @@ class ModelConfig:
             sliding_window=d.get("sliding_window"),
             use_sliding_window=d.get("use_sliding_window"),
             partial_rotary_factor=float(d.get("partial_rotary_factor", 1.0)),
+            rope_scaling=dict(d["rope_scaling"]) if d.get("rope_scaling") else None,
             name=d.get("_name_or_path", d.get("name", "custom")),
         )
         if cfg.num_kv_heads is not None:
@@ -164,6 +171,8 @@ class ModelConfig:
         }
         if self.head_dim_override:
             d["head_dim"] = self.head_dim_override
+        if self.rope_scaling:
+            d["rope_scaling"] = dict(self.rope_scaling)
         return d
 
 
@@ -173,12 +182,17 @@ def _preset(**kw) -> ModelConfig:
     return cfg
 
 
+# RoPE frequency scaling of the Llama 3.1 / 3.2 releases (their config.json `rope_scaling`)
+LLAMA3_ROPE_SCALING = {"rope_type": "llama3", "factor": 32.0, "low_freq_factor": 1.0,
+                       "high_freq_factor": 4.0, "original_max_position_embeddings": 8192}
+
 # Shapes named by the benchmark configs (random-init weights of these architectures).
 PRESETS = {
     "llama-3.2-1b": dict(name="llama-3.2-1b", hidden_size=2048, num_layers=16, num_heads=32,
                          num_kv_heads=8, intermediate_size=8192, vocab_size=128256,
                          rope_theta=500000.0, rms_norm_eps=1e-5, tie_word_embeddings=True,
                          max_position_embeddings=131072, torch_dtype="bfloat16",
+                         rope_scaling=dict(LLAMA3_ROPE_SCALING),
                          architectures=["LlamaForCausalLM"], eos_token_id=[128001]),
     "qwen2.5-3b": dict(name="qwen2.5-3b", hidden_size=2048, num_layers=36, num_heads=16,
                        num_kv_heads=2, intermediate_size=11008, vocab_size=151936,
@@ -192,6 +206,26 @@ PRESETS = {
                        # the 128k-prompt benchmark decodes 256 tokens past position 131072
                        max_position_embeddings=262144, torch_dtype="bfloat16",
                        architectures=["LlamaForCausalLM"], eos_token_id=[128001]),
+    # Further shapes of the model families the reference runs (its validation and serving runs
+    # use Qwen2-0.5B and Qwen2.5-7B): GQA groups of 7 and 3 query heads per KV head.
+    "qwen2-0.5b": dict(name="qwen2-0.5b", hidden_size=896, num_layers=24, num_heads=14,
+                       num_kv_heads=2, intermediate_size=4864, vocab_size=151936,
+                       rope_theta=1000000.0, rms_norm_eps=1e-6, tie_word_embeddings=True,
+                       attention_bias=True, max_position_embeddings=131072,
+                       torch_dtype="bfloat16", architectures=["Qwen2ForCausalLM"],
+                       eos_token_id=[151643]),
+    "qwen2.5-7b": dict(name="qwen2.5-7b", hidden_size=3584, num_layers=28, num_heads=28,
+                       num_kv_heads=4, intermediate_size=18944, vocab_size=152064,
+                       rope_theta=1000000.0, rms_norm_eps=1e-6, tie_word_embeddings=False,
+                       attention_bias=True, max_position_embeddings=131072,
+                       torch_dtype="bfloat16", architectures=["Qwen2ForCausalLM"],
+                       eos_token_id=[151643]),
+    "llama-3.2-3b": dict(name="llama-3.2-3b", hidden_size=3072, num_layers=28, num_heads=24,
+                         num_kv_heads=8, intermediate_size=8192, vocab_size=128256,
+                         rope_theta=500000.0, rms_norm_eps=1e-5, tie_word_embeddings=True,
+                         max_position_embeddings=131072, torch_dtype="bfloat16",
+                         rope_scaling=dict(LLAMA3_ROPE_SCALING),
+                         architectures=["LlamaForCausalLM"], eos_token_id=[128001]),
     # Tiny shapes used by tests (the reference's synthetic model is hidden 32, 2 layers, GQA 4/1,
     # vocab 100: rust/src/model/model.rs:676-740).
     "tiny": dict(name="tiny", hidden_size=32, num_layers=2, num_heads=4, num_kv_heads=1,

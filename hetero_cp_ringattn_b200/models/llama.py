@@ -116,7 +116,8 @@ class LlamaCPEngine:
                 max_batch * -(-decode_reserve // self.page_size) + 2
         self.kv = KvArenaManager(kv_pages, self.page_size, self.L)
         max_pos = self.max_context + max(decode_reserve, 1) + 8
-        cos, sin = ref.rope_cos_sin(torch.arange(max_pos, device=self.device), self.D, cfg.rope_theta)
+        cos, sin = ref.rope_cos_sin(torch.arange(max_pos, device=self.device), self.D, cfg.rope_theta,
+                                       scaling=cfg.rope_scaling)
         self.cos, self.sin = cos.contiguous(), sin.contiguous()
         self.reqs: Dict[int, RequestState] = {}
         self.prefill_epoch = 0
@@ -346,9 +347,9 @@ class LlamaCPEngine:
         for li, lw in enumerate(w.layers):
             h = ref.rmsnorm(x, lw.in_norm, cfg.rms_norm_eps)
             qkv = ref.linear(h, lw.wqkv, lw.bqkv)
-            q = ref.apply_rope(qkv[:, : self.H * self.D].view(T, self.H, self.D), pos, cfg.rope_theta)
+            q = ref.apply_rope(qkv[:, : self.H * self.D].view(T, self.H, self.D), pos, cfg.rope_theta, cfg.rope_scaling)
             k = ref.apply_rope(qkv[:, self.H * self.D:(self.H + self.Hkv) * self.D].view(T, self.Hkv, self.D),
-                               pos, cfg.rope_theta)
+                               pos, cfg.rope_theta, cfg.rope_scaling)
             v = qkv[:, (self.H + self.Hkv) * self.D:].reshape(T, self.Hkv, self.D)
             st.host_kv.append([k.clone(), v.clone(), pos.clone(), torch.ones(T, dtype=torch.bool)])
             o = self._ring_fold(q, pos, self._gather_rows(k), self._gather_rows(v),
@@ -485,9 +486,9 @@ class LlamaCPEngine:
         for li, lw in enumerate(w.layers):
             h = ref.rmsnorm(x, lw.in_norm, cfg.rms_norm_eps)
             qkv = ref.linear(h, lw.wqkv, lw.bqkv)
-            q = ref.apply_rope(qkv[:, : self.H * self.D].view(B, self.H, self.D), posn, cfg.rope_theta)
+            q = ref.apply_rope(qkv[:, : self.H * self.D].view(B, self.H, self.D), posn, cfg.rope_theta, cfg.rope_scaling)
             k = ref.apply_rope(qkv[:, self.H * self.D:(self.H + self.Hkv) * self.D].view(B, self.Hkv, self.D),
-                               posn, cfg.rope_theta)
+                               posn, cfg.rope_theta, cfg.rope_scaling)
             v = qkv[:, (self.H + self.Hkv) * self.D:].reshape(B, self.Hkv, self.D)
             outs = []
             for b, rid in enumerate(req_ids):
@@ -625,9 +626,9 @@ class LlamaCPEngine:
             if T:
                 h = ref.rmsnorm(x, lw.in_norm, cfg.rms_norm_eps)
                 qkv = ref.linear(h, lw.wqkv, lw.bqkv)
-                q = ref.apply_rope(qkv[:, : self.H * self.D].view(T, self.H, self.D), pos, cfg.rope_theta)
+                q = ref.apply_rope(qkv[:, : self.H * self.D].view(T, self.H, self.D), pos, cfg.rope_theta, cfg.rope_scaling)
                 k = ref.apply_rope(qkv[:, self.H * self.D:(self.H + self.Hkv) * self.D].view(T, self.Hkv, self.D),
-                                   pos, cfg.rope_theta)
+                                   pos, cfg.rope_theta, cfg.rope_scaling)
                 v = qkv[:, (self.H + self.Hkv) * self.D:].reshape(T, self.Hkv, self.D)
                 kv[0] = torch.cat([kv[0], k])
                 kv[1] = torch.cat([kv[1], v])

@@ -56,8 +56,8 @@ def forward(w: ModelWeights, ids: torch.Tensor, positions: Optional[torch.Tensor
         tap(f"q_proj_layer_{i}", q)
         tap(f"k_proj_layer_{i}", k)
         tap(f"v_proj_layer_{i}", v)
-        q = ref.apply_rope(q.reshape(L, H, D), pos, cfg.rope_theta)
-        k = ref.apply_rope(k.reshape(L, Hkv, D), pos, cfg.rope_theta)
+        q = ref.apply_rope(q.reshape(L, H, D), pos, cfg.rope_theta, cfg.rope_scaling)
+        k = ref.apply_rope(k.reshape(L, Hkv, D), pos, cfg.rope_theta, cfg.rope_scaling)
         tap(f"prefill_k_layer_{i}", k.transpose(0, 1).unsqueeze(0))
         tap(f"prefill_v_layer_{i}", v.view(L, Hkv, D).transpose(0, 1).unsqueeze(0))
         o, _ = ref.full_attention(q, k, v.view(L, Hkv, D), pos, pos, causal=True)

@@ -108,19 +108,30 @@ class ModelWeights:
         model_dir.mkdir(parents=True, exist_ok=True)
         with open(model_dir / "config.json", "w") as f:
             json.dump(self.cfg.to_hf_dict(), f, indent=2)
-        shard: Dict[str, torch.Tensor] = {}
+        # HF layout: one `model.safetensors`, or `model-0000i-of-0000n.safetensors` shards plus
+        # `model.safetensors.index.json` (transformers and this loader read either)
+        shards: list = [{}]
         size = 0
-        idx = 0
-        names = sorted(self.tensors)
-        for n in names:
+        total = 0
+        for n in sorted(self.tensors):
             t = self.tensors[n].detach().contiguous().cpu()
-            if size + t.numel() * t.element_size() > shard_bytes and shard:
-                save_file(shard, str(model_dir / f"model-{idx:05d}.safetensors"))
-                shard, size, idx = {}, 0, idx + 1
-            shard[n] = t
-            size += t.numel() * t.element_size()
-        if shard:
-            save_file(shard, str(model_dir / f"model-{idx:05d}.safetensors"))
+            nb = t.numel() * t.element_size()
+            if size + nb > shard_bytes and shards[-1]:
+                shards.append({})
+                size = 0
+            shards[-1][n] = t
+            size += nb
+            total += nb
+        if len(shards) == 1:
+            save_file(shards[0], str(model_dir / "model.safetensors"), metadata={"format": "pt"})
+            return
+        weight_map = {}
+        for i, shard in enumerate(shards):
+            fname = f"model-{i + 1:05d}-of-{len(shards):05d}.safetensors"
+            save_file(shard, str(model_dir / fname), metadata={"format": "pt"})
+            weight_map.update({n: fname for n in shard})
+        with open(model_dir / "model.safetensors.index.json", "w") as f:
+            json.dump({"metadata": {"total_size": total}, "weight_map": weight_map}, f, indent=2)
 
     @classmethod
     def random_init(cls, cfg: ModelConfig, seed: int = 0, device="cpu", dtype=torch.bfloat16,

@@ -143,17 +143,72 @@ def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
     return (y * w.float()).to(x.dtype)
 
 
-def rope_cos_sin(positions: torch.Tensor, head_dim: int, theta: float, dtype=torch.float32):
-    inv = 1.0 / (theta ** (torch.arange(0, head_dim, 2, dtype=torch.float64,
-                                        device=positions.device) / head_dim))
+def rope_inv_freq(head_dim: int, theta: float, scaling: Optional[dict] = None, device=None):
+    """RoPE inverse frequencies (float64, [D/2]) and the cos/sin amplitude.
+
+    Without `scaling`: theta ** (-2i / D). With an HF `rope_scaling` dict:
+      * linear: every frequency divided by `factor` (positions interpolated);
+      * llama3 (the Llama 3.1 release's frequency-dependent rule): wavelengths shorter than
+        original_max_position_embeddings / high_freq_factor keep their frequency, wavelengths
+        longer than original_max_position_embeddings / low_freq_factor are divided by `factor`,
+        and the band between is interpolated linearly in original_max / wavelength;
+      * yarn (Peng et al. 2023, "YaRN: Efficient Context Window Extension of Large Language
+        Models"): dimensions that rotate fewer than beta_slow times over the original context are
+        interpolated (divided by `factor`), those rotating more than beta_fast times are kept, a
+        linear ramp in between; cos and sin are scaled by attention_factor (default
+        0.1 ln(factor) + 1).
+    """
+    inv = 1.0 / (theta ** (torch.arange(0, head_dim, 2, dtype=torch.float64, device=device) /
+                           head_dim))
+    amp = 1.0
+    if not scaling:
+        return inv, amp
+    kind = scaling.get("rope_type", scaling.get("type", "default"))
+    factor = float(scaling.get("factor", 1.0))
+    if kind == "default":
+        return inv, amp
+    if kind == "linear":
+        return inv / factor, amp
+    orig = float(scaling.get("original_max_position_embeddings", 8192))
+    if kind == "llama3":
+        lo, hi = float(scaling.get("low_freq_factor", 1.0)), float(scaling.get("high_freq_factor", 4.0))
+        wavelen = 2 * math.pi / inv
+        smooth = ((orig / wavelen - lo) / (hi - lo)).clamp(0.0, 1.0)
+        mixed = (1.0 - smooth) * inv / factor + smooth * inv
+        out = torch.where(wavelen > orig / lo, inv / factor, mixed)
+        return torch.where(wavelen < orig / hi, inv, out), amp
+    if kind == "yarn":
+        beta_fast = float(scaling.get("beta_fast", 32.0))
+        beta_slow = float(scaling.get("beta_slow", 1.0))
+
+        def dim_of(rotations: float) -> float:   # dimension index rotating `rotations` times
+            return head_dim * math.log(orig / (rotations * 2 * math.pi)) / (2 * math.log(theta))
+
+        low = max(math.floor(dim_of(beta_fast)), 0)
+        high = min(math.ceil(dim_of(beta_slow)), head_dim - 1)
+        if low == high:
+            high += 0.001
+        ramp = ((torch.arange(head_dim // 2, dtype=torch.float64, device=device) - low) /
+                 (high - low)).clamp(0.0, 1.0)
+        keep = 1.0 - ramp                                  # 1: extrapolate (keep the frequency)
+        out = inv / factor * (1.0 - keep) + inv * keep
+        amp = float(scaling.get("attention_factor") or (0.1 * math.log(factor) + 1.0))
+        return out, amp
+    raise ValueError(f"unsupported rope_scaling type {kind!r}")
+
+
+def rope_cos_sin(positions: torch.Tensor, head_dim: int, theta: float, dtype=torch.float32,
+                 scaling: Optional[dict] = None):
+    inv, amp = rope_inv_freq(head_dim, theta, scaling, positions.device)
     f = positions.to(torch.float64).unsqueeze(-1) * inv.unsqueeze(0)   # [T, D/2]
-    return f.cos().to(dtype), f.sin().to(dtype)
+    return (f.cos() * amp).to(dtype), (f.sin() * amp).to(dtype)
 
 
-def apply_rope(x: torch.Tensor, positions: torch.Tensor, theta: float) -> torch.Tensor:
+def apply_rope(x: torch.Tensor, positions: torch.Tensor, theta: float,
+               scaling: Optional[dict] = None) -> torch.Tensor:
     """Rotate-half RoPE. x [T, heads, D] at absolute positions [T]."""
     d = x.shape[-1]
-    cos, sin = rope_cos_sin(positions, d, theta)
+    cos, sin = rope_cos_sin(positions, d, theta, scaling=scaling)
     cos = cos.unsqueeze(1)
     sin = sin.unsqueeze(1)
     xf = x.float()
