@@ -248,3 +248,35 @@ def test_session_lifecycle_matches_reference_rules(stack):
     bad = coord.generate([5] * 600, max_tokens=2, session_id="t", append=True)
     assert "error" in bad and "t" not in coord.sessions and not eng.reqs
     assert coord.ledger.free_bytes() == free0
+
+
+def test_kv_capacity_wall_queues_instead_of_failing(stack):
+    """More concurrent long prompts than the KV byte budget holds (the reference's KV-wall scan,
+    docs/PHASE3_KV_WALL_SCAN.md): admission keeps the ledger within budget, requests that do not
+    fit wait for KV to be released, every request completes with the oracle's tokens; a request
+    larger than the whole budget fails alone with a capacity error."""
+    from hetero_cp_ringattn_b200.parallel.capacity import KvLedger
+    cfg, w, eng, coord, tok = stack
+    saved = coord.ledger
+    per_req = (150 + 8) * cfg.num_layers * coord.bytes_per_token_layer
+    budget = int(2.5 * per_req)
+    coord.ledger = KvLedger([budget])
+    try:
+        outs, peak = {}, [0]
+        prompts = [[(7 * i + j) % cfg.vocab_size for j in range(140)] for i in range(5)]
+        for i, ids in enumerate(prompts):
+            coord.submit(Job(request_id=coord.next_request_id(), prompt_ids=ids, max_tokens=4,
+                             done=lambda r, i=i: outs.__setitem__(i, r)))
+        while len(outs) < len(prompts):
+            coord.iteration()
+            peak[0] = max(peak[0], coord.ledger.used[0])
+            assert len(coord.sched.active) <= 2
+        assert peak[0] <= budget
+        for i, ids in enumerate(prompts):
+            ref_tokens, _ = reference_model.greedy_generate(w, torch.tensor(ids), 3)
+            assert outs[i].get("tokens") == ref_tokens, outs[i]
+        huge = coord.generate([1] * 400, max_tokens=2)
+        assert "error" in huge and huge["status"] == 400
+        assert coord.ledger.used == [0] and not eng.reqs
+    finally:
+        coord.ledger = saved
