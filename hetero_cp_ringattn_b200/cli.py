@@ -372,7 +372,10 @@ def cmd_gen_prompt(args) -> int:
 
 
 def main(argv: Optional[List[str]] = None) -> int:
-    logging.basicConfig(level=os.environ.get("HCP_LOG", "WARNING"))
+    # every line names its rank (the reference prefixes [coordinator] / [worker N])
+    role = "coordinator" if os.environ.get("RANK", "0") == "0" else f"worker {os.environ['RANK']}"
+    logging.basicConfig(level=os.environ.get("HCP_LOG", "WARNING"),
+                        format=f"%(asctime)s [{role}] %(name)s %(levelname)s: %(message)s")
     ap = argparse.ArgumentParser(prog="hcp")
     sub = ap.add_subparsers(dest="cmd", required=True)
     c = sub.add_parser("correctness")
