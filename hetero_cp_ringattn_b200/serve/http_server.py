@@ -140,13 +140,23 @@ def make_handler(state: ApiState):
                 self.wfile.write(f"data: {data}\n\n".encode())
                 self.wfile.flush()
 
+            ids: list = []
+            sent = 0   # characters of the decoded text already streamed
             while True:
                 kind, a, b = events.get()
                 if kind == "tok":
+                    # incremental detokenization: decode the whole generation and stream the new
+                    # suffix, holding back a trailing partial character (a multi-byte character
+                    # split over tokens decodes to U+FFFD until its last byte arrives)
+                    ids.append(a)
+                    text = state.tok.decode(ids)
+                    if b is None and text.endswith("\ufffd"):
+                        delta = ""
+                    else:
+                        delta, sent = text[sent:], len(text)
                     chunk = {"id": f"hcp-completion-{rid}", "object": "text_completion",
                              "created": created, "model": model,
-                             "choices": [{"text": state.tok.decode([a]), "index": 0,
-                                          "finish_reason": b}]}
+                             "choices": [{"text": delta, "index": 0, "finish_reason": b}]}
                     send(json.dumps(chunk))
                 elif kind == "done":
                     if "error" in a:

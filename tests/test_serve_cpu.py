@@ -280,3 +280,37 @@ def test_kv_capacity_wall_queues_instead_of_failing(stack):
         assert coord.ledger.used == [0] and not eng.reqs
     finally:
         coord.ledger = saved
+
+
+def test_sse_streams_whole_characters():
+    """Streamed deltas are incremental detokenizations: a multi-byte UTF-8 character split over
+    tokens arrives whole, and the concatenated deltas equal the decoded completion."""
+    from hetero_cp_ringattn_b200.serve.coordinator import Metrics
+    from hetero_cp_ringattn_b200.serve.http_server import ApiServer, ApiState
+
+    tok = ByteTokenizer(512)
+    text = "héllo ✓ \U0001F600!"
+    gen = tok.encode(text)                       # one token per UTF-8 byte
+
+    class StubCoordinator:
+        metrics = Metrics()
+
+        def next_request_id(self):
+            return 1
+
+        def submit(self, job):
+            for i, t in enumerate(gen):
+                job.on_token(t, "length" if i == len(gen) - 1 else None)
+            job.done({"request_id": 1, "tokens": gen, "prompt_tokens": 1,
+                      "finish_reason": "length"})
+
+    srv = ApiServer(ApiState(StubCoordinator(), tok, "stub", 1)).start()
+    try:
+        sse = _post(srv.port, {"prompt": "x", "max_tokens": len(gen), "stream": True}, raw=True)
+    finally:
+        srv.stop()
+    events = [ln[6:] for ln in sse.split("\n") if ln.startswith("data: ")]
+    assert events[-1] == "[DONE]"
+    deltas = [json.loads(e)["choices"][0]["text"] for e in events[:-1]]
+    assert len(deltas) == len(gen) and "".join(deltas) == text
+    assert all("�" not in d for d in deltas)
