@@ -140,20 +140,24 @@ def make_handler(state: ApiState):
                 self.wfile.write(f"data: {data}\n\n".encode())
                 self.wfile.flush()
 
+            # incremental detokenization over a sliding window: decode the tokens since
+            # `prefix` (already streamed, kept as left context so merges and leading spaces
+            # decode as in the full text) and stream what `read` onward adds; a trailing partial
+            # character (a multi-byte character split over tokens decodes to U+FFFD until its
+            # last byte arrives) is held back until it completes or the stream ends
             ids: list = []
-            sent = 0   # characters of the decoded text already streamed
+            prefix = read = 0
             while True:
                 kind, a, b = events.get()
                 if kind == "tok":
-                    # incremental detokenization: decode the whole generation and stream the new
-                    # suffix, holding back a trailing partial character (a multi-byte character
-                    # split over tokens decodes to U+FFFD until its last byte arrives)
                     ids.append(a)
-                    text = state.tok.decode(ids)
-                    if b is None and text.endswith("\ufffd"):
+                    done_text = state.tok.decode(ids[prefix:read]) if read > prefix else ""
+                    text = state.tok.decode(ids[prefix:])
+                    if b is None and (text.endswith("\ufffd") or len(text) <= len(done_text)):
                         delta = ""
                     else:
-                        delta, sent = text[sent:], len(text)
+                        delta = text[len(done_text):]
+                        prefix, read = read, len(ids)
                     chunk = {"id": f"hcp-completion-{rid}", "object": "text_completion",
                              "created": created, "model": model,
                              "choices": [{"text": delta, "index": 0, "finish_reason": b}]}
