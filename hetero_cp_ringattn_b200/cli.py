@@ -231,6 +231,8 @@ def cmd_serve(args) -> int:
                         max_context=args.max_context, max_batch=args.max_batch_size)
     control = P.ControlPlane(group, rank, world)
     worker = Worker(eng, control)
+    if not args.no_warmup:
+        eng.warmup()   # decode graphs captured before the first request (every rank)
     caps = control.all_gather(query_device_capacity_mb(str(dev)))  # the handshake
     # torchrun forwards SIGINT / SIGTERM to every rank: both end the serve loop the same way
     signal.signal(signal.SIGTERM, _raise_interrupt)
@@ -421,6 +423,8 @@ def main(argv: Optional[List[str]] = None) -> int:
     s.add_argument("--session-continuation-tokens", type=int, default=64)
     s.add_argument("--http-addr", default=None)
     s.add_argument("--prompt-file", default=None, help="one prompt: the whole file")
+    s.add_argument("--no-warmup", action="store_true",
+                   help="skip the start-up dummy requests that capture the decode graphs")
     s.add_argument("--num-domains", type=int, default=None,
                    help="expected number of ranks (checked against WORLD_SIZE)")
     s.add_argument("--export-logits", default=None, metavar="DIR",

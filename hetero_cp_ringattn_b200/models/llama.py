@@ -692,6 +692,16 @@ class LlamaCPEngine:
         return torch.cat(toks)
 
     @torch.no_grad()
+    def warmup(self, batch_sizes: Optional[Sequence[int]] = None) -> None:
+        """Run short dummy requests through every decode batch bucket (1, 2, 4, 8 up to
+        max_batch) so kernel set-up and the decode CUDA-graph captures happen before the first
+        real request instead of inside its latency. SPMD: every rank calls it at the same point.
+        The dummy request ids (from 2^40) never meet a coordinator's ids."""
+        sizes = batch_sizes or [b for b in (1, 2, 4, 8) if b <= self.max_batch]
+        prompt = torch.arange(max(8, self.world), dtype=torch.int64) % self.cfg.vocab_size
+        for b in sizes:
+            self.generate_batch([prompt] * b, 2, first_id=(1 << 40) + 16 * b)
+
     def generate_batch(self, prompts: Sequence[torch.Tensor], max_new_tokens: int,
                        chunks_for=None, strategy="vanilla", first_id: int = 1 << 20) -> List[torch.Tensor]:
         """Greedy generation for several prompts (rust/src/model/generator.rs:123-270

@@ -289,3 +289,15 @@ def test_decode_perf_events_two_ranks(tmp_path):
     rows = [sum(e["kv_rows_appended"] for e in map(json.loads, open(tmp_path / f"perf{r}.jsonl"))
                 if e["event"] == "stationary_decode") for r in range(world)]
     assert sum(rows) == 3 * cfg.num_layers
+
+
+def test_warmup_leaves_no_state():
+    cfg, w = tiny_weights()
+    pw = PreparedWeights.from_weights(w, dtype=torch.float32)
+    eng = LlamaCPEngine(cfg, pw, device=torch.device("cpu"), max_context=128, max_batch=4)
+    free = eng.kv.alloc.free_pages
+    eng.warmup()
+    assert not eng.reqs and eng.kv.alloc.free_pages == free
+    prompt = torch.randint(0, cfg.vocab_size, (20,), generator=torch.Generator().manual_seed(3))
+    ref_tokens, _ = reference_model.greedy_generate(w, prompt, 3)
+    assert [int(t) for t in eng.generate_batch([prompt], 4)[0]] == ref_tokens
