@@ -410,6 +410,12 @@ class Coordinator:
             if job is None:
                 break
             did = True
+            if job.cancelled:   # the client left while the request was queued
+                self.trace.emit("aborted", request=job.request_id, completion_tokens=0)
+                if job.done:
+                    job.done({"request_id": job.request_id, "tokens": [],
+                              "prompt_tokens": len(job.prompt_ids), "finish_reason": "abort"})
+                continue
             try:
                 self._prefill(job)
             except CapacityError as e:
@@ -420,6 +426,12 @@ class Coordinator:
             except Exception as e:
                 self._fail(job, e)
         active = self.sched.active_list()
+        for a in [a for a in active if a.job.cancelled]:
+            # the client went away: finish now (KV released, or kept for a keep_kv session)
+            a.finish_reason = "abort"
+            self._finish(a)
+            did = True
+        active = [a for a in active if not a.job.cancelled]
         if active:
             did = True
             pairs = [[a.job.request_id, a.next_token] for a in active]

@@ -111,7 +111,7 @@ def make_handler(state: ApiState):
                 coord.metrics.bump("failed")
                 return self._text(400, str(e))
             if body.get("stream"):
-                return self._stream(rid, created, model, events)
+                return self._stream(rid, created, model, events, job)
             toks = []
             while True:
                 kind, a, b = events.get()
@@ -129,7 +129,7 @@ def make_handler(state: ApiState):
                              "finish_reason": res["finish_reason"]}],
                 "usage": {"prompt_tokens": pt, "completion_tokens": ct, "total_tokens": pt + ct}})
 
-        def _stream(self, rid, created, model, events):
+        def _stream(self, rid, created, model, events, job):
             self.send_response(200)
             self.send_header("Content-Type", "text/event-stream")
             self.send_header("Cache-Control", "no-cache")
@@ -137,8 +137,12 @@ def make_handler(state: ApiState):
             self.end_headers()
 
             def send(data: str):
-                self.wfile.write(f"data: {data}\n\n".encode())
-                self.wfile.flush()
+                try:
+                    self.wfile.write(f"data: {data}\n\n".encode())
+                    self.wfile.flush()
+                except OSError:   # the client closed the stream: stop generating for it
+                    job.cancelled = True
+                    raise
 
             # incremental detokenization over a sliding window: decode the tokens since
             # `prefix` (already streamed, kept as left context so merges and leading spaces
@@ -168,6 +172,12 @@ def make_handler(state: ApiState):
                     break
             send("[DONE]")
             self.close_connection = True
+
+        def handle_one_request(self):
+            try:
+                super().handle_one_request()
+            except (BrokenPipeError, ConnectionResetError):
+                self.close_connection = True   # client gone mid-stream; the job was cancelled
 
     return Handler
 

@@ -32,6 +32,7 @@ class Job:
     done: Optional[Callable[[dict], None]] = None
     enqueued_at: float = dataclasses.field(default_factory=time.time)
     holds_session: bool = False   # set by the coordinator while this job owns its session
+    cancelled: bool = False       # set by the API when the client went away: stop generating
 
 
 @dataclasses.dataclass

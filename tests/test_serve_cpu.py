@@ -314,3 +314,45 @@ def test_sse_streams_whole_characters():
     deltas = [json.loads(e)["choices"][0]["text"] for e in events[:-1]]
     assert len(deltas) == len(gen) and "".join(deltas) == text
     assert all("�" not in d for d in deltas)
+
+
+def test_stream_client_disconnect_aborts_generation(stack, tmp_path):
+    """A streaming client that goes away stops its generation: the request finishes with
+    finish_reason "abort" long before max_tokens and its KV is released."""
+    from hetero_cp_ringattn_b200.serve.coordinator import TraceSink
+    cfg, w, eng, coord, tok = stack
+    saved = coord.trace
+    coord.trace = TraceSink(str(tmp_path / "trace.jsonl"))
+    stop = threading.Event()
+    loop = threading.Thread(target=lambda: [coord.iteration() or stop.wait(0.002)
+                                            for _ in iter(stop.is_set, True)], daemon=True)
+    loop.start()
+    srv = ApiServer(ApiState(coord, tok, "tiny", 1)).start()
+    try:
+        req = urllib.request.Request(
+            f"http://127.0.0.1:{srv.port}/v1/completions",
+            data=json.dumps({"prompt": "abc", "max_tokens": 450, "stream": True,
+                             "ignore_eos": True}).encode(),
+            headers={"Content-Type": "application/json"})
+        r = urllib.request.urlopen(req, timeout=30)
+        assert r.readline().startswith(b"data: ")
+        r.close()
+        done = None
+        for _ in range(500):
+            evs = [json.loads(l) for l in open(tmp_path / "trace.jsonl")]
+            done = [e for e in evs if e["event"] == "completed"]
+            if done:
+                break
+            stop.wait(0.02)
+        assert done and done[0]["finish_reason"] == "abort"
+        assert done[0]["completion_tokens"] < 450
+        for _ in range(100):
+            if not eng.reqs:
+                break
+            stop.wait(0.02)
+        assert not eng.reqs and not coord.sched.active
+    finally:
+        srv.stop()
+        stop.set()
+        loop.join(timeout=5)
+        coord.trace = saved
