@@ -87,6 +87,9 @@ class LlamaCPEngine:
         self.cuda = self.device.type == "cuda"
         self.max_context = int(max_context)
         self.max_batch = int(max_batch)
+        if self.cuda and not 1 <= self.max_batch <= 8:
+            raise CapacityError(f"max_batch {self.max_batch}: the CUDA decode step batches 1 to 8 "
+                                "requests (graph buckets 1, 2, 4, 8)")
         # tokens per KV page: HCP_KV_CACHE_BLOCK_SIZE unless given; the arena is always paged
         # (HCP_KV_CACHE_BLOCK_TABLE has nothing to switch off)
         self.page_size = int(page_size if page_size is not None else self.env.kv_block_size)
