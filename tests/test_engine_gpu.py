@@ -50,3 +50,45 @@ def test_engine_gqa_groups_match_oracle(h, hkv, d, bias):
         scale = max(1.0, float(ref.std()))
         assert err.max() < 0.15 * scale and err.mean() < 0.025 * scale, \
             (i, float(err.max()), float(err.mean()), scale)
+
+
+def test_session_append_matches_oracle():
+    """A kept session continued by an appended segment (the keep_kv / append path): prefill,
+    decode, append a segment after the last generated token, decode again; every step's logits
+    against the oracle on the same token sequence."""
+    from hetero_cp_ringattn_b200.config import preset
+    from hetero_cp_ringattn_b200.models import reference_model
+    from hetero_cp_ringattn_b200.models.llama import LlamaCPEngine
+    from hetero_cp_ringattn_b200.models.weights import ModelWeights, PreparedWeights
+    dev = torch.device("cuda", 0)
+    cfg = preset("tiny-gpu")
+    hf = ModelWeights.random_init(cfg, seed=5, device=dev, dtype=torch.bfloat16)
+    w = PreparedWeights.from_weights(hf)
+    g = torch.Generator().manual_seed(9)
+    a = torch.randint(0, cfg.vocab_size, (300,), generator=g)
+    b = torch.randint(0, cfg.vocab_size, (150,), generator=g).tolist()
+    eng = LlamaCPEngine(cfg, w, device=dev, max_context=1024, max_batch=1, decode_reserve=64)
+    tok, lg = eng.prefill(3, a, [300], decode_horizon=4, keep_kv=True, return_logits=True)
+    seq = a.tolist() + [int(tok)]
+    got = [(len(seq) - 1, lg.float().cpu())]
+    for _ in range(3):
+        nxt = eng.decode_step([3], torch.tensor([seq[-1]], device=dev))
+        got.append((len(seq), eng.last_logits(1)[0].float().cpu()))
+        seq.append(int(nxt))
+    L0 = eng.reqs[3].context_len
+    seg = [seq[-1]] + b
+    tok2, lg2 = eng.append(3, torch.tensor(seg), list(range(L0, L0 + len(seg))), [1],
+                           return_logits=True)
+    seq = seq + b
+    got.append((len(seq), lg2.float().cpu()))
+    seq.append(int(tok2))
+    for _ in range(2):
+        nxt = eng.decode_step([3], torch.tensor([seq[-1]], device=dev))
+        got.append((len(seq), eng.last_logits(1)[0].float().cpu()))
+        seq.append(int(nxt))
+    eng.check_device()
+    eng.close()
+    for n, lgt in got:
+        ref = reference_model.forward(hf, torch.tensor(seq[:n], device=dev), last_only=True)[0]
+        err = (lgt - ref.float().cpu()).abs()
+        assert err.max() < 0.15 and err.mean() < 0.02, (n, float(err.max()), float(err.mean()))
