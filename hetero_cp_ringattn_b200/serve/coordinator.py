@@ -224,7 +224,8 @@ class Coordinator:
                self.bytes_per_token_layer for c, t in zip(continuation_split(n, tickets), tickets)]
         self.ledger.try_reserve(rid, per)
         self.trace.emit("kv_reserved", request=rid, bytes=per)
-        resp = self.run_command(P.StationaryContinuation(rid, seg, positions, tickets, 0))
+        horizon = max(1, job.max_tokens) + (self.args.session_continuation_tokens if job.keep_kv else 0)
+        resp = self.run_command(P.StationaryContinuation(rid, seg, positions, tickets, 0, horizon))
         if self.args.export_logits_dir and self.worker.last_logits is not None:
             export_logits_dump(self._dump_dir(rid), {"continuation_last_logits": self.worker.last_logits}, {
                 "mode": "service", "device": "distributed-workers", "request_id": rid,
@@ -297,7 +298,8 @@ class Coordinator:
             decode_logits = self._snapshot_logits()  # the decode graph reuses its buffer
             decode_argmax = int(d.token)
             positions = list(range(L + 1, L + 1 + n))
-            c = self.run_command(P.StationaryContinuation(rid, list(segment), positions, tickets, 0))
+            c = self.run_command(P.StationaryContinuation(rid, list(segment), positions, tickets, 0,
+                                                          max_tokens))
             cont_logits = self._snapshot_logits()
             nxt = int(c.token)
             generated.append(nxt)

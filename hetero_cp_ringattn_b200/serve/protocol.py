@@ -56,6 +56,7 @@ class StationaryContinuation:
     position_ids: List[int]
     capacity_tickets: List[int]
     starter_domain: int = 0
+    decode_horizon: int = 128            # decode tokens the continued request may still take
 
 
 @dataclasses.dataclass

@@ -81,7 +81,8 @@ class Worker:
                 P.validate_stationary_continuation(e.world, cmd.tokens, cmd.position_ids,
                                                    cmd.capacity_tickets, cmd.starter_domain)
                 tok, logits = e.append(cmd.request_id, torch.as_tensor(cmd.tokens, dtype=torch.int64),
-                                       cmd.position_ids, cmd.capacity_tickets, return_logits=True)
+                                       cmd.position_ids, cmd.capacity_tickets, return_logits=True,
+                                       extra_horizon=max(1, int(cmd.decode_horizon)))
                 self.last_logits = logits
                 return P.StationaryContinuationDone(cmd.request_id, int(tok))
             if isinstance(cmd, P.SyncGlobalSeqLen):

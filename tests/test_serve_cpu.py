@@ -356,3 +356,16 @@ def test_stream_client_disconnect_aborts_generation(stack, tmp_path):
         stop.set()
         loop.join(timeout=5)
         coord.trace = saved
+
+
+def test_session_append_longer_than_default_horizon(stack):
+    """An append may generate more tokens than the default continuation horizon: the horizon
+    travels with the continuation command."""
+    cfg, w, eng, coord, tok = stack
+    p1 = tok.encode("long")
+    r1 = coord.generate(p1, max_tokens=2, session_id="long", keep_kv=True)
+    seg = tok.encode(" tail")
+    r2 = coord.generate(seg, max_tokens=150, session_id="long", append=True)
+    assert "error" not in r2 and len(r2["tokens"]) == 150
+    ref, _ = reference_model.greedy_generate(w, torch.tensor(p1 + r1["tokens"] + seg), 149)
+    assert r2["tokens"] == ref
