@@ -253,7 +253,8 @@ def cmd_serve(args) -> int:
                          activation_reserve_mb=args.activation_reserve_mb,
                          session_continuation_tokens=args.session_continuation_tokens,
                          trace_jsonl=args.trace_jsonl, eos_ids=cfg.eos_token_id,
-                         export_logits_dir=args.export_logits)
+                         export_logits_dir=args.export_logits,
+                         prefill_chunk_tokens=args.prefill_chunk_tokens)
     coord = Coordinator(worker, control, tok, cfg, ca, capacities_mb=caps)
     prompts = []
     if args.prompt:
@@ -423,6 +424,9 @@ def main(argv: Optional[List[str]] = None) -> int:
     s.add_argument("--session-continuation-tokens", type=int, default=64)
     s.add_argument("--http-addr", default=None)
     s.add_argument("--prompt-file", default=None, help="one prompt: the whole file")
+    s.add_argument("--prefill-chunk-tokens", type=int, default=0,
+                   help="prefill prompts longer than this in pieces, decoding the active "
+                        "requests between pieces (0: one prefill per prompt)")
     s.add_argument("--no-warmup", action="store_true",
                    help="skip the start-up dummy requests that capture the decode graphs")
     s.add_argument("--num-domains", type=int, default=None,

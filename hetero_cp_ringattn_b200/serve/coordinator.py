@@ -47,6 +47,8 @@ class CoordinatorArgs:
     trace_jsonl: Optional[str] = None
     eos_ids: Optional[List[int]] = None
     export_logits_dir: Optional[str] = None  # per-request logits dumps (coordinator.rs:1170)
+    prefill_chunk_tokens: int = 0            # >0: prompts longer than this prefill in pieces,
+                                             # with decode steps of the active requests between
 
 
 class TraceSink:
@@ -59,6 +61,15 @@ class TraceSink:
             return
         with self.lock, open(self.path, "a") as f:
             f.write(json.dumps({"ts": time.time(), "event": kind, **kw}) + "\n")
+
+
+@dataclasses.dataclass
+class ChunkedPrefill:
+    """A prompt being prefilled piece by piece: `done` tokens have KV on the ranks."""
+    job: Job
+    chunks: List[int]        # per-rank token shares used for tickets and the KV ledger
+    done: int
+    horizon: int
 
 
 @dataclasses.dataclass
@@ -95,6 +106,7 @@ class Coordinator:
         self.metrics = Metrics()
         self.sessions: Dict[str, Session] = {}
         self._busy: set = set()   # session ids with a keep_kv / append request in flight
+        self._prefilling: List[ChunkedPrefill] = []
         self._ids = itertools.count(1)
         caps = list(capacities_mb) if capacities_mb else [UNKNOWN_CAPACITY] * self.world
         self.capacities_mb = caps
@@ -186,6 +198,9 @@ class Coordinator:
         except RingError as e:
             raise AdmissionError(str(e)) from e
         self._reserve(rid, chunks, horizon)  # CapacityError: requeued while others hold KV
+        piece = int(self.args.prefill_chunk_tokens)
+        if piece > 0 and len(job.prompt_ids) > max(piece, self.world) and not self.args.chunk_sizes:
+            return self._start_chunked(job, chunks, horizon, max(piece, self.world))
         try:
             resp = self.run_command(P.Prefill(rid, list(job.prompt_ids), chunks, self.args.strategy,
                                               horizon, self._tickets(chunks), job.keep_kv))
@@ -202,6 +217,63 @@ class Coordinator:
                 "prefill_argmax": int(resp.token)})
         req = ActiveRequest(job=job, chunks=chunks, next_position=len(job.prompt_ids))
         self._emit_token(req, resp.token)
+
+    # ------------------------------------------------------------------ chunked prefill
+    def _start_chunked(self, job: Job, chunks: List[int], horizon: int, first: int) -> None:
+        """Prefill the first `first` tokens with the ring layout; the rest follows one piece per
+        iteration as continuation segments (the engine's append path), so decode steps of the
+        active requests run between the pieces. The request holds a batch slot meanwhile."""
+        rid = job.request_id
+        pchunks = chunk_sizes(first, self.world, capacities_mb=self.capacities_mb,
+                              capacity_aware=self.args.capacity_aware, ratio=self.args.ratio,
+                              activation_reserve_mb=self.args.activation_reserve_mb)
+        try:
+            self.run_command(P.Prefill(rid, list(job.prompt_ids[:first]), pchunks,
+                                       self.args.strategy, horizon, self._tickets(chunks),
+                                       job.keep_kv))
+        except Exception:
+            self.ledger.release(rid)
+            raise
+        self.sched.occupy(rid)
+        self._prefilling.append(ChunkedPrefill(job, list(chunks), first, horizon))
+        self.trace.emit("prefill_chunk", request=rid, done=first, total=len(job.prompt_ids))
+
+    def _advance_chunked(self, pf: ChunkedPrefill) -> None:
+        job, rid = pf.job, pf.job.request_id
+        if job.cancelled:
+            self._prefilling.remove(pf)
+            self._abort_started(job)
+            return
+        n = len(job.prompt_ids)
+        end = min(n, pf.done + max(int(self.args.prefill_chunk_tokens), 1))
+        try:
+            resp = self.run_command(P.StationaryContinuation(
+                rid, list(job.prompt_ids[pf.done:end]), list(range(pf.done, end)),
+                self._tickets(pf.chunks), 0, pf.horizon))
+        except Exception as e:
+            self._prefilling.remove(pf)
+            self._fail(job, e)
+            return
+        pf.done = end
+        self.trace.emit("prefill_chunk", request=rid, done=end, total=n)
+        if end == n:
+            self._prefilling.remove(pf)
+            self.trace.emit("prefill_accepted", request=rid, chunks=pf.chunks,
+                            hops_per_prefill=self.cfg.num_layers * max(0, self.world - 1))
+            self._emit_token(ActiveRequest(job=job, chunks=pf.chunks, next_position=n), resp.token)
+
+    def _abort_started(self, job: Job) -> None:
+        """A request that holds KV but produced no token yet, whose client went away."""
+        self.sched.complete(job.request_id)
+        if job.holds_session:
+            self._busy.discard(job.session_id)
+            job.holds_session = False
+        self.run_command(P.ReleaseRequest(job.request_id))
+        self.ledger.release(job.request_id)
+        self.trace.emit("aborted", request=job.request_id, completion_tokens=0)
+        if job.done:
+            job.done({"request_id": job.request_id, "tokens": [],
+                      "prompt_tokens": len(job.prompt_ids), "finish_reason": "abort"})
 
     def _append(self, job: Job) -> None:
         sess = self.sessions.get(job.session_id)
@@ -427,6 +499,9 @@ class Coordinator:
                 self._fail(job, e)
             except Exception as e:
                 self._fail(job, e)
+        for pf in list(self._prefilling):
+            did = True
+            self._advance_chunked(pf)
         active = self.sched.active_list()
         for a in [a for a in active if a.job.cancelled]:
             # the client went away: finish now (KV released, or kept for a keep_kv session)

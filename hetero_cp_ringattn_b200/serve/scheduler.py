@@ -75,6 +75,10 @@ class BatchScheduler:
         self.active[req.job.request_id] = req
         self._core.activate(req.job.request_id)
 
+    def occupy(self, request_id: int) -> None:
+        """Take a batch slot for a request that is not decoding yet (a chunked prefill)."""
+        self._core.activate(request_id)
+
     def complete(self, request_id: int) -> Optional[ActiveRequest]:
         self._core.complete(request_id)
         return self.active.pop(request_id, None)

@@ -369,3 +369,34 @@ def test_session_append_longer_than_default_horizon(stack):
     assert "error" not in r2 and len(r2["tokens"]) == 150
     ref, _ = reference_model.greedy_generate(w, torch.tensor(p1 + r1["tokens"] + seg), 149)
     assert r2["tokens"] == ref
+
+
+def test_chunked_prefill_interleaves_with_decode(stack):
+    """With prefill_chunk_tokens a long prompt is prefilled piece by piece while an active
+    request keeps decoding between the pieces; both outputs equal the oracle's, and a keep_kv
+    session built by a chunked prefill continues correctly."""
+    cfg, w, eng, coord, tok = stack
+    coord.args.prefill_chunk_tokens = 16
+    try:
+        events = []
+        outs = {}
+        short = tok.encode("short one")
+        long_ = [(11 * j + 5) % cfg.vocab_size for j in range(100)]
+        for name, ids, n in (("short", short, 12), ("long", long_, 4)):
+            coord.submit(Job(request_id=coord.next_request_id(), prompt_ids=ids, max_tokens=n,
+                             on_token=lambda t, fr, name=name: events.append(name),
+                             done=lambda r, name=name: outs.__setitem__(name, r)))
+        while len(outs) < 2:
+            coord.iteration()
+        for name, ids, n in (("short", short, 12), ("long", long_, 4)):
+            ref, _ = reference_model.greedy_generate(w, torch.tensor(ids), n - 1)
+            assert outs[name]["tokens"] == ref
+        # the short request emitted tokens while the long prompt was still being prefilled
+        assert events.index("long") >= 5 and events[:5] == ["short"] * 5
+        r1 = coord.generate(long_, max_tokens=3, session_id="chunked", keep_kv=True)
+        seg = tok.encode(" next")
+        r2 = coord.generate(seg, max_tokens=3, session_id="chunked", append=True)
+        ref2, _ = reference_model.greedy_generate(w, torch.tensor(long_ + r1["tokens"] + seg), 2)
+        assert r2["tokens"] == ref2 and not eng.reqs
+    finally:
+        coord.args.prefill_chunk_tokens = 0

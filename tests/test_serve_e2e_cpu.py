@@ -243,6 +243,29 @@ def test_serve_bench_client_against_two_ranks(server):
     assert res["median_ttft_ms"] <= res["p99_ttft_ms"]
 
 
+def test_two_rank_chunked_prefill_cli(tmp_path):
+    """`serve --prefill-chunk-tokens` under torchrun on two ranks (zigzag, 3:1): the prompt is
+    prefilled in pieces (ring layout for the first, continuation segments after) and the tokens
+    equal the oracle's."""
+    cfg = preset("tiny")
+    w = ModelWeights.random_init(cfg, seed=7, dtype=torch.float32, std=0.2)
+    mdir = tmp_path / "model"
+    w.save(str(mdir))
+    prompt = [(13 * j + 1) % cfg.vocab_size for j in range(90)]
+    env = dict(os.environ, HCP_QUIC_TIMEOUT_SECS="60", PYTHONPATH=REPO, OMP_NUM_THREADS="2")
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2",
+           "--master-addr", "127.0.0.1", "--master-port", str(_port()),
+           "-m", "hetero_cp_ringattn_b200", "serve", "--model-dir", str(mdir), "--device", "cpu",
+           "--max-context", "256", "--ratio", "3:1", "--ring-strategy", "zigzag",
+           "--prefill-chunk-tokens", "20", "--max-tokens", "5",
+           "--prompt-token-ids", ",".join(map(str, prompt))]
+    out = subprocess.run(cmd, cwd=REPO, env=env, capture_output=True, text=True, timeout=300)
+    assert out.returncode == 0, out.stdout[-2000:] + out.stderr[-3000:]
+    res = json.loads([ln for ln in out.stdout.splitlines() if ln.startswith('{"prompt_token_ids"')][0])
+    ref, _ = reference_model.greedy_generate(w, torch.tensor(prompt), 4)
+    assert res["tokens"] == ref
+
+
 # stops the module's server: keep it the last test that uses the fixture
 def test_two_rank_server_exits_on_interrupt(server):
     """Ctrl-C reaches every rank through torchrun; each rank leaves its loop without a
