@@ -93,3 +93,14 @@ def test_infer_sampling_is_seeded(tmp_path, capsys):
     assert main(args[:-1] + ["4"]) == 0
     other = json.loads(capsys.readouterr().out.strip().splitlines()[-1])["tokens"]
     assert len(other) == 6
+
+
+def test_package_root_exports():
+    import hetero_cp_ringattn_b200 as h
+    for name in h.__all__:
+        assert getattr(h, name) is not None
+    eng = h.LlamaCPEngine(h.preset("tiny"),
+                          h.PreparedWeights.from_weights(h.ModelWeights.random_init(
+                              h.preset("tiny"), seed=0, dtype=torch.float32), dtype=torch.float32),
+                          device=torch.device("cpu"), max_context=64)
+    assert eng.world == 1
