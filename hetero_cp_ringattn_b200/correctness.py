@@ -19,7 +19,7 @@ import torch
 
 from .errors import ToleranceTier
 from .ops import reference as ref
-from .parallel.strategy import RingStrategy, layout_positions
+from .parallel.strategy import layout_positions
 
 
 @dataclasses.dataclass
