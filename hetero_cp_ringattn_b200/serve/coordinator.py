@@ -107,6 +107,7 @@ class Coordinator:
         self.sessions: Dict[str, Session] = {}
         self._busy: set = set()   # session ids with a keep_kv / append request in flight
         self._prefilling: List[ChunkedPrefill] = []
+        self.control_failed: Optional[str] = None   # set when the control group broke
         self._ids = itertools.count(1)
         caps = list(capacities_mb) if capacities_mb else [UNKNOWN_CAPACITY] * self.world
         self.capacities_mb = caps
@@ -139,10 +140,18 @@ class Coordinator:
 
     # ------------------------------------------------------------------ engine commands
     def run_command(self, cmd):
+        """Broadcast `cmd`, execute it here, gather every rank's response. A failure of the
+        control group itself (a rank died, the group timed out) leaves the job unusable: it is
+        recorded in `control_failed`, which /health reports, and re-raised."""
         with self.lock:
-            self.control.broadcast(cmd)
-            resp = self.worker.execute(cmd)
-            all_resp = self.control.gather(resp)
+            try:
+                self.control.broadcast(cmd)
+                resp = self.worker.execute(cmd)
+                all_resp = self.control.gather(resp)
+            except (RuntimeError, OSError) as e:
+                self.control_failed = f"{type(e).__name__}: {e}"
+                self.trace.emit("control_failed", error=self.control_failed)
+                raise
         errs = [r for r in (all_resp or [resp]) if isinstance(r, P.Error)]
         if errs:
             raise ProtocolError("; ".join(f"rank error: {e.message}" for e in errs))

@@ -64,6 +64,10 @@ def make_handler(state: ApiState):
 
         def do_GET(self):
             if self.path == "/health":
+                failed = getattr(state.coord, "control_failed", None)
+                if failed:   # a rank is gone: the job must be restarted (no elastic recovery)
+                    return self._json(503, {"status": "unhealthy", "workers_connected": 0,
+                                            "num_domains": state.num_domains, "error": failed})
                 return self._json(200, {"status": "ok", "workers_connected": state.workers_connected,
                                         "num_domains": state.num_domains})
             if self.path == "/metrics":

@@ -125,3 +125,55 @@ def test_errors_become_responses_and_the_worker_keeps_serving():
     r = worker.execute(P.StationaryDecode(2, r.token, 4, [1], 0, 0, 4))
     assert isinstance(r, P.DecodeDone)
     assert isinstance(worker.execute(P.ReleaseRequest(2)), P.Ack)
+
+
+def test_broken_control_group_fails_requests_and_health():
+    """A control-group failure (here a fake whose collectives raise, as a dead rank's gloo
+    connection does) fails the request with a 500, and /health turns 503 so an orchestrator can
+    restart the job; rank-level errors keep /health ok."""
+    import json
+    import urllib.error
+    import urllib.request
+    from hetero_cp_ringattn_b200.serve.coordinator import Coordinator, CoordinatorArgs
+    from hetero_cp_ringattn_b200.serve.http_server import ApiServer, ApiState
+    from hetero_cp_ringattn_b200.serve.tokenizer import ByteTokenizer
+
+    class BrokenControl(P.ControlPlane):
+        def __init__(self):
+            super().__init__(None, 0, 1)
+            self.broken = False
+
+        def broadcast(self, cmd=None):
+            if self.broken:
+                raise RuntimeError("Connection closed by peer [127.0.0.1]:1234")
+            return cmd
+
+        def gather(self, resp):
+            return [resp]
+
+    cfg = preset("tiny")
+    w = ModelWeights.random_init(cfg, seed=0, dtype=torch.float32, std=0.2)
+    eng = LlamaCPEngine(cfg, PreparedWeights.from_weights(w, dtype=torch.float32),
+                        device=torch.device("cpu"), max_context=64)
+    control = BrokenControl()
+    tok = ByteTokenizer(cfg.vocab_size)
+    coord = Coordinator(Worker(eng, control), control, tok, cfg, CoordinatorArgs())
+    srv = ApiServer(ApiState(coord, tok, "tiny", 1)).start()
+
+    def health():
+        try:
+            with urllib.request.urlopen(f"http://127.0.0.1:{srv.port}/health", timeout=10) as r:
+                return r.status, json.loads(r.read())
+        except urllib.error.HTTPError as e:
+            return e.code, json.loads(e.read())
+
+    try:
+        ok = coord.generate(tok.encode("fine"), max_tokens=2)
+        assert "error" not in ok and health()[0] == 200
+        control.broken = True
+        bad = coord.generate(tok.encode("broken"), max_tokens=2)
+        assert bad.get("status") == 500 and "Connection closed" in bad["error"]
+        code, body = health()
+        assert code == 503 and body["status"] == "unhealthy" and "Connection closed" in body["error"]
+    finally:
+        srv.stop()
