@@ -122,8 +122,45 @@ def run_case(name: str, cfg: CaseConfig, seeds: Sequence[int], tier: ToleranceTi
         r[key]["max_abs_err"] <= tol.max_abs_err and r[key]["mean_abs_err"] <= tol.mean_abs_err
         and r[key]["nonfinite_mismatch"] == 0
         for r in per_seed for key in ("output", "lse"))
-    return {"name": name, "config": dataclasses.asdict(cfg), "seeds": list(seeds),
-            "worst_seed": worst, "passed": passed, "tolerance_tier": tier.value}
+    rep = {"name": name, "config": dataclasses.asdict(cfg), "seeds": list(seeds),
+           "worst_seed": worst, "passed": passed, "tolerance_tier": tier.value}
+    # the reference's report keys for the same case (rust/src/report.rs: status, seed,
+    # tolerance, metrics, config with per-domain entries, ring trace summary)
+    rep.update({
+        "status": "pass" if passed else "fail",
+        "seed": worst["seed"],
+        "tolerance": {"max_abs_err": tol.max_abs_err, "mean_abs_err": tol.mean_abs_err},
+        "metrics": {k: max(worst["output"][k], worst["lse"][k])
+                    for k in ("max_abs_err", "mean_abs_err")},
+    })
+    rep["config"].update({
+        "global_seq_len": cfg.global_seq_len, "dtype": str(dtype).replace("torch.", ""),
+        "domains": [{"domain_id": f"domain-{d}", "seq_chunk_len": c, "block_size": b,
+                     "device": "model"} for d, (c, b) in enumerate(zip(cfg.chunks, cfg.block_sizes))]})
+    rep["ring_trace_summary"] = ring_trace_summary(cfg)
+    return rep
+
+
+def ring_trace_summary(cfg: CaseConfig, first: int = 4) -> list:
+    """Per domain: its positions, how many KV blocks it folds and the first `first` of them in
+    fold order (own chunk first, then the ring's other sources), as ring_attention_model walks
+    them. Blocks index each source's local rows; with the vanilla layout those are global
+    positions."""
+    n = cfg.domains
+    offs = [sum(cfg.chunks[:d]) for d in range(n)]
+    out = []
+    for t in range(n):
+        blocks = []
+        for step in range(n):
+            src = (t + step) % n
+            bs = max(1, int(cfg.block_sizes[src]))
+            for b0 in range(0, cfg.chunks[src], bs):
+                b1 = min(cfg.chunks[src], b0 + bs)
+                blocks.append({"source_domain": f"domain-{src}", "block_start": offs[src] + b0,
+                               "block_stop": offs[src] + b1, "block_len": b1 - b0})
+        out.append({"domain_id": f"domain-{t}", "seq_offset": offs[t], "seq_chunk_len": cfg.chunks[t],
+                    "block_visits": len(blocks), "first_blocks": blocks[:first]})
+    return out
 
 
 def case_from_ring_config(cfg) -> CaseConfig:
@@ -141,9 +178,12 @@ def run_suite(tier: ToleranceTier = ToleranceTier.STRICT, stress_seeds: int = 5,
         small = cfg.global_seq_len <= 256
         seeds = list(range(stress_seeds)) if small else [0]
         reports.append(run_case(name, cfg, seeds, tier, dtype))
+    n_pass = sum(1 for r in reports if r["passed"])
     return {"suite": "ring_attention_correctness", "tolerance": dataclasses.asdict(tier.tolerance()),
-            "passed": all(r["passed"] for r in reports), "cases": reports,
-            "elapsed_s": time.time() - t0}
+            "passed": n_pass == len(reports), "cases": reports, "elapsed_s": time.time() - t0,
+            # the reference's top-level keys
+            "status": "pass" if n_pass == len(reports) else "fail",
+            "summary": {"cases": len(reports), "passed": n_pass, "failed": len(reports) - n_pass}}
 
 
 def write_report(report: dict, path: str) -> None:

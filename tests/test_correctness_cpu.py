@@ -73,3 +73,24 @@ def test_domain_layout_files_run_as_cases(tmp_path):
     assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
     names = [c["name"] for c in json.load(open(out))["cases"]]
     assert os.path.basename(files[0]) in names
+
+
+def test_report_carries_the_reference_schema(tmp_path):
+    """Reports also carry the reference's keys (reports/ringattn_correctness.json: status,
+    summary, per case status / seed / tolerance / metrics / domains / ring_trace_summary); the
+    trace of the 2-domain uneven case equals the reference report's."""
+    from hetero_cp_ringattn_b200.correctness import default_cases, run_case
+    from hetero_cp_ringattn_b200.errors import ToleranceTier
+    name, cfg = default_cases()[0]
+    rep = run_case(name, cfg, [42], ToleranceTier.STRICT)
+    assert rep["status"] == "pass" and rep["seed"] == 42
+    assert set(rep["tolerance"]) == {"max_abs_err", "mean_abs_err"}
+    assert rep["metrics"]["max_abs_err"] < 1e-12
+    assert rep["config"]["global_seq_len"] == 128
+    assert [d["seq_chunk_len"] for d in rep["config"]["domains"]] == [80, 48]
+    t0, t1 = rep["ring_trace_summary"]
+    assert (t0["seq_offset"], t0["block_visits"], t1["seq_offset"], t1["block_visits"]) == (0, 9, 80, 9)
+    assert [(b["block_start"], b["block_stop"]) for b in t0["first_blocks"]] == \
+        [(0, 16), (16, 32), (32, 48), (48, 64)]
+    assert [(b["source_domain"], b["block_start"], b["block_len"]) for b in t1["first_blocks"][:1]] == \
+        [("domain-1", 80, 12)]
