@@ -13,7 +13,8 @@
 //     self_driving.rs:146-331 reserved slabs);
 //   * the iterative batch scheduler's queue / active-set core (rust/src/distributed/scheduler.rs);
 //   * the binary frames of the coordinator <-> rank control protocol
-//     (rust/src/distributed/protocol.rs:14-192 message set).
+//     (rust/src/distributed/protocol.rs:14-192 message set);
+//   * a float64 attention / ring-attention oracle (rust/src/smoke/reference_algo.rs).
 #pragma once
 
 #include <condition_variable>
@@ -199,5 +200,23 @@ std::vector<Field> DecodeFrame(const std::string& frame, int* type);
 struct ProtocolError : RingError {
   using RingError::RingError;
 };
+
+// ----------------------------------------------------------------------------- f64 oracle
+// Double-precision attention oracle on the CPU (the reference's f64 ring algorithm check):
+// q [L, H, D], k / v [L, Hkv, D] row-major; GQA by head // (H / Hkv); causal compares positions.
+struct AttnResult {
+  std::vector<double> o;    // [L, H, D]
+  std::vector<double> lse;  // [H, L] natural log; -inf for a row with no visible key
+};
+AttnResult FullAttentionF64(const std::vector<double>& q, const std::vector<double>& k,
+                            const std::vector<double>& v, int64_t L, int64_t H, int64_t Hkv,
+                            int64_t D, bool causal);
+// Ring attention with uneven chunks: rank t owns positions[t] (global positions, any layout) and
+// folds the sources (t + step) % N in blocks of block_sizes[source] rows with an online softmax;
+// fully-future blocks are skipped when causal. Returns the same layout as FullAttentionF64.
+AttnResult RingAttentionF64(const std::vector<double>& q, const std::vector<double>& k,
+                            const std::vector<double>& v, int64_t L, int64_t H, int64_t Hkv,
+                            int64_t D, const std::vector<std::vector<int64_t>>& positions,
+                            const std::vector<int64_t>& block_sizes, bool causal);
 
 }  // namespace hcp::host

@@ -209,6 +209,38 @@ PYBIND11_MODULE(_host, m) {
     return py::make_tuple(type, out);
   }, py::arg("frame"));
 
+  // f64 attention oracle: q [L, H, D], k / v [L, Hkv, D] float64 arrays
+  using F64Arr = py::array_t<double, py::array::c_style | py::array::forcecast>;
+  auto vec3 = [](const F64Arr& a, int64_t* L, int64_t* H, int64_t* D) {
+    if (a.ndim() != 3) throw RingError("attention oracle: expected a [L, heads, D] array");
+    *L = a.shape(0);
+    *H = a.shape(1);
+    *D = a.shape(2);
+    return std::vector<double>(a.data(), a.data() + a.size());
+  };
+  auto result = [](const AttnResult& r, int64_t L, int64_t H, int64_t D) {
+    py::array_t<double> o({py::ssize_t(L), py::ssize_t(H), py::ssize_t(D)});
+    py::array_t<double> lse({py::ssize_t(H), py::ssize_t(L)});
+    if (!r.o.empty()) std::memcpy(o.mutable_data(), r.o.data(), r.o.size() * sizeof(double));
+    if (!r.lse.empty()) std::memcpy(lse.mutable_data(), r.lse.data(), r.lse.size() * sizeof(double));
+    return py::make_tuple(o, lse);
+  };
+  m.def("attention_f64", [vec3, result](const F64Arr& q, const F64Arr& k, const F64Arr& v, bool causal) {
+    int64_t L, H, D, Lk, Hkv, Dk;
+    auto qv = vec3(q, &L, &H, &D), kv = vec3(k, &Lk, &Hkv, &Dk), vv = vec3(v, &Lk, &Hkv, &Dk);
+    return result(FullAttentionF64(qv, kv, vv, L, H, Hkv, D, causal), L, H, D);
+  }, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("causal"));
+  m.def("ring_attention_f64", [vec3, result](const F64Arr& q, const F64Arr& k, const F64Arr& v,
+                                             const py::list& positions,
+                                             const std::vector<int64_t>& block_sizes, bool causal) {
+    int64_t L, H, D, Lk, Hkv, Dk;
+    auto qv = vec3(q, &L, &H, &D), kv = vec3(k, &Lk, &Hkv, &Dk), vv = vec3(v, &Lk, &Hkv, &Dk);
+    std::vector<std::vector<int64_t>> pos;
+    for (const auto& p : positions) pos.push_back(ToVec(p));
+    return result(RingAttentionF64(qv, kv, vv, L, H, Hkv, D, pos, block_sizes, causal), L, H, D);
+  }, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("positions"), py::arg("block_sizes"),
+     py::arg("causal"));
+
   // scheduler core
   py::class_<BatchSchedulerCore>(m, "BatchSchedulerCore")
       .def(py::init<int64_t>(), py::arg("max_batch_size"))

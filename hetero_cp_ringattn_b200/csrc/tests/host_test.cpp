@@ -4,7 +4,9 @@
 // Exit status 0 and "host_test ok" on success; the first failed check prints its line.
 #include <cstdio>
 #include <cstdlib>
+#include <cmath>
 #include <cstring>
+#include <random>
 #include <thread>
 
 #include "../host/hcp_host.h"
@@ -217,6 +219,45 @@ static void Protocol() {
   CHECK(Throws<ProtocolError>([&] { EncodeFrame(3, {Arr({1, 2, 3})}); }));
 }
 
+static void Oracle() {
+  // the reference's seven uneven chunk / block cases (non-causal MHA) plus causal GQA layouts:
+  // ring == full attention in double precision
+  struct Case {
+    V chunks, blocks;
+    int64_t H, Hkv, D;
+    bool causal;
+    RingStrategy s;
+  };
+  const std::vector<Case> cases = {
+      {{80, 48}, {16, 12}, 4, 4, 16, false, RingStrategy::kVanilla},
+      {{64, 40, 56}, {32, 10, 14}, 3, 3, 24, false, RingStrategy::kVanilla},
+      {{32, 64, 48, 48}, {7, 16, 11, 13}, 2, 2, 32, false, RingStrategy::kVanilla},
+      {{512, 256, 256}, {128, 64, 64}, 8, 8, 64, false, RingStrategy::kVanilla},
+      {{64}, {64}, 4, 4, 16, false, RingStrategy::kVanilla},
+      {{16, 16}, {1, 1}, 2, 2, 8, false, RingStrategy::kVanilla},
+      {{128}, {32}, 4, 4, 16, false, RingStrategy::kVanilla},
+      {{250, 250, 50}, {64, 64, 64}, 8, 2, 32, true, RingStrategy::kZigzag},
+      {{64, 32, 48, 16}, {16, 8, 16, 4}, 4, 1, 16, true, RingStrategy::kStriped},
+  };
+  std::mt19937_64 rng(42);
+  std::normal_distribution<double> nd(0.0, 1.0);
+  for (const auto& c : cases) {
+    int64_t L = 0;
+    for (int64_t x : c.chunks) L += x;
+    std::vector<double> q(size_t(L * c.H * c.D)), k(size_t(L * c.Hkv * c.D)), v(k.size());
+    for (auto* t : {&q, &k, &v})
+      for (auto& x : *t) x = nd(rng);
+    const auto full = FullAttentionF64(q, k, v, L, c.H, c.Hkv, c.D, c.causal);
+    const auto pos = BuildDomainPositions(BuildAssignment(c.chunks, c.s), int64_t(c.chunks.size()));
+    const auto ring = RingAttentionF64(q, k, v, L, c.H, c.Hkv, c.D, pos, c.blocks, c.causal);
+    double err = 0.0;
+    for (size_t i = 0; i < full.o.size(); ++i) err = std::max(err, std::fabs(full.o[i] - ring.o[i]));
+    for (size_t i = 0; i < full.lse.size(); ++i) err = std::max(err, std::fabs(full.lse[i] - ring.lse[i]));
+    CHECK(err < 1e-10);
+  }
+  CHECK(Throws<RingError>([] { FullAttentionF64({1.0}, {1.0}, {1.0}, 1, 2, 1, 1, false); }));
+}
+
 int main() {
   Layouts();
   Capacity();
@@ -224,6 +265,7 @@ int main() {
   Pages();
   Scheduler();
   Protocol();
+  Oracle();
   std::printf("host_test ok (%d checks)\n", g_checks);
   return 0;
 }

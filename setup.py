@@ -36,7 +36,7 @@ SOURCES = [
 
 # host runtime library (no CUDA, no libtorch): layouts, capacity, schedule, pages, scheduler
 HOST_SOURCES = ["layout.cpp", "capacity.cpp", "schedule.cpp", "pages.cpp", "scheduler.cpp",
-                "protocol.cpp", "host_bindings.cpp"]
+                "protocol.cpp", "ref_attention.cpp", "host_bindings.cpp"]
 
 setup(
     name=PKG,

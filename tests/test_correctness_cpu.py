@@ -94,3 +94,24 @@ def test_report_carries_the_reference_schema(tmp_path):
         [(0, 16), (16, 32), (32, 48), (48, 64)]
     assert [(b["source_domain"], b["block_start"], b["block_len"]) for b in t1["first_blocks"][:1]] == \
         [("domain-1", 80, 12)]
+
+
+@pytest.mark.parametrize("name,cfg", C.default_cases()[:4] + C.extended_cases()[1:],
+                         ids=lambda x: x if isinstance(x, str) else "")
+def test_native_oracle_matches_python_oracle(name, cfg):
+    """The C++ float64 oracle (host library) and the Python one agree on ring and full attention
+    to rounding level, for the reference's cases and causal GQA zigzag / striped layouts."""
+    import numpy as np
+    from hetero_cp_ringattn_b200.host import lib
+    from hetero_cp_ringattn_b200.ops import reference as ref
+    from hetero_cp_ringattn_b200.parallel.strategy import layout_positions
+    q, k, v = C.make_case_tensors(cfg, seed=3)
+    pos = layout_positions(cfg.chunks, cfg.strategy)
+    o_n, l_n = lib().ring_attention_f64(q.numpy(), k.numpy(), v.numpy(), list(pos),
+                                        list(cfg.block_sizes), cfg.causal)
+    f_n, fl_n = lib().attention_f64(q.numpy(), k.numpy(), v.numpy(), cfg.causal)
+    L = cfg.global_seq_len
+    all_pos = torch.arange(L)
+    f_p, fl_p = ref.full_attention(q, k, v, all_pos, all_pos, causal=cfg.causal)
+    assert np.abs(f_n - f_p.numpy()).max() < 1e-12 and np.abs(fl_n - fl_p.numpy()).max() < 1e-12
+    assert np.abs(o_n - f_p.numpy()).max() < 1e-10 and np.abs(l_n - fl_p.numpy()).max() < 1e-10

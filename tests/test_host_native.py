@@ -1,7 +1,8 @@
 """The host runtime library's own C++ test (`csrc/tests/host_test.cpp`), built with g++ and run
 on the CPU: reference golden vectors for layouts, capacity allocation, admission and the KV-growth
 schedule, the page allocator, the batch scheduler core under concurrent producers, and the control
-protocol's binary frames (round trips, every truncation, versions, lying counts)."""
+protocol's binary frames (round trips, every truncation, versions, lying counts), and the f64
+ring-attention oracle against full attention on the reference's cases plus causal GQA layouts."""
 
 import os
 import shutil
@@ -13,7 +14,8 @@ CSRC = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))),
                     "hetero_cp_ringattn_b200", "csrc")
 SOURCES = ["tests/host_test.cpp"] + [f"host/{f}" for f in ("layout.cpp", "capacity.cpp",
                                                          "schedule.cpp", "pages.cpp",
-                                                         "scheduler.cpp", "protocol.cpp")]
+                                                         "scheduler.cpp", "protocol.cpp",
+                                                         "ref_attention.cpp")]
 
 
 @pytest.mark.skipif(shutil.which("g++") is None, reason="no C++ compiler")
