@@ -71,7 +71,7 @@ def cmd_correctness(args) -> int:
     tier = ToleranceTier.parse(args.tolerance_tier)
     extra = [(os.path.basename(p), case_from_ring_config(RingAttnConfig.from_file(p)))
              for p in (args.config or [])]
-    rep = run_suite(tier, stress_seeds=args.stress_test, extra_cases=extra)
+    rep = run_suite(tier, stress_seeds=args.stress_test, extra_cases=extra, oracle=args.oracle)
     for c in rep["cases"]:
         w = c["worst_seed"]
         print(f"[{'PASS' if c['passed'] else 'FAIL'}] {c['name']}: out max_abs={w['output']['max_abs_err']:.3e} "
@@ -385,6 +385,8 @@ def main(argv: Optional[List[str]] = None) -> int:
     c.add_argument("--report-path", default=None)
     c.add_argument("--tolerance-tier", default="strict")
     c.add_argument("--stress-test", type=int, default=5)
+    c.add_argument("--oracle", choices=["python", "native"], default="python",
+                   help="float64 oracle: torch (python) or the C++ host library (native)")
     c.add_argument("--config", action="append", default=None,
                    help="domain layout JSON (global_seq_len, heads, domains[seq_chunk_len, block_size])")
     c.set_defaults(fn=cmd_correctness)

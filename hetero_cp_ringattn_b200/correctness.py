@@ -93,9 +93,19 @@ def make_case_tensors(cfg: CaseConfig, seed: int, dtype=torch.float64, device="c
         v.to(device=device, dtype=dtype)
 
 
-def run_case_single_seed(cfg: CaseConfig, seed: int, dtype=torch.float64) -> dict:
+def run_case_single_seed(cfg: CaseConfig, seed: int, dtype=torch.float64,
+                         oracle: str = "python") -> dict:
     q, k, v = make_case_tensors(cfg, seed, dtype)
     L = cfg.global_seq_len
+    if oracle == "native":
+        # the C++ float64 oracle of the host library (both the ring and the full attention)
+        from .host import lib
+        qn, kn, vn = (t.double().numpy() for t in (q, k, v))
+        pos = layout_positions(cfg.chunks, cfg.strategy)
+        fo, fl = lib().attention_f64(qn, kn, vn, cfg.causal)
+        ro, rl = lib().ring_attention_f64(qn, kn, vn, list(pos), list(cfg.block_sizes), cfg.causal)
+        return {"seed": seed, "output": _metrics(torch.from_numpy(ro), torch.from_numpy(fo)),
+                "lse": _metrics(torch.from_numpy(rl), torch.from_numpy(fl))}
     pos_all = torch.arange(L)
     full_o, full_lse = ref.full_attention(q, k, v, pos_all, pos_all, causal=cfg.causal)
     positions = [torch.as_tensor(p) for p in layout_positions(cfg.chunks, cfg.strategy)]
@@ -114,8 +124,8 @@ def run_case_single_seed(cfg: CaseConfig, seed: int, dtype=torch.float64) -> dic
 
 
 def run_case(name: str, cfg: CaseConfig, seeds: Sequence[int], tier: ToleranceTier,
-             dtype=torch.float64) -> dict:
-    per_seed = [run_case_single_seed(cfg, s, dtype) for s in seeds]
+             dtype=torch.float64, oracle: str = "python") -> dict:
+    per_seed = [run_case_single_seed(cfg, s, dtype, oracle) for s in seeds]
     worst = max(per_seed, key=lambda r: max(r["output"]["max_abs_err"], r["lse"]["max_abs_err"]))
     tol = tier.tolerance()
     passed = all(
@@ -123,7 +133,7 @@ def run_case(name: str, cfg: CaseConfig, seeds: Sequence[int], tier: ToleranceTi
         and r[key]["nonfinite_mismatch"] == 0
         for r in per_seed for key in ("output", "lse"))
     rep = {"name": name, "config": dataclasses.asdict(cfg), "seeds": list(seeds),
-           "worst_seed": worst, "passed": passed, "tolerance_tier": tier.value}
+           "worst_seed": worst, "passed": passed, "tolerance_tier": tier.value, "oracle": oracle}
     # the reference's report keys for the same case (rust/src/report.rs: status, seed,
     # tolerance, metrics, config with per-domain entries, ring trace summary)
     rep.update({
@@ -170,14 +180,15 @@ def case_from_ring_config(cfg) -> CaseConfig:
 
 
 def run_suite(tier: ToleranceTier = ToleranceTier.STRICT, stress_seeds: int = 5,
-              include_extended: bool = True, dtype=torch.float64, extra_cases=()) -> dict:
+              include_extended: bool = True, dtype=torch.float64, extra_cases=(),
+              oracle: str = "python") -> dict:
     t0 = time.time()
     cases = default_cases() + (extended_cases() if include_extended else []) + list(extra_cases)
     reports = []
     for name, cfg in cases:
         small = cfg.global_seq_len <= 256
         seeds = list(range(stress_seeds)) if small else [0]
-        reports.append(run_case(name, cfg, seeds, tier, dtype))
+        reports.append(run_case(name, cfg, seeds, tier, dtype, oracle))
     n_pass = sum(1 for r in reports if r["passed"])
     return {"suite": "ring_attention_correctness", "tolerance": dataclasses.asdict(tier.tolerance()),
             "passed": n_pass == len(reports), "cases": reports, "elapsed_s": time.time() - t0,

@@ -115,3 +115,12 @@ def test_native_oracle_matches_python_oracle(name, cfg):
     f_p, fl_p = ref.full_attention(q, k, v, all_pos, all_pos, causal=cfg.causal)
     assert np.abs(f_n - f_p.numpy()).max() < 1e-12 and np.abs(fl_n - fl_p.numpy()).max() < 1e-12
     assert np.abs(o_n - f_p.numpy()).max() < 1e-10 and np.abs(l_n - fl_p.numpy()).max() < 1e-10
+
+
+def test_cli_correctness_with_native_oracle(tmp_path):
+    out = tmp_path / "native.json"
+    assert cli_main(["correctness", "--oracle", "native", "--stress-test", "2",
+                     "--report-path", str(out)]) == 0
+    rep = json.loads(out.read_text())
+    assert rep["status"] == "pass" and rep["summary"]["failed"] == 0
+    assert all(c["oracle"] == "native" for c in rep["cases"])
