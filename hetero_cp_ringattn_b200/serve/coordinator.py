@@ -197,16 +197,16 @@ class Coordinator:
         if job.append:
             return self._append(job)
         horizon = max(1, job.max_tokens) + (self.args.session_continuation_tokens if job.keep_kv else 0)
-        if job.keep_kv:
-            if job.session_id in self.sessions or job.session_id in self._busy:
-                raise AdmissionError(f"session_id {job.session_id!r} already has resident KV")
-            self._busy.add(job.session_id)
-            job.holds_session = True
+        if job.keep_kv and (job.session_id in self.sessions or job.session_id in self._busy):
+            raise AdmissionError(f"session_id {job.session_id!r} already has resident KV")
         try:
             chunks = self._chunks(len(job.prompt_ids))
         except RingError as e:
             raise AdmissionError(str(e)) from e
         self._reserve(rid, chunks, horizon)  # CapacityError: requeued while others hold KV
+        if job.keep_kv:   # own the session only once admitted (a requeued job owns nothing)
+            self._busy.add(job.session_id)
+            job.holds_session = True
         piece = int(self.args.prefill_chunk_tokens)
         if piece > 0 and len(job.prompt_ids) > max(piece, self.world) and not self.args.chunk_sizes:
             return self._start_chunked(job, chunks, horizon, max(piece, self.world))
@@ -290,8 +290,6 @@ class Coordinator:
             raise AdmissionError(f"unknown or expired session {job.session_id!r}")
         if job.session_id in self._busy:
             raise AdmissionError(f"session {job.session_id!r} already has a request in flight")
-        self._busy.add(job.session_id)
-        job.holds_session = True
         rid = sess.request_id
         # the session's last generated token was never fed back, so it has no KV yet: it leads
         # the continuation segment (the context is exactly the text the client has seen)
@@ -303,8 +301,10 @@ class Coordinator:
         tot = sum(tickets)
         per = [(c + -(-max(1, job.max_tokens) * t // tot) + 1) * self.cfg.num_layers *
                self.bytes_per_token_layer for c, t in zip(continuation_split(n, tickets), tickets)]
-        self.ledger.try_reserve(rid, per)
+        self.ledger.try_reserve(rid, per)   # CapacityError: requeued while others hold KV
         self.trace.emit("kv_reserved", request=rid, bytes=per)
+        self._busy.add(job.session_id)      # own the session only once admitted
+        job.holds_session = True
         horizon = max(1, job.max_tokens) + (self.args.session_continuation_tokens if job.keep_kv else 0)
         resp = self.run_command(P.StationaryContinuation(rid, seg, positions, tickets, 0, horizon))
         if self.args.export_logits_dir and self.worker.last_logits is not None:

@@ -400,3 +400,32 @@ def test_chunked_prefill_interleaves_with_decode(stack):
         assert r2["tokens"] == ref2 and not eng.reqs
     finally:
         coord.args.prefill_chunk_tokens = 0
+
+
+def test_session_requests_survive_a_capacity_wait(stack):
+    """keep_kv and append jobs that wait for KV (ledger full while another request runs) are
+    admitted later and keep their session semantics."""
+    from hetero_cp_ringattn_b200.parallel.capacity import KvLedger
+    cfg, w, eng, coord, tok = stack
+    saved = coord.ledger
+    per_req = (60 + 40) * cfg.num_layers * coord.bytes_per_token_layer
+    coord.ledger = KvLedger([int(1.5 * per_req)])
+    try:
+        outs = {}
+        blocker = [(3 * j + 2) % cfg.vocab_size for j in range(60)]
+        p1 = [(5 * j + 1) % cfg.vocab_size for j in range(60)]
+        coord.submit(Job(request_id=coord.next_request_id(), prompt_ids=blocker, max_tokens=6,
+                         done=lambda r: outs.__setitem__("blocker", r)))
+        coord.submit(Job(request_id=coord.next_request_id(), prompt_ids=p1, max_tokens=3,
+                         session_id="wait", keep_kv=True, done=lambda r: outs.__setitem__("s", r)))
+        while len(outs) < 2:
+            coord.iteration()
+        assert "error" not in outs["s"] and "wait" in coord.sessions
+        ref1, _ = reference_model.greedy_generate(w, torch.tensor(p1), 2)
+        assert outs["s"]["tokens"] == ref1
+        seg = tok.encode(" go")
+        r2 = coord.generate(seg, max_tokens=2, session_id="wait", append=True)
+        ref2, _ = reference_model.greedy_generate(w, torch.tensor(p1 + ref1 + seg), 1)
+        assert r2["tokens"] == ref2 and not eng.reqs
+    finally:
+        coord.ledger = saved
