@@ -254,7 +254,8 @@ def cmd_serve(args) -> int:
                          session_continuation_tokens=args.session_continuation_tokens,
                          trace_jsonl=args.trace_jsonl, eos_ids=cfg.eos_token_id,
                          export_logits_dir=args.export_logits,
-                         prefill_chunk_tokens=args.prefill_chunk_tokens)
+                         prefill_chunk_tokens=args.prefill_chunk_tokens,
+                         max_queue=args.max_queue)
     coord = Coordinator(worker, control, tok, cfg, ca, capacities_mb=caps)
     prompts = []
     if args.prompt:
@@ -426,6 +427,8 @@ def main(argv: Optional[List[str]] = None) -> int:
     s.add_argument("--session-continuation-tokens", type=int, default=64)
     s.add_argument("--http-addr", default=None)
     s.add_argument("--prompt-file", default=None, help="one prompt: the whole file")
+    s.add_argument("--max-queue", type=int, default=0,
+                   help="reject requests with 503 while this many are queued (0: no limit)")
     s.add_argument("--prefill-chunk-tokens", type=int, default=0,
                    help="prefill prompts longer than this in pieces, decoding the active "
                         "requests between pieces (0: one prefill per prompt)")

@@ -39,6 +39,10 @@ class CapacityError(RingError):
     """KV byte admission / reservation failure."""
 
 
+class Overloaded(RingError):
+    """The coordinator's queue is at its limit; the HTTP API answers 503 (retry later)."""
+
+
 class AdmissionError(RingError):
     """The coordinator rejected a request before any rank ran it (e.g. a prompt shorter than
     the number of ranks). The HTTP API answers 400, as for a `CapacityError`."""

@@ -24,7 +24,7 @@ import threading
 import time
 from typing import Dict, List, Optional, Sequence
 
-from ..errors import AdmissionError, CapacityError, ProtocolError, RingError
+from ..errors import AdmissionError, CapacityError, Overloaded, ProtocolError, RingError
 from ..models.sampling import sample_token
 from ..parallel.capacity import (DEFAULT_ACTIVATION_RESERVE_MB, KvLedger, UNKNOWN_CAPACITY,
                                  chunk_sizes, continuation_split)
@@ -47,6 +47,7 @@ class CoordinatorArgs:
     trace_jsonl: Optional[str] = None
     eos_ids: Optional[List[int]] = None
     export_logits_dir: Optional[str] = None  # per-request logits dumps (coordinator.rs:1170)
+    max_queue: int = 0                       # >0: submissions beyond this many queued get 503
     prefill_chunk_tokens: int = 0            # >0: prompts longer than this prefill in pieces,
                                              # with decode steps of the active requests between
 
@@ -128,6 +129,10 @@ class Coordinator:
 
     def submit(self, job: Job) -> None:
         self.metrics.bump("total")
+        if self.args.max_queue and self.sched.queued >= self.args.max_queue:
+            self.metrics.bump("failed")
+            raise Overloaded(f"{self.sched.queued} requests queued (limit {self.args.max_queue}); "
+                             "retry later")
         if job.append or job.keep_kv:
             if not job.session_id:
                 raise ProtocolError(("append" if job.append else "keep_kv") + "=true requires session_id")

@@ -17,7 +17,7 @@ import time
 from http.server import BaseHTTPRequestHandler, ThreadingHTTPServer
 from typing import Optional
 
-from ..errors import ProtocolError
+from ..errors import Overloaded, ProtocolError
 from .scheduler import Job
 
 
@@ -111,6 +111,8 @@ def make_handler(state: ApiState):
                       done=lambda r: events.put(("done", r, None)))
             try:
                 coord.submit(job)
+            except Overloaded as e:
+                return self._text(503, str(e))
             except ProtocolError as e:
                 coord.metrics.bump("failed")
                 return self._text(400, str(e))

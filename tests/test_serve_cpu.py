@@ -429,3 +429,26 @@ def test_session_requests_survive_a_capacity_wait(stack):
         assert r2["tokens"] == ref2 and not eng.reqs
     finally:
         coord.ledger = saved
+
+
+def test_queue_limit_answers_503(stack):
+    cfg, w, eng, coord, tok = stack
+    from hetero_cp_ringattn_b200.errors import Overloaded
+    from hetero_cp_ringattn_b200.serve.http_server import ApiServer, ApiState
+    coord.args.max_queue = 2
+    srv = ApiServer(ApiState(coord, tok, "tiny", 1)).start()
+    try:
+        jobs = [Job(request_id=coord.next_request_id(), prompt_ids=[1, 2, 3], max_tokens=2)
+                for _ in range(2)]
+        for j in jobs:
+            coord.submit(j)
+        with pytest.raises(Overloaded):
+            coord.submit(Job(request_id=coord.next_request_id(), prompt_ids=[1, 2], max_tokens=1))
+        with pytest.raises(urllib.error.HTTPError) as ei:
+            _post(srv.port, {"prompt": "over the limit", "max_tokens": 1})
+        assert ei.value.code == 503
+        while coord.sched.queued or coord.sched.active:
+            coord.iteration()
+    finally:
+        srv.stop()
+        coord.args.max_queue = 0
