@@ -37,3 +37,18 @@ def test_kernel_bench_helpers():
     assert kb.causal_flops(8, 8, 2, 4) == 4.0 * 2 * 4 * 36
     p = kb.peaks()
     assert p["hbm_gbs"] > 0 and p["tflops"] > 0
+
+
+def test_host_bench_reports_native_and_json_costs(capsys):
+    import importlib.util
+    import json
+    import os
+    path = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))),
+                        "benchmarks", "host_bench.py")
+    spec = importlib.util.spec_from_file_location("host_bench", path)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    assert mod.main() == 0
+    out = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
+    f = out["prefill_frame_32k"]
+    assert f["native_ms"] > 0 and f["json_ms"] > 0 and f["bytes"] > 32768 * 8
