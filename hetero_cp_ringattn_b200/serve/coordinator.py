@@ -415,6 +415,21 @@ class Coordinator:
             return set()
         return set(job.stop_ids or self.args.eos_ids or [])
 
+    def _finish_reason(self, req: ActiveRequest, tok: int) -> Optional[str]:
+        """"stop" on an EOS / stop id or once the generated text contains a stop string (checked
+        on a tail window of tokens that covers the longest one), "length" at max_tokens."""
+        job = req.job
+        if tok in self._eos(job):
+            return "stop"
+        if job.stop_strings and self.tok is not None:
+            window = max(len(x) for x in job.stop_strings) + 8
+            tail = self.tok.decode(req.generated[-window:])
+            if any(x and x in tail for x in job.stop_strings):
+                return "stop"
+        if len(req.generated) >= job.max_tokens:
+            return "length"
+        return None
+
     def _emit_token(self, req: ActiveRequest, argmax_token: int) -> None:
         job = req.job
         tok = argmax_token
@@ -427,11 +442,7 @@ class Coordinator:
             req.first_token_at = time.time()
             self.trace.emit("first_token", request=job.request_id,
                             ttft_s=req.first_token_at - job.enqueued_at)
-        eos = self._eos(job)
-        if tok in eos:
-            req.finish_reason = "stop"
-        elif len(req.generated) >= job.max_tokens:
-            req.finish_reason = "length"
+        req.finish_reason = self._finish_reason(req, tok)
         if job.on_token:
             job.on_token(tok, req.finish_reason)
         if req.finish_reason:
@@ -538,11 +549,7 @@ class Coordinator:
                     tok = sample_token(logits[i], a.job.temperature, a.job.top_p)
                 a.generated.append(tok)
                 a.next_token = tok
-                eos = self._eos(a.job)
-                if tok in eos:
-                    a.finish_reason = "stop"
-                elif len(a.generated) >= a.job.max_tokens:
-                    a.finish_reason = "length"
+                a.finish_reason = self._finish_reason(a, tok)
                 if a.job.on_token:
                     a.job.on_token(tok, a.finish_reason)
                 if a.finish_reason:

@@ -29,6 +29,14 @@ def validate_session_fields(body: dict) -> Optional[str]:
     return None
 
 
+def _cut_at_stop(text: str, stops) -> str:
+    """The text before the earliest stop string (OpenAI semantics: the stop is not returned)."""
+    if not stops:
+        return text
+    cut = min((i for i in (text.find(x) for x in stops if x) if i >= 0), default=-1)
+    return text if cut < 0 else text[:cut]
+
+
 class ApiState:
     def __init__(self, coordinator, tokenizer, model_name: str, num_domains: int):
         self.coord = coordinator
@@ -98,15 +106,15 @@ def make_handler(state: ApiState):
             created = int(time.time())
             model = body.get("model") or state.model_name
             ids = state.tok.encode(body["prompt"])
-            stop_ids = None
-            if body.get("stop"):
-                stop_ids = [i for s in body["stop"] for i in state.tok.encode(s)[:1]]
+            stop = body.get("stop")
+            stop_strings = [stop] if isinstance(stop, str) else [x for x in (stop or []) if x]
             events: "queue.Queue" = queue.Queue()
             job = Job(request_id=rid, prompt_ids=ids, max_tokens=int(body.get("max_tokens", 20)),
                       temperature=float(body.get("temperature", 0.0)),
                       top_p=float(body.get("top_p", 1.0)), session_id=body.get("session_id"),
                       keep_kv=bool(body.get("keep_kv", False)), append=bool(body.get("append", False)),
-                      stop_ids=stop_ids, ignore_eos=bool(body.get("ignore_eos", False)),
+                      stop_strings=stop_strings or None,
+                      ignore_eos=bool(body.get("ignore_eos", False)),
                       on_token=lambda t, fr: events.put(("tok", t, fr)),
                       done=lambda r: events.put(("done", r, None)))
             try:
@@ -117,6 +125,8 @@ def make_handler(state: ApiState):
                 coord.metrics.bump("failed")
                 return self._text(400, str(e))
             if body.get("stream"):
+                if stop_strings:
+                    return self._stream_with_stops(rid, created, model, events, job, stop_strings)
                 return self._stream(rid, created, model, events, job)
             toks = []
             while True:
@@ -126,7 +136,7 @@ def make_handler(state: ApiState):
                     break
             if "error" in res:
                 return self._text(int(res.get("status", 500)), res["error"])
-            text = state.tok.decode(res["tokens"])
+            text = _cut_at_stop(state.tok.decode(res["tokens"]), stop_strings)
             pt, ct = res["prompt_tokens"], len(res["tokens"])
             return self._json(200, {
                 "id": f"hcp-completion-{rid}", "object": "text_completion", "created": created,
@@ -168,6 +178,52 @@ def make_handler(state: ApiState):
                     else:
                         delta = text[len(done_text):]
                         prefix, read = read, len(ids)
+                    chunk = {"id": f"hcp-completion-{rid}", "object": "text_completion",
+                             "created": created, "model": model,
+                             "choices": [{"text": delta, "index": 0, "finish_reason": b}]}
+                    send(json.dumps(chunk))
+                elif kind == "done":
+                    if "error" in a:
+                        send(json.dumps({"error": a["error"]}))
+                    break
+            send("[DONE]")
+            self.close_connection = True
+
+        def _stream_with_stops(self, rid, created, model, events, job, stops):
+            """Streaming with stop strings: the text is decoded whole each token and the last
+            (longest stop - 1) characters are held back until they cannot start a stop string,
+            so no part of a stop sequence is ever streamed (cost grows with the generation
+            length; only requests that set `stop` take this path)."""
+            self.send_response(200)
+            self.send_header("Content-Type", "text/event-stream")
+            self.send_header("Cache-Control", "no-cache")
+            self.send_header("Connection", "close")
+            self.end_headers()
+
+            def send(data: str):
+                try:
+                    self.wfile.write(f"data: {data}\n\n".encode())
+                    self.wfile.flush()
+                except OSError:
+                    job.cancelled = True
+                    raise
+
+            hold = max(len(x) for x in stops) - 1
+            ids: list = []
+            sent = 0
+            while True:
+                kind, a, b = events.get()
+                if kind == "tok":
+                    ids.append(a)
+                    text = _cut_at_stop(state.tok.decode(ids), stops)
+                    if b is None:
+                        upto = len(text) - hold
+                        if text.endswith("\ufffd"):
+                            upto = min(upto, len(text) - 1)
+                    else:
+                        upto = len(text)
+                    delta = text[sent:max(sent, upto)]
+                    sent = max(sent, upto)
                     chunk = {"id": f"hcp-completion-{rid}", "object": "text_completion",
                              "created": created, "model": model,
                              "choices": [{"text": delta, "index": 0, "finish_reason": b}]}

@@ -27,6 +27,7 @@ class Job:
     keep_kv: bool = False
     append: bool = False
     stop_ids: Optional[List[int]] = None
+    stop_strings: Optional[List[str]] = None   # text stop sequences (excluded from the output)
     ignore_eos: bool = False      # generate exactly max_tokens (benchmarks)
     on_token: Optional[Callable[[int, Optional[str]], None]] = None   # (token, finish_reason)
     done: Optional[Callable[[dict], None]] = None

@@ -452,3 +452,35 @@ def test_queue_limit_answers_503(stack):
     finally:
         srv.stop()
         coord.args.max_queue = 0
+
+
+def test_stop_strings_cut_the_completion(stack):
+    """`stop` ends generation once the text contains a stop string and the string is not
+    returned, in plain and streamed responses (no part of it is ever streamed)."""
+    cfg, w, eng, coord, tok = stack
+    from hetero_cp_ringattn_b200.serve.http_server import ApiServer, ApiState
+    prompt = "stop sequences"
+    ref_tokens, _ = reference_model.greedy_generate(w, torch.tensor(tok.encode(prompt)), 15)
+    full = tok.decode(ref_tokens)
+    stop = full[6:8]
+    expected = full[:full.find(stop)]
+    stopper = threading.Event()
+    loop = threading.Thread(target=lambda: [coord.iteration() or stopper.wait(0.002)
+                                            for _ in iter(stopper.is_set, True)], daemon=True)
+    loop.start()
+    srv = ApiServer(ApiState(coord, tok, "tiny", 1)).start()
+    try:
+        res = _post(srv.port, {"prompt": prompt, "max_tokens": 16, "stop": [stop, "never-there"]})
+        assert res["choices"][0]["text"] == expected
+        assert res["choices"][0]["finish_reason"] == "stop"
+        assert res["usage"]["completion_tokens"] < 16
+        sse = _post(srv.port, {"prompt": prompt, "max_tokens": 16, "stop": stop, "stream": True},
+                    raw=True)
+        events = [ln[6:] for ln in sse.split("\n") if ln.startswith("data: ")]
+        deltas = [json.loads(e)["choices"][0]["text"] for e in events[:-1]]
+        assert "".join(deltas) == expected
+        assert json.loads(events[-2])["choices"][0]["finish_reason"] == "stop"
+    finally:
+        srv.stop()
+        stopper.set()
+        loop.join(timeout=5)
