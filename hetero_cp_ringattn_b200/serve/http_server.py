@@ -78,6 +78,9 @@ def make_handler(state: ApiState):
                                             "num_domains": state.num_domains, "error": failed})
                 return self._json(200, {"status": "ok", "workers_connected": state.workers_connected,
                                         "num_domains": state.num_domains})
+            if self.path == "/v1/models":   # for OpenAI-style clients and benchmark tools
+                return self._json(200, {"object": "list", "data": [
+                    {"id": state.model_name, "object": "model", "owned_by": "hcp-b200"}]})
             if self.path == "/metrics":
                 m = state.coord.metrics
                 return self._json(200, {"total_requests": m.total, "completed_requests": m.completed,

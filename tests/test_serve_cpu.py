@@ -153,6 +153,8 @@ def test_http_api(stack):
         with urllib.request.urlopen(f"http://127.0.0.1:{srv.port}/health", timeout=10) as r:
             h = json.loads(r.read())
         assert h == {"status": "ok", "workers_connected": 1, "num_domains": 1}
+        with urllib.request.urlopen(f"http://127.0.0.1:{srv.port}/v1/models", timeout=10) as r:
+            assert json.loads(r.read())["data"][0]["id"] == "tiny"
         res = _post(srv.port, {"prompt": "ring attention", "max_tokens": 4})
         assert res["object"] == "text_completion"
         assert res["usage"]["completion_tokens"] == 4
