@@ -389,8 +389,9 @@ class LlamaCPEngine:
             own = (st.assignee[t] == self.rank)
             if self.cuda:
                 counts = st.kv.layer_counts
-                for li in np.nonzero(own)[0]:
-                    st.kv.check_room(int(li))
+                full = np.nonzero(own & (counts + 1 > st.kv.capacity))[0]
+                if full.size:
+                    st.kv.check_room(int(full[0]))   # raises for the first full layer
                 owner[b] = own
                 slot[b] = counts
                 ntok[:, b] = counts + own
@@ -403,8 +404,8 @@ class LlamaCPEngine:
         for b, rid in enumerate(req_ids):
             st = self.reqs[rid]
             if self.cuda:
-                for li in np.nonzero(owner[b])[0]:
-                    st.kv.slot_pos[li, st.kv.layer_counts[li]] = pos[b]
+                li = np.nonzero(owner[b])[0]
+                st.kv.slot_pos[li, st.kv.layer_counts[li]] = pos[b]
                 st.kv.layer_counts += owner[b]
             st.decode_offset += 1
             st.context_len += 1

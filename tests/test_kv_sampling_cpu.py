@@ -98,3 +98,72 @@ def test_top_p_samples_only_the_nucleus():
     assert set(draws) == {0, 1}
     frac0 = draws.count(0) / len(draws)
     assert abs(frac0 - 0.64 / 0.88) < 0.03
+
+
+def _old_meta_advance(eng, rids):
+    """The per-layer loop form of the decode bookkeeping (the oracle for the vectorised one)."""
+    B = len(rids)
+    pos = np.zeros(B, dtype=np.int32)
+    owner = np.zeros((B, eng.L), dtype=np.int32)
+    slot = np.zeros((B, eng.L), dtype=np.int32)
+    ntok = np.zeros((eng.L, B), dtype=np.int32)
+    for b, rid in enumerate(rids):
+        st = eng.reqs[rid]
+        pos[b] = st.context_len
+        own = (st.assignee[st.decode_offset] == eng.rank)
+        for li in np.nonzero(own)[0]:
+            st.kv.check_room(int(li))
+        owner[b], slot[b], ntok[:, b] = own, st.kv.layer_counts, st.kv.layer_counts + own
+    for b, rid in enumerate(rids):
+        st = eng.reqs[rid]
+        for li in np.nonzero(owner[b])[0]:
+            st.kv.slot_pos[li, st.kv.layer_counts[li]] = pos[b]
+        st.kv.layer_counts += owner[b]
+        st.decode_offset += 1
+        st.context_len += 1
+    return pos, owner, slot, ntok
+
+
+def test_vectorised_decode_bookkeeping_matches_the_loop_form():
+    """Decode metadata and KV slot bookkeeping (owner, slot, token counts, slot positions,
+    the reserved-slab capacity error) on the CUDA path's data, vectorised vs per-layer loops."""
+    from hetero_cp_ringattn_b200.config import preset
+    from hetero_cp_ringattn_b200.models.llama import LlamaCPEngine, RequestState
+    from hetero_cp_ringattn_b200.models.weights import ModelWeights, PreparedWeights
+    from hetero_cp_ringattn_b200.parallel.strategy import RingStrategy
+    cfg = preset("tiny")
+    cfg.num_layers = 6
+    w = PreparedWeights.from_weights(ModelWeights.random_init(cfg, seed=0, dtype=torch.float32),
+                                     dtype=torch.float32)
+    engines = []
+    for _ in range(2):
+        e = LlamaCPEngine(cfg, w, device=torch.device("cpu"), max_context=1024, kv_pages=64,
+                          page_size=16)
+        e.rank, e.world = 1, 3          # owners vary per (token, layer)
+        for b, rid in enumerate((5, 6, 7)):
+            st = RequestState(req_id=rid, prompt_len=100, chunks=[100], strategy=RingStrategy.VANILLA,
+                              positions=np.arange(100), owner_of_last=0, horizon=400,
+                              assignee=e._schedule(rid, [2, 1, 1], 400, 0, 100), context_len=100)
+            st.kv = e.kv.reserve(rid, 30 + b, 30 + b + 5 + 3 * b, np.arange(30 + b))
+            e.reqs[rid] = st
+        e.cuda = True                   # the CUDA branch of the bookkeeping is pure host code
+        engines.append(e)
+    new, old = engines
+    rids = [5, 6, 7]
+    for step in range(400):
+        try:
+            ref = _old_meta_advance(old, rids)
+        except CapacityError as e_old:
+            with pytest.raises(CapacityError) as e_new:
+                new._decode_meta(rids)
+            assert str(e_new.value) == str(e_old)
+            break
+        got = new._decode_meta(rids)
+        new._advance(rids, got[1], got[0])
+        for a, b in zip(got, ref):
+            assert np.array_equal(a, b), step
+        for rid in rids:
+            assert np.array_equal(new.reqs[rid].kv.layer_counts, old.reqs[rid].kv.layer_counts)
+            assert np.array_equal(new.reqs[rid].kv.slot_pos, old.reqs[rid].kv.slot_pos)
+    else:
+        raise AssertionError("the reserved slabs never filled up")
