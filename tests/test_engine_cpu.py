@@ -95,6 +95,10 @@ def _worker(rank, world, port, chunks, strategy, steps, out_path, tickets):
     ([20, 17], "zigzag", None),
     ([25, 25, 5], "vanilla", [5, 5, 1]),
     ([25, 25, 5], "striped", [5, 5, 1]),
+    # a rank holding a single token whose peers hold only future (or only past) positions
+    # (the reference's single-token causal prefill with future peer KV, tch_backend.rs:1809)
+    ([1, 12], "vanilla", None),
+    ([12, 1], "zigzag", [1, 1]),
 ])
 def test_gloo_ranks_match_single_device(chunks, strategy, tickets):
     world = len(chunks)
