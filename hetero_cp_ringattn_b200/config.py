@@ -46,6 +46,7 @@ class ModelConfig:
     use_sliding_window: Optional[bool] = None
     partial_rotary_factor: float = 1.0    # parsed, unused
     rope_scaling: Optional[dict] = None   # HF rope_scaling: linear / llama3 / yarn frequencies
+    mlp_bias: bool = False                # HF Llama option; biases on the MLP are not supported
     name: str = "custom"
 
     # ------------------------------------------------------------------ derived
@@ -94,6 +95,8 @@ class ModelConfig:
             raise RingError("head_dim must be even for rotate-half RoPE")
         if self.hidden_act not in ("silu", "swish"):
             raise RingError(f"unsupported hidden_act {self.hidden_act}")
+        if self.mlp_bias:
+            raise RingError("mlp_bias=true (biases on the MLP projections) is not supported")
         if self.rope_scaling:
             kind = self.rope_scaling.get("rope_type", self.rope_scaling.get("type", "default"))
             if kind not in ("default", "linear", "llama3", "yarn"):
@@ -136,10 +139,18 @@ class ModelConfig:
             use_sliding_window=d.get("use_sliding_window"),
             partial_rotary_factor=float(d.get("partial_rotary_factor", 1.0)),
             rope_scaling=dict(d["rope_scaling"]) if d.get("rope_scaling") else None,
+            mlp_bias=bool(d.get("mlp_bias", False)),
             name=d.get("_name_or_path", d.get("name", "custom")),
         )
         if cfg.num_kv_heads is not None:
             cfg.num_kv_heads = int(cfg.num_kv_heads)
+        if cfg.use_sliding_window and cfg.sliding_window and cfg.max_position_embeddings and \
+                cfg.sliding_window < cfg.max_position_embeddings:
+            import logging
+            logging.getLogger("hcp.config").warning(
+                "use_sliding_window is set (window %d): this engine attends over the full "
+                "context, so positions beyond the window differ from a sliding-window model",
+                cfg.sliding_window)
         cfg.validate()
         return cfg
 

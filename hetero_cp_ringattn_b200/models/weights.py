@@ -76,6 +76,13 @@ class ModelWeights:
         return self.tensors["model.embed_tokens.weight"]
 
     def validate(self) -> None:
+        # biases this engine does not apply must not be silently dropped (HF Llama puts one on
+        # o_proj when attention_bias is set; mlp_bias puts them on the MLP)
+        ignored = [n for n in self.tensors if n.endswith(("o_proj.bias", "gate_proj.bias",
+                                                           "up_proj.bias", "down_proj.bias"))]
+        if ignored:
+            raise RingError(f"checkpoint has {ignored[0]} (and {len(ignored) - 1} more): biases on "
+                            "the output projection or the MLP are not supported")
         for name, shape in expected_shapes(self.cfg).items():
             if name not in self.tensors:
                 raise RingError(f"missing weight {name}")

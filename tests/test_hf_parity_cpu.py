@@ -85,3 +85,18 @@ def test_rope_scaling_config_round_trip_and_unsupported_types():
     d["rope_scaling"] = {"rope_type": "dynamic", "factor": 2.0}
     with pytest.raises(RingError, match="unsupported rope_scaling"):
         ModelConfig.from_dict(d)
+
+
+def test_unsupported_checkpoint_options_fail_loudly(tmp_path, caplog):
+    from hetero_cp_ringattn_b200.config import ModelConfig
+    from hetero_cp_ringattn_b200.errors import RingError
+    d = preset("llama-3.2-1b").to_hf_dict()
+    with pytest.raises(RingError, match="mlp_bias"):
+        ModelConfig.from_dict(dict(d, mlp_bias=True))
+    cfg, w, _ = _model(tmp_path, "bias-check", False, None)
+    w.tensors["model.layers.0.self_attn.o_proj.bias"] = torch.zeros(cfg.hidden_size)
+    with pytest.raises(RingError, match="o_proj.bias"):
+        w.validate()
+    with caplog.at_level("WARNING"):
+        ModelConfig.from_dict(dict(d, use_sliding_window=True, sliding_window=4096))
+    assert "sliding" in caplog.text
