@@ -486,3 +486,48 @@ def test_stop_strings_cut_the_completion(stack):
         srv.stop()
         stopper.set()
         loop.join(timeout=5)
+
+
+def test_streaming_with_a_byte_level_bpe_tokenizer(tmp_path):
+    """HF tokenizer.json (a byte-level BPE trained here offline): load_tokenizer picks it up,
+    and the streamed deltas of a text with spaces and multi-byte characters, decoded through the
+    sliding window, concatenate to the full decode."""
+    tokenizers = pytest.importorskip("tokenizers")
+    from tokenizers import decoders, models, pre_tokenizers, trainers
+    from hetero_cp_ringattn_b200.serve.coordinator import Metrics
+    from hetero_cp_ringattn_b200.serve.http_server import ApiServer, ApiState
+    from hetero_cp_ringattn_b200.serve.tokenizer import HfTokenizer, load_tokenizer
+
+    bpe = tokenizers.Tokenizer(models.BPE())
+    bpe.pre_tokenizer = pre_tokenizers.ByteLevel(add_prefix_space=False)
+    bpe.decoder = decoders.ByteLevel()
+    trainer = trainers.BpeTrainer(vocab_size=400, initial_alphabet=pre_tokenizers.ByteLevel.alphabet())
+    bpe.train_from_iterator(["hello world, ring attention over many ranks", "héllo wörld ✓ 😀"] * 20,
+                            trainer)
+    bpe.save(str(tmp_path / "tokenizer.json"))
+    tok = load_tokenizer(str(tmp_path), 512)
+    assert isinstance(tok, HfTokenizer)
+    text = "hello wörld, ring ✓ over ranks 😀!"
+    gen = tok.encode(text)
+    assert tok.decode(gen) == text
+
+    class StubCoordinator:
+        metrics = Metrics()
+
+        def next_request_id(self):
+            return 1
+
+        def submit(self, job):
+            for i, t in enumerate(gen):
+                job.on_token(t, "length" if i == len(gen) - 1 else None)
+            job.done({"request_id": 1, "tokens": gen, "prompt_tokens": 1,
+                      "finish_reason": "length"})
+
+    srv = ApiServer(ApiState(StubCoordinator(), tok, "bpe", 1)).start()
+    try:
+        sse = _post(srv.port, {"prompt": "x", "max_tokens": len(gen), "stream": True}, raw=True)
+    finally:
+        srv.stop()
+    events = [ln[6:] for ln in sse.split("\n") if ln.startswith("data: ")]
+    deltas = [json.loads(e)["choices"][0]["text"] for e in events[:-1]]
+    assert "".join(deltas) == text and all("�" not in d for d in deltas)
