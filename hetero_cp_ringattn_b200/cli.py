@@ -348,22 +348,37 @@ def cmd_compare_hidden(args) -> int:
 
 
 def cmd_perf_summary(args) -> int:
-    """Aggregate an HCP_PERF_LOG JSONL file per event (the reference's parse_worker_perf.py)."""
+    """Aggregate HCP_PERF_LOG JSONL files per event (the reference's parse_worker_perf.py): the
+    mean of every numeric field; `--ledger` adds the KV transport ledger of the reference's
+    kv_transport_ledger.py, total bytes sent / received per event and rank (`domain`)."""
     import collections
     agg = collections.defaultdict(lambda: collections.defaultdict(float))
     counts = collections.Counter()
-    for line in open(args.path):
-        try:
-            ev = json.loads(line)
-        except json.JSONDecodeError:
-            continue
-        name = ev.get("event", "?")
-        counts[name] += 1
-        for k, v in ev.items():
-            if isinstance(v, (int, float)) and not isinstance(v, bool) and k not in ("ts", "layer", "domain"):
-                agg[name][k] += v
+    ledger = collections.defaultdict(lambda: collections.defaultdict(float))
+    byte_fields = ("kv_sent_bytes", "kv_recv_bytes", "wire_sent_bytes", "wire_recv_bytes")
+    for path in args.path:
+        for line in open(path):
+            try:
+                ev = json.loads(line)
+            except json.JSONDecodeError:
+                continue
+            name = ev.get("event", "?")
+            counts[name] += 1
+            for k, v in ev.items():
+                if isinstance(v, (int, float)) and not isinstance(v, bool) and \
+                        k not in ("ts", "layer", "domain"):
+                    agg[name][k] += v
+            if args.ledger:
+                key = f"{name}/domain-{ev.get('domain', '?')}"
+                for k in byte_fields:
+                    v = ev.get(k)
+                    if isinstance(v, (int, float)) and v >= 0:
+                        ledger[key][k] += v
+                ledger[key]["events"] += 1
     out = {name: {"count": counts[name], **{k: v / counts[name] for k, v in fields.items()}}
            for name, fields in agg.items()}
+    if args.ledger:
+        out["kv_transport_ledger"] = {k: dict(v) for k, v in sorted(ledger.items())}
     print(json.dumps(out, indent=2))
     return 0
 
@@ -456,7 +471,9 @@ def main(argv: Optional[List[str]] = None) -> int:
     cl.add_argument("--tolerance", type=float, default=2e-2)
     cl.set_defaults(fn=cmd_compare_logits)
     ps = sub.add_parser("perf-summary")
-    ps.add_argument("path")
+    ps.add_argument("path", nargs="+", help="HCP_PERF_LOG JSONL file(s), e.g. one per rank")
+    ps.add_argument("--ledger", action="store_true",
+                    help="add total KV bytes sent / received per event and rank")
     ps.set_defaults(fn=cmd_perf_summary)
     g = sub.add_parser("gen-prompt")
     g.add_argument("--tokens", type=int, required=True)

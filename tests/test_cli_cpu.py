@@ -104,3 +104,22 @@ def test_package_root_exports():
                               h.preset("tiny"), seed=0, dtype=torch.float32), dtype=torch.float32),
                           device=torch.device("cpu"), max_context=64)
     assert eng.world == 1
+
+
+def test_perf_summary_ledger_over_rank_files(tmp_path, capsys):
+    files = []
+    for r in range(2):
+        p = tmp_path / f"perf{r}.jsonl"
+        log = PerfLog(str(p))
+        for i in range(3):
+            log.emit("ring_attention", domain=r, layer=i, kv_sent_bytes=100 * (r + 1),
+                     kv_recv_bytes=50, wire_sent_bytes=100 * (r + 1), wire_recv_bytes=50)
+        log.emit("stationary_decode", domain=r, wire_sent_bytes=8, wire_recv_bytes=-1)
+        files.append(str(p))
+    assert main(["perf-summary", *files, "--ledger"]) == 0
+    out = json.loads(capsys.readouterr().out)
+    led = out["kv_transport_ledger"]
+    assert led["ring_attention/domain-1"]["kv_sent_bytes"] == 600
+    assert led["ring_attention/domain-0"]["events"] == 3
+    assert led["stationary_decode/domain-0"] == {"wire_sent_bytes": 8, "events": 1}
+    assert out["ring_attention"]["count"] == 6
