@@ -216,6 +216,7 @@ def _raise_interrupt(signum, frame):
 
 
 def cmd_serve(args) -> int:
+    from .config import EnvConfig
     from .errors import RingError
     from .models.llama import LlamaCPEngine
     from .parallel.capacity import query_device_capacity_mb
@@ -227,13 +228,19 @@ def cmd_serve(args) -> int:
     dev = _device(args)
     rank, world, group = _init_ranks(dev, args.num_domains)
     cfg, w = _load_model(args, dev)
+    # the engine decodes at most 8 rows per step on CUDA; more concurrent requests are decoded
+    # in several engine steps per coordinator iteration
+    eng_batch = min(args.max_batch_size, 8) if dev.type == "cuda" else args.max_batch_size
+    page = EnvConfig.from_env().kv_block_size
+    kv_pages = -(-args.max_context // page) + args.max_batch_size * -(-512 // page) + 2
     eng = LlamaCPEngine(cfg, w, rank=rank, world=world, device=dev, group=group,
-                        max_context=args.max_context, max_batch=args.max_batch_size)
+                        max_context=args.max_context, max_batch=eng_batch, kv_pages=kv_pages)
     control = P.ControlPlane(group, rank, world)
     worker = Worker(eng, control)
     if not args.no_warmup:
         eng.warmup()   # decode graphs captured before the first request (every rank)
     caps = control.all_gather(query_device_capacity_mb(str(dev)))  # the handshake
+    arenas = control.all_gather(eng.kv_capacity_bytes())
     # torchrun forwards SIGINT / SIGTERM to every rank: both end the serve loop the same way
     signal.signal(signal.SIGTERM, _raise_interrupt)
     if rank != 0:
@@ -255,8 +262,10 @@ def cmd_serve(args) -> int:
                          trace_jsonl=args.trace_jsonl, eos_ids=cfg.eos_token_id,
                          export_logits_dir=args.export_logits,
                          prefill_chunk_tokens=args.prefill_chunk_tokens,
-                         max_queue=args.max_queue)
-    coord = Coordinator(worker, control, tok, cfg, ca, capacities_mb=caps)
+                         max_queue=args.max_queue, decode_batch_limit=eng_batch,
+                         kv_page_tokens=eng.page_size if dev.type == "cuda" else 1)
+    coord = Coordinator(worker, control, tok, cfg, ca, capacities_mb=caps,
+                        kv_budget_bytes=arenas if all(a is not None for a in arenas) else None)
     prompts = []
     if args.prompt:
         prompts.append(args.prompt)

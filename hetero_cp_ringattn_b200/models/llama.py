@@ -140,6 +140,14 @@ class LlamaCPEngine:
             self.num_sms = native().num_sms(self.device.index or 0)
 
     # ------------------------------------------------------------------ helpers
+    def kv_capacity_bytes(self) -> Optional[int]:
+        """Bytes of this rank's preallocated KV arena (bf16 K and V, every layer); None on the
+        host path, whose KV lives in ordinary tensors."""
+        if not self.cuda:
+            return None
+        return int(self.kv.alloc.num_pages * self.page_size * self.L *
+                   self.cfg.kv_bytes_per_token_per_layer(2))
+
     def close(self, sync: bool = True) -> None:
         """Free the graphs and the runtime. `sync` waits for every rank first (peers may still
         read this rank's region); pass False when the other ranks are stopping as well."""

@@ -48,6 +48,9 @@ class CoordinatorArgs:
     eos_ids: Optional[List[int]] = None
     export_logits_dir: Optional[str] = None  # per-request logits dumps (coordinator.rs:1170)
     max_queue: int = 0                       # >0: submissions beyond this many queued get 503
+    kv_page_tokens: int = 1                  # ledger rounds each rank's rows up to whole pages
+    decode_batch_limit: int = 8              # rows per engine decode step; more active requests
+                                             # decode in several steps per iteration
     prefill_chunk_tokens: int = 0            # >0: prompts longer than this prefill in pieces,
                                              # with decode steps of the active requests between
 
@@ -95,7 +98,8 @@ class Metrics:
 
 class Coordinator:
     def __init__(self, worker, control: P.ControlPlane, tokenizer, cfg, args: CoordinatorArgs,
-                 capacities_mb: Optional[Sequence[int]] = None):
+                 capacities_mb: Optional[Sequence[int]] = None,
+                 kv_budget_bytes: Optional[Sequence[int]] = None):
         self.worker = worker
         self.control = control
         self.tok = tokenizer
@@ -118,6 +122,10 @@ class Coordinator:
                 budgets.append(1 << 62)
             else:
                 budgets.append(max(0, int(c) - args.activation_reserve_mb) * 1024 * 1024)
+        if kv_budget_bytes:
+            # the ranks' preallocated KV arenas bound what can be admitted, whatever the free
+            # device memory says
+            budgets = [min(b, int(k)) for b, k in zip(budgets, kv_budget_bytes)]
         self.ledger = KvLedger(budgets)
         self.bytes_per_token_layer = cfg.kv_bytes_per_token_per_layer(2)
         self._stop = threading.Event()
@@ -159,7 +167,10 @@ class Coordinator:
                 raise
         errs = [r for r in (all_resp or [resp]) if isinstance(r, P.Error)]
         if errs:
-            raise ProtocolError("; ".join(f"rank error: {e.message}" for e in errs))
+            msg = "; ".join(f"rank error: {e.message}" for e in errs)
+            if all(e.message.startswith("CapacityError:") for e in errs):
+                raise CapacityError(msg)   # a rank's KV arena is full: wait or reject (400)
+            raise ProtocolError(msg)
         return resp
 
     def shutdown(self) -> bool:
@@ -186,13 +197,18 @@ class Coordinator:
             return list(self.args.ratio)
         return [max(1, c) for c in chunks]
 
+    def _pages(self, rows: int) -> int:
+        """Rows rounded up to whole KV pages (the arena hands out pages, not rows)."""
+        p = max(1, int(self.args.kv_page_tokens))
+        return -(-int(rows) // p) * p
+
     def _reserve(self, rid: int, chunks: Sequence[int], horizon: int) -> List[int]:
         tickets = self._tickets(chunks)
         tot = sum(tickets)
         per = []
         for c, t in zip(chunks, tickets):
             growth = -(-horizon * t // tot) + 1
-            per.append((c + growth) * self.cfg.num_layers * self.bytes_per_token_layer)
+            per.append(self._pages(c + growth) * self.cfg.num_layers * self.bytes_per_token_layer)
         self.ledger.try_reserve(rid, per)
         self.trace.emit("kv_reserved", request=rid, bytes=per)
         return per
@@ -304,7 +320,7 @@ class Coordinator:
         tickets = self._tickets(sess.chunks)
         # KV bytes of the segment and its decode growth join the session's ledger entry
         tot = sum(tickets)
-        per = [(c + -(-max(1, job.max_tokens) * t // tot) + 1) * self.cfg.num_layers *
+        per = [self._pages(c + -(-max(1, job.max_tokens) * t // tot) + 1) * self.cfg.num_layers *
                self.bytes_per_token_layer for c, t in zip(continuation_split(n, tickets), tickets)]
         self.ledger.try_reserve(rid, per)   # CapacityError: requeued while others hold KV
         self.trace.emit("kv_reserved", request=rid, bytes=per)
@@ -534,15 +550,22 @@ class Coordinator:
             self._finish(a)
             did = True
         active = [a for a in active if not a.job.cancelled]
-        if active:
+        step = max(1, int(self.args.decode_batch_limit))
+        for b0 in range(0, len(active), step):
             did = True
+            self._decode_rows(active[b0:b0 + step])
+        return did
+
+    def _decode_rows(self, active: List[ActiveRequest]) -> None:
+        """One engine decode step for up to `decode_batch_limit` active requests."""
+        if active:
             pairs = [[a.job.request_id, a.next_token] for a in active]
             try:
                 resp = self.run_command(P.DecodeBatch(pairs))
             except Exception as e:
                 for a in active:
                     self._fail(a.job, e)
-                return did
+                return
             logits = self.worker.last_logits
             for i, (a, (_, tok)) in enumerate(zip(active, resp.request_tokens)):
                 if a.job.temperature > 0 and logits is not None:
@@ -554,7 +577,6 @@ class Coordinator:
                     a.job.on_token(tok, a.finish_reason)
                 if a.finish_reason:
                     self._finish(a)
-        return did
 
     def run_forever(self) -> None:
         while not self._stop.is_set():

@@ -531,3 +531,68 @@ def test_streaming_with_a_byte_level_bpe_tokenizer(tmp_path):
     events = [ln[6:] for ln in sse.split("\n") if ln.startswith("data: ")]
     deltas = [json.loads(e)["choices"][0]["text"] for e in events[:-1]]
     assert "".join(deltas) == text and all("�" not in d for d in deltas)
+
+
+def test_more_active_requests_than_one_engine_decode_batch(stack):
+    """Six concurrent requests with an engine decode batch of 4: each iteration decodes them in
+    two engine steps; every output equals the oracle's."""
+    cfg, w, eng, coord, tok = stack
+    saved = (coord.sched, coord.args.decode_batch_limit)
+    from hetero_cp_ringattn_b200.serve.scheduler import BatchScheduler
+    coord.sched = BatchScheduler(6)
+    coord.args.decode_batch_limit = 4
+    seen = []
+    orig = coord.run_command
+
+    def spy(cmd):
+        if isinstance(cmd, P.DecodeBatch):
+            seen.append(len(cmd.request_tokens))
+        return orig(cmd)
+
+    coord.run_command = spy
+    try:
+        outs = {}
+        prompts = [tok.encode(f"request {i} " + "x" * i) for i in range(6)]
+        for i, ids in enumerate(prompts):
+            coord.submit(Job(request_id=coord.next_request_id(), prompt_ids=ids, max_tokens=5,
+                             done=lambda r, i=i: outs.__setitem__(i, r)))
+        while len(outs) < 6:
+            coord.iteration()
+        assert max(seen) == 4 and 2 in seen
+        for i, ids in enumerate(prompts):
+            ref, _ = reference_model.greedy_generate(w, torch.tensor(ids), 4)
+            assert outs[i]["tokens"] == ref
+    finally:
+        del coord.run_command
+        coord.sched, coord.args.decode_batch_limit = saved
+
+
+def test_ledger_follows_the_kv_arena_in_pages():
+    """With the ranks' KV arena sizes the ledger budget is the smaller of free memory and arena
+    bytes, and each rank's rows are rounded up to whole pages; a rank's own capacity error
+    ("CapacityError: ...") takes the capacity path (wait for KV, else 400), not a 500."""
+    from hetero_cp_ringattn_b200.serve.coordinator import Coordinator, CoordinatorArgs
+
+    class Fake:
+        last_logits = None
+        fail = False
+
+        def execute(self, cmd):
+            if isinstance(cmd, P.Prefill):
+                if self.fail:
+                    return P.Error(cmd.request_id, "CapacityError: KV arena out of pages")
+                return P.PrefillDone(cmd.request_id, 7, len(cmd.prompt))
+            return P.Ack(getattr(cmd, "request_id", -1))
+
+    cfg = preset("tiny")
+    bpt = cfg.kv_bytes_per_token_per_layer(2) * cfg.num_layers
+    fake = Fake()
+    coord = Coordinator(fake, P.ControlPlane(), ByteTokenizer(cfg.vocab_size), cfg,
+                        CoordinatorArgs(kv_page_tokens=16, activation_reserve_mb=0),
+                        capacities_mb=[1024], kv_budget_bytes=[10 * 16 * bpt])
+    assert coord.ledger.budgets == [10 * 16 * bpt]
+    per = coord._reserve(1, [20], 3)          # 20 rows + 4 growth -> 2 pages
+    assert per == [2 * 16 * bpt]
+    fake.fail = True
+    res = coord.generate([1, 2, 3], max_tokens=2)
+    assert res["status"] == 400 and "CapacityError" in res["error"]
