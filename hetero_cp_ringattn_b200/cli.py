@@ -263,6 +263,7 @@ def cmd_serve(args) -> int:
                          export_logits_dir=args.export_logits,
                          prefill_chunk_tokens=args.prefill_chunk_tokens,
                          max_queue=args.max_queue, decode_batch_limit=eng_batch,
+                         session_ttl_s=args.session_ttl_s,
                          kv_page_tokens=eng.page_size if dev.type == "cuda" else 1)
     coord = Coordinator(worker, control, tok, cfg, ca, capacities_mb=caps,
                         kv_budget_bytes=arenas if all(a is not None for a in arenas) else None)
@@ -451,6 +452,8 @@ def main(argv: Optional[List[str]] = None) -> int:
     s.add_argument("--session-continuation-tokens", type=int, default=64)
     s.add_argument("--http-addr", default=None)
     s.add_argument("--prompt-file", default=None, help="one prompt: the whole file")
+    s.add_argument("--session-ttl-s", type=float, default=0.0,
+                   help="release keep_kv sessions idle this many seconds (0: keep until ended)")
     s.add_argument("--max-queue", type=int, default=0,
                    help="reject requests with 503 while this many are queued (0: no limit)")
     s.add_argument("--prefill-chunk-tokens", type=int, default=0,

@@ -49,6 +49,7 @@ class CoordinatorArgs:
     export_logits_dir: Optional[str] = None  # per-request logits dumps (coordinator.rs:1170)
     max_queue: int = 0                       # >0: submissions beyond this many queued get 503
     kv_page_tokens: int = 1                  # ledger rounds each rank's rows up to whole pages
+    session_ttl_s: float = 0.0               # >0: sessions idle this long release their KV
     decode_batch_limit: int = 8              # rows per engine decode step; more active requests
                                              # decode in several steps per iteration
     prefill_chunk_tokens: int = 0            # >0: prompts longer than this prefill in pieces,
@@ -82,6 +83,7 @@ class Session:
     context_len: int
     chunks: List[int]
     last_token: int
+    last_used: float = dataclasses.field(default_factory=time.time)
 
 
 class Metrics:
@@ -518,8 +520,25 @@ class Coordinator:
                       "status": 400 if isinstance(err, (AdmissionError, CapacityError)) else 500})
 
     # ------------------------------------------------------------------ iteration
+    def _expire_sessions(self) -> None:
+        """Release sessions idle longer than session_ttl_s (their KV would otherwise stay
+        resident until an append without keep_kv ends them)."""
+        now = time.time()
+        for sid, sess in list(self.sessions.items()):
+            if sid in self._busy or now - sess.last_used <= self.args.session_ttl_s:
+                continue
+            del self.sessions[sid]
+            try:
+                self.run_command(P.ReleaseRequest(sess.request_id))
+            except (ProtocolError, RuntimeError, OSError) as e:
+                self.trace.emit("release_failed", request=sess.request_id, error=str(e))
+            self.ledger.release(sess.request_id)
+            self.trace.emit("session_expired", session=sid, request=sess.request_id)
+
     def iteration(self) -> bool:
         did = False
+        if self.args.session_ttl_s > 0 and self.sessions:
+            self._expire_sessions()
         while self.sched.has_capacity():
             job = self.sched.pop_pending()
             if job is None:

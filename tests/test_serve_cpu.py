@@ -596,3 +596,21 @@ def test_ledger_follows_the_kv_arena_in_pages():
     fake.fail = True
     res = coord.generate([1, 2, 3], max_tokens=2)
     assert res["status"] == 400 and "CapacityError" in res["error"]
+
+
+def test_idle_sessions_expire_with_a_ttl(stack):
+    cfg, w, eng, coord, tok = stack
+    free0 = coord.ledger.free_bytes()
+    coord.args.session_ttl_s = 0.05
+    try:
+        coord.generate(tok.encode("ttl"), max_tokens=2, session_id="idle", keep_kv=True)
+        assert "idle" in coord.sessions and eng.reqs
+        import time
+        time.sleep(0.1)
+        coord.iteration()
+        assert "idle" not in coord.sessions and not eng.reqs
+        assert coord.ledger.free_bytes() == free0
+        with pytest.raises(ProtocolError, match="unknown or expired"):
+            coord.generate(tok.encode("x"), max_tokens=1, session_id="idle", append=True)
+    finally:
+        coord.args.session_ttl_s = 0.0
