@@ -29,6 +29,33 @@ def validate_session_fields(body: dict) -> Optional[str]:
     return None
 
 
+# request fields and the JSON types they accept (the reference's CompletionRequest, api/types.rs:
+# a value of the wrong type is a 422 there too)
+_FIELD_TYPES = {"model": (str,), "max_tokens": (int,), "temperature": (int, float),
+                "top_p": (int, float), "stream": (bool,), "session_id": (str,), "keep_kv": (bool,),
+                "append": (bool,), "ignore_eos": (bool,)}
+
+
+def _field_type_error(body: dict) -> Optional[str]:
+    for name, types in _FIELD_TYPES.items():
+        v = body.get(name)
+        if v is None:
+            continue
+        if not isinstance(v, types) or (bool not in types and isinstance(v, bool)):
+            return f"{name}: expected {' or '.join(t.__name__ for t in types)}"
+    if "max_tokens" in body and body["max_tokens"] is not None and body["max_tokens"] < 1:
+        return "max_tokens: must be at least 1"
+    if body.get("temperature") is not None and body["temperature"] < 0:
+        return "temperature: must not be negative"
+    if body.get("top_p") is not None and not 0 < body["top_p"] <= 1:
+        return "top_p: must be in (0, 1]"
+    stop = body.get("stop")
+    if stop is not None and not (isinstance(stop, str) or
+                                 (isinstance(stop, list) and all(isinstance(x, str) for x in stop))):
+        return "stop: expected a string or a list of strings"
+    return None
+
+
 def _cut_at_stop(text: str, stops) -> str:
     """The text before the earliest stop string (OpenAI semantics: the stop is not returned)."""
     if not stops:
@@ -97,8 +124,11 @@ def make_handler(state: ApiState):
                 body = json.loads(self.rfile.read(n) or b"{}")
             except json.JSONDecodeError as e:
                 return self._text(400, f"invalid JSON: {e}")
-            if not isinstance(body.get("prompt"), str):
+            if not isinstance(body, dict) or not isinstance(body.get("prompt"), str):
                 return self._text(422, "prompt (string) is required")
+            bad = _field_type_error(body)
+            if bad:
+                return self._text(422, bad)
             err = validate_session_fields(body)
             coord = state.coord
             if err:

@@ -170,6 +170,13 @@ def test_http_api(stack):
         with pytest.raises(urllib.error.HTTPError) as ei:
             _post(srv.port, {"prompt": "x", "append": True})
         assert ei.value.code == 400
+        for bad in ({"prompt": "x", "max_tokens": "5"}, {"prompt": "x", "max_tokens": 0},
+                    {"prompt": "x", "temperature": -1}, {"prompt": "x", "top_p": 0},
+                    {"prompt": "x", "stream": "yes"}, {"prompt": "x", "stop": [1]},
+                    {"prompt": "x", "max_tokens": True}, {"prompt": 3}):
+            with pytest.raises(urllib.error.HTTPError) as ei:
+                _post(srv.port, bad)
+            assert ei.value.code == 422, bad
         with pytest.raises(urllib.error.HTTPError) as ei:
             _post(srv.port, {"prompt": "x", "keep_kv": True})
         assert ei.value.code == 400
