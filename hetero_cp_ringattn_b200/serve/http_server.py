@@ -29,6 +29,8 @@ def validate_session_fields(body: dict) -> Optional[str]:
     return None
 
 
+MAX_BODY_BYTES = 64 << 20   # a 1M-token prompt as text is a few MB
+
 # request fields and the JSON types they accept (the reference's CompletionRequest, api/types.rs:
 # a value of the wrong type is a 422 there too)
 _FIELD_TYPES = {"model": (str,), "max_tokens": (int,), "temperature": (int, float),
@@ -119,7 +121,12 @@ def make_handler(state: ApiState):
         def do_POST(self):
             if self.path != "/v1/completions":
                 return self._text(404, "not found")
-            n = int(self.headers.get("Content-Length", "0"))
+            try:
+                n = int(self.headers.get("Content-Length", "0"))
+            except ValueError:
+                return self._text(400, "bad Content-Length")
+            if n < 0 or n > MAX_BODY_BYTES:
+                return self._text(413, f"request body over {MAX_BODY_BYTES} bytes")
             try:
                 body = json.loads(self.rfile.read(n) or b"{}")
             except json.JSONDecodeError as e:

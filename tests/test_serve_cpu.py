@@ -177,6 +177,13 @@ def test_http_api(stack):
             with pytest.raises(urllib.error.HTTPError) as ei:
                 _post(srv.port, bad)
             assert ei.value.code == 422, bad
+        import http.client
+        conn = http.client.HTTPConnection("127.0.0.1", srv.port, timeout=10)
+        conn.putrequest("POST", "/v1/completions")
+        conn.putheader("Content-Length", str(1 << 40))
+        conn.endheaders()
+        assert conn.getresponse().status == 413
+        conn.close()
         with pytest.raises(urllib.error.HTTPError) as ei:
             _post(srv.port, {"prompt": "x", "keep_kv": True})
         assert ei.value.code == 400
