@@ -16,89 +16,89 @@ from typing import Optional
 import torch
 
 from . import protocol as P
+from .backend import EngineBackend, WorkerBackend
 
 log = logging.getLogger("hcp.worker")
 
 
 class Worker:
-    def __init__(self, engine, control: P.ControlPlane):
-        self.engine = engine
+    """Executes control commands on a `WorkerBackend` (an `LlamaCPEngine` is wrapped in
+    `EngineBackend`). A failing command becomes an `Error` response; the worker keeps serving."""
+
+    def __init__(self, backend, control: P.ControlPlane):
+        self.backend = backend if isinstance(backend, WorkerBackend) else EngineBackend(backend)
         self.control = control
         self.last_logits: Optional[torch.Tensor] = None
 
+    @property
+    def engine(self):
+        """The wrapped engine (for callers that need engine-level state)."""
+        return getattr(self.backend, "engine", None)
+
     # ------------------------------------------------------------------ backend-trait surface
     def capacity_mb(self) -> int:
-        from ..parallel.capacity import query_device_capacity_mb
-        return query_device_capacity_mb(str(self.engine.device))
+        return self.backend.capacity_mb()
 
     def num_layers(self) -> int:
-        return self.engine.L
+        return self.backend.num_layers()
 
     def device(self) -> str:
-        return str(self.engine.device)
+        return self.backend.device()
 
     def handshake(self) -> bytes:
-        return P.pack_handshake(self.engine.rank, self.capacity_mb())
+        return P.pack_handshake(self.backend.rank, self.capacity_mb())
 
     # ------------------------------------------------------------------ execution
     def execute(self, cmd):
         rid = getattr(cmd, "request_id", -1)
-        e = self.engine
+        b = self.backend
         try:
             if isinstance(cmd, P.Prefill):
                 prompt = torch.as_tensor(cmd.prompt, dtype=torch.int64)  # no copy from the frame
-                tok, logits = e.prefill(cmd.request_id, prompt, cmd.chunks, cmd.strategy,
-                                        decode_horizon=cmd.decode_horizon,
-                                        tickets=cmd.capacity_tickets, return_logits=True,
-                                        keep_kv=cmd.keep_kv)
-                self.last_logits = logits
-                return P.PrefillDone(cmd.request_id, int(tok), len(cmd.prompt))
+                tok, self.last_logits = b.prefill(cmd.request_id, prompt, cmd.chunks, cmd.strategy,
+                                                  cmd.decode_horizon, cmd.capacity_tickets,
+                                                  cmd.keep_kv)
+                return P.PrefillDone(cmd.request_id, tok, len(cmd.prompt))
             if isinstance(cmd, (P.Decode, P.DecodeBatch)):
                 pairs = [(cmd.request_id, cmd.token)] if isinstance(cmd, P.Decode) else \
                     [tuple(x) for x in cmd.request_tokens]
                 rids = [int(r) for r, _ in pairs]
-                toks = torch.tensor([int(t) for _, t in pairs], dtype=torch.int64, device=e.device)
-                out = e.decode_step(rids, toks)
-                self.last_logits = e.last_logits(len(rids))
-                vals = [int(v) for v in out.view(-1).tolist()]
+                vals, self.last_logits = b.decode_batch(rids, [int(t) for _, t in pairs])
                 if isinstance(cmd, P.Decode):
                     return P.DecodeDone(cmd.request_id, vals[0])
                 return P.DecodeBatchDone([[r, v] for r, v in zip(rids, vals)])
             if isinstance(cmd, P.StationaryDecode):
-                P.validate_stationary_decode(e.world, cmd.capacity_tickets, cmd.starter_domain,
+                P.validate_stationary_decode(b.world, cmd.capacity_tickets, cmd.starter_domain,
                                              cmd.token_offset, cmd.decode_horizon)
-                st = e.reqs.get(cmd.request_id)
-                if st is None:
+                off = b.decode_offset(cmd.request_id)
+                if off is None:
                     raise P.ProtocolError(f"unknown request {cmd.request_id}")
-                if st.decode_offset != cmd.token_offset:
+                if off != cmd.token_offset:
                     raise P.ProtocolError(f"request {cmd.request_id}: token_offset {cmd.token_offset} "
-                                          f"!= engine offset {st.decode_offset}")
-                toks = torch.tensor([cmd.token], dtype=torch.int64, device=e.device)
-                out = e.decode_step([cmd.request_id], toks)
-                self.last_logits = e.last_logits(1)
-                return P.DecodeDone(cmd.request_id, int(out.view(-1)[0]))
+                                          f"!= engine offset {off}")
+                vals, self.last_logits = b.decode_batch([cmd.request_id], [cmd.token])
+                return P.DecodeDone(cmd.request_id, vals[0])
             if isinstance(cmd, P.StationaryContinuation):
-                P.validate_stationary_continuation(e.world, cmd.tokens, cmd.position_ids,
+                P.validate_stationary_continuation(b.world, cmd.tokens, cmd.position_ids,
                                                    cmd.capacity_tickets, cmd.starter_domain)
-                tok, logits = e.append(cmd.request_id, torch.as_tensor(cmd.tokens, dtype=torch.int64),
-                                       cmd.position_ids, cmd.capacity_tickets, return_logits=True,
-                                       extra_horizon=max(1, int(cmd.decode_horizon)))
-                self.last_logits = logits
-                return P.StationaryContinuationDone(cmd.request_id, int(tok))
+                tok, self.last_logits = b.continuation(
+                    cmd.request_id, torch.as_tensor(cmd.tokens, dtype=torch.int64),
+                    cmd.position_ids, cmd.capacity_tickets, cmd.decode_horizon)
+                return P.StationaryContinuationDone(cmd.request_id, tok)
             if isinstance(cmd, P.SyncGlobalSeqLen):
-                st = e.reqs.get(cmd.request_id)
-                if st is not None and st.context_len != cmd.len:
-                    raise P.ProtocolError(f"request {cmd.request_id}: global length {st.context_len} "
+                n = b.context_len(cmd.request_id)
+                if n is not None and n != cmd.len:
+                    raise P.ProtocolError(f"request {cmd.request_id}: global length {n} "
                                           f"!= coordinator's {cmd.len}")
                 return P.Ack(cmd.request_id)
             if isinstance(cmd, P.ReleaseRequest):
-                e.release(cmd.request_id)
+                b.release(cmd.request_id)
                 return P.Ack(cmd.request_id)
             if isinstance(cmd, P.Shutdown):
                 return P.Ack()
             raise P.ProtocolError(f"unsupported command {type(cmd).__name__}")
         except Exception as ex:  # the failing request is reported, the worker keeps serving
-            log.warning("rank %d: %s failed: %s", e.rank, type(cmd).__name__, ex)
+            log.warning("rank %d: %s failed: %s", b.rank, type(cmd).__name__, ex)
             log.debug(traceback.format_exc())
             return P.Error(rid, f"{type(ex).__name__}: {ex}")
 

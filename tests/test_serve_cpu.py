@@ -628,3 +628,64 @@ def test_idle_sessions_expire_with_a_ttl(stack):
             coord.generate(tok.encode("x"), max_tokens=1, session_id="idle", append=True)
     finally:
         coord.args.session_ttl_s = 0.0
+
+
+def test_worker_backend_interface_drives_the_control_plane():
+    """Any `WorkerBackend` implementation can sit under the worker: a scripted backend serves a
+    request through the coordinator; an incomplete implementation cannot be instantiated."""
+    from hetero_cp_ringattn_b200.serve.backend import WorkerBackend
+    from hetero_cp_ringattn_b200.serve.coordinator import Coordinator, CoordinatorArgs
+
+    class Counting(WorkerBackend):
+        def __init__(self):
+            self.reqs = {}
+
+        def prefill(self, request_id, prompt, chunks, strategy, decode_horizon, tickets, keep_kv):
+            self.reqs[request_id] = [len(prompt), 0]
+            return 10, None
+
+        def decode_batch(self, request_ids, tokens):
+            for r in request_ids:
+                self.reqs[r][0] += 1
+                self.reqs[r][1] += 1
+            return [t + 1 for t in tokens], None
+
+        def continuation(self, request_id, tokens, position_ids, tickets, horizon):
+            self.reqs[request_id][0] += len(tokens)
+            return 99, None
+
+        def release(self, request_id):
+            return self.reqs.pop(request_id, None) is not None
+
+        def context_len(self, request_id):
+            return self.reqs[request_id][0] if request_id in self.reqs else None
+
+        def decode_offset(self, request_id):
+            return self.reqs[request_id][1] if request_id in self.reqs else None
+
+        world = property(lambda self: 1)
+        rank = property(lambda self: 0)
+
+        def capacity_mb(self):
+            return 1024
+
+        def num_layers(self):
+            return 2
+
+        def device(self):
+            return "scripted"
+
+    backend = Counting()
+    worker = Worker(backend, P.ControlPlane())
+    cfg = preset("tiny")
+    coord = Coordinator(worker, P.ControlPlane(), ByteTokenizer(cfg.vocab_size), cfg,
+                        CoordinatorArgs())
+    res = coord.generate([1, 2, 3], max_tokens=4)
+    assert res["tokens"] == [10, 11, 12, 13] and not backend.reqs
+    assert worker.handshake() == P.pack_handshake(0, 1024) and worker.device() == "scripted"
+
+    class Incomplete(WorkerBackend):
+        pass
+
+    with pytest.raises(TypeError):
+        Incomplete()
