@@ -1,9 +1,9 @@
 // Allocation-free single-rank decode attention (C ABI).
 //
 // This entry point has no counterpart in the reference: it exists for callers that cannot
-// allocate device memory themselves. Examples are code that runs inside a CUDA-graph capture of
-// someone else's stream, plug-ins hosted by a runtime that owns the device allocator, and
-// embedders that only hand out input and output buffers. Such a caller cannot provide the split-KV
+// allocate device memory themselves, such as plug-ins hosted by a runtime that owns the device
+// allocator (an allocation behind its back would escape its memory accounting) and embedders
+// that only hand this library input and output buffers. Such a caller cannot provide the split-KV
 // scratch (partial outputs, partial log-sum-exps, completion counters) that the regular entry
 // point takes as arguments, so this variant keeps that scratch in a fixed-size array that is part
 // of the loaded library (`static __device__`), sized kDecodeNoAllocScratchBytes.
