@@ -19,8 +19,8 @@ struct Schema {
 
 // commands 1-8, responses 64-69
 constexpr Schema kSchemas[] = {
-    {1, "iAAsiOb"},    // Prefill: request_id, prompt, chunks, strategy, decode_horizon,
-                       //          capacity_tickets?, keep_kv
+    {1, "iAAsiObb"},   // Prefill: request_id, prompt, chunks, strategy, decode_horizon,
+                       //          capacity_tickets?, keep_kv, want_logits
     {2, "ii"},         // Decode: request_id, token
     {3, "P"},          // DecodeBatch: (request_id, token) rows
     {4, "iAAAii"},     // StationaryContinuation: request_id, tokens, position_ids, tickets, starter,

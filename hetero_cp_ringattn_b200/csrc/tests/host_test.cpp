@@ -180,15 +180,15 @@ static void Protocol() {
   strat.s = "zigzag";
   Field none;
   none.present = false;
-  std::vector<Field> prefill{I(5), Arr({9, 8, 7, 6}), Arr({3, 1}), strat, I(16), none, I(1)};
+  std::vector<Field> prefill{I(5), Arr({9, 8, 7, 6}), Arr({3, 1}), strat, I(16), none, I(1), I(0)};
   const std::string fr = EncodeFrame(1, prefill);
   uint32_t payload;
   std::memcpy(&payload, fr.data(), 4);
   CHECK(payload == fr.size() - 4 && uint8_t(fr[4]) == kProtocolVersion && uint8_t(fr[5]) == 1);
   int type = 0;
   auto back = DecodeFrame(fr, &type);
-  CHECK(type == 1 && back.size() == 7 && back[0].i == 5 && (back[1].a == V{9, 8, 7, 6}));
-  CHECK(back[3].s == "zigzag" && !back[5].present && back[6].i == 1);
+  CHECK(type == 1 && back.size() == 8 && back[0].i == 5 && (back[1].a == V{9, 8, 7, 6}));
+  CHECK(back[3].s == "zigzag" && !back[5].present && back[6].i == 1 && back[7].i == 0);
   // every truncation and any trailing byte is rejected
   for (size_t n = 0; n < fr.size(); ++n)
     CHECK(Throws<ProtocolError>([&] { DecodeFrame(fr.substr(0, n), &type); }));

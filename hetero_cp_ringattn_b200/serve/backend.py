@@ -23,8 +23,9 @@ class WorkerBackend(abc.ABC):
     @abc.abstractmethod
     def prefill(self, request_id: int, prompt: torch.Tensor, chunks: Sequence[int],
                 strategy: str, decode_horizon: int, capacity_tickets: Optional[Sequence[int]],
-                keep_kv: bool) -> Tuple[int, Optional[torch.Tensor]]:
-        """Prefill the whole prompt (every rank its chunk); the first token and its logits."""
+                keep_kv: bool, want_logits: bool = True) -> Tuple[int, Optional[torch.Tensor]]:
+        """Prefill the whole prompt (every rank its chunk); the first token and, if wanted, its
+        logits."""
 
     @abc.abstractmethod
     def decode_batch(self, request_ids: Sequence[int],
@@ -79,10 +80,10 @@ class EngineBackend(WorkerBackend):
         self.engine = engine
 
     def prefill(self, request_id, prompt, chunks, strategy, decode_horizon, capacity_tickets,
-                keep_kv):
+                keep_kv, want_logits=True):
         tok, logits = self.engine.prefill(request_id, prompt, chunks, strategy,
                                           decode_horizon=decode_horizon, tickets=capacity_tickets,
-                                          return_logits=True, keep_kv=keep_kv)
+                                          return_logits=want_logits, keep_kv=keep_kv)
         return int(tok), logits
 
     def decode_batch(self, request_ids, tokens):

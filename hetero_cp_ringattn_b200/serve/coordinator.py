@@ -199,6 +199,10 @@ class Coordinator:
             return list(self.args.ratio)
         return [max(1, c) for c in chunks]
 
+    def _wants_logits(self, job: Job) -> bool:
+        """Full logits travel to the ranks only when something reads them: sampling or dumps."""
+        return job.temperature > 0 or bool(self.args.export_logits_dir)
+
     def _pages(self, rows: int) -> int:
         """Rows rounded up to whole KV pages (the arena hands out pages, not rows)."""
         p = max(1, int(self.args.kv_page_tokens))
@@ -235,7 +239,8 @@ class Coordinator:
             return self._start_chunked(job, chunks, horizon, max(piece, self.world))
         try:
             resp = self.run_command(P.Prefill(rid, list(job.prompt_ids), chunks, self.args.strategy,
-                                              horizon, self._tickets(chunks), job.keep_kv))
+                                              horizon, self._tickets(chunks), job.keep_kv,
+                                              self._wants_logits(job)))
         except Exception:
             self.ledger.release(rid)
             raise
@@ -262,7 +267,7 @@ class Coordinator:
         try:
             self.run_command(P.Prefill(rid, list(job.prompt_ids[:first]), pchunks,
                                        self.args.strategy, horizon, self._tickets(chunks),
-                                       job.keep_kv))
+                                       job.keep_kv, False))
         except Exception:
             self.ledger.release(rid)
             raise

@@ -36,6 +36,7 @@ class Prefill:
     decode_horizon: int = 128
     capacity_tickets: Optional[List[int]] = None
     keep_kv: bool = False
+    want_logits: bool = True             # ship the first token's logits to every rank
 
 
 @dataclasses.dataclass

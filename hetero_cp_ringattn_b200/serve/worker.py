@@ -57,7 +57,7 @@ class Worker:
                 prompt = torch.as_tensor(cmd.prompt, dtype=torch.int64)  # no copy from the frame
                 tok, self.last_logits = b.prefill(cmd.request_id, prompt, cmd.chunks, cmd.strategy,
                                                   cmd.decode_horizon, cmd.capacity_tickets,
-                                                  cmd.keep_kv)
+                                                  cmd.keep_kv, cmd.want_logits)
                 return P.PrefillDone(cmd.request_id, tok, len(cmd.prompt))
             if isinstance(cmd, (P.Decode, P.DecodeBatch)):
                 pairs = [(cmd.request_id, cmd.token)] if isinstance(cmd, P.Decode) else \

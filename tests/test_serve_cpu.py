@@ -640,7 +640,8 @@ def test_worker_backend_interface_drives_the_control_plane():
         def __init__(self):
             self.reqs = {}
 
-        def prefill(self, request_id, prompt, chunks, strategy, decode_horizon, tickets, keep_kv):
+        def prefill(self, request_id, prompt, chunks, strategy, decode_horizon, tickets, keep_kv,
+                    want_logits=True):
             self.reqs[request_id] = [len(prompt), 0]
             return 10, None
 
@@ -689,3 +690,26 @@ def test_worker_backend_interface_drives_the_control_plane():
 
     with pytest.raises(TypeError):
         Incomplete()
+
+
+def test_prefill_ships_logits_only_when_read(stack):
+    """Greedy requests do not move the first token's logits to the ranks; sampling does."""
+    cfg, w, eng, coord, tok = stack
+    seen = []
+    orig = coord.run_command
+
+    def spy(cmd):
+        if isinstance(cmd, P.Prefill):
+            seen.append(cmd.want_logits)
+        return orig(cmd)
+
+    coord.run_command = spy
+    try:
+        g = coord.generate(tok.encode("greedy"), max_tokens=3)
+        ref, _ = reference_model.greedy_generate(w, torch.tensor(tok.encode("greedy")), 2)
+        assert g["tokens"] == ref
+        s = coord.generate(tok.encode("sampled"), max_tokens=3, temperature=0.8)
+        assert len(s["tokens"]) == 3 and all(0 <= t < cfg.vocab_size for t in s["tokens"])
+        assert seen == [False, True]
+    finally:
+        del coord.run_command

@@ -67,7 +67,7 @@ def server(tmp_path_factory):
     proc = subprocess.Popen(cmd, cwd=REPO, env=env, stdout=log, stderr=subprocess.STDOUT,
                             start_new_session=True)
     try:
-        deadline = time.time() + 180
+        deadline = time.time() + 420
         while True:
             try:
                 health = _get(http, "/health")
@@ -180,7 +180,7 @@ def test_two_rank_continuation_e2e_cli(tmp_path):
            "--continuation-segment", ",".join(map(str, seg)),
            "--continuation-request-id", "9", "--continuation-capacity-tickets", "3,1",
            "--export-logits", str(dump)]
-    out = subprocess.run(cmd, cwd=REPO, env=env, capture_output=True, text=True, timeout=300)
+    out = subprocess.run(cmd, cwd=REPO, env=env, capture_output=True, text=True, timeout=600)
     assert out.returncode == 0, out.stdout[-2000:] + out.stderr[-3000:]
     line = [ln for ln in out.stdout.splitlines() if ln.startswith('{"continuation_e2e"')][0]
     meta = json.loads(line)["continuation_e2e"]
@@ -207,14 +207,14 @@ def test_infer_under_torchrun_matches_single_process(tmp_path):
     base = ["-m", "hetero_cp_ringattn_b200", "infer", "--model-dir", str(mdir), "--device", "cpu",
             "--prompt", "distributed logits export check", "--max-tokens", "5"]
     one = subprocess.run([sys.executable] + base + ["--export-logits", str(tmp_path / "a.bin")],
-                         cwd=REPO, env=env, capture_output=True, text=True, timeout=300)
+                         cwd=REPO, env=env, capture_output=True, text=True, timeout=600)
     assert one.returncode == 0, one.stderr[-3000:]
     two = subprocess.run([sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
                           "--nproc-per-node", "2", "--master-addr", "127.0.0.1",
                           "--master-port", str(_port())] + base +
                          ["--export-logits", str(tmp_path / "b.bin"), "--ratio", "3:1",
                           "--ring-strategy", "zigzag", "--num-domains", "2"],
-                         cwd=REPO, env=env, capture_output=True, text=True, timeout=300)
+                         cwd=REPO, env=env, capture_output=True, text=True, timeout=600)
     assert two.returncode == 0, two.stdout[-2000:] + two.stderr[-3000:]
     r1 = json.loads(one.stdout.strip().splitlines()[-1])
     r2 = json.loads([ln for ln in two.stdout.splitlines() if ln.startswith("{")][-1])
@@ -259,7 +259,7 @@ def test_two_rank_chunked_prefill_cli(tmp_path):
            "--max-context", "256", "--ratio", "3:1", "--ring-strategy", "zigzag",
            "--prefill-chunk-tokens", "20", "--max-tokens", "5",
            "--prompt-token-ids", ",".join(map(str, prompt))]
-    out = subprocess.run(cmd, cwd=REPO, env=env, capture_output=True, text=True, timeout=300)
+    out = subprocess.run(cmd, cwd=REPO, env=env, capture_output=True, text=True, timeout=600)
     assert out.returncode == 0, out.stdout[-2000:] + out.stderr[-3000:]
     res = json.loads([ln for ln in out.stdout.splitlines() if ln.startswith('{"prompt_token_ids"')][0])
     ref, _ = reference_model.greedy_generate(w, torch.tensor(prompt), 4)
