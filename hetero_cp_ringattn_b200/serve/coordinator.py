@@ -87,15 +87,55 @@ class Session:
 
 
 class Metrics:
+    """Request counters (the JSON `/metrics` fields) plus generated tokens and latency
+    histograms for the Prometheus text endpoint."""
+
+    BUCKETS = (0.005, 0.01, 0.025, 0.05, 0.1, 0.25, 0.5, 1.0, 2.5, 5.0, 10.0, 30.0, 60.0)
+
     def __init__(self):
         self.total = 0
         self.completed = 0
         self.failed = 0
+        self.tokens = 0
         self.lock = threading.Lock()
+        self.hist = {"ttft_seconds": [0] * (len(self.BUCKETS) + 1) + [0.0],
+                     "request_latency_seconds": [0] * (len(self.BUCKETS) + 1) + [0.0]}
 
     def bump(self, field: str, n: int = 1) -> None:
         with self.lock:
             setattr(self, field, getattr(self, field) + n)
+
+    def observe(self, name: str, value: float) -> None:
+        """Histogram sample: per-bucket counts (non-cumulative), the overflow count, the sum."""
+        with self.lock:
+            h = self.hist[name]
+            i = next((k for k, le in enumerate(self.BUCKETS) if value <= le), len(self.BUCKETS))
+            h[i] += 1
+            h[-1] += value
+
+    def prometheus(self, queued: int, active: int) -> str:
+        """Prometheus text exposition format (version 0.0.4)."""
+        with self.lock:
+            out = []
+            for name, help_, kind, v in (
+                    ("hcp_requests_total", "requests submitted", "counter", self.total),
+                    ("hcp_requests_completed_total", "requests finished", "counter", self.completed),
+                    ("hcp_requests_failed_total", "requests failed", "counter", self.failed),
+                    ("hcp_generated_tokens_total", "tokens generated", "counter", self.tokens),
+                    ("hcp_requests_queued", "requests waiting for admission", "gauge", queued),
+                    ("hcp_requests_active", "requests decoding", "gauge", active)):
+                out += [f"# HELP {name} {help_}", f"# TYPE {name} {kind}", f"{name} {v}"]
+            for name, h in self.hist.items():
+                full = f"hcp_{name}"
+                out += [f"# HELP {full} {name.replace('_', ' ')}", f"# TYPE {full} histogram"]
+                acc = 0
+                for le, c in zip(self.BUCKETS, h):
+                    acc += c
+                    out.append(f'{full}_bucket{{le="{le}"}} {acc}')
+                acc += h[len(self.BUCKETS)]
+                out += [f'{full}_bucket{{le="+Inf"}} {acc}', f"{full}_sum {h[-1]}",
+                        f"{full}_count {acc}"]
+            return "\n".join(out) + "\n"
 
 
 class Coordinator:
@@ -463,6 +503,7 @@ class Coordinator:
         req.next_token = tok
         if req.first_token_at is None:
             req.first_token_at = time.time()
+            self.metrics.observe("ttft_seconds", req.first_token_at - job.enqueued_at)
             self.trace.emit("first_token", request=job.request_id,
                             ttft_s=req.first_token_at - job.enqueued_at)
         req.finish_reason = self._finish_reason(req, tok)
@@ -493,6 +534,8 @@ class Coordinator:
             released = self.ledger.release(job.request_id)
             self.trace.emit("kv_released", request=job.request_id, bytes=released)
         self.metrics.bump("completed")
+        self.metrics.bump("tokens", len(req.generated))
+        self.metrics.observe("request_latency_seconds", time.time() - job.enqueued_at)
         self.trace.emit("completed", request=job.request_id, completion_tokens=len(req.generated),
                         finish_reason=req.finish_reason,
                         decode_hops=self.cfg.num_layers * max(0, self.world - 1) * max(0, len(req.generated) - 1))

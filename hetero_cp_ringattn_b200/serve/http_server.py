@@ -110,6 +110,15 @@ def make_handler(state: ApiState):
             if self.path == "/v1/models":   # for OpenAI-style clients and benchmark tools
                 return self._json(200, {"object": "list", "data": [
                     {"id": state.model_name, "object": "model", "owned_by": "hcp-b200"}]})
+            if self.path == "/metrics/prometheus":
+                data = state.coord.metrics.prometheus(state.coord.sched.queued,
+                                                      len(state.coord.sched.active)).encode()
+                self.send_response(200)
+                self.send_header("Content-Type", "text/plain; version=0.0.4; charset=utf-8")
+                self.send_header("Content-Length", str(len(data)))
+                self.end_headers()
+                self.wfile.write(data)
+                return None
             if self.path == "/metrics":
                 m = state.coord.metrics
                 return self._json(200, {"total_requests": m.total, "completed_requests": m.completed,

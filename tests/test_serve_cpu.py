@@ -192,6 +192,18 @@ def test_http_api(stack):
         assert m["completed_requests"] >= 2 and m["failed_requests"] >= 2
         assert set(m) == {"total_requests", "completed_requests", "failed_requests",
                           "queued_requests", "active_requests"}
+        with urllib.request.urlopen(f"http://127.0.0.1:{srv.port}/metrics/prometheus",
+                                    timeout=10) as r:
+            prom = r.read().decode()
+        lines = dict(ln.rsplit(" ", 1) for ln in prom.splitlines() if not ln.startswith("#"))
+        assert int(lines["hcp_requests_completed_total"]) == m["completed_requests"]
+        assert int(lines["hcp_generated_tokens_total"]) >= 7
+        assert int(lines['hcp_ttft_seconds_bucket{le="+Inf"}']) == int(lines["hcp_ttft_seconds_count"])
+        assert int(lines["hcp_ttft_seconds_count"]) >= 2
+        parser = pytest.importorskip("prometheus_client.parser")
+        fams = {f.name: f for f in parser.text_string_to_metric_families(prom)}
+        assert fams["hcp_ttft_seconds"].type == "histogram"
+        assert fams["hcp_requests_active"].type == "gauge"
     finally:
         srv.stop()
         stop.set()
