@@ -36,6 +36,15 @@ __device__ __forceinline__ void report_error(int* status, int code, int site, in
   }
 }
 
+// Debug builds (`HCP_DEBUG_BOUNDS=1 python setup.py build_ext --inplace`) add device-side checks
+// of the page ids read from page tables: an id outside the arena is reported into the status word
+// (kOutOfBounds, the site, the id, the batch row) and the access it would address is skipped or
+// redirected to page 0. Slot and position indices are checked in every build; these extra checks
+// are compiled out by default.
+#ifndef HCP_DEBUG_BOUNDS
+#define HCP_DEBUG_BOUNDS 0
+#endif
+
 __device__ __forceinline__ bool error_raised(const int* status) {
   if (status == nullptr) return false;
   return *reinterpret_cast<const volatile int*>(status) != 0;

@@ -232,9 +232,17 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(GemvArgs a) {
             const int page = rp.page_tables[(long)b * rp.pt_stride + slot / rp.geom.page];
             const int kv = hh < rp.H + rp.Hkv ? 0 : 1;
             const int kh = hh - rp.H - kv * rp.Hkv;
+#if HCP_DEBUG_BOUNDS
+            if (page < 0 || page >= rp.geom.pages) {
+              if (j == 0) report_error(rp.status, int(StatusCode::kOutOfBounds), 333, page, b);
+            } else {
+#endif
             __nv_bfloat16* dst = rp.arena + rp.geom.offset(rp.layer, page, kv, kh, slot % rp.geom.page);
             dst[j] = __float2bfloat16(o1);
             dst[j + half] = __float2bfloat16(o2);
+#if HCP_DEBUG_BOUNDS
+            }
+#endif
           } else if (j == 0) {
             report_error(rp.status, int(StatusCode::kOutOfBounds), 331, slot, b);
           }
@@ -425,7 +433,15 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(const __grid_constant_
   const long rows_per_layer = (long)a.geom.pages * 2 * a.geom.hkv * a.geom.page;
   auto issue = [&](int c) {
     const int t0 = s0 + c * CC;
+#if HCP_DEBUG_BOUNDS
+    int page = pt[t0 / a.geom.page];
+    if (page < 0 || page >= a.geom.pages) {   // read page 0 instead; the result is flagged
+      report_error(a.status, int(StatusCode::kOutOfBounds), 334, page, b);
+      page = 0;
+    }
+#else
     const int page = pt[t0 / a.geom.page];
+#endif
     const long krow = (long)a.layer * rows_per_layer +
                       ((long)(page * 2 + 0) * a.geom.hkv + h) * a.geom.page + (t0 % a.geom.page);
     const long vrow = krow + (long)a.geom.hkv * a.geom.page;

@@ -220,6 +220,12 @@ __global__ void qkv_decode_kernel(QkvDecodeArgs a) {
   if (own) {
     if (slot >= 0 && slot < a.slot_cap) page = a.page_tables[(long)b * a.pt_stride + slot / a.geom.page];
     else if (threadIdx.x == 0) report_error(a.status, int(StatusCode::kOutOfBounds), 331, slot, b);
+#if HCP_DEBUG_BOUNDS
+    if (page >= a.geom.pages) {   // skip the KV writes below
+      if (threadIdx.x == 0) report_error(a.status, int(StatusCode::kOutOfBounds), 335, page, b);
+      page = -1;
+    }
+#endif
   }
   const int n_pairs = (H + Hkv) * half;
   for (int i = threadIdx.x; i < n_pairs; i += blockDim.x) {

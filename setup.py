@@ -21,7 +21,9 @@ os.environ.setdefault("TORCH_CUDA_ARCH_LIST", "10.0a")
 os.environ.setdefault("MAX_JOBS", str(os.cpu_count() or 8))
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-NVCC_FLAGS = ARCH + ["-O3", "-std=c++17", "-lineinfo", "--use_fast_math", "-Xptxas=-v",
+# HCP_DEBUG_BOUNDS=1: kernels also check the page ids they read from page tables (status word)
+DEBUG = ["-DHCP_DEBUG_BOUNDS=1"] if os.environ.get("HCP_DEBUG_BOUNDS") == "1" else []
+NVCC_FLAGS = ARCH + DEBUG + ["-O3", "-std=c++17", "-lineinfo", "--use_fast_math", "-Xptxas=-v",
                      "-U__CUDA_NO_HALF_OPERATORS__", "-U__CUDA_NO_HALF_CONVERSIONS__",
                      "-U__CUDA_NO_BFLOAT16_CONVERSIONS__", "-U__CUDA_NO_BFLOAT162_OPERATORS__",
                      "--expt-relaxed-constexpr"]
