@@ -23,8 +23,8 @@ constexpr Schema kSchemas[] = {
                        //          capacity_tickets?, keep_kv, want_logits
     {2, "ii"},         // Decode: request_id, token
     {3, "P"},          // DecodeBatch: (request_id, token) rows
-    {4, "iAAAii"},     // StationaryContinuation: request_id, tokens, position_ids, tickets, starter,
-                       //                         decode_horizon
+    {4, "iAAAiib"},    // StationaryContinuation: request_id, tokens, position_ids, tickets, starter,
+                       //                         decode_horizon, want_logits
     {5, "iiiAiii"},    // StationaryDecode: request_id, token, position, tickets, starter,
                        //                   token_offset, decode_horizon
     {6, "ii"},         // SyncGlobalSeqLen: request_id, len

@@ -34,9 +34,9 @@ class WorkerBackend(abc.ABC):
 
     @abc.abstractmethod
     def continuation(self, request_id: int, tokens: torch.Tensor, position_ids: Sequence[int],
-                     capacity_tickets: Sequence[int],
-                     decode_horizon: int) -> Tuple[int, Optional[torch.Tensor]]:
-        """Append a segment to a kept request; the next token and its logits."""
+                     capacity_tickets: Sequence[int], decode_horizon: int,
+                     want_logits: bool = True) -> Tuple[int, Optional[torch.Tensor]]:
+        """Append a segment to a kept request; the next token and, if wanted, its logits."""
 
     @abc.abstractmethod
     def release(self, request_id: int) -> bool:
@@ -92,9 +92,11 @@ class EngineBackend(WorkerBackend):
         out = e.decode_step([int(r) for r in request_ids], toks)
         return [int(v) for v in out.view(-1).tolist()], e.last_logits(len(request_ids))
 
-    def continuation(self, request_id, tokens, position_ids, capacity_tickets, decode_horizon):
+    def continuation(self, request_id, tokens, position_ids, capacity_tickets, decode_horizon,
+                     want_logits=True):
         tok, logits = self.engine.append(request_id, tokens, position_ids, capacity_tickets,
-                                         return_logits=True, extra_horizon=max(1, int(decode_horizon)))
+                                         return_logits=want_logits,
+                                         extra_horizon=max(1, int(decode_horizon)))
         return int(tok), logits
 
     def release(self, request_id):

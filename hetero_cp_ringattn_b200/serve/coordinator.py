@@ -326,7 +326,7 @@ class Coordinator:
         try:
             resp = self.run_command(P.StationaryContinuation(
                 rid, list(job.prompt_ids[pf.done:end]), list(range(pf.done, end)),
-                self._tickets(pf.chunks), 0, pf.horizon))
+                self._tickets(pf.chunks), 0, pf.horizon, self._wants_logits(job) and end == n))
         except Exception as e:
             self._prefilling.remove(pf)
             self._fail(job, e)
@@ -374,7 +374,8 @@ class Coordinator:
         self._busy.add(job.session_id)      # own the session only once admitted
         job.holds_session = True
         horizon = max(1, job.max_tokens) + (self.args.session_continuation_tokens if job.keep_kv else 0)
-        resp = self.run_command(P.StationaryContinuation(rid, seg, positions, tickets, 0, horizon))
+        resp = self.run_command(P.StationaryContinuation(rid, seg, positions, tickets, 0, horizon,
+                                                         self._wants_logits(job)))
         if self.args.export_logits_dir and self.worker.last_logits is not None:
             export_logits_dump(self._dump_dir(rid), {"continuation_last_logits": self.worker.last_logits}, {
                 "mode": "service", "device": "distributed-workers", "request_id": rid,

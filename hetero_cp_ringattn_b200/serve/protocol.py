@@ -58,6 +58,7 @@ class StationaryContinuation:
     capacity_tickets: List[int]
     starter_domain: int = 0
     decode_horizon: int = 128            # decode tokens the continued request may still take
+    want_logits: bool = True             # ship the next token's logits to every rank
 
 
 @dataclasses.dataclass

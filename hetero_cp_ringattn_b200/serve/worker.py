@@ -83,7 +83,7 @@ class Worker:
                                                    cmd.capacity_tickets, cmd.starter_domain)
                 tok, self.last_logits = b.continuation(
                     cmd.request_id, torch.as_tensor(cmd.tokens, dtype=torch.int64),
-                    cmd.position_ids, cmd.capacity_tickets, cmd.decode_horizon)
+                    cmd.position_ids, cmd.capacity_tickets, cmd.decode_horizon, cmd.want_logits)
                 return P.StationaryContinuationDone(cmd.request_id, tok)
             if isinstance(cmd, P.SyncGlobalSeqLen):
                 n = b.context_len(cmd.request_id)

@@ -663,7 +663,8 @@ def test_worker_backend_interface_drives_the_control_plane():
                 self.reqs[r][1] += 1
             return [t + 1 for t in tokens], None
 
-        def continuation(self, request_id, tokens, position_ids, tickets, horizon):
+        def continuation(self, request_id, tokens, position_ids, tickets, horizon,
+                         want_logits=True):
             self.reqs[request_id][0] += len(tokens)
             return 99, None
 
