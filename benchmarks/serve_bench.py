@@ -46,7 +46,7 @@ def random_prompt(rng: random.Random, n_chars: int) -> str:
     return "".join(rng.choice(alphabet) for _ in range(n_chars))
 
 
-def one_request(url: str, prompt: str, max_tokens: int, timeout: float) -> dict:
+def one_request(url: str, prompt, max_tokens: int, timeout: float) -> dict:
     body = {"prompt": prompt, "max_tokens": max_tokens, "stream": True, "ignore_eos": True}
     req = urllib.request.Request(url.rstrip("/") + "/v1/completions",
                                  data=json.dumps(body).encode(),
@@ -82,9 +82,15 @@ def one_request(url: str, prompt: str, max_tokens: int, timeout: float) -> dict:
 
 def run(url: str, num_prompts: int, input_len: int, output_len: int,
         request_rate: float = float("inf"), max_concurrency: Optional[int] = None, seed: int = 0,
-        timeout: float = 600.0) -> dict:
+        timeout: float = 600.0, token_ids_below: int = 0) -> dict:
+    """`token_ids_below` > 0 sends each prompt as `input_len` random token ids below that bound
+    (exact prompt lengths with any tokenizer) instead of random text."""
     rng = random.Random(seed)
-    prompts = [random_prompt(rng, input_len) for _ in range(num_prompts)]
+    if token_ids_below > 0:
+        prompts = [[rng.randrange(token_ids_below) for _ in range(input_len)]
+                   for _ in range(num_prompts)]
+    else:
+        prompts = [random_prompt(rng, input_len) for _ in range(num_prompts)]
     gaps = [rng.expovariate(request_rate) if request_rate != float("inf") else 0.0
             for _ in range(num_prompts)]
     sem = threading.Semaphore(max_concurrency) if max_concurrency else None
@@ -138,9 +144,11 @@ def main(argv=None) -> int:
     ap.add_argument("--max-concurrency", type=int, default=None)
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--timeout", type=float, default=600.0)
+    ap.add_argument("--token-ids", type=int, default=0, metavar="VOCAB",
+                    help="send prompts as random token ids below VOCAB (exact input lengths)")
     a = ap.parse_args(argv)
     res = run(a.url, a.num_prompts, a.input_len, a.output_len, a.request_rate, a.max_concurrency,
-              a.seed, a.timeout)
+              a.seed, a.timeout, a.token_ids)
     print(json.dumps(res))
     return 0 if res["failed"] == 0 else 1
 

@@ -67,9 +67,13 @@ def _cut_at_stop(text: str, stops) -> str:
 
 
 class ApiState:
-    def __init__(self, coordinator, tokenizer, model_name: str, num_domains: int):
+    def __init__(self, coordinator, tokenizer, model_name: str, num_domains: int,
+                 vocab_size: Optional[int] = None):
         self.coord = coordinator
         self.tok = tokenizer
+        cfg = getattr(coordinator, "cfg", None)
+        self.vocab_size = vocab_size or getattr(cfg, "vocab_size", None) or \
+            getattr(tokenizer, "vocab_size", None) or (1 << 31)
         self.model_name = model_name
         self.num_domains = num_domains
         self.workers_connected = num_domains
@@ -140,8 +144,13 @@ def make_handler(state: ApiState):
                 body = json.loads(self.rfile.read(n) or b"{}")
             except json.JSONDecodeError as e:
                 return self._text(400, f"invalid JSON: {e}")
-            if not isinstance(body, dict) or not isinstance(body.get("prompt"), str):
-                return self._text(422, "prompt (string) is required")
+            prompt = body.get("prompt") if isinstance(body, dict) else None
+            token_prompt = isinstance(prompt, list) and bool(prompt) and all(
+                isinstance(t, int) and not isinstance(t, bool) for t in prompt)
+            if not (isinstance(prompt, str) or token_prompt):
+                return self._text(422, "prompt (a string or a list of token ids) is required")
+            if token_prompt and not all(0 <= t < state.vocab_size for t in prompt):
+                return self._text(422, f"prompt token ids must be in [0, {state.vocab_size})")
             bad = _field_type_error(body)
             if bad:
                 return self._text(422, bad)
@@ -154,7 +163,7 @@ def make_handler(state: ApiState):
             rid = coord.next_request_id()
             created = int(time.time())
             model = body.get("model") or state.model_name
-            ids = state.tok.encode(body["prompt"])
+            ids = list(prompt) if token_prompt else state.tok.encode(prompt)
             stop = body.get("stop")
             stop_strings = [stop] if isinstance(stop, str) else [x for x in (stop or []) if x]
             events: "queue.Queue" = queue.Queue()

@@ -155,6 +155,15 @@ def test_http_api(stack):
         assert h == {"status": "ok", "workers_connected": 1, "num_domains": 1}
         with urllib.request.urlopen(f"http://127.0.0.1:{srv.port}/v1/models", timeout=10) as r:
             assert json.loads(r.read())["data"][0]["id"] == "tiny"
+        ids_prompt = tok.encode("token ids")
+        by_ids = _post(srv.port, {"prompt": ids_prompt, "max_tokens": 3})
+        ref_ids, _ = reference_model.greedy_generate(w, torch.tensor(ids_prompt), 2)
+        assert by_ids["choices"][0]["text"] == tok.decode(ref_ids)
+        assert by_ids["usage"]["prompt_tokens"] == len(ids_prompt)
+        for bad in ({"prompt": [1, "a"]}, {"prompt": []}, {"prompt": [cfg.vocab_size]}):
+            with pytest.raises(urllib.error.HTTPError) as ei:
+                _post(srv.port, bad)
+            assert ei.value.code == 422
         res = _post(srv.port, {"prompt": "ring attention", "max_tokens": 4})
         assert res["object"] == "text_completion"
         assert res["usage"]["completion_tokens"] == 4

@@ -241,6 +241,9 @@ def test_serve_bench_client_against_two_ranks(server):
     assert res["completed"] == 6 and res["failed"] == 0
     assert res["output_throughput"] > 0 and res["mean_ttft_ms"] > 0 and res["mean_tpot_ms"] > 0
     assert res["median_ttft_ms"] <= res["p99_ttft_ms"]
+    ids = serve_bench.run(f"http://127.0.0.1:{port}", num_prompts=3, input_len=9, output_len=3,
+                          max_concurrency=3, seed=2, token_ids_below=100)
+    assert ids["completed"] == 3 and ids["failed"] == 0
 
 
 def test_two_rank_chunked_prefill_cli(tmp_path):
