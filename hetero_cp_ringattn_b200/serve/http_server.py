@@ -58,6 +58,49 @@ def _field_type_error(body: dict) -> Optional[str]:
     return None
 
 
+class _WindowDeltas:
+    """Incremental detokenization over a sliding window: decode the tokens since `prefix`
+    (already streamed, kept as left context so merges and leading spaces decode as in the full
+    text) and return what the tokens from `read` on add. A trailing partial character (a
+    multi-byte character split over tokens decodes to U+FFFD until its last byte arrives) is held
+    back until it completes or the stream ends. Linear in the stream length."""
+
+    def __init__(self, tok):
+        self.tok, self.ids, self.prefix, self.read = tok, [], 0, 0
+
+    def __call__(self, token: int, last: bool) -> str:
+        self.ids.append(token)
+        done = self.tok.decode(self.ids[self.prefix:self.read]) if self.read > self.prefix else ""
+        text = self.tok.decode(self.ids[self.prefix:])
+        if not last and (text.endswith("\ufffd") or len(text) <= len(done)):
+            return ""
+        self.prefix, self.read = self.read, len(self.ids)
+        return text[len(done):]
+
+
+class _StopStringDeltas:
+    """Deltas for a request with stop strings: the whole text is decoded each token and the
+    last (longest stop - 1) characters are held back until they cannot start a stop string, so
+    no part of a stop sequence is ever streamed (cost grows with the generation length; only
+    requests that set `stop` pay it)."""
+
+    def __init__(self, tok, stops):
+        self.tok, self.stops, self.ids, self.sent = tok, stops, [], 0
+        self.hold = max(len(x) for x in stops) - 1
+
+    def __call__(self, token: int, last: bool) -> str:
+        self.ids.append(token)
+        text = _cut_at_stop(self.tok.decode(self.ids), self.stops)
+        upto = len(text)
+        if not last:
+            upto -= self.hold
+            if text.endswith("\ufffd"):
+                upto = min(upto, len(text) - 1)
+        delta = text[self.sent:max(self.sent, upto)]
+        self.sent = max(self.sent, upto)
+        return delta
+
+
 def _cut_at_stop(text: str, stops) -> str:
     """The text before the earliest stop string (OpenAI semantics: the stop is not returned)."""
     if not stops:
@@ -183,9 +226,7 @@ def make_handler(state: ApiState):
                 coord.metrics.bump("failed")
                 return self._text(400, str(e))
             if body.get("stream"):
-                if stop_strings:
-                    return self._stream_with_stops(rid, created, model, events, job, stop_strings)
-                return self._stream(rid, created, model, events, job)
+                return self._stream(rid, created, model, events, job, stop_strings)
             toks = []
             while True:
                 kind, a, b = events.get()
@@ -203,7 +244,9 @@ def make_handler(state: ApiState):
                              "finish_reason": res["finish_reason"]}],
                 "usage": {"prompt_tokens": pt, "completion_tokens": ct, "total_tokens": pt + ct}})
 
-        def _stream(self, rid, created, model, events, job):
+        def _stream(self, rid, created, model, events, job, stops=None):
+            """Server-sent events: one chunk per generated token, then `[DONE]`. A client that
+            goes away cancels the job (the coordinator stops generating for it)."""
             self.send_response(200)
             self.send_header("Content-Type", "text/event-stream")
             self.send_header("Cache-Control", "no-cache")
@@ -218,73 +261,14 @@ def make_handler(state: ApiState):
                     job.cancelled = True
                     raise
 
-            # incremental detokenization over a sliding window: decode the tokens since
-            # `prefix` (already streamed, kept as left context so merges and leading spaces
-            # decode as in the full text) and stream what `read` onward adds; a trailing partial
-            # character (a multi-byte character split over tokens decodes to U+FFFD until its
-            # last byte arrives) is held back until it completes or the stream ends
-            ids: list = []
-            prefix = read = 0
+            delta_of = _StopStringDeltas(state.tok, stops) if stops else _WindowDeltas(state.tok)
             while True:
                 kind, a, b = events.get()
                 if kind == "tok":
-                    ids.append(a)
-                    done_text = state.tok.decode(ids[prefix:read]) if read > prefix else ""
-                    text = state.tok.decode(ids[prefix:])
-                    if b is None and (text.endswith("\ufffd") or len(text) <= len(done_text)):
-                        delta = ""
-                    else:
-                        delta = text[len(done_text):]
-                        prefix, read = read, len(ids)
                     chunk = {"id": f"hcp-completion-{rid}", "object": "text_completion",
                              "created": created, "model": model,
-                             "choices": [{"text": delta, "index": 0, "finish_reason": b}]}
-                    send(json.dumps(chunk))
-                elif kind == "done":
-                    if "error" in a:
-                        send(json.dumps({"error": a["error"]}))
-                    break
-            send("[DONE]")
-            self.close_connection = True
-
-        def _stream_with_stops(self, rid, created, model, events, job, stops):
-            """Streaming with stop strings: the text is decoded whole each token and the last
-            (longest stop - 1) characters are held back until they cannot start a stop string,
-            so no part of a stop sequence is ever streamed (cost grows with the generation
-            length; only requests that set `stop` take this path)."""
-            self.send_response(200)
-            self.send_header("Content-Type", "text/event-stream")
-            self.send_header("Cache-Control", "no-cache")
-            self.send_header("Connection", "close")
-            self.end_headers()
-
-            def send(data: str):
-                try:
-                    self.wfile.write(f"data: {data}\n\n".encode())
-                    self.wfile.flush()
-                except OSError:
-                    job.cancelled = True
-                    raise
-
-            hold = max(len(x) for x in stops) - 1
-            ids: list = []
-            sent = 0
-            while True:
-                kind, a, b = events.get()
-                if kind == "tok":
-                    ids.append(a)
-                    text = _cut_at_stop(state.tok.decode(ids), stops)
-                    if b is None:
-                        upto = len(text) - hold
-                        if text.endswith("\ufffd"):
-                            upto = min(upto, len(text) - 1)
-                    else:
-                        upto = len(text)
-                    delta = text[sent:max(sent, upto)]
-                    sent = max(sent, upto)
-                    chunk = {"id": f"hcp-completion-{rid}", "object": "text_completion",
-                             "created": created, "model": model,
-                             "choices": [{"text": delta, "index": 0, "finish_reason": b}]}
+                             "choices": [{"text": delta_of(a, b is not None), "index": 0,
+                                          "finish_reason": b}]}
                     send(json.dumps(chunk))
                 elif kind == "done":
                     if "error" in a:
