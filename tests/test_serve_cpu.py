@@ -735,3 +735,32 @@ def test_prefill_ships_logits_only_when_read(stack):
         assert seen == [False, True]
     finally:
         del coord.run_command
+
+
+def test_single_token_generations_on_every_path(stack):
+    """max_tokens=1 finishes at the first token on the plain, chunked-prefill and session paths,
+    and an EOS as the first token ends the request with finish_reason "stop"; no KV is left."""
+    cfg, w, eng, coord, tok = stack
+    ids = [(7 * j + 3) % cfg.vocab_size for j in range(40)]
+    ref, _ = reference_model.greedy_generate(w, torch.tensor(ids), 0)
+    r = coord.generate(ids, max_tokens=1)
+    assert r["tokens"] == ref[:1] and r["finish_reason"] == "length"
+    coord.args.prefill_chunk_tokens = 8
+    try:
+        r = coord.generate(ids, max_tokens=1)
+        assert r["tokens"] == ref[:1]
+    finally:
+        coord.args.prefill_chunk_tokens = 0
+    r = coord.generate(ids, max_tokens=1, session_id="one", keep_kv=True)
+    seg = [5, 6, 7]
+    r2 = coord.generate(seg, max_tokens=1, session_id="one", append=True)
+    ref2, _ = reference_model.greedy_generate(w, torch.tensor(ids + ref[:1] + seg), 0)
+    assert r2["tokens"] == ref2[:1]
+    saved = coord.args.eos_ids
+    coord.args.eos_ids = [ref[0]]
+    try:
+        r = coord.generate(ids, max_tokens=5)
+        assert r["tokens"] == ref[:1] and r["finish_reason"] == "stop"
+    finally:
+        coord.args.eos_ids = saved
+    assert not eng.reqs and not coord.sched.active and not coord._prefilling
