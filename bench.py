@@ -34,7 +34,7 @@ CONFIGS = {
 }
 
 
-def parse():
+def parse(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5)
@@ -52,7 +52,7 @@ def parse():
     ap.add_argument("--no-graphs", action="store_true")
     ap.add_argument("--decode-batch", type=int, default=1,
                     help="also time batched decode of B requests that share the prompt length")
-    return ap.parse_args()
+    return ap.parse_args(argv)
 
 
 def reference_unavailable(args) -> None:

@@ -405,6 +405,12 @@ def main(argv: Optional[List[str]] = None) -> int:
     role = "coordinator" if os.environ.get("RANK", "0") == "0" else f"worker {os.environ['RANK']}"
     logging.basicConfig(level=os.environ.get("HCP_LOG", "WARNING"),
                         format=f"%(asctime)s [{role}] %(name)s %(levelname)s: %(message)s")
+    args = build_parser().parse_args(argv)
+    return args.fn(args)
+
+
+def build_parser() -> argparse.ArgumentParser:
+    """The `hcp` command line: one sub-command per tool, each bound to its `cmd_*` function."""
     ap = argparse.ArgumentParser(prog="hcp")
     sub = ap.add_subparsers(dest="cmd", required=True)
     c = sub.add_parser("correctness")
@@ -492,8 +498,7 @@ def main(argv: Optional[List[str]] = None) -> int:
     g.add_argument("--vocab", type=int, default=128256)
     g.add_argument("--seed", type=int, default=0)
     g.set_defaults(fn=cmd_gen_prompt)
-    args = ap.parse_args(argv)
-    return args.fn(args)
+    return ap
 
 
 if __name__ == "__main__":
