@@ -503,9 +503,9 @@ static int hv64() {
   return env == 1 ? 1 : 2;
 }
 
-// Polynomial share per head_dim (out of 8 exponential pairs); HCP_ATTN_POLY overrides it (0, 2,
-// 3 or 4).
-static int poly_share(int D) {
+// Polynomial share (out of 8 exponential pairs), the same for head_dim 64 and 128; HCP_ATTN_POLY
+// overrides it (0, 2, 3 or 4).
+static int poly_share() {
   static int env = -2;
   if (env == -2) {
     const char* s = getenv("HCP_ATTN_POLY");
@@ -520,7 +520,7 @@ static int poly_share(int D) {
 template <int D, int HV>
 static cudaError_t launch_hv(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                              const KParams& p, cudaStream_t stream) {
-  switch (poly_share(D)) {
+  switch (poly_share()) {
     case 2: return launch<D, 2, HV>(tq, tk, tv, p, stream);
     case 3: return launch<D, 3, HV>(tq, tk, tv, p, stream);
     case 4: return launch<D, 4, HV>(tq, tk, tv, p, stream);
