@@ -21,7 +21,8 @@ SOURCES = ["tests/host_test.cpp"] + [f"host/{f}" for f in ("layout.cpp", "capaci
 @pytest.mark.skipif(shutil.which("g++") is None, reason="no C++ compiler")
 def test_host_library_native_tests(tmp_path):
     exe = str(tmp_path / "host_test")
-    cc = subprocess.run(["g++", "-O2", "-std=c++17", "-Wall", "-Werror", "-pthread", "-o", exe] +
+    cc = subprocess.run(["g++", "-O2", "-std=c++17", "-Wall", "-Wextra", "-Wshadow", "-Werror",
+                         "-pthread", "-o", exe] +
                         [os.path.join(CSRC, s) for s in SOURCES], capture_output=True, text=True,
                         timeout=300)
     assert cc.returncode == 0, cc.stderr[-4000:]
