@@ -2,7 +2,7 @@
 
 Every `hetero_cp_ringattn_b200 <command> ...` and `bench.py ...` line in the README parses with
 the real argument parsers, and every `HCP_*` switch the README names is read somewhere in the
-package's sources.
+package's sources; the README's Python example runs (on the CPU here).
 """
 
 import pathlib
@@ -18,12 +18,12 @@ ROOT = pathlib.Path(__file__).resolve().parents[1]
 
 def _readme_commands():
     """Shell lines of the README's code blocks, continuation lines joined, comments dropped."""
-    lines, out, buf, fenced = ROOT.joinpath("README.md").read_text().splitlines(), [], "", False
+    lines, out, buf, fenced = ROOT.joinpath("README.md").read_text().splitlines(), [], "", None
     for ln in lines:
         if ln.startswith("```"):
-            fenced = not fenced
+            fenced = ln[3:].strip() if fenced is None else None
             continue
-        if not fenced or ln.lstrip().startswith("#"):
+        if fenced != "" or ln.lstrip().startswith("#"):
             continue
         code = ln.split(" #", 1)[0].rstrip()
         if code.endswith("\\"):
@@ -72,3 +72,13 @@ def test_readme_environment_switches_are_read_by_the_code():
     src += ROOT.joinpath("setup.py").read_text()
     missing = sorted(n for n in names if f'"{n}"' not in src)
     assert not missing, missing
+
+
+def test_readme_python_example_runs():
+    text = ROOT.joinpath("README.md").read_text()
+    blocks = re.findall(r"```python\n(.*?)```", text, re.S)
+    assert len(blocks) == 1
+    scope = {}
+    exec(compile(blocks[0], "README.md", "exec"), scope)
+    ids, eng = scope["ids"], scope["eng"]
+    assert ids.numel() == 8 and not eng.reqs
