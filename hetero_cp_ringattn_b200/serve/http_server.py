@@ -12,6 +12,8 @@ from __future__ import annotations
 
 import json
 import queue
+import select
+import socket
 import threading
 import time
 from http.server import BaseHTTPRequestHandler, ThreadingHTTPServer
@@ -56,6 +58,16 @@ def _field_type_error(body: dict) -> Optional[str]:
                                  (isinstance(stop, list) and all(isinstance(x, str) for x in stop))):
         return "stop: expected a string or a list of strings"
     return None
+
+
+def _peer_closed(sock) -> bool:
+    """True once the client has closed its end of the connection: the socket reads as ready
+    with nothing left to read. A request pipelined behind this one reads as data, not a close."""
+    try:
+        ready, _, _ = select.select([sock], [], [], 0)
+        return bool(ready) and sock.recv(1, socket.MSG_PEEK) == b""
+    except (OSError, ValueError):
+        return True
 
 
 class _WindowDeltas:
@@ -227,12 +239,21 @@ def make_handler(state: ApiState):
                 return self._text(400, str(e))
             if body.get("stream"):
                 return self._stream(rid, created, model, events, job, stop_strings)
-            toks = []
+            next_poll = 0.0
             while True:
-                kind, a, b = events.get()
+                try:
+                    kind, res, _ = events.get(timeout=0.05)
+                except queue.Empty:
+                    kind = None
                 if kind == "done":
-                    res = a
                     break
+                now = time.monotonic()
+                if now >= next_poll and not job.cancelled:
+                    next_poll = now + 0.05
+                    if _peer_closed(self.connection):
+                        job.cancelled = True    # the client went away: stop generating for it
+            if job.cancelled:
+                return None                     # nobody is left to answer
             if "error" in res:
                 return self._text(int(res.get("status", 500)), res["error"])
             text = _cut_at_stop(state.tok.decode(res["tokens"]), stop_strings)

@@ -764,3 +764,53 @@ def test_single_token_generations_on_every_path(stack):
     finally:
         coord.args.eos_ids = saved
     assert not eng.reqs and not coord.sched.active and not coord._prefilling
+
+
+def test_plain_client_disconnect_aborts_generation(stack, tmp_path):
+    """A non-streaming client that closes its connection while it waits also stops its
+    generation: the handler sees the close, the request finishes with "abort", KV released."""
+    import socket
+    from hetero_cp_ringattn_b200.serve.coordinator import TraceSink
+    cfg, w, eng, coord, tok = stack
+    saved = coord.trace
+    coord.trace = TraceSink(str(tmp_path / "trace.jsonl"))
+    stop = threading.Event()
+    loop = threading.Thread(target=lambda: [coord.iteration() or stop.wait(0.002)
+                                            for _ in iter(stop.is_set, True)], daemon=True)
+    loop.start()
+    srv = ApiServer(ApiState(coord, tok, "tiny", 1)).start()
+    try:
+        body = json.dumps({"prompt": "abc", "max_tokens": 450, "ignore_eos": True}).encode()
+        s = socket.create_connection(("127.0.0.1", srv.port), timeout=30)
+        s.sendall(b"POST /v1/completions HTTP/1.1\r\nHost: x\r\nContent-Type: application/json\r\n"
+                  + f"Content-Length: {len(body)}\r\n\r\n".encode() + body)
+        trace = tmp_path / "trace.jsonl"
+
+        def events():
+            return [json.loads(l) for l in open(trace)] if trace.exists() else []
+
+        done = None
+        for _ in range(500):
+            evs = events()
+            if any(e["event"] in ("prefill_accepted", "token") for e in evs):
+                break
+            stop.wait(0.01)
+        s.close()
+        for _ in range(500):
+            evs = events()
+            done = [e for e in evs if e["event"] == "completed"]
+            if done:
+                break
+            stop.wait(0.02)
+        assert done and done[0]["finish_reason"] == "abort"
+        assert done[0]["completion_tokens"] < 450
+        for _ in range(100):
+            if not eng.reqs:
+                break
+            stop.wait(0.02)
+        assert not eng.reqs and not coord.sched.active
+    finally:
+        srv.stop()
+        stop.set()
+        loop.join(5)
+        coord.trace = saved
