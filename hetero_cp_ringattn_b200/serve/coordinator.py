@@ -96,6 +96,7 @@ class Metrics:
         self.total = 0
         self.completed = 0
         self.failed = 0
+        self.aborted = 0                 # ended early because the client went away
         self.tokens = 0
         self.lock = threading.Lock()
         self.hist = {"ttft_seconds": [0] * (len(self.BUCKETS) + 1) + [0.0],
@@ -121,6 +122,8 @@ class Metrics:
                     ("hcp_requests_total", "requests submitted", "counter", self.total),
                     ("hcp_requests_completed_total", "requests finished", "counter", self.completed),
                     ("hcp_requests_failed_total", "requests failed", "counter", self.failed),
+                    ("hcp_requests_aborted_total", "requests ended by a client disconnect",
+                     "counter", self.aborted),
                     ("hcp_generated_tokens_total", "tokens generated", "counter", self.tokens),
                     ("hcp_requests_queued", "requests waiting for admission", "gauge", queued),
                     ("hcp_requests_active", "requests decoding", "gauge", active)):
@@ -347,6 +350,7 @@ class Coordinator:
             job.holds_session = False
         self.run_command(P.ReleaseRequest(job.request_id))
         self.ledger.release(job.request_id)
+        self.metrics.bump("aborted")
         self.trace.emit("aborted", request=job.request_id, completion_tokens=0)
         if job.done:
             job.done({"request_id": job.request_id, "tokens": [],
@@ -535,6 +539,8 @@ class Coordinator:
             released = self.ledger.release(job.request_id)
             self.trace.emit("kv_released", request=job.request_id, bytes=released)
         self.metrics.bump("completed")
+        if req.finish_reason == "abort":
+            self.metrics.bump("aborted")
         self.metrics.bump("tokens", len(req.generated))
         self.metrics.observe("request_latency_seconds", time.time() - job.enqueued_at)
         self.trace.emit("completed", request=job.request_id, completion_tokens=len(req.generated),
@@ -594,6 +600,7 @@ class Coordinator:
                 break
             did = True
             if job.cancelled:   # the client left while the request was queued
+                self.metrics.bump("aborted")
                 self.trace.emit("aborted", request=job.request_id, completion_tokens=0)
                 if job.done:
                     job.done({"request_id": job.request_id, "tokens": [],

@@ -778,6 +778,7 @@ def test_plain_client_disconnect_aborts_generation(stack, tmp_path):
     loop = threading.Thread(target=lambda: [coord.iteration() or stop.wait(0.002)
                                             for _ in iter(stop.is_set, True)], daemon=True)
     loop.start()
+    aborted0 = coord.metrics.aborted
     srv = ApiServer(ApiState(coord, tok, "tiny", 1)).start()
     try:
         body = json.dumps({"prompt": "abc", "max_tokens": 450, "ignore_eos": True}).encode()
@@ -804,6 +805,8 @@ def test_plain_client_disconnect_aborts_generation(stack, tmp_path):
             stop.wait(0.02)
         assert done and done[0]["finish_reason"] == "abort"
         assert done[0]["completion_tokens"] < 450
+        assert coord.metrics.aborted == aborted0 + 1
+        assert f"hcp_requests_aborted_total {aborted0 + 1}" in coord.metrics.prometheus(0, 0)
         for _ in range(100):
             if not eng.reqs:
                 break
