@@ -15,6 +15,13 @@ using hcp::ArenaGeom;
 
 #define HCP_CHECK_OK(err) TORCH_CHECK((err) == nullptr, "hcp kernel: ", (err))
 
+// Decode page tables: int32 [B, pages per row] with contiguous rows (the kernels read row b at
+// b * stride(0) and bound each row's KV length by stride(0) * page).
+static void check_page_tables(const torch::Tensor& pt) {
+  TORCH_CHECK(pt.is_cuda() && pt.scalar_type() == torch::kInt32, "page_tables must be a CUDA int32 tensor");
+  TORCH_CHECK(pt.dim() == 2 && pt.stride(1) == 1 && pt.size(1) >= 1, "page_tables must be [B, pages] with contiguous rows");
+}
+
 void check_cuda_bf16(const torch::Tensor& t, const char* name) {
   TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
   TORCH_CHECK(t.scalar_type() == torch::kBFloat16, name, " must be bfloat16");
@@ -371,6 +378,7 @@ class PyRuntime {
     a.geom = c.geom;
     a.layer = int(layer);
     a.page_tables = page_tables.data_ptr<int>();
+    check_page_tables(page_tables);
     a.pt_stride = int(page_tables.stride(0));
     a.slot_cap = int(page_tables.size(1)) * c.geom.page;
     a.owner = owner.data_ptr<int>();
@@ -393,6 +401,7 @@ class PyRuntime {
     a.geom = c.geom;
     a.layer = int(layer);
     a.page_tables = page_tables.data_ptr<int>();
+    check_page_tables(page_tables);
     a.pt_stride = int(page_tables.stride(0));
     a.n_tokens = n_tokens.data_ptr<int>();
     a.B = int(q.size(0));
@@ -468,6 +477,7 @@ class PyRuntime {
     r.geom = c.geom;
     r.layer = int(layer);
     r.page_tables = page_tables.data_ptr<int>();
+    check_page_tables(page_tables);
     r.pt_stride = int(page_tables.stride(0));
     r.slot_cap = int(page_tables.size(1)) * c.geom.page;
     r.owner = owner.data_ptr<int>();

@@ -33,6 +33,7 @@
 #include "attn_fwd_sm100.h"
 #include "common.cuh"
 #include "gemm_sm100.h"
+#include "launch.h"
 
 namespace hcp {
 namespace attn {
@@ -481,13 +482,12 @@ static cudaError_t launch(const CUtensorMap& tq, const CUtensorMap& tk, const CU
   static_assert(128 * Cfg<D>::wg0_regs(HV) + (Cfg<D>::threads(HV) - 128) * Cfg<D>::sm_regs(HV) <=
                     Cfg<D>::threads(HV) * ((65536 / Cfg<D>::threads(HV)) / 8 * 8),
                 "register split exceeds the launch's registers");
-  static bool attr = false;
-  if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(attn_fwd_kernel<D, POLY, HV>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<D>::SMEM);
-    if (e != cudaSuccess) return e;
-    attr = true;
-  }
+  static std::atomic<unsigned long long> attr{0};
+  cudaError_t e = once_per_device(attr, [] {
+    return cudaFuncSetAttribute(attn_fwd_kernel<D, POLY, HV>,
+                                cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<D>::SMEM);
+  });
+  if (e != cudaSuccess) return e;
   const int grid = p.num_pairs * p.H;
   attn_fwd_kernel<D, POLY, HV><<<grid, Cfg<D>::threads(HV), Cfg<D>::SMEM, stream>>>(tq, tk, tv, p);
   return cudaGetLastError();

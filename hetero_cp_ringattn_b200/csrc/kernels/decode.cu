@@ -269,13 +269,14 @@ template <int EPI, bool NORM>
 static cudaError_t gemv_launch(const GemvArgs& a, cudaStream_t s) {
   const size_t smem = size_t(a.B) * a.K * 2;
   auto go = [&](auto kernel) -> cudaError_t {
-    static bool carveout = false;
-    if (!carveout) {
-      // the whole decode chain runs with the maximum shared-memory carveout, so consecutive
-      // (overlapping) kernels never need the SM's L1 / shared split reconfigured
-      cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
-      carveout = true;
-    }
+    // the whole decode chain runs with the maximum shared-memory carveout, so consecutive
+    // (overlapping) kernels never need the SM's L1 / shared split reconfigured
+    static std::atomic<unsigned long long> carveout{0};
+    cudaError_t ce = once_per_device(carveout, [&] {
+      return cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                  cudaSharedmemCarveoutMaxShared);
+    });
+    if (ce != cudaSuccess) return ce;
     if (smem > 48 * 1024) {
       cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
       if (e != cudaSuccess) return e;
@@ -411,7 +412,15 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(const __grid_constant_
   const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int lane = threadIdx.x % 32, warp = threadIdx.x / 32;
   const int g = lane / 4, t = lane % 4;    // MMA fragment row group / column pair
-  const int n = a.n_tokens[b];
+  // a row's KV length is bounded by its page-table row (pt_stride pages); a longer one is
+  // reported and clamped, so the page-table reads below stay inside the caller's row
+  int n = a.n_tokens[b];
+  const int n_cap = a.pt_stride * a.geom.page;
+  if (n > n_cap || n < 0) {
+    if (threadIdx.x == 0 && blockIdx.x == 0 && blockIdx.y == 0)
+      report_error(a.status, int(StatusCode::kOutOfBounds), 304, n, b);
+    n = n < 0 ? 0 : n_cap;
+  }
   // chunk-aligned split ranges
   int per = (n + a.splits - 1) / a.splits;
   per = (per + CC - 1) / CC * CC;
@@ -772,15 +781,15 @@ __global__ void decode_combine_kernel(DecodeCombineArgs a) {
 
 template <int D, int G>
 static cudaError_t prepare_attn() {
-  static bool done = false;
-  if (done) return cudaSuccess;
-  cudaError_t e = cudaFuncSetAttribute(decode_attn_kernel<D, G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       DecCfg<D>::SMEM);
-  if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(decode_attn_kernel<D, G>, cudaFuncAttributePreferredSharedMemoryCarveout,
-                             cudaSharedmemCarveoutMaxShared);
-  done = (e == cudaSuccess);
-  return e;
+  static std::atomic<unsigned long long> done{0};
+  return once_per_device(done, [] {
+    cudaError_t e = cudaFuncSetAttribute(decode_attn_kernel<D, G>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, DecCfg<D>::SMEM);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(decode_attn_kernel<D, G>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                               cudaSharedmemCarveoutMaxShared);
+    return e;
+  });
 }
 
 template <int D, int G>
@@ -800,6 +809,7 @@ const char* decode_attn(const DecodeAttnArgs& a, cudaStream_t s) {
   if ((a.D != 64 && a.D != 128) || a.geom.page % kDecCC)
     return "decode_attn: head_dim must be 64 or 128 and the page a multiple of 64 rows";
   if (G > 8) return "decode_attn: at most 8 query heads per KV head";
+  if (a.pt_stride < 1) return "decode_attn: page-table row stride must be at least 1";
   if (reinterpret_cast<uintptr_t>(a.arena) & 15) return "decode_attn: arena must be 16-byte aligned";
   // the whole arena as one [rows, D] bf16 matrix; boxes of 64 rows x 64 dims, 128-byte swizzle
   const unsigned long long rows =
@@ -889,10 +899,11 @@ const char* add_u64(unsigned long long* p, unsigned long long v, cudaStream_t s)
 // Allocation-free single-rank decode attention (see decode_noalloc.h for the contract).
 //
 // For callers that cannot allocate device memory: the split-KV scratch (partials, counters, the
-// one-rank exchange slot and its pointer tables) lives in `g_decode_noalloc_scratch`, a
-// file-scope array every device holds while the library is loaded. Host code never passes the
-// array's name to a kernel (in host code it is only a stand-in for the symbol); it passes the
-// device address obtained once per device with cudaGetSymbolAddress.
+// one-rank exchange slot and its pointer tables) and a device status word live in
+// `g_decode_noalloc_scratch`, a file-scope array every device holds while the library is
+// loaded. Host code never passes the array's name to a kernel (in host code it is only a
+// stand-in for the symbol); it passes the device address obtained with cudaGetSymbolAddress once
+// per device context.
 // ============================================================================================
 #include <mutex>
 #include <string>
@@ -903,14 +914,53 @@ namespace {
 
 constexpr unsigned long long kNoAllocBytes = HCP_DECODE_NOALLOC_SCRATCH_BYTES;
 constexpr int kNoAllocMaxDevices = 64;
+constexpr unsigned long long kNoAllocTooBig = ~0ull;
 
 static __device__ __align__(256) unsigned char g_decode_noalloc_scratch[HCP_DECODE_NOALLOC_SCRATCH_BYTES];
 
+// Status area at the start of the array: the live words the kernels of the current call report
+// into (code, site, info, info), then the first error of an earlier call that was not read yet.
+constexpr unsigned long long kStatusLive = 0;
+constexpr unsigned long long kStatusHeld = 16;
+constexpr unsigned long long kStatusBytes = 256;
+
+struct DeviceSlot {
+  void* addr = nullptr;            // device address of the scratch array in this context
+  unsigned long long ctx_id = 0;   // the context it was looked up in (0: unknown)
+};
+
 std::mutex g_noalloc_mu;
-void* g_noalloc_addr[kNoAllocMaxDevices] = {nullptr};
+DeviceSlot g_noalloc_slot[kNoAllocMaxDevices];
 thread_local std::string g_noalloc_err;
 
-// Byte layout inside the scratch array (all offsets 256-byte aligned).
+// Identifier of the current context (driver API, looked up at run time): a primary context that
+// was reset and created again gets a new identifier, so a cached address is looked up again.
+unsigned long long current_context_id() {
+  typedef int (*CtxGetCurrent)(void**);
+  typedef int (*CtxGetId)(void*, unsigned long long*);
+  static CtxGetCurrent get_cur = nullptr;
+  static CtxGetId get_id = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void* f = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_cur = reinterpret_cast<CtxGetCurrent>(f);
+    f = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<CtxGetId>(f);
+  });
+  if (get_cur == nullptr || get_id == nullptr) return 0;
+  void* ctx = nullptr;
+  unsigned long long id = 0;
+  if (get_cur(&ctx) != 0 || ctx == nullptr || get_id(ctx, &id) != 0) return 0;
+  return id;
+}
+
+// Byte layout inside the scratch array (all offsets 256-byte aligned, sizes in 64-bit
+// arithmetic so no product of the caller's sizes can overflow).
 struct NoAllocLayout {
   unsigned long long counters, tables, flag, part_o, part_lse, xslot, total;
 };
@@ -918,29 +968,39 @@ struct NoAllocLayout {
 unsigned long long align256(unsigned long long v) { return (v + 255ull) & ~255ull; }
 
 NoAllocLayout noalloc_layout(int B, int H, int Hkv, int D, int splits) {
+  const unsigned long long b = (unsigned long long)B, h = (unsigned long long)H,
+                           hkv = (unsigned long long)Hkv, d = (unsigned long long)D,
+                           sp = (unsigned long long)splits;
   NoAllocLayout l{};
-  unsigned long long off = 0;
+  unsigned long long off = kStatusBytes;
   l.counters = off;
-  off = align256(off + sizeof(unsigned int) * (unsigned long long)(B * Hkv + 1));
+  off = align256(off + sizeof(unsigned int) * (b * hkv + 1ull));
   l.tables = off;  // float* xslot_ptrs[1]; unsigned long long* ready_ptrs[1]
   off = align256(off + 2 * sizeof(void*));
   l.flag = off;
   off = align256(off + sizeof(unsigned long long));
   l.part_o = off;
-  off = align256(off + sizeof(float) * (unsigned long long)B * H * splits * D);
+  off = align256(off + sizeof(float) * b * h * sp * d);
   l.part_lse = off;
-  off = align256(off + sizeof(float) * (unsigned long long)B * H * splits);
+  off = align256(off + sizeof(float) * b * h * sp);
   l.xslot = off;
-  off = align256(off + sizeof(float) * 2ull * B * H * (D + 1));
+  off = align256(off + sizeof(float) * 2ull * b * h * (d + 1ull));
   l.total = off;
   return l;
 }
 
-// Resets the state that must start at zero and points the one-entry tables at the scratch.
+// Start of a call: the first unread error of the previous calls moves to the held slot, the live
+// words restart at zero (so a stale error cannot cut this call's waits short), the completion
+// counters are cleared and the one-entry tables point at the scratch.
 __global__ void noalloc_setup_kernel(unsigned char* base, NoAllocLayout l, int n_counters) {
   unsigned int* counters = reinterpret_cast<unsigned int*>(base + l.counters);
   for (int i = threadIdx.x; i < n_counters; i += blockDim.x) counters[i] = 0u;
   if (threadIdx.x == 0) {
+    int* live = reinterpret_cast<int*>(base + kStatusLive);
+    int* held = reinterpret_cast<int*>(base + kStatusHeld);
+    if (live[0] != 0 && held[0] == 0)
+      for (int i = 0; i < 4; ++i) held[i] = live[i];
+    for (int i = 0; i < 4; ++i) live[i] = 0;
     void** tables = reinterpret_cast<void**>(base + l.tables);
     tables[0] = base + l.xslot;
     tables[1] = base + l.flag;
@@ -953,15 +1013,58 @@ int noalloc_fail(int code, const std::string& msg) {
   return code;
 }
 
+// Device address of the scratch array for the current device and context (looked up the first
+// time a device or a new context is seen).
+int noalloc_base(unsigned char** base) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return noalloc_fail(int(e), cudaGetErrorString(e));
+  if (dev < 0 || dev >= kNoAllocMaxDevices)
+    return noalloc_fail(-8, "hcp_decode_attention_noalloc: device index out of range");
+  const unsigned long long ctx = current_context_id();
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  DeviceSlot& slot = g_noalloc_slot[dev];
+  if (slot.addr == nullptr || (ctx != 0 && slot.ctx_id != ctx)) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_decode_noalloc_scratch);
+    if (e != cudaSuccess)
+      return noalloc_fail(int(e), std::string("cudaGetSymbolAddress: ") + cudaGetErrorString(e));
+    slot.addr = p;
+    slot.ctx_id = ctx;
+  }
+  *base = static_cast<unsigned char*>(slot.addr);
+  return 0;
+}
+
 }  // namespace
 
 extern "C" unsigned long long hcp_decode_attention_noalloc_scratch_bytes(int batch, int heads,
                                                                          int hkv, int d,
                                                                          int splits) {
+  if (batch < 1 || heads < 1 || hkv < 1 || d < 1 || splits < 1) return kNoAllocTooBig;
   return noalloc_layout(batch, heads, hkv, d, splits).total;
 }
 
 extern "C" const char* hcp_decode_attention_noalloc_error(void) { return g_noalloc_err.c_str(); }
+
+extern "C" int hcp_decode_attention_noalloc_status(int* words, cudaStream_t stream) {
+  g_noalloc_err.clear();
+  if (words == nullptr) return noalloc_fail(-1, "hcp_decode_attention_noalloc_status: null words");
+  unsigned char* base = nullptr;
+  int rc = noalloc_base(&base);
+  if (rc != 0) return rc;
+  cudaError_t e = cudaStreamSynchronize(stream);
+  if (e != cudaSuccess) return noalloc_fail(int(e), cudaGetErrorString(e));
+  int st[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  e = cudaMemcpy(st, base + kStatusLive, sizeof(st), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return noalloc_fail(int(e), cudaGetErrorString(e));
+  const int* first = st[4] != 0 ? st + 4 : st;   // an earlier call's unread error comes first
+  for (int i = 0; i < 4; ++i) words[i] = first[i];
+  const int zero[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  e = cudaMemcpy(base + kStatusLive, zero, sizeof(zero), cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) return noalloc_fail(int(e), cudaGetErrorString(e));
+  return 0;
+}
 
 extern "C" int hcp_decode_attention_noalloc(const void* q, const void* arena, int layers,
                                             int pages, int page, int hkv, int d, int layer,
@@ -972,8 +1075,9 @@ extern "C" int hcp_decode_attention_noalloc(const void* q, const void* arena, in
   g_noalloc_err.clear();
   if (!q || !arena || !page_tables || !n_tokens || !out)
     return noalloc_fail(-1, "hcp_decode_attention_noalloc: null pointer argument");
-  if (batch < 1 || heads < 1 || hkv < 1 || splits < 1 || layers < 1 || pages < 1 || page < 1)
-    return noalloc_fail(-2, "hcp_decode_attention_noalloc: sizes must be positive");
+  if (batch < 1 || heads < 1 || hkv < 1 || splits < 1 || layers < 1 || pages < 1 || page < 1 ||
+      pt_stride < 1)
+    return noalloc_fail(-2, "hcp_decode_attention_noalloc: sizes (and the page-table row stride) must be positive");
   if (layer < 0 || layer >= layers)
     return noalloc_fail(-3, "hcp_decode_attention_noalloc: layer out of range");
   if (d != 64 && d != 128) return noalloc_fail(-4, "hcp_decode_attention_noalloc: head_dim must be 64 or 128");
@@ -981,28 +1085,17 @@ extern "C" int hcp_decode_attention_noalloc(const void* q, const void* arena, in
   const int G = heads / hkv;
   if (G < 1 || G > 8)
     return noalloc_fail(-6, "hcp_decode_attention_noalloc: heads / kv_heads must be 1 to 8");
+  if ((long long)pt_stride * page > 0x7fffffffLL)
+    return noalloc_fail(-2, "hcp_decode_attention_noalloc: pt_stride * page exceeds 2^31 - 1 tokens");
   const NoAllocLayout lay = noalloc_layout(batch, heads, hkv, d, splits);
   if (lay.total > kNoAllocBytes)
     return noalloc_fail(-7, "hcp_decode_attention_noalloc: problem needs " + std::to_string(lay.total) +
                                 " bytes of scratch, more than the static maximum of " +
                                 std::to_string(kNoAllocBytes) + " bytes; lower batch or splits");
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return noalloc_fail(int(e), cudaGetErrorString(e));
-  if (dev < 0 || dev >= kNoAllocMaxDevices)
-    return noalloc_fail(-8, "hcp_decode_attention_noalloc: device index out of range");
   unsigned char* base = nullptr;
-  {
-    std::lock_guard<std::mutex> lk(g_noalloc_mu);
-    if (g_noalloc_addr[dev] == nullptr) {
-      // one-time set-up for this device (device `dev` is current): device address of the array
-      void* p = nullptr;
-      e = cudaGetSymbolAddress(&p, g_decode_noalloc_scratch);
-      if (e != cudaSuccess) return noalloc_fail(int(e), std::string("cudaGetSymbolAddress: ") + cudaGetErrorString(e));
-      g_noalloc_addr[dev] = p;
-    }
-    base = static_cast<unsigned char*>(g_noalloc_addr[dev]);
-  }
+  int rc = noalloc_base(&base);
+  if (rc != 0) return rc;
+  int* status = reinterpret_cast<int*>(base + kStatusLive);
   noalloc_setup_kernel<<<1, 256, 0, stream>>>(base, lay, batch * hkv + 1);
   hcp::dec::DecodeAttnArgs a{};
   a.q = static_cast<const __nv_bfloat16*>(q);
@@ -1029,7 +1122,7 @@ extern "C" int hcp_decode_attention_noalloc(const void* q, const void* arena, in
   a.epoch_parity_src = nullptr;
   a.epoch_mul = 0;
   a.epoch_add = 1;
-  a.status = nullptr;
+  a.status = status;
   const char* err = hcp::dec::decode_attn(a, stream);
   if (err) return noalloc_fail(-9, err);
   hcp::dec::DecodeCombineArgs c{};
@@ -1044,9 +1137,9 @@ extern "C" int hcp_decode_attention_noalloc(const void* q, const void* arena, in
   c.D = d;
   c.out = static_cast<__nv_bfloat16*>(out);
   c.budget_ns = 0;
-  c.status = nullptr;
+  c.status = status;
   err = hcp::dec::decode_combine(c, stream);
   if (err) return noalloc_fail(-10, err);
-  e = cudaGetLastError();
+  cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? 0 : noalloc_fail(int(e), cudaGetErrorString(e));
 }

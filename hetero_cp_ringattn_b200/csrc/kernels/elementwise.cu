@@ -278,11 +278,12 @@ const char* qkv_prefill(const QkvPrefillArgs& a, cudaStream_t s) {
   if (a.T == 0) return nullptr;
   const size_t smem = size_t(a.H + a.Hkv) * a.D * sizeof(float);
   if (smem > 48 * 1024) {
-    static bool set = false;
-    if (!set) {
-      cudaFuncSetAttribute(qkv_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-      set = true;
-    }
+    static std::atomic<unsigned long long> attr{0};
+    if (once_per_device(attr, [] {
+          return cudaFuncSetAttribute(qkv_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      200 * 1024);
+        }) != cudaSuccess)
+      return "qkv_prefill: shared-memory opt-in failed";
   }
   qkv_prefill_kernel<<<a.T, 256, smem, s>>>(a);
   return cudaGetLastError() == cudaSuccess ? nullptr : "qkv_prefill: launch failed";

@@ -18,6 +18,7 @@
 
 #include "common.cuh"
 #include "gemm_sm100.h"
+#include "launch.h"
 
 namespace hcp {
 namespace gemm {
@@ -450,13 +451,12 @@ bool make_tma_3d_bf16(CUtensorMap* map, const void* base, uint64_t d0, uint64_t 
 template <int EPI>
 static cudaError_t launch(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p,
                           int grid, cudaStream_t stream) {
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_kernel<EPI>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-    if (e != cudaSuccess) return e;
-    attr_set = true;
-  }
+  static std::atomic<unsigned long long> attr{0};
+  cudaError_t e = once_per_device(attr, [] {
+    return cudaFuncSetAttribute(gemm_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                SMEM_BYTES);
+  });
+  if (e != cudaSuccess) return e;
   gemm_kernel<EPI><<<grid, 256, SMEM_BYTES, stream>>>(ta, tb, p);
   return cudaGetLastError();
 }

@@ -5,6 +5,7 @@
 
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstdlib>
 
 namespace hcp {
@@ -32,6 +33,23 @@ cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t s
   cfg.attrs = attr;
   cfg.numAttrs = pdl_enabled() ? 1 : 0;
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+// Kernel function attributes (dynamic shared-memory opt-in, carveout) belong to a device's
+// context, so a process that launches on several GPUs has to set them on each. `once_per_device`
+// runs `set` the first time a call site meets the current device (devices 0-63 are remembered in
+// `done`; higher ones set it on every call) and returns its result; afterwards cudaSuccess. Two
+// host threads that race both run `set`, which is harmless: the attribute calls are idempotent.
+template <typename F>
+cudaError_t once_per_device(std::atomic<unsigned long long>& done, F&& set) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const unsigned long long bit = dev < 64 ? (1ull << dev) : 0ull;
+  if (bit && (done.load(std::memory_order_acquire) & bit)) return cudaSuccess;
+  e = set();
+  if (e == cudaSuccess && bit) done.fetch_or(bit, std::memory_order_acq_rel);
+  return e;
 }
 
 }  // namespace hcp

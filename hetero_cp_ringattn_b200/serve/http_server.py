@@ -61,13 +61,26 @@ def _field_type_error(body: dict) -> Optional[str]:
 
 
 def _peer_closed(sock) -> bool:
-    """True once the client has closed its end of the connection: the socket reads as ready
-    with nothing left to read. A request pipelined behind this one reads as data, not a close."""
+    """True once the client has closed its end of the connection: the socket polls readable
+    (or hung up) and a non-blocking peek returns no bytes. A request pipelined behind this one
+    peeks as data, not a close. poll() has no descriptor-number limit (select() fails for
+    descriptors >= FD_SETSIZE, which a busy server reaches), and only an orderly shutdown or a
+    reset counts as closed."""
     try:
-        ready, _, _ = select.select([sock], [], [], 0)
-        return bool(ready) and sock.recv(1, socket.MSG_PEEK) == b""
-    except (OSError, ValueError):
+        poller = select.poll()
+        poller.register(sock, select.POLLIN | select.POLLHUP | select.POLLERR)
+        if not poller.poll(0):
+            return False
+    except ValueError:            # the socket was already closed on this side (fileno -1)
         return True
+    try:
+        return sock.recv(1, socket.MSG_PEEK | socket.MSG_DONTWAIT) == b""
+    except (BlockingIOError, InterruptedError):
+        return False
+    except (ConnectionResetError, BrokenPipeError, ConnectionAbortedError):
+        return True
+    except OSError:
+        return False
 
 
 class _WindowDeltas:
@@ -284,7 +297,13 @@ def make_handler(state: ApiState):
 
             delta_of = _StopStringDeltas(state.tok, stops) if stops else _WindowDeltas(state.tok)
             while True:
-                kind, a, b = events.get()
+                try:
+                    kind, a, b = events.get(timeout=0.05)
+                except queue.Empty:
+                    # queued or still prefilling: no write fails yet, so look at the socket
+                    if not job.cancelled and _peer_closed(self.connection):
+                        job.cancelled = True
+                    continue
                 if kind == "tok":
                     chunk = {"id": f"hcp-completion-{rid}", "object": "text_completion",
                              "created": created, "model": model,

@@ -817,3 +817,36 @@ def test_plain_client_disconnect_aborts_generation(stack, tmp_path):
         stop.set()
         loop.join(5)
         coord.trace = saved
+
+
+def test_peer_closed_handles_descriptors_above_fd_setsize():
+    """The disconnect probe works for socket descriptors above FD_SETSIZE (1024), which a busy
+    server reaches: an open idle socket is not closed, pending (pipelined) bytes are not a close,
+    and an orderly shutdown by the peer is."""
+    import os
+    import resource
+    import socket
+    from hetero_cp_ringattn_b200.serve.http_server import _peer_closed
+    target = 1500
+    soft, hard = resource.getrlimit(resource.RLIMIT_NOFILE)
+    if hard != resource.RLIM_INFINITY and hard <= target + 8:
+        pytest.skip(f"RLIMIT_NOFILE hard limit {hard} is too low for descriptor {target}")
+    if soft <= target + 8:
+        resource.setrlimit(resource.RLIMIT_NOFILE, (target + 64, hard))
+    a, b = socket.socketpair()
+    hi = None
+    try:
+        hi = socket.socket(fileno=os.dup2(a.fileno(), target))
+        a.close()
+        assert hi.fileno() == target
+        assert not _peer_closed(hi)
+        b.sendall(b"x")
+        assert not _peer_closed(hi)          # a pipelined byte is data, not a close
+        assert hi.recv(1) == b"x"
+        b.close()
+        assert _peer_closed(hi)
+    finally:
+        if hi is not None:
+            hi.close()
+        b.close()
+        resource.setrlimit(resource.RLIMIT_NOFILE, (soft, hard))
