@@ -52,6 +52,10 @@ def parse(argv=None):
     ap.add_argument("--no-graphs", action="store_true")
     ap.add_argument("--decode-batch", type=int, default=1,
                     help="also time batched decode of B requests that share the prompt length")
+    ap.add_argument("--no-check", action="store_true",
+                    help="skip the CP=N vs single-GPU vs fp32 output check (3 layers, 8k prompt)")
+    ap.add_argument("--no-secondary", action="store_true",
+                    help="skip the other BASELINE configs measured at this N (#3; #4 at N=8)")
     return ap.parse_args(argv)
 
 
@@ -134,6 +138,168 @@ def run_restatement(args) -> int:
     return 0
 
 
+def _engine(cfg, weights, rank, world, dev, group, chunks, new_tokens, B, use_graphs):
+    from hetero_cp_ringattn_b200.models.llama import LlamaCPEngine
+    page = 256
+    kv_pages = B * (-(-max(chunks) // page) + -(-(new_tokens + 8) // page)) + 2
+    return LlamaCPEngine(cfg, weights, rank=rank, world=world, device=dev, group=group,
+                         max_context=sum(chunks), max_batch=B, decode_reserve=new_tokens + 8,
+                         kv_pages=kv_pages, use_graphs=use_graphs)
+
+
+def measure_requests(eng, prompt_dev, chunks, strategy, new_tokens, steps, warmup, barrier, req):
+    """Device-timed requests (prefill + new_tokens - 1 greedy decode steps): returns the mean
+    prefill and decode milliseconds of this rank and the whole timed interval per step."""
+    def one():
+        req[0] += 1
+        e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+        e0.record()
+        tok, _ = eng.prefill(req[0], prompt_dev, chunks, strategy, decode_horizon=new_tokens)
+        e1.record()
+        cur = tok
+        for _ in range(new_tokens - 1):
+            cur = eng.decode_step([req[0]], cur)
+        e2.record()
+        eng.release(req[0])
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1), e1.elapsed_time(e2)
+
+    for _ in range(warmup):
+        one()
+    pre, dec = [], []
+    barrier()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(steps):
+        p_ms, d_ms = one()
+        pre.append(p_ms)
+        dec.append(d_ms)
+    t1.record()
+    barrier()
+    return sum(pre) / len(pre), sum(dec) / len(dec), t0.elapsed_time(t1) / steps
+
+
+def measure_batch_decode(eng, prompt_dev, chunks, strategy, new_tokens, B, barrier, req):
+    """Batched greedy decode of B requests with the same prompt: device ms per decode step."""
+    ids, toks = [], []
+    for _ in range(B):
+        req[0] += 1
+        tok, _ = eng.prefill(req[0], prompt_dev, chunks, strategy, decode_horizon=new_tokens)
+        ids.append(req[0])
+        toks.append(tok.view(1))
+    cur = torch.cat(toks)
+    for _ in range(3):
+        cur = eng.decode_step(ids, cur)
+    barrier()
+    b0, b1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n_dec = new_tokens - 4
+    b0.record()
+    for _ in range(n_dec):
+        cur = eng.decode_step(ids, cur)
+    b1.record()
+    barrier()
+    for i in ids:
+        eng.release(i)
+    return b0.elapsed_time(b1) / n_dec, n_dec
+
+
+def correctness_check(model, rank, world, dev, group, strategy, ratio, barrier):
+    """CP=N output against a single-GPU run and the float32 oracle, on the headline model's layer
+    shapes cut to 3 layers and an 8192-token prompt split like the headline run: the greedy
+    tokens of the CP run and of the single-GPU run, and the largest absolute logit differences."""
+    from hetero_cp_ringattn_b200.config import parse_ratio, preset
+    from hetero_cp_ringattn_b200.models import reference_model
+    from hetero_cp_ringattn_b200.models.llama import LlamaCPEngine
+    from hetero_cp_ringattn_b200.models.weights import ModelWeights, PreparedWeights
+    from hetero_cp_ringattn_b200.parallel.capacity import chunks_from_ratio, equal_chunks
+    cfg = preset(model)
+    cfg.num_layers = 3
+    L, steps = 8192, 6
+    chunks = chunks_from_ratio(L, parse_ratio(ratio)) if ratio else equal_chunks(L, world)
+    hf = ModelWeights.random_init(cfg, seed=0, device=dev, dtype=torch.bfloat16)
+    w = PreparedWeights.from_weights(hf)
+    prompt = torch.randint(0, cfg.vocab_size, (L,), generator=torch.Generator().manual_seed(5))
+
+    def run(eng, ch, strat):
+        tok, logits = eng.prefill(7, prompt, ch, strat, decode_horizon=steps + 1, return_logits=True)
+        toks, cur = [int(tok)], tok
+        for _ in range(steps):
+            cur = eng.decode_step([7], cur)
+            toks.append(int(cur))
+        eng.release(7)
+        eng.check_device()
+        return toks, logits.float()
+
+    eng = LlamaCPEngine(cfg, w, rank=rank, world=world, device=dev, group=group, max_context=L,
+                        max_batch=1, decode_reserve=16)
+    cp_toks, cp_logits = run(eng, chunks, strategy)
+    eng.close()
+    out = None
+    if rank == 0:
+        single = LlamaCPEngine(cfg, w, device=dev, max_context=L, max_batch=1, decode_reserve=16)
+        one_toks, one_logits = run(single, [L], "vanilla")
+        single.close()
+        oracle = reference_model.forward(hf, prompt.to(dev), last_only=True)[0].float()
+        out = {"layers": 3, "prompt": L, "chunks": chunks, "strategy": strategy,
+               "decode_steps": steps,
+               "logits_max_abs_err": float((cp_logits - one_logits).abs().max()),
+               "logits_max_abs_err_vs_fp32": float((cp_logits - oracle).abs().max()),
+               "single_gpu_max_abs_err_vs_fp32": float((one_logits - oracle).abs().max()),
+               "tokens_match": cp_toks == one_toks,
+               "argmax_matches_fp32": int(torch.argmax(cp_logits)) == int(torch.argmax(oracle)),
+               "target": "logits_max_abs_err <= 2e-2 (CP=N vs one GPU, both bf16)"}
+        out["pass"] = bool(out["tokens_match"] and out["logits_max_abs_err"] <= 2e-2)
+    del w, hf
+    torch.cuda.empty_cache()
+    barrier()
+    return out
+
+
+def secondary_configs(world):
+    """BASELINE configs measured besides the headline at this N (config id, bench config,
+    capacity ratio or None for equal chunks, decode batch sizes)."""
+    out = [("#3", "qwen2.5-3b-64k", "5:5:5:5:2:2:1:1" if world == 8 else None, [1])]
+    if world == 8:
+        out.append(("#4", "llama-3-8b-128k", None, [1, 8]))
+    return out
+
+
+def run_secondary(cid, name, ratio, batches, rank, world, dev, group, barrier, req, max_over):
+    from hetero_cp_ringattn_b200.config import parse_ratio, preset
+    from hetero_cp_ringattn_b200.models.weights import PreparedWeights
+    from hetero_cp_ringattn_b200.parallel.capacity import chunks_from_ratio, equal_chunks
+    spec = CONFIGS[name]
+    cfg = preset(spec["model"])
+    Lp, new_tokens = spec["prompt"], spec["new_tokens"]
+    chunks = chunks_from_ratio(Lp, parse_ratio(ratio)) if ratio else equal_chunks(Lp, world)
+    strategy = "zigzag" if world > 1 else "vanilla"
+    weights = PreparedWeights.random(cfg, seed=0, device=dev)
+    B = max(batches)
+    eng = _engine(cfg, weights, rank, world, dev, group, chunks, new_tokens, B, True)
+    prompt = torch.randint(0, cfg.vocab_size, (Lp,), generator=torch.Generator().manual_seed(99))
+    prompt_dev = prompt.to(dev)
+    pre, dec, _ = measure_requests(eng, prompt_dev, chunks, strategy, new_tokens, 1, 1, barrier, req)
+    pre, dec = max_over(pre), max_over(dec)
+    res = {"config": cid, "model": spec["model"], "seq_len": Lp, "chunks": chunks,
+           "ratio": ratio or "equal", "strategy": strategy, "steps": 1, "warmup": 1,
+           "prefill_tok_s": Lp / (pre / 1e3), "ttft_ms": pre,
+           "decode_ms_per_token": dec / max(1, new_tokens - 1),
+           "decode_tok_s": (new_tokens - 1) / (dec / 1e3), "new_tokens": new_tokens}
+    for b in batches:
+        if b > 1:
+            ms, n = measure_batch_decode(eng, prompt_dev, chunks, strategy, new_tokens, b, barrier, req)
+            ms = max_over(ms)
+            res[f"decode_batch{b}"] = {"decode_ms_per_step": ms, "decode_tok_s": b * 1e3 / ms,
+                                       "steps_timed": n}
+    eng.check_device()
+    eng.close()
+    del weights, eng
+    torch.cuda.empty_cache()
+    barrier()
+    return res
+
+
 def main():
     args = parse()
     if args.impl == "reference":
@@ -143,7 +309,6 @@ def main():
         return run_restatement(args)
 
     from hetero_cp_ringattn_b200.config import preset, parse_ratio
-    from hetero_cp_ringattn_b200.models.llama import LlamaCPEngine
     from hetero_cp_ringattn_b200.models.weights import PreparedWeights
     from hetero_cp_ringattn_b200.parallel.capacity import chunks_from_ratio, equal_chunks
     from hetero_cp_ringattn_b200.utils import launches
@@ -175,59 +340,33 @@ def main():
     else:
         chunks = equal_chunks(Lp, world)
 
-    weights = PreparedWeights.random(cfg, seed=0, device=dev)
-    B = max(1, args.decode_batch)
-    page = 256
-    kv_pages = B * (-(-max(chunks) // page) + -(-(new_tokens + 8) // page)) + 2
-    eng = LlamaCPEngine(cfg, weights, rank=rank, world=world, device=dev, group=group,
-                        max_context=Lp, max_batch=B, decode_reserve=new_tokens + 8,
-                        kv_pages=kv_pages, use_graphs=not args.no_graphs)
-    gen = torch.Generator().manual_seed(1234)
-    prompt = torch.randint(0, cfg.vocab_size, (Lp,), generator=gen, dtype=torch.int64).pin_memory()
-    prompt_dev = prompt.to(dev)
-
     def barrier():
         if world > 1:
             dist.barrier(group=group)
         torch.cuda.synchronize()
 
+    def max_over(v):
+        return max_over_ranks(v, group)
+
+    weights = PreparedWeights.random(cfg, seed=0, device=dev)
+    B = max(1, args.decode_batch)
+    eng = _engine(cfg, weights, rank, world, dev, group, chunks, new_tokens, B, not args.no_graphs)
+    gen = torch.Generator().manual_seed(1234)
+    prompt = torch.randint(0, cfg.vocab_size, (Lp,), generator=gen, dtype=torch.int64).pin_memory()
+    prompt_dev = prompt.to(dev)
     req = [100]
 
-    def one_request(dev_prompt):
-        """Device-timed request: prefill (events) + decode (events). Returns (prefill_ms, decode_ms)."""
-        req[0] += 1
-        e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
-        e0.record()
-        tok, _ = eng.prefill(req[0], dev_prompt, chunks, strategy, decode_horizon=new_tokens)
-        e1.record()
-        cur = tok
-        for _ in range(new_tokens - 1):
-            cur = eng.decode_step([req[0]], cur)
-        e2.record()
-        eng.release(req[0])
-        torch.cuda.synchronize()
-        return e0.elapsed_time(e1), e1.elapsed_time(e2), cur
-
     for _ in range(args.warmup):
-        one_request(prompt_dev)
+        measure_requests(eng, prompt_dev, chunks, strategy, new_tokens, 1, 0, barrier, req)
     barrier()
     launches.reset()
-    pre_ms, dec_ms = [], []
     with ClockSampler(local_rank) as clocks:
-        barrier()
-        t_all0 = torch.cuda.Event(enable_timing=True)
-        t_all1 = torch.cuda.Event(enable_timing=True)
-        t_all0.record()
-        for _ in range(args.steps):
-            p, d, _ = one_request(prompt_dev)
-            pre_ms.append(p)
-            dec_ms.append(d)
-        t_all1.record()
-        barrier()
+        pre_ms, dec_ms, step_ms = measure_requests(eng, prompt_dev, chunks, strategy, new_tokens,
+                                                   args.steps, 0, barrier, req)
     n_launch = launches.total() // max(1, args.steps)
-    total_ms = max_over_ranks(t_all0.elapsed_time(t_all1) / args.steps, group)
-    prefill_ms = max_over_ranks(sum(pre_ms) / len(pre_ms), group)
-    decode_ms = max_over_ranks(sum(dec_ms) / len(dec_ms), group)
+    total_ms = max_over(step_ms)
+    prefill_ms = max_over(pre_ms)
+    decode_ms = max_over(dec_ms)
     eng.check_device()
 
     # ---------------------------------------------------------------- end to end (public API)
@@ -253,8 +392,8 @@ def main():
             if i > 0:  # first iteration is a warm-up of the host path
                 ttfts.append(t1 - t0)
                 totals.append(t2 - t0)
-        ttft = max_over_ranks(sum(ttfts) / len(ttfts), group)
-        total = max_over_ranks(sum(totals) / len(totals), group)
+        ttft = max_over(sum(ttfts) / len(ttfts))
+        total = max_over(sum(totals) / len(totals))
         e2e = {"value": Lp / ttft, "unit": "prompt tokens/s (end to end: pinned prompt H2D, "
                "prefill, first-token D2H)", "ttft_ms": ttft * 1e3, "request_ms": total * 1e3,
                "decode_tok_s": (new_tokens - 1) / max(1e-9, total - ttft),
@@ -263,32 +402,32 @@ def main():
     # ---------------------------------------------------------------- batched decode (B requests)
     batch = None
     if B > 1:
-        ids = []
-        toks = []
-        for b in range(B):
-            req[0] += 1
-            tok, _ = eng.prefill(req[0], prompt_dev, chunks, strategy, decode_horizon=new_tokens)
-            ids.append(req[0])
-            toks.append(tok.view(1))
-        cur = torch.cat(toks)
-        for _ in range(3):
-            cur = eng.decode_step(ids, cur)
-        barrier()
-        b0, b1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        n_dec = new_tokens - 4
-        b0.record()
-        for _ in range(n_dec):
-            cur = eng.decode_step(ids, cur)
-        b1.record()
-        barrier()
-        bms = max_over_ranks(b0.elapsed_time(b1) / n_dec, group)
-        for i in ids:
-            eng.release(i)
+        bms, n_dec = measure_batch_decode(eng, prompt_dev, chunks, strategy, new_tokens, B, barrier, req)
+        bms = max_over(bms)
         batch = {"batch": B, "context": Lp, "decode_ms_per_step": bms,
                  "decode_tok_s": B * 1e3 / bms, "steps_timed": n_dec}
+    eng.close()
+    del eng, weights
+    torch.cuda.empty_cache()
+    barrier()
+
+    # ---------------------------------------------------------------- after the timed region
+    # output check of the CP=N pipeline (3 layers of the headline shape) and the other BASELINE
+    # configs at this N; each is its own device-timed measurement, none changes `value`
+    check = None
+    if not args.no_check:
+        check = correctness_check(spec["model"], rank, world, dev, group, strategy, args.ratio, barrier)
+    secondary = []
+    if not args.no_secondary:
+        for cid, name, ratio, batches in secondary_configs(world):
+            secondary.append(run_secondary(cid, name, ratio, batches, rank, world, dev, group,
+                                           barrier, req, max_over))
 
     clk = clocks.summary()
     value = Lp / (prefill_ms / 1e3)
+    ring_mode = ("single rank" if world == 1 else
+                 "serial (HCP_DISABLE_OVERLAP=1)" if os.environ.get("HCP_DISABLE_OVERLAP") == "1"
+                 else "overlapped, in the attention kernel")
     if rank == 0:
         out = {
             "metric": "prefill tok/s & TTFT @32k and decode tok/s (CP=N B200, max over ranks)",
@@ -310,6 +449,7 @@ def main():
             "config": {"model": spec["model"], "global_batch": 1, "seq_len": Lp,
                        "new_tokens": new_tokens, "parallelism": f"cp{world}",
                        "chunks": chunks, "strategy": strategy,
+                       "ring": ring_mode,
                        "l2": "no flush: weights + activations (>2.5 GB) exceed the 126 MB L2",
                        "step": "one request = prefill of the prompt + 127 decode steps"},
             "clocks": clk,
@@ -317,8 +457,11 @@ def main():
         }
         if batch is not None:
             out["decode_batch"] = batch
+        if check is not None:
+            out["check"] = check
+        if secondary:
+            out["secondary"] = secondary
         print(json.dumps(out), flush=True)
-    eng.close()
     if world > 1:
         dist.barrier(group=group)
         dist.destroy_process_group()

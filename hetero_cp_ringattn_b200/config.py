@@ -343,8 +343,9 @@ class EnvConfig:
     perf_log: Optional[str] = None          # HCP_PERF_LOG: JSONL perf events
     micro_kv_block_size: int = 0            # HCP_MICRO_KV_BLOCK_SIZE: host-path ring fold block
                                             # (0 -> 128, the CUDA kernels' fixed KV tile)
-    disable_overlap: bool = False           # HCP_DISABLE_OVERLAP: accepted; both paths already
-                                            # stage every rank's KV before the attention reads it
+    disable_overlap: bool = False           # HCP_DISABLE_OVERLAP=1: serial ring (push every
+                                            # rank's KV, wait for all, then attend) instead of the
+                                            # overlapped in-kernel ring
     decode_ring: bool = True                # HCP_RING_DECODE_RING=0: legacy KV re-send decode
                                             # (host path; CUDA ranks warn and keep the exchange)
     decode_sd: bool = True                  # HCP_RING_DECODE_SD: capacity-scheduled KV growth;
@@ -356,8 +357,9 @@ class EnvConfig:
     p2p_spin_budget_ms: int = 5000          # HCP_P2P_SPIN_BUDGET_MS: device-side peer-wait limit
     device: Optional[str] = None            # HCP_TORCH_DEVICE / HCP_TCH_DEVICE
     nvtx: bool = False                      # HCP_NVTX: NVTX ranges per prefill layer / decode step
-    fused_qkv: Optional[bool] = None        # HCP_FUSED_QKV: projection GEMM epilogue pushes K/V
-                                            # (default: on a single rank only, see the engine)
+    fused_qkv: Optional[bool] = None        # HCP_FUSED_QKV: the projection GEMM's epilogue does
+                                            # RoPE + the K/V writes (default on; 0: GEMM + a
+                                            # separate RoPE / K/V kernel)
 
     @classmethod
     def from_env(cls) -> "EnvConfig":

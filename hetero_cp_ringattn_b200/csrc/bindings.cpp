@@ -206,6 +206,37 @@ int64_t decode_attn_ctas_per_sm(int64_t D, int64_t G) {
 }
 
 // ----------------------------------------------------------------------------- runtime
+// The overlapped ring's per-request plan (built on the host once per request): tile_src int64
+// [ceil(L / 128)] bitmask of the ranks with rows in each KV tile, push_tiles int32 [n, 3] this
+// rank's own tiles as (tile, first, end) row ranges of `pos`, pair_start int32 first kv tile per
+// q-tile pair. No tile_src: the serial ring.
+struct RingPlan {
+  c10::optional<torch::Tensor> tile_src, push_tiles, pair_start;
+  RingPlan(c10::optional<torch::Tensor> t, c10::optional<torch::Tensor> p, c10::optional<torch::Tensor> s)
+      : tile_src(std::move(t)), push_tiles(std::move(p)), pair_start(std::move(s)) {}
+  void apply(hcp::RingLayerArgs& a, int world) const {
+    if (!tile_src.has_value() || !tile_src->defined()) return;
+    TORCH_CHECK(tile_src->is_cuda() && tile_src->scalar_type() == torch::kInt64 && tile_src->is_contiguous(),
+                "tile_src must be a contiguous CUDA int64 tensor");
+    TORCH_CHECK(tile_src->numel() >= (a.L + 127) / 128, "tile_src needs one word per KV tile");
+    a.tile_src = reinterpret_cast<const unsigned long long*>(tile_src->data_ptr<int64_t>());
+    if (push_tiles.has_value() && push_tiles->defined() && push_tiles->numel() > 0) {
+      TORCH_CHECK(push_tiles->is_cuda() && push_tiles->scalar_type() == torch::kInt32 &&
+                      push_tiles->is_contiguous() && push_tiles->dim() == 2 && push_tiles->size(1) == 3,
+                  "push_tiles must be a contiguous CUDA int32 [n, 3] tensor");
+      a.push_tiles = push_tiles->data_ptr<int>();
+      a.n_push = int(push_tiles->size(0));
+    }
+    if (pair_start.has_value() && pair_start->defined() && pair_start->numel() > 0) {
+      TORCH_CHECK(pair_start->is_cuda() && pair_start->scalar_type() == torch::kInt32 && pair_start->is_contiguous(),
+                  "pair_start must be a contiguous CUDA int32 tensor");
+      TORCH_CHECK(pair_start->numel() >= ((a.T + 127) / 128 + 1) / 2, "pair_start needs one entry per q-tile pair");
+      a.pair_start = pair_start->data_ptr<int>();
+    }
+    (void)world;
+  }
+};
+
 class PyRuntime {
  public:
   PyRuntime(int64_t rank, int64_t world, int64_t device, int64_t layers, int64_t pages,
@@ -254,7 +285,8 @@ class PyRuntime {
                                 int64_t L, int64_t kv_start_tile, double scale, bool causal,
                                 torch::Tensor q_out, torch::Tensor o_out,
                                 c10::optional<torch::Tensor> lse_out, int64_t epoch,
-                                c10::optional<torch::Tensor> existing_slot_pos, bool has_qkv = true) {
+                                c10::optional<torch::Tensor> existing_slot_pos, bool has_qkv,
+                                const RingPlan& ring) {
     check_cuda_bf16(qkv, "qkv");
     check_cuda_bf16(q_out, "q_out");
     check_cuda_bf16(o_out, "o_out");
@@ -296,6 +328,7 @@ class PyRuntime {
       a.existing_slot_pos = existing_slot_pos->data_ptr<int>();
       a.existing_n = int(existing_slot_pos->numel());
     }
+    ring.apply(a, c.world);
     return a;
   }
 
@@ -303,10 +336,13 @@ class PyRuntime {
                   int64_t layer, c10::optional<torch::Tensor> page_table, int64_t slot_base,
                   int64_t L, int64_t kv_start_tile, double scale, bool causal, torch::Tensor q_out,
                   torch::Tensor o_out, c10::optional<torch::Tensor> lse_out, int64_t epoch,
-                  c10::optional<torch::Tensor> existing_slot_pos) {
+                  c10::optional<torch::Tensor> existing_slot_pos,
+                  c10::optional<torch::Tensor> tile_src, c10::optional<torch::Tensor> push_tiles,
+                  c10::optional<torch::Tensor> pair_start) {
     const c10::cuda::CUDAGuard g(qkv.device());
     auto a = layer_args(qkv, pos, cos_t, sin_t, layer, page_table, slot_base, L, kv_start_tile,
-                        scale, causal, q_out, o_out, lse_out, epoch, existing_slot_pos);
+                        scale, causal, q_out, o_out, lse_out, epoch, existing_slot_pos, true,
+                        RingPlan(tile_src, push_tiles, pair_start));
     auto st = rt_.PushLayer(a, cur_stream());
     TORCH_CHECK(st.ok(), "push_layer: ", st.ToString());
   }
@@ -318,14 +354,17 @@ class PyRuntime {
                         c10::optional<torch::Tensor> page_table, int64_t slot_base, int64_t L,
                         int64_t kv_start_tile, double scale, bool causal, torch::Tensor q_out,
                         torch::Tensor o_out, c10::optional<torch::Tensor> lse_out, int64_t epoch,
-                        c10::optional<torch::Tensor> existing_slot_pos) {
+                        c10::optional<torch::Tensor> existing_slot_pos,
+                        c10::optional<torch::Tensor> tile_src, c10::optional<torch::Tensor> push_tiles,
+                        c10::optional<torch::Tensor> pair_start) {
     check_cuda_bf16(x, "x");
     check_cuda_bf16(w_qkv, "w_qkv");
     TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1 && w_qkv.is_contiguous() && x.size(1) == w_qkv.size(1),
                 "x [T, hidden] row-major and w_qkv [N, hidden] contiguous");
     const c10::cuda::CUDAGuard g(x.device());
     auto a = layer_args(x, pos, cos_t, sin_t, layer, page_table, slot_base, L, kv_start_tile, scale,
-                        causal, q_out, o_out, lse_out, epoch, existing_slot_pos, /*has_qkv=*/false);
+                        causal, q_out, o_out, lse_out, epoch, existing_slot_pos, /*has_qkv=*/false,
+                        RingPlan(tile_src, push_tiles, pair_start));
     a.x = x.data_ptr();
     a.ldx = x.stride(0);
     a.w_qkv = w_qkv.data_ptr();
@@ -344,13 +383,35 @@ class PyRuntime {
                     int64_t layer, c10::optional<torch::Tensor> page_table, int64_t slot_base,
                     int64_t L, int64_t kv_start_tile, double scale, bool causal,
                     torch::Tensor q_out, torch::Tensor o_out, c10::optional<torch::Tensor> lse_out,
-                    int64_t epoch, c10::optional<torch::Tensor> existing_slot_pos) {
+                    int64_t epoch, c10::optional<torch::Tensor> existing_slot_pos,
+                    c10::optional<torch::Tensor> tile_src, c10::optional<torch::Tensor> push_tiles,
+                    c10::optional<torch::Tensor> pair_start) {
     // `qkv` only gives the row count here (the projection output or the layer input)
     const c10::cuda::CUDAGuard g(qkv.device());
     auto a = layer_args(qkv, pos, cos_t, sin_t, layer, page_table, slot_base, L, kv_start_tile,
-                        scale, causal, q_out, o_out, lse_out, epoch, existing_slot_pos, false);
+                        scale, causal, q_out, o_out, lse_out, epoch, existing_slot_pos, false,
+                        RingPlan(tile_src, push_tiles, pair_start));
     auto st = rt_.AttendLayer(a, cur_stream());
     TORCH_CHECK(st.ok(), "attend_layer: ", st.ToString());
+  }
+
+  void publish_tiles(torch::Tensor push_tiles, int64_t epoch) {
+    TORCH_CHECK(push_tiles.is_cuda() && push_tiles.scalar_type() == torch::kInt32 &&
+                    push_tiles.is_contiguous() && push_tiles.dim() == 2 && push_tiles.size(1) == 3,
+                "push_tiles must be a contiguous CUDA int32 [n, 3] tensor");
+    const c10::cuda::CUDAGuard g(push_tiles.device());
+    auto st = rt_.PublishTiles(push_tiles.data_ptr<int>(), int(push_tiles.size(0)), uint64_t(epoch),
+                               cur_stream());
+    TORCH_CHECK(st.ok(), "publish_tiles: ", st.ToString());
+  }
+
+  void broadcast_token(torch::Tensor tok, int64_t src, int64_t epoch) {
+    TORCH_CHECK(tok.is_cuda() && tok.scalar_type() == torch::kInt64 && tok.numel() >= 1,
+                "tok must be a CUDA int64 tensor");
+    const c10::cuda::CUDAGuard g(tok.device());
+    auto st = rt_.BroadcastToken(reinterpret_cast<long long*>(tok.data_ptr<int64_t>()), int(src),
+                                 uint64_t(epoch), cur_stream());
+    TORCH_CHECK(st.ok(), "broadcast_token: ", st.ToString());
   }
 
   void qkv_decode(torch::Tensor qkv_f32, torch::Tensor pos, torch::Tensor cos_t, torch::Tensor sin_t,
@@ -593,16 +654,21 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       .def("push_layer", &PyRuntime::push_layer, py::arg("qkv"), py::arg("pos"), py::arg("cos_t"),
            py::arg("sin_t"), py::arg("layer"), py::arg("page_table"), py::arg("slot_base"), py::arg("L"),
            py::arg("kv_start_tile"), py::arg("scale"), py::arg("causal"), py::arg("q_out"),
-           py::arg("o_out"), py::arg("lse_out"), py::arg("epoch"), py::arg("existing_slot_pos") = py::none())
+           py::arg("o_out"), py::arg("lse_out"), py::arg("epoch"),
+           py::arg("existing_slot_pos") = py::none(), py::arg("tile_src") = py::none(), py::arg("push_tiles") = py::none(), py::arg("pair_start") = py::none())
       .def("push_layer_fused", &PyRuntime::push_layer_fused, py::arg("x"), py::arg("w_qkv"),
            py::arg("b_qkv"), py::arg("pos"), py::arg("cos_t"), py::arg("sin_t"), py::arg("layer"),
            py::arg("page_table"), py::arg("slot_base"), py::arg("L"), py::arg("kv_start_tile"),
            py::arg("scale"), py::arg("causal"), py::arg("q_out"), py::arg("o_out"),
-           py::arg("lse_out"), py::arg("epoch"), py::arg("existing_slot_pos") = py::none())
+           py::arg("lse_out"), py::arg("epoch"),
+           py::arg("existing_slot_pos") = py::none(), py::arg("tile_src") = py::none(), py::arg("push_tiles") = py::none(), py::arg("pair_start") = py::none())
       .def("attend_layer", &PyRuntime::attend_layer, py::arg("qkv"), py::arg("pos"), py::arg("cos_t"),
            py::arg("sin_t"), py::arg("layer"), py::arg("page_table"), py::arg("slot_base"), py::arg("L"),
            py::arg("kv_start_tile"), py::arg("scale"), py::arg("causal"), py::arg("q_out"),
-           py::arg("o_out"), py::arg("lse_out"), py::arg("epoch"), py::arg("existing_slot_pos") = py::none())
+           py::arg("o_out"), py::arg("lse_out"), py::arg("epoch"),
+           py::arg("existing_slot_pos") = py::none(), py::arg("tile_src") = py::none(), py::arg("push_tiles") = py::none(), py::arg("pair_start") = py::none())
+      .def("publish_tiles", &PyRuntime::publish_tiles, py::arg("push_tiles"), py::arg("epoch"))
+      .def("broadcast_token", &PyRuntime::broadcast_token, py::arg("tok"), py::arg("src"), py::arg("epoch"))
       .def("qkv_decode", &PyRuntime::qkv_decode)
       .def("decode_attn", &PyRuntime::decode_attn, py::arg("q"), py::arg("layer"), py::arg("page_tables"),
            py::arg("n_tokens"), py::arg("scale"), py::arg("splits"), py::arg("part_o"),

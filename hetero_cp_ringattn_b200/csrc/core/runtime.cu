@@ -38,7 +38,10 @@ Status DomainRuntime::Init(const RuntimeConfig& cfg) {
   if (!st.ok()) return st;
   off_flags_ = 0;
   size_t flags_bytes = size_t(kFlagWords) * sizeof(unsigned long long);
-  off_xslot_ = align_up(off_flags_ + flags_bytes, 4096);
+  off_tflags_ = align_up(off_flags_ + flags_bytes, 4096);
+  const size_t tiles = (size_t(cfg.stage_cap) + kRingTile - 1) / kRingTile;
+  tflag_parity_bytes_ = align_up(tiles * cfg.world * sizeof(unsigned long long), 256);
+  off_xslot_ = align_up(off_tflags_ + 2 * tflag_parity_bytes_, 4096);
   xslot_bytes_ = size_t(2) * cfg.world * cfg.max_batch * cfg.num_heads * (cfg.geom.d + 1) * sizeof(float);
   off_stage_ = align_up(off_xslot_ + xslot_bytes_, 4096);
   stage_parity_bytes_ = size_t(2) * cfg.geom.hkv * size_t(cfg.stage_cap) * cfg.geom.d * 2;
@@ -110,7 +113,7 @@ Status DomainRuntime::OpenPeersLocal(const std::vector<DomainRuntime*>& peers) {
 Status DomainRuntime::BuildTables() {
   const int n = cfg_.world;
   std::vector<void*> st0(n), st1(n);
-  std::vector<unsigned long long*> ready(n), consumed(n), dready(n);
+  std::vector<unsigned long long*> ready(n), consumed(n), dready(n), tf0(n), tf1(n), tok(n);
   std::vector<float*> xs(n);
   for (int r = 0; r < n; ++r) {
     uint8_t* b = peer_base_[r];
@@ -121,6 +124,9 @@ Status DomainRuntime::BuildTables() {
     ready[r] = fl + kFlagKvReady + cfg_.rank;
     consumed[r] = fl + kFlagConsumed + cfg_.rank;
     dready[r] = fl + kFlagDecReady + cfg_.rank;
+    tok[r] = fl + kFlagToken;
+    tf0[r] = reinterpret_cast<unsigned long long*>(b + off_tflags_);
+    tf1[r] = reinterpret_cast<unsigned long long*>(b + off_tflags_ + tflag_parity_bytes_);
     xs[r] = reinterpret_cast<float*>(b + off_xslot_);
   }
   auto alloc_copy = [&](void** dst, const void* src, size_t bytes) -> Status {
@@ -138,6 +144,9 @@ Status DomainRuntime::BuildTables() {
   if (!(s = alloc_copy(reinterpret_cast<void**>(&consumed_tab_), consumed.data(), pb)).ok()) return s;
   if (!(s = alloc_copy(reinterpret_cast<void**>(&dec_ready_tab_), dready.data(), pb)).ok()) return s;
   if (!(s = alloc_copy(reinterpret_cast<void**>(&xslot_tab_), xs.data(), pb)).ok()) return s;
+  if (!(s = alloc_copy(reinterpret_cast<void**>(&tflag_tab_[0]), tf0.data(), pb)).ok()) return s;
+  if (!(s = alloc_copy(reinterpret_cast<void**>(&tflag_tab_[1]), tf1.data(), pb)).ok()) return s;
+  if (!(s = alloc_copy(reinterpret_cast<void**>(&token_tab_), tok.data(), pb)).ok()) return s;
   return Status::Ok();
 }
 
@@ -154,8 +163,15 @@ Status DomainRuntime::PushLayer(const RingLayerArgs& a, cudaStream_t stream) {
   const int parity = int(a.epoch & 1ull);
   const int n = cfg_.world;
   unsigned long long* fl = flags();
+  const bool overlap = a.tile_src != nullptr && n > 1;
+  if (overlap && a.existing_n > 0)
+    return Status::InvalidArgument("continuation segments use the serial ring (no tile sources)");
+  // overlapped ring: this rank's rows go to its own staging buffer only (the attention kernel
+  // pushes them to the peers); nothing to wait for, only this rank reads its own buffer
+  void* const* stage_dst = overlap ? stage_tab_[parity] + cfg_.rank : stage_tab_[parity];
+  const int n_dst = overlap ? 1 : n;
   // 1. the staging parity we write must have been released by every rank (epoch - 2 consumed)
-  if (n > 1 && a.epoch > 2) {
+  if (!overlap && n > 1 && a.epoch > 2) {
     const char* e = ew::wait_consumed(fl + kFlagConsumed, n, a.epoch - 2, cfg_.peer_wait_budget_ns,
                                       status_, stream);
     if (e) return Status::Internal(e);
@@ -204,10 +220,10 @@ Status DomainRuntime::PushLayer(const RingLayerArgs& a, cudaStream_t stream) {
     q.page_table = a.page_table;
     q.slot_base = a.slot_base;
     q.slot_cap = a.slot_cap;
-    q.stage_ptrs = stage_tab_[parity];
-    q.n_stage = n;
+    q.stage_ptrs = stage_dst;
+    q.n_stage = n_dst;
     q.stage_cap = cfg_.stage_cap;
-    q.done_counter = n > 1 ? counters_ : nullptr;
+    q.done_counter = (n > 1 && !overlap) ? counters_ : nullptr;
     q.ready_ptrs = kv_ready_tab_;
     q.epoch = a.epoch;
     const char* e = gemm::gemm_qkv_push(g, q, stream);
@@ -232,17 +248,17 @@ Status DomainRuntime::PushLayer(const RingLayerArgs& a, cudaStream_t stream) {
   q.page_table = a.page_table;
   q.slot_base = a.slot_base;
   q.slot_cap = a.slot_cap;
-  q.stage_ptrs = stage_tab_[parity];
-  q.n_stage = n;
+  q.stage_ptrs = stage_dst;
+  q.n_stage = n_dst;
   q.stage_cap = cfg_.stage_cap;
-  q.done_counter = n > 1 ? counters_ : nullptr;
+  q.done_counter = (n > 1 && !overlap) ? counters_ : nullptr;
   q.ready_ptrs = kv_ready_tab_;
   q.epoch = a.epoch;
   q.status = status_;
   if (a.T > 0) {
     const char* e = ew::qkv_prefill(q, stream);
     if (e) return Status::Internal(e);
-  } else if (n > 1) {
+  } else if (n > 1 && !overlap) {
     // a rank without tokens still has to publish its (empty) contribution
     const char* e = ew::signal_peers(kv_ready_tab_, n, a.epoch, stream);
     if (e) return Status::Internal(e);
@@ -274,8 +290,31 @@ Status DomainRuntime::AttendLayer(const RingLayerArgs& a, cudaStream_t stream) {
     at.scale = a.scale;
     at.causal = a.causal;
     at.kv_start_tile = a.kv_start_tile;
-    at.kv_ready = nullptr;
+    at.wait_budget_ns = cfg_.peer_wait_budget_ns;
     at.status = status_;
+    if (a.tile_src != nullptr && n > 1) {
+      // overlapped ring: the kernel pushes this rank's rows, waits per remote tile and releases
+      // the parity itself (no barrier or signal launches)
+      attn::RingArgs& rg = at.ring;
+      rg.world = n;
+      rg.my_rank = cfg_.rank;
+      rg.epoch = a.epoch;
+      rg.tile_src = a.tile_src;
+      rg.tile_flags = tile_flags(parity);
+      rg.pair_start = a.pair_start;
+      rg.push_tiles = a.push_tiles;
+      rg.n_push = a.n_push;
+      rg.own_stage = sk;
+      rg.stage_ptrs = stage_tab_[parity];
+      rg.tflag_ptrs = tflag_tab_[parity];
+      rg.consumed = fl + kFlagConsumed;
+      rg.consumed_ptrs = consumed_tab_;
+      rg.counters = counters_ + 16;
+      rg.stage_cap = cfg_.stage_cap;
+      const char* e = attn::attn_fwd(at, stream);
+      if (e) return Status::Internal(e);
+      return Status::Ok();
+    }
     if (n > 1) {
       // all ranks' pushes must have landed before the kernel reads remote rows
       const char* e = ew::wait_consumed(fl + kFlagKvReady, n, a.epoch, cfg_.peer_wait_budget_ns,
@@ -291,6 +330,24 @@ Status DomainRuntime::AttendLayer(const RingLayerArgs& a, cudaStream_t stream) {
     if (e) return Status::Internal(e);
   }
   return Status::Ok();
+}
+
+Status DomainRuntime::PublishTiles(const int* push_tiles, int n_push, uint64_t epoch,
+                                   cudaStream_t stream) {
+  if (base_ == nullptr || stage_tab_[0] == nullptr) return Status::InvalidArgument("runtime not ready");
+  if (n_push == 0) return Status::Ok();
+  const char* e = ew::publish_tiles(push_tiles, n_push, tflag_tab_[int(epoch & 1ull)], cfg_.world,
+                                    cfg_.rank, epoch, stream);
+  return e ? Status::Internal(e) : Status::Ok();
+}
+
+Status DomainRuntime::BroadcastToken(long long* tok, int src, uint64_t epoch, cudaStream_t stream) {
+  if (base_ == nullptr || token_tab_ == nullptr) return Status::InvalidArgument("runtime not ready");
+  if (src < 0 || src >= cfg_.world) return Status::InvalidArgument("token source rank out of range");
+  if (cfg_.world == 1) return Status::Ok();
+  const char* e = ew::token_bcast(tok, token_tab_, flags() + kFlagToken, cfg_.world,
+                                  src == cfg_.rank, epoch, cfg_.peer_wait_budget_ns, status_, stream);
+  return e ? Status::Internal(e) : Status::Ok();
 }
 
 Status DomainRuntime::CheckDevice(cudaStream_t stream) {
@@ -318,9 +375,13 @@ Status DomainRuntime::Shutdown() {
   peer_opened_ipc_.clear();
   for (void* t : {static_cast<void*>(stage_tab_[0]), static_cast<void*>(stage_tab_[1]),
                   static_cast<void*>(kv_ready_tab_), static_cast<void*>(consumed_tab_),
-                  static_cast<void*>(dec_ready_tab_), static_cast<void*>(xslot_tab_)})
+                  static_cast<void*>(dec_ready_tab_), static_cast<void*>(xslot_tab_),
+                  static_cast<void*>(tflag_tab_[0]), static_cast<void*>(tflag_tab_[1]),
+                  static_cast<void*>(token_tab_)})
     if (t) cudaFree(t);
   stage_tab_[0] = stage_tab_[1] = nullptr;
+  tflag_tab_[0] = tflag_tab_[1] = nullptr;
+  token_tab_ = nullptr;
   kv_ready_tab_ = consumed_tab_ = dec_ready_tab_ = nullptr;
   xslot_tab_ = nullptr;
   if (status_) cudaFree(status_);

@@ -9,6 +9,7 @@
 //
 // Shared region (one cudaMalloc, exported with one IPC handle; identical offsets on every rank):
 //   flags     uint64[kFlagWords]                           (kv_ready / consumed / dec_ready / ...)
+//   tflags    uint64[2][ceil(stage_cap / 128)][world]      per-(KV tile, source rank) ready epochs
 //   xslot     fp32 [2][world][max_batch][H][D+1]          decode (O, LSE) exchange slots
 //   stage     bf16 [2 parity][2 K/V][Hkv][stage_cap][D]   position-ordered prefill KV
 //   arena     bf16 [layers][pages][2][Hkv][page][D]       paged KV cache shard
@@ -70,6 +71,14 @@ struct RingLayerArgs {
   const void* w_qkv = nullptr;      // [(H + 2 Hkv) D, hidden] bf16
   const void* b_qkv = nullptr;      // optional [(H + 2 Hkv) D] bias
   int hidden = 0;
+  // overlapped ring (context-parallel prefill, tile_src set): PushLayer writes only this rank's
+  // own staging buffer, and AttendLayer's attention kernel pushes the rows to the peers itself
+  // and waits per KV tile. Unset: serial ring (every row pushed and waited for before the
+  // attention launch), which continuation segments (existing_n > 0) always use.
+  const unsigned long long* tile_src = nullptr;  // [ceil(L / 128)] bitmask of ranks per tile
+  const int* push_tiles = nullptr;  // [n_push][3] (tile, first, end) rows of `pos` per own tile
+  int n_push = 0;
+  const int* pair_start = nullptr;  // [ceil(ceil(T / 128) / 2)] first kv tile per q-tile pair
 };
 
 class DomainRuntime {
@@ -93,6 +102,14 @@ class DomainRuntime {
   Status RunRingAttentionLayer(const RingLayerArgs& a, cudaStream_t stream);
   Status PushLayer(const RingLayerArgs& a, cudaStream_t stream);
   Status AttendLayer(const RingLayerArgs& a, cudaStream_t stream);
+  // Marks this rank's own tiles `push_tiles[k][0]` of the layer step `epoch` as present on every
+  // rank (tile flags), for rows already stored everywhere by a serial push (tests emulating
+  // several ranks on one GPU, where no kernel may wait on another launch).
+  Status PublishTiles(const int* push_tiles, int n_push, uint64_t epoch, cudaStream_t stream);
+  // First token of a prefill: rank `src` stores the int64 at `tok` into every rank's token slot
+  // (value, then a release of `epoch`); every other rank waits (bounded) for `epoch` in its own
+  // slot and copies the value into `tok`. All on the device, no host round trip.
+  Status BroadcastToken(long long* tok, int src, uint64_t epoch, cudaStream_t stream);
   Status Shutdown();
 
   // Reads and clears the device status words (synchronises the given stream first).
@@ -103,6 +120,9 @@ class DomainRuntime {
   uint8_t* base() const { return base_; }
   size_t region_bytes() const { return region_bytes_; }
   unsigned long long* flags() const { return reinterpret_cast<unsigned long long*>(base_ + off_flags_); }
+  unsigned long long* tile_flags(int parity) const {
+    return reinterpret_cast<unsigned long long*>(base_ + off_tflags_ + size_t(parity) * tflag_parity_bytes_);
+  }
   float* xslot() const { return reinterpret_cast<float*>(base_ + off_xslot_); }
   void* stage(int parity) const { return base_ + off_stage_ + size_t(parity) * stage_parity_bytes_; }
   void* arena() const { return base_ + off_arena_; }
@@ -126,7 +146,8 @@ class DomainRuntime {
   RuntimeConfig cfg_{};
   uint8_t* base_ = nullptr;
   size_t region_bytes_ = 0;
-  size_t off_flags_ = 0, off_xslot_ = 0, off_stage_ = 0, off_arena_ = 0;
+  size_t off_flags_ = 0, off_tflags_ = 0, off_xslot_ = 0, off_stage_ = 0, off_arena_ = 0;
+  size_t tflag_parity_bytes_ = 0;
   size_t xslot_bytes_ = 0, stage_parity_bytes_ = 0, arena_bytes_ = 0;
   int* status_ = nullptr;            // kStatusWords int32
   unsigned int* counters_ = nullptr; // 64 uint32 (last-CTA-done counters)
@@ -135,6 +156,8 @@ class DomainRuntime {
   unsigned long long** kv_ready_tab_ = nullptr;
   unsigned long long** consumed_tab_ = nullptr;
   unsigned long long** dec_ready_tab_ = nullptr;
+  unsigned long long** tflag_tab_[2] = {nullptr, nullptr};
+  unsigned long long** token_tab_ = nullptr;
   float** xslot_tab_ = nullptr;
   std::vector<uint8_t*> peer_base_;
   std::vector<bool> peer_opened_ipc_;

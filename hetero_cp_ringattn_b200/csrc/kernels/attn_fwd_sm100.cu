@@ -9,14 +9,20 @@
 // launches, one CTA streams KV tiles through shared memory and keeps S, P and O in TMEM.
 //
 // KV operand: a position-ordered K/V staging buffer [Hkv, L, D] (row p holds the key of global
-// position p). In context-parallel runs every rank pushes its rows into every rank's staging
-// buffer over NVLink; the kernel's kv-tile order starts at `kv_start_tile` (this rank's own
-// chunk) and an optional per-tile ready-flag array lets the producer wait (bounded) for a tile.
+// position p). In context-parallel runs every rank's rows have to reach every rank's staging
+// buffer. Overlapped mode (the default; the reference's pipelined ring, ring.rs:1195-1339): the
+// projection writes only the local buffer and this kernel does the ring itself: warps 2 and 3
+// store this rank's rows into every peer's buffer over NVLink tile by tile and publish a flag
+// per (tile, source rank), while the q tiles start on the rank's own run of KV tiles (the
+// per-pair start tile) and the TMA producer waits (bounded) for the flags of each remote tile
+// just before loading it. The last CTA releases the staging parity to every rank. Serial mode
+// (the reference's HCP_DISABLE_OVERLAP=1, ring.rs:164-166): every row was pushed and waited for
+// before the launch, and the kernel only computes.
 //
 // CTA layout (one CTA per SM): two q tiles of 128 rows of one head share every K/V tile.
 //   warp 0      TMA producer (Q0, Q1 once; K/V tiles through a STAGES-deep ring)
 //   warp 1      MMA issuer: S_i = Q_i K^T (SS) and O += P V (TS: P read from TMEM)
-//   warp 2      TMEM allocator
+//   warp 2      TMEM allocator; with warp 3 the KV ring push (overlapped mode)
 //   warpgroups 1..  softmax streams (thread <-> row <-> TMEM lane): head_dim 128 has one stream
 //               per q tile (384 threads); head_dim 64 splits each tile's 128 keys into two
 //               64-column streams with their own running max, row sum and O (640 threads), so
@@ -71,12 +77,61 @@ struct KParams {
   int causal;
   int num_pairs;        // ceil(num_q_tiles / 2)
   int kv_start_tile;
-  const unsigned long long* kv_ready;  // optional [Hkv][num_kv_tiles] ready epochs
-  unsigned long long kv_epoch;
-  int num_kv_tiles_total;
+  RingArgs ring;        // in-kernel KV ring (ring.tile_src == nullptr: off)
   unsigned long long wait_budget_ns;
   int* status;
 };
+
+// Push of this rank's K/V rows to the peers (one warp; the calling warps take turns through the
+// work counter, so whichever CTAs are resident finish every item). An item is (own tile k, peer
+// d): wait (bounded) until d has released this staging parity (consumed[d] >= epoch - 2), copy
+// the rows of tile k from the local staging buffer to d's with 16-byte loads / peer stores (eight
+// in flight per lane), then publish tflags[d][tile][my_rank] = epoch with a system-scope release.
+// Items run tile-major from this rank's last tile down, each tile to every peer in rank order
+// starting after this rank, so all peers receive the tiles in the same order.
+template <int D>
+__device__ __forceinline__ void ring_push(const KParams& p, int lane) {
+  const RingArgs& g = p.ring;
+  const int peers = g.world - 1;
+  const int n_items = g.n_push * peers;
+  constexpr int dvec = D / 8;                 // 16-byte units of one head row
+  const int units = 2 * p.Hkv * dvec;         // units of one position (K and V, every KV head)
+  while (true) {
+    int item = 0;
+    if (lane == 0) item = int(atomicAdd(g.counters, 1u));
+    item = __shfl_sync(0xffffffffu, item, 0);
+    if (item >= n_items) break;
+    const int k = item / peers;
+    const int dst = (g.my_rank + 1 + item % peers) % g.world;
+    const int tile = g.push_tiles[3 * k], lo = g.push_tiles[3 * k + 1], hi = g.push_tiles[3 * k + 2];
+    int ok = 1;
+    if (lane == 0 && g.epoch > 2)
+      ok = wait_flag_geq_sys(g.consumed + dst, g.epoch - 2, p.wait_budget_ns, p.status, 214, dst);
+    if (!__shfl_sync(0xffffffffu, ok, 0)) break;
+    __nv_bfloat16* dstb = static_cast<__nv_bfloat16*>(g.stage_ptrs[dst]);
+    const int total = (hi - lo) * units;
+    for (int u0 = lane; u0 < total; u0 += 32 * 8) {
+      uint4 v[8];
+      long off[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int u = u0 + 32 * i;
+        off[i] = -1;
+        if (u < total) {
+          const int row = lo + u / units, rem = u % units;
+          off[i] = ((long)(rem / dvec) * g.stage_cap + p.q_pos[row]) * D + (rem % dvec) * 8;
+          v[i] = ld_nc_v4(g.own_stage + off[i]);
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        if (off[i] >= 0) *reinterpret_cast<uint4*>(dstb + off[i]) = v[i];
+    }
+    __threadfence_system();
+    __syncwarp();
+    if (lane == 0) st_release_sys(g.tflag_ptrs[dst] + (long)tile * g.world + g.my_rank, g.epoch);
+  }
+}
 
 // processing order: kv_start_tile .. n-1 ascending, then kv_start_tile-1 .. 0 descending
 __device__ __forceinline__ int kv_tile_at(int j, int n, int start) {
@@ -258,7 +313,8 @@ __global__ void __launch_bounds__(Cfg<D>::threads(HV), 1)
   const int kv_tiles_L = (p.L + BKV - 1) / BKV;
   int n_tiles = p.causal ? (qmax_all >= 0 ? qmax_all / BKV + 1 : 0) : kv_tiles_L;
   if (n_tiles > kv_tiles_L) n_tiles = kv_tiles_L;
-  const int start = p.kv_start_tile < n_tiles ? p.kv_start_tile : 0;
+  const int start0 = p.ring.pair_start != nullptr ? p.ring.pair_start[pair] : p.kv_start_tile;
+  const int start = (start0 >= 0 && start0 < n_tiles) ? start0 : 0;
   const bool tile1_live = (row0 + BQ) < p.T;
 
   // register split: warpgroup 0 (TMA, MMA, TMEM allocator, idle warp) hands registers to the
@@ -283,9 +339,22 @@ __global__ void __launch_bounds__(Cfg<D>::threads(HV), 1)
         const int t = kv_tile_at(j, n_tiles, start);
         const int s = j % C::STAGES;
         const uint32_t ph = (j / C::STAGES) & 1;
-        if (p.kv_ready != nullptr) {
-          const unsigned long long* f = p.kv_ready + (long)kv_head * p.num_kv_tiles_total + t;
-          if (!wait_flag_geq_gpu(f, p.kv_epoch, p.wait_budget_ns, p.status, 210, t)) break;
+        if (p.ring.tile_src != nullptr) {
+          // remote rows of this tile: wait (bounded) for every other source rank's flag, then
+          // order what the flags made visible before the TMA (async proxy) reads it
+          unsigned long long m = p.ring.tile_src[t] & ~(1ull << p.ring.my_rank);
+          bool arrived = true;
+          while (m != 0ull) {
+            const int src = __ffsll((long long)m) - 1;
+            m &= m - 1ull;
+            if (!wait_flag_geq_sys(p.ring.tile_flags + (long)t * p.ring.world + src, p.ring.epoch,
+                                   p.wait_budget_ns, p.status, 210, t)) {
+              arrived = false;
+              break;
+            }
+          }
+          if (!arrived) break;
+          fence_proxy_async_global();
         }
         if (!mbar_wait(&k_empty[s], ph ^ 1, p.status, 201)) break;
         mbar_arrive_expect_tx(&k_full[s], C::KV_BYTES);
@@ -375,6 +444,9 @@ __global__ void __launch_bounds__(Cfg<D>::threads(HV), 1)
         }
       }
     }
+  } else if (p.ring.n_push > 0) {
+    // ------------------------------------------------------------------ KV ring push (warps 2, 3)
+    ring_push<D>(p, int(threadIdx.x % 32));
   }
   } else {
     reg_alloc<C::sm_regs(HV)>();
@@ -473,6 +545,18 @@ __global__ void __launch_bounds__(Cfg<D>::threads(HV), 1)
     tc_fence_after();
     tmem_dealloc(tmem_base, C::TMEM_COLS);
   }
+  if (p.ring.consumed_ptrs != nullptr && threadIdx.x == 0) {
+    // last CTA: every CTA's reads of this staging parity and pushes are done; tell every rank
+    // it may overwrite the parity (layer step epoch + 2) and reset the counters for the next step
+    __threadfence_system();
+    const unsigned prev = atomicAdd(p.ring.counters + 1, 1u);
+    if (prev == gridDim.x - 1) {
+      __threadfence_system();
+      for (int r = 0; r < p.ring.world; ++r) st_release_sys(p.ring.consumed_ptrs[r], p.ring.epoch);
+      p.ring.counters[0] = 0u;
+      p.ring.counters[1] = 0u;
+    }
+  }
 }
 
 template <int D, int POLY, int HV>
@@ -568,9 +652,19 @@ const char* attn_fwd(const AttnArgs& a, cudaStream_t stream) {
   const int num_q_tiles = (a.T + BQ - 1) / BQ;
   p.num_pairs = (num_q_tiles + QT - 1) / QT;
   p.kv_start_tile = a.kv_start_tile;
-  p.kv_ready = a.kv_ready;
-  p.kv_epoch = a.kv_epoch;
-  p.num_kv_tiles_total = (a.L + BKV - 1) / BKV;
+  p.ring = a.ring;
+  if (p.ring.tile_src != nullptr) {
+    if (p.ring.world < 2 || p.ring.world > 64 || p.ring.my_rank < 0 || p.ring.my_rank >= p.ring.world)
+      return "attn: ring needs 2 to 64 ranks";
+    if (p.ring.tile_flags == nullptr || p.ring.consumed_ptrs == nullptr || p.ring.counters == nullptr)
+      return "attn: ring flags / counters missing";
+    if (p.ring.n_push > 0 &&
+        (p.ring.push_tiles == nullptr || p.ring.own_stage == nullptr || p.ring.stage_ptrs == nullptr ||
+         p.ring.tflag_ptrs == nullptr || p.ring.consumed == nullptr || p.ring.stage_cap < a.L))
+      return "attn: ring push arguments missing";
+  } else if (p.ring.n_push > 0 || p.ring.consumed_ptrs != nullptr) {
+    return "attn: ring push / consumed signal need the tile sources";
+  }
   p.wait_budget_ns = a.wait_budget_ns;
   p.status = a.status;
   cudaError_t e = a.D == 64 ? launch_d<64>(tq, tk, tv, p, stream) : launch_d<128>(tq, tk, tv, p, stream);

@@ -126,6 +126,20 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* s
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
+// Orders global-memory data this thread has observed through the generic proxy (e.g. rows a
+// peer stored, made visible by an acquire of its flag) before later async-proxy reads (TMA).
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+// 16-byte global load through the non-coherent path (data no kernel in flight writes).
+__device__ __forceinline__ uint4 ld_nc_v4(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
 
 // ------------------------------------------------------------------------------- dependent launch
 // Programmatic dependent launch: a kernel launched with the programmatic-serialization attribute

@@ -203,6 +203,36 @@ __global__ void signal_kernel(unsigned long long* const* ptrs, int n, unsigned l
   if (r < n) st_release_sys(ptrs[r], epoch);
 }
 
+// Tile flags of rows already present on every rank (see DomainRuntime::PublishTiles).
+__global__ void publish_tiles_kernel(const int* push_tiles, int n_push,
+                                     unsigned long long* const* tflag_ptrs, int world, int my_rank,
+                                     unsigned long long epoch) {
+  __threadfence_system();
+  for (int i = threadIdx.x; i < n_push * world; i += blockDim.x) {
+    const int k = i / world, r = i % world;
+    st_release_sys(tflag_ptrs[r] + (long)push_tiles[3 * k] * world + my_rank, epoch);
+  }
+}
+
+// First-token broadcast from the rank that holds the last prompt position (one thread).
+__global__ void token_bcast_kernel(long long* tok, unsigned long long* const* slots,
+                                   const unsigned long long* own_slot, int world, int is_src,
+                                   unsigned long long epoch, unsigned long long budget_ns,
+                                   int* status) {
+  if (threadIdx.x != 0) return;
+  const int par = int(epoch & 1ull);
+  if (is_src) {
+    const unsigned long long v = static_cast<unsigned long long>(*tok);
+    for (int r = 0; r < world; ++r) {
+      unsigned long long* sl = slots[r] + 2 * par;
+      *reinterpret_cast<volatile unsigned long long*>(sl) = v;
+      st_release_sys(sl + 1, epoch);   // orders the value store before the epoch
+    }
+  } else if (wait_flag_geq_sys(own_slot + 2 * par + 1, epoch, budget_ns, status, 323, 0)) {
+    *tok = static_cast<long long>(*reinterpret_cast<const volatile unsigned long long*>(own_slot + 2 * par));
+  }
+}
+
 // ----------------------------------------------------------------------------- decode QKV post
 // One CTA per request row b. qkv [B, (H+2Hkv)D] fp32 (GEMV output incl. bias). RoPE at pos[b],
 // q -> q_out [B,H,D] bf16, and on the owner rank k/v -> arena slot `slot[b]` (owner[b] != 0).
@@ -307,6 +337,22 @@ const char* signal_peers(unsigned long long* const* ptrs, int n, unsigned long l
   if (n > 64) return "signal: too many ranks";
   signal_kernel<<<1, 64, 0, s>>>(ptrs, n, epoch);
   return cudaGetLastError() == cudaSuccess ? nullptr : "signal: launch failed";
+}
+
+const char* publish_tiles(const int* push_tiles, int n_push, unsigned long long* const* tflag_ptrs,
+                          int world, int my_rank, unsigned long long epoch, cudaStream_t s) {
+  if (n_push == 0) return nullptr;
+  publish_tiles_kernel<<<1, 256, 0, s>>>(push_tiles, n_push, tflag_ptrs, world, my_rank, epoch);
+  return cudaGetLastError() == cudaSuccess ? nullptr : "publish_tiles: launch failed";
+}
+
+const char* token_bcast(long long* tok, unsigned long long* const* slots,
+                        const unsigned long long* own_slot, int world, bool is_src,
+                        unsigned long long epoch, unsigned long long budget_ns, int* status,
+                        cudaStream_t s) {
+  token_bcast_kernel<<<1, 32, 0, s>>>(tok, slots, own_slot, world, is_src ? 1 : 0, epoch,
+                                       budget_ns, status);
+  return cudaGetLastError() == cudaSuccess ? nullptr : "token_bcast: launch failed";
 }
 
 const char* qkv_decode(const QkvDecodeArgs& a, cudaStream_t s) {

@@ -16,7 +16,14 @@
 //     [64, 128)  prefill consumed[dst]     epoch when `dst` finished reading a layer
 //     [128, 192) decode dec_ready[src]     epoch when `src` stored its (O, LSE) partial
 //     [192]      decode step epoch counter (advanced on device once per decode step)
+//     [200, 204) first-token broadcast: value / epoch pairs of two parities
 //     [256, ...) counters for last-CTA-done signalling (uint32 pairs)
+//
+// Tile flags (per rank, after the flag region, exported with it): uint64
+//     tflags[2 (parity)][tiles = ceil(Lcap / 128)][world]
+// tflags[p][t][src] = epoch once `src` has stored all of its rows of KV tile t (positions
+// [128 t, 128 t + 128)) of the layer step `epoch` into this rank's staging parity p. The
+// overlapped ring attention waits on exactly the (tile, src) pairs it reads.
 #pragma once
 
 #include <stdint.h>
@@ -28,6 +35,8 @@ constexpr int kFlagKvReady = 0;
 constexpr int kFlagConsumed = 64;
 constexpr int kFlagDecReady = 128;
 constexpr int kFlagDecEpoch = 192;
+constexpr int kFlagToken = 200;      // [value, epoch] x 2 parities
+constexpr int kRingTile = 128;       // KV tile (positions) of the tile flags and the attention
 constexpr int kFlagCounters = 256;   // uint32 counters start here (as uint64 index)
 constexpr int kFlagWords = 1024;     // total uint64 words in the flag region
 

@@ -50,6 +50,39 @@ from ..utils.perf import PerfLog, peak_bf16_tflops
 from .weights import PreparedWeights
 
 
+def ring_plan(positions: Sequence[np.ndarray], rank: int, L: int, tile: int = 128,
+              pair_rows: int = 256):
+    """Host plan of the overlapped in-kernel ring for one request (the same for every layer).
+
+    positions[r] are rank r's global prompt positions (ascending, any layout). Returns
+      tile_src   int64 [ceil(L / tile)]: bit r set when rank r holds rows of KV tile t (the
+                 attention waits for the flags of exactly these (tile, rank) pairs);
+      push_tiles int32 [n, 3]: this rank's own tiles as (tile, first row, end row) ranges of its
+                 positions, last tile first (the order in which its kernel pushes them);
+      pair_start int32 [q-tile pairs]: per pair of 128-row q tiles, the KV tile where the pair's
+                 contiguous run of positions starts, so each CTA begins with its own rows.
+    """
+    ntiles = -(-int(L) // tile)
+    src = np.zeros(ntiles, dtype=np.uint64)
+    for r, p in enumerate(positions):
+        if len(p):
+            src[np.unique(np.asarray(p, dtype=np.int64) // tile)] |= np.uint64(1) << np.uint64(r)
+    own = np.asarray(positions[rank], dtype=np.int64)
+    if len(own) == 0:
+        return src.view(np.int64), np.zeros((0, 3), dtype=np.int32), np.zeros(0, dtype=np.int32)
+    if np.any(np.diff(own) <= 0):
+        raise RingError("ring plan: a rank's positions must be strictly increasing")
+    tiles, lo = np.unique(own // tile, return_index=True)
+    hi = np.r_[lo[1:], len(own)]
+    push = np.stack([tiles, lo, hi], 1)[::-1].astype(np.int32)
+    npairs = -(-(-(-len(own) // 128)) // 2)
+    first = np.arange(npairs, dtype=np.int64) * pair_rows
+    runs = np.r_[0, np.nonzero(np.diff(own) != 1)[0] + 1]
+    run_of = runs[np.searchsorted(runs, first, side="right") - 1]
+    pair_start = (own[run_of] // tile).astype(np.int32)
+    return src.view(np.int64), np.ascontiguousarray(push), pair_start
+
+
 @dataclasses.dataclass
 class RequestState:
     req_id: int
@@ -67,6 +100,7 @@ class RequestState:
                                      # shared: the row lives on this rank only (prompt / segment /
                                      # owned growth); False: a replicated legacy-decode row
     keep_kv: bool = False
+    ring: Optional[tuple] = None     # device tensors of ring_plan (overlapped CUDA ring only)
 
 
 class LlamaCPEngine:
@@ -110,10 +144,19 @@ class LlamaCPEngine:
         self.scale = 1.0 / math.sqrt(self.D)
         self.use_graphs = use_graphs and self.cuda
         self.perf = perf_log or PerfLog.from_env(self.env)
-        # fused QKV projection + K/V push: measured faster on one rank (+2% prefill), slower at
-        # CP=8 (the GEMM epilogue's 4 warps per SM then carry every peer store); an explicit
-        # HCP_FUSED_QKV overrides
-        self.fused_qkv = self.env.fused_qkv if self.env.fused_qkv is not None else (world == 1)
+        # overlapped ring (default with several ranks): the attention kernel pushes this rank's
+        # K/V rows to the peers and waits per tile; HCP_DISABLE_OVERLAP=1 selects the serial ring
+        # (push everything, wait for every rank, then attend), as the reference's switch does
+        self.overlap = world > 1 and not self.env.disable_overlap
+        # fused QKV projection (RoPE + Q / arena / staging writes in the GEMM epilogue): faster on
+        # one rank (+2% prefill) and in the overlapped ring, where the epilogue writes only the
+        # local staging buffer; the serial ring keeps the separate push kernel, which spreads the
+        # peer stores over every SM's threads instead of the epilogue's 4 warps (1.05M vs 1.22M
+        # prefill tok/s at CP=8). An explicit HCP_FUSED_QKV overrides.
+        self.fused_qkv = (self.env.fused_qkv if self.env.fused_qkv is not None
+                          else (world == 1 or self.overlap))
+        self.fused_qkv_serial = self.env.fused_qkv if self.env.fused_qkv is not None else world == 1
+        self.tok_epoch = 0
         if kv_pages is None:
             kv_pages = -(-self.max_context // self.page_size) + \
                 max_batch * -(-decode_reserve // self.page_size) + 2
@@ -217,6 +260,9 @@ class LlamaCPEngine:
         if self.cuda:
             st.kv = self.kv.reserve(req_id, T, T + growth, my_pos)
             st.kv.pt_device = torch.tensor(st.kv.pages, dtype=torch.int32, device=self.device)
+            if self.overlap:
+                plan = ring_plan(positions, self.rank, Lp)
+                st.ring = tuple(torch.from_numpy(x).to(self.device) for x in plan)
             ids_local = prompt_ids.to(self.device, non_blocking=True)[torch.from_numpy(my_pos).to(self.device)]
             tok, logits = self._prefill_cuda(st, ids_local.int(), Lp, return_logits)
         else:
@@ -237,6 +283,10 @@ class LlamaCPEngine:
         q_buf = torch.empty(T, self.H, self.D, dtype=torch.bfloat16, device=dev)
         o_buf = torch.empty_like(q_buf)
         start_tile = int(st.positions[0]) // 128 if st.strategy is RingStrategy.VANILLA else 0
+        ring = {}
+        if st.ring is not None:
+            ring = dict(tile_src=st.ring[0], push_tiles=st.ring[1], pair_start=st.ring[2])
+        fused = self.fused_qkv if (self.world == 1 or st.ring is not None) else self.fused_qkv_serial
         trace = self.perf.enabled
         nvtx = self.env.nvtx
         for li, lw in enumerate(w.layers):
@@ -251,19 +301,24 @@ class LlamaCPEngine:
                     self.scale, True, q_buf, o_buf, None, self.prefill_epoch)
             if trace:
                 ev[1].record()
-            if self.fused_qkv:
-                # one kernel: QKV GEMM whose epilogue rotates, writes Q and pushes K/V to every rank
-                self.rt.push_layer_fused(xn, lw.wqkv, lw.bqkv, *tail)
+            if fused:
+                # one kernel: QKV GEMM whose epilogue rotates, writes Q and writes K/V (into every
+                # rank's staging buffer in the serial ring, into this rank's own otherwise)
+                self.rt.push_layer_fused(xn, lw.wqkv, lw.bqkv, *tail, **ring)
             else:
                 qkv = K.gemm(xn, lw.wqkv, "bias" if lw.bqkv is not None else "store", bias=lw.bqkv)
-                self.rt.push_layer(qkv, *tail)
+                self.rt.push_layer(qkv, *tail, **ring)
                 del qkv
             if trace:
                 ev[2].record()
-            self.rt.attend_layer(xn, *tail)
+            # overlapped ring: this one kernel also pushes the rank's rows to the peers
+            self.rt.attend_layer(xn, *tail, **ring)
             if trace:
                 ev[3].record()
-            launches.count(2 + (3 if self.world > 1 else 0) - (1 if self.world > 1 and self.prefill_epoch <= 2 else 0))
+            if self.world == 1 or self.overlap:
+                launches.count(2)
+            else:   # + wait for released parity (after the first two steps), wait for pushes, signal
+                launches.count(5 - (1 if self.prefill_epoch <= 2 else 0))
             K.gemm(o_buf.view(T, self.H * self.D), lw.wo, "residual", residual=x)
             K.rmsnorm(x, lw.post_norm, self.cfg.rms_norm_eps, out=xn)
             g = K.gemm(xn, lw.wgu, "swiglu")
@@ -285,15 +340,25 @@ class LlamaCPEngine:
         sent = T * row_bytes * (self.world - 1)
         recv = (Lp - T) * row_bytes
         attn_ms = ev[2].elapsed_time(ev[3])
+        proj_ms = ev[1].elapsed_time(ev[2])
         tflops = 4.0 * self.H * self.D * float(np.sum(st.positions + 1)) / max(attn_ms, 1e-6) / 1e9
+        overlap = self.overlap and st.ring is not None
+        # overlapped ring: the push runs inside the attention kernel, so the attention interval
+        # holds local compute, peer compute and the push, and the NVLink rate is averaged over it;
+        # serial ring: the push (and its waits) sit between the projection and the attention
+        span_ms = attn_ms if overlap else proj_ms
         self.perf.emit("ring_attention", domain=self.rank, layer=layer, request=st.req_id,
                        total_ms=ev[0].elapsed_time(ev[4]), qkv_ms=ev[0].elapsed_time(ev[1]),
-                       send_ms=ev[1].elapsed_time(ev[2]), local_compute_ms=attn_ms,
-                       peer_compute_ms=0.0, recv_ms=0.0, forward_ms=0.0, flush_ms=0.0,
+                       send_ms=proj_ms, local_compute_ms=attn_ms,
+                       peer_compute_ms=None if (overlap or self.world == 1) else 0.0,
+                       recv_ms=0.0, forward_ms=0.0, flush_ms=0.0,
                        mlp_ms=ev[3].elapsed_time(ev[4]), kv_sent_bytes=sent, kv_recv_bytes=recv,
                        wire_sent_bytes=sent, wire_recv_bytes=recv, micro_blocks=-(-Lp // 128),
-                       num_domains=self.world, seq_len=T, overlap=True,
-                       nvlink_gbps=sent / max(ev[1].elapsed_time(ev[2]), 1e-6) / 1e6,
+                       num_domains=self.world, seq_len=T, overlap=overlap,
+                       ring_mode=("single" if self.world == 1 else
+                                  "overlap_in_kernel" if overlap else "serial"),
+                       nvlink_gbps=sent / max(span_ms, 1e-6) / 1e6,
+                       nvlink_span="attention" if overlap else "projection+push",
                        attn_tflops=tflops, roofline_frac=tflops / peak_bf16_tflops())
 
     def _first_token_cuda(self, st: RequestState, x: torch.Tensor, return_logits: bool):
@@ -310,7 +375,11 @@ class LlamaCPEngine:
             native().argmax_finalize(am, None, tok)
             launches.count()
         if self.world > 1:
-            dist.broadcast(tok, src=st.owner_of_last, group=self.group)
+            # the token goes from the owner's memory to every rank's token slot over NVLink (a
+            # bounded device wait on the others): no host round trip inside the TTFT
+            self.tok_epoch += 1
+            self.rt.broadcast_token(tok, st.owner_of_last, self.tok_epoch)
+            launches.count()
             if return_logits:
                 if logits is None:
                     logits = torch.empty(1, self.cfg.vocab_size, dtype=torch.float32, device=dev)
@@ -612,7 +681,7 @@ class LlamaCPEngine:
                     True, q_buf, o_buf, None, self.prefill_epoch, existing)
             if T:
                 K.rmsnorm(x, lw.in_norm, self.cfg.rms_norm_eps, out=xn)
-            if T and self.fused_qkv:
+            if T and self.fused_qkv_serial:   # continuation segments use the serial ring
                 self.rt.push_layer_fused(xn, lw.wqkv, lw.bqkv, *tail)
                 self.rt.attend_layer(xn, *tail)
             else:

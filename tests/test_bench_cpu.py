@@ -52,3 +52,18 @@ def test_host_bench_reports_native_and_json_costs(capsys):
     out = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
     f = out["prefill_frame_32k"]
     assert f["native_ms"] > 0 and f["json_ms"] > 0 and f["bytes"] > 32768 * 8
+
+
+def test_bench_secondary_configs_per_n():
+    """Besides the headline, every N also measures BASELINE config #3 (the uneven
+    5:5:5:5:2:2:1:1 split at 8 ranks, equal chunks otherwise) and N=8 config #4 with batch-1 and
+    batch-8 decode; the CP output check runs by default."""
+    import bench
+    assert [c[0] for c in bench.secondary_configs(1)] == ["#3"]
+    assert [c[0] for c in bench.secondary_configs(8)] == ["#3", "#4"]
+    c3 = bench.secondary_configs(8)[0]
+    assert c3[1] == "qwen2.5-3b-64k" and c3[2] == "5:5:5:5:2:2:1:1"
+    c4 = bench.secondary_configs(8)[1]
+    assert c4[1] == "llama-3-8b-128k" and c4[3] == [1, 8]
+    a = bench.parse([])
+    assert not a.no_check and not a.no_secondary

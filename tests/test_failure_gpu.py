@@ -29,3 +29,41 @@ def test_device_wait_times_out_into_status(dev):
     x = torch.ones(1024, device=dev)
     assert float(x.sum()) == 1024.0
     rt.shutdown()
+
+
+def test_overlapped_ring_missing_peer_times_out_into_status(dev):
+    """The overlapped ring's per-tile wait on a peer that never publishes its tiles runs out after
+    the runtime's budget (100 ms here), reports a peer timeout at the producer's wait site and the
+    kernel returns; the runtime stays usable."""
+    import math
+    from hetero_cp_ringattn_b200.models.llama import ring_plan
+    from hetero_cp_ringattn_b200.ops import reference as ref
+    from hetero_cp_ringattn_b200.parallel.strategy import layout_positions
+    H, HKV, D, PAGE = 8, 2, 64, 256
+    rts = [native().Runtime(r, 2, dev.index or 0, 1, 8, PAGE, HKV, D, H, 1024, 1, 100) for r in range(2)]
+    for rt in rts:
+        rt.open_peers_local(rts)
+    chunks = [256, 256]
+    L = sum(chunks)
+    positions = layout_positions(chunks, "zigzag")
+    src, push, pair = ring_plan(positions, 0, L)
+    plan = dict(tile_src=torch.from_numpy(src).to(dev), push_tiles=torch.from_numpy(push).to(dev),
+                pair_start=torch.from_numpy(pair).to(dev))
+    p = torch.as_tensor(positions[0], device=dev).int()
+    cos, sin = ref.rope_cos_sin(torch.arange(2048, device=dev), D, 10000.0)
+    qkv = torch.randn(len(p), (H + 2 * HKV) * D, device=dev).bfloat16()
+    q_out = torch.empty(len(p), H, D, device=dev, dtype=torch.bfloat16)
+    o_out = torch.empty_like(q_out)
+    args = (qkv, p, cos.contiguous(), sin.contiguous(), 0, torch.arange(0, 2, dtype=torch.int32, device=dev),
+            0, L, 0, 1.0 / math.sqrt(D), True, q_out, o_out, None, 1)
+    t0 = time.time()
+    rts[0].push_layer(*args, **plan)
+    rts[0].attend_layer(*args, **plan)     # rank 1 never pushes or publishes its tiles
+    torch.cuda.synchronize(dev)
+    assert time.time() - t0 < 5.0
+    with pytest.raises(RuntimeError, match="code=17.*site 210"):
+        rts[0].check()
+    x = torch.ones(1024, device=dev)
+    assert float(x.sum()) == 1024.0
+    for rt in rts:
+        rt.shutdown()

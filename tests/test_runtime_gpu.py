@@ -280,3 +280,72 @@ def test_decode_attention_group_shapes(dev, h, hkv, d, n):
                                torch.arange(n, device=dev), causal=True)
     assert (out.view(h, d).float() - ro[0]).abs().max() < 2e-2
     rt.shutdown()
+
+
+def _plan(positions, rank, L, dev):
+    from hetero_cp_ringattn_b200.models.llama import ring_plan
+    src, push, pair = ring_plan([p.cpu().numpy() for p in positions], rank, L)
+    return dict(tile_src=torch.from_numpy(src).to(dev), push_tiles=torch.from_numpy(push).to(dev),
+                pair_start=torch.from_numpy(pair).to(dev))
+
+
+def run_overlap_ranks(dev, chunks, strategy, epoch, rts=None, layer=0):
+    """The overlapped ring (the attention kernel pushes this rank's rows to the peers and waits
+    per KV tile) with ranks emulated on one GPU. No launch may wait on a later one, so ranks
+    1..n-1 first store their rows everywhere with the serial push and mark their tiles present;
+    rank 0 then runs the overlapped path (local projection, attention that pushes its rows to the
+    others and waits per tile); then ranks 1..n-1 run the overlapped attention, whose waits rank
+    0's finished kernel satisfied. Rank 0's rows reach the other ranks only through its kernel."""
+    L = sum(chunks)
+    n = len(chunks)
+    torch.manual_seed(100 + epoch)
+    qkv_all = (torch.randn(L, (H + 2 * HKV) * D, device=dev) * 0.5).bfloat16()
+    pos_all = torch.arange(L, device=dev)
+    cos, sin = tables(dev)
+    positions = [torch.as_tensor(p, device=dev) for p in layout_positions(chunks, strategy)]
+    if rts is None:
+        rts = [make_rt(r, n) for r in range(n)]
+        for rt in rts:
+            rt.open_peers_local(rts)
+    args, plans, outs = [], [], []
+    for r in range(n):
+        p = positions[r]
+        qkv = qkv_all[p].contiguous()
+        pt = torch.arange(r * 4, r * 4 + 4, dtype=torch.int32, device=dev)
+        q_out = torch.empty(len(p), H, D, device=dev, dtype=torch.bfloat16)
+        o_out = torch.empty_like(q_out)
+        lse = torch.empty(H, len(p), device=dev, dtype=torch.float32)
+        args.append((qkv, p.int().contiguous(), cos, sin, layer, pt, 0, L, 0, 1.0 / math.sqrt(D),
+                     True, q_out, o_out, lse, epoch))
+        plans.append(_plan(positions, r, L, dev))
+        outs.append((o_out, lse))
+    for r in range(1, n):
+        rts[r].push_layer(*args[r])                              # serial push to every rank
+        rts[r].publish_tiles(plans[r]["push_tiles"], epoch)
+    rts[0].push_layer(*args[0], **plans[0])                      # local rows only
+    rts[0].attend_layer(*args[0], **plans[0])                    # pushes rank 0's rows, waits
+    for r in range(1, n):
+        rts[r].attend_layer(*args[r], **plans[r])
+    torch.cuda.synchronize()
+    for rt in rts:
+        rt.check()
+    _, _, _, o_ref, lse_ref = reference_layer(qkv_all, pos_all)
+    for r in range(n):
+        p = positions[r]
+        o, lse = outs[r]
+        assert (o.float() - o_ref[p]).abs().max() < 2e-2, f"rank {r}"
+        assert (lse - lse_ref[:, p]).abs().max() < 2e-2, f"rank {r}"
+    return rts
+
+
+@pytest.mark.parametrize("strategy", ["vanilla", "zigzag", "striped"])
+def test_overlapped_ring_emulated_two_ranks(dev, strategy):
+    run_overlap_ranks(dev, [640, 300], strategy, epoch=1)
+
+
+def test_overlapped_ring_uneven_three_ranks_several_steps(dev):
+    """5:5:1-like uneven chunks, several layer steps on the same runtimes (both staging parities,
+    the consumed handshake of step epoch - 2, counters reset by the last CTA)."""
+    rts = run_overlap_ranks(dev, [500, 500, 100], "vanilla", epoch=1)
+    for epoch, strategy in [(2, "zigzag"), (3, "vanilla"), (4, "striped"), (5, "zigzag")]:
+        run_overlap_ranks(dev, [500, 500, 100], strategy, epoch=epoch, rts=rts, layer=epoch % 2)
