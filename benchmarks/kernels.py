@@ -272,7 +272,7 @@ def bench_ring(args, pk):
 
     def layer():
         epoch[0] += 1
-        a = (qkv, pos, cos, sin, 0, pt, 0, L, 0, scale, True, q_buf, o_buf, None, epoch[0])
+        a = (qkv, pos, cos, sin, 0, pt, 0, L, scale, True, q_buf, o_buf, None, epoch[0])
         rt.push_layer(*a)
         rt.attend_layer(*a)
 

@@ -82,7 +82,7 @@ void gemm(torch::Tensor A, torch::Tensor B, torch::Tensor C, int64_t epi,
 
 void attn_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o,
               c10::optional<torch::Tensor> lse, torch::Tensor q_pos, int64_t L,
-              int64_t kv_head_stride, double scale, bool causal, int64_t kv_start_tile,
+              int64_t kv_head_stride, double scale, bool causal,
               c10::optional<torch::Tensor> status) {
   check_cuda_bf16(q, "q");
   check_cuda_bf16(k, "k");
@@ -115,7 +115,6 @@ void attn_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o
   TORCH_CHECK(kv_head_stride >= L * a.D, "kv_head_stride too small");
   a.scale = float(scale);
   a.causal = causal ? 1 : 0;
-  a.kv_start_tile = int(kv_start_tile);
   a.status = ptr_or_null<int>(status);
   HCP_CHECK_OK(hcp::attn::attn_fwd(a, cur_stream()));
 }
@@ -208,12 +207,11 @@ int64_t decode_attn_ctas_per_sm(int64_t D, int64_t G) {
 // ----------------------------------------------------------------------------- runtime
 // The overlapped ring's per-request plan (built on the host once per request): tile_src int64
 // [ceil(L / 128)] bitmask of the ranks with rows in each KV tile, push_tiles int32 [n, 3] this
-// rank's own tiles as (tile, first, end) row ranges of `pos`, pair_start int32 first kv tile per
-// q-tile pair. No tile_src: the serial ring.
+// rank's own tiles as (tile, first, end) row ranges of `pos`. No tile_src: the serial ring.
 struct RingPlan {
-  c10::optional<torch::Tensor> tile_src, push_tiles, pair_start;
-  RingPlan(c10::optional<torch::Tensor> t, c10::optional<torch::Tensor> p, c10::optional<torch::Tensor> s)
-      : tile_src(std::move(t)), push_tiles(std::move(p)), pair_start(std::move(s)) {}
+  c10::optional<torch::Tensor> tile_src, push_tiles;
+  RingPlan(c10::optional<torch::Tensor> t, c10::optional<torch::Tensor> p)
+      : tile_src(std::move(t)), push_tiles(std::move(p)) {}
   void apply(hcp::RingLayerArgs& a, int world) const {
     if (!tile_src.has_value() || !tile_src->defined()) return;
     TORCH_CHECK(tile_src->is_cuda() && tile_src->scalar_type() == torch::kInt64 && tile_src->is_contiguous(),
@@ -226,12 +224,6 @@ struct RingPlan {
                   "push_tiles must be a contiguous CUDA int32 [n, 3] tensor");
       a.push_tiles = push_tiles->data_ptr<int>();
       a.n_push = int(push_tiles->size(0));
-    }
-    if (pair_start.has_value() && pair_start->defined() && pair_start->numel() > 0) {
-      TORCH_CHECK(pair_start->is_cuda() && pair_start->scalar_type() == torch::kInt32 && pair_start->is_contiguous(),
-                  "pair_start must be a contiguous CUDA int32 tensor");
-      TORCH_CHECK(pair_start->numel() >= ((a.T + 127) / 128 + 1) / 2, "pair_start needs one entry per q-tile pair");
-      a.pair_start = pair_start->data_ptr<int>();
     }
     (void)world;
   }
@@ -282,7 +274,7 @@ class PyRuntime {
   hcp::RingLayerArgs layer_args(torch::Tensor qkv, torch::Tensor pos, torch::Tensor cos_t,
                                 torch::Tensor sin_t, int64_t layer,
                                 c10::optional<torch::Tensor> page_table, int64_t slot_base,
-                                int64_t L, int64_t kv_start_tile, double scale, bool causal,
+                                int64_t L, double scale, bool causal,
                                 torch::Tensor q_out, torch::Tensor o_out,
                                 c10::optional<torch::Tensor> lse_out, int64_t epoch,
                                 c10::optional<torch::Tensor> existing_slot_pos, bool has_qkv,
@@ -315,8 +307,7 @@ class PyRuntime {
     }
     a.slot_base = int(slot_base);
     a.L = int(L);
-    a.kv_start_tile = int(kv_start_tile);
-    a.scale = float(scale);
+      a.scale = float(scale);
     a.causal = causal ? 1 : 0;
     a.q_out = q_out.data_ptr();
     a.o_out = o_out.data_ptr();
@@ -334,15 +325,14 @@ class PyRuntime {
 
   void push_layer(torch::Tensor qkv, torch::Tensor pos, torch::Tensor cos_t, torch::Tensor sin_t,
                   int64_t layer, c10::optional<torch::Tensor> page_table, int64_t slot_base,
-                  int64_t L, int64_t kv_start_tile, double scale, bool causal, torch::Tensor q_out,
+                  int64_t L, double scale, bool causal, torch::Tensor q_out,
                   torch::Tensor o_out, c10::optional<torch::Tensor> lse_out, int64_t epoch,
                   c10::optional<torch::Tensor> existing_slot_pos,
-                  c10::optional<torch::Tensor> tile_src, c10::optional<torch::Tensor> push_tiles,
-                  c10::optional<torch::Tensor> pair_start) {
+                  c10::optional<torch::Tensor> tile_src, c10::optional<torch::Tensor> push_tiles) {
     const c10::cuda::CUDAGuard g(qkv.device());
-    auto a = layer_args(qkv, pos, cos_t, sin_t, layer, page_table, slot_base, L, kv_start_tile,
+    auto a = layer_args(qkv, pos, cos_t, sin_t, layer, page_table, slot_base, L,
                         scale, causal, q_out, o_out, lse_out, epoch, existing_slot_pos, true,
-                        RingPlan(tile_src, push_tiles, pair_start));
+                        RingPlan(tile_src, push_tiles));
     auto st = rt_.PushLayer(a, cur_stream());
     TORCH_CHECK(st.ok(), "push_layer: ", st.ToString());
   }
@@ -352,19 +342,18 @@ class PyRuntime {
   void push_layer_fused(torch::Tensor x, torch::Tensor w_qkv, c10::optional<torch::Tensor> b_qkv,
                         torch::Tensor pos, torch::Tensor cos_t, torch::Tensor sin_t, int64_t layer,
                         c10::optional<torch::Tensor> page_table, int64_t slot_base, int64_t L,
-                        int64_t kv_start_tile, double scale, bool causal, torch::Tensor q_out,
+                        double scale, bool causal, torch::Tensor q_out,
                         torch::Tensor o_out, c10::optional<torch::Tensor> lse_out, int64_t epoch,
                         c10::optional<torch::Tensor> existing_slot_pos,
-                        c10::optional<torch::Tensor> tile_src, c10::optional<torch::Tensor> push_tiles,
-                        c10::optional<torch::Tensor> pair_start) {
+                        c10::optional<torch::Tensor> tile_src, c10::optional<torch::Tensor> push_tiles) {
     check_cuda_bf16(x, "x");
     check_cuda_bf16(w_qkv, "w_qkv");
     TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1 && w_qkv.is_contiguous() && x.size(1) == w_qkv.size(1),
                 "x [T, hidden] row-major and w_qkv [N, hidden] contiguous");
     const c10::cuda::CUDAGuard g(x.device());
-    auto a = layer_args(x, pos, cos_t, sin_t, layer, page_table, slot_base, L, kv_start_tile, scale,
+    auto a = layer_args(x, pos, cos_t, sin_t, layer, page_table, slot_base, L, scale,
                         causal, q_out, o_out, lse_out, epoch, existing_slot_pos, /*has_qkv=*/false,
-                        RingPlan(tile_src, push_tiles, pair_start));
+                        RingPlan(tile_src, push_tiles));
     a.x = x.data_ptr();
     a.ldx = x.stride(0);
     a.w_qkv = w_qkv.data_ptr();
@@ -381,16 +370,15 @@ class PyRuntime {
 
   void attend_layer(torch::Tensor qkv, torch::Tensor pos, torch::Tensor cos_t, torch::Tensor sin_t,
                     int64_t layer, c10::optional<torch::Tensor> page_table, int64_t slot_base,
-                    int64_t L, int64_t kv_start_tile, double scale, bool causal,
+                    int64_t L, double scale, bool causal,
                     torch::Tensor q_out, torch::Tensor o_out, c10::optional<torch::Tensor> lse_out,
                     int64_t epoch, c10::optional<torch::Tensor> existing_slot_pos,
-                    c10::optional<torch::Tensor> tile_src, c10::optional<torch::Tensor> push_tiles,
-                    c10::optional<torch::Tensor> pair_start) {
+                    c10::optional<torch::Tensor> tile_src, c10::optional<torch::Tensor> push_tiles) {
     // `qkv` only gives the row count here (the projection output or the layer input)
     const c10::cuda::CUDAGuard g(qkv.device());
-    auto a = layer_args(qkv, pos, cos_t, sin_t, layer, page_table, slot_base, L, kv_start_tile,
+    auto a = layer_args(qkv, pos, cos_t, sin_t, layer, page_table, slot_base, L,
                         scale, causal, q_out, o_out, lse_out, epoch, existing_slot_pos, false,
-                        RingPlan(tile_src, push_tiles, pair_start));
+                        RingPlan(tile_src, push_tiles));
     auto st = rt_.AttendLayer(a, cur_stream());
     TORCH_CHECK(st.ok(), "attend_layer: ", st.ToString());
   }
@@ -403,6 +391,18 @@ class PyRuntime {
     auto st = rt_.PublishTiles(push_tiles.data_ptr<int>(), int(push_tiles.size(0)), uint64_t(epoch),
                                cur_stream());
     TORCH_CHECK(st.ok(), "publish_tiles: ", st.ToString());
+  }
+
+  // Marks this rank's decode partials of rows [0, B) as present on every rank (group flags), for
+  // partials already stored by a decode_attn launch without the in-kernel combine: tests that
+  // emulate several ranks on one GPU, where no kernel may wait on another launch.
+  void publish_decode_groups(int64_t B, int64_t epoch) {
+    const auto& c = rt_.config();
+    TORCH_CHECK(B >= 1 && B <= c.max_batch, "rows out of range");
+    const c10::cuda::CUDAGuard g(c10::Device(c10::DeviceType::CUDA, c.device));
+    HCP_CHECK_OK(hcp::ew::publish_range(rt_.group_flag_table(), c.world,
+                                        long(c.rank) * c.max_batch * c.geom.hkv,
+                                        int(B) * c.geom.hkv, uint64_t(epoch), cur_stream()));
   }
 
   void broadcast_token(torch::Tensor tok, int64_t src, int64_t epoch) {
@@ -452,7 +452,8 @@ class PyRuntime {
   void decode_attn(torch::Tensor q, int64_t layer, torch::Tensor page_tables, torch::Tensor n_tokens,
                    double scale, int64_t splits, torch::Tensor part_o, torch::Tensor part_lse,
                    torch::Tensor counters, c10::optional<torch::Tensor> epoch_src,
-                   int64_t epoch_mul, int64_t epoch_add, c10::optional<torch::Tensor> final_out) {
+                   int64_t epoch_mul, int64_t epoch_add, c10::optional<torch::Tensor> final_out,
+                   c10::optional<torch::Tensor> combine_out) {
     check_cuda_bf16(q, "q");
     const c10::cuda::CUDAGuard g(q.device());
     const auto& c = rt_.config();
@@ -495,6 +496,17 @@ class PyRuntime {
       TORCH_CHECK(c.world == 1, "final_out: the exchange is skipped only on a single rank");
       TORCH_CHECK(final_out->numel() >= int64_t(a.B) * a.H * a.D, "final_out too small");
       a.final_out = reinterpret_cast<__nv_bfloat16*>(final_out->data_ptr());
+    }
+    if (combine_out.has_value() && combine_out->defined()) {
+      // several ranks: the exchange and the rank-order combine happen inside the kernel
+      check_cuda_bf16(*combine_out, "combine_out");
+      TORCH_CHECK(c.world > 1, "combine_out: the in-kernel combine is for several ranks");
+      TORCH_CHECK(combine_out->numel() >= int64_t(a.B) * a.H * a.D, "combine_out too small");
+      a.combine_out = reinterpret_cast<__nv_bfloat16*>(combine_out->data_ptr());
+      a.group_flag_ptrs = rt_.group_flag_table();
+      a.group_flags = rt_.group_flags();
+      a.group_stride = c.max_batch * c.geom.hkv;
+      a.budget_ns = c.peer_wait_budget_ns;
     }
     HCP_CHECK_OK(hcp::dec::decode_attn(a, cur_stream()));
   }
@@ -653,27 +665,28 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       .def("open_peers_local", &PyRuntime::open_peers_local)
       .def("push_layer", &PyRuntime::push_layer, py::arg("qkv"), py::arg("pos"), py::arg("cos_t"),
            py::arg("sin_t"), py::arg("layer"), py::arg("page_table"), py::arg("slot_base"), py::arg("L"),
-           py::arg("kv_start_tile"), py::arg("scale"), py::arg("causal"), py::arg("q_out"),
+           py::arg("scale"), py::arg("causal"), py::arg("q_out"),
            py::arg("o_out"), py::arg("lse_out"), py::arg("epoch"),
-           py::arg("existing_slot_pos") = py::none(), py::arg("tile_src") = py::none(), py::arg("push_tiles") = py::none(), py::arg("pair_start") = py::none())
+           py::arg("existing_slot_pos") = py::none(), py::arg("tile_src") = py::none(), py::arg("push_tiles") = py::none())
       .def("push_layer_fused", &PyRuntime::push_layer_fused, py::arg("x"), py::arg("w_qkv"),
            py::arg("b_qkv"), py::arg("pos"), py::arg("cos_t"), py::arg("sin_t"), py::arg("layer"),
-           py::arg("page_table"), py::arg("slot_base"), py::arg("L"), py::arg("kv_start_tile"),
+           py::arg("page_table"), py::arg("slot_base"), py::arg("L"),
            py::arg("scale"), py::arg("causal"), py::arg("q_out"), py::arg("o_out"),
            py::arg("lse_out"), py::arg("epoch"),
-           py::arg("existing_slot_pos") = py::none(), py::arg("tile_src") = py::none(), py::arg("push_tiles") = py::none(), py::arg("pair_start") = py::none())
+           py::arg("existing_slot_pos") = py::none(), py::arg("tile_src") = py::none(), py::arg("push_tiles") = py::none())
       .def("attend_layer", &PyRuntime::attend_layer, py::arg("qkv"), py::arg("pos"), py::arg("cos_t"),
            py::arg("sin_t"), py::arg("layer"), py::arg("page_table"), py::arg("slot_base"), py::arg("L"),
-           py::arg("kv_start_tile"), py::arg("scale"), py::arg("causal"), py::arg("q_out"),
+           py::arg("scale"), py::arg("causal"), py::arg("q_out"),
            py::arg("o_out"), py::arg("lse_out"), py::arg("epoch"),
-           py::arg("existing_slot_pos") = py::none(), py::arg("tile_src") = py::none(), py::arg("push_tiles") = py::none(), py::arg("pair_start") = py::none())
+           py::arg("existing_slot_pos") = py::none(), py::arg("tile_src") = py::none(), py::arg("push_tiles") = py::none())
       .def("publish_tiles", &PyRuntime::publish_tiles, py::arg("push_tiles"), py::arg("epoch"))
       .def("broadcast_token", &PyRuntime::broadcast_token, py::arg("tok"), py::arg("src"), py::arg("epoch"))
+      .def("publish_decode_groups", &PyRuntime::publish_decode_groups, py::arg("B"), py::arg("epoch"))
       .def("qkv_decode", &PyRuntime::qkv_decode)
       .def("decode_attn", &PyRuntime::decode_attn, py::arg("q"), py::arg("layer"), py::arg("page_tables"),
            py::arg("n_tokens"), py::arg("scale"), py::arg("splits"), py::arg("part_o"),
            py::arg("part_lse"), py::arg("counters"), py::arg("epoch_src"), py::arg("epoch_mul"),
-           py::arg("epoch_add"), py::arg("final_out") = py::none())
+           py::arg("epoch_add"), py::arg("final_out") = py::none(), py::arg("combine_out") = py::none())
       .def("qkv_gemv_rope", &PyRuntime::qkv_gemv_rope)
       .def("decode_combine", &PyRuntime::decode_combine)
       .def("wait_flags", &PyRuntime::wait_flags)

@@ -41,7 +41,9 @@ Status DomainRuntime::Init(const RuntimeConfig& cfg) {
   off_tflags_ = align_up(off_flags_ + flags_bytes, 4096);
   const size_t tiles = (size_t(cfg.stage_cap) + kRingTile - 1) / kRingTile;
   tflag_parity_bytes_ = align_up(tiles * cfg.world * sizeof(unsigned long long), 256);
-  off_xslot_ = align_up(off_tflags_ + 2 * tflag_parity_bytes_, 4096);
+  off_gflags_ = align_up(off_tflags_ + 2 * tflag_parity_bytes_, 256);
+  const size_t gflag_bytes = size_t(cfg.world) * cfg.max_batch * cfg.geom.hkv * sizeof(unsigned long long);
+  off_xslot_ = align_up(off_gflags_ + gflag_bytes, 4096);
   xslot_bytes_ = size_t(2) * cfg.world * cfg.max_batch * cfg.num_heads * (cfg.geom.d + 1) * sizeof(float);
   off_stage_ = align_up(off_xslot_ + xslot_bytes_, 4096);
   stage_parity_bytes_ = size_t(2) * cfg.geom.hkv * size_t(cfg.stage_cap) * cfg.geom.d * 2;
@@ -113,7 +115,7 @@ Status DomainRuntime::OpenPeersLocal(const std::vector<DomainRuntime*>& peers) {
 Status DomainRuntime::BuildTables() {
   const int n = cfg_.world;
   std::vector<void*> st0(n), st1(n);
-  std::vector<unsigned long long*> ready(n), consumed(n), dready(n), tf0(n), tf1(n), tok(n);
+  std::vector<unsigned long long*> ready(n), consumed(n), dready(n), tf0(n), tf1(n), tok(n), gf(n);
   std::vector<float*> xs(n);
   for (int r = 0; r < n; ++r) {
     uint8_t* b = peer_base_[r];
@@ -125,6 +127,7 @@ Status DomainRuntime::BuildTables() {
     consumed[r] = fl + kFlagConsumed + cfg_.rank;
     dready[r] = fl + kFlagDecReady + cfg_.rank;
     tok[r] = fl + kFlagToken;
+    gf[r] = reinterpret_cast<unsigned long long*>(b + off_gflags_);
     tf0[r] = reinterpret_cast<unsigned long long*>(b + off_tflags_);
     tf1[r] = reinterpret_cast<unsigned long long*>(b + off_tflags_ + tflag_parity_bytes_);
     xs[r] = reinterpret_cast<float*>(b + off_xslot_);
@@ -147,6 +150,7 @@ Status DomainRuntime::BuildTables() {
   if (!(s = alloc_copy(reinterpret_cast<void**>(&tflag_tab_[0]), tf0.data(), pb)).ok()) return s;
   if (!(s = alloc_copy(reinterpret_cast<void**>(&tflag_tab_[1]), tf1.data(), pb)).ok()) return s;
   if (!(s = alloc_copy(reinterpret_cast<void**>(&token_tab_), tok.data(), pb)).ok()) return s;
+  if (!(s = alloc_copy(reinterpret_cast<void**>(&gflag_tab_), gf.data(), pb)).ok()) return s;
   return Status::Ok();
 }
 
@@ -289,7 +293,6 @@ Status DomainRuntime::AttendLayer(const RingLayerArgs& a, cudaStream_t stream) {
     at.kv_head_stride = long(cfg_.stage_cap) * cfg_.geom.d;
     at.scale = a.scale;
     at.causal = a.causal;
-    at.kv_start_tile = a.kv_start_tile;
     at.wait_budget_ns = cfg_.peer_wait_budget_ns;
     at.status = status_;
     if (a.tile_src != nullptr && n > 1) {
@@ -301,7 +304,6 @@ Status DomainRuntime::AttendLayer(const RingLayerArgs& a, cudaStream_t stream) {
       rg.epoch = a.epoch;
       rg.tile_src = a.tile_src;
       rg.tile_flags = tile_flags(parity);
-      rg.pair_start = a.pair_start;
       rg.push_tiles = a.push_tiles;
       rg.n_push = a.n_push;
       rg.own_stage = sk;
@@ -377,11 +379,12 @@ Status DomainRuntime::Shutdown() {
                   static_cast<void*>(kv_ready_tab_), static_cast<void*>(consumed_tab_),
                   static_cast<void*>(dec_ready_tab_), static_cast<void*>(xslot_tab_),
                   static_cast<void*>(tflag_tab_[0]), static_cast<void*>(tflag_tab_[1]),
-                  static_cast<void*>(token_tab_)})
+                  static_cast<void*>(token_tab_), static_cast<void*>(gflag_tab_)})
     if (t) cudaFree(t);
   stage_tab_[0] = stage_tab_[1] = nullptr;
   tflag_tab_[0] = tflag_tab_[1] = nullptr;
   token_tab_ = nullptr;
+  gflag_tab_ = nullptr;
   kv_ready_tab_ = consumed_tab_ = dec_ready_tab_ = nullptr;
   xslot_tab_ = nullptr;
   if (status_) cudaFree(status_);

@@ -10,6 +10,7 @@
 // Shared region (one cudaMalloc, exported with one IPC handle; identical offsets on every rank):
 //   flags     uint64[kFlagWords]                           (kv_ready / consumed / dec_ready / ...)
 //   tflags    uint64[2][ceil(stage_cap / 128)][world]      per-(KV tile, source rank) ready epochs
+//   gflags    uint64[world][max_batch][Hkv]                decode (O, LSE) per-(source, row, KV head)
 //   xslot     fp32 [2][world][max_batch][H][D+1]          decode (O, LSE) exchange slots
 //   stage     bf16 [2 parity][2 K/V][Hkv][stage_cap][D]   position-ordered prefill KV
 //   arena     bf16 [layers][pages][2][Hkv][page][D]       paged KV cache shard
@@ -53,7 +54,6 @@ struct RingLayerArgs {
   int slot_base = 0;
   int slot_cap = 0;
   int L = 0;                        // total context length (positions 0..L-1)
-  int kv_start_tile = 0;            // first kv tile of this rank's own chunk
   float scale = 0.f;
   int causal = 1;
   void* q_out = nullptr;            // [T, H, D] scratch
@@ -78,7 +78,6 @@ struct RingLayerArgs {
   const unsigned long long* tile_src = nullptr;  // [ceil(L / 128)] bitmask of ranks per tile
   const int* push_tiles = nullptr;  // [n_push][3] (tile, first, end) rows of `pos` per own tile
   int n_push = 0;
-  const int* pair_start = nullptr;  // [ceil(ceil(T / 128) / 2)] first kv tile per q-tile pair
 };
 
 class DomainRuntime {
@@ -120,6 +119,10 @@ class DomainRuntime {
   uint8_t* base() const { return base_; }
   size_t region_bytes() const { return region_bytes_; }
   unsigned long long* flags() const { return reinterpret_cast<unsigned long long*>(base_ + off_flags_); }
+  unsigned long long* group_flags() const {
+    return reinterpret_cast<unsigned long long*>(base_ + off_gflags_);
+  }
+  unsigned long long* const* group_flag_table() const { return gflag_tab_; }
   unsigned long long* tile_flags(int parity) const {
     return reinterpret_cast<unsigned long long*>(base_ + off_tflags_ + size_t(parity) * tflag_parity_bytes_);
   }
@@ -146,7 +149,7 @@ class DomainRuntime {
   RuntimeConfig cfg_{};
   uint8_t* base_ = nullptr;
   size_t region_bytes_ = 0;
-  size_t off_flags_ = 0, off_tflags_ = 0, off_xslot_ = 0, off_stage_ = 0, off_arena_ = 0;
+  size_t off_flags_ = 0, off_tflags_ = 0, off_gflags_ = 0, off_xslot_ = 0, off_stage_ = 0, off_arena_ = 0;
   size_t tflag_parity_bytes_ = 0;
   size_t xslot_bytes_ = 0, stage_parity_bytes_ = 0, arena_bytes_ = 0;
   int* status_ = nullptr;            // kStatusWords int32
@@ -158,6 +161,7 @@ class DomainRuntime {
   unsigned long long** dec_ready_tab_ = nullptr;
   unsigned long long** tflag_tab_[2] = {nullptr, nullptr};
   unsigned long long** token_tab_ = nullptr;
+  unsigned long long** gflag_tab_ = nullptr;
   float** xslot_tab_ = nullptr;
   std::vector<uint8_t*> peer_base_;
   std::vector<bool> peer_opened_ipc_;

@@ -13,9 +13,9 @@
 // buffer. Overlapped mode (the default; the reference's pipelined ring, ring.rs:1195-1339): the
 // projection writes only the local buffer and this kernel does the ring itself: warps 2 and 3
 // store this rank's rows into every peer's buffer over NVLink tile by tile and publish a flag
-// per (tile, source rank), while the q tiles start on the rank's own run of KV tiles (the
-// per-pair start tile) and the TMA producer waits (bounded) for the flags of each remote tile
-// just before loading it. The last CTA releases the staging parity to every rank. Serial mode
+// per (tile, source rank), while the q tiles start on the rank's own rows (each CTA walks its
+// KV tiles down from its diagonal, which is always local) and the TMA producer waits (bounded)
+// for the flags of each remote tile just before loading it. The last CTA releases the staging parity to every rank. Serial mode
 // (the reference's HCP_DISABLE_OVERLAP=1, ring.rs:164-166): every row was pushed and waited for
 // before the launch, and the kernel only computes.
 //
@@ -76,7 +76,6 @@ struct KParams {
   float scale_log2;
   int causal;
   int num_pairs;        // ceil(num_q_tiles / 2)
-  int kv_start_tile;
   RingArgs ring;        // in-kernel KV ring (ring.tile_src == nullptr: off)
   unsigned long long wait_budget_ns;
   int* status;
@@ -133,12 +132,13 @@ __device__ __forceinline__ void ring_push(const KParams& p, int lane) {
   }
 }
 
-// processing order: kv_start_tile .. n-1 ascending, then kv_start_tile-1 .. 0 descending
-__device__ __forceinline__ int kv_tile_at(int j, int n, int start) {
-  if (start >= n) start = 0;
-  const int up = n - start;
-  return j < up ? start + j : start - 1 - (j - up);
-}
+// Processing order of the KV tiles: from the CTA's last visible tile (its diagonal) down to
+// tile 0. Every row therefore folds its visible tiles in the same order (its own diagonal tile
+// first, then descending) whatever q rows share its CTA: tiles above a row's diagonal are fully
+// masked for it and leave no trace (the first visible tile resets the running state with
+// alpha = 0). The result is the same bits for a row on one GPU and under any context-parallel
+// layout, and in a ring the rows of the rank's own contiguous run come first.
+__device__ __forceinline__ int kv_tile_at(int j, int n) { return n - 1 - j; }
 
 // One softmax step of one stream (a q-tile row over CW key columns) held in TMEM: one batch of
 // TMEM loads brings the stream's scores into registers, row max with 3-input maxima, lazy
@@ -225,7 +225,7 @@ __device__ __forceinline__ void softmax_step(uint32_t s_addr, uint32_t o_addr, i
 // 64-column streams with their own running max, row sum and O accumulator (TMEM: S 2 x 128
 // columns, O 4 x 64), so four warpgroups share the softmax work, and merges the two streams of a
 // row in the epilogue. HV = 1 (head_dim 128) keeps one stream per q tile.
-template <int D, int POLY, int HV>
+template <int D, int POLY, int HV, bool RING>
 __global__ void __launch_bounds__(Cfg<D>::threads(HV), 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, KParams p) {
@@ -313,8 +313,6 @@ __global__ void __launch_bounds__(Cfg<D>::threads(HV), 1)
   const int kv_tiles_L = (p.L + BKV - 1) / BKV;
   int n_tiles = p.causal ? (qmax_all >= 0 ? qmax_all / BKV + 1 : 0) : kv_tiles_L;
   if (n_tiles > kv_tiles_L) n_tiles = kv_tiles_L;
-  const int start0 = p.ring.pair_start != nullptr ? p.ring.pair_start[pair] : p.kv_start_tile;
-  const int start = (start0 >= 0 && start0 < n_tiles) ? start0 : 0;
   const bool tile1_live = (row0 + BQ) < p.T;
 
   // register split: warpgroup 0 (TMA, MMA, TMEM allocator, idle warp) hands registers to the
@@ -336,10 +334,10 @@ __global__ void __launch_bounds__(Cfg<D>::threads(HV), 1)
           tma_load_3d(sQ + i * C::Q_BYTES + a * (BQ * 128), &tmQ, q_full, a * 64, head,
                       row0 + i * BQ);
       for (int j = 0; j < n_tiles; ++j) {
-        const int t = kv_tile_at(j, n_tiles, start);
+        const int t = kv_tile_at(j, n_tiles);
         const int s = j % C::STAGES;
         const uint32_t ph = (j / C::STAGES) & 1;
-        if (p.ring.tile_src != nullptr) {
+        if (RING) {
           // remote rows of this tile: wait (bounded) for every other source rank's flag, then
           // order what the flags made visible before the TMA (async proxy) reads it
           unsigned long long m = p.ring.tile_src[t] & ~(1ull << p.ring.my_rank);
@@ -444,7 +442,7 @@ __global__ void __launch_bounds__(Cfg<D>::threads(HV), 1)
         }
       }
     }
-  } else if (p.ring.n_push > 0) {
+  } else if (RING && p.ring.n_push > 0) {
     // ------------------------------------------------------------------ KV ring push (warps 2, 3)
     ring_push<D>(p, int(threadIdx.x % 32));
   }
@@ -460,7 +458,7 @@ __global__ void __launch_bounds__(Cfg<D>::threads(HV), 1)
     float l_sum = 0.f;
     bool ok = true;
     for (int j = 0; j < n_tiles; ++j) {
-      const int t = kv_tile_at(j, n_tiles, start);
+      const int t = kv_tile_at(j, n_tiles);
       if (!mbar_wait(&s_full[tile], j & 1, p.status, 208)) {
         ok = false;
         break;
@@ -545,7 +543,7 @@ __global__ void __launch_bounds__(Cfg<D>::threads(HV), 1)
     tc_fence_after();
     tmem_dealloc(tmem_base, C::TMEM_COLS);
   }
-  if (p.ring.consumed_ptrs != nullptr && threadIdx.x == 0) {
+  if (RING && threadIdx.x == 0) {
     // last CTA: every CTA's reads of this staging parity and pushes are done; tell every rank
     // it may overwrite the parity (layer step epoch + 2) and reset the counters for the next step
     __threadfence_system();
@@ -559,7 +557,7 @@ __global__ void __launch_bounds__(Cfg<D>::threads(HV), 1)
   }
 }
 
-template <int D, int POLY, int HV>
+template <int D, int POLY, int HV, bool RING>
 static cudaError_t launch(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                           const KParams& p, cudaStream_t stream) {
   static_assert(Cfg<D>::threads(HV) <= 1024, "threads");
@@ -568,12 +566,12 @@ static cudaError_t launch(const CUtensorMap& tq, const CUtensorMap& tk, const CU
                 "register split exceeds the launch's registers");
   static std::atomic<unsigned long long> attr{0};
   cudaError_t e = once_per_device(attr, [] {
-    return cudaFuncSetAttribute(attn_fwd_kernel<D, POLY, HV>,
+    return cudaFuncSetAttribute(attn_fwd_kernel<D, POLY, HV, RING>,
                                 cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<D>::SMEM);
   });
   if (e != cudaSuccess) return e;
   const int grid = p.num_pairs * p.H;
-  attn_fwd_kernel<D, POLY, HV><<<grid, Cfg<D>::threads(HV), Cfg<D>::SMEM, stream>>>(tq, tk, tv, p);
+  attn_fwd_kernel<D, POLY, HV, RING><<<grid, Cfg<D>::threads(HV), Cfg<D>::SMEM, stream>>>(tq, tk, tv, p);
   return cudaGetLastError();
 }
 
@@ -605,17 +603,23 @@ template <int D, int HV>
 static cudaError_t launch_hv(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                              const KParams& p, cudaStream_t stream) {
   switch (poly_share()) {
-    case 2: return launch<D, 2, HV>(tq, tk, tv, p, stream);
-    case 3: return launch<D, 3, HV>(tq, tk, tv, p, stream);
-    case 4: return launch<D, 4, HV>(tq, tk, tv, p, stream);
-    default: return launch<D, 0, HV>(tq, tk, tv, p, stream);
+    case 2: return launch<D, 2, HV, false>(tq, tk, tv, p, stream);
+    case 3: return launch<D, 3, HV, false>(tq, tk, tv, p, stream);
+    case 4: return launch<D, 4, HV, false>(tq, tk, tv, p, stream);
+    default: return launch<D, 0, HV, false>(tq, tk, tv, p, stream);
   }
 }
 
 template <int D>
 static cudaError_t launch_d(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                             const KParams& p, cudaStream_t stream) {
-  if (D == 64 && hv64() == 2) return launch_hv<64, 2>(tq, tk, tv, p, stream);
+  const bool hv2 = D == 64 && hv64() == 2;
+  if (p.ring.tile_src != nullptr) {
+    // the in-kernel ring (push warps, per-tile waits, consumed release) is compiled into its own
+    // variants, with the default exponential split, so the single-rank kernels carry none of it
+    return hv2 ? launch<64, 3, 2, true>(tq, tk, tv, p, stream) : launch<D, 3, 1, true>(tq, tk, tv, p, stream);
+  }
+  if (hv2) return launch_hv<64, 2>(tq, tk, tv, p, stream);
   return launch_hv<D, 1>(tq, tk, tv, p, stream);
 }
 
@@ -651,7 +655,6 @@ const char* attn_fwd(const AttnArgs& a, cudaStream_t stream) {
   p.causal = a.causal;
   const int num_q_tiles = (a.T + BQ - 1) / BQ;
   p.num_pairs = (num_q_tiles + QT - 1) / QT;
-  p.kv_start_tile = a.kv_start_tile;
   p.ring = a.ring;
   if (p.ring.tile_src != nullptr) {
     if (p.ring.world < 2 || p.ring.world > 64 || p.ring.my_rank < 0 || p.ring.my_rank >= p.ring.world)

@@ -20,7 +20,6 @@ struct RingArgs {
   unsigned long long epoch = 0;
   const unsigned long long* tile_src = nullptr;  // [kv tiles] bitmask of ranks with rows in tile
   const unsigned long long* tile_flags = nullptr;  // local flags of this parity [tiles][world]
-  const int* pair_start = nullptr;   // [q-tile pairs] first kv tile of the pair's own run
   // push of this rank's rows (n_push = 0: nothing to push)
   const int* push_tiles = nullptr;   // [n_push][3]: (tile, first row, end row) of q_pos
   int n_push = 0;
@@ -45,7 +44,6 @@ struct AttnArgs {
   long kv_head_stride;      // elements between consecutive KV heads (>= L * D)
   float scale;
   int causal;
-  int kv_start_tile;        // first kv tile in processing order (this rank's own chunk)
   RingArgs ring;            // ring.tile_src == nullptr: every KV row is already in place
   unsigned long long wait_budget_ns;
   int* status;

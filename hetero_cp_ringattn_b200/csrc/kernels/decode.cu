@@ -730,6 +730,48 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(const __grid_constant_
   }
   if (threadIdx.x == 0) a.split_counter[b * a.Hkv + h] = 0;
   if (a.final_out != nullptr) return;  // single rank: nothing to signal
+  if (a.combine_out != nullptr) {
+    // in-kernel exchange of this (row, KV head) group: publish, wait for the other ranks' partial
+    // of the same group, combine in rank order (every rank computes identical bits)
+    __shared__ int all_arrived;
+    const long gslot = (long)b * a.Hkv + h;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      all_arrived = 1;
+      __threadfence_system();
+      for (int r = 0; r < a.n_ranks; ++r)
+        st_release_sys(a.group_flag_ptrs[r] + (long)a.my_rank * a.group_stride + gslot, epoch);
+    }
+    __syncthreads();
+    if (threadIdx.x < a.n_ranks && threadIdx.x != a.my_rank &&
+        !wait_flag_geq_sys(a.group_flags + (long)threadIdx.x * a.group_stride + gslot, epoch,
+                           a.budget_ns, a.status, 305, threadIdx.x))
+      all_arrived = 0;
+    __syncthreads();
+    const float* xs = a.xslot_ptrs[a.my_rank] + (long)parity * a.n_ranks * a.B * H * (D + 1);
+    for (int i = threadIdx.x; i < G * D; i += blockDim.x) {
+      const int g = i / D, d = i % D;
+      const int hh = h * G + g;
+      float out = 0.f;
+      if (all_arrived) {
+        float mx = -INFINITY;
+        for (int r = 0; r < a.n_ranks; ++r)
+          mx = fmaxf(mx, __ldcg(xs + (((long)r * a.B + b) * H + hh) * (D + 1) + D));
+        if (mx > -INFINITY) {
+          float ws = 0.f, o = 0.f;
+          for (int r = 0; r < a.n_ranks; ++r) {
+            const long base = (((long)r * a.B + b) * H + hh) * (D + 1);
+            const float w = fast_exp2(__ldcg(xs + base + D) - mx);
+            ws += w;
+            o += w * __ldcg(xs + base + d);
+          }
+          out = o / ws;
+        }
+      }
+      a.combine_out[((long)b * H + hh) * D + d] = __float2bfloat16(out);
+    }
+    return;
+  }
   // grid-wide last CTA signals every rank that this rank's partial has landed
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -797,6 +839,14 @@ static cudaError_t launch_attn(const CUtensorMap& tm, const DecodeAttnArgs& a, c
   cudaError_t e = prepare_attn<D, G>();
   if (e != cudaSuccess) return e;
   dim3 grid(a.splits, a.Hkv, a.B);
+  if (a.combine_out != nullptr) {
+    // the groups' last CTAs wait for the other ranks' CTAs: every CTA must be resident at once
+    int occ = 0, dev = 0, sms = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, decode_attn_kernel<D, G>, 128, DecCfg<D>::SMEM);
+    if (long(a.splits) * a.Hkv * a.B > long(occ) * sms) return cudaErrorCooperativeLaunchTooLarge;
+  }
   return launch_pdl(decode_attn_kernel<D, G>, grid, dim3(128), size_t(DecCfg<D>::SMEM), s, tm, a);
 }
 
@@ -805,6 +855,10 @@ const char* decode_attn(const DecodeAttnArgs& a, cudaStream_t s) {
   if (a.H % a.Hkv) return "decode_attn: H % Hkv";
   if (a.n_ranks < 1 || a.n_ranks > kMaxRanks) return "decode_attn: bad n_ranks";
   if (a.final_out != nullptr && a.n_ranks != 1) return "decode_attn: final_out is for a single rank";
+  if (a.combine_out != nullptr &&
+      (a.n_ranks < 2 || a.n_ranks > 128 || a.group_flag_ptrs == nullptr || a.group_flags == nullptr ||
+       a.group_stride < a.B * a.Hkv))
+    return "decode_attn: the in-kernel combine needs 2+ ranks and the group flags";
   if (a.splits < 1 || a.splits > kMaxDecodeSplits) return "decode_attn: splits must be in [1, 128]";
   if ((a.D != 64 && a.D != 128) || a.geom.page % kDecCC)
     return "decode_attn: head_dim must be 64 or 128 and the page a multiple of 64 rows";

@@ -78,6 +78,15 @@ struct DecodeAttnArgs {
   int my_rank;
   unsigned long long* const* ready_ptrs;  // device array [n_ranks]: &dec_ready[my_rank] on rank r
   __nv_bfloat16* final_out;    // single rank: the last CTA writes O [B, H*D] here (no exchange)
+  // several ranks, in-kernel combine (combine_out set): the last CTA of each (row b, KV head h)
+  // stores the rank's partial into every rank's slots, publishes group_flag[my_rank][b][h] =
+  // epoch on every rank, waits (bounded) for every other rank's flag of the same group and
+  // writes the log-sum-exp combine in rank order into combine_out [B, H*D] (no combine launch)
+  __nv_bfloat16* combine_out;
+  unsigned long long* const* group_flag_ptrs;  // [n_ranks]: rank r's group-flag base
+  const unsigned long long* group_flags;       // local base [n_ranks][group_stride]
+  int group_stride;                            // max_batch * Hkv
+  unsigned long long budget_ns;
   const unsigned long long* epoch_parity_src;  // device step counter (may be null)
   unsigned long long epoch_mul;  // epoch = (*src) * mul + add
   unsigned long long epoch_add;

@@ -214,6 +214,13 @@ __global__ void publish_tiles_kernel(const int* push_tiles, int n_push,
   }
 }
 
+__global__ void publish_range_kernel(unsigned long long* const* ptrs, int world, long base, int n,
+                                     unsigned long long epoch) {
+  __threadfence_system();
+  for (int i = threadIdx.x; i < n * world; i += blockDim.x)
+    st_release_sys(ptrs[i % world] + base + i / world, epoch);
+}
+
 // First-token broadcast from the rank that holds the last prompt position (one thread).
 __global__ void token_bcast_kernel(long long* tok, unsigned long long* const* slots,
                                    const unsigned long long* own_slot, int world, int is_src,
@@ -344,6 +351,13 @@ const char* publish_tiles(const int* push_tiles, int n_push, unsigned long long*
   if (n_push == 0) return nullptr;
   publish_tiles_kernel<<<1, 256, 0, s>>>(push_tiles, n_push, tflag_ptrs, world, my_rank, epoch);
   return cudaGetLastError() == cudaSuccess ? nullptr : "publish_tiles: launch failed";
+}
+
+const char* publish_range(unsigned long long* const* ptrs, int world, long base, int n,
+                          unsigned long long epoch, cudaStream_t s) {
+  if (n <= 0) return nullptr;
+  publish_range_kernel<<<1, 256, 0, s>>>(ptrs, world, base, n, epoch);
+  return cudaGetLastError() == cudaSuccess ? nullptr : "publish_range: launch failed";
 }
 
 const char* token_bcast(long long* tok, unsigned long long* const* slots,

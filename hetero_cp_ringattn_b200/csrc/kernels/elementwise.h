@@ -82,6 +82,9 @@ const char* signal_peers(unsigned long long* const* ptrs, int n, unsigned long l
 // tflag_ptrs[r][push_tiles[k][0] * world + my_rank] = epoch for every own tile k and rank r.
 const char* publish_tiles(const int* push_tiles, int n_push, unsigned long long* const* tflag_ptrs,
                           int world, int my_rank, unsigned long long epoch, cudaStream_t s);
+// ptrs[r][base + i] = epoch for every rank r and i < n (release stores after a system fence).
+const char* publish_range(unsigned long long* const* ptrs, int world, long base, int n,
+                          unsigned long long epoch, cudaStream_t s);
 // Source: slots[r][2 p] = *tok, release slots[r][2 p + 1] = epoch (p = epoch & 1) for every rank;
 // others: bounded wait for own_slot[2 p + 1] >= epoch, then *tok = own_slot[2 p].
 const char* token_bcast(long long* tok, unsigned long long* const* slots,

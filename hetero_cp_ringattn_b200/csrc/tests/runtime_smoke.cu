@@ -141,7 +141,6 @@ int main() {
     a.slot_base = 0;
     a.slot_cap = 2 * 256;
     a.L = L;
-    a.kv_start_tile = offset / 128;
     a.scale = 1.f / std::sqrt(float(D));
     a.causal = 1;
     a.q_out = qo;

@@ -50,17 +50,14 @@ from ..utils.perf import PerfLog, peak_bf16_tflops
 from .weights import PreparedWeights
 
 
-def ring_plan(positions: Sequence[np.ndarray], rank: int, L: int, tile: int = 128,
-              pair_rows: int = 256):
+def ring_plan(positions: Sequence[np.ndarray], rank: int, L: int, tile: int = 128):
     """Host plan of the overlapped in-kernel ring for one request (the same for every layer).
 
     positions[r] are rank r's global prompt positions (ascending, any layout). Returns
       tile_src   int64 [ceil(L / tile)]: bit r set when rank r holds rows of KV tile t (the
                  attention waits for the flags of exactly these (tile, rank) pairs);
       push_tiles int32 [n, 3]: this rank's own tiles as (tile, first row, end row) ranges of its
-                 positions, last tile first (the order in which its kernel pushes them);
-      pair_start int32 [q-tile pairs]: per pair of 128-row q tiles, the KV tile where the pair's
-                 contiguous run of positions starts, so each CTA begins with its own rows.
+                 positions, last tile first (the order in which its kernel pushes them).
     """
     ntiles = -(-int(L) // tile)
     src = np.zeros(ntiles, dtype=np.uint64)
@@ -69,18 +66,13 @@ def ring_plan(positions: Sequence[np.ndarray], rank: int, L: int, tile: int = 12
             src[np.unique(np.asarray(p, dtype=np.int64) // tile)] |= np.uint64(1) << np.uint64(r)
     own = np.asarray(positions[rank], dtype=np.int64)
     if len(own) == 0:
-        return src.view(np.int64), np.zeros((0, 3), dtype=np.int32), np.zeros(0, dtype=np.int32)
+        return src.view(np.int64), np.zeros((0, 3), dtype=np.int32)
     if np.any(np.diff(own) <= 0):
         raise RingError("ring plan: a rank's positions must be strictly increasing")
     tiles, lo = np.unique(own // tile, return_index=True)
     hi = np.r_[lo[1:], len(own)]
     push = np.stack([tiles, lo, hi], 1)[::-1].astype(np.int32)
-    npairs = -(-(-(-len(own) // 128)) // 2)
-    first = np.arange(npairs, dtype=np.int64) * pair_rows
-    runs = np.r_[0, np.nonzero(np.diff(own) != 1)[0] + 1]
-    run_of = runs[np.searchsorted(runs, first, side="right") - 1]
-    pair_start = (own[run_of] // tile).astype(np.int32)
-    return src.view(np.int64), np.ascontiguousarray(push), pair_start
+    return src.view(np.int64), np.ascontiguousarray(push)
 
 
 @dataclasses.dataclass
@@ -282,10 +274,9 @@ class LlamaCPEngine:
         xn = torch.empty_like(x)
         q_buf = torch.empty(T, self.H, self.D, dtype=torch.bfloat16, device=dev)
         o_buf = torch.empty_like(q_buf)
-        start_tile = int(st.positions[0]) // 128 if st.strategy is RingStrategy.VANILLA else 0
         ring = {}
         if st.ring is not None:
-            ring = dict(tile_src=st.ring[0], push_tiles=st.ring[1], pair_start=st.ring[2])
+            ring = dict(tile_src=st.ring[0], push_tiles=st.ring[1])
         fused = self.fused_qkv if (self.world == 1 or st.ring is not None) else self.fused_qkv_serial
         trace = self.perf.enabled
         nvtx = self.env.nvtx
@@ -297,8 +288,8 @@ class LlamaCPEngine:
                 ev[0].record()
             K.rmsnorm(x, lw.in_norm, self.cfg.rms_norm_eps, out=xn)
             self.prefill_epoch += 1
-            tail = (pos, self.cos, self.sin, li, st.kv.pt_device, 0, Lp, start_tile,
-                    self.scale, True, q_buf, o_buf, None, self.prefill_epoch)
+            tail = (pos, self.cos, self.sin, li, st.kv.pt_device, 0, Lp, self.scale, True,
+                    q_buf, o_buf, None, self.prefill_epoch)
             if trace:
                 ev[1].record()
             if fused:
@@ -671,14 +662,13 @@ class LlamaCPEngine:
         xn = torch.empty_like(x)
         q_buf = torch.empty(T, self.H, self.D, dtype=torch.bfloat16, device=dev)
         o_buf = torch.empty_like(q_buf)
-        start_tile = int(my_pos[0]) // 128 if T else 0
         empty_qkv = torch.empty(0, self.cfg.qkv_size, dtype=torch.bfloat16, device=dev)
         for li, lw in enumerate(w.layers):
             c = int(kv.layer_counts[li])
             existing = torch.from_numpy(kv.slot_pos[li, :c].astype(np.int32)).to(dev)
             self.prefill_epoch += 1
-            tail = (pos, self.cos, self.sin, li, kv.pt_device, c, Ltot, start_tile, self.scale,
-                    True, q_buf, o_buf, None, self.prefill_epoch, existing)
+            tail = (pos, self.cos, self.sin, li, kv.pt_device, c, Ltot, self.scale, True, q_buf,
+                    o_buf, None, self.prefill_epoch, existing)
             if T:
                 K.rmsnorm(x, lw.in_norm, self.cfg.rms_norm_eps, out=xn)
             if T and self.fused_qkv_serial:   # continuation segments use the serial ring
@@ -862,13 +852,13 @@ class DecodeGraph:
             rt.qkv_gemv_rope(self.x, lw.wqkv, lw.bqkv, lw.in_norm, eps, self.pos, e.cos, e.sin, li,
                              self.pt, self.owner, self.slot, self.q)
             # split-KV attention; on one rank its last CTA writes the layer output directly,
-            # otherwise the (O, LSE) partials go to every rank and are combined in rank order
+            # otherwise the last CTA of each (row, KV head) stores the rank's (O, LSE) partial
+            # into every rank's slots and, once the other ranks' partials of that group have
+            # arrived (bounded wait), writes their log-sum-exp combine in rank order
             rt.decode_attn(self.q, li, self.pt, self.ntok[li], e.scale, self.splits, self.part_o,
                            self.part_l, self.counters, e.dec_step, e.L, li + 1,
-                           self.o if single else None)
-            if not single:
-                rt.decode_combine(self.o, self.B, e.H, e.dec_step, e.L, li + 1)
-            launches.count(2 if single else 3)
+                           self.o if single else None, None if single else self.o)
+            launches.count(2)
             K.gemv(self.o, lw.wo, "residual", y_bf16=self.x)
             K.gemv(self.x, lw.wgu, "swiglu", y_bf16=self.g, norm_w=lw.post_norm, eps=eps)
             K.gemv(self.g, lw.wd, "residual", y_bf16=self.x)

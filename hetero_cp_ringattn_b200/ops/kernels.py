@@ -81,7 +81,7 @@ def gemm(a: torch.Tensor, w: torch.Tensor, epi: str = "store", bias: Optional[to
 
 # --------------------------------------------------------------------------- attention
 def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, q_pos: torch.Tensor, L: int,
-              causal: bool = True, scale: Optional[float] = None, kv_start_tile: int = 0,
+              causal: bool = True, scale: Optional[float] = None,
               want_lse: bool = True, status: Optional[torch.Tensor] = None):
     """Flash attention of q [T,H,D] over position-ordered k/v [Hkv, Lcap, D] (rows 0..L-1).
 
@@ -96,7 +96,7 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, q_pos: torch.Te
         return o.to(q.dtype), (lse if want_lse else None)
     o = torch.empty_like(q)
     lse = torch.empty(h, t, dtype=torch.float32, device=q.device) if want_lse else None
-    native().attn_fwd(q, k, v, o, lse, q_pos, L, k.stride(0), scale, causal, kv_start_tile, status)
+    native().attn_fwd(q, k, v, o, lse, q_pos, L, k.stride(0), scale, causal, status)
     launches.count()
     return o, lse
 

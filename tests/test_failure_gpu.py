@@ -46,16 +46,15 @@ def test_overlapped_ring_missing_peer_times_out_into_status(dev):
     chunks = [256, 256]
     L = sum(chunks)
     positions = layout_positions(chunks, "zigzag")
-    src, push, pair = ring_plan(positions, 0, L)
-    plan = dict(tile_src=torch.from_numpy(src).to(dev), push_tiles=torch.from_numpy(push).to(dev),
-                pair_start=torch.from_numpy(pair).to(dev))
+    src, push = ring_plan(positions, 0, L)
+    plan = dict(tile_src=torch.from_numpy(src).to(dev), push_tiles=torch.from_numpy(push).to(dev))
     p = torch.as_tensor(positions[0], device=dev).int()
     cos, sin = ref.rope_cos_sin(torch.arange(2048, device=dev), D, 10000.0)
     qkv = torch.randn(len(p), (H + 2 * HKV) * D, device=dev).bfloat16()
     q_out = torch.empty(len(p), H, D, device=dev, dtype=torch.bfloat16)
     o_out = torch.empty_like(q_out)
     args = (qkv, p, cos.contiguous(), sin.contiguous(), 0, torch.arange(0, 2, dtype=torch.int32, device=dev),
-            0, L, 0, 1.0 / math.sqrt(D), True, q_out, o_out, None, 1)
+            0, L, 1.0 / math.sqrt(D), True, q_out, o_out, None, 1)
     t0 = time.time()
     rts[0].push_layer(*args, **plan)
     rts[0].attend_layer(*args, **plan)     # rank 1 never pushes or publishes its tiles

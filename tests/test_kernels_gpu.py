@@ -104,8 +104,7 @@ def test_attention(dev, d, layout):
     q = q_all[pos].contiguous()
     ks, vs = _stage(k_all, v_all, cap=1024)
     st = status_tensor(dev)
-    start = int(pos[0]) // 128 if layout == "suffix" else 0
-    o, lse = K.attention(q, ks, vs, pos.int(), L, causal=causal, kv_start_tile=start, status=st)
+    o, lse = K.attention(q, ks, vs, pos.int(), L, causal=causal, status=st)
     assert_status_clean(st)
     ro, rl = ref.full_attention(q.float(), k_all.float(), v_all.float(), pos, torch.arange(L, device=dev),
                                 causal=causal)
@@ -243,8 +242,7 @@ def test_attention_edge_shapes(dev, L, T, h, hkv, d):
     pos = torch.arange(L - T, L, device=dev)
     ks, vs = _stage(k_all, v_all, cap=max(128, L))
     st = status_tensor(dev)
-    o, lse = K.attention(q_all[pos].contiguous(), ks, vs, pos.int(), L, causal=True,
-                         kv_start_tile=(L - T) // 128, status=st)
+    o, lse = K.attention(q_all[pos].contiguous(), ks, vs, pos.int(), L, causal=True, status=st)
     assert_status_clean(st)
     ro, rl = ref.full_attention(q_all[pos].float(), k_all.float(), v_all.float(), pos,
                                 torch.arange(L, device=dev), causal=True)

@@ -57,8 +57,7 @@ def run_ranks(dev, chunks, strategy, layer=0, epoch=1, rts=None):
         q_out = torch.empty(len(p), H, D, device=dev, dtype=torch.bfloat16)
         o_out = torch.empty_like(q_out)
         lse = torch.empty(H, len(p), device=dev, dtype=torch.float32)
-        start = int(p[0]) // 128 if strategy == "vanilla" else 0
-        a = (qkv, p.int().contiguous(), cos, sin, layer, pt, 0, L, start, 1.0 / math.sqrt(D), True,
+        a = (qkv, p.int().contiguous(), cos, sin, layer, pt, 0, L, 1.0 / math.sqrt(D), True,
              q_out, o_out, lse, epoch)
         args.append(a)
         outs.append((o_out, lse))
@@ -150,6 +149,57 @@ def test_decode_exchange(dev, world, b):
         assert torch.equal(outs[r], outs[0]), "ranks must produce bit-identical combined outputs"
 
 
+@pytest.mark.parametrize("world,b", [(2, 1), (3, 4), (4, 2)])
+def test_decode_in_kernel_combine(dev, world, b):
+    """The multi-rank decode attention with the exchange and the rank-order combine inside the
+    kernel (the last CTA of each (row, KV head) publishes its partial, waits for the other ranks'
+    and combines), with ranks emulated on one GPU: ranks 1.. first store their partials with the
+    plain kernel and publish their group flags, so every wait is satisfied when it is launched.
+    All ranks' outputs are bit-identical and match float32 attention over every rank's KV."""
+    torch.manual_seed(19)
+    counts = [300, 257, 129, 64][:world]
+    rts = [make_rt(r, world) for r in range(world)]
+    for rt in rts:
+        rt.open_peers_local(rts)
+    q = torch.randn(b, H, D, device=dev, dtype=torch.bfloat16)
+    ks, vs, pts = [], [], []
+    for r in range(world):
+        arena = rts[r].arena()
+        k = torch.randn(counts[r], HKV, D, device=dev, dtype=torch.bfloat16)
+        v = torch.randn(counts[r], HKV, D, device=dev, dtype=torch.bfloat16)
+        for i in range(counts[r]):
+            arena[0, [2, 5][i // PAGE], 0, :, i % PAGE] = k[i]
+            arena[0, [2, 5][i // PAGE], 1, :, i % PAGE] = v[i]
+        ks.append(k)
+        vs.append(v)
+        pts.append(torch.tensor([[2, 5]] * b, dtype=torch.int32, device=dev))
+    splits, epoch = 4, 9
+
+    def attn(r, combine_out=None):
+        part_o = torch.empty(b * H * splits * D, device=dev)
+        part_l = torch.empty(b * H * splits, device=dev)
+        cnt = torch.zeros(b * HKV + 1, dtype=torch.int32, device=dev)
+        ntok = torch.full((b,), counts[r], dtype=torch.int32, device=dev)
+        rts[r].decode_attn(q, 0, pts[r], ntok, 1.0 / math.sqrt(D), splits, part_o, part_l, cnt,
+                           None, 1, epoch, None, combine_out)
+        torch.cuda.synchronize()   # the scratch tensors live until the launch is done
+
+    for r in range(1, world):
+        attn(r)
+        rts[r].publish_decode_groups(b, epoch)
+    outs = [torch.full((b, H * D), float("nan"), device=dev, dtype=torch.bfloat16) for _ in range(world)]
+    for r in range(world):
+        attn(r, outs[r])
+    for rt in rts:
+        rt.check()
+    k_all, v_all = torch.cat(ks), torch.cat(vs)
+    for bb in range(b):
+        ro, _ = ref.full_attention(q[bb:bb + 1].float(), k_all.float(), v_all.float(), causal=False)
+        assert (outs[0][bb].view(H, D).float() - ro[0]).abs().max() < 2e-2
+    for r in range(1, world):
+        assert torch.equal(outs[r], outs[0]), "ranks must produce bit-identical combined outputs"
+
+
 @pytest.mark.parametrize("d,chunks,strategy", [(64, [700], "vanilla"), (128, [333, 400], "zigzag"),
                                                (64, [300, 200, 257], "striped")])
 def test_fused_projection_push(dev, d, chunks, strategy):
@@ -179,8 +229,7 @@ def test_fused_projection_push(dev, d, chunks, strategy):
         q_out = torch.empty(len(p), H, d, device=dev, dtype=torch.bfloat16)
         o_out = torch.empty_like(q_out)
         lse = torch.empty(H, len(p), device=dev, dtype=torch.float32)
-        start = int(p[0]) // 128 if strategy == "vanilla" else 0
-        tail = (p.int().contiguous(), cos, sin, 0, pt, 0, L, start, 1.0 / math.sqrt(d), True,
+        tail = (p.int().contiguous(), cos, sin, 0, pt, 0, L, 1.0 / math.sqrt(d), True,
                 q_out, o_out, lse, 1)
         runs.append((x, tail, q_out, o_out, lse))
     for r in range(n):
@@ -284,9 +333,8 @@ def test_decode_attention_group_shapes(dev, h, hkv, d, n):
 
 def _plan(positions, rank, L, dev):
     from hetero_cp_ringattn_b200.models.llama import ring_plan
-    src, push, pair = ring_plan([p.cpu().numpy() for p in positions], rank, L)
-    return dict(tile_src=torch.from_numpy(src).to(dev), push_tiles=torch.from_numpy(push).to(dev),
-                pair_start=torch.from_numpy(pair).to(dev))
+    src, push = ring_plan([p.cpu().numpy() for p in positions], rank, L)
+    return dict(tile_src=torch.from_numpy(src).to(dev), push_tiles=torch.from_numpy(push).to(dev))
 
 
 def run_overlap_ranks(dev, chunks, strategy, epoch, rts=None, layer=0):
@@ -315,7 +363,7 @@ def run_overlap_ranks(dev, chunks, strategy, epoch, rts=None, layer=0):
         q_out = torch.empty(len(p), H, D, device=dev, dtype=torch.bfloat16)
         o_out = torch.empty_like(q_out)
         lse = torch.empty(H, len(p), device=dev, dtype=torch.float32)
-        args.append((qkv, p.int().contiguous(), cos, sin, layer, pt, 0, L, 0, 1.0 / math.sqrt(D),
+        args.append((qkv, p.int().contiguous(), cos, sin, layer, pt, 0, L, 1.0 / math.sqrt(D),
                      True, q_out, o_out, lse, epoch))
         plans.append(_plan(positions, r, L, dev))
         outs.append((o_out, lse))
@@ -330,11 +378,23 @@ def run_overlap_ranks(dev, chunks, strategy, epoch, rts=None, layer=0):
     for rt in rts:
         rt.check()
     _, _, _, o_ref, lse_ref = reference_layer(qkv_all, pos_all)
+    # one rank over the whole sequence: every row folds its KV tiles in the same order, so the
+    # ranks' rows are the same bits as the single rank's
+    one = make_rt(0, 1)
+    o_one = torch.empty(L, H, D, device=dev, dtype=torch.bfloat16)
+    a1 = (qkv_all, pos_all.int(), cos, sin, 0, torch.arange(0, 8, dtype=torch.int32, device=dev), 0,
+          L, 1.0 / math.sqrt(D), True, torch.empty_like(o_one), o_one, None, 1)
+    one.push_layer(*a1)
+    one.attend_layer(*a1)
+    torch.cuda.synchronize()
+    one.check()
+    one.shutdown()
     for r in range(n):
         p = positions[r]
         o, lse = outs[r]
         assert (o.float() - o_ref[p]).abs().max() < 2e-2, f"rank {r}"
         assert (lse - lse_ref[:, p]).abs().max() < 2e-2, f"rank {r}"
+        assert torch.equal(o, o_one[p]), f"rank {r}: not bit-identical to one rank"
     return rts
 
 
