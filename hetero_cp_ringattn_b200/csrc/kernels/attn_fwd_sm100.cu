@@ -50,7 +50,6 @@ constexpr int BQ = 128;      // q rows per tile
 constexpr int BKV = 128;     // kv rows per tile
 constexpr int QT = 2;        // q tiles per CTA
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
-constexpr int kExpBf16 = 8;  // POLY value selecting the bf16-pair MUFU exponentials
 
 template <int D>
 struct Cfg {
@@ -64,8 +63,9 @@ struct Cfg {
   // threads: warpgroup 0 (TMA, MMA, TMEM allocator, idle) + one warpgroup per softmax stream
   __host__ __device__ static constexpr int threads(int hv) { return 128 + QT * hv * 128; }
   // register split (setmaxnreg): 128 x wg0 + (threads - 128) x sm must not exceed the launch's
-  // threads x registers (168 at 384 threads, 96 at 640)
-  __host__ __device__ static constexpr int wg0_regs(int hv) { return hv == 1 ? 88 : 80; }
+  // threads x registers (168 at 384 threads: 11264 + 53248 <= 64512; 96 at 640: 11264 + 49152
+  // <= 61440)
+  __host__ __device__ static constexpr int wg0_regs(int hv) { return 88; }
   __host__ __device__ static constexpr int sm_regs(int hv) { return hv == 1 ? 208 : 96; }
 };
 
@@ -183,38 +183,6 @@ __device__ __forceinline__ void softmax_step(uint32_t s_addr, uint32_t o_addr, i
   float2 rs0 = make_float2(0.f, 0.f), rs1 = make_float2(0.f, 0.f);
   const float2 negm = make_float2(-m_use, -m_use);
   const float2 sc2 = make_float2(scale_log2, scale_log2);
-  if constexpr (POLY == kExpBf16) {
-    // exponentials in bf16 pairs on the MUFU: the argument is rounded to bf16 (P is consumed in
-    // bf16 by the P V product anyway), P comes out packed, and the row sum adds exactly the bf16
-    // values the product uses, in fp32
-    // pass 1 folds each score pair into one packed bf16x2 argument, in place (half the live
-    // registers); pass 2 exponentiates, sums and stores P 16 packed columns at a time
-#pragma unroll
-    for (int e = 0; e < CW; e += 2) {
-      const float2 x = __ffma2_rn(make_float2(__uint_as_float(r[e]), __uint_as_float(r[e + 1])), sc2, negm);
-      r[e >> 1] = pack_bf16x2(x.x, x.y);
-    }
-    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
-#pragma unroll
-    for (int hh = 0; hh < CW / 32; ++hh) {
-      uint32_t pk[16];
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const uint32_t pb = exp2_bf16x2(r[hh * 16 + i]);
-        pk[i] = pb;
-        if (i & 1) {
-          a2 = add_bf16_lo(pb, a2);
-          a3 = add_bf16_hi(pb, a3);
-        } else {
-          a0 = add_bf16_lo(pb, a0);
-          a1 = add_bf16_hi(pb, a1);
-        }
-      }
-      tmem_st16(s_addr + hh * 16, pk);
-    }
-    rs0 = make_float2(a0, a1);
-    rs1 = make_float2(a2, a3);
-  } else {
 #pragma unroll
   for (int hh = 0; hh < CW / 32; ++hh) {
     uint32_t pk[16];
@@ -234,7 +202,6 @@ __device__ __forceinline__ void softmax_step(uint32_t s_addr, uint32_t o_addr, i
       pk[e >> 1] = pack_bf16x2(pp.x, pp.y);
     }
     tmem_st16(s_addr + hh * 16, pk);
-  }
   }
   // O rescale after the scores are dead (lower register peak). PV(j-1) of this stream completed
   // before S(j) did (same issuing thread, in-order commits), so O is stable, and PV(j) is only
@@ -620,14 +587,14 @@ static int hv64() {
 }
 
 // Polynomial share (out of 8 exponential pairs), the same for head_dim 64 and 128; HCP_ATTN_POLY
-// overrides it (0, 2, 3 or 4; 8 selects bf16-pair MUFU exponentials for every pair).
+// overrides it (0, 2, 3 or 4).
 static int poly_share() {
   static int env = -2;
   if (env == -2) {
     const char* s = getenv("HCP_ATTN_POLY");
     env = (s && *s) ? atoi(s) : -1;
   }
-  if (env == 0 || (env >= 2 && env <= 4) || env == kExpBf16) return env;
+  if (env == 0 || (env >= 2 && env <= 4)) return env;
   // measured on B200 (32k causal, 32/8 heads, one TMEM read of S per step): 3 of 8 pairs is the
   // best split for D=64 and 128 (748 / 1263 TFLOP/s; 4 of 8 gives 703 / 1152)
   return 3;
@@ -640,7 +607,6 @@ static cudaError_t launch_hv(const CUtensorMap& tq, const CUtensorMap& tk, const
     case 2: return launch<D, 2, HV, false>(tq, tk, tv, p, stream);
     case 3: return launch<D, 3, HV, false>(tq, tk, tv, p, stream);
     case 4: return launch<D, 4, HV, false>(tq, tk, tv, p, stream);
-    case kExpBf16: return launch<D, kExpBf16, HV, false>(tq, tk, tv, p, stream);
     default: return launch<D, 0, HV, false>(tq, tk, tv, p, stream);
   }
 }

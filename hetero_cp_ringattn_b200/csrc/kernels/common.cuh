@@ -356,26 +356,6 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
-// Two 2^x at once on the MUFU, in bf16: the input pair is packed to bf16x2 (round to nearest)
-// and the results come back packed, low half first, ready to be stored as the P operand.
-__device__ __forceinline__ uint32_t exp2_bf16x2(uint32_t x) {
-  uint32_t y;
-  asm("ex2.approx.ftz.bf16x2 %0, %1;" : "=r"(y) : "r"(x));
-  return y;
-}
-
-// acc (fp32) += the low / high bf16 half of a packed pair, one instruction each.
-__device__ __forceinline__ float add_bf16_lo(uint32_t v, float acc) {
-  asm("{\n\t.reg .b16 lo, hi;\n\tmov.b32 {lo, hi}, %1;\n\tadd.f32.bf16 %0, lo, %0;\n\t}"
-      : "+f"(acc) : "r"(v));
-  return acc;
-}
-__device__ __forceinline__ float add_bf16_hi(uint32_t v, float acc) {
-  asm("{\n\t.reg .b16 lo, hi;\n\tmov.b32 {lo, hi}, %1;\n\tadd.f32.bf16 %0, hi, %0;\n\t}"
-      : "+f"(acc) : "r"(v));
-  return acc;
-}
-
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);

@@ -855,10 +855,13 @@ class DecodeGraph:
             # otherwise the last CTA of each (row, KV head) stores the rank's (O, LSE) partial
             # into every rank's slots and, once the other ranks' partials of that group have
             # arrived (bounded wait), writes their log-sum-exp combine in rank order
+            fused = single or e.env.decode_kernel_combine
             rt.decode_attn(self.q, li, self.pt, self.ntok[li], e.scale, self.splits, self.part_o,
                            self.part_l, self.counters, e.dec_step, e.L, li + 1,
-                           self.o if single else None, None if single else self.o)
-            launches.count(2)
+                           self.o if single else None, None if single or not fused else self.o)
+            if not fused:   # HCP_DECODE_KERNEL_COMBINE=0: wait + combine in their own launch
+                rt.decode_combine(self.o, self.B, e.H, e.dec_step, e.L, li + 1)
+            launches.count(2 if fused else 3)
             K.gemv(self.o, lw.wo, "residual", y_bf16=self.x)
             K.gemv(self.x, lw.wgu, "swiglu", y_bf16=self.g, norm_w=lw.post_norm, eps=eps)
             K.gemv(self.g, lw.wd, "residual", y_bf16=self.x)
