@@ -357,8 +357,9 @@ class EnvConfig:
     p2p_spin_budget_ms: int = 5000          # HCP_P2P_SPIN_BUDGET_MS: device-side peer-wait limit
     device: Optional[str] = None            # HCP_TORCH_DEVICE / HCP_TCH_DEVICE
     nvtx: bool = False                      # HCP_NVTX: NVTX ranges per prefill layer / decode step
-    decode_kernel_combine: bool = True      # HCP_DECODE_KERNEL_COMBINE=0: separate combine launch
-                                            # after the decode attention (several ranks)
+    decode_kernel_combine: bool = False     # HCP_DECODE_KERNEL_COMBINE=1: cross-rank combine inside
+                                            # the decode attention kernel (several ranks; measured
+                                            # slower at 2 ranks than the separate combine launch)
     fused_qkv: Optional[bool] = None        # HCP_FUSED_QKV: the projection GEMM's epilogue does
                                             # RoPE + the K/V writes (default on; 0: GEMM + a
                                             # separate RoPE / K/V kernel)
@@ -377,7 +378,7 @@ class EnvConfig:
             p2p_spin_budget_ms=_env_int("HCP_P2P_SPIN_BUDGET_MS", 5000),
             device=os.environ.get("HCP_TORCH_DEVICE") or os.environ.get("HCP_TCH_DEVICE") or None,
             nvtx=_env_bool("HCP_NVTX", False),
-            decode_kernel_combine=_env_bool("HCP_DECODE_KERNEL_COMBINE", True),
+            decode_kernel_combine=_env_bool("HCP_DECODE_KERNEL_COMBINE", False),
             fused_qkv=(_env_bool("HCP_FUSED_QKV", True) if os.environ.get("HCP_FUSED_QKV") else None),
         )
 

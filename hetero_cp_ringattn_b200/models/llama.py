@@ -851,15 +851,16 @@ class DecodeGraph:
             # RMSNorm + QKV GEMV whose epilogue applies RoPE, writes q and appends k/v on the owner
             rt.qkv_gemv_rope(self.x, lw.wqkv, lw.bqkv, lw.in_norm, eps, self.pos, e.cos, e.sin, li,
                              self.pt, self.owner, self.slot, self.q)
-            # split-KV attention; on one rank its last CTA writes the layer output directly,
-            # otherwise the last CTA of each (row, KV head) stores the rank's (O, LSE) partial
-            # into every rank's slots and, once the other ranks' partials of that group have
-            # arrived (bounded wait), writes their log-sum-exp combine in rank order
+            # split-KV attention; on one rank its last CTA writes the layer output directly.
+            # With several ranks the rank's (O, LSE) partial goes into every rank's slots and
+            # the log-sum-exp combine in rank order follows a bounded wait for the other ranks'
+            # partials: in its own launch (default), or with HCP_DECODE_KERNEL_COMBINE=1 inside
+            # the attention kernel, by the last CTA of each (row, KV head)
             fused = single or e.env.decode_kernel_combine
             rt.decode_attn(self.q, li, self.pt, self.ntok[li], e.scale, self.splits, self.part_o,
                            self.part_l, self.counters, e.dec_step, e.L, li + 1,
                            self.o if single else None, None if single or not fused else self.o)
-            if not fused:   # HCP_DECODE_KERNEL_COMBINE=0: wait + combine in their own launch
+            if not fused:   # the default with several ranks: wait + combine in their own launch
                 rt.decode_combine(self.o, self.B, e.H, e.dec_step, e.L, li + 1)
             launches.count(2 if fused else 3)
             K.gemv(self.o, lw.wo, "residual", y_bf16=self.x)
