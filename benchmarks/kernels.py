@@ -269,12 +269,18 @@ def bench_ring(args, pk):
     o_buf = torch.empty_like(q_buf)
     scale = 1.0 / math.sqrt(D)
     epoch = [0]
+    ring = {}
+    if world > 1 and not args.serial:
+        # overlapped ring: local projection, the attention kernel pushes and waits per tile
+        from hetero_cp_ringattn_b200.models.llama import ring_plan
+        src, push = ring_plan(positions, rank, L)
+        ring = dict(tile_src=torch.from_numpy(src).to(dev), push_tiles=torch.from_numpy(push).to(dev))
 
     def layer():
         epoch[0] += 1
         a = (qkv, pos, cos, sin, 0, pt, 0, L, scale, True, q_buf, o_buf, None, epoch[0])
-        rt.push_layer(*a)
-        rt.attend_layer(*a)
+        rt.push_layer(*a, **ring)
+        rt.attend_layer(*a, **ring)
 
     iters = args.iters
     for _ in range(3):
@@ -300,6 +306,7 @@ def bench_ring(args, pk):
     t_link = push_max / (NVLINK_GBS * 1e6)
     roof = max(t_compute, t_link)
     row = dict(kernel="ring_attention_layer", cp=world, seq=L, chunks=chunks, strategy=args.strategy,
+               ring="serial" if (args.serial or world == 1) else "overlapped",
                H=H, Hkv=Hkv, D=D, ms=round(ms, 3), tflops_total=round(fl_total / ms / 1e9, 1),
                tflops_per_gpu=round(fl_total / ms / 1e9 / world, 1),
                nvlink_gbs_per_gpu=round(push_max / ms / 1e6, 1),
@@ -353,6 +360,9 @@ def main(argv=None):
     ap.add_argument("--kv-heads", type=int, default=8)
     ap.add_argument("--head-dim", type=int, default=128)
     ap.add_argument("--compare", action="store_true", help="also time the NCCL send/recv ring restatement")
+    ap.add_argument("--serial", action="store_true",
+                    help="ring: the serial ring (push, wait for every rank, attend) instead of the "
+                         "overlapped ring inside the attention kernel")
     ap.add_argument("--compare-max-seq", type=int, default=131072)
     args = ap.parse_args(argv)
     pk = peaks()
