@@ -387,6 +387,33 @@ def cmd_perf_summary(args) -> int:
                 ledger[key]["events"] += 1
     out = {name: {"count": counts[name], **{k: v / counts[name] for k, v in fields.items()}}
            for name, fields in agg.items()}
+    if getattr(args, "by_domain", False):
+        # per rank: the mean of every numeric field of each event, and per field the spread
+        # between the slowest and the fastest rank (max - min of the per-rank means)
+        per = collections.defaultdict(lambda: collections.defaultdict(float))
+        cnt = collections.Counter()
+        for path in args.path:
+            for line in open(path):
+                try:
+                    ev = json.loads(line)
+                except json.JSONDecodeError:
+                    continue
+                key = (ev.get("event", "?"), ev.get("domain", ev.get("rank", "?")))
+                cnt[key] += 1
+                for k, v in ev.items():
+                    if isinstance(v, (int, float)) and not isinstance(v, bool) and \
+                            k not in ("ts", "layer", "domain", "rank"):
+                        per[key][k] += v
+        by = collections.defaultdict(dict)
+        for (name, dom), fields in sorted(per.items(), key=lambda kv: (kv[0][0], str(kv[0][1]))):
+            by[name][str(dom)] = {"count": cnt[(name, dom)],
+                                  **{k: v / cnt[(name, dom)] for k, v in fields.items()}}
+        for name, doms in by.items():
+            fields = {k for d in doms.values() for k in d if k != "count"}
+            out.setdefault(name, {})["rank_spread"] = {
+                k: max(d.get(k, 0.0) for d in doms.values()) - min(d.get(k, 0.0) for d in doms.values())
+                for k in sorted(fields)}
+        out["by_domain"] = dict(by)
     if args.ledger:
         out["kv_transport_ledger"] = {k: dict(v) for k, v in sorted(ledger.items())}
     print(json.dumps(out, indent=2))
@@ -492,6 +519,8 @@ def build_parser() -> argparse.ArgumentParser:
     ps.add_argument("path", nargs="+", help="HCP_PERF_LOG JSONL file(s), e.g. one per rank")
     ps.add_argument("--ledger", action="store_true",
                     help="add total KV bytes sent / received per event and rank")
+    ps.add_argument("--by-domain", action="store_true",
+                    help="add per-rank means of every field and the spread between the ranks")
     ps.set_defaults(fn=cmd_perf_summary)
     g = sub.add_parser("gen-prompt")
     g.add_argument("--tokens", type=int, required=True)

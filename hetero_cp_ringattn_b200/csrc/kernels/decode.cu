@@ -396,8 +396,12 @@ template <int D, int G>
 __global__ void __launch_bounds__(128) decode_attn_kernel(const __grid_constant__ CUtensorMap tm_kv,
                                                           DecodeAttnArgs a) {
   using C = DecCfg<D>;
+  // Programmatic dependent launch: this kernel starts while the QKV projection (which writes q and
+  // the new token's K/V row n - 1 on its owner rank) is still running. Everything before
+  // pdl_wait() below reads only data no kernel in flight writes: the row lengths and page tables
+  // (copied from the host before the step) and the KV rows of earlier tokens, so the first
+  // pipeline stages stream while the projection finishes.
   pdl_trigger();
-  pdl_wait();
   constexpr int NW = 4;                    // warps per CTA
   constexpr int CC = kDecCC;
   constexpr int DQ = D / 4;                // contiguous dims of a K row per lane in S = Q K^T
@@ -464,10 +468,14 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(const __grid_constant_
     }
   };
   const bool producer = threadIdx.x == 0;
+  int pre = 0;   // chunks issued before the dependency wait: those that end before row n - 1
   if (producer) {
     tma_prefetch_desc(&tm_kv);
-    for (int c = 0; c < C::STAGES - 1 && c < nc; ++c) issue(c);
+    while (pre < C::STAGES - 1 && pre < nc && s0 + (pre + 1) * CC <= n - 1) issue(pre++);
   }
+  pdl_wait();
+  if (producer)
+    for (int c = pre; c < C::STAGES - 1 && c < nc; ++c) issue(c);
 
   // q fragments (A of S = Q K^T): row g = head g of the group, pre-scaled into the log2 domain;
   // k-step ks, lane t covers dims t * DQ + 4 ks + {0, 1} (a0) and + {2, 3} (a2)

@@ -123,3 +123,19 @@ def test_perf_summary_ledger_over_rank_files(tmp_path, capsys):
     assert led["ring_attention/domain-0"]["events"] == 3
     assert led["stationary_decode/domain-0"] == {"wire_sent_bytes": 8, "events": 1}
     assert out["ring_attention"]["count"] == 6
+
+
+def test_perf_summary_by_domain_spread(tmp_path, capsys):
+    """--by-domain: per-rank means of every field and the slowest-minus-fastest spread."""
+    p = tmp_path / "perf.jsonl"
+    log = PerfLog(str(p))
+    for r, ms in [(0, 1.0), (1, 3.0)]:
+        for i in range(2):
+            log.emit("ring_attention", domain=r, layer=i, local_compute_ms=ms + i, mlp_ms=0.5)
+    assert main(["perf-summary", str(p), "--by-domain"]) == 0
+    out = json.loads(capsys.readouterr().out)
+    by = out["by_domain"]["ring_attention"]
+    assert by["0"]["local_compute_ms"] == 1.5 and by["1"]["local_compute_ms"] == 3.5
+    assert by["1"]["count"] == 2
+    assert out["ring_attention"]["rank_spread"]["local_compute_ms"] == 2.0
+    assert out["ring_attention"]["rank_spread"]["mlp_ms"] == 0.0
