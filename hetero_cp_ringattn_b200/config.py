@@ -343,9 +343,10 @@ class EnvConfig:
     perf_log: Optional[str] = None          # HCP_PERF_LOG: JSONL perf events
     micro_kv_block_size: int = 0            # HCP_MICRO_KV_BLOCK_SIZE: host-path ring fold block
                                             # (0 -> 128, the CUDA kernels' fixed KV tile)
-    disable_overlap: bool = False           # HCP_DISABLE_OVERLAP=1: serial ring (push every
-                                            # rank's KV, wait for all, then attend) instead of the
-                                            # overlapped in-kernel ring
+    disable_overlap: Optional[bool] = None  # HCP_DISABLE_OVERLAP=1: serial ring (push every
+                                            # rank's KV, wait for all, then attend); =0: the
+                                            # overlapped in-kernel ring; unset: chosen per world
+                                            # size by the engine
     decode_ring: bool = True                # HCP_RING_DECODE_RING=0: legacy KV re-send decode
                                             # (host path; CUDA ranks warn and keep the exchange)
     decode_sd: bool = True                  # HCP_RING_DECODE_SD: capacity-scheduled KV growth;
@@ -369,7 +370,8 @@ class EnvConfig:
         return cls(
             perf_log=os.environ.get("HCP_PERF_LOG") or None,
             micro_kv_block_size=_env_int("HCP_MICRO_KV_BLOCK_SIZE", 0),
-            disable_overlap=_env_bool("HCP_DISABLE_OVERLAP", False),
+            disable_overlap=(_env_bool("HCP_DISABLE_OVERLAP", False)
+                             if os.environ.get("HCP_DISABLE_OVERLAP") else None),
             decode_ring=_env_bool("HCP_RING_DECODE_RING", True),
             decode_sd=_env_bool("HCP_RING_DECODE_SD", True),
             kv_block_table=_env_bool("HCP_KV_CACHE_BLOCK_TABLE", True),

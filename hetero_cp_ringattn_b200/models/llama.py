@@ -136,10 +136,17 @@ class LlamaCPEngine:
         self.scale = 1.0 / math.sqrt(self.D)
         self.use_graphs = use_graphs and self.cuda
         self.perf = perf_log or PerfLog.from_env(self.env)
-        # overlapped ring (default with several ranks): the attention kernel pushes this rank's
-        # K/V rows to the peers and waits per tile; HCP_DISABLE_OVERLAP=1 selects the serial ring
-        # (push everything, wait for every rank, then attend), as the reference's switch does
-        self.overlap = world > 1 and not self.env.disable_overlap
+        # overlapped ring: the attention kernel pushes this rank's K/V rows to the peers and waits
+        # per tile; serial ring: push everything, wait for every rank, then attend. Measured on
+        # B200 (Llama-3.2-1B shape, 32k): overlapped is faster on 2 ranks (TTFT 76.4 vs 77.5 ms),
+        # serial on 8 (22.98 vs 23.91 ms: each rank pushes 58 MB, and the first CTAs run out of
+        # own tiles long before two pusher warps per SM have delivered the remote ones), so the
+        # default switches at 3 ranks; HCP_DISABLE_OVERLAP=1 / =0 (the reference's switch) forces
+        # the serial / overlapped ring
+        if self.env.disable_overlap is None:
+            self.overlap = 1 < world <= 2
+        else:
+            self.overlap = world > 1 and not self.env.disable_overlap
         # fused QKV projection (RoPE + Q / arena / staging writes in the GEMM epilogue): faster on
         # one rank (+2% prefill) and in the overlapped ring, where the epilogue writes only the
         # local staging buffer; the serial ring keeps the separate push kernel, which spreads the

@@ -116,13 +116,19 @@ def _check(r):
     assert int(torch.argmax(cp_logits[0])) == int(torch.argmax(oracle[0]))
     # decode (same inputs): per-rank partials combined in rank order instead of per-split ones,
     # so the sums round differently; the CP pipeline must be as close to the fp32 oracle as the
-    # single-GPU pipeline is, step by step, and pick the same greedy tokens
+    # single-GPU pipeline is, step by step, and pick the same greedy token unless the two tokens
+    # are tied within the pipelines' error against the oracle
+    assert cp_toks[0] == one_toks[0]
     for i in range(1, len(cp_logits)):
         err_cp = (cp_logits[i] - oracle[i]).abs()
         err_one = (one_logits[i] - oracle[i]).abs()
         assert err_cp.mean() <= 1.25 * err_one.mean() + 1e-3, f"decode step {i}"
         assert err_cp.max() <= 0.15, f"decode step {i}"
-    assert cp_toks == one_toks
+        a, b = cp_toks[i], one_toks[i]
+        if a != b:
+            margin = abs(float(oracle[i][a] - oracle[i][b]))
+            assert margin <= float(err_cp.max() + err_one.max()), \
+                f"decode step {i}: tokens {a} / {b} differ by {margin} in the fp32 oracle"
 
 
 @pytest.mark.parametrize("chunks,strategy", [([1536, 1536], "vanilla"), ([2048, 1024], "zigzag"),
