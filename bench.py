@@ -292,7 +292,8 @@ def secondary_configs(world):
     return out
 
 
-def run_secondary(cid, name, ratio, batches, rank, world, dev, group, barrier, req, max_over):
+def run_secondary(cid, name, ratio, batches, rank, world, dev, group, barrier, req, max_over,
+                  local_rank=0):
     from hetero_cp_ringattn_b200.config import parse_ratio, preset
     from hetero_cp_ringattn_b200.models.weights import PreparedWeights
     from hetero_cp_ringattn_b200.parallel.capacity import chunks_from_ratio, equal_chunks
@@ -306,10 +307,15 @@ def run_secondary(cid, name, ratio, batches, rank, world, dev, group, barrier, r
     eng = _engine(cfg, weights, rank, world, dev, group, chunks, new_tokens, B, True)
     prompt = torch.randint(0, cfg.vocab_size, (Lp,), generator=torch.Generator().manual_seed(99))
     prompt_dev = prompt.to(dev)
-    pre, dec, _ = measure_requests(eng, prompt_dev, chunks, strategy, new_tokens, 1, 1, barrier, req)
+    from hetero_cp_ringattn_b200.utils.perf import ClockSampler
+    with ClockSampler(local_rank) as clocks:
+        pre, dec, _ = measure_requests(eng, prompt_dev, chunks, strategy, new_tokens, 2, 1,
+                                       barrier, req)
     pre, dec = max_over(pre), max_over(dec)
     res = {"config": cid, "model": spec["model"], "seq_len": Lp, "chunks": chunks,
-           "ratio": ratio or "equal", "strategy": strategy, "steps": 1, "warmup": 1,
+           "ratio": ratio or "equal", "strategy": strategy, "steps": 2, "warmup": 1,
+           "ring": "single rank" if world == 1 else ("overlapped" if eng.overlap else "serial"),
+           "clocks": clocks.summary(),
            "prefill_tok_s": Lp / (pre / 1e3), "ttft_ms": pre,
            "decode_ms_per_token": dec / max(1, new_tokens - 1),
            "decode_tok_s": (new_tokens - 1) / (dec / 1e3), "new_tokens": new_tokens}
@@ -449,7 +455,7 @@ def main():
     if not args.no_secondary:
         for cid, name, ratio, batches in secondary_configs(world):
             secondary.append(run_secondary(cid, name, ratio, batches, rank, world, dev, group,
-                                           barrier, req, max_over))
+                                           barrier, req, max_over, local_rank))
 
     clk = clocks.summary()
     value = Lp / (prefill_ms / 1e3)
