@@ -365,6 +365,7 @@ const char* gemv(const GemvArgs& a, cudaStream_t s) {
 // the end; the 4 warps are merged through shared memory and the split's (O, LSE) partial written.
 constexpr int kDecCC = 64;   // tokens per chunk (one TMA box of rows)
 constexpr int kDecWR = 16;   // rows of a chunk per warp (two 8-token MMA n-tiles)
+constexpr int kDecMinChunks = 4;  // chunks a split streams at least (fewer active splits)
 
 template <int D>
 struct DecCfg {
@@ -425,8 +426,14 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(const __grid_constant_
       report_error(a.status, int(StatusCode::kOutOfBounds), 304, n, b);
     n = n < 0 ? 0 : n_cap;
   }
+  // active splits: as many as the launch has, but each streams at least kDecMinChunks chunks
+  // (a short local shard, e.g. a rank's part at high CP, would otherwise give every split a
+  // single chunk and pay the pipeline latency and the split combine for nothing); the CTAs of
+  // the other splits exit here
+  const int eff = max(1, min(a.splits, (n + kDecMinChunks * CC - 1) / (kDecMinChunks * CC)));
+  if (split >= eff) return;
   // chunk-aligned split ranges
-  int per = (n + a.splits - 1) / a.splits;
+  int per = (n + eff - 1) / eff;
   per = (per + CC - 1) / CC * CC;
   const int s0 = min(n, split * per);
   const int s1 = min(n, s0 + per);
@@ -653,7 +660,7 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(const __grid_constant_
   if (threadIdx.x == 0) {
     __threadfence();
     const unsigned prev = atomicAdd(a.split_counter + b * a.Hkv + h, 1u);
-    is_last = (prev == unsigned(a.splits) - 1);
+    is_last = (prev == unsigned(eff) - 1);
   }
   __syncthreads();
   if (!is_last) return;
@@ -665,17 +672,17 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(const __grid_constant_
   // visible after the fence + counter), then one warp per head reduces max and weight sum
   __shared__ float s_w[G][kMaxDecodeSplits];
   __shared__ float s_mx[G], s_ws[G];
-  for (int i = threadIdx.x; i < G * a.splits; i += blockDim.x) {
-    const int g = i / a.splits, s = i % a.splits;
+  for (int i = threadIdx.x; i < G * eff; i += blockDim.x) {
+    const int g = i / eff, s = i % eff;
     s_w[g][s] = __ldcg(a.part_lse + (long)(b * H + h * G + g) * a.splits + s);
   }
   __syncthreads();
   for (int g = warp; g < G; g += 4) {
     float mx = -INFINITY;
-    for (int s = lane; s < a.splits; s += 32) mx = fmaxf(mx, s_w[g][s]);
+    for (int s = lane; s < eff; s += 32) mx = fmaxf(mx, s_w[g][s]);
     mx = warp_max(mx);
     float ws = 0.f;
-    for (int s = lane; s < a.splits; s += 32) {
+    for (int s = lane; s < eff; s += 32) {
       const float w = mx == -INFINITY ? 0.f : fast_exp2(s_w[g][s] - mx);
       s_w[g][s] = w;
       ws += w;
@@ -695,14 +702,14 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(const __grid_constant_
     float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
     if (s_mx[g] != -INFINITY) {
       const float4* pof = reinterpret_cast<const float4*>(a.part_o + (long)(b * H + h * G + g) * a.splits * D) + d4;
-      for (int s0 = 0; s0 < a.splits; s0 += 16) {
+      for (int s0 = 0; s0 < eff; s0 += 16) {
         float4 v[16];
 #pragma unroll
         for (int j = 0; j < 16; ++j)
-          v[j] = (s0 + j < a.splits) ? __ldcg(pof + (long)(s0 + j) * (D / 4)) : make_float4(0.f, 0.f, 0.f, 0.f);
+          v[j] = (s0 + j < eff) ? __ldcg(pof + (long)(s0 + j) * (D / 4)) : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
-          if (s0 + j < a.splits) {
+          if (s0 + j < eff) {
             const float w = s_w[g][s0 + j];
             o.x = fmaf(w, v[j].x, o.x);
             o.y = fmaf(w, v[j].y, o.y);
