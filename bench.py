@@ -158,7 +158,7 @@ def measure_requests(eng, prompt_dev, chunks, strategy, new_tokens, steps, warmu
         e1.record()
         cur = tok
         for _ in range(new_tokens - 1):
-            cur = eng.decode_step([req[0]], cur)
+            cur = eng.decode_step([req[0]], cur, logits=False)
         e2.record()
         eng.release(req[0])
         torch.cuda.synchronize()
@@ -190,13 +190,13 @@ def measure_batch_decode(eng, prompt_dev, chunks, strategy, new_tokens, B, barri
         toks.append(tok.view(1))
     cur = torch.cat(toks)
     for _ in range(3):
-        cur = eng.decode_step(ids, cur)
+        cur = eng.decode_step(ids, cur, logits=False)
     barrier()
     b0, b1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     n_dec = new_tokens - 4
     b0.record()
     for _ in range(n_dec):
-        cur = eng.decode_step(ids, cur)
+        cur = eng.decode_step(ids, cur, logits=False)
     b1.record()
     barrier()
     for i in ids:
@@ -227,14 +227,15 @@ def correctness_check(model, rank, world, dev, group, strategy, ratio, barrier):
     w = PreparedWeights.from_weights(hf)
     prompt = torch.randint(0, cfg.vocab_size, (L,), generator=torch.Generator().manual_seed(5))
 
-    def run(eng, ch, strat, forced=None):
+    def run(eng, ch, strat, forced=None, keep_logits=True):
         tok, logits = eng.prefill(7, prompt, ch, strat, decode_horizon=steps + 1, return_logits=True)
         toks, step_logits, cur = [int(tok)], [logits.float()], tok
         for i in range(steps):
             inp = cur if forced is None else torch.tensor([forced[i]], device=dev)
-            cur = eng.decode_step([7], inp)
+            cur = eng.decode_step([7], inp, logits=keep_logits)
             toks.append(int(cur))
-            step_logits.append(eng.last_logits(1)[0].float().clone())
+            if keep_logits:
+                step_logits.append(eng.last_logits(1)[0].float().clone())
         eng.release(7)
         eng.check_device()
         return toks, step_logits
@@ -250,6 +251,9 @@ def correctness_check(model, rank, world, dev, group, strategy, ratio, barrier):
     eng = LlamaCPEngine(cfg, w, rank=rank, world=world, device=dev, group=group, max_context=L,
                         max_batch=1, decode_reserve=16)
     cp_toks, cp_logits = run(eng, chunks, strategy, forced=single.tolist())
+    # the timed decode's greedy steps (LM head split over the ranks' vocabulary slices on
+    # several ranks) on the same inputs: the same tokens as the whole head, bit for bit
+    split_toks, _ = run(eng, chunks, strategy, forced=single.tolist(), keep_logits=False)
     eng.close()
     out = None
     if rank == 0:
@@ -267,6 +271,7 @@ def correctness_check(model, rank, world, dev, group, strategy, ratio, barrier):
                "single_gpu_max_abs_err_vs_fp32": float((one_logits[0] - oracle[0]).abs().max()),
                "decode_mean_abs_err_vs_fp32": {"cp": max(cp_err[1:]), "one_gpu": max(one_err[1:])},
                "tokens_match": cp_toks == one_toks,
+               "greedy_head_tokens_match": split_toks == cp_toks,
                "token_flips_at_near_ties_only": all(
                    a == b or abs(float(o[a] - o[b])) <= float((c - o).abs().max() + (u - o).abs().max())
                    for a, b, o, c, u in zip(cp_toks, one_toks, oracle, cp_logits, one_logits)),
@@ -275,6 +280,7 @@ def correctness_check(model, rank, world, dev, group, strategy, ratio, barrier):
                          "as close to the fp32 oracle as one GPU (mean abs err <= 1.25x + 1e-3); "
                          "the same first token, later tokens equal or tied within the error"}
         out["pass"] = bool(cp_toks[0] == one_toks[0] and out["token_flips_at_near_ties_only"] and
+                           split_toks == cp_toks and
                            diff[0] <= 2e-2 and
                            all(c <= 1.25 * o + 1e-3 for c, o in zip(cp_err[1:], one_err[1:])))
     del w, hf
@@ -417,7 +423,7 @@ def main():
             cur = tok
             outs = [tok]
             for _ in range(new_tokens - 1):
-                cur = eng.decode_step([req[0]], cur)
+                cur = eng.decode_step([req[0]], cur, logits=False)
                 outs.append(cur.view(1))
             gen_ids = torch.cat(outs).cpu()  # device -> host read of the generated tokens
             t2 = time.perf_counter()

@@ -195,13 +195,13 @@ def bench_decode(args, dev, pk):
     tok, _ = eng.prefill(1, prompt, [ctx], decode_horizon=args.iters + 8)
     cur = tok
     for _ in range(3):
-        cur = eng.decode_step([1], cur)
+        cur = eng.decode_step([1], cur, logits=False)
     torch.cuda.synchronize()
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     n = args.iters
     s.record()
     for _ in range(n):
-        cur = eng.decode_step([1], cur)
+        cur = eng.decode_step([1], cur, logits=False)
     e.record()
     e.synchronize()
     ms = s.elapsed_time(e) / n

@@ -364,6 +364,10 @@ class EnvConfig:
     fused_qkv: Optional[bool] = None        # HCP_FUSED_QKV: the projection GEMM's epilogue does
                                             # RoPE + the K/V writes (default on; 0: GEMM + a
                                             # separate RoPE / K/V kernel)
+    split_lm_head: bool = True              # HCP_SPLIT_LM_HEAD=0: every rank runs the whole LM
+                                            # head in greedy decode steps (default: each rank
+                                            # takes 1/N of the vocabulary and the ranks exchange
+                                            # their packed argmax over NVLink)
 
     @classmethod
     def from_env(cls) -> "EnvConfig":
@@ -382,6 +386,7 @@ class EnvConfig:
             nvtx=_env_bool("HCP_NVTX", False),
             decode_kernel_combine=_env_bool("HCP_DECODE_KERNEL_COMBINE", False),
             fused_qkv=(_env_bool("HCP_FUSED_QKV", True) if os.environ.get("HCP_FUSED_QKV") else None),
+            split_lm_head=_env_bool("HCP_SPLIT_LM_HEAD", True),
         )
 
 

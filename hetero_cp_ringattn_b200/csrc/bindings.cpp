@@ -147,7 +147,8 @@ void rmsnorm(torch::Tensor x, torch::Tensor w, torch::Tensor y, double eps) {
 
 void gemv(torch::Tensor x, torch::Tensor W, int64_t epi, c10::optional<torch::Tensor> bias,
           c10::optional<torch::Tensor> y_f32, c10::optional<torch::Tensor> y_bf16,
-          c10::optional<torch::Tensor> argmax, c10::optional<torch::Tensor> norm_w, double eps) {
+          c10::optional<torch::Tensor> argmax, c10::optional<torch::Tensor> norm_w, double eps,
+          int64_t index_base) {
   check_cuda_bf16(x, "x");
   check_cuda_bf16(W, "W");
   const c10::cuda::CUDAGuard g(x.device());
@@ -166,6 +167,8 @@ void gemv(torch::Tensor x, torch::Tensor W, int64_t epi, c10::optional<torch::Te
   if (y_f32.has_value() && y_f32->defined()) a.ldy = y_f32->stride(0);
   else if (y_bf16.has_value() && y_bf16->defined()) a.ldy = y_bf16->stride(0);
   a.argmax = ptr_or_null<unsigned long long>(argmax);
+  a.index_base = int(index_base);
+  TORCH_CHECK(index_base >= 0 && index_base + a.N < (int64_t(1) << 31), "index_base out of range");
   a.num_sms = sm_count(x.get_device());
   a.norm_w = ptr_or_null<const __nv_bfloat16>(norm_w);
   a.eps = float(eps);
@@ -414,6 +417,24 @@ class PyRuntime {
     TORCH_CHECK(st.ok(), "broadcast_token: ", st.ToString());
   }
 
+  void argmax_exchange(torch::Tensor local, torch::Tensor epoch_src, c10::optional<torch::Tensor> tok32,
+                       c10::optional<torch::Tensor> tok64) {
+    TORCH_CHECK(local.is_cuda() && local.element_size() == 8 && local.is_contiguous(),
+                "local must be a contiguous CUDA 64-bit tensor");
+    TORCH_CHECK(epoch_src.is_cuda() && epoch_src.element_size() == 8, "epoch_src must be a CUDA 64-bit tensor");
+    const int B = int(local.numel());
+    if (tok32.has_value() && tok32->defined())
+      TORCH_CHECK(tok32->is_cuda() && tok32->scalar_type() == torch::kInt32 && tok32->numel() >= B, "tok32 [B] int32");
+    if (tok64.has_value() && tok64->defined())
+      TORCH_CHECK(tok64->is_cuda() && tok64->scalar_type() == torch::kInt64 && tok64->numel() >= B, "tok64 [B] int64");
+    const c10::cuda::CUDAGuard g(local.device());
+    auto st = rt_.ArgmaxExchange(reinterpret_cast<const unsigned long long*>(local.data_ptr()), B,
+                                 ptr_or_null<int>(tok32), ptr_or_null<long long>(tok64),
+                                 reinterpret_cast<const unsigned long long*>(epoch_src.data_ptr()),
+                                 cur_stream());
+    TORCH_CHECK(st.ok(), "argmax_exchange: ", st.ToString());
+  }
+
   void qkv_decode(torch::Tensor qkv_f32, torch::Tensor pos, torch::Tensor cos_t, torch::Tensor sin_t,
                   int64_t layer, torch::Tensor page_tables, torch::Tensor owner, torch::Tensor slot,
                   torch::Tensor q_out) {
@@ -608,6 +629,12 @@ class PyRuntime {
     auto opts = torch::TensorOptions().dtype(torch::kInt64).device(torch::kCUDA, c.device);
     return torch::from_blob(rt_.flags(), {hcp::kFlagWords}, opts);
   }
+  // The greedy-argmax exchange slots [2 parity][world source][max_batch][value, epoch].
+  torch::Tensor argmax_slots() {
+    const auto& c = rt_.config();
+    auto opts = torch::TensorOptions().dtype(torch::kInt64).device(torch::kCUDA, c.device);
+    return torch::from_blob(rt_.argmax_slots(), {2, c.world, c.max_batch, 2}, opts);
+  }
   torch::Tensor status_words() {
     const auto& c = rt_.config();
     auto opts = torch::TensorOptions().dtype(torch::kInt32).device(torch::kCUDA, c.device);
@@ -638,7 +665,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("rmsnorm", &rmsnorm);
   m.def("gemv", &gemv, py::arg("x"), py::arg("W"), py::arg("epi"), py::arg("bias") = py::none(),
         py::arg("y_f32") = py::none(), py::arg("y_bf16") = py::none(), py::arg("argmax") = py::none(),
-        py::arg("norm_w") = py::none(), py::arg("eps") = 1e-6);
+        py::arg("norm_w") = py::none(), py::arg("eps") = 1e-6, py::arg("index_base") = 0);
   m.def("fill_u64", &fill_u64);
   m.def("argmax_finalize", &argmax_finalize, py::arg("packed"), py::arg("tok32") = py::none(),
         py::arg("tok64") = py::none());
@@ -681,6 +708,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
            py::arg("existing_slot_pos") = py::none(), py::arg("tile_src") = py::none(), py::arg("push_tiles") = py::none())
       .def("publish_tiles", &PyRuntime::publish_tiles, py::arg("push_tiles"), py::arg("epoch"))
       .def("broadcast_token", &PyRuntime::broadcast_token, py::arg("tok"), py::arg("src"), py::arg("epoch"))
+      .def("argmax_exchange", &PyRuntime::argmax_exchange, py::arg("local"), py::arg("epoch_src"),
+           py::arg("tok32") = py::none(), py::arg("tok64") = py::none())
       .def("publish_decode_groups", &PyRuntime::publish_decode_groups, py::arg("B"), py::arg("epoch"))
       .def("qkv_decode", &PyRuntime::qkv_decode)
       .def("decode_attn", &PyRuntime::decode_attn, py::arg("q"), py::arg("layer"), py::arg("page_tables"),
@@ -693,6 +722,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       .def("arena", &PyRuntime::arena)
       .def("stage", &PyRuntime::stage)
       .def("flags", &PyRuntime::flags)
+      .def("argmax_slots", &PyRuntime::argmax_slots)
       .def("status_words", &PyRuntime::status_words)
       .def("check", &PyRuntime::check)
       .def("shutdown", &PyRuntime::shutdown)

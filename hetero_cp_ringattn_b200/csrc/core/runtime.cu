@@ -5,6 +5,7 @@
 #include <cstring>
 
 #include "../kernels/attn_fwd_sm100.h"
+#include "../kernels/decode.h"
 #include "../kernels/elementwise.h"
 #include "../kernels/gemm_sm100.h"
 
@@ -43,7 +44,9 @@ Status DomainRuntime::Init(const RuntimeConfig& cfg) {
   tflag_parity_bytes_ = align_up(tiles * cfg.world * sizeof(unsigned long long), 256);
   off_gflags_ = align_up(off_tflags_ + 2 * tflag_parity_bytes_, 256);
   const size_t gflag_bytes = size_t(cfg.world) * cfg.max_batch * cfg.geom.hkv * sizeof(unsigned long long);
-  off_xslot_ = align_up(off_gflags_ + gflag_bytes, 4096);
+  off_aslot_ = align_up(off_gflags_ + gflag_bytes, 256);
+  const size_t aslot_bytes = size_t(2) * cfg.world * cfg.max_batch * 2 * sizeof(unsigned long long);
+  off_xslot_ = align_up(off_aslot_ + aslot_bytes, 4096);
   xslot_bytes_ = size_t(2) * cfg.world * cfg.max_batch * cfg.num_heads * (cfg.geom.d + 1) * sizeof(float);
   off_stage_ = align_up(off_xslot_ + xslot_bytes_, 4096);
   stage_parity_bytes_ = size_t(2) * cfg.geom.hkv * size_t(cfg.stage_cap) * cfg.geom.d * 2;
@@ -115,7 +118,8 @@ Status DomainRuntime::OpenPeersLocal(const std::vector<DomainRuntime*>& peers) {
 Status DomainRuntime::BuildTables() {
   const int n = cfg_.world;
   std::vector<void*> st0(n), st1(n);
-  std::vector<unsigned long long*> ready(n), consumed(n), dready(n), tf0(n), tf1(n), tok(n), gf(n);
+  std::vector<unsigned long long*> ready(n), consumed(n), dready(n), tf0(n), tf1(n), tok(n), gf(n),
+      as(n);
   std::vector<float*> xs(n);
   for (int r = 0; r < n; ++r) {
     uint8_t* b = peer_base_[r];
@@ -128,6 +132,7 @@ Status DomainRuntime::BuildTables() {
     dready[r] = fl + kFlagDecReady + cfg_.rank;
     tok[r] = fl + kFlagToken;
     gf[r] = reinterpret_cast<unsigned long long*>(b + off_gflags_);
+    as[r] = reinterpret_cast<unsigned long long*>(b + off_aslot_);
     tf0[r] = reinterpret_cast<unsigned long long*>(b + off_tflags_);
     tf1[r] = reinterpret_cast<unsigned long long*>(b + off_tflags_ + tflag_parity_bytes_);
     xs[r] = reinterpret_cast<float*>(b + off_xslot_);
@@ -151,6 +156,7 @@ Status DomainRuntime::BuildTables() {
   if (!(s = alloc_copy(reinterpret_cast<void**>(&tflag_tab_[1]), tf1.data(), pb)).ok()) return s;
   if (!(s = alloc_copy(reinterpret_cast<void**>(&token_tab_), tok.data(), pb)).ok()) return s;
   if (!(s = alloc_copy(reinterpret_cast<void**>(&gflag_tab_), gf.data(), pb)).ok()) return s;
+  if (!(s = alloc_copy(reinterpret_cast<void**>(&aslot_tab_), as.data(), pb)).ok()) return s;
   return Status::Ok();
 }
 
@@ -352,6 +358,28 @@ Status DomainRuntime::BroadcastToken(long long* tok, int src, uint64_t epoch, cu
   return e ? Status::Internal(e) : Status::Ok();
 }
 
+Status DomainRuntime::ArgmaxExchange(const unsigned long long* local, int B, int* tok32,
+                                     long long* tok64, const unsigned long long* epoch_src,
+                                     cudaStream_t stream) {
+  if (base_ == nullptr || aslot_tab_ == nullptr) return Status::InvalidArgument("runtime not ready");
+  if (B < 1 || B > cfg_.max_batch) return Status::InvalidArgument("argmax exchange: rows out of range");
+  dec::ArgmaxXchgArgs a{};
+  a.local = local;
+  a.B = B;
+  a.slot_ptrs = aslot_tab_;
+  a.own_slots = argmax_slots();
+  a.world = cfg_.world;
+  a.my_rank = cfg_.rank;
+  a.max_batch = cfg_.max_batch;
+  a.epoch_src = epoch_src;
+  a.tok32 = tok32;
+  a.tok64 = tok64;
+  a.budget_ns = cfg_.peer_wait_budget_ns;
+  a.status = status_;
+  const char* e = dec::argmax_exchange(a, stream);
+  return e ? Status::Internal(e) : Status::Ok();
+}
+
 Status DomainRuntime::CheckDevice(cudaStream_t stream) {
   if (status_ == nullptr) return Status::Ok();
   auto st = cuda_status(cudaStreamSynchronize(stream), "cudaStreamSynchronize");
@@ -379,12 +407,14 @@ Status DomainRuntime::Shutdown() {
                   static_cast<void*>(kv_ready_tab_), static_cast<void*>(consumed_tab_),
                   static_cast<void*>(dec_ready_tab_), static_cast<void*>(xslot_tab_),
                   static_cast<void*>(tflag_tab_[0]), static_cast<void*>(tflag_tab_[1]),
-                  static_cast<void*>(token_tab_), static_cast<void*>(gflag_tab_)})
+                  static_cast<void*>(token_tab_), static_cast<void*>(gflag_tab_),
+                  static_cast<void*>(aslot_tab_)})
     if (t) cudaFree(t);
   stage_tab_[0] = stage_tab_[1] = nullptr;
   tflag_tab_[0] = tflag_tab_[1] = nullptr;
   token_tab_ = nullptr;
   gflag_tab_ = nullptr;
+  aslot_tab_ = nullptr;
   kv_ready_tab_ = consumed_tab_ = dec_ready_tab_ = nullptr;
   xslot_tab_ = nullptr;
   if (status_) cudaFree(status_);

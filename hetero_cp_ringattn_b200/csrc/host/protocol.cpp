@@ -22,7 +22,7 @@ constexpr Schema kSchemas[] = {
     {1, "iAAsiObb"},   // Prefill: request_id, prompt, chunks, strategy, decode_horizon,
                        //          capacity_tickets?, keep_kv, want_logits
     {2, "ii"},         // Decode: request_id, token
-    {3, "P"},          // DecodeBatch: (request_id, token) rows
+    {3, "Pb"},         // DecodeBatch: (request_id, token) rows, want_logits
     {4, "iAAAiib"},    // StationaryContinuation: request_id, tokens, position_ids, tickets, starter,
                        //                         decode_horizon, want_logits
     {5, "iiiAiii"},    // StationaryDecode: request_id, token, position, tickets, starter,

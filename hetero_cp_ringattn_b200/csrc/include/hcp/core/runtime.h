@@ -11,6 +11,7 @@
 //   flags     uint64[kFlagWords]                           (kv_ready / consumed / dec_ready / ...)
 //   tflags    uint64[2][ceil(stage_cap / 128)][world]      per-(KV tile, source rank) ready epochs
 //   gflags    uint64[world][max_batch][Hkv]                decode (O, LSE) per-(source, row, KV head)
+//   aslot     uint64[2][world][max_batch][2]               greedy argmax exchange (value, epoch)
 //   xslot     fp32 [2][world][max_batch][H][D+1]          decode (O, LSE) exchange slots
 //   stage     bf16 [2 parity][2 K/V][Hkv][stage_cap][D]   position-ordered prefill KV
 //   arena     bf16 [layers][pages][2][Hkv][page][D]       paged KV cache shard
@@ -109,6 +110,12 @@ class DomainRuntime {
   // (value, then a release of `epoch`); every other rank waits (bounded) for `epoch` in its own
   // slot and copies the value into `tok`. All on the device, no host round trip.
   Status BroadcastToken(long long* tok, int src, uint64_t epoch, cudaStream_t stream);
+  // Greedy decode with the LM head split over the vocabulary: `local` [B] holds this rank's packed
+  // (value, index) maxima; the tokens of the whole vocabulary's argmax go to tok32 / tok64 [B]
+  // (either may be null) on every rank. epoch = *epoch_src, the decode step counter (>= 1, the
+  // same on every rank); the slots are double-buffered on its parity.
+  Status ArgmaxExchange(const unsigned long long* local, int B, int* tok32, long long* tok64,
+                        const unsigned long long* epoch_src, cudaStream_t stream);
   Status Shutdown();
 
   // Reads and clears the device status words (synchronises the given stream first).
@@ -123,6 +130,9 @@ class DomainRuntime {
     return reinterpret_cast<unsigned long long*>(base_ + off_gflags_);
   }
   unsigned long long* const* group_flag_table() const { return gflag_tab_; }
+  unsigned long long* argmax_slots() const {
+    return reinterpret_cast<unsigned long long*>(base_ + off_aslot_);
+  }
   unsigned long long* tile_flags(int parity) const {
     return reinterpret_cast<unsigned long long*>(base_ + off_tflags_ + size_t(parity) * tflag_parity_bytes_);
   }
@@ -149,7 +159,8 @@ class DomainRuntime {
   RuntimeConfig cfg_{};
   uint8_t* base_ = nullptr;
   size_t region_bytes_ = 0;
-  size_t off_flags_ = 0, off_tflags_ = 0, off_gflags_ = 0, off_xslot_ = 0, off_stage_ = 0, off_arena_ = 0;
+  size_t off_flags_ = 0, off_tflags_ = 0, off_gflags_ = 0, off_aslot_ = 0, off_xslot_ = 0,
+         off_stage_ = 0, off_arena_ = 0;
   size_t tflag_parity_bytes_ = 0;
   size_t xslot_bytes_ = 0, stage_parity_bytes_ = 0, arena_bytes_ = 0;
   int* status_ = nullptr;            // kStatusWords int32
@@ -162,6 +173,7 @@ class DomainRuntime {
   unsigned long long** tflag_tab_[2] = {nullptr, nullptr};
   unsigned long long** token_tab_ = nullptr;
   unsigned long long** gflag_tab_ = nullptr;
+  unsigned long long** aslot_tab_ = nullptr;
   float** xslot_tab_ = nullptr;
   std::vector<uint8_t*> peer_base_;
   std::vector<bool> peer_opened_ipc_;

@@ -183,7 +183,7 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(GemvArgs a) {
     for (int b = 0; b < B; ++b) {
       const float v = acc[0][b];
       if (EPI == kGemvArgmax) {
-        const unsigned long long cnd = pack_argmax(v, o);
+        const unsigned long long cnd = pack_argmax(v, o + a.index_base);
         best[b] = cnd > best[b] ? cnd : best[b];
       }
       if (lane != b) continue;
@@ -941,6 +941,35 @@ __global__ void argmax_finalize_kernel(const unsigned long long* packed, int B, 
   }
 }
 
+// One CTA: thread t < world * B first stores row b = t % B of this rank's maxima into rank
+// t / B's slot [parity][my_rank][b], then reads rank t / B's entry of row b from its own slots.
+// For t / B == my_rank the store and the read are the same thread's, in program order.
+__global__ void argmax_exchange_kernel(ArgmaxXchgArgs a) {
+  pdl_trigger();
+  pdl_wait();
+  __shared__ unsigned long long best[8];
+  const int t = threadIdx.x;
+  const unsigned long long e = *a.epoch_src;
+  const int par = int(e & 1ull);
+  if (t < a.B) best[t] = 0ull;
+  __syncthreads();
+  if (t < a.world * a.B) {
+    const int r = t / a.B, b = t % a.B;
+    unsigned long long* sl = a.slot_ptrs[r] + ((long(par) * a.world + a.my_rank) * a.max_batch + b) * 2;
+    *reinterpret_cast<volatile unsigned long long*>(sl) = a.local[b];
+    st_release_sys(sl + 1, e);   // orders the value store before the epoch
+    const unsigned long long* own = a.own_slots + ((long(par) * a.world + r) * a.max_batch + b) * 2;
+    if (wait_flag_geq_sys(own + 1, e, a.budget_ns, a.status, 306, r))
+      atomicMax(&best[b], *reinterpret_cast<const volatile unsigned long long*>(own));
+  }
+  __syncthreads();
+  if (t < a.B) {
+    const int idx = int(0xFFFFFFFFu - uint32_t(best[t] & 0xFFFFFFFFull));
+    if (a.tok32) a.tok32[t] = idx;
+    if (a.tok64) a.tok64[t] = idx;
+  }
+}
+
 __global__ void add_u64_kernel(unsigned long long* p, unsigned long long v) {
   pdl_trigger();
   pdl_wait();
@@ -955,6 +984,17 @@ const char* fill_u64(unsigned long long* p, int n, unsigned long long v, cudaStr
 const char* argmax_finalize(const unsigned long long* packed, int B, int* tok, long long* tok64,
                             cudaStream_t s) {
   return launch_pdl(argmax_finalize_kernel, dim3(1), dim3(32), 0, s, packed, B, tok, tok64) == cudaSuccess ? nullptr : "argmax_finalize: launch failed";
+}
+
+const char* argmax_exchange(const ArgmaxXchgArgs& a, cudaStream_t s) {
+  if (a.B < 1 || a.B > 8 || a.B > a.max_batch) return "argmax_exchange: B must be in [1, min(8, max_batch)]";
+  if (a.world < 1 || a.world * a.B > 1024 || a.my_rank < 0 || a.my_rank >= a.world)
+    return "argmax_exchange: bad world / rank";
+  if (!a.local || !a.slot_ptrs || !a.own_slots || !a.epoch_src) return "argmax_exchange: null pointer";
+  const int threads = (a.world * a.B + 31) / 32 * 32;
+  return launch_pdl(argmax_exchange_kernel, dim3(1), dim3(threads), 0, s, a) == cudaSuccess
+             ? nullptr
+             : "argmax_exchange: launch failed";
 }
 
 const char* add_u64(unsigned long long* p, unsigned long long v, cudaStream_t s) {

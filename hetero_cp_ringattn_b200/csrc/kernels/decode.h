@@ -51,6 +51,7 @@ struct GemvArgs {
   __nv_bfloat16* y_bf16;
   long ldy;
   unsigned long long* argmax;  // [B] packed (value, index); caller zeroes it
+  int index_base;              // kGemvArgmax: added to the row index (W is a vocabulary slice)
   int num_sms;
   const __nv_bfloat16* norm_w; // optional fused input RMSNorm weight [K]
   float eps;
@@ -105,7 +106,27 @@ struct DecodeCombineArgs {
   int* status;
 };
 
+// Greedy argmax across the ranks of a vocabulary-split LM head: every rank holds the packed
+// (value, index) maximum of its own vocabulary rows per decode row in `local` [B]. Each rank
+// stores its entries into every rank's slots (value, then a release of the epoch), waits
+// (bounded) for every rank's entries in its own slots and writes the largest one's index to
+// tok32 / tok64 [B]. Ties between ranks go to the smaller index, as inside one GEMV, so the token
+// is the full head's argmax.
+struct ArgmaxXchgArgs {
+  const unsigned long long* local;        // [B] this rank's packed maxima
+  int B;                                  // <= 8
+  unsigned long long* const* slot_ptrs;   // device array [world]: rank r's slot base
+  const unsigned long long* own_slots;    // this rank's slot base: [2][world][max_batch][2]
+  int world, my_rank, max_batch;
+  const unsigned long long* epoch_src;    // device step counter; epoch = *epoch_src (>= 1)
+  int* tok32;                             // optional [B]
+  long long* tok64;                       // optional [B]
+  unsigned long long budget_ns;
+  int* status;
+};
+
 const char* gemv(const GemvArgs& a, cudaStream_t s);
+const char* argmax_exchange(const ArgmaxXchgArgs& a, cudaStream_t s);
 const char* decode_attn(const DecodeAttnArgs& a, cudaStream_t s);
 // Resident decode_attn CTAs per SM for (head_dim, GQA group size); 0 when unsupported. Callers
 // size the split count so the grid fills the GPU in one wave.

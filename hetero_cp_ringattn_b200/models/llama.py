@@ -179,7 +179,18 @@ class LlamaCPEngine:
                 dist.barrier(group=group)
             self.dec_step = torch.zeros(1, dtype=torch.int64, device=self.device)
             self._graphs: Dict[int, "DecodeGraph"] = {}
+            self._last_split = False
             self.num_sms = native().num_sms(self.device.index or 0)
+            # greedy decode on several ranks: rank r runs the LM head over vocabulary rows
+            # [vocab_lo, vocab_hi) only and the ranks exchange their packed argmax (the token is
+            # the whole head's argmax, ties to the smaller id); steps that need logits run the
+            # whole head on every rank
+            V = cfg.vocab_size
+            part = -(-V // (world * 8)) * 8
+            self.vocab_lo = min(V, rank * part)
+            self.vocab_hi = min(V, self.vocab_lo + part)
+            self.split_head = world > 1 and self.env.split_lm_head and V - (world - 1) * part > 0
+            self.lm_head_slice = self.w.lm_head[self.vocab_lo:self.vocab_hi]
 
     # ------------------------------------------------------------------ helpers
     def kv_capacity_bytes(self) -> Optional[int]:
@@ -486,9 +497,13 @@ class LlamaCPEngine:
             st.context_len += 1
 
     @torch.no_grad()
-    def decode_step(self, req_ids: Sequence[int], tokens: torch.Tensor) -> torch.Tensor:
+    def decode_step(self, req_ids: Sequence[int], tokens: torch.Tensor,
+                    logits: bool = True) -> torch.Tensor:
         """One greedy decode step for a batch of requests. `tokens` [B] holds each row's last
-        token (int64 or int32, on the engine device). Returns the next tokens [B] (int64)."""
+        token (int64 or int32, on the engine device). Returns the next tokens [B] (int64).
+        `logits=False` promises that `last_logits` is not read for this step: on several ranks
+        each one then runs the LM head over its own slice of the vocabulary only (the same
+        tokens, bit for bit)."""
         B = len(req_ids)
         if B == 0:
             return tokens
@@ -500,7 +515,8 @@ class LlamaCPEngine:
                 ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
                 ev[0].record()
         if self.cuda:
-            out = self._decode_cuda(req_ids, tokens, pos, owner, slot, ntok)
+            out = self._decode_cuda(req_ids, tokens, pos, owner, slot, ntok,
+                                    split=self.split_head and not logits)
         else:
             out = self._decode_host(req_ids, tokens, pos, owner)
         if timing:
@@ -548,14 +564,15 @@ class LlamaCPEngine:
             self._graphs[B] = g
         return g
 
-    def _decode_cuda(self, req_ids, tokens, pos, owner, slot, ntok):
+    def _decode_cuda(self, req_ids, tokens, pos, owner, slot, ntok, split: bool = False):
         B = len(req_ids)
         bucket = 1 if B == 1 else 2 if B == 2 else 4 if B <= 4 else 8
         if B > self.max_batch or bucket > self.max_batch:
             raise CapacityError(f"decode batch {B} exceeds max_batch {self.max_batch}")
         g = self._graph_for(bucket)
         self._last_bucket = bucket
-        return g.run(req_ids, tokens, pos, owner, slot, ntok)
+        self._last_split = split
+        return g.run(req_ids, tokens, pos, owner, slot, ntok, split)
 
     def _decode_host(self, req_ids, tokens, pos, owner):
         w, cfg = self.w, self.cfg
@@ -606,9 +623,10 @@ class LlamaCPEngine:
         return torch.argmax(logits, dim=-1)
 
     def last_logits(self, n: int) -> Optional[torch.Tensor]:
-        """Logits [n, vocab] of the most recent decode step (for non-greedy sampling)."""
+        """Logits [n, vocab] of the most recent decode step (for non-greedy sampling); None
+        after a step run with `logits=False` on several ranks (no rank holds them all)."""
         if self.cuda:
-            if not self._graphs:
+            if not self._graphs or self._last_split:
                 return None
             g = self._graphs.get(self._last_bucket)
             return None if g is None else g.logits[:n]
@@ -761,7 +779,7 @@ class LlamaCPEngine:
         cur = first.view(1)
         try:
             for _ in range(max_new_tokens - 1):
-                cur = self.decode_step([req_id], cur).view(1)
+                cur = self.decode_step([req_id], cur, logits=False).view(1)
                 toks.append(cur)
                 if stop_ids is not None and int(cur) in stop_ids:
                     break
@@ -779,12 +797,16 @@ class LlamaCPEngine:
         prompt = torch.arange(max(8, self.world), dtype=torch.int64) % self.cfg.vocab_size
         for b in sizes:
             self.generate_batch([prompt] * b, 2, first_id=(1 << 40) + 16 * b)
+            if self.cuda and self.split_head:   # the logits-keeping graph (sampled requests)
+                self.generate_batch([prompt] * b, 2, first_id=(1 << 40) + 16 * b + 8, logits=True)
 
     def generate_batch(self, prompts: Sequence[torch.Tensor], max_new_tokens: int,
-                       chunks_for=None, strategy="vanilla", first_id: int = 1 << 20) -> List[torch.Tensor]:
+                       chunks_for=None, strategy="vanilla", first_id: int = 1 << 20,
+                       logits: bool = False) -> List[torch.Tensor]:
         """Greedy generation for several prompts (rust/src/model/generator.rs:123-270
         `BatchGenerator`): each prompt is prefilled (with its own chunk split), then every decode
-        step advances all rows in one batched step. Returns the generated ids per prompt."""
+        step advances all rows in one batched step. Returns the generated ids per prompt.
+        `logits=True` keeps every step's logits (the whole LM head on every rank)."""
         from ..parallel.capacity import equal_chunks
         chunks_for = chunks_for or (lambda n: equal_chunks(n, self.world))
         rids = list(range(first_id, first_id + len(prompts)))
@@ -797,7 +819,7 @@ class LlamaCPEngine:
             cur = torch.cat(firsts)
             outs = [cur]
             for _ in range(max_new_tokens - 1):
-                cur = self.decode_step(rids, cur).view(-1)
+                cur = self.decode_step(rids, cur, logits=logits).view(-1)
                 outs.append(cur)
         finally:
             for rid in rids:
@@ -842,10 +864,11 @@ class DecodeGraph:
         self.part_o = torch.zeros(B * eng.H * self.splits * eng.D, dtype=torch.float32, device=dev)
         self.part_l = torch.zeros(B * eng.H * self.splits, dtype=torch.float32, device=dev)
         self.counters = torch.zeros(B * eng.Hkv + 1, dtype=torch.int32, device=dev)
-        self.graph = None
+        self.graphs: Dict[bool, torch.cuda.CUDAGraph] = {}
+        self.graph_launches: Dict[bool, int] = {}
         self.copied = None
 
-    def body(self) -> None:
+    def body(self, split: bool = False) -> None:
         e, w, cfg = self.e, self.e.w, self.e.cfg
         rt = e.rt
         nat = native()
@@ -874,12 +897,19 @@ class DecodeGraph:
             K.gemv(self.x, lw.wgu, "swiglu", y_bf16=self.g, norm_w=lw.post_norm, eps=eps)
             K.gemv(self.g, lw.wd, "residual", y_bf16=self.x)
         nat.fill_u64(self.am, 0)
-        K.gemv(self.x, w.lm_head, "argmax", y_f32=self.logits, argmax=self.am, norm_w=w.final_norm,
-               eps=eps)
-        nat.argmax_finalize(self.am, self.tokens, self.out_tok)
+        if split:
+            # greedy step, head split over the vocabulary: this rank's rows only (no logits),
+            # then every rank stores its packed maxima into every rank's slots and takes the max
+            K.gemv(self.x, e.lm_head_slice, "argmax", argmax=self.am, norm_w=w.final_norm, eps=eps,
+                   index_base=e.vocab_lo)
+            rt.argmax_exchange(self.am, e.dec_step, self.tokens, self.out_tok)
+        else:
+            K.gemv(self.x, w.lm_head, "argmax", y_f32=self.logits, argmax=self.am,
+                   norm_w=w.final_norm, eps=eps)
+            nat.argmax_finalize(self.am, self.tokens, self.out_tok)
         launches.count(2)
 
-    def run(self, req_ids, tokens, pos, owner, slot, ntok) -> torch.Tensor:
+    def run(self, req_ids, tokens, pos, owner, slot, ntok, split: bool = False) -> torch.Tensor:
         n = len(req_ids)
         # the pinned host buffers are reused every step: wait until the previous step's
         # host-to-device copies have executed before overwriting them
@@ -908,22 +938,25 @@ class DecodeGraph:
             self.tokens.zero_()
         self.tokens[:n].copy_(tokens.view(-1)[:n].to(torch.int32))
         if not self.e.use_graphs:
-            self.body()
+            self.body(split)
         else:
-            if self.graph is None:
+            graph = self.graphs.get(split)
+            if graph is None:
                 # every kernel of the body writes into preallocated buffers (function attributes
                 # and TMA descriptors are host-side calls, legal during capture), so the graph is
                 # captured directly (no eager warm-up step, which would advance the cross-rank
-                # exchange epochs and overwrite `tokens`)
-                self.graph = torch.cuda.CUDAGraph()
+                # exchange epochs and overwrite `tokens`). One graph per LM-head mode; both
+                # share the buffers.
+                graph = torch.cuda.CUDAGraph()
                 with launches.capture() as cap:
-                    with torch.cuda.graph(self.graph):
-                        self.body()
-                self.graph_launches = cap.launches
+                    with torch.cuda.graph(graph):
+                        self.body(split)
+                self.graphs[split] = graph
+                self.graph_launches[split] = cap.launches
             if self.e.env.nvtx:
                 torch.cuda.nvtx.range_push(f"decode step B={self.B}")
-            self.graph.replay()
+            graph.replay()
             if self.e.env.nvtx:
                 torch.cuda.nvtx.range_pop()
-            launches.count(self.graph_launches)
+            launches.count(self.graph_launches[split])
         return self.out_tok[:n].clone()

@@ -129,8 +129,10 @@ def embedding(ids: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = 
 
 # --------------------------------------------------------------------------- GEMV (decode)
 def gemv(x: torch.Tensor, w: torch.Tensor, epi: str, bias=None, y_f32=None, y_bf16=None,
-         argmax=None, norm_w=None, eps: float = 1e-6):
-    """Decode GEMV y = f(x) @ w.T with a fused epilogue; `norm_w` applies RMSNorm to x first."""
+         argmax=None, norm_w=None, eps: float = 1e-6, index_base: int = 0):
+    """Decode GEMV y = f(x) @ w.T with a fused epilogue; `norm_w` applies RMSNorm to x first.
+    With the "argmax" epilogue `index_base` is added to every row index of the packed maximum
+    (w is then the vocabulary slice starting at that row)."""
     if not x.is_cuda:
         if norm_w is not None:
             x = ref.rmsnorm(x, norm_w, eps)
@@ -149,7 +151,7 @@ def gemv(x: torch.Tensor, w: torch.Tensor, epi: str, bias=None, y_f32=None, y_bf
         if epi == "argmax":
             if y_f32 is not None:
                 y_f32.copy_(y)
-            return y.argmax(-1)
-    native().gemv(x, w, GEMV[epi], bias, y_f32, y_bf16, argmax, norm_w, eps)
+            return y.argmax(-1) + index_base
+    native().gemv(x, w, GEMV[epi], bias, y_f32, y_bf16, argmax, norm_w, eps, index_base)
     launches.count()
     return y_bf16 if y_bf16 is not None else y_f32

@@ -28,9 +28,10 @@ class WorkerBackend(abc.ABC):
         logits."""
 
     @abc.abstractmethod
-    def decode_batch(self, request_ids: Sequence[int],
-                     tokens: Sequence[int]) -> Tuple[List[int], Optional[torch.Tensor]]:
-        """One greedy decode step for each request; the next tokens and their logits."""
+    def decode_batch(self, request_ids: Sequence[int], tokens: Sequence[int],
+                     want_logits: bool = True) -> Tuple[List[int], Optional[torch.Tensor]]:
+        """One greedy decode step for each request; the next tokens and, if wanted, their
+        logits (greedy-only batches pass False, which lets the ranks split the LM head)."""
 
     @abc.abstractmethod
     def continuation(self, request_id: int, tokens: torch.Tensor, position_ids: Sequence[int],
@@ -86,11 +87,12 @@ class EngineBackend(WorkerBackend):
                                           return_logits=want_logits, keep_kv=keep_kv)
         return int(tok), logits
 
-    def decode_batch(self, request_ids, tokens):
+    def decode_batch(self, request_ids, tokens, want_logits=True):
         e = self.engine
         toks = torch.tensor([int(t) for t in tokens], dtype=torch.int64, device=e.device)
-        out = e.decode_step([int(r) for r in request_ids], toks)
-        return [int(v) for v in out.view(-1).tolist()], e.last_logits(len(request_ids))
+        out = e.decode_step([int(r) for r in request_ids], toks, logits=bool(want_logits))
+        logits = e.last_logits(len(request_ids)) if want_logits else None
+        return [int(v) for v in out.view(-1).tolist()], logits
 
     def continuation(self, request_id, tokens, position_ids, capacity_tickets, decode_horizon,
                      want_logits=True):

@@ -636,7 +636,9 @@ class Coordinator:
         if active:
             pairs = [[a.job.request_id, a.next_token] for a in active]
             try:
-                resp = self.run_command(P.DecodeBatch(pairs))
+                # greedy-only batches ask for no logits, so the ranks may split the LM head
+                want = any(a.job.temperature > 0 for a in active)
+                resp = self.run_command(P.DecodeBatch(pairs, want))
             except Exception as e:
                 for a in active:
                     self._fail(a.job, e)

@@ -48,6 +48,7 @@ class Decode:
 @dataclasses.dataclass
 class DecodeBatch:
     request_tokens: List[Any]            # [(request_id, token)]
+    want_logits: bool = True             # False: greedy rows only, no rank needs the logits
 
 
 @dataclasses.dataclass

@@ -63,7 +63,8 @@ class Worker:
                 pairs = [(cmd.request_id, cmd.token)] if isinstance(cmd, P.Decode) else \
                     [tuple(x) for x in cmd.request_tokens]
                 rids = [int(r) for r, _ in pairs]
-                vals, self.last_logits = b.decode_batch(rids, [int(t) for _, t in pairs])
+                vals, self.last_logits = b.decode_batch(rids, [int(t) for _, t in pairs],
+                                                        want_logits=getattr(cmd, "want_logits", True))
                 if isinstance(cmd, P.Decode):
                     return P.DecodeDone(cmd.request_id, vals[0])
                 return P.DecodeBatchDone([[r, v] for r, v in zip(rids, vals)])

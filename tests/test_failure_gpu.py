@@ -66,3 +66,27 @@ def test_overlapped_ring_missing_peer_times_out_into_status(dev):
     assert float(x.sum()) == 1024.0
     for rt in rts:
         rt.shutdown()
+
+
+def test_argmax_exchange_missing_peer_times_out_into_status(dev):
+    """The vocabulary-split LM head's argmax exchange waits (bounded, 100 ms here) for a peer
+    that never stores its maximum: it reports a peer timeout at its wait site, returns with this
+    rank's own maximum as the token, and the runtime stays usable."""
+    rts = [native().Runtime(r, 2, dev.index or 0, 1, 2, 256, 2, 64, 8, 1024, 1, 100) for r in range(2)]
+    for rt in rts:
+        rt.open_peers_local(rts)
+    packed = ((0x3F800000 | 0x80000000) << 32) | (0xFFFFFFFF - 42)   # value 1.0 at id 42
+    local = torch.tensor([packed - (1 << 64)], dtype=torch.int64, device=dev)
+    step = torch.tensor([3], dtype=torch.int64, device=dev)
+    tok = torch.full((1,), -1, dtype=torch.int64, device=dev)
+    t0 = time.time()
+    rts[0].argmax_exchange(local, step, None, tok)    # rank 1 never runs its exchange
+    torch.cuda.synchronize(dev)
+    assert time.time() - t0 < 5.0
+    with pytest.raises(RuntimeError, match="code=17.*site 306"):
+        rts[0].check()
+    assert int(tok[0]) == 42
+    x = torch.ones(1024, device=dev)
+    assert float(x.sum()) == 1024.0
+    for rt in rts:
+        rt.shutdown()

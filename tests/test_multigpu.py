@@ -37,18 +37,22 @@ def _cfg():
     return cfg
 
 
-def _run(eng, prompt, chunks, strategy, forced=None):
+def _run(eng, prompt, chunks, strategy, forced=None, logits=True):
     """Prefill (logits of the last prompt position) and STEPS decode steps; with `forced`, step i
     consumes forced[i] instead of the previous step's token (teacher forcing), so two pipelines
-    are compared on identical inputs at every step."""
-    tok, logits = eng.prefill(1, prompt, chunks, strategy, decode_horizon=STEPS + 1,
-                              return_logits=True)
-    toks, step_logits, cur = [int(tok)], [logits.float().cpu()], tok
+    are compared on identical inputs at every step. `logits=False` runs the greedy steps with
+    the LM head split over the ranks' vocabulary slices (no logits kept)."""
+    tok, lg = eng.prefill(1, prompt, chunks, strategy, decode_horizon=STEPS + 1,
+                          return_logits=True)
+    toks, step_logits, cur = [int(tok)], [lg.float().cpu()], tok
     for i in range(STEPS):
         inp = cur if forced is None else torch.tensor([forced[i]], device=tok.device)
-        cur = eng.decode_step([1], inp)
+        cur = eng.decode_step([1], inp, logits=logits)
         toks.append(int(cur))
-        step_logits.append(eng.last_logits(1)[0].float().cpu())
+        if logits:
+            step_logits.append(eng.last_logits(1)[0].float().cpu())
+        else:
+            assert eng.last_logits(1) is None or eng.world == 1
     eng.release(1)
     return toks, step_logits
 
@@ -80,6 +84,10 @@ def _worker(rank, world, port, chunks, strategy, out):
         eng = LlamaCPEngine(cfg, w, rank=rank, world=world, device=dev, group=group,
                             max_context=L, max_batch=1, decode_reserve=16)
         res = _run(eng, prompt, chunks, strategy, forced=single_toks.tolist())
+        # the same inputs with the vocabulary-split LM head: the same tokens, bit for bit
+        split_toks, _ = _run(eng, prompt, chunks, strategy, forced=single_toks.tolist(),
+                             logits=False)
+        assert eng.split_head and split_toks == res[0], (split_toks, res[0])
         eng.check_device()
         eng.close()
         if rank == 0:

@@ -18,7 +18,7 @@ def build_smoke() -> str:
     os.makedirs(OUT, exist_ok=True)
     exe = os.path.join(OUT, "hcp_runtime_smoke")
     srcs = ["tests/runtime_smoke.cu", "core/runtime.cu", "kernels/attn_fwd_sm100.cu",
-            "kernels/elementwise.cu", "kernels/gemm_sm100.cu"]
+            "kernels/elementwise.cu", "kernels/gemm_sm100.cu", "kernels/decode.cu"]
     cmd = [nvcc, "-gencode", "arch=compute_100a,code=sm_100a", "-O2", "-std=c++17", "-lineinfo",
            "-I" + os.path.join(CSRC, "include"), "-I" + CSRC, "-o", exe] + \
         [os.path.join(CSRC, s) for s in srcs] + ["-lcudart"]

@@ -409,3 +409,60 @@ def test_overlapped_ring_uneven_three_ranks_several_steps(dev):
     rts = run_overlap_ranks(dev, [500, 500, 100], "vanilla", epoch=1)
     for epoch, strategy in [(2, "zigzag"), (3, "vanilla"), (4, "striped"), (5, "zigzag")]:
         run_overlap_ranks(dev, [500, 500, 100], strategy, epoch=epoch, rts=rts, layer=epoch % 2)
+
+
+@pytest.mark.parametrize("world,b", [(2, 1), (3, 4), (8, 8)])
+def test_split_lm_head_argmax_exchange(dev, world, b):
+    """Greedy decode with the LM head split over the vocabulary: each emulated rank runs the
+    argmax GEMV over its own vocabulary rows (global row ids through `index_base`) and the
+    exchange kernel keeps the largest packed maximum over the ranks. Every rank's tokens equal
+    the whole head's argmax, including an exact tie across slices, which goes to the smaller id.
+    Ranks 1.. publish by storing into every rank's slots before rank 0's launch, so no wait
+    depends on a later launch."""
+    from hetero_cp_ringattn_b200.ops import kernels as K
+    torch.manual_seed(23)
+    V, KD, EPOCH = 1000, 256, 7                       # epoch 7: parity 1
+    x = torch.randn(b, KD, device=dev, dtype=torch.bfloat16)
+    W = (torch.randn(V, KD, device=dev) * 0.05).bfloat16()
+    part = -(-V // (world * 8)) * 8
+    lo = [min(V, r * part) for r in range(world)]
+    hi = [min(V, lo_r + part) for lo_r in lo]
+    tie = lo[-1] + 3                                  # a row of the last rank's slice
+    W[5] = W[tie] = (torch.sign(x[0].float()) * 0.25).bfloat16()
+    rts = [make_rt(r, world) for r in range(world)]
+    for rt in rts:
+        rt.open_peers_local(rts)
+    step = torch.tensor([EPOCH], dtype=torch.int64, device=dev)
+    am = []
+    for r in range(world):
+        a = torch.zeros(b, dtype=torch.int64, device=dev)
+        K.gemv(x, W[lo[r]:hi[r]], "argmax", argmax=a, index_base=lo[r])
+        am.append(a)
+    for r in range(1, world):
+        for d in range(world):
+            sl = rts[d].argmax_slots()
+            sl[1, r, :b, 0] = am[r]
+            sl[1, r, :b, 1] = EPOCH
+    toks = []
+    for r in range(world):
+        t32 = torch.full((b,), -1, dtype=torch.int32, device=dev)
+        t64 = torch.full((b,), -1, dtype=torch.int64, device=dev)
+        rts[r].argmax_exchange(am[r], step, t32, t64)
+        torch.cuda.synchronize()
+        toks.append((t32, t64))
+    for rt in rts:
+        rt.check()
+    full = torch.zeros(b, dtype=torch.int64, device=dev)
+    K.gemv(x, W, "argmax", argmax=full)
+    want = torch.zeros(b, dtype=torch.int64, device=dev)
+    native().argmax_finalize(full, None, want)
+    assert int(want[0]) == 5
+    logits = x.float() @ W.float().t()
+    assert bool((logits.gather(1, want.view(-1, 1)).view(-1) >= logits.max(1).values - 1e-2).all())
+    for t32, t64 in toks:
+        assert torch.equal(t64, want) and torch.equal(t32.long(), want)
+    for d in range(world):      # rank 0's kernel stored its maxima into every rank's slots
+        sl = rts[d].argmax_slots()
+        assert torch.equal(sl[1, 0, :b, 0], am[0]) and bool((sl[1, 0, :b, 1] == EPOCH).all())
+    for rt in rts:
+        rt.shutdown()

@@ -666,7 +666,7 @@ def test_worker_backend_interface_drives_the_control_plane():
             self.reqs[request_id] = [len(prompt), 0]
             return 10, None
 
-        def decode_batch(self, request_ids, tokens):
+        def decode_batch(self, request_ids, tokens, want_logits=True):
             for r in request_ids:
                 self.reqs[r][0] += 1
                 self.reqs[r][1] += 1
