@@ -47,6 +47,7 @@ from ..parallel.schedule import assignee_table
 from ..parallel.strategy import RingStrategy, build_assignment, build_domain_positions
 from ..utils import launches
 from ..utils.perf import PerfLog, peak_bf16_tflops
+from .attention import AttentionBackend, LayerCall, default_backend, positions_tensor
 from .weights import PreparedWeights
 
 
@@ -101,7 +102,8 @@ class LlamaCPEngine:
                  group: Optional["dist.ProcessGroup"] = None, max_context: int = 8192,
                  max_batch: int = 8, page_size: Optional[int] = None, kv_pages: Optional[int] = None,
                  decode_reserve: int = 512, env: Optional[EnvConfig] = None,
-                 use_graphs: bool = True, perf_log: Optional[PerfLog] = None):
+                 use_graphs: bool = True, perf_log: Optional[PerfLog] = None,
+                 attention_backend=None):
         cfg.validate()
         self.cfg = cfg
         self.w = weights
@@ -156,6 +158,11 @@ class LlamaCPEngine:
                           else (world == 1 or self.overlap))
         self.fused_qkv_serial = self.env.fused_qkv if self.env.fused_qkv is not None else world == 1
         self.tok_epoch = 0
+        # prefill / continuation attention (models/attention.py): an AttentionBackend instance,
+        # or a class taking the engine; default: the CUDA ring on GPUs, the host ring on CPU
+        if isinstance(attention_backend, type):
+            attention_backend = attention_backend(self)
+        self.attn: AttentionBackend = attention_backend or default_backend(self)
         if kv_pages is None:
             kv_pages = -(-self.max_context // self.page_size) + \
                 max_batch * -(-decode_reserve // self.page_size) + 2
@@ -236,14 +243,15 @@ class LlamaCPEngine:
     # ------------------------------------------------------------------ prefill
     @torch.no_grad()
     def prefill(self, req_id: int, prompt_ids: torch.Tensor, chunks: Sequence[int],
-                strategy="vanilla", decode_horizon: int = 128,
+                strategy=None, decode_horizon: int = 128,
                 tickets: Optional[Sequence[int]] = None, return_logits: bool = False,
                 keep_kv: bool = False):
         """SPMD prefill of one request. Every rank passes the same full prompt and chunk split.
 
         Returns (first_token: int64 device tensor [1], logits or None). The first token is
-        broadcast from the rank holding the last prompt position."""
-        strategy = RingStrategy.parse(strategy)
+        broadcast from the rank holding the last prompt position. `strategy` None: the attention
+        backend's default layout (`self.attn.set_strategy`, vanilla unless set)."""
+        strategy = RingStrategy.parse(strategy if strategy is not None else self.attn.strategy)
         chunks = [int(c) for c in chunks]
         if len(chunks) != self.world:
             raise RingError(f"{len(chunks)} chunks for {self.world} ranks")
@@ -287,7 +295,7 @@ class LlamaCPEngine:
     def _prefill_cuda(self, st: RequestState, ids: torch.Tensor, Lp: int, return_logits: bool):
         w, dev = self.w, self.device
         T = ids.numel()
-        pos = torch.from_numpy(st.positions.astype(np.int32)).to(dev, non_blocking=True)
+        pos = positions_tensor(st.positions, dev)
         x = K.embedding(ids, w.embed)
         xn = torch.empty_like(x)
         q_buf = torch.empty(T, self.H, self.D, dtype=torch.bfloat16, device=dev)
@@ -295,7 +303,6 @@ class LlamaCPEngine:
         ring = {}
         if st.ring is not None:
             ring = dict(tile_src=st.ring[0], push_tiles=st.ring[1])
-        fused = self.fused_qkv if (self.world == 1 or st.ring is not None) else self.fused_qkv_serial
         trace = self.perf.enabled
         nvtx = self.env.nvtx
         for li, lw in enumerate(w.layers):
@@ -306,29 +313,13 @@ class LlamaCPEngine:
                 ev[0].record()
             K.rmsnorm(x, lw.in_norm, self.cfg.rms_norm_eps, out=xn)
             self.prefill_epoch += 1
-            tail = (pos, self.cos, self.sin, li, st.kv.pt_device, 0, Lp, self.scale, True,
-                    q_buf, o_buf, None, self.prefill_epoch)
             if trace:
                 ev[1].record()
-            if fused:
-                # one kernel: QKV GEMM whose epilogue rotates, writes Q and writes K/V (into every
-                # rank's staging buffer in the serial ring, into this rank's own otherwise)
-                self.rt.push_layer_fused(xn, lw.wqkv, lw.bqkv, *tail, **ring)
-            else:
-                qkv = K.gemm(xn, lw.wqkv, "bias" if lw.bqkv is not None else "store", bias=lw.bqkv)
-                self.rt.push_layer(qkv, *tail, **ring)
-                del qkv
-            if trace:
-                ev[2].record()
-            # overlapped ring: this one kernel also pushes the rank's rows to the peers
-            self.rt.attend_layer(xn, *tail, **ring)
+            o = self.attn.forward(xn, lw, LayerCall(st, li, pos, Lp, q_buf, o_buf, self.prefill_epoch,
+                                                    ring=ring, ev=ev if trace else None))
             if trace:
                 ev[3].record()
-            if self.world == 1 or self.overlap:
-                launches.count(2)
-            else:   # + wait for released parity (after the first two steps), wait for pushes, signal
-                launches.count(5 - (1 if self.prefill_epoch <= 2 else 0))
-            K.gemm(o_buf.view(T, self.H * self.D), lw.wo, "residual", residual=x)
+            K.gemm(o, lw.wo, "residual", residual=x)
             K.rmsnorm(x, lw.post_norm, self.cfg.rms_norm_eps, out=xn)
             g = K.gemm(xn, lw.wgu, "swiglu")
             K.gemm(g, lw.wd, "residual", residual=x)
@@ -366,6 +357,7 @@ class LlamaCPEngine:
                        num_domains=self.world, seq_len=T, overlap=overlap,
                        ring_mode=("single" if self.world == 1 else
                                   "overlap_in_kernel" if overlap else "serial"),
+                       attention_backend=self.attn.name,
                        nvlink_gbps=sent / max(span_ms, 1e-6) / 1e6,
                        nvlink_span="attention" if overlap else "projection+push",
                        attn_tflops=tflops, roofline_frac=tflops / peak_bf16_tflops())
@@ -409,41 +401,15 @@ class LlamaCPEngine:
         dist.all_gather(bufs, pad, group=self.group)
         return [b[: int(s)] for b, s in zip(bufs, sizes)]
 
-    def _ring_fold(self, q, q_pos, ks, vs, ps) -> torch.Tensor:
-        """Host ring attention: fold the sources in ring arrival order (own chunk first, then
-        the predecessor's, ...), each cut into micro blocks of `micro_kv` rows, with the online
-        softmax and the fully-future block skip (ring.rs:861-1399)."""
-        Tq = q.shape[0]
-        m = torch.full((self.H, Tq), ref.NEG_INIT, dtype=q.dtype)
-        l = torch.zeros(self.H, Tq, dtype=q.dtype)
-        acc = torch.zeros_like(q)
-        for step in range(self.world):
-            src = (self.rank - step) % self.world
-            k, v, kp = ks[src], vs[src], ps[src]
-            for b0 in range(0, k.shape[0], self.micro_kv):
-                b1 = min(b0 + self.micro_kv, k.shape[0])
-                m, l, acc = ref.online_update_block(m, l, acc, q, k[b0:b1].to(q.dtype),
-                                                    v[b0:b1].to(q.dtype), q_pos, kp[b0:b1],
-                                                    True, self.scale)
-        return ref.finalize_state(m, l, acc)[0]
-
     def _prefill_host(self, st: RequestState, ids: torch.Tensor, Lp: int, return_logits: bool):
         w, cfg = self.w, self.cfg
-        T = ids.numel()
-        pos = torch.from_numpy(st.positions)
+        pos = positions_tensor(st.positions, self.device)
         x = w.embed[ids.long()].float()
         st.host_kv = []
         for li, lw in enumerate(w.layers):
             h = ref.rmsnorm(x, lw.in_norm, cfg.rms_norm_eps)
-            qkv = ref.linear(h, lw.wqkv, lw.bqkv)
-            q = ref.apply_rope(qkv[:, : self.H * self.D].view(T, self.H, self.D), pos, cfg.rope_theta, cfg.rope_scaling)
-            k = ref.apply_rope(qkv[:, self.H * self.D:(self.H + self.Hkv) * self.D].view(T, self.Hkv, self.D),
-                               pos, cfg.rope_theta, cfg.rope_scaling)
-            v = qkv[:, (self.H + self.Hkv) * self.D:].reshape(T, self.Hkv, self.D)
-            st.host_kv.append([k.clone(), v.clone(), pos.clone(), torch.ones(T, dtype=torch.bool)])
-            o = self._ring_fold(q, pos, self._gather_rows(k), self._gather_rows(v),
-                                self._gather_rows(pos))
-            x = x + ref.linear(o.reshape(T, self.H * self.D), lw.wo)
+            o = self.attn.forward(h, lw, LayerCall(st, li, pos, Lp))
+            x = x + ref.linear(o, lw.wo)
             h = ref.rmsnorm(x, lw.post_norm, cfg.rms_norm_eps)
             x = x + ref.linear(K.swiglu_from_interleaved(ref.linear(h, lw.wgu)), lw.wd)
         tok = torch.zeros(1, dtype=torch.int64)
@@ -687,25 +653,17 @@ class LlamaCPEngine:
         xn = torch.empty_like(x)
         q_buf = torch.empty(T, self.H, self.D, dtype=torch.bfloat16, device=dev)
         o_buf = torch.empty_like(q_buf)
-        empty_qkv = torch.empty(0, self.cfg.qkv_size, dtype=torch.bfloat16, device=dev)
         for li, lw in enumerate(w.layers):
             c = int(kv.layer_counts[li])
             existing = torch.from_numpy(kv.slot_pos[li, :c].astype(np.int32)).to(dev)
             self.prefill_epoch += 1
-            tail = (pos, self.cos, self.sin, li, kv.pt_device, c, Ltot, self.scale, True, q_buf,
-                    o_buf, None, self.prefill_epoch, existing)
             if T:
                 K.rmsnorm(x, lw.in_norm, self.cfg.rms_norm_eps, out=xn)
-            if T and self.fused_qkv_serial:   # continuation segments use the serial ring
-                self.rt.push_layer_fused(xn, lw.wqkv, lw.bqkv, *tail)
-                self.rt.attend_layer(xn, *tail)
-            else:
-                qkv = K.gemm(xn, lw.wqkv, "bias" if lw.bqkv is not None else "store",
-                             bias=lw.bqkv) if T else empty_qkv
-                self.rt.push_layer(qkv, *tail)
-                self.rt.attend_layer(qkv, *tail)
+            # continuation segments use the serial ring (every rank calls, with or without rows)
+            o = self.attn.forward(xn, lw, LayerCall(st, li, pos, Ltot, q_buf, o_buf, self.prefill_epoch,
+                                                    slot_base=c, existing=existing))
             if T:
-                K.gemm(o_buf.view(T, self.H * self.D), lw.wo, "residual", residual=x)
+                K.gemm(o, lw.wo, "residual", residual=x)
                 K.rmsnorm(x, lw.post_norm, self.cfg.rms_norm_eps, out=xn)
                 g = K.gemm(xn, lw.wgu, "swiglu")
                 K.gemm(g, lw.wd, "residual", residual=x)
@@ -715,35 +673,14 @@ class LlamaCPEngine:
     def _append_host(self, st, ids, my_pos, Ltot, last_owner, return_logits):
         w, cfg = self.w, self.cfg
         T = ids.numel()
-        pos = torch.from_numpy(my_pos)
+        pos = positions_tensor(my_pos, self.device)
         x = w.embed[ids.long()].float()
         for li, lw in enumerate(w.layers):
-            kv = st.host_kv[li]
+            h = ref.rmsnorm(x, lw.in_norm, cfg.rms_norm_eps) if T else x
+            # every rank takes part in the backend's gathers, with or without rows
+            o = self.attn.forward(h, lw, LayerCall(st, li, pos, Ltot, existing=st.host_kv[li][2]))
             if T:
-                h = ref.rmsnorm(x, lw.in_norm, cfg.rms_norm_eps)
-                qkv = ref.linear(h, lw.wqkv, lw.bqkv)
-                q = ref.apply_rope(qkv[:, : self.H * self.D].view(T, self.H, self.D), pos, cfg.rope_theta, cfg.rope_scaling)
-                k = ref.apply_rope(qkv[:, self.H * self.D:(self.H + self.Hkv) * self.D].view(T, self.Hkv, self.D),
-                                   pos, cfg.rope_theta, cfg.rope_scaling)
-                v = qkv[:, (self.H + self.Hkv) * self.D:].reshape(T, self.Hkv, self.D)
-                kv[0] = torch.cat([kv[0], k])
-                kv[1] = torch.cat([kv[1], v])
-                kv[2] = torch.cat([kv[2], pos])
-                kv[3] = torch.cat([kv[3], torch.ones(T, dtype=torch.bool)])
-            sh = kv[3]
-            ks, vs, ps = (self._gather_rows(kv[0][sh]), self._gather_rows(kv[1][sh]),
-                          self._gather_rows(kv[2][sh]))
-            if T:
-                kk = torch.zeros(Ltot, self.Hkv, self.D, dtype=torch.float32)
-                vv = torch.zeros_like(kk)
-                for a, b, p in zip(ks, vs, ps):
-                    kk[p] = a.float()
-                    vv[p] = b.float()
-                # replicated legacy-decode rows (identical on every rank): once, from here
-                kk[kv[2][~sh]] = kv[0][~sh].float()
-                vv[kv[2][~sh]] = kv[1][~sh].float()
-                o, _ = ref.full_attention(q, kk, vv, pos, torch.arange(Ltot), causal=True)
-                x = x + ref.linear(o.reshape(T, self.H * self.D), lw.wo)
+                x = x + ref.linear(o, lw.wo)
                 h = ref.rmsnorm(x, lw.post_norm, cfg.rms_norm_eps)
                 x = x + ref.linear(K.swiglu_from_interleaved(ref.linear(h, lw.wgu)), lw.wd)
         tok = torch.zeros(1, dtype=torch.int64)
@@ -768,7 +705,7 @@ class LlamaCPEngine:
 
     @torch.no_grad()
     def generate(self, req_id: int, prompt_ids: torch.Tensor, max_new_tokens: int,
-                 chunks: Sequence[int], strategy="vanilla", tickets=None,
+                 chunks: Sequence[int], strategy=None, tickets=None,
                  stop_ids: Optional[Sequence[int]] = None) -> torch.Tensor:
         """Greedy generation (SPMD across ranks). Returns the generated ids [n] on the device.
 
@@ -801,7 +738,7 @@ class LlamaCPEngine:
                 self.generate_batch([prompt] * b, 2, first_id=(1 << 40) + 16 * b + 8, logits=True)
 
     def generate_batch(self, prompts: Sequence[torch.Tensor], max_new_tokens: int,
-                       chunks_for=None, strategy="vanilla", first_id: int = 1 << 20,
+                       chunks_for=None, strategy=None, first_id: int = 1 << 20,
                        logits: bool = False) -> List[torch.Tensor]:
         """Greedy generation for several prompts (rust/src/model/generator.rs:123-270
         `BatchGenerator`): each prompt is prefilled (with its own chunk split), then every decode
