@@ -338,6 +338,16 @@ def _env_int(name: str, default: int) -> int:
         return default
 
 
+def _env_choice(name: str, default: str, choices) -> str:
+    v = os.environ.get(name)
+    if v is None or not v.strip():
+        return default
+    v = v.strip().lower()
+    if v not in choices:
+        raise ValueError(f"{name}={v!r}: expected one of {', '.join(choices)}")
+    return v
+
+
 @dataclasses.dataclass
 class EnvConfig:
     perf_log: Optional[str] = None          # HCP_PERF_LOG: JSONL perf events
@@ -358,9 +368,13 @@ class EnvConfig:
     p2p_spin_budget_ms: int = 5000          # HCP_P2P_SPIN_BUDGET_MS: device-side peer-wait limit
     device: Optional[str] = None            # HCP_TORCH_DEVICE / HCP_TCH_DEVICE
     nvtx: bool = False                      # HCP_NVTX: NVTX ranges per prefill layer / decode step
-    decode_kernel_combine: bool = False     # HCP_DECODE_KERNEL_COMBINE=1: cross-rank combine inside
-                                            # the decode attention kernel (several ranks; measured
-                                            # slower at 2 ranks than the separate combine launch)
+    decode_combine: str = "launch"          # HCP_DECODE_COMBINE: where several ranks' decode
+                                            # (O, LSE) partials are waited for and combined:
+                                            # "launch" (a combine kernel of its own), "gemv" (the
+                                            # output projection's prologue), "attn" (the attention
+                                            # kernel's last CTA per (row, KV head); also
+                                            # HCP_DECODE_KERNEL_COMBINE=1). Measured on 2 B200s:
+                                            # launch 1.156, gemv 1.231, attn 1.285 ms per token
     fused_qkv: Optional[bool] = None        # HCP_FUSED_QKV: the projection GEMM's epilogue does
                                             # RoPE + the K/V writes (default on; 0: GEMM + a
                                             # separate RoPE / K/V kernel)
@@ -384,7 +398,8 @@ class EnvConfig:
             p2p_spin_budget_ms=_env_int("HCP_P2P_SPIN_BUDGET_MS", 5000),
             device=os.environ.get("HCP_TORCH_DEVICE") or os.environ.get("HCP_TCH_DEVICE") or None,
             nvtx=_env_bool("HCP_NVTX", False),
-            decode_kernel_combine=_env_bool("HCP_DECODE_KERNEL_COMBINE", False),
+            decode_combine=("attn" if _env_bool("HCP_DECODE_KERNEL_COMBINE", False)
+                            else _env_choice("HCP_DECODE_COMBINE", "launch", ("launch", "gemv", "attn"))),
             fused_qkv=(_env_bool("HCP_FUSED_QKV", True) if os.environ.get("HCP_FUSED_QKV") else None),
             split_lm_head=_env_bool("HCP_SPLIT_LM_HEAD", True),
         )

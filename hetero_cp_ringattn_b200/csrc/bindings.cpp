@@ -581,6 +581,47 @@ class PyRuntime {
     HCP_CHECK_OK(hcp::dec::gemv(a, cur_stream()));
   }
 
+  // Output projection of a decode step on several ranks with the cross-rank combine in its
+  // prologue: y += bf16(combine(partials) W^T), where the combine waits for every rank's
+  // dec_ready flag at epoch = (*epoch_src) * epoch_mul + epoch_add and merges the (O, LSE)
+  // partials of the exchange slots in rank order (x only gives the shape [B, H * D]).
+  void o_proj_combine(torch::Tensor x, torch::Tensor w, torch::Tensor y, torch::Tensor epoch_src,
+                      int64_t epoch_mul, int64_t epoch_add) {
+    check_cuda_bf16(x, "x");
+    check_cuda_bf16(w, "w");
+    check_cuda_bf16(y, "y");
+    TORCH_CHECK(epoch_src.is_cuda() && epoch_src.element_size() == 8, "epoch_src must be a CUDA 64-bit tensor");
+    const c10::cuda::CUDAGuard g(x.device());
+    const auto& c = rt_.config();
+    hcp::dec::GemvArgs a{};
+    a.x = reinterpret_cast<const __nv_bfloat16*>(x.data_ptr());
+    a.ldx = x.stride(0);
+    a.W = reinterpret_cast<const __nv_bfloat16*>(w.data_ptr());
+    a.B = int(x.size(0));
+    a.N = int(w.size(0));
+    a.K = int(w.size(1));
+    TORCH_CHECK(x.size(1) == a.K && y.size(0) == a.B && y.size(1) == a.N, "o_proj_combine shapes");
+    TORCH_CHECK(a.B <= c.max_batch, "o_proj_combine: rows exceed max_batch");
+    a.epi = hcp::dec::kGemvResidual;
+    a.y_bf16 = reinterpret_cast<__nv_bfloat16*>(y.data_ptr());
+    a.ldy = y.stride(0);
+    a.num_sms = sm_count(x.get_device());
+    auto& m = a.cmb;
+    m.xslot = rt_.xslot();
+    m.ready = rt_.flags() + hcp::kFlagDecReady;
+    m.epoch_src = reinterpret_cast<const unsigned long long*>(epoch_src.data_ptr());
+    m.epoch_mul = uint64_t(epoch_mul);
+    m.epoch_add = uint64_t(epoch_add);
+    m.ranks = c.world;
+    m.H = c.num_heads;
+    m.D = c.geom.d;
+    m.slot_B = a.B;
+    m.row0 = 0;
+    m.budget_ns = c.peer_wait_budget_ns;
+    m.status = rt_.status();
+    HCP_CHECK_OK(hcp::dec::gemv(a, cur_stream()));
+  }
+
   void decode_combine(torch::Tensor out, int64_t B, int64_t H, c10::optional<torch::Tensor> epoch_src,
                       int64_t epoch_mul, int64_t epoch_add) {
     check_cuda_bf16(out, "out");
@@ -718,6 +759,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
            py::arg("epoch_add"), py::arg("final_out") = py::none(), py::arg("combine_out") = py::none())
       .def("qkv_gemv_rope", &PyRuntime::qkv_gemv_rope)
       .def("decode_combine", &PyRuntime::decode_combine)
+      .def("o_proj_combine", &PyRuntime::o_proj_combine, py::arg("x"), py::arg("w"), py::arg("y"),
+           py::arg("epoch_src"), py::arg("epoch_mul"), py::arg("epoch_add"))
       .def("wait_flags", &PyRuntime::wait_flags)
       .def("arena", &PyRuntime::arena)
       .def("stage", &PyRuntime::stage)

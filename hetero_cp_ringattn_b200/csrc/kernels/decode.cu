@@ -141,6 +141,48 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(GemvArgs a) {
         xs[b * kvec + k] = make_uint4(o[0], o[1], o[2], o[3]);
       }
     }
+  } else if (EPI == kGemvResidual && a.cmb.xslot != nullptr) {
+    // x = the rank-order log-sum-exp combine of every rank's (O, LSE) partial (see
+    // GemvCombineArgs); thread k builds the 8 columns [8k, 8k + 8) of head 8k / D of every row
+    const GemvCombineArgs& c = a.cmb;
+    const unsigned long long e = *c.epoch_src * c.epoch_mul + c.epoch_add;
+    __shared__ int ok;
+    if (tid == 0) ok = 1;
+    __syncthreads();
+    if (tid < c.ranks && !wait_flag_geq_sys(c.ready + tid, e, c.budget_ns, c.status, 402, tid)) ok = 0;
+    __syncthreads();
+    const long rank_stride = (long)c.slot_B * c.H * (c.D + 1);
+    const float* xsl = c.xslot + (long)(e & 1ull) * c.ranks * rank_stride;
+    for (int k = tid; k < kvec; k += GEMV_THREADS) {
+      const int hh = (k * 8) / c.D, d0 = (k * 8) % c.D;
+#pragma unroll
+      for (int b = 0; b < B; ++b) {
+        float out[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) out[j] = 0.f;
+        const float* row = xsl + ((long)(c.row0 + b) * c.H + hh) * (c.D + 1);
+        if (ok) {
+          float mx = -INFINITY;
+          for (int r = 0; r < c.ranks; ++r) mx = fmaxf(mx, __ldcg(row + r * rank_stride + c.D));
+          if (mx > -INFINITY) {
+            float ws = 0.f, acc[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+            for (int r = 0; r < c.ranks; ++r) {
+              const float* src = row + r * rank_stride;
+              const float w = fast_exp2(__ldcg(src + c.D) - mx);
+              ws += w;
+#pragma unroll
+              for (int j = 0; j < 8; ++j) acc[j] += w * __ldcg(src + d0 + j);
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j) out[j] = acc[j] / ws;
+          }
+        }
+        xs[b * kvec + k] = make_uint4(pack_bf16x2(out[0], out[1]), pack_bf16x2(out[2], out[3]),
+                                      pack_bf16x2(out[4], out[5]), pack_bf16x2(out[6], out[7]));
+      }
+    }
   } else {
     for (int k = tid; k < kvec; k += GEMV_THREADS)
 #pragma unroll
@@ -312,6 +354,11 @@ const char* gemv(const GemvArgs& a, cudaStream_t s) {
     return "gemv: QKV rope epilogue needs q_out and N = (H + 2 Hkv) D";
   if ((reinterpret_cast<uintptr_t>(a.W) | reinterpret_cast<uintptr_t>(a.x)) & 15)
     return "gemv: W/x must be 16-byte aligned";
+  if (a.cmb.xslot != nullptr &&
+      (a.epi != kGemvResidual || a.norm_w != nullptr || a.cmb.D % 8 || a.K != a.cmb.H * a.cmb.D ||
+       a.cmb.ranks < 1 || a.cmb.ranks > GEMV_THREADS || a.cmb.row0 + a.B > a.cmb.slot_B ||
+       !a.cmb.ready || !a.cmb.epoch_src))
+    return "gemv: the combine prologue needs the residual epilogue, no norm, K = H * D, D % 8 == 0";
   if (size_t(a.K) * 2 > 200 * 1024) return "gemv: needs K*2 <= 200 KB (x is staged in shared memory)";
   if (size_t(a.B) * a.K * 2 > 200 * 1024) {
     // x rows are staged in shared memory: run the batch in halves (their rows are independent)
@@ -322,6 +369,7 @@ const char* gemv(const GemvArgs& a, cudaStream_t s) {
     if (a.y_f32) hi.y_f32 = a.y_f32 + (long)o * a.ldy;
     if (a.y_bf16) hi.y_bf16 = a.y_bf16 + (long)o * a.ldy;
     if (a.argmax) hi.argmax = a.argmax + o;
+    hi.cmb.row0 = a.cmb.row0 + o;
     if (a.epi == kGemvQkvRope) {
       hi.rope.pos = a.rope.pos + o;
       hi.rope.q_out = a.rope.q_out + (long)o * a.rope.H * a.rope.D;

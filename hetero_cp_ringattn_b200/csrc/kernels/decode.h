@@ -40,6 +40,22 @@ struct GemvRopeArgs {
   int* status;
 };
 
+// kGemvResidual with `xslot` set: x is not read. Each CTA waits (bounded) until every rank's
+// dec_ready flag reaches the epoch, then builds x in shared memory as the log-sum-exp combine in
+// rank order of the ranks' (O, LSE) partials in the exchange slots [2][ranks][slot_B][H][D+1]
+// (rows row0 .. row0 + B - 1), the same arithmetic as decode_combine, so the decode step needs
+// no combine launch between the attention and the output projection.
+struct GemvCombineArgs {
+  const float* xslot;                  // local exchange slots (null: x is read)
+  const unsigned long long* ready;     // local dec_ready[ranks]
+  const unsigned long long* epoch_src; // epoch = (*epoch_src) * epoch_mul + epoch_add
+  unsigned long long epoch_mul;
+  unsigned long long epoch_add;
+  int ranks, H, D, slot_B, row0;
+  unsigned long long budget_ns;
+  int* status;
+};
+
 struct GemvArgs {
   const __nv_bfloat16* x;  // [B, K]
   long ldx;
@@ -56,6 +72,7 @@ struct GemvArgs {
   const __nv_bfloat16* norm_w; // optional fused input RMSNorm weight [K]
   float eps;
   GemvRopeArgs rope;           // kGemvQkvRope only
+  GemvCombineArgs cmb;         // kGemvResidual only (optional)
 };
 
 struct DecodeAttnArgs {

@@ -821,16 +821,22 @@ class DecodeGraph:
             # split-KV attention; on one rank its last CTA writes the layer output directly.
             # With several ranks the rank's (O, LSE) partial goes into every rank's slots and
             # the log-sum-exp combine in rank order follows a bounded wait for the other ranks'
-            # partials: in its own launch (default), or with HCP_DECODE_KERNEL_COMBINE=1 inside
-            # the attention kernel, by the last CTA of each (row, KV head)
-            fused = single or e.env.decode_kernel_combine
+            # partials: in a launch of its own (HCP_DECODE_COMBINE=launch, the default and the
+            # fastest measured), in the output projection's prologue (=gemv: every CTA of the
+            # GEMV waits and combines the same partials) or in the attention kernel's last CTA
+            # of each (row, KV head) (=attn)
+            mode = "single" if single else e.env.decode_combine
             rt.decode_attn(self.q, li, self.pt, self.ntok[li], e.scale, self.splits, self.part_o,
                            self.part_l, self.counters, e.dec_step, e.L, li + 1,
-                           self.o if single else None, None if single or not fused else self.o)
-            if not fused:   # the default with several ranks: wait + combine in their own launch
+                           self.o if single else None, self.o if mode == "attn" else None)
+            if mode == "launch":
                 rt.decode_combine(self.o, self.B, e.H, e.dec_step, e.L, li + 1)
-            launches.count(2 if fused else 3)
-            K.gemv(self.o, lw.wo, "residual", y_bf16=self.x)
+            launches.count(3 if mode == "launch" else 2)
+            if mode == "gemv":
+                rt.o_proj_combine(self.o, lw.wo, self.x, e.dec_step, e.L, li + 1)
+                launches.count()
+            else:
+                K.gemv(self.o, lw.wo, "residual", y_bf16=self.x)
             K.gemv(self.x, lw.wgu, "swiglu", y_bf16=self.g, norm_w=lw.post_norm, eps=eps)
             K.gemv(self.g, lw.wd, "residual", y_bf16=self.x)
         nat.fill_u64(self.am, 0)

@@ -90,3 +90,27 @@ def test_argmax_exchange_missing_peer_times_out_into_status(dev):
     assert float(x.sum()) == 1024.0
     for rt in rts:
         rt.shutdown()
+
+
+def test_output_projection_combine_missing_peer_times_out_into_status(dev):
+    """The combine prologue of the decode output projection waits (bounded, 100 ms here) for a
+    peer whose partial never arrives: it reports a peer timeout at its wait site and returns;
+    the runtime stays usable."""
+    H, D = 8, 64
+    rts = [native().Runtime(r, 2, dev.index or 0, 1, 2, 256, 2, D, H, 1024, 1, 100) for r in range(2)]
+    for rt in rts:
+        rt.open_peers_local(rts)
+    x = torch.zeros(1, H * D, device=dev, dtype=torch.bfloat16)
+    W = torch.zeros(128, H * D, device=dev, dtype=torch.bfloat16)
+    y = torch.zeros(1, 128, device=dev, dtype=torch.bfloat16)
+    step = torch.zeros(1, dtype=torch.int64, device=dev)
+    t0 = time.time()
+    rts[0].o_proj_combine(x, W, y, step, 1, 3)          # no rank ever releases epoch 3
+    torch.cuda.synchronize(dev)
+    assert time.time() - t0 < 5.0
+    with pytest.raises(RuntimeError, match="code=17.*site 402"):
+        rts[0].check()
+    x1 = torch.ones(1024, device=dev)
+    assert float(x1.sum()) == 1024.0
+    for rt in rts:
+        rt.shutdown()

@@ -466,3 +466,60 @@ def test_split_lm_head_argmax_exchange(dev, world, b):
         assert torch.equal(sl[1, 0, :b, 0], am[0]) and bool((sl[1, 0, :b, 1] == EPOCH).all())
     for rt in rts:
         rt.shutdown()
+
+
+@pytest.mark.parametrize("world,b", [(2, 1), (3, 4), (4, 8)])
+def test_output_projection_with_combine_prologue(dev, world, b):
+    """The decode step's output projection with the cross-rank combine in its prologue (the
+    default on several ranks): after every emulated rank's split-KV attention has stored its
+    (O, LSE) partial into every rank's slots and released its ready flag, each rank's
+    `o_proj_combine` equals the combine launch followed by the plain residual GEMV, bit for
+    bit, and the combined attention matches float32 attention over every rank's KV."""
+    from hetero_cp_ringattn_b200.ops import kernels as K
+    torch.manual_seed(29)
+    counts = [300, 257, 129, 64][:world]
+    rts = [make_rt(r, world) for r in range(world)]
+    for rt in rts:
+        rt.open_peers_local(rts)
+    q = torch.randn(b, H, D, device=dev, dtype=torch.bfloat16)
+    ks, vs, pts = [], [], []
+    for r in range(world):
+        arena = rts[r].arena()
+        k = torch.randn(counts[r], HKV, D, device=dev, dtype=torch.bfloat16)
+        v = torch.randn(counts[r], HKV, D, device=dev, dtype=torch.bfloat16)
+        for i in range(counts[r]):
+            arena[0, [4, 2][i // PAGE], 0, :, i % PAGE] = k[i]
+            arena[0, [4, 2][i // PAGE], 1, :, i % PAGE] = v[i]
+        ks.append(k)
+        vs.append(v)
+        pts.append(torch.tensor([[4, 2]] * b, dtype=torch.int32, device=dev))
+    splits, epoch = 4, 11
+    keep = []
+    for r in range(world):
+        part_o = torch.empty(b * H * splits * D, device=dev)
+        part_l = torch.empty(b * H * splits, device=dev)
+        cnt = torch.zeros(b * HKV + 1, dtype=torch.int32, device=dev)
+        ntok = torch.full((b,), counts[r], dtype=torch.int32, device=dev)
+        keep.append((part_o, part_l, cnt, ntok))
+        rts[r].decode_attn(q, 0, pts[r], ntok, 1.0 / math.sqrt(D), splits, part_o, part_l, cnt,
+                           None, 1, epoch)
+    torch.cuda.synchronize()
+    W = (torch.randn(384, H * D, device=dev) * 0.05).bfloat16()
+    y0 = torch.randn(b, 384, device=dev).bfloat16()
+    step = torch.zeros(1, dtype=torch.int64, device=dev)     # epoch = 0 * 1 + epoch
+    k_all, v_all = torch.cat(ks).float(), torch.cat(vs).float()
+    for r in range(world):
+        o = torch.empty(b, H * D, device=dev, dtype=torch.bfloat16)
+        rts[r].decode_combine(o, b, H, None, 1, epoch)
+        want = y0.clone()
+        K.gemv(o, W, "residual", y_bf16=want)
+        got = y0.clone()
+        rts[r].o_proj_combine(torch.empty_like(o), W, got, step, 1, epoch)
+        torch.cuda.synchronize()
+        rts[r].check()
+        assert torch.equal(got, want), f"rank {r}: max diff {(got.float() - want.float()).abs().max()}"
+        for bb in range(b):
+            ro, _ = ref.full_attention(q[bb:bb + 1].float(), k_all, v_all, causal=False)
+            assert (o[bb].view(H, D).float() - ro[0]).abs().max() < 2e-2
+    for rt in rts:
+        rt.shutdown()
