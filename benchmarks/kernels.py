@@ -121,10 +121,21 @@ def bench_attn(args, dev, pk):
         v = torch.randn_like(k)
         pos = torch.arange(L, device=dev, dtype=torch.int32)
         iters = max(2, args.iters if L <= 32768 else 3)
-        ms = timed(lambda: K.attention(q, k, v, pos, L, causal=True), iters)
         fl = causal_flops(L, L, H, D)
-        row = dict(kernel="attn_fwd_sm100", L=L, H=H, Hkv=Hkv, D=D, causal=True, ms=round(ms, 3),
-                   tflops=round(fl / ms / 1e9, 1),
+        variants = args.variants if D == 64 else [0]
+        # head_dim 64 variants timed in alternation (--variants 0,3), best of the repetitions
+        best = {}
+        for _ in range(args.reps):
+            for vv in variants:
+                t = timed(lambda: K.attention(q, k, v, pos, L, causal=True, variant=vv), iters)
+                best[vv] = min(best.get(vv, t), t)
+        for vv in variants[:-1]:
+            emit(kernel="attn_fwd_sm100", L=L, H=H, Hkv=Hkv, D=D, causal=True, variant=vv,
+                 ms=round(best[vv], 3), tflops=round(fl / best[vv] / 1e9, 1),
+                 frac_of_measured=round(fl / best[vv] / 1e9 / pk["tflops"], 3), peaks=pk["source"])
+        ms = best[variants[-1]]
+        row = dict(kernel="attn_fwd_sm100", L=L, H=H, Hkv=Hkv, D=D, causal=True,
+                   variant=variants[-1], ms=round(ms, 3), tflops=round(fl / ms / 1e9, 1),
                    frac_of_measured=round(fl / ms / 1e9 / pk["tflops"], 3), peaks=pk["source"])
         if not args.small and L <= 65536:
             qs = q.transpose(0, 1).unsqueeze(0)
@@ -359,6 +370,9 @@ def main(argv=None):
     ap.add_argument("--heads", type=int, default=32)
     ap.add_argument("--kv-heads", type=int, default=8)
     ap.add_argument("--head-dim", type=int, default=128)
+    ap.add_argument("--variants", type=lambda s: [int(x) for x in s.split(",")], default=[0],
+                    help="attn: head_dim-64 kernel variants to time (0 default, 1, 2, 3 pipelined)")
+    ap.add_argument("--reps", type=int, default=1, help="attn: alternating repetitions")
     ap.add_argument("--compare", action="store_true", help="also time the NCCL send/recv ring restatement")
     ap.add_argument("--serial", action="store_true",
                     help="ring: the serial ring (push, wait for every rank, attend) instead of the "

@@ -378,6 +378,8 @@ class EnvConfig:
     fused_qkv: Optional[bool] = None        # HCP_FUSED_QKV: the projection GEMM's epilogue does
                                             # RoPE + the K/V writes (default on; 0: GEMM + a
                                             # separate RoPE / K/V kernel)
+    decode_prefetch: bool = False           # HCP_DECODE_PREFETCH=1: decode kernels pull
+                                            # the next kernels' weights into L2 while they run
     split_lm_head: bool = True              # HCP_SPLIT_LM_HEAD=0: every rank runs the whole LM
                                             # head in greedy decode steps (default: each rank
                                             # takes 1/N of the vocabulary and the ranks exchange
@@ -402,6 +404,7 @@ class EnvConfig:
                             else _env_choice("HCP_DECODE_COMBINE", "launch", ("launch", "gemv", "attn"))),
             fused_qkv=(_env_bool("HCP_FUSED_QKV", True) if os.environ.get("HCP_FUSED_QKV") else None),
             split_lm_head=_env_bool("HCP_SPLIT_LM_HEAD", True),
+            decode_prefetch=_env_bool("HCP_DECODE_PREFETCH", False),
         )
 
 

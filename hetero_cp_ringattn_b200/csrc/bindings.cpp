@@ -45,6 +45,18 @@ int sm_count(int dev) {
 
 cudaStream_t cur_stream() { return at::cuda::getCurrentCUDAStream().stream(); }
 
+// Up to two weight tensors a decode kernel prefetches into L2 for the kernels after it.
+hcp::dec::L2Prefetch make_prefetch(const std::vector<torch::Tensor>& ts) {
+  TORCH_CHECK(ts.size() <= 2, "at most two L2 prefetch ranges");
+  hcp::dec::L2Prefetch pf{};
+  for (size_t i = 0; i < ts.size(); ++i) {
+    TORCH_CHECK(ts[i].is_cuda() && ts[i].is_contiguous(), "prefetch ranges must be contiguous CUDA tensors");
+    pf.ptr[i] = ts[i].data_ptr();
+    pf.bytes[i] = uint64_t(ts[i].numel()) * ts[i].element_size();
+  }
+  return pf;
+}
+
 // ----------------------------------------------------------------------------- kernels
 void gemm(torch::Tensor A, torch::Tensor B, torch::Tensor C, int64_t epi,
           c10::optional<torch::Tensor> bias, c10::optional<torch::Tensor> R,
@@ -83,7 +95,7 @@ void gemm(torch::Tensor A, torch::Tensor B, torch::Tensor C, int64_t epi,
 void attn_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o,
               c10::optional<torch::Tensor> lse, torch::Tensor q_pos, int64_t L,
               int64_t kv_head_stride, double scale, bool causal,
-              c10::optional<torch::Tensor> status) {
+              c10::optional<torch::Tensor> status, int64_t variant) {
   check_cuda_bf16(q, "q");
   check_cuda_bf16(k, "k");
   check_cuda_bf16(v, "v");
@@ -116,6 +128,7 @@ void attn_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o
   a.scale = float(scale);
   a.causal = causal ? 1 : 0;
   a.status = ptr_or_null<int>(status);
+  a.variant = int(variant);
   HCP_CHECK_OK(hcp::attn::attn_fwd(a, cur_stream()));
 }
 
@@ -148,7 +161,7 @@ void rmsnorm(torch::Tensor x, torch::Tensor w, torch::Tensor y, double eps) {
 void gemv(torch::Tensor x, torch::Tensor W, int64_t epi, c10::optional<torch::Tensor> bias,
           c10::optional<torch::Tensor> y_f32, c10::optional<torch::Tensor> y_bf16,
           c10::optional<torch::Tensor> argmax, c10::optional<torch::Tensor> norm_w, double eps,
-          int64_t index_base) {
+          int64_t index_base, std::vector<torch::Tensor> prefetch) {
   check_cuda_bf16(x, "x");
   check_cuda_bf16(W, "W");
   const c10::cuda::CUDAGuard g(x.device());
@@ -169,6 +182,7 @@ void gemv(torch::Tensor x, torch::Tensor W, int64_t epi, c10::optional<torch::Te
   a.argmax = ptr_or_null<unsigned long long>(argmax);
   a.index_base = int(index_base);
   TORCH_CHECK(index_base >= 0 && index_base + a.N < (int64_t(1) << 31), "index_base out of range");
+  a.pf = make_prefetch(prefetch);
   a.num_sms = sm_count(x.get_device());
   a.norm_w = ptr_or_null<const __nv_bfloat16>(norm_w);
   a.eps = float(eps);
@@ -474,7 +488,7 @@ class PyRuntime {
                    double scale, int64_t splits, torch::Tensor part_o, torch::Tensor part_lse,
                    torch::Tensor counters, c10::optional<torch::Tensor> epoch_src,
                    int64_t epoch_mul, int64_t epoch_add, c10::optional<torch::Tensor> final_out,
-                   c10::optional<torch::Tensor> combine_out) {
+                   c10::optional<torch::Tensor> combine_out, std::vector<torch::Tensor> prefetch) {
     check_cuda_bf16(q, "q");
     const c10::cuda::CUDAGuard g(q.device());
     const auto& c = rt_.config();
@@ -529,6 +543,7 @@ class PyRuntime {
       a.group_stride = c.max_batch * c.geom.hkv;
       a.budget_ns = c.peer_wait_budget_ns;
     }
+    a.pf = make_prefetch(prefetch);
     HCP_CHECK_OK(hcp::dec::decode_attn(a, cur_stream()));
   }
 
@@ -537,7 +552,7 @@ class PyRuntime {
                      c10::optional<torch::Tensor> norm_w, double eps, torch::Tensor pos,
                      torch::Tensor cos_t, torch::Tensor sin_t, int64_t layer,
                      torch::Tensor page_tables, torch::Tensor owner, torch::Tensor slot,
-                     torch::Tensor q_out) {
+                     torch::Tensor q_out, std::vector<torch::Tensor> prefetch) {
     check_cuda_bf16(x, "x");
     check_cuda_bf16(w, "w");
     check_cuda_bf16(q_out, "q_out");
@@ -578,6 +593,7 @@ class PyRuntime {
     r.slot = slot.data_ptr<int>();
     r.owner_stride = int(owner.size(1));
     r.status = rt_.status();
+    a.pf = make_prefetch(prefetch);
     HCP_CHECK_OK(hcp::dec::gemv(a, cur_stream()));
   }
 
@@ -701,12 +717,16 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm", &gemm, "tcgen05 GEMM with fused epilogue", py::arg("A"), py::arg("B"), py::arg("C"),
         py::arg("epi") = 0, py::arg("bias") = py::none(), py::arg("R") = py::none(),
         py::arg("status") = py::none());
-  m.def("attn_fwd", &attn_fwd, "tcgen05 flash attention with LSE and position-causal skip");
+  m.def("attn_fwd", &attn_fwd, "tcgen05 flash attention with LSE and position-causal skip",
+        py::arg("q"), py::arg("k"), py::arg("v"), py::arg("o"), py::arg("lse"), py::arg("q_pos"),
+        py::arg("L"), py::arg("kv_head_stride"), py::arg("scale"), py::arg("causal"),
+        py::arg("status") = py::none(), py::arg("variant") = 0);
   m.def("embedding", &embedding, py::arg("ids"), py::arg("W"), py::arg("out"), py::arg("status") = py::none());
   m.def("rmsnorm", &rmsnorm);
   m.def("gemv", &gemv, py::arg("x"), py::arg("W"), py::arg("epi"), py::arg("bias") = py::none(),
         py::arg("y_f32") = py::none(), py::arg("y_bf16") = py::none(), py::arg("argmax") = py::none(),
-        py::arg("norm_w") = py::none(), py::arg("eps") = 1e-6, py::arg("index_base") = 0);
+        py::arg("norm_w") = py::none(), py::arg("eps") = 1e-6, py::arg("index_base") = 0,
+        py::arg("prefetch") = std::vector<torch::Tensor>{});
   m.def("fill_u64", &fill_u64);
   m.def("argmax_finalize", &argmax_finalize, py::arg("packed"), py::arg("tok32") = py::none(),
         py::arg("tok64") = py::none());
@@ -756,8 +776,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       .def("decode_attn", &PyRuntime::decode_attn, py::arg("q"), py::arg("layer"), py::arg("page_tables"),
            py::arg("n_tokens"), py::arg("scale"), py::arg("splits"), py::arg("part_o"),
            py::arg("part_lse"), py::arg("counters"), py::arg("epoch_src"), py::arg("epoch_mul"),
-           py::arg("epoch_add"), py::arg("final_out") = py::none(), py::arg("combine_out") = py::none())
-      .def("qkv_gemv_rope", &PyRuntime::qkv_gemv_rope)
+           py::arg("epoch_add"), py::arg("final_out") = py::none(), py::arg("combine_out") = py::none(),
+           py::arg("prefetch") = std::vector<torch::Tensor>{})
+      .def("qkv_gemv_rope", &PyRuntime::qkv_gemv_rope, py::arg("x"), py::arg("w"), py::arg("bias"),
+           py::arg("norm_w"), py::arg("eps"), py::arg("pos"), py::arg("cos_t"), py::arg("sin_t"),
+           py::arg("layer"), py::arg("page_tables"), py::arg("owner"), py::arg("slot"),
+           py::arg("q_out"), py::arg("prefetch") = std::vector<torch::Tensor>{})
       .def("decode_combine", &PyRuntime::decode_combine)
       .def("o_proj_combine", &PyRuntime::o_proj_combine, py::arg("x"), py::arg("w"), py::arg("y"),
            py::arg("epoch_src"), py::arg("epoch_mul"), py::arg("epoch_add"))

@@ -34,6 +34,15 @@
 // (only when the running max grows by more than 2^8), a share of the exponentials (POLY of every
 // 8 pairs) on the FMA pipe, a mask-free variant for tiles below every row's causal bound.
 // Registers: warpgroup 0 hands registers to the softmax warpgroups with setmaxnreg.
+//
+// Pipelined variant (PIPE, head_dim 64, one stream per q tile): P goes to TMEM columns of its own
+// (S_i at 128 i, O_i at 256 + 64 i, P_i at 384 + 64 i), so the scores' columns are free as soon
+// as the softmax has loaded them. The softmax threads signal that (s_free) right after their
+// TMEM load, and the MMA warp issues S_i(j+1) = Q_i K_{j+1}^T at once, while the same q tile's
+// exponentials of step j are still being computed; the softmax of step j + 1 in turn computes
+// its exponentials while P V of step j runs and only waits for that product (p_free) before it
+// stores P and rescales O. Per q tile the serial chain per KV tile is the softmax alone instead
+// of softmax + P V + Q K^T.
 #include <cstdlib>
 
 #include "attn_fwd_sm100.h"
@@ -51,7 +60,7 @@ constexpr int BKV = 128;     // kv rows per tile
 constexpr int QT = 2;        // q tiles per CTA
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 
-template <int D>
+template <int D, bool PIPE = false>
 struct Cfg {
   static constexpr int ATOMS = D / 64;           // 128-byte swizzle atoms along D
   static constexpr int Q_BYTES = BQ * D * 2;     // one q tile
@@ -60,6 +69,7 @@ struct Cfg {
   static constexpr int SMEM = 1024 + QT * Q_BYTES + 2 * STAGES * KV_BYTES + 4096;
   static constexpr int TMEM_COLS = 512;
   static constexpr int O_COL = 256;
+  static constexpr int P_COL = 384;              // PIPE: P_i at P_COL + 64 i (head_dim 64)
   // threads: warpgroup 0 (TMA, MMA, TMEM allocator, idle) + one warpgroup per softmax stream
   __host__ __device__ static constexpr int threads(int hv) { return 128 + QT * hv * 128; }
   // register split (setmaxnreg): 128 x wg0 + (threads - 128) x sm must not exceed the launch's
@@ -67,6 +77,7 @@ struct Cfg {
   // <= 61440)
   __host__ __device__ static constexpr int wg0_regs(int hv) { return 88; }
   __host__ __device__ static constexpr int sm_regs(int hv) { return hv == 1 ? 208 : 96; }
+  static_assert(!PIPE || D == 64, "the pipelined variant needs head_dim 64 (TMEM columns)");
 };
 
 struct KParams {
@@ -221,16 +232,97 @@ __device__ __forceinline__ void softmax_step(uint32_t s_addr, uint32_t o_addr, i
   l_sum = l_sum * alpha + ((rs0.x + rs0.y) + (rs1.x + rs1.y));
 }
 
+// One step of a pipelined stream (PIPE: 128 key columns per q-tile row, P in its own TMEM
+// columns). After the TMEM load of S the thread arrives on s_free (the MMA warp may write
+// S(j+1) into the same columns); the exponentials are computed into registers, then the thread
+// waits until P V of the previous step has completed (p_free: P's columns and O are free) before
+// it rescales O (lazy, as above) and stores P. Returns false if a bounded wait ran out.
+template <int D, int POLY, bool MASK>
+__device__ __forceinline__ bool softmax_step_pipe(uint32_t s_addr, uint32_t o_addr, uint32_t p_addr,
+                                                  int kv0, int lim, float scale_log2, int j,
+                                                  uint64_t* s_free, uint64_t* p_free, int* status,
+                                                  float& m_ref, float& l_sum) {
+  constexpr int CW = BKV;
+  uint32_t r[CW];
+#pragma unroll
+  for (int c = 0; c < CW / 32; ++c) tmem_ld32(s_addr + c * 32, r + c * 32);
+  tmem_wait_ld();
+  tc_fence_before();
+  mbar_arrive(s_free);
+  if (MASK) {
+#pragma unroll
+    for (int e = 0; e < CW; ++e)
+      if (kv0 + e > lim) r[e] = __float_as_uint(-INFINITY);
+  }
+  float tmax;
+  {
+    float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+    for (int e = 0; e < CW; e += 8)
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        m4[k] = max3f(m4[k], __uint_as_float(r[e + 2 * k]), __uint_as_float(r[e + 2 * k + 1]));
+    tmax = max3f(m4[0], m4[1], fmaxf(m4[2], m4[3])) * scale_log2;
+  }
+  float alpha = 1.f;
+  bool resc = false;
+  if (tmax > m_ref + kRescaleThreshold || (m_ref == -INFINITY && tmax > -INFINITY)) {
+    alpha = (m_ref == -INFINITY) ? 0.f : fast_exp2(m_ref - tmax);
+    m_ref = tmax;
+    resc = true;
+  }
+  const float m_use = (m_ref == -INFINITY) ? 0.f : m_ref;
+  float2 rs0 = make_float2(0.f, 0.f), rs1 = make_float2(0.f, 0.f);
+  const float2 negm = make_float2(-m_use, -m_use);
+  const float2 sc2 = make_float2(scale_log2, scale_log2);
+  uint32_t pk[CW / 2];
+#pragma unroll
+  for (int e = 0; e < CW; e += 2) {
+    const float2 x = __ffma2_rn(make_float2(__uint_as_float(r[e]), __uint_as_float(r[e + 1])), sc2, negm);
+    float2 pp;
+    if (POLY > 0 && ((e >> 1) & 7) >= 8 - POLY) {
+      pp = poly_exp2_x2(x);
+    } else {
+      pp.x = fast_exp2(x.x);
+      pp.y = fast_exp2(x.y);
+    }
+    if ((e >> 1) & 1) rs1 = __fadd2_rn(rs1, pp);
+    else rs0 = __fadd2_rn(rs0, pp);
+    pk[e >> 1] = pack_bf16x2(pp.x, pp.y);
+  }
+  if (j > 0) {
+    if (!mbar_wait(p_free, uint32_t(j - 1) & 1u, status, 215)) return false;
+    tc_fence_after();
+    if (__any_sync(0xffffffffu, resc)) {
+#pragma unroll 1
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t o[32];
+        tmem_ld32(o_addr + c * 32, o);
+        tmem_wait_ld();
+#pragma unroll
+        for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+        tmem_st32(o_addr + c * 32, o);
+      }
+    }
+  }
+#pragma unroll
+  for (int hh = 0; hh < CW / 32; ++hh) tmem_st16(p_addr + hh * 16, pk + hh * 16);
+  tmem_wait_st();
+  l_sum = l_sum * alpha + ((rs0.x + rs0.y) + (rs1.x + rs1.y));
+  return true;
+}
+
 // POLY: how many of every 8 exponential pairs use the FMA-pipe polynomial instead of the MUFU.
 // HV: softmax warpgroups per q tile. HV = 2 (head_dim 64) splits each 128-key tile into two
 // 64-column streams with their own running max, row sum and O accumulator (TMEM: S 2 x 128
 // columns, O 4 x 64), so four warpgroups share the softmax work, and merges the two streams of a
 // row in the epilogue. HV = 1 (head_dim 128) keeps one stream per q tile.
-template <int D, int POLY, int HV, bool RING>
+template <int D, int POLY, int HV, bool RING, bool PIPE>
 __global__ void __launch_bounds__(Cfg<D>::threads(HV), 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, KParams p) {
-  using C = Cfg<D>;
+  using C = Cfg<D, PIPE>;
+  static_assert(!PIPE || HV == 1, "the pipelined variant has one stream per q tile");
   constexpr int CW = BKV / HV;               // key columns per stream
   constexpr int NS = QT * HV;                // softmax streams per CTA
   static_assert(C::O_COL + NS * D <= C::TMEM_COLS, "TMEM columns");
@@ -250,7 +342,9 @@ __global__ void __launch_bounds__(Cfg<D>::threads(HV), 1)
   uint64_t* p_full = s_full + QT;          // [NS]
   uint64_t* o_done = p_full + NS;          // [QT]
   uint64_t* merged = o_done + QT;          // [QT] HV = 2: both streams posted (m, l)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(merged + QT);
+  uint64_t* s_free = merged + QT;          // [QT] PIPE: the stream has loaded S (128 arrivals)
+  uint64_t* p_free = s_free + QT;          // [QT] PIPE: P V of the stream's last step completed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(p_free + QT);
   int* s_qmin = reinterpret_cast<int*>(tmem_slot + 1);  // [QT]
   int* s_qmax = s_qmin + QT;                            // [QT]
   float* s_ml = reinterpret_cast<float*>(s_qmax + QT);  // [QT][2][BQ] m, l of stream h = 1
@@ -281,6 +375,8 @@ __global__ void __launch_bounds__(Cfg<D>::threads(HV), 1)
       mbar_init(&s_full[i], 1);
       mbar_init(&o_done[i], 1);
       mbar_init(&merged[i], BQ);
+      mbar_init(&s_free[i], BQ);
+      mbar_init(&p_free[i], 1);
       s_qmin[i] = 0x7fffffff;
       s_qmax[i] = -1;
     }
@@ -406,7 +502,55 @@ __global__ void __launch_bounds__(Cfg<D>::threads(HV), 1)
         umma_commit(&s_full[1]);
         umma_commit(&k_empty[0]);
       }
-      for (int j = 0; ok && j < n_tiles; ++j) {
+      if (PIPE) {
+        // S_i(j+1) as soon as stream i has loaded S_i(j); P_i(j) V_j as soon as it stored P_i(j)
+        for (int j = 0; ok && j < n_tiles; ++j) {
+          const int s = j % C::STAGES;
+          const int s1 = (j + 1) % C::STAGES;
+          const bool more = j + 1 < n_tiles;
+          if (more) {
+            if (!mbar_wait(&k_full[s1], ((j + 1) / C::STAGES) & 1, p.status, 206)) {
+              ok = false;
+              break;
+            }
+#pragma unroll
+            for (int i = 0; i < QT; ++i) {
+              if (!mbar_wait(&s_free[i], j & 1, p.status, 216)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+              issue_qk(i, s1);
+              umma_commit(&s_full[i]);
+            }
+            if (!ok) break;
+            umma_commit(&k_empty[s1]);
+          }
+          if (!mbar_wait(&v_full[s], (j / C::STAGES) & 1, p.status, 205)) {
+            ok = false;
+            break;
+          }
+          const uint32_t sv = smem_u32(sV + s * C::KV_BYTES);
+#pragma unroll
+          for (int i = 0; i < QT; ++i) {
+            if (!mbar_wait(&p_full[i], j & 1, p.status, 204 + 3 * i)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+#pragma unroll
+            for (int kk = 0; kk < BKV / 16; ++kk)
+              umma_bf16_ts(tmem_base + C::O_COL + i * D, tmem_base + C::P_COL + i * (BKV / 2) + kk * 8,
+                           sdesc_sw128(sv + kk * 2048, BKV * 128, 1024), idesc_o,
+                           (j > 0 || kk > 0) ? 1u : 0u);
+            umma_commit(&p_free[i]);
+            if (!more) umma_commit(&o_done[i]);
+          }
+          if (!ok) break;
+          umma_commit(&v_empty[s]);
+        }
+      }
+      for (int j = 0; !PIPE && ok && j < n_tiles; ++j) {
         const int s = j % C::STAGES;
         const int s1 = (j + 1) % C::STAGES;
         const bool more = j + 1 < n_tiles;
@@ -458,6 +602,7 @@ __global__ void __launch_bounds__(Cfg<D>::threads(HV), 1)
     float m_ref = -INFINITY;  // max used for exponentiation (log2 domain)
     float l_sum = 0.f;
     bool ok = true;
+    const uint32_t p_addr = tmem_base + lane_off + uint32_t(C::P_COL + tile * (BKV / 2));
     for (int j = 0; j < n_tiles; ++j) {
       const int t = kv_tile_at(j, n_tiles);
       if (!mbar_wait(&s_full[tile], j & 1, p.status, 208)) {
@@ -468,10 +613,18 @@ __global__ void __launch_bounds__(Cfg<D>::threads(HV), 1)
       const int kv0 = t * BKV + half * CW;
       const int lim = p.causal ? min(my_pos, p.L - 1) : p.L - 1;  // last visible kv position
       // the masked variant only for tiles that cross some row's bound (diagonal / tail tiles)
-      if (__any_sync(0xffffffffu, kv0 + CW - 1 > lim))
+      const bool masked = __any_sync(0xffffffffu, kv0 + CW - 1 > lim);
+      if (PIPE) {
+        ok = masked ? softmax_step_pipe<D, POLY, true>(s_addr, o_addr, p_addr, kv0, lim, p.scale_log2, j,
+                                                       &s_free[tile], &p_free[tile], p.status, m_ref, l_sum)
+                    : softmax_step_pipe<D, POLY, false>(s_addr, o_addr, p_addr, kv0, lim, p.scale_log2, j,
+                                                        &s_free[tile], &p_free[tile], p.status, m_ref, l_sum);
+        if (!ok) break;
+      } else if (masked) {
         softmax_step<D, POLY, CW, true>(s_addr, o_addr, kv0, lim, p.scale_log2, j > 0, m_ref, l_sum);
-      else
+      } else {
         softmax_step<D, POLY, CW, false>(s_addr, o_addr, kv0, lim, p.scale_log2, j > 0, m_ref, l_sum);
+      }
       tc_fence_before();
       mbar_arrive(&p_full[st]);
     }
@@ -558,7 +711,7 @@ __global__ void __launch_bounds__(Cfg<D>::threads(HV), 1)
   }
 }
 
-template <int D, int POLY, int HV, bool RING>
+template <int D, int POLY, int HV, bool RING, bool PIPE = false>
 static cudaError_t launch(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                           const KParams& p, cudaStream_t stream) {
   static_assert(Cfg<D>::threads(HV) <= 1024, "threads");
@@ -567,23 +720,24 @@ static cudaError_t launch(const CUtensorMap& tq, const CUtensorMap& tk, const CU
                 "register split exceeds the launch's registers");
   static std::atomic<unsigned long long> attr{0};
   cudaError_t e = once_per_device(attr, [] {
-    return cudaFuncSetAttribute(attn_fwd_kernel<D, POLY, HV, RING>,
+    return cudaFuncSetAttribute(attn_fwd_kernel<D, POLY, HV, RING, PIPE>,
                                 cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<D>::SMEM);
   });
   if (e != cudaSuccess) return e;
   const int grid = p.num_pairs * p.H;
-  attn_fwd_kernel<D, POLY, HV, RING><<<grid, Cfg<D>::threads(HV), Cfg<D>::SMEM, stream>>>(tq, tk, tv, p);
+  attn_fwd_kernel<D, POLY, HV, RING, PIPE><<<grid, Cfg<D>::threads(HV), Cfg<D>::SMEM, stream>>>(tq, tk, tv, p);
   return cudaGetLastError();
 }
 
-// Softmax streams per q tile for head_dim 64 (HCP_ATTN_HV=1 keeps one stream per tile).
+// Head_dim 64 kernel variant: HCP_ATTN_HV=2 two softmax streams per q tile, =1 one stream,
+// =3 one stream with P in its own TMEM columns (the pipelined variant, PIPE).
 static int hv64() {
   static int env = -2;
   if (env == -2) {
     const char* s = getenv("HCP_ATTN_HV");
     env = (s && *s) ? atoi(s) : 2;
   }
-  return env == 1 ? 1 : 2;
+  return (env == 1 || env == 3) ? env : 2;
 }
 
 // Polynomial share (out of 8 exponential pairs), the same for head_dim 64 and 128; HCP_ATTN_POLY
@@ -600,27 +754,29 @@ static int poly_share() {
   return 3;
 }
 
-template <int D, int HV>
+template <int D, int HV, bool PIPE = false>
 static cudaError_t launch_hv(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                              const KParams& p, cudaStream_t stream) {
   switch (poly_share()) {
-    case 2: return launch<D, 2, HV, false>(tq, tk, tv, p, stream);
-    case 3: return launch<D, 3, HV, false>(tq, tk, tv, p, stream);
-    case 4: return launch<D, 4, HV, false>(tq, tk, tv, p, stream);
-    default: return launch<D, 0, HV, false>(tq, tk, tv, p, stream);
+    case 2: return launch<D, 2, HV, false, PIPE>(tq, tk, tv, p, stream);
+    case 3: return launch<D, 3, HV, false, PIPE>(tq, tk, tv, p, stream);
+    case 4: return launch<D, 4, HV, false, PIPE>(tq, tk, tv, p, stream);
+    default: return launch<D, 0, HV, false, PIPE>(tq, tk, tv, p, stream);
   }
 }
 
 template <int D>
 static cudaError_t launch_d(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
-                            const KParams& p, cudaStream_t stream) {
-  const bool hv2 = D == 64 && hv64() == 2;
+                            const KParams& p, int variant, cudaStream_t stream) {
+  const int v = D == 64 ? (variant >= 1 && variant <= 3 ? variant : hv64()) : 1;
   if (p.ring.tile_src != nullptr) {
     // the in-kernel ring (push warps, per-tile waits, consumed release) is compiled into its own
     // variants, with the default exponential split, so the single-rank kernels carry none of it
-    return hv2 ? launch<64, 3, 2, true>(tq, tk, tv, p, stream) : launch<D, 3, 1, true>(tq, tk, tv, p, stream);
+    if (v == 3) return launch<64, 3, 1, true, true>(tq, tk, tv, p, stream);
+    return v == 2 ? launch<64, 3, 2, true>(tq, tk, tv, p, stream) : launch<D, 3, 1, true>(tq, tk, tv, p, stream);
   }
-  if (hv2) return launch_hv<64, 2>(tq, tk, tv, p, stream);
+  if (v == 3) return launch_hv<64, 1, true>(tq, tk, tv, p, stream);
+  if (v == 2) return launch_hv<64, 2>(tq, tk, tv, p, stream);
   return launch_hv<D, 1>(tq, tk, tv, p, stream);
 }
 
@@ -671,7 +827,9 @@ const char* attn_fwd(const AttnArgs& a, cudaStream_t stream) {
   }
   p.wait_budget_ns = a.wait_budget_ns;
   p.status = a.status;
-  cudaError_t e = a.D == 64 ? launch_d<64>(tq, tk, tv, p, stream) : launch_d<128>(tq, tk, tv, p, stream);
+  if (a.variant < 0 || a.variant > 3) return "attn: variant must be 0 to 3";
+  cudaError_t e = a.D == 64 ? launch_d<64>(tq, tk, tv, p, a.variant, stream)
+                            : launch_d<128>(tq, tk, tv, p, a.variant, stream);
   return e == cudaSuccess ? nullptr : cudaGetErrorString(e);
 }
 

@@ -47,6 +47,10 @@ struct AttnArgs {
   RingArgs ring;            // ring.tile_src == nullptr: every KV row is already in place
   unsigned long long wait_budget_ns;
   int* status;
+  // head_dim 64 kernel variant: 0 = the build's default (HCP_ATTN_HV), 1 = one softmax stream
+  // per q tile, 2 = two 64-column streams per tile, 3 = one stream with P in its own TMEM
+  // columns (pipelined Q K^T); head_dim 128 always runs one stream per tile
+  int variant;
 };
 
 const char* attn_fwd(const AttnArgs& args, cudaStream_t stream);

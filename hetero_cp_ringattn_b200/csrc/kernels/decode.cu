@@ -48,6 +48,26 @@ __device__ __forceinline__ uint4 ld_stream(const uint4* p) {
   return v;
 }
 
+// Thread 0 of each CTA: one async bulk prefetch into L2 of this CTA's slice of each range.
+__device__ __forceinline__ void prefetch_l2_slices(const L2Prefetch& pf) {
+  if (threadIdx.x != 0) return;
+  const unsigned long long nblk = (unsigned long long)gridDim.x * gridDim.y * gridDim.z;
+  const unsigned long long blk =
+      blockIdx.x + (unsigned long long)gridDim.x * (blockIdx.y + (unsigned long long)gridDim.y * blockIdx.z);
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const unsigned long long total = pf.bytes[i];
+    if (pf.ptr[i] == nullptr || total == 0) continue;
+    const unsigned long long per = ((total + nblk - 1) / nblk + 15) & ~15ull;
+    const unsigned long long off = blk * per;
+    if (off >= total) continue;
+    const unsigned long long n = total - off < per ? total - off : per;
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;"
+                 ::"l"(static_cast<const char*>(pf.ptr[i]) + off), "r"(uint32_t(n))
+                 : "memory");
+  }
+}
+
 __device__ __forceinline__ unsigned long long pack_argmax(float v, int idx) {
   uint32_t u = __float_as_uint(v);
   u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);  // order-preserving float -> uint
@@ -97,6 +117,7 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(GemvArgs a) {
   };
   uint4 bufA[NWR][KC], bufB[NWR][KC];
   pdl_trigger();
+  prefetch_l2_slices(a.pf);
   if (items > 0) load(0, bufA);  // weights: nothing in flight writes them
   pdl_wait();                    // x, residual rows, positions, ... come from predecessors
   if (NORM) {
@@ -354,6 +375,9 @@ const char* gemv(const GemvArgs& a, cudaStream_t s) {
     return "gemv: QKV rope epilogue needs q_out and N = (H + 2 Hkv) D";
   if ((reinterpret_cast<uintptr_t>(a.W) | reinterpret_cast<uintptr_t>(a.x)) & 15)
     return "gemv: W/x must be 16-byte aligned";
+  for (int i = 0; i < 2; ++i)
+    if (a.pf.ptr[i] && ((reinterpret_cast<uintptr_t>(a.pf.ptr[i]) | a.pf.bytes[i]) & 15))
+      return "gemv: L2 prefetch ranges must be 16-byte aligned multiples of 16 bytes";
   if (a.cmb.xslot != nullptr &&
       (a.epi != kGemvResidual || a.norm_w != nullptr || a.cmb.D % 8 || a.K != a.cmb.H * a.cmb.D ||
        a.cmb.ranks < 1 || a.cmb.ranks > GEMV_THREADS || a.cmb.row0 + a.B > a.cmb.slot_B ||
@@ -451,6 +475,7 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(const __grid_constant_
   // (copied from the host before the step) and the KV rows of earlier tokens, so the first
   // pipeline stages stream while the projection finishes.
   pdl_trigger();
+  prefetch_l2_slices(a.pf);               // later kernels' weights (before any early return)
   constexpr int NW = 4;                    // warps per CTA
   constexpr int CC = kDecCC;
   constexpr int DQ = D / 4;                // contiguous dims of a K row per lane in S = Q K^T
@@ -926,6 +951,9 @@ const char* decode_attn(const DecodeAttnArgs& a, cudaStream_t s) {
   if ((a.D != 64 && a.D != 128) || a.geom.page % kDecCC)
     return "decode_attn: head_dim must be 64 or 128 and the page a multiple of 64 rows";
   if (G > 8) return "decode_attn: at most 8 query heads per KV head";
+  for (int i = 0; i < 2; ++i)
+    if (a.pf.ptr[i] && ((reinterpret_cast<uintptr_t>(a.pf.ptr[i]) | a.pf.bytes[i]) & 15))
+      return "decode_attn: L2 prefetch ranges must be 16-byte aligned multiples of 16 bytes";
   if (a.pt_stride < 1) return "decode_attn: page-table row stride must be at least 1";
   if (reinterpret_cast<uintptr_t>(a.arena) & 15) return "decode_attn: arena must be 16-byte aligned";
   // the whole arena as one [rows, D] bf16 matrix; boxes of 64 rows x 64 dims, 128-byte swizzle

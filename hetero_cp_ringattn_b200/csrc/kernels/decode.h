@@ -17,6 +17,16 @@ enum GemvEpilogue : int {
   kGemvQkvRope = 4,   // QKV projection + bias + RoPE, q -> rope.q_out, k/v appended (GemvRopeArgs)
 };
 
+// Weights of later kernels of the decode step to pull into L2 while this kernel runs: CTA i of
+// n issues one bulk L2 prefetch of the i-th 1/n slice of each range when it starts (before its
+// dependency wait: weights are never written in flight). A decode step reads ~120 MB of weights
+// per layer in small latency-bound kernels; prefetched, the next kernel finds them in L2.
+// Ranges must start 16-byte aligned and be a multiple of 16 bytes long (null / 0: none).
+struct L2Prefetch {
+  const void* ptr[2];
+  unsigned long long bytes[2];
+};
+
 // kGemvQkvRope epilogue: the projection rows of a head are computed in rotation pairs (j, j + D/2),
 // rounded to bf16 (the bf16 linear output), rotated at pos[b] (q and k heads); q goes to q_out
 // [B, H, D], k and v to the arena slot slot[b, layer] when this rank stores the row
@@ -73,6 +83,7 @@ struct GemvArgs {
   float eps;
   GemvRopeArgs rope;           // kGemvQkvRope only
   GemvCombineArgs cmb;         // kGemvResidual only (optional)
+  L2Prefetch pf;               // optional
 };
 
 struct DecodeAttnArgs {
@@ -109,6 +120,7 @@ struct DecodeAttnArgs {
   unsigned long long epoch_mul;  // epoch = (*src) * mul + add
   unsigned long long epoch_add;
   int* status;
+  L2Prefetch pf;               // optional
 };
 
 struct DecodeCombineArgs {

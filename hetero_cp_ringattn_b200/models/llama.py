@@ -814,10 +814,12 @@ class DecodeGraph:
         K.embedding(self.tokens, w.embed, out=self.x)
         eps = cfg.rms_norm_eps
         single = e.world == 1
+        head = e.lm_head_slice if split else w.lm_head
+        pf = self.prefetch_plan(head)
         for li, lw in enumerate(w.layers):
             # RMSNorm + QKV GEMV whose epilogue applies RoPE, writes q and appends k/v on the owner
             rt.qkv_gemv_rope(self.x, lw.wqkv, lw.bqkv, lw.in_norm, eps, self.pos, e.cos, e.sin, li,
-                             self.pt, self.owner, self.slot, self.q)
+                             self.pt, self.owner, self.slot, self.q, prefetch=pf[li][0])
             # split-KV attention; on one rank its last CTA writes the layer output directly.
             # With several ranks the rank's (O, LSE) partial goes into every rank's slots and
             # the log-sum-exp combine in rank order follows a bounded wait for the other ranks'
@@ -828,7 +830,8 @@ class DecodeGraph:
             mode = "single" if single else e.env.decode_combine
             rt.decode_attn(self.q, li, self.pt, self.ntok[li], e.scale, self.splits, self.part_o,
                            self.part_l, self.counters, e.dec_step, e.L, li + 1,
-                           self.o if single else None, self.o if mode == "attn" else None)
+                           self.o if single else None, self.o if mode == "attn" else None,
+                           prefetch=pf[li][1])
             if mode == "launch":
                 rt.decode_combine(self.o, self.B, e.H, e.dec_step, e.L, li + 1)
             launches.count(3 if mode == "launch" else 2)
@@ -836,8 +839,9 @@ class DecodeGraph:
                 rt.o_proj_combine(self.o, lw.wo, self.x, e.dec_step, e.L, li + 1)
                 launches.count()
             else:
-                K.gemv(self.o, lw.wo, "residual", y_bf16=self.x)
-            K.gemv(self.x, lw.wgu, "swiglu", y_bf16=self.g, norm_w=lw.post_norm, eps=eps)
+                K.gemv(self.o, lw.wo, "residual", y_bf16=self.x, prefetch=pf[li][2])
+            K.gemv(self.x, lw.wgu, "swiglu", y_bf16=self.g, norm_w=lw.post_norm, eps=eps,
+                   prefetch=pf[li][3])
             K.gemv(self.g, lw.wd, "residual", y_bf16=self.x)
         nat.fill_u64(self.am, 0)
         if split:
@@ -851,6 +855,25 @@ class DecodeGraph:
                    norm_w=w.final_norm, eps=eps)
             nat.argmax_finalize(self.am, self.tokens, self.out_tok)
         launches.count(2)
+
+    def prefetch_plan(self, head: torch.Tensor) -> list:
+        """Per layer, the weights each decode kernel pulls into L2 for a later kernel while it
+        runs (HCP_DECODE_PREFETCH=1): the QKV GEMV the output projection's, the
+        attention (which streams KV at a fraction of HBM bandwidth) the gate/up weights, the
+        output projection the down projection's, gate/up the next layer's QKV weights or, after
+        the last layer, an LM head of at most 96 MB (the vocabulary slice on several ranks)."""
+        w = self.e.w
+        L = len(w.layers)
+        if not self.e.env.decode_prefetch:
+            return [([], [], [], [])] * L
+        plan = []
+        for li, lw in enumerate(w.layers):
+            if li + 1 < L:
+                nxt = [w.layers[li + 1].wqkv]
+            else:
+                nxt = [head] if head.numel() * head.element_size() <= (96 << 20) else []
+            plan.append(([lw.wo], [lw.wgu], [lw.wd], nxt))
+        return plan
 
     def run(self, req_ids, tokens, pos, owner, slot, ntok, split: bool = False) -> torch.Tensor:
         n = len(req_ids)

@@ -82,8 +82,10 @@ def gemm(a: torch.Tensor, w: torch.Tensor, epi: str = "store", bias: Optional[to
 # --------------------------------------------------------------------------- attention
 def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, q_pos: torch.Tensor, L: int,
               causal: bool = True, scale: Optional[float] = None,
-              want_lse: bool = True, status: Optional[torch.Tensor] = None):
+              want_lse: bool = True, status: Optional[torch.Tensor] = None, variant: int = 0):
     """Flash attention of q [T,H,D] over position-ordered k/v [Hkv, Lcap, D] (rows 0..L-1).
+    `variant` picks the head_dim-64 kernel (0: the default; 1: one softmax stream per q tile;
+    2: two streams; 3: pipelined, P in its own TMEM columns).
 
     Returns (o [T,H,D], lse [H,T] natural log or None)."""
     t, h, d = q.shape
@@ -96,7 +98,7 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, q_pos: torch.Te
         return o.to(q.dtype), (lse if want_lse else None)
     o = torch.empty_like(q)
     lse = torch.empty(h, t, dtype=torch.float32, device=q.device) if want_lse else None
-    native().attn_fwd(q, k, v, o, lse, q_pos, L, k.stride(0), scale, causal, status)
+    native().attn_fwd(q, k, v, o, lse, q_pos, L, k.stride(0), scale, causal, status, variant)
     launches.count()
     return o, lse
 
@@ -129,10 +131,11 @@ def embedding(ids: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = 
 
 # --------------------------------------------------------------------------- GEMV (decode)
 def gemv(x: torch.Tensor, w: torch.Tensor, epi: str, bias=None, y_f32=None, y_bf16=None,
-         argmax=None, norm_w=None, eps: float = 1e-6, index_base: int = 0):
+         argmax=None, norm_w=None, eps: float = 1e-6, index_base: int = 0, prefetch=()):
     """Decode GEMV y = f(x) @ w.T with a fused epilogue; `norm_w` applies RMSNorm to x first.
     With the "argmax" epilogue `index_base` is added to every row index of the packed maximum
-    (w is then the vocabulary slice starting at that row)."""
+    (w is then the vocabulary slice starting at that row). `prefetch`: up to two contiguous weight
+    tensors of later kernels that the launch pulls into L2 while it runs."""
     if not x.is_cuda:
         if norm_w is not None:
             x = ref.rmsnorm(x, norm_w, eps)
@@ -152,6 +155,7 @@ def gemv(x: torch.Tensor, w: torch.Tensor, epi: str, bias=None, y_f32=None, y_bf
             if y_f32 is not None:
                 y_f32.copy_(y)
             return y.argmax(-1) + index_base
-    native().gemv(x, w, GEMV[epi], bias, y_f32, y_bf16, argmax, norm_w, eps, index_base)
+    native().gemv(x, w, GEMV[epi], bias, y_f32, y_bf16, argmax, norm_w, eps, index_base,
+                  list(prefetch))
     launches.count()
     return y_bf16 if y_bf16 is not None else y_f32

@@ -84,9 +84,9 @@ def _stage(k_tok, v_tok, cap):
     return ks, vs
 
 
-@pytest.mark.parametrize("d", [64, 128])
+@pytest.mark.parametrize("d,variant", [(64, 0), (64, 1), (64, 3), (128, 0)])
 @pytest.mark.parametrize("layout", ["prefix", "suffix", "striped", "noncausal"])
-def test_attention(dev, d, layout):
+def test_attention(dev, d, variant, layout):
     torch.manual_seed(3)
     L, h, hkv = 700, 8, 2
     q_all = torch.randn(L, h, d, device=dev, dtype=torch.bfloat16)
@@ -104,7 +104,7 @@ def test_attention(dev, d, layout):
     q = q_all[pos].contiguous()
     ks, vs = _stage(k_all, v_all, cap=1024)
     st = status_tensor(dev)
-    o, lse = K.attention(q, ks, vs, pos.int(), L, causal=causal, status=st)
+    o, lse = K.attention(q, ks, vs, pos.int(), L, causal=causal, status=st, variant=variant)
     assert_status_clean(st)
     ro, rl = ref.full_attention(q.float(), k_all.float(), v_all.float(), pos, torch.arange(L, device=dev),
                                 causal=causal)
@@ -112,7 +112,8 @@ def test_attention(dev, d, layout):
     assert (lse - rl).abs().max() < 2e-2
 
 
-def test_attention_long_gqa(dev):
+@pytest.mark.parametrize("variant", [0, 3])
+def test_attention_long_gqa(dev, variant):
     torch.manual_seed(4)
     L, h, hkv, d = 4096, 32, 8, 64
     q = torch.randn(L, h, d, device=dev, dtype=torch.bfloat16)
@@ -121,7 +122,7 @@ def test_attention_long_gqa(dev):
     pos = torch.arange(L, device=dev)
     ks, vs = _stage(k, v, cap=L)
     st = status_tensor(dev)
-    o, lse = K.attention(q, ks, vs, pos.int(), L, causal=True, status=st)
+    o, lse = K.attention(q, ks, vs, pos.int(), L, causal=True, status=st, variant=variant)
     assert_status_clean(st)
     ro, rl = ref.full_attention(q.float(), k.float(), v.float(), pos, pos, causal=True)
     assert (o.float() - ro).abs().max() < 2e-2
