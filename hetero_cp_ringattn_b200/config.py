@@ -378,8 +378,13 @@ class EnvConfig:
     fused_qkv: Optional[bool] = None        # HCP_FUSED_QKV: the projection GEMM's epilogue does
                                             # RoPE + the K/V writes (default on; 0: GEMM + a
                                             # separate RoPE / K/V kernel)
-    decode_prefetch: bool = False           # HCP_DECODE_PREFETCH=1: decode kernels pull
-                                            # the next kernels' weights into L2 while they run
+    decode_prefetch: int = 0                # HCP_DECODE_PREFETCH: decode kernels pull later
+                                            # kernels' weights into L2 while they run (1: bulk
+                                            # prefetches of every GEMV's weights, 2: the same
+                                            # with per-line prefetches, 3: per-line, only the
+                                            # output and QKV projections' weights). Measured on
+                                            # B200 (Llama-3.2-1B, 32k, ms per token): off 1.09,
+                                            # 1: 1.19-1.20, 2: 1.20-1.22, 3: within the noise
     split_lm_head: bool = True              # HCP_SPLIT_LM_HEAD=0: every rank runs the whole LM
                                             # head in greedy decode steps (default: each rank
                                             # takes 1/N of the vocabulary and the ranks exchange
@@ -404,7 +409,7 @@ class EnvConfig:
                             else _env_choice("HCP_DECODE_COMBINE", "launch", ("launch", "gemv", "attn"))),
             fused_qkv=(_env_bool("HCP_FUSED_QKV", True) if os.environ.get("HCP_FUSED_QKV") else None),
             split_lm_head=_env_bool("HCP_SPLIT_LM_HEAD", True),
-            decode_prefetch=_env_bool("HCP_DECODE_PREFETCH", False),
+            decode_prefetch=_env_int("HCP_DECODE_PREFETCH", 0),
         )
 
 

@@ -49,6 +49,11 @@ cudaStream_t cur_stream() { return at::cuda::getCurrentCUDAStream().stream(); }
 hcp::dec::L2Prefetch make_prefetch(const std::vector<torch::Tensor>& ts) {
   TORCH_CHECK(ts.size() <= 2, "at most two L2 prefetch ranges");
   hcp::dec::L2Prefetch pf{};
+  static const int lines = [] {
+    const char* e = getenv("HCP_DECODE_PREFETCH");
+    return (e && atoi(e) >= 2) ? 1 : 0;
+  }();
+  pf.lines = lines;
   for (size_t i = 0; i < ts.size(); ++i) {
     TORCH_CHECK(ts[i].is_cuda() && ts[i].is_contiguous(), "prefetch ranges must be contiguous CUDA tensors");
     pf.ptr[i] = ts[i].data_ptr();

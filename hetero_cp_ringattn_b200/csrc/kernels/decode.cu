@@ -48,23 +48,29 @@ __device__ __forceinline__ uint4 ld_stream(const uint4* p) {
   return v;
 }
 
-// Thread 0 of each CTA: one async bulk prefetch into L2 of this CTA's slice of each range.
+// This CTA's slice of each range into L2: one async bulk prefetch by thread 0, or (pf.lines) a
+// 128-byte line prefetch per thread and line, which leaves the CTA's TMA unit to its own loads.
 __device__ __forceinline__ void prefetch_l2_slices(const L2Prefetch& pf) {
-  if (threadIdx.x != 0) return;
+  if (!pf.lines && threadIdx.x != 0) return;
   const unsigned long long nblk = (unsigned long long)gridDim.x * gridDim.y * gridDim.z;
   const unsigned long long blk =
       blockIdx.x + (unsigned long long)gridDim.x * (blockIdx.y + (unsigned long long)gridDim.y * blockIdx.z);
+  const int nthr = blockDim.x * blockDim.y * blockDim.z;
 #pragma unroll
   for (int i = 0; i < 2; ++i) {
     const unsigned long long total = pf.bytes[i];
     if (pf.ptr[i] == nullptr || total == 0) continue;
-    const unsigned long long per = ((total + nblk - 1) / nblk + 15) & ~15ull;
+    const unsigned long long per = ((total + nblk - 1) / nblk + 127) & ~127ull;
     const unsigned long long off = blk * per;
     if (off >= total) continue;
     const unsigned long long n = total - off < per ? total - off : per;
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;"
-                 ::"l"(static_cast<const char*>(pf.ptr[i]) + off), "r"(uint32_t(n))
-                 : "memory");
+    const char* base = static_cast<const char*>(pf.ptr[i]) + off;
+    if (!pf.lines) {
+      asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(base), "r"(uint32_t(n)) : "memory");
+    } else {
+      for (unsigned long long o = (unsigned long long)threadIdx.x * 128; o < n; o += (unsigned long long)nthr * 128)
+        asm volatile("prefetch.global.L2::evict_last [%0];" ::"l"(base + o) : "memory");
+    }
   }
 }
 

@@ -25,6 +25,7 @@ enum GemvEpilogue : int {
 struct L2Prefetch {
   const void* ptr[2];
   unsigned long long bytes[2];
+  int lines;   // 0: one bulk prefetch per CTA and range; 1: every thread prefetches 128-byte lines
 };
 
 // kGemvQkvRope epilogue: the projection rows of a head are computed in rotation pairs (j, j + D/2),

@@ -858,13 +858,15 @@ class DecodeGraph:
 
     def prefetch_plan(self, head: torch.Tensor) -> list:
         """Per layer, the weights each decode kernel pulls into L2 for a later kernel while it
-        runs (HCP_DECODE_PREFETCH=1): the QKV GEMV the output projection's, the
-        attention (which streams KV at a fraction of HBM bandwidth) the gate/up weights, the
-        output projection the down projection's, gate/up the next layer's QKV weights or, after
-        the last layer, an LM head of at most 96 MB (the vocabulary slice on several ranks)."""
+        runs (HCP_DECODE_PREFETCH=1 or 2; 3 keeps only the first and the last): the QKV GEMV
+        the output projection's, the attention (which streams KV at a fraction of HBM
+        bandwidth) the gate/up weights, the output projection the down projection's, gate/up
+        the next layer's QKV weights or, after the last layer, an LM head of at most 96 MB (the
+        vocabulary slice on several ranks)."""
         w = self.e.w
         L = len(w.layers)
-        if not self.e.env.decode_prefetch:
+        mode = self.e.env.decode_prefetch
+        if not mode:
             return [([], [], [], [])] * L
         plan = []
         for li, lw in enumerate(w.layers):
@@ -872,7 +874,10 @@ class DecodeGraph:
                 nxt = [w.layers[li + 1].wqkv]
             else:
                 nxt = [head] if head.numel() * head.element_size() <= (96 << 20) else []
-            plan.append(([lw.wo], [lw.wgu], [lw.wd], nxt))
+            if mode == 3:   # only the small projections' weights
+                plan.append(([lw.wo], [], [], nxt if li + 1 < L else []))
+            else:
+                plan.append(([lw.wo], [lw.wgu], [lw.wd], nxt))
         return plan
 
     def run(self, req_ids, tokens, pos, owner, slot, ntok, split: bool = False) -> torch.Tensor:
