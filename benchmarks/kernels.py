@@ -116,28 +116,41 @@ def bench_attn(args, dev, pk):
     cases = [(8192, args.head_dim)] if args.small else [(s, d) for d in (64, 128) for s in args.seqs]
     H, Hkv = 32, 8
     for L, D in cases:
-        q = torch.randn(L, H, D, device=dev, dtype=torch.bfloat16)
         k = torch.randn(Hkv, L, D, device=dev, dtype=torch.bfloat16)
         v = torch.randn_like(k)
-        pos = torch.arange(L, device=dev, dtype=torch.int32)
+        if args.cp > 1:
+            # one context-parallel rank's rows (zigzag, equal chunks) against the whole key range
+            from hetero_cp_ringattn_b200.parallel.capacity import equal_chunks
+            from hetero_cp_ringattn_b200.parallel.strategy import layout_positions
+            pos_np = layout_positions(equal_chunks(L, args.cp), args.strategy)[args.rank]
+            pos = torch.as_tensor(pos_np, device=dev).int()
+            fl = 4.0 * H * D * float((pos_np + 1).sum())
+        else:
+            pos = torch.arange(L, device=dev, dtype=torch.int32)
+            fl = causal_flops(L, L, H, D)
+        T = int(pos.numel())
+        q = torch.randn(T, H, D, device=dev, dtype=torch.bfloat16)
         iters = max(2, args.iters if L <= 32768 else 3)
-        fl = causal_flops(L, L, H, D)
-        variants = args.variants if D == 64 else [0]
-        # head_dim 64 variants timed in alternation (--variants 0,3), best of the repetitions
+        variants = [(vv, o) for vv in (args.variants if D == 64 else [0]) for o in args.orders]
+        # kernel variants / CTA orders timed in alternation (--variants 0,3 --orders 0,1), best of
+        # the repetitions
         best = {}
         for _ in range(args.reps):
-            for vv in variants:
-                t = timed(lambda: K.attention(q, k, v, pos, L, causal=True, variant=vv), iters)
-                best[vv] = min(best.get(vv, t), t)
-        for vv in variants[:-1]:
-            emit(kernel="attn_fwd_sm100", L=L, H=H, Hkv=Hkv, D=D, causal=True, variant=vv,
-                 ms=round(best[vv], 3), tflops=round(fl / best[vv] / 1e9, 1),
-                 frac_of_measured=round(fl / best[vv] / 1e9 / pk["tflops"], 3), peaks=pk["source"])
+            for vv, o in variants:
+                t = timed(lambda: K.attention(q, k, v, pos, L, causal=True, variant=vv, order=o), iters)
+                best[(vv, o)] = min(best.get((vv, o), t), t)
+        base = dict(kernel="attn_fwd_sm100", L=L, T=T, H=H, Hkv=Hkv, D=D, causal=True)
+        if args.cp > 1:
+            base.update(cp=args.cp, rank=args.rank, strategy=args.strategy)
+        for vv, o in variants[:-1]:
+            emit(**base, variant=vv, order=o, ms=round(best[(vv, o)], 3),
+                 tflops=round(fl / best[(vv, o)] / 1e9, 1),
+                 frac_of_measured=round(fl / best[(vv, o)] / 1e9 / pk["tflops"], 3), peaks=pk["source"])
         ms = best[variants[-1]]
-        row = dict(kernel="attn_fwd_sm100", L=L, H=H, Hkv=Hkv, D=D, causal=True,
-                   variant=variants[-1], ms=round(ms, 3), tflops=round(fl / ms / 1e9, 1),
+        row = dict(**base, variant=variants[-1][0], order=variants[-1][1], ms=round(ms, 3),
+                   tflops=round(fl / ms / 1e9, 1),
                    frac_of_measured=round(fl / ms / 1e9 / pk["tflops"], 3), peaks=pk["source"])
-        if not args.small and L <= 65536:
+        if not args.small and L <= 65536 and args.cp == 1:
             qs = q.transpose(0, 1).unsqueeze(0)
             ks, vs = k.unsqueeze(0), v.unsqueeze(0)
             ms_s = timed(lambda: F.scaled_dot_product_attention(qs, ks, vs, is_causal=True,
@@ -373,6 +386,10 @@ def main(argv=None):
     ap.add_argument("--variants", type=lambda s: [int(x) for x in s.split(",")], default=[0],
                     help="attn: head_dim-64 kernel variants to time (0 default, 1, 2, 3 pipelined)")
     ap.add_argument("--reps", type=int, default=1, help="attn: alternating repetitions")
+    ap.add_argument("--orders", type=lambda s: [int(x) for x in s.split(",")], default=[-1],
+                    help="attn: CTA orders to time (-1 kernel's choice, 0 KV-head major, 1 pair major)")
+    ap.add_argument("--cp", type=int, default=1, help="attn: time one rank's rows of this CP degree")
+    ap.add_argument("--rank", type=int, default=0, help="attn: the rank for --cp")
     ap.add_argument("--compare", action="store_true", help="also time the NCCL send/recv ring restatement")
     ap.add_argument("--serial", action="store_true",
                     help="ring: the serial ring (push, wait for every rank, attend) instead of the "

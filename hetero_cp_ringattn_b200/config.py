@@ -385,6 +385,8 @@ class EnvConfig:
                                             # output and QKV projections' weights). Measured on
                                             # B200 (Llama-3.2-1B, 32k, ms per token): off 1.09,
                                             # 1: 1.19-1.20, 2: 1.20-1.22, 3: within the noise
+    decode_splits: int = 0                  # HCP_DECODE_SPLITS: at most this many KV splits per
+                                            # (row, KV head) in decode attention (0: one wave)
     split_lm_head: bool = True              # HCP_SPLIT_LM_HEAD=0: every rank runs the whole LM
                                             # head in greedy decode steps (default: each rank
                                             # takes 1/N of the vocabulary and the ranks exchange
@@ -410,6 +412,7 @@ class EnvConfig:
             fused_qkv=(_env_bool("HCP_FUSED_QKV", True) if os.environ.get("HCP_FUSED_QKV") else None),
             split_lm_head=_env_bool("HCP_SPLIT_LM_HEAD", True),
             decode_prefetch=_env_int("HCP_DECODE_PREFETCH", 0),
+            decode_splits=_env_int("HCP_DECODE_SPLITS", 0),
         )
 
 

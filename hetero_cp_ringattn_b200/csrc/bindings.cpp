@@ -100,7 +100,7 @@ void gemm(torch::Tensor A, torch::Tensor B, torch::Tensor C, int64_t epi,
 void attn_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o,
               c10::optional<torch::Tensor> lse, torch::Tensor q_pos, int64_t L,
               int64_t kv_head_stride, double scale, bool causal,
-              c10::optional<torch::Tensor> status, int64_t variant) {
+              c10::optional<torch::Tensor> status, int64_t variant, int64_t order) {
   check_cuda_bf16(q, "q");
   check_cuda_bf16(k, "k");
   check_cuda_bf16(v, "v");
@@ -134,6 +134,7 @@ void attn_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o
   a.causal = causal ? 1 : 0;
   a.status = ptr_or_null<int>(status);
   a.variant = int(variant);
+  a.order = int(order);
   HCP_CHECK_OK(hcp::attn::attn_fwd(a, cur_stream()));
 }
 
@@ -725,7 +726,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn_fwd", &attn_fwd, "tcgen05 flash attention with LSE and position-causal skip",
         py::arg("q"), py::arg("k"), py::arg("v"), py::arg("o"), py::arg("lse"), py::arg("q_pos"),
         py::arg("L"), py::arg("kv_head_stride"), py::arg("scale"), py::arg("causal"),
-        py::arg("status") = py::none(), py::arg("variant") = 0);
+        py::arg("status") = py::none(), py::arg("variant") = 0, py::arg("order") = -1);
   m.def("embedding", &embedding, py::arg("ids"), py::arg("W"), py::arg("out"), py::arg("status") = py::none());
   m.def("rmsnorm", &rmsnorm);
   m.def("gemv", &gemv, py::arg("x"), py::arg("W"), py::arg("epi"), py::arg("bias") = py::none(),

@@ -88,6 +88,7 @@ struct KParams {
   float scale_log2;
   int causal;
   int num_pairs;        // ceil(num_q_tiles / 2)
+  int pair_major;       // CTA order: 1 = heaviest q-tile pairs first across all heads
   RingArgs ring;        // in-kernel KV ring (ring.tile_src == nullptr: off)
   unsigned long long wait_budget_ns;
   int* status;
@@ -351,16 +352,26 @@ __global__ void __launch_bounds__(Cfg<D>::threads(HV), 1)
 
   const int warp = threadIdx.x / 32;
 
-  // CTA order: KV-head major, so the CTAs resident at any time (one per SM) are the q heads of
-  // one GQA group over a run of q-tile pairs and stream the same K/V tiles in the same order
-  // (one KV head's K and V stay in L2 instead of every group's); within a group, heaviest tile
-  // pairs first (largest positions are last in local order), an LPT-like balance.
+  // CTA order. KV-head major (long contexts): the CTAs resident at any time (one per SM) are the
+  // q heads of one GQA group over a run of q-tile pairs and stream the same K/V tiles in the same
+  // order (one KV head's K and V stay in L2 instead of every group's); within a group, heaviest
+  // tile pairs first (largest positions are last in local order). Pair major (grids of a few
+  // waves): the heaviest pairs of all heads first, a global longest-first order that keeps the
+  // last wave short when there are few CTAs per SM (a context-parallel rank's share of the
+  // rows, whose zigzag halves differ widely in length).
   const int group = p.H / p.Hkv;
-  const int per_kv = p.num_pairs * group;
-  const int kv_head = int(blockIdx.x) / per_kv;
-  const int rem = int(blockIdx.x) % per_kv;
-  const int pair = p.num_pairs - 1 - rem / group;
-  const int head = kv_head * group + rem % group;
+  int pair, head;
+  if (p.pair_major) {
+    pair = p.num_pairs - 1 - int(blockIdx.x) / p.H;
+    head = int(blockIdx.x) % p.H;
+  } else {
+    const int per_kv = p.num_pairs * group;
+    const int kv_head = int(blockIdx.x) / per_kv;
+    const int rem = int(blockIdx.x) % per_kv;
+    pair = p.num_pairs - 1 - rem / group;
+    head = kv_head * group + rem % group;
+  }
+  const int kv_head = head / group;
   const int row0 = pair * QT * BQ;
 
   if (threadIdx.x == 0) {
@@ -812,6 +823,24 @@ const char* attn_fwd(const AttnArgs& a, cudaStream_t stream) {
   p.causal = a.causal;
   const int num_q_tiles = (a.T + BQ - 1) / BQ;
   p.num_pairs = (num_q_tiles + QT - 1) / QT;
+  // pair-major order when the grid is at most 8 waves of one CTA per SM (a context-parallel
+  // rank's share of the rows: measured on B200 at CP=8, 32k, head_dim 64, the slowest rank's
+  // attention 0.876 -> 0.804 ms); KV-head major for longer grids, where its L2 reuse wins (one
+  // rank at 32k: 5.52 vs 5.72 ms at head_dim 64, 7.31 vs 7.81 at 128). HCP_ATTN_ORDER=0 / 1
+  // forces one order, AttnArgs::order overrides both
+  {
+    static int env = -2;
+    if (env == -2) {
+      const char* e = getenv("HCP_ATTN_ORDER");
+      env = (e && *e) ? atoi(e) : -1;
+    }
+    int dev = 0, sms = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess)
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const long grid = long(p.num_pairs) * a.H;
+    p.pair_major = env >= 0 ? (env != 0) : (grid <= 8L * sms ? 1 : 0);
+    if (a.order >= 0) p.pair_major = a.order;
+  }
   p.ring = a.ring;
   if (p.ring.tile_src != nullptr) {
     if (p.ring.world < 2 || p.ring.world > 64 || p.ring.my_rank < 0 || p.ring.my_rank >= p.ring.world)

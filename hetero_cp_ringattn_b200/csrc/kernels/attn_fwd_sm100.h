@@ -51,6 +51,9 @@ struct AttnArgs {
   // per q tile, 2 = two 64-column streams per tile, 3 = one stream with P in its own TMEM
   // columns (pipelined Q K^T); head_dim 128 always runs one stream per tile
   int variant;
+  // CTA order: -1 = the build's choice (pair major for grids of at most 8 waves, else KV-head
+  // major; HCP_ATTN_ORDER overrides), 0 = KV-head major, 1 = pair major
+  int order = -1;
 };
 
 const char* attn_fwd(const AttnArgs& args, cudaStream_t stream);

@@ -798,6 +798,8 @@ class DecodeGraph:
         # one wave: resident decode-attention CTAs per SM x SMs, spread over the (row, KV head) pairs
         occ = max(1, int(native().decode_attn_ctas_per_sm(eng.D, eng.H // eng.Hkv)))
         self.splits = max(1, min(128, (occ * eng.num_sms) // (B * eng.Hkv)))  # floor: never a 2nd wave
+        if eng.env.decode_splits > 0:
+            self.splits = min(self.splits, eng.env.decode_splits)
         self.part_o = torch.zeros(B * eng.H * self.splits * eng.D, dtype=torch.float32, device=dev)
         self.part_l = torch.zeros(B * eng.H * self.splits, dtype=torch.float32, device=dev)
         self.counters = torch.zeros(B * eng.Hkv + 1, dtype=torch.int32, device=dev)

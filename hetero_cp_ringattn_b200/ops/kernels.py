@@ -82,10 +82,13 @@ def gemm(a: torch.Tensor, w: torch.Tensor, epi: str = "store", bias: Optional[to
 # --------------------------------------------------------------------------- attention
 def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, q_pos: torch.Tensor, L: int,
               causal: bool = True, scale: Optional[float] = None,
-              want_lse: bool = True, status: Optional[torch.Tensor] = None, variant: int = 0):
+              want_lse: bool = True, status: Optional[torch.Tensor] = None, variant: int = 0,
+              order: int = -1):
     """Flash attention of q [T,H,D] over position-ordered k/v [Hkv, Lcap, D] (rows 0..L-1).
     `variant` picks the head_dim-64 kernel (0: the default; 1: one softmax stream per q tile;
-    2: two streams; 3: pipelined, P in its own TMEM columns).
+    2: two streams; 3: pipelined, P in its own TMEM columns). `order` picks the CTA order (-1:
+    the kernel's choice: pair major for grids of at most 8 waves; 0: KV-head major; 1: heaviest
+    q-tile pairs of all heads first).
 
     Returns (o [T,H,D], lse [H,T] natural log or None)."""
     t, h, d = q.shape
@@ -98,7 +101,8 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, q_pos: torch.Te
         return o.to(q.dtype), (lse if want_lse else None)
     o = torch.empty_like(q)
     lse = torch.empty(h, t, dtype=torch.float32, device=q.device) if want_lse else None
-    native().attn_fwd(q, k, v, o, lse, q_pos, L, k.stride(0), scale, causal, status, variant)
+    native().attn_fwd(q, k, v, o, lse, q_pos, L, k.stride(0), scale, causal, status, variant,
+                      order)
     launches.count()
     return o, lse
 

@@ -249,3 +249,28 @@ def test_attention_edge_shapes(dev, L, T, h, hkv, d):
                                 torch.arange(L, device=dev), causal=True)
     assert (o.float() - ro).abs().max() < 2e-2
     assert (lse - rl).abs().max() < 2e-2
+
+
+@pytest.mark.parametrize("d", [64, 128])
+def test_attention_cta_orders_bit_identical(dev, d):
+    """The two CTA orders (KV-head major; heaviest q-tile pairs of all heads first) only change
+    which CTA runs when: every row's output and LSE are the same bits, here on one context-
+    parallel rank's zigzag rows (the case the pair-major order is for)."""
+    from hetero_cp_ringattn_b200.parallel.capacity import equal_chunks
+    from hetero_cp_ringattn_b200.parallel.strategy import layout_positions
+    torch.manual_seed(6)
+    L, h, hkv = 4096, 8, 2
+    pos = torch.as_tensor(layout_positions(equal_chunks(L, 4), "zigzag")[1], device=dev)
+    k_all = torch.randn(L, hkv, d, device=dev, dtype=torch.bfloat16)
+    v_all = torch.randn(L, hkv, d, device=dev, dtype=torch.bfloat16)
+    q = torch.randn(len(pos), h, d, device=dev, dtype=torch.bfloat16)
+    ks, vs = _stage(k_all, v_all, cap=L)
+    outs = []
+    for order in (0, 1):
+        st = status_tensor(dev)
+        outs.append(K.attention(q, ks, vs, pos.int(), L, causal=True, status=st, order=order))
+        assert_status_clean(st)
+    assert torch.equal(outs[0][0], outs[1][0]) and torch.equal(outs[0][1], outs[1][1])
+    ro, _ = ref.full_attention(q.float(), k_all.float(), v_all.float(), pos, torch.arange(L, device=dev),
+                               causal=True)
+    assert (outs[1][0].float() - ro).abs().max() < 2e-2
