@@ -94,13 +94,16 @@ def bench_gemm(args, dev, pk):
         w = torch.randn(n, k, device=dev, dtype=torch.bfloat16) * 0.02
         res = torch.randn(T, n, device=dev, dtype=torch.bfloat16) if epi == "residual" else None
         out = torch.empty(T, n // 2 if epi == "swiglu" else n, device=dev, dtype=torch.bfloat16)
-        ms = timed(lambda: K.gemm(a, w, epi, residual=res, out=out), args.iters, flush=flush)
-        ms_cublas = timed(lambda: torch.matmul(a, w.t()), args.iters, flush=flush)
         fl = 2.0 * T * n * k
-        emit(kernel="gemm_sm100", shape=name, M=T, N=n, K=k, epilogue=epi, ms=round(ms, 4),
-             tflops=round(fl / ms / 1e9, 1), frac_of_measured=round(fl / ms / 1e9 / pk["tflops"], 3),
-             cublas_tflops=round(fl / ms_cublas / 1e9, 1), vs_cublas=round(ms_cublas / ms, 3),
-             peaks=pk["source"])
+        ms_cublas = timed(lambda: torch.matmul(a, w.t()), args.iters, flush=flush)
+        for gv in args.gemm_variants:
+            ms = timed(lambda: K.gemm(a, w, epi, residual=res, out=out, variant=gv), args.iters,
+                       flush=flush)
+            emit(kernel="gemm_sm100", shape=name, M=T, N=n, K=k, epilogue=epi, variant=gv,
+                 ms=round(ms, 4), tflops=round(fl / ms / 1e9, 1),
+                 frac_of_measured=round(fl / ms / 1e9 / pk["tflops"], 3),
+                 cublas_tflops=round(fl / ms_cublas / 1e9, 1), vs_cublas=round(ms_cublas / ms, 3),
+                 peaks=pk["source"])
 
 
 # ----------------------------------------------------------------------------- attention
@@ -386,6 +389,8 @@ def main(argv=None):
     ap.add_argument("--variants", type=lambda s: [int(x) for x in s.split(",")], default=[0],
                     help="attn: head_dim-64 kernel variants to time (0 default, 1, 2, 3 pipelined)")
     ap.add_argument("--reps", type=int, default=1, help="attn: alternating repetitions")
+    ap.add_argument("--gemm-variants", type=lambda s: [int(x) for x in s.split(",")], default=[0],
+                    help="gemm: kernels to time (0 default, 1 one CTA per tile, 2 CTA pairs)")
     ap.add_argument("--orders", type=lambda s: [int(x) for x in s.split(",")], default=[-1],
                     help="attn: CTA orders to time (-1 kernel's choice, 0 KV-head major, 1 pair major)")
     ap.add_argument("--cp", type=int, default=1, help="attn: time one rank's rows of this CP degree")

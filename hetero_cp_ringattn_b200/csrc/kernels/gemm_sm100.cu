@@ -14,6 +14,14 @@
 //     warp 2: TMEM allocator; warps 4-7: epilogue (thread i owns accumulator row i);
 //   * two 256-column TMEM accumulators so the epilogue of tile i overlaps the mainloop of i+1;
 //   * every mbarrier wait is bounded and reports through the status word.
+//
+// Pair variant (gemm2_kernel, the default): clusters of two CTAs on two SMs compute 256x256
+// tiles with tcgen05.mma.cta_group::2 (M = 256): each CTA loads its own 128 rows of A and its own
+// 128 rows of B (the N half) into its own shared memory with plain per-CTA TMA loads,
+// both signalling the leader CTA's full barrier; the leader's single MMA thread reads both CTAs'
+// tiles, each CTA's TMEM receives its 128 rows of the 256-column accumulator, and the commits
+// arrive on the barriers of both CTAs. Per SM that moves 32 KB instead of 48 KB of operands
+// from L2 per 64-deep k step for the same MMA work.
 #include <cudaTypedefs.h>
 
 #include "common.cuh"
@@ -33,10 +41,15 @@ constexpr int A_STAGE = BM * BK * 2;  // 16 KB
 constexpr int B_STAGE = BN * BK * 2;  // 32 KB
 constexpr int TMEM_COLS = 512;
 constexpr int SMEM_BYTES = 1024 + STAGES * (A_STAGE + B_STAGE) + 256;
+// pair variant: per CTA 128 rows of A and 128 rows of B per stage
+constexpr int STAGES2 = 6;
+constexpr int HALF_STAGE = 128 * BK * 2;                 // 16 KB
+constexpr int SMEM_BYTES2 = 1024 + STAGES2 * 2 * HALF_STAGE + 256;
 
 struct Params {
   int M, N, K;
   int num_m_tiles, num_n_tiles;
+  int group_m;      // tile order: bands of group_m m-blocks, m fastest inside a band (0: n fastest)
   __nv_bfloat16* C;
   long ldc;
   const __nv_bfloat16* bias;
@@ -47,9 +60,22 @@ struct Params {
 };
 
 __device__ __forceinline__ void tile_coords(int tile, const Params& p, int& mb, int& nb) {
-  // n fastest: concurrently running CTAs share A tiles through L2 and sweep all of B.
-  mb = tile / p.num_n_tiles;
-  nb = tile % p.num_n_tiles;
+  if (p.group_m <= 0) {
+    // n fastest: concurrently running CTAs share A tiles through L2 and sweep all of B
+    mb = tile / p.num_n_tiles;
+    nb = tile % p.num_n_tiles;
+    return;
+  }
+  // bands of group_m m-blocks, m fastest within a band: the band's A tiles stay in L2 while B is
+  // swept once per band (n fastest sweeps all of B once per m-block, which for a weight larger
+  // than L2, e.g. a 28672 x 4096 gate/up projection, re-reads it from DRAM every time)
+  const int per_band = p.group_m * p.num_n_tiles;
+  const int band = tile / per_band;
+  const int first = band * p.group_m;
+  const int rows = min(p.group_m, p.num_m_tiles - first);
+  const int r = tile - band * per_band;
+  mb = first + r % rows;
+  nb = r / rows;
 }
 
 template <int EPI>
@@ -405,6 +431,224 @@ __global__ void __launch_bounds__(256, 1)
   }
 }
 
+// ----------------------------------------------------------------------------- CTA-pair kernel
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// shared::cluster address of the same shared-memory offset in CTA `rank` of the cluster
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t saddr, uint32_t rank) {
+  uint32_t d;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(d) : "r"(saddr), "r"(rank));
+  return d;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+// TMA load into this CTA's shared memory whose completion is counted on a barrier of the pair's
+// leader CTA (cluster address)
+__device__ __forceinline__ void tma_load_2d_pair(void* smem_dst, const void* map, uint32_t bar_cluster,
+                                                 int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(smem_dst)),
+      "l"(map), "r"(bar_cluster), "r"(c0), "r"(c1)
+      : "memory");
+}
+__device__ __forceinline__ void umma_pair_bf16_ss(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
+                                                  uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// commit of the pair's MMAs: one arrival on the barrier at this offset in both CTAs
+__device__ __forceinline__ void umma_pair_commit_both(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;"
+      ::"r"(smem_u32(bar)), "h"(uint16_t(3))
+      : "memory");
+}
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* smem_slot, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                   smem_u32(smem_slot)),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+
+// Tiles of 256 x 256 (num_m_tiles counts 256-row blocks), persistent over the grid's CTA pairs.
+// Warp roles as in gemm_kernel; the MMA warp of the follower CTA (cluster rank 1) idles.
+// Barriers: full[s] of the leader counts both CTAs' TMA bytes (the leader arrives with the
+// expected 64 KB); empty[s] and acc_full[b] of both CTAs receive the leader's commits;
+// acc_empty[b] of the leader collects the 4 epilogue warps of each CTA (the follower's arrive
+// remotely). The kernel has no early exit: every thread reaches the final cluster barrier, after
+// which both CTAs free their TMEM.
+template <int EPI>
+__global__ void __launch_bounds__(256, 1)
+    gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                 Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES2 * HALF_STAGE;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + STAGES2 * HALF_STAGE);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + STAGES2;
+  uint64_t* acc_full = bars + 2 * STAGES2;
+  uint64_t* acc_empty = bars + 2 * STAGES2 + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES2 + 4);
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES2; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 8);
+    }
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 2) {
+    tmem_alloc_pair(tmem_slot, TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync_all();   // both CTAs' barriers are initialised before any remote arrival
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int total_tiles = p.num_m_tiles * p.num_n_tiles;
+  const int k_iters = (p.K + BK - 1) / BK;
+  const int pair = int(blockIdx.x) / 2, npairs = int(gridDim.x) / 2;
+
+  if (warp == 0) {
+    if (elect_one()) {
+      int it = 0;
+      bool ok = true;
+      for (int tile = pair; ok && tile < total_tiles; tile += npairs) {
+        int mb, nb;
+        tile_coords(tile, p, mb, nb);
+        for (int k = 0; k < k_iters; ++k, ++it) {
+          const int s = it % STAGES2;
+          const uint32_t ph = (it / STAGES2) & 1;
+          if (!mbar_wait(&empty[s], ph ^ 1, p.status, 121)) {
+            ok = false;
+            break;
+          }
+          if (leader) mbar_arrive_expect_tx(&full[s], 4 * HALF_STAGE);
+          const uint32_t fb = mapa_shared(smem_u32(&full[s]), 0);
+          tma_load_2d_pair(sA + s * HALF_STAGE, &tmA, fb, k * BK, mb * 256 + int(rank) * 128);
+          tma_load_2d_pair(sB + s * HALF_STAGE, &tmB, fb, k * BK, nb * BN + int(rank) * 128);
+        }
+      }
+      // drain: the last commits on this CTA's empty barriers have landed before the CTA exits
+      for (int d = 0; ok && d < STAGES2 && d < it; ++d) {
+        const int j = it - 1 - d;
+        if (!mbar_wait(&empty[j % STAGES2], (j / STAGES2) & 1, p.status, 125)) ok = false;
+      }
+    }
+  } else if (warp == 1) {
+    if (leader && elect_one()) {
+      constexpr uint32_t idesc = idesc_bf16_f32(256, BN, false, false);
+      int it = 0;
+      int local = 0;
+      for (int tile = pair; tile < total_tiles; tile += npairs, ++local) {
+        const int b = local & 1;
+        const uint32_t aph = (local >> 1) & 1;
+        if (!mbar_wait(&acc_empty[b], aph ^ 1, p.status, 122)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + uint32_t(b * BN);
+        bool ok = true;
+        for (int k = 0; k < k_iters; ++k, ++it) {
+          const int s = it % STAGES2;
+          const uint32_t ph = (it / STAGES2) & 1;
+          if (!mbar_wait(&full[s], ph, p.status, 123)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sA + s * HALF_STAGE);
+          const uint32_t b0 = smem_u32(sB + s * HALF_STAGE);
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            const uint64_t ad = sdesc_sw128(a0 + kk * 32, 16, 1024);
+            const uint64_t bd = sdesc_sw128(b0 + kk * 32, 16, 1024);
+            umma_pair_bf16_ss(d_tmem, ad, bd, idesc, (k | kk) != 0 ? 1u : 0u);
+          }
+          umma_pair_commit_both(&empty[s]);
+        }
+        if (!ok) break;
+        umma_pair_commit_both(&acc_full[b]);
+      }
+    }
+  } else if (warp >= 4) {
+    const int q = warp - 4;
+    const int row_in_tile = q * 32 + lane;
+    const uint32_t acc_empty_leader[2] = {mapa_shared(smem_u32(&acc_empty[0]), 0),
+                                          mapa_shared(smem_u32(&acc_empty[1]), 0)};
+    int local = 0;
+    for (int tile = pair; tile < total_tiles; tile += npairs, ++local) {
+      const int b = local & 1;
+      const uint32_t aph = (local >> 1) & 1;
+      if (!mbar_wait(&acc_full[b], aph, p.status, 124)) break;
+      tc_fence_after();
+      int mb, nb;
+      tile_coords(tile, p, mb, nb);
+      const uint32_t tacc = tmem_base + (uint32_t(q * 32) << 16) + uint32_t(b * BN);
+      // this CTA's 128 rows of the 256-row tile, as the 128-row block 2 mb + rank
+      epilogue_tile<EPI>(p, tacc, 2 * mb + int(rank), nb, row_in_tile);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_remote(acc_empty_leader[b]);
+    }
+  }
+
+  if constexpr (EPI == kEpiQkvPush) {
+    if (warp >= 4) __threadfence_system();
+  }
+  tc_fence_before();
+  cluster_sync_all();
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, TMEM_COLS);
+  }
+  if constexpr (EPI == kEpiQkvPush) {
+    if (threadIdx.x == 0 && p.qkv.done_counter != nullptr) {
+      __threadfence_system();
+      const unsigned prev = atomicAdd(p.qkv.done_counter, 1u);
+      if (prev == gridDim.x - 1) {
+        __threadfence_system();
+        for (int rk = 0; rk < p.qkv.n_stage; ++rk) st_release_sys(p.qkv.ready_ptrs[rk], p.qkv.epoch);
+        *p.qkv.done_counter = 0;
+      }
+    }
+  }
+}
+
 // ----------------------------------------------------------------------------- host side
 static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -461,6 +705,69 @@ static cudaError_t launch(const CUtensorMap& ta, const CUtensorMap& tb, const Pa
   return cudaGetLastError();
 }
 
+// Pair kernel launch: clusters of 2 CTAs, as many pairs as can be resident at once (at most one
+// per tile).
+template <int EPI>
+static cudaError_t launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p,
+                               int tiles, cudaStream_t stream) {
+  static std::atomic<unsigned long long> attr{0};
+  cudaError_t e = once_per_device(attr, [] {
+    return cudaFuncSetAttribute(gemm2_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                SMEM_BYTES2);
+  });
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = 2;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(256);
+  cfg.dynamicSmemBytes = SMEM_BYTES2;
+  cfg.stream = stream;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  static int max_pairs[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (max_pairs[dev] == 0) {
+    cfg.gridDim = dim3(2);
+    int n = 0;
+    e = cudaOccupancyMaxActiveClusters(&n, gemm2_kernel<EPI>, &cfg);
+    if (e != cudaSuccess) return e;
+    max_pairs[dev] = n > 0 ? n : 1;
+  }
+  const int pairs = tiles < max_pairs[dev] ? tiles : max_pairs[dev];
+  cfg.gridDim = dim3(2 * pairs);
+  return cudaLaunchKernelEx(&cfg, gemm2_kernel<EPI>, ta, tb, p);
+}
+
+// Tile-order band height in m-blocks: bands of 16 when the weight B (N x K) is larger than
+// 64 MB, which does not stay in L2 while n-fastest order sweeps it once per m-block; n fastest
+// otherwise. Measured on B200 with the pair kernel (ms, n fastest -> bands of 16): 28672 x 4096
+// gate/up at M = 32768 7.55 -> 5.56, 16384 x 2048 gate/up 1.75 -> 1.37; the 2048 x 8192 down
+// projection (33 MB) 0.74 -> 0.82 and 6144 x 4096 QKV 1.06 -> 1.22 prefer n fastest.
+// HCP_GEMM_GROUP=n forces bands of n (0: n fastest).
+static int group_for(long N, long K) {
+  static int env = -2;
+  if (env == -2) {
+    const char* e = getenv("HCP_GEMM_GROUP");
+    env = (e && *e) ? atoi(e) : -1;
+  }
+  if (env >= 0) return env;
+  return double(N) * double(K) * 2.0 > 64.0 * (1 << 20) ? 16 : 0;
+}
+
+// 1: CTA-pair kernel (default), 0: one CTA per tile (HCP_GEMM_PAIR=0)
+static int pair_default() {
+  static int env = -2;
+  if (env == -2) {
+    const char* e = getenv("HCP_GEMM_PAIR");
+    env = (e && *e) ? atoi(e) : 1;
+  }
+  return env != 0 ? 1 : 0;
+}
+
 const char* gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
   if (a.M <= 0 || a.N <= 0 || a.K <= 0) return "gemm: empty problem";
   if ((a.lda * 2) % 16 || (a.ldb * 2) % 16) return "gemm: lda/ldb must be multiples of 8 elements";
@@ -473,10 +780,11 @@ const char* gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
                                 (reinterpret_cast<uintptr_t>(a.R) & 15)))
     return "gemm: residual must be 16-byte aligned with ldr % 8 == 0";
   if (a.epi == kEpiBias && a.bias == nullptr) return "gemm: bias missing";
+  const bool pair = a.variant == 2 || (a.variant == 0 && pair_default());
   CUtensorMap ta, tb;
   if (!make_tma_2d_bf16(&ta, a.A, a.K, a.M, uint64_t(a.lda) * 2, BK, BM))
     return "gemm: TMA descriptor for A failed";
-  if (!make_tma_2d_bf16(&tb, a.B, a.K, a.N, uint64_t(a.ldb) * 2, BK, BN))
+  if (!make_tma_2d_bf16(&tb, a.B, a.K, a.N, uint64_t(a.ldb) * 2, BK, pair ? 128 : BN))
     return "gemm: TMA descriptor for B failed";
   Params p;
   p.M = a.M;
@@ -490,6 +798,20 @@ const char* gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
   p.R = a.R;
   p.ldr = a.ldr;
   p.status = a.status;
+  p.group_m = group_for(a.N, a.K);
+  if (pair) {
+    p.num_m_tiles = (a.M + 255) / 256;
+    const int tiles2 = p.num_m_tiles * p.num_n_tiles;
+    cudaError_t e2;
+    switch (a.epi) {
+      case kEpiStore: e2 = launch_pair<kEpiStore>(ta, tb, p, tiles2, stream); break;
+      case kEpiBias: e2 = launch_pair<kEpiBias>(ta, tb, p, tiles2, stream); break;
+      case kEpiResidual: e2 = launch_pair<kEpiResidual>(ta, tb, p, tiles2, stream); break;
+      case kEpiSwiGLU: e2 = launch_pair<kEpiSwiGLU>(ta, tb, p, tiles2, stream); break;
+      default: return "gemm: unknown epilogue";
+    }
+    return e2 == cudaSuccess ? nullptr : cudaGetErrorString(e2);
+  }
   const int tiles = p.num_m_tiles * p.num_n_tiles;
   const int grid = tiles < a.num_sms ? tiles : a.num_sms;
   cudaError_t e;
@@ -516,10 +838,11 @@ const char* gemm_qkv_push(const GemmArgs& a, const QkvPushArgs& q, cudaStream_t 
        reinterpret_cast<uintptr_t>(q.sin_t)) & 15)
     return "gemm_qkv_push: q_out and the RoPE tables must be 16-byte aligned";
   if (q.n_stage > 0 && q.stage_ptrs == nullptr) return "gemm_qkv_push: staging pointers missing";
+  const bool pair = a.variant == 2 || (a.variant == 0 && pair_default());
   CUtensorMap ta, tb;
   if (!make_tma_2d_bf16(&ta, a.A, a.K, a.M, uint64_t(a.lda) * 2, BK, BM))
     return "gemm_qkv_push: TMA descriptor for A failed";
-  if (!make_tma_2d_bf16(&tb, a.B, a.K, a.N, uint64_t(a.ldb) * 2, BK, BN))
+  if (!make_tma_2d_bf16(&tb, a.B, a.K, a.N, uint64_t(a.ldb) * 2, BK, pair ? 128 : BN))
     return "gemm_qkv_push: TMA descriptor for B failed";
   Params p{};
   p.M = a.M;
@@ -530,6 +853,12 @@ const char* gemm_qkv_push(const GemmArgs& a, const QkvPushArgs& q, cudaStream_t 
   p.bias = a.bias;
   p.status = a.status;
   p.qkv = q;
+  p.group_m = group_for(a.N, a.K);
+  if (pair) {
+    p.num_m_tiles = (a.M + 255) / 256;
+    cudaError_t e2 = launch_pair<kEpiQkvPush>(ta, tb, p, p.num_m_tiles * p.num_n_tiles, stream);
+    return e2 == cudaSuccess ? nullptr : cudaGetErrorString(e2);
+  }
   const int tiles = p.num_m_tiles * p.num_n_tiles;
   const int grid = tiles < a.num_sms ? tiles : a.num_sms;
   cudaError_t e = launch<kEpiQkvPush>(ta, tb, p, grid, stream);

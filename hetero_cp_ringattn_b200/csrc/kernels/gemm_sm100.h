@@ -57,6 +57,8 @@ struct GemmArgs {
   long ldr;
   int* status;             // device status words (may be null)
   int num_sms;
+  int variant;             // 0: the build's default (HCP_GEMM_PAIR), 1: one CTA per 128x256
+                           // tile, 2: CTA pairs on 256x256 tiles (tcgen05 cta_group::2)
 };
 
 // Returns nullptr on success, otherwise a static error string.

@@ -54,8 +54,9 @@ def swiglu_from_interleaved(y: torch.Tensor, block: int = SWIGLU_BLOCK) -> torch
 # --------------------------------------------------------------------------- GEMM
 def gemm(a: torch.Tensor, w: torch.Tensor, epi: str = "store", bias: Optional[torch.Tensor] = None,
          residual: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
-         status: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """out = a @ w.T with a fused epilogue (`store`, `bias`, `residual`, `swiglu`)."""
+         status: Optional[torch.Tensor] = None, variant: int = 0) -> torch.Tensor:
+    """out = a @ w.T with a fused epilogue (`store`, `bias`, `residual`, `swiglu`). `variant`: 0
+    the default kernel, 1 one CTA per 128x256 tile, 2 CTA pairs on 256x256 tiles."""
     m, n = a.shape[0], w.shape[0]
     n_out = n // 2 if epi == "swiglu" else n
     if not a.is_cuda:
@@ -74,7 +75,7 @@ def gemm(a: torch.Tensor, w: torch.Tensor, epi: str = "store", bias: Optional[to
     if out is None:
         out = residual if (epi == "residual" and residual is not None) else torch.empty(
             m, n_out, dtype=a.dtype, device=a.device)
-    native().gemm(a, w, out, EPI[epi], bias, residual, status)
+    native().gemm(a, w, out, EPI[epi], bias, residual, status, variant)
     launches.count()
     return out
 

@@ -27,37 +27,44 @@ def assert_status_clean(st):
     assert int(st[0]) == 0, f"device status {st.tolist()}"
 
 
-@pytest.mark.parametrize("m,n,k", [(128, 256, 64), (300, 512, 256), (1000, 768, 1000), (4096, 3072, 2048)])
-def test_gemm_store(dev, m, n, k):
+@pytest.mark.parametrize("variant", [1, 2])
+@pytest.mark.parametrize("m,n,k", [(128, 256, 64), (300, 512, 256), (1000, 768, 1000), (4096, 3072, 2048),
+                                   (260, 384, 128)])
+def test_gemm_store(dev, m, n, k, variant):
+    """Both GEMM kernels (one CTA per 128x256 tile; CTA pairs on 256x256 tiles with
+    cta_group::2) against float32, including row and column tails (M = 260: the second CTA of
+    the last pair holds 4 rows; N = 384: the last tile's second half of B is out of range)."""
     torch.manual_seed(0)
     a = torch.randn(m, k, device=dev, dtype=torch.bfloat16)
     w = torch.randn(n, k, device=dev, dtype=torch.bfloat16) / math.sqrt(k)
     st = status_tensor(dev)
-    y = K.gemm(a, w, "store", status=st)
+    y = K.gemm(a, w, "store", status=st, variant=variant)
     assert_status_clean(st)
     r = a.float() @ w.float().t()
     assert rel_err(y, r) < 1e-2
 
 
-def test_gemm_bias_residual(dev):
+@pytest.mark.parametrize("variant", [1, 2])
+def test_gemm_bias_residual(dev, variant):
     torch.manual_seed(1)
     m, n, k = 513, 1280, 512
     a = torch.randn(m, k, device=dev, dtype=torch.bfloat16)
     w = torch.randn(n, k, device=dev, dtype=torch.bfloat16) / math.sqrt(k)
     b = torch.randn(n, device=dev, dtype=torch.bfloat16)
     st = status_tensor(dev)
-    y = K.gemm(a, w, "bias", bias=b, status=st)
+    y = K.gemm(a, w, "bias", bias=b, status=st, variant=variant)
     r = a.float() @ w.float().t() + b.float()
     assert rel_err(y, r) < 1e-2
     res = torch.randn(m, n, device=dev, dtype=torch.bfloat16)
     expect = (a.float() @ w.float().t()).bfloat16().float() + res.float()
-    y2 = K.gemm(a, w, "residual", residual=res, status=st)  # in place on res
+    y2 = K.gemm(a, w, "residual", residual=res, status=st, variant=variant)  # in place on res
     assert_status_clean(st)
     assert y2.data_ptr() == res.data_ptr()
     assert rel_err(y2, expect) < 1e-2
 
 
-def test_gemm_swiglu(dev):
+@pytest.mark.parametrize("variant", [1, 2])
+def test_gemm_swiglu(dev, variant):
     torch.manual_seed(2)
     m, i, k = 700, 512, 384
     a = torch.randn(m, k, device=dev, dtype=torch.bfloat16)
@@ -65,7 +72,7 @@ def test_gemm_swiglu(dev):
     u = torch.randn(i, k, device=dev, dtype=torch.bfloat16) / math.sqrt(k)
     wgu = K.interleave_gate_up(g, u)
     st = status_tensor(dev)
-    y = K.gemm(a, wgu, "swiglu", status=st)
+    y = K.gemm(a, wgu, "swiglu", status=st, variant=variant)
     assert_status_clean(st)
     gg = (a.float() @ g.float().t()).bfloat16().float()
     uu = (a.float() @ u.float().t()).bfloat16().float()
