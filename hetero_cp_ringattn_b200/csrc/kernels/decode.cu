@@ -751,9 +751,20 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(const __grid_constant_
   // visible after the fence + counter), then one warp per head reduces max and weight sum
   __shared__ float s_w[G][kMaxDecodeSplits];
   __shared__ float s_mx[G], s_ws[G];
-  for (int i = threadIdx.x; i < G * eff; i += blockDim.x) {
-    const int g = i / eff, s = i % eff;
-    s_w[g][s] = __ldcg(a.part_lse + (long)(b * H + h * G + g) * a.splits + s);
+  {
+    // every load issued before any store (G * eff <= 8 * 128: at most 8 per thread)
+    constexpr int LW = (G * kMaxDecodeSplits + 127) / 128;
+    float lw[LW];
+#pragma unroll
+    for (int k = 0; k < LW; ++k) {
+      const int i = threadIdx.x + k * 128;
+      lw[k] = i < G * eff ? __ldcg(a.part_lse + (long)(b * H + h * G + i / eff) * a.splits + i % eff) : 0.f;
+    }
+#pragma unroll
+    for (int k = 0; k < LW; ++k) {
+      const int i = threadIdx.x + k * 128;
+      if (i < G * eff) s_w[i / eff][i % eff] = lw[k];
+    }
   }
   __syncthreads();
   for (int g = warp; g < G; g += 4) {
@@ -773,30 +784,62 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(const __grid_constant_
     }
   }
   __syncthreads();
-  // each thread owns 4 consecutive dims of one head; 16-byte L2 loads, 16 splits per round in
-  // flight (this tail runs after every split of the group is done, so its latency adds to the
-  // kernel's)
-  for (int c = threadIdx.x; c < G * (D / 4); c += blockDim.x) {
-    const int g = c / (D / 4), d4 = c % (D / 4);
+  // work item = 4 consecutive dims of one head (G * D / 4 items); with fewer items than threads
+  // the splits of an item are dealt to `parts` threads (split s to thread s % parts) whose
+  // partial sums meet in shared memory, so each thread has ceil(eff / parts) instead of eff
+  // splits to load: 16-byte L2 loads, 16 in flight per round. This tail runs after every split
+  // of the group is done, so its latency adds to the kernel's.
+  constexpr int ITEMS = G * (D / 4);
+  constexpr int PARTS = ITEMS >= 128 ? 1 : 128 / ITEMS;
+  __shared__ float4 s_part[PARTS > 1 ? (PARTS - 1) * ITEMS : 1];
+  auto accum = [&](int g, int d4, int first) {
     float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (s_mx[g] != -INFINITY) {
-      const float4* pof = reinterpret_cast<const float4*>(a.part_o + (long)(b * H + h * G + g) * a.splits * D) + d4;
-      for (int s0 = 0; s0 < eff; s0 += 16) {
-        float4 v[16];
+    if (s_mx[g] == -INFINITY) return o;
+    const float4* pof = reinterpret_cast<const float4*>(a.part_o + (long)(b * H + h * G + g) * a.splits * D) + d4;
+    for (int s0 = first; s0 < eff; s0 += 16 * PARTS) {
+      float4 v[16];
 #pragma unroll
-        for (int j = 0; j < 16; ++j)
-          v[j] = (s0 + j < eff) ? __ldcg(pof + (long)(s0 + j) * (D / 4)) : make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int j = 0; j < 16; ++j) {
+        const int sp = s0 + j * PARTS;
+        v[j] = sp < eff ? __ldcg(pof + (long)sp * (D / 4)) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          if (s0 + j < eff) {
-            const float w = s_w[g][s0 + j];
-            o.x = fmaf(w, v[j].x, o.x);
-            o.y = fmaf(w, v[j].y, o.y);
-            o.z = fmaf(w, v[j].z, o.z);
-            o.w = fmaf(w, v[j].w, o.w);
-          }
+      for (int j = 0; j < 16; ++j) {
+        const int sp = s0 + j * PARTS;
+        if (sp < eff) {
+          const float w = s_w[g][sp];
+          o.x = fmaf(w, v[j].x, o.x);
+          o.y = fmaf(w, v[j].y, o.y);
+          o.z = fmaf(w, v[j].z, o.z);
+          o.w = fmaf(w, v[j].w, o.w);
         }
       }
+    }
+    return o;
+  };
+  float4 o_part = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (PARTS > 1) {
+    const int item = threadIdx.x % ITEMS, part = threadIdx.x / ITEMS;
+    if (part < PARTS) {
+      o_part = accum(item / (D / 4), item % (D / 4), part);
+      if (part > 0) s_part[(part - 1) * ITEMS + item] = o_part;
+    }
+    __syncthreads();
+  }
+  for (int c = threadIdx.x; c < ITEMS; c += blockDim.x) {
+    const int g = c / (D / 4), d4 = c % (D / 4);
+    float4 o;
+    if (PARTS > 1) {
+      o = o_part;
+#pragma unroll
+      for (int q = 1; q < PARTS; ++q) {
+        const float4 u = s_part[(q - 1) * ITEMS + c];
+        o = make_float4(o.x + u.x, o.y + u.y, o.z + u.z, o.w + u.w);
+      }
+    } else {
+      o = accum(g, d4, 0);
+    }
+    if (s_mx[g] != -INFINITY) {
       const float inv = 1.f / s_ws[g];
       o = make_float4(o.x * inv, o.y * inv, o.z * inv, o.w * inv);
     }
