@@ -92,3 +92,42 @@ def test_session_append_matches_oracle():
         ref = reference_model.forward(hf, torch.tensor(seq[:n], device=dev), last_only=True)[0]
         err = (lgt - ref.float().cpu()).abs()
         assert err.max() < 0.15 and err.mean() < 0.02, (n, float(err.max()), float(err.mean()))
+
+
+@pytest.mark.parametrize("env_kwargs", [dict(decode_prefetch=1), dict(decode_prefetch=3),
+                                        dict(decode_splits=8), dict(decode_combine="gemv")])
+def test_decode_switches_keep_the_tokens(env_kwargs):
+    """Decode switches that only move work around (L2 prefetch of later weights, a cap on the
+    KV splits, where the cross-rank combine runs: unused on one rank) give the default engine's
+    greedy tokens; the split cap changes the attention's summation order, so its logits are
+    held to the bf16 tolerance instead of bit equality."""
+    from hetero_cp_ringattn_b200.config import EnvConfig, preset
+    from hetero_cp_ringattn_b200.models.llama import LlamaCPEngine
+    from hetero_cp_ringattn_b200.models.weights import ModelWeights, PreparedWeights
+    dev = torch.device("cuda", 0)
+    cfg = preset("tiny-gpu")
+    hf = ModelWeights.random_init(cfg, seed=5, device=dev, dtype=torch.bfloat16)
+    w = PreparedWeights.from_weights(hf)
+    L = 2000
+    prompt = torch.randint(0, cfg.vocab_size, (L,), generator=torch.Generator().manual_seed(9))
+
+    def run(env):
+        eng = LlamaCPEngine(cfg, w, device=dev, max_context=L, max_batch=1, decode_reserve=16, env=env)
+        tok, _ = eng.prefill(1, prompt, [L], decode_horizon=8)
+        toks, logits, cur = [int(tok)], [], tok
+        for _ in range(6):
+            cur = eng.decode_step([1], cur)
+            toks.append(int(cur))
+            logits.append(eng.last_logits(1)[0].float().cpu())
+        eng.check_device()
+        eng.release(1)
+        eng.close()
+        return toks, torch.stack(logits)
+
+    base_t, base_l = run(EnvConfig())
+    got_t, got_l = run(EnvConfig(**env_kwargs))
+    if "decode_splits" in env_kwargs:
+        assert (got_l - base_l).abs().max() < 0.1 * max(1.0, float(base_l.std()))
+    else:
+        assert torch.equal(got_l, base_l)
+        assert got_t == base_t
