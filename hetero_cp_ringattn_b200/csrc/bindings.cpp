@@ -65,7 +65,7 @@ hcp::dec::L2Prefetch make_prefetch(const std::vector<torch::Tensor>& ts) {
 // ----------------------------------------------------------------------------- kernels
 void gemm(torch::Tensor A, torch::Tensor B, torch::Tensor C, int64_t epi,
           c10::optional<torch::Tensor> bias, c10::optional<torch::Tensor> R,
-          c10::optional<torch::Tensor> status, int64_t variant) {
+          c10::optional<torch::Tensor> status, int64_t variant, int64_t group) {
   check_cuda_bf16(A, "A");
   check_cuda_bf16(B, "B");
   check_cuda_bf16(C, "C");
@@ -95,6 +95,7 @@ void gemm(torch::Tensor A, torch::Tensor B, torch::Tensor C, int64_t epi,
   a.status = ptr_or_null<int>(status);
   a.num_sms = sm_count(A.get_device());
   a.variant = int(variant);
+  a.group = int(group);
   HCP_CHECK_OK(hcp::gemm::gemm_bf16(a, cur_stream()));
 }
 
@@ -723,7 +724,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "hetero_cp_ringattn_b200 sm_100a kernels and domain runtime";
   m.def("gemm", &gemm, "tcgen05 GEMM with fused epilogue", py::arg("A"), py::arg("B"), py::arg("C"),
         py::arg("epi") = 0, py::arg("bias") = py::none(), py::arg("R") = py::none(),
-        py::arg("status") = py::none(), py::arg("variant") = 0);
+        py::arg("status") = py::none(), py::arg("variant") = 0, py::arg("group") = -1);
   m.def("attn_fwd", &attn_fwd, "tcgen05 flash attention with LSE and position-causal skip",
         py::arg("q"), py::arg("k"), py::arg("v"), py::arg("o"), py::arg("lse"), py::arg("q_pos"),
         py::arg("L"), py::arg("kv_head_stride"), py::arg("scale"), py::arg("causal"),

@@ -798,7 +798,7 @@ const char* gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
   p.R = a.R;
   p.ldr = a.ldr;
   p.status = a.status;
-  p.group_m = group_for(a.N, a.K);
+  p.group_m = a.group >= 0 ? a.group : group_for(a.N, a.K);
   if (pair) {
     p.num_m_tiles = (a.M + 255) / 256;
     const int tiles2 = p.num_m_tiles * p.num_n_tiles;
@@ -853,7 +853,7 @@ const char* gemm_qkv_push(const GemmArgs& a, const QkvPushArgs& q, cudaStream_t 
   p.bias = a.bias;
   p.status = a.status;
   p.qkv = q;
-  p.group_m = group_for(a.N, a.K);
+  p.group_m = a.group >= 0 ? a.group : group_for(a.N, a.K);
   if (pair) {
     p.num_m_tiles = (a.M + 255) / 256;
     cudaError_t e2 = launch_pair<kEpiQkvPush>(ta, tb, p, p.num_m_tiles * p.num_n_tiles, stream);

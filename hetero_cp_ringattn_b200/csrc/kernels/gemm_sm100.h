@@ -59,6 +59,8 @@ struct GemmArgs {
   int num_sms;
   int variant;             // 0: the build's default (HCP_GEMM_PAIR), 1: one CTA per 128x256
                            // tile, 2: CTA pairs on 256x256 tiles (tcgen05 cta_group::2)
+  int group = -1;          // tile order: bands of this many m-blocks (0: n fastest; -1: by the
+                           // weight's size, HCP_GEMM_GROUP overrides)
 };
 
 // Returns nullptr on success, otherwise a static error string.

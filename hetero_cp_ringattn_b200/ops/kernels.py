@@ -54,9 +54,10 @@ def swiglu_from_interleaved(y: torch.Tensor, block: int = SWIGLU_BLOCK) -> torch
 # --------------------------------------------------------------------------- GEMM
 def gemm(a: torch.Tensor, w: torch.Tensor, epi: str = "store", bias: Optional[torch.Tensor] = None,
          residual: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
-         status: Optional[torch.Tensor] = None, variant: int = 0) -> torch.Tensor:
+         status: Optional[torch.Tensor] = None, variant: int = 0, group: int = -1) -> torch.Tensor:
     """out = a @ w.T with a fused epilogue (`store`, `bias`, `residual`, `swiglu`). `variant`: 0
-    the default kernel, 1 one CTA per 128x256 tile, 2 CTA pairs on 256x256 tiles."""
+    the default kernel, 1 one CTA per 128x256 tile, 2 CTA pairs on 256x256 tiles. `group`: tile
+    order in bands of that many m-blocks (0: n fastest; -1: chosen by the weight's size)."""
     m, n = a.shape[0], w.shape[0]
     n_out = n // 2 if epi == "swiglu" else n
     if not a.is_cuda:
@@ -75,7 +76,7 @@ def gemm(a: torch.Tensor, w: torch.Tensor, epi: str = "store", bias: Optional[to
     if out is None:
         out = residual if (epi == "residual" and residual is not None) else torch.empty(
             m, n_out, dtype=a.dtype, device=a.device)
-    native().gemm(a, w, out, EPI[epi], bias, residual, status, variant)
+    native().gemm(a, w, out, EPI[epi], bias, residual, status, variant, group)
     launches.count()
     return out
 

@@ -45,6 +45,23 @@ def test_gemm_store(dev, m, n, k, variant):
 
 
 @pytest.mark.parametrize("variant", [1, 2])
+@pytest.mark.parametrize("m,n", [(1000, 768), (4096, 3072)])
+def test_gemm_tile_orders_bit_identical(dev, variant, m, n):
+    """Banded tile orders (3 or 16 m-blocks per band, m fastest inside a band; a short last
+    band when the blocks do not divide) only change which CTA computes a tile when: the output is
+    the same bits as n-fastest order, and matches float32."""
+    torch.manual_seed(4)
+    k = 256
+    a = torch.randn(m, k, device=dev, dtype=torch.bfloat16)
+    w = torch.randn(n, k, device=dev, dtype=torch.bfloat16) / math.sqrt(k)
+    st = status_tensor(dev)
+    outs = [K.gemm(a, w, "store", status=st, variant=variant, group=g) for g in (0, 3, 16)]
+    assert_status_clean(st)
+    assert torch.equal(outs[0], outs[1]) and torch.equal(outs[0], outs[2])
+    assert rel_err(outs[0], a.float() @ w.float().t()) < 1e-2
+
+
+@pytest.mark.parametrize("variant", [1, 2])
 def test_gemm_bias_residual(dev, variant):
     torch.manual_seed(1)
     m, n, k = 513, 1280, 512
