@@ -834,9 +834,16 @@ const char* attn_fwd(const AttnArgs& a, cudaStream_t stream) {
       const char* e = getenv("HCP_ATTN_ORDER");
       env = (e && *e) ? atoi(e) : -1;
     }
+    static int sm_cache[64] = {0};
     int dev = 0, sms = 148;
-    if (cudaGetDevice(&dev) == cudaSuccess)
-      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (cudaGetDevice(&dev) == cudaSuccess && dev >= 0 && dev < 64) {
+      if (sm_cache[dev] == 0) {
+        int n = 0;
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        sm_cache[dev] = n > 0 ? n : 148;
+      }
+      sms = sm_cache[dev];
+    }
     const long grid = long(p.num_pairs) * a.H;
     p.pair_major = env >= 0 ? (env != 0) : (grid <= 8L * sms ? 1 : 0);
     if (a.order >= 0) p.pair_major = a.order;
