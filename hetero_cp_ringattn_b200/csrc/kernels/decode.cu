@@ -487,7 +487,10 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(const __grid_constant_
   constexpr int DQ = D / 4;                // contiguous dims of a K row per lane in S = Q K^T
   constexpr int KS = D / 16;               // MMA k-steps over the head dim
   constexpr int NT = D / 8;                // 8-dim n-tiles of O
-  static_assert(G >= 1 && G <= 8, "GQA group of at most 8 query heads");
+  static_assert(G >= 1 && G <= 16, "GQA group of at most 16 query heads");
+  // heads g and g + 8 of the group are rows g and g + 8 of the 16-row MMA tiles: groups of up to
+  // 8 heads use rows 0..7 only, larger groups the second row group too (R2)
+  constexpr bool R2 = G > 8;
   static_assert(NW * kDecWR == CC, "warps x rows per warp = chunk");
   extern __shared__ uint8_t dsm_raw[];
   uint8_t* dsm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dsm_raw) + 1023) & ~uintptr_t(1023));
@@ -566,35 +569,46 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(const __grid_constant_
   // q fragments (A of S = Q K^T): row g = head g of the group, pre-scaled into the log2 domain;
   // k-step ks, lane t covers dims t * DQ + 4 ks + {0, 1} (a0) and + {2, 3} (a2)
   uint32_t qa[KS][2];
+  uint32_t qb[KS][2];                      // R2: head g + 8 (zero otherwise)
   {
     const float qs = a.scale * kLog2e;
-    float qf[DQ];
-    if (g < G) {
-      const __nv_bfloat16* qp = a.q + ((long)b * H + h * G + g) * D + t * DQ;
+    auto load_q = [&](int gg, uint32_t (&dst)[KS][2]) {
+      float qf[DQ];
+      if (gg < G) {
+        const __nv_bfloat16* qp = a.q + ((long)b * H + h * G + gg) * D + t * DQ;
 #pragma unroll
-      for (int v = 0; v < DQ / 8; ++v) {
-        const uint4 w = *reinterpret_cast<const uint4*>(qp + v * 8);
-        const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+        for (int v = 0; v < DQ / 8; ++v) {
+          const uint4 w = *reinterpret_cast<const uint4*>(qp + v * 8);
+          const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          qf[v * 8 + 2 * j] = bf16_lo(ww[j]) * qs;
-          qf[v * 8 + 2 * j + 1] = bf16_hi(ww[j]) * qs;
+          for (int j = 0; j < 4; ++j) {
+            qf[v * 8 + 2 * j] = bf16_lo(ww[j]) * qs;
+            qf[v * 8 + 2 * j + 1] = bf16_hi(ww[j]) * qs;
+          }
         }
+      } else {
+#pragma unroll
+        for (int i = 0; i < DQ; ++i) qf[i] = 0.f;
       }
+#pragma unroll
+      for (int ks = 0; ks < KS; ++ks) {
+        dst[ks][0] = pack_bf16x2(qf[4 * ks], qf[4 * ks + 1]);
+        dst[ks][1] = pack_bf16x2(qf[4 * ks + 2], qf[4 * ks + 3]);
+      }
+    };
+    load_q(g, qa);
+    if (R2) {
+      load_q(g + 8, qb);
     } else {
 #pragma unroll
-      for (int i = 0; i < DQ; ++i) qf[i] = 0.f;
-    }
-#pragma unroll
-    for (int ks = 0; ks < KS; ++ks) {
-      qa[ks][0] = pack_bf16x2(qf[4 * ks], qf[4 * ks + 1]);
-      qa[ks][1] = pack_bf16x2(qf[4 * ks + 2], qf[4 * ks + 3]);
+      for (int ks = 0; ks < KS; ++ks) qb[ks][0] = qb[ks][1] = 0u;
     }
   }
   float acc[NT][4];
 #pragma unroll
   for (int i = 0; i < NT; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
   float m = -INFINITY, l = 0.f;  // head g's running max (log2 domain) and this lane's row-sum part
+  float m2 = -INFINITY, l2 = 0.f;  // R2: the same for head g + 8
   int issued = min(nc, C::STAGES - 1);
   bool ok = true;
   const int wr0 = warp * kDecWR;           // this warp's rows inside a chunk
@@ -644,35 +658,46 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(const __grid_constant_
         }
 #pragma unroll
         for (int ks = 0; ks < KS; ++ks) {
-          const uint32_t af[4] = {qa[ks][0], 0u, qa[ks][1], 0u};
+          const uint32_t af[4] = {qa[ks][0], qb[ks][0], qa[ks][1], qb[ks][1]};
           mma16816(s[nt], af, kw[2 * ks], kw[2 * ks + 1]);
         }
       }
-      // head g's scores: tokens 2t, 2t + 1 (n-tile 0) and 8 + 2t, 9 + 2t (n-tile 1)
+      // head g's scores: tokens 2t, 2t + 1 (n-tile 0) and 8 + 2t, 9 + 2t (n-tile 1); head g + 8's
+      // (R2) are the accumulators' second row pair
       float sc[4] = {s[0][0], s[0][1], s[1][0], s[1][1]};
+      float sc2[4] = {s[0][2], s[0][3], s[1][2], s[1][3]};
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const int tok = (e >> 1) * 8 + 2 * t + (e & 1);
-        if (tok >= valid) sc[e] = -INFINITY;
+        if (tok >= valid) sc[e] = sc2[e] = -INFINITY;
       }
-      float cm = fmaxf(fmaxf(sc[0], sc[1]), fmaxf(sc[2], sc[3]));
-      cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 1));
-      cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 2));
-      if (cm > m) {
-        const float al = fast_exp2(m - cm);  // 0 while nothing has been accumulated
-        m = cm;
-        l *= al;
+      // online softmax of one row: running max mm / row-sum part ll, O columns acc[][c0, c0 + 1]
+      auto row_softmax = [&](const float (&x)[4], float& mm, float& ll, int c0, float (&pe)[4]) {
+        float cm = fmaxf(fmaxf(x[0], x[1]), fmaxf(x[2], x[3]));
+        cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 1));
+        cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 2));
+        if (cm > mm) {
+          const float al = fast_exp2(mm - cm);  // 0 while nothing has been accumulated
+          mm = cm;
+          ll *= al;
 #pragma unroll
-        for (int i = 0; i < NT; ++i) {
-          acc[i][0] *= al;
-          acc[i][1] *= al;
+          for (int i = 0; i < NT; ++i) {
+            acc[i][c0] *= al;
+            acc[i][c0 + 1] *= al;
+          }
         }
-      }
-      float pe[4];
 #pragma unroll
-      for (int e = 0; e < 4; ++e) pe[e] = (m == -INFINITY) ? 0.f : fast_exp2(sc[e] - m);
-      l += (pe[0] + pe[1]) + (pe[2] + pe[3]);
-      const uint32_t pa[4] = {pack_bf16x2(pe[0], pe[1]), 0u, pack_bf16x2(pe[2], pe[3]), 0u};
+        for (int e = 0; e < 4; ++e) pe[e] = (mm == -INFINITY) ? 0.f : fast_exp2(x[e] - mm);
+        ll += (pe[0] + pe[1]) + (pe[2] + pe[3]);
+      };
+      float pe[4], pe2[4];
+      row_softmax(sc, m, l, 0, pe);
+      uint32_t pa[4] = {pack_bf16x2(pe[0], pe[1]), 0u, pack_bf16x2(pe[2], pe[3]), 0u};
+      if (R2) {
+        row_softmax(sc2, m2, l2, 2, pe2);
+        pa[1] = pack_bf16x2(pe2[0], pe2[1]);
+        pa[3] = pack_bf16x2(pe2[2], pe2[3]);
+      }
       // O += P V: ldmatrix.trans gives the V fragments of two 8-dim n-tiles per call
       const int lr = wr0 + (lane & 7) + ((lane >> 3) & 1) * 8;  // token row this lane addresses
       const int lc = lane >> 4;                                  // +0 / +1 chunk (second n-tile)
@@ -693,24 +718,35 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(const __grid_constant_
     for (int c = 0; c < issued; ++c)
       mbar_wait(&full[c % C::STAGES], (c / C::STAGES) & 1, a.status, 302);
   }
-  // the 4 lanes of a row group hold parts of head g's row sum
+  // the 4 lanes of a row group hold parts of head g's (and g + 8's) row sum
   l += __shfl_xor_sync(0xffffffffu, l, 1);
   l += __shfl_xor_sync(0xffffffffu, l, 2);
+  l2 += __shfl_xor_sync(0xffffffffu, l2, 1);
+  l2 += __shfl_xor_sync(0xffffffffu, l2, 2);
   // merge the 4 warps through shared memory, reusing the ring (every warp is past its last read
   // of it and every issued copy has landed: each was waited on)
-  static_assert(NW * 8 * (D + 2) * 4 <= C::STAGES * C::STAGE, "merge buffers fit in the ring");
+  constexpr int GR = R2 ? 16 : 8;          // heads per warp's accumulators
+  static_assert(NW * GR * (D + 2) * 4 <= C::STAGES * C::STAGE, "merge buffers fit in the ring");
   __syncthreads();
-  float (*sm_acc)[8][D] = reinterpret_cast<float (*)[8][D]>(dsm);
-  float (*sm_m)[8] = reinterpret_cast<float (*)[8]>(dsm + NW * 8 * D * 4);
-  float (*sm_l)[8] = reinterpret_cast<float (*)[8]>(dsm + NW * 8 * D * 4 + NW * 8 * 4);
+  float (*sm_acc)[GR][D] = reinterpret_cast<float (*)[GR][D]>(dsm);
+  float (*sm_m)[GR] = reinterpret_cast<float (*)[GR]>(dsm + NW * GR * D * 4);
+  float (*sm_l)[GR] = reinterpret_cast<float (*)[GR]>(dsm + NW * GR * D * 4 + NW * GR * 4);
   if (t == 0) {
     sm_m[warp][g] = m;
     sm_l[warp][g] = l;
+    if (R2) {
+      sm_m[warp][(g + 8) % GR] = m2;
+      sm_l[warp][(g + 8) % GR] = l2;
+    }
   }
 #pragma unroll
   for (int i = 0; i < NT; ++i) {
     sm_acc[warp][g][i * 8 + 2 * t] = acc[i][0];
     sm_acc[warp][g][i * 8 + 2 * t + 1] = acc[i][1];
+    if (R2) {
+      sm_acc[warp][(g + 8) % GR][i * 8 + 2 * t] = acc[i][2];
+      sm_acc[warp][(g + 8) % GR][i * 8 + 2 * t + 1] = acc[i][3];
+    }
   }
   __syncthreads();
   // each thread finalises (g, d) entries: G * D outputs over 128 threads
@@ -752,7 +788,7 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(const __grid_constant_
   __shared__ float s_w[G][kMaxDecodeSplits];
   __shared__ float s_mx[G], s_ws[G];
   {
-    // every load issued before any store (G * eff <= 8 * 128: at most 8 per thread)
+    // every load issued before any store (G * eff <= 16 * 128: at most 16 per thread)
     constexpr int LW = (G * kMaxDecodeSplits + 127) / 128;
     float lw[LW];
 #pragma unroll
@@ -999,7 +1035,7 @@ const char* decode_attn(const DecodeAttnArgs& a, cudaStream_t s) {
   if (a.splits < 1 || a.splits > kMaxDecodeSplits) return "decode_attn: splits must be in [1, 128]";
   if ((a.D != 64 && a.D != 128) || a.geom.page % kDecCC)
     return "decode_attn: head_dim must be 64 or 128 and the page a multiple of 64 rows";
-  if (G > 8) return "decode_attn: at most 8 query heads per KV head";
+  if (G > 16) return "decode_attn: at most 16 query heads per KV head";
   for (int i = 0; i < 2; ++i)
     if (a.pf.ptr[i] && ((reinterpret_cast<uintptr_t>(a.pf.ptr[i]) | a.pf.bytes[i]) & 15))
       return "decode_attn: L2 prefetch ranges must be 16-byte aligned multiples of 16 bytes";
@@ -1015,12 +1051,17 @@ const char* decode_attn(const DecodeAttnArgs& a, cudaStream_t s) {
   cudaError_t e = cudaErrorInvalidValue;
 #define HCP_DEC_CASE(DD, GG) \
   if (a.D == DD && G == GG) e = launch_attn<DD, GG>(tm, a, s);
-  // every GQA group size up to 8 query heads per KV head: 1, 2, 4, 8 (Llama 3, Qwen2.5-3B),
-  // 3 (Llama-3.2-3B), 5 (Qwen2.5-14B), 6 (Qwen2.5-1.5B), 7 (Qwen2-0.5B, Qwen2.5-7B)
+  // every GQA group size up to 16 query heads per KV head: 1, 2, 4, 8 (Llama 3, Qwen2.5-3B),
+  // 3 (Llama-3.2-3B), 5 (Qwen2.5-14B), 6 (Qwen2.5-1.5B), 7 (Qwen2-0.5B, Qwen2.5-7B), 16
+  // (Llama-3.1-405B) and the sizes between
   HCP_DEC_CASE(64, 1) HCP_DEC_CASE(64, 2) HCP_DEC_CASE(64, 3) HCP_DEC_CASE(64, 4)
   HCP_DEC_CASE(64, 5) HCP_DEC_CASE(64, 6) HCP_DEC_CASE(64, 7) HCP_DEC_CASE(64, 8)
+  HCP_DEC_CASE(64, 9) HCP_DEC_CASE(64, 10) HCP_DEC_CASE(64, 11) HCP_DEC_CASE(64, 12)
+  HCP_DEC_CASE(64, 13) HCP_DEC_CASE(64, 14) HCP_DEC_CASE(64, 15) HCP_DEC_CASE(64, 16)
   HCP_DEC_CASE(128, 1) HCP_DEC_CASE(128, 2) HCP_DEC_CASE(128, 3) HCP_DEC_CASE(128, 4)
   HCP_DEC_CASE(128, 5) HCP_DEC_CASE(128, 6) HCP_DEC_CASE(128, 7) HCP_DEC_CASE(128, 8)
+  HCP_DEC_CASE(128, 9) HCP_DEC_CASE(128, 10) HCP_DEC_CASE(128, 11) HCP_DEC_CASE(128, 12)
+  HCP_DEC_CASE(128, 13) HCP_DEC_CASE(128, 14) HCP_DEC_CASE(128, 15) HCP_DEC_CASE(128, 16)
 #undef HCP_DEC_CASE
   if (e == cudaErrorInvalidValue) return "decode_attn: unsupported (D, H/Hkv)";
   return e == cudaSuccess ? nullptr : cudaGetErrorString(e);
@@ -1033,8 +1074,12 @@ int decode_attn_ctas_per_sm(int D, int G) {
     cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, decode_attn_kernel<DD, GG>, 128, DecCfg<DD>::SMEM);
   HCP_DEC_OCC(64, 1) HCP_DEC_OCC(64, 2) HCP_DEC_OCC(64, 3) HCP_DEC_OCC(64, 4)
   HCP_DEC_OCC(64, 5) HCP_DEC_OCC(64, 6) HCP_DEC_OCC(64, 7) HCP_DEC_OCC(64, 8)
+  HCP_DEC_OCC(64, 9) HCP_DEC_OCC(64, 10) HCP_DEC_OCC(64, 11) HCP_DEC_OCC(64, 12)
+  HCP_DEC_OCC(64, 13) HCP_DEC_OCC(64, 14) HCP_DEC_OCC(64, 15) HCP_DEC_OCC(64, 16)
   HCP_DEC_OCC(128, 1) HCP_DEC_OCC(128, 2) HCP_DEC_OCC(128, 3) HCP_DEC_OCC(128, 4)
   HCP_DEC_OCC(128, 5) HCP_DEC_OCC(128, 6) HCP_DEC_OCC(128, 7) HCP_DEC_OCC(128, 8)
+  HCP_DEC_OCC(128, 9) HCP_DEC_OCC(128, 10) HCP_DEC_OCC(128, 11) HCP_DEC_OCC(128, 12)
+  HCP_DEC_OCC(128, 13) HCP_DEC_OCC(128, 14) HCP_DEC_OCC(128, 15) HCP_DEC_OCC(128, 16)
 #undef HCP_DEC_OCC
   return n;
 }
@@ -1317,8 +1362,8 @@ extern "C" int hcp_decode_attention_noalloc(const void* q, const void* arena, in
   if (d != 64 && d != 128) return noalloc_fail(-4, "hcp_decode_attention_noalloc: head_dim must be 64 or 128");
   if (heads % hkv) return noalloc_fail(-5, "hcp_decode_attention_noalloc: heads % kv_heads != 0");
   const int G = heads / hkv;
-  if (G < 1 || G > 8)
-    return noalloc_fail(-6, "hcp_decode_attention_noalloc: heads / kv_heads must be 1 to 8");
+  if (G < 1 || G > 16)
+    return noalloc_fail(-6, "hcp_decode_attention_noalloc: heads / kv_heads must be 1 to 16");
   if ((long long)pt_stride * page > 0x7fffffffLL)
     return noalloc_fail(-2, "hcp_decode_attention_noalloc: pt_stride * page exceeds 2^31 - 1 tokens");
   const NoAllocLayout lay = noalloc_layout(batch, heads, hkv, d, splits);

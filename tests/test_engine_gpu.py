@@ -1,6 +1,7 @@
 """The whole engine on one GPU against the float32 model oracle, for the attention shapes of the
 model families the reference serves: GQA groups of 7 (Qwen2-0.5B, head_dim 64, QKV bias),
-3 (Llama-3.2-3B, head_dim 128), 5 (Qwen2.5-14B) and 6 (Qwen2.5-1.5B) query heads per KV head.
+3 (Llama-3.2-3B, head_dim 128), 5 (Qwen2.5-14B) and 6 (Qwen2.5-1.5B) query heads per KV head,
+and a group of 16 (the decode kernel's second MMA row group).
 
 Prefill logits are compared with the oracle's, then every decode step's logits with the oracle
 run on the same token sequence (teacher forcing), so bf16 rounding cannot move the comparison
@@ -16,7 +17,7 @@ STEPS = 4
 
 
 @pytest.mark.parametrize("h,hkv,d,bias", [(14, 2, 64, True), (24, 8, 128, False), (40, 8, 128, True),
-                                          (12, 2, 128, True)])
+                                          (12, 2, 128, True), (32, 2, 64, False)])
 def test_engine_gqa_groups_match_oracle(h, hkv, d, bias):
     from hetero_cp_ringattn_b200.config import preset
     from hetero_cp_ringattn_b200.models import reference_model

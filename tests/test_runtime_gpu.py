@@ -298,11 +298,14 @@ def test_qkv_gemv_rope_matches_two_kernel_path(dev, b, d):
 
 @pytest.mark.parametrize("h,hkv,d,n", [(16, 2, 128, 5000), (4, 4, 64, 70), (8, 1, 64, 1),
                                        (14, 2, 64, 333), (24, 8, 128, 1000), (40, 8, 128, 300),
-                                       (12, 2, 128, 700)])
+                                       (12, 2, 128, 700), (32, 2, 64, 900), (128, 8, 128, 600),
+                                       (9, 1, 64, 200), (24, 2, 128, 450)])
 def test_decode_attention_group_shapes(dev, h, hkv, d, n):
     """Tensor-core split-KV decode attention for 8-head GQA groups at head_dim 128 (Qwen2.5-3B),
-    no GQA, MQA with a single cached token, and the groups of 7 (Qwen2-0.5B), 3 (Llama-3.2-3B),
-    5 (Qwen2.5-14B) and 6 (Qwen2.5-1.5B) query heads per KV head, against an fp32 reference."""
+    no GQA, MQA with a single cached token, the groups of 7 (Qwen2-0.5B), 3 (Llama-3.2-3B),
+    5 (Qwen2.5-14B) and 6 (Qwen2.5-1.5B) query heads per KV head, and groups of 9 to 16 heads,
+    which use the MMA tile's second row group (16: Llama-3.1-405B's 128 / 8), against an fp32
+    reference."""
     torch.manual_seed(14)
     pages_n = -(-n // PAGE) + 1
     rt = native().Runtime(0, 1, 0, 1, pages_n + 1, PAGE, hkv, d, h, 1024, 8, 2000)

@@ -70,7 +70,7 @@ def _reference(q, arena, layer, page_tables, n_tokens, scale, hkv):
     return out.view(B, H * D)
 
 
-@pytest.mark.parametrize("d,heads,hkv", [(64, 8, 2), (128, 4, 4), (128, 16, 2), (64, 8, 1)])
+@pytest.mark.parametrize("d,heads,hkv", [(64, 8, 2), (128, 4, 4), (128, 16, 2), (64, 8, 1), (64, 24, 2)])
 def test_noalloc_decode_matches_runtime_entry_point_and_fp32(dev, d, heads, hkv):
     fn, err, nbytes, status = _lib()
     native = _ext.native()
