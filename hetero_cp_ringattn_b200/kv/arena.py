@@ -20,6 +20,20 @@ from ..errors import CapacityError
 from ..host import lib
 
 
+def staging_bytes(stage_cap: int, kv_heads: int, head_dim: int) -> int:
+    """Bytes of one rank's prefill KV staging buffers: two parities (layer steps alternate) of
+    position-ordered bf16 K and V for every position up to `stage_cap` (the engine's
+    `max_context`), [2][2][Hkv][stage_cap][D]. This is per rank whatever the number of ranks, so
+    it bounds the longest context a rank can prefill: a Llama-3-8B shape (8 KV heads, head_dim
+    128) at 512k positions needs 4.3 GB on every rank."""
+    return 2 * 2 * int(kv_heads) * int(stage_cap) * int(head_dim) * 2
+
+
+def max_staged_context(budget_bytes: int, kv_heads: int, head_dim: int) -> int:
+    """Longest context whose staging buffers fit in `budget_bytes` on a rank."""
+    return int(budget_bytes) // staging_bytes(1, kv_heads, head_dim)
+
+
 class PageAllocator:
     """Page ids of this rank's arena, handed out and taken back by the native allocator
     (`csrc/host/pages.cpp`)."""

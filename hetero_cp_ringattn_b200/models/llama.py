@@ -208,6 +208,15 @@ class LlamaCPEngine:
         return int(self.kv.alloc.num_pages * self.page_size * self.L *
                    self.cfg.kv_bytes_per_token_per_layer(2))
 
+    def staging_capacity_bytes(self) -> Optional[int]:
+        """Bytes of this rank's prefill KV staging buffers (two parities of position-ordered K
+        and V up to `max_context`; the same on every rank, see `kv.arena.staging_bytes`); None
+        on the host path."""
+        if not self.cuda:
+            return None
+        from ..kv.arena import staging_bytes
+        return staging_bytes(self.max_context, self.Hkv, self.D)
+
     def close(self, sync: bool = True) -> None:
         """Free the graphs and the runtime. `sync` waits for every rank first (peers may still
         read this rank's region); pass False when the other ranks are stopping as well."""

@@ -167,3 +167,15 @@ def test_vectorised_decode_bookkeeping_matches_the_loop_form():
             assert np.array_equal(new.reqs[rid].kv.slot_pos, old.reqs[rid].kv.slot_pos)
     else:
         raise AssertionError("the reserved slabs never filled up")
+
+
+def test_staging_memory_ceiling():
+    """The prefill staging buffers are O(L) per rank whatever the number of ranks: two parities of
+    position-ordered bf16 K and V. 512k positions of the Llama-3-8B shape need 4.3 GB per rank;
+    the ceiling for a budget inverts the formula."""
+    from hetero_cp_ringattn_b200.kv.arena import max_staged_context, staging_bytes
+    assert staging_bytes(524288, 8, 128) == 2 * 2 * 8 * 524288 * 128 * 2
+    assert abs(staging_bytes(524288, 8, 128) / 1e9 - 4.29) < 0.01
+    assert staging_bytes(32768, 8, 64) == 134217728          # Llama-3.2-1B shape at 32k: 128 MiB
+    ctx = max_staged_context(16 << 30, 8, 128)
+    assert staging_bytes(ctx, 8, 128) <= 16 << 30 < staging_bytes(ctx + 1, 8, 128)

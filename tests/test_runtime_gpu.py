@@ -526,3 +526,25 @@ def test_output_projection_with_combine_prologue(dev, world, b):
             assert (o[bb].view(H, D).float() - ro[0]).abs().max() < 2e-2
     for rt in rts:
         rt.shutdown()
+
+
+def test_context_longer_than_staging_is_rejected_before_any_kernel(dev):
+    """The staging buffers bound the context a rank can prefill (two parities of position-ordered
+    K/V up to the runtime's staging capacity): a layer step over a longer context is rejected by
+    the runtime's host check with a clear error, nothing is launched, and the runtime stays
+    usable for a context that fits."""
+    cap = 512
+    rt = native().Runtime(0, 1, 0, 1, 8, PAGE, HKV, D, H, cap, 8, 2000)
+    cos, sin = tables(dev)
+    T = 640
+    qkv = torch.zeros(T, (H + 2 * HKV) * D, device=dev, dtype=torch.bfloat16)
+    pos = torch.arange(T, device=dev, dtype=torch.int32)
+    pt = torch.arange(0, 4, dtype=torch.int32, device=dev)
+    q_out = torch.empty(T, H, D, device=dev, dtype=torch.bfloat16)
+    o_out = torch.empty_like(q_out)
+    with pytest.raises(RuntimeError, match="staging capacity"):
+        rt.push_layer(qkv, pos, cos, sin, 0, pt, 0, T, 1.0 / math.sqrt(D), True, q_out, o_out, None, 1)
+    torch.cuda.synchronize()
+    rt.check()
+    run_ranks(dev, [cap], "vanilla", rts=[rt])
+    rt.shutdown()
