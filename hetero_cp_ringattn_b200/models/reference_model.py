@@ -60,7 +60,9 @@ def forward(w: ModelWeights, ids: torch.Tensor, positions: Optional[torch.Tensor
         k = ref.apply_rope(k.reshape(L, Hkv, D), pos, cfg.rope_theta, cfg.rope_scaling)
         tap(f"prefill_k_layer_{i}", k.transpose(0, 1).unsqueeze(0))
         tap(f"prefill_v_layer_{i}", v.view(L, Hkv, D).transpose(0, 1).unsqueeze(0))
-        o, _ = ref.full_attention(q, k, v.view(L, Hkv, D), pos, pos, causal=True)
+        # queries in chunks whose [H, chunk, L] score matrix stays near 4 GB (long contexts)
+        chunk = max(1, (1 << 30) // max(1, H * L))
+        o, _ = ref.full_attention(q, k, v.view(L, Hkv, D), pos, pos, causal=True, q_chunk=chunk)
         x = x + ref.linear(o.reshape(L, H * D), t(p + "self_attn.o_proj.weight"))
         tap(f"layer_{i}_post_attn", x)
         h = ref.rmsnorm(x, t(p + "post_attention_layernorm.weight"), cfg.rms_norm_eps)

@@ -34,12 +34,25 @@ def _expand_kv(k: torch.Tensor, num_heads: int) -> torch.Tensor:
 
 def full_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
                    q_pos: Optional[torch.Tensor] = None, k_pos: Optional[torch.Tensor] = None,
-                   causal: bool = True, scale: Optional[float] = None):
+                   causal: bool = True, scale: Optional[float] = None,
+                   q_chunk: Optional[int] = None):
     """Dense softmax attention.  q [Tq,H,D], k/v [Tk,Hkv,D] -> (o [Tq,H,D], lse [H,Tq]).
 
     lse is the natural-log log-sum-exp of the scaled scores over the unmasked keys; rows with no
-    unmasked key get o = 0 and lse = -inf."""
+    unmasked key get o = 0 and lse = -inf. With `q_chunk`, the queries are processed that many at
+    a time (the score matrix of a chunk is [H, q_chunk, Tk]), for long contexts; each row's
+    result is the same as without chunking."""
     tq, h, d = q.shape
+    if q_chunk is not None and tq > q_chunk:
+        if causal and q_pos is None:
+            q_pos = torch.arange(tq, device=q.device)
+        outs, lses = [], []
+        for c0 in range(0, tq, q_chunk):
+            qp = q_pos[c0:c0 + q_chunk] if q_pos is not None else None
+            o, l = full_attention(q[c0:c0 + q_chunk], k, v, qp, k_pos, causal, scale)
+            outs.append(o)
+            lses.append(l)
+        return torch.cat(outs), torch.cat(lses, dim=1)
     scale = scale if scale is not None else 1.0 / math.sqrt(d)
     kk = _expand_kv(k, h)
     vv = _expand_kv(v, h)

@@ -124,3 +124,19 @@ def test_cli_correctness_with_native_oracle(tmp_path):
     rep = json.loads(out.read_text())
     assert rep["status"] == "pass" and rep["summary"]["failed"] == 0
     assert all(c["oracle"] == "native" for c in rep["cases"])
+
+
+def test_query_chunked_dense_attention_matches():
+    """The float32 oracle's long-context mode (queries in chunks) gives every row the same result
+    as the one-shot dense attention, causal on positions and not."""
+    import torch
+    from hetero_cp_ringattn_b200.ops import reference as ref
+    g = torch.Generator().manual_seed(3)
+    q = torch.randn(37, 8, 16, generator=g)
+    k = torch.randn(50, 2, 16, generator=g)
+    v = torch.randn(50, 2, 16, generator=g)
+    qp = torch.arange(13, 50)
+    for causal in (True, False):
+        o1, l1 = ref.full_attention(q, k, v, qp, None, causal=causal)
+        o2, l2 = ref.full_attention(q, k, v, qp, None, causal=causal, q_chunk=5)
+        assert torch.allclose(o1, o2, atol=1e-6) and torch.allclose(l1, l2, atol=1e-6)

@@ -132,3 +132,35 @@ def test_decode_switches_keep_the_tokens(env_kwargs):
     else:
         assert torch.equal(got_l, base_l)
         assert got_t == base_t
+
+
+def test_long_context_prefill_64k_matches_oracle():
+    """A 65,536-token prefill through the engine (two layers of the Llama-3.2-1B shape) and one
+    decode step against the float32 oracle, whose attention runs in query chunks at this
+    length: the long-context path end to end on one GPU (KV pages, staging buffers of 64k
+    positions, 512 KV tiles per q tile at the end of the prompt, decode over 64k cached rows)."""
+    from hetero_cp_ringattn_b200.config import preset
+    from hetero_cp_ringattn_b200.models import reference_model
+    from hetero_cp_ringattn_b200.models.llama import LlamaCPEngine
+    from hetero_cp_ringattn_b200.models.weights import ModelWeights, PreparedWeights
+    dev = torch.device("cuda", 0)
+    cfg = preset("llama-3.2-1b")
+    cfg.num_layers = 2
+    hf = ModelWeights.random_init(cfg, seed=8, device=dev, dtype=torch.bfloat16)
+    w = PreparedWeights.from_weights(hf)
+    L = 65536
+    prompt = torch.randint(0, cfg.vocab_size, (L,), generator=torch.Generator().manual_seed(12))
+    eng = LlamaCPEngine(cfg, w, device=dev, max_context=L, max_batch=1, decode_reserve=16)
+    tok, logits = eng.prefill(1, prompt, [L], decode_horizon=4, return_logits=True)
+    nxt = eng.decode_step([1], tok)
+    dec_logits = eng.last_logits(1)[0].float().cpu()
+    eng.check_device()
+    eng.release(1)
+    eng.close()
+    seq = torch.cat([prompt.to(dev), tok.view(1).to(dev)])
+    for i, got in enumerate((logits.float().cpu(), dec_logits)):
+        ref = reference_model.forward(hf, seq[:L + i], last_only=True)[0].float().cpu()
+        err = (got - ref).abs()
+        scale = max(1.0, float(ref.std()))
+        assert err.max() < 0.15 * scale and err.mean() < 0.025 * scale, (i, float(err.max()))
+    assert int(nxt) >= 0
