@@ -169,23 +169,27 @@ def bench_gemv(args, dev, pk):
     hid = 2048
     nw = torch.ones(hid, device=dev, dtype=torch.bfloat16)
     cases = [("qkv+norm", 3072, hid, "f32"), ("gate_up+norm+swiglu", 16384, hid, "swiglu"),
-             ("down+residual", 2048, 8192, "residual"), ("lm_head+norm+argmax", 128256, hid, "argmax")]
+             ("down+residual", 2048, 8192, "residual"), ("lm_head+norm+argmax", 128256, hid, "argmax"),
+             ("8b gate_up+swiglu", 28672, 4096, "swiglu"), ("8b down+residual", 4096, 14336, "residual")]
     if args.small:
         cases = cases[1:2]
-    for name, n, k, epi in cases:
-        xx = torch.randn(1, k, device=dev, dtype=torch.bfloat16)
-        w = torch.randn(n, k, device=dev, dtype=torch.bfloat16) * 0.02
-        y32 = torch.empty(1, n, device=dev, dtype=torch.float32)
-        yb = torch.zeros(1, n // 2 if epi == "swiglu" else n, device=dev, dtype=torch.bfloat16)
-        am = torch.zeros(1, dtype=torch.int64, device=dev)
-        norm = nw[:k] if (epi != "residual" and k == hid) else None
-        kw = dict(y_f32=y32 if epi in ("f32",) else None, y_bf16=yb if epi in ("swiglu", "residual") else None,
-                  argmax=am if epi == "argmax" else None, norm_w=norm)
-        ms = timed(lambda: K.gemv(xx, w, epi, **kw), args.iters, flush=flush)
-        byts = n * k * 2.0
-        emit(kernel="gemv_sm100", shape=name, N=n, K=k, epilogue=epi, us=round(ms * 1e3, 2),
-             gbs=round(byts / ms / 1e6, 1), frac_of_measured_hbm=round(byts / ms / 1e6 / pk["hbm_gbs"], 3),
-             peaks=pk["source"])
+    nw = torch.ones(4096, device=dev, dtype=torch.bfloat16)
+    for B in args.batches:
+        for name, n, k, epi in cases:
+            xx = torch.randn(B, k, device=dev, dtype=torch.bfloat16)
+            w = torch.randn(n, k, device=dev, dtype=torch.bfloat16) * 0.02
+            y32 = torch.empty(B, n, device=dev, dtype=torch.float32)
+            yb = torch.zeros(B, n // 2 if epi == "swiglu" else n, device=dev, dtype=torch.bfloat16)
+            am = torch.zeros(B, dtype=torch.int64, device=dev)
+            norm = nw[:k] if epi != "residual" else None
+            kw = dict(y_f32=y32 if epi in ("f32",) else None,
+                      y_bf16=yb if epi in ("swiglu", "residual") else None,
+                      argmax=am if epi == "argmax" else None, norm_w=norm)
+            ms = timed(lambda: K.gemv(xx, w, epi, **kw), args.iters, flush=flush)
+            byts = n * k * 2.0
+            emit(kernel="gemv_sm100", shape=name, B=B, N=n, K=k, epilogue=epi, us=round(ms * 1e3, 2),
+                 gbs=round(byts / ms / 1e6, 1),
+                 frac_of_measured_hbm=round(byts / ms / 1e6 / pk["hbm_gbs"], 3), peaks=pk["source"])
 
 
 def bench_norm(args, dev, pk):
@@ -207,7 +211,8 @@ def bench_norm(args, dev, pk):
 
 
 def bench_decode(args, dev, pk):
-    """Decode step of a model preset (``--model``) over a prefilled ``--seq`` context.
+    """Decode step of a model preset (``--model``) over a prefilled ``--seq`` context, for each
+    batch size of ``--batches`` (that many requests of the same context decoded together).
 
     The step is the captured CUDA graph the engine replays per token; ``--small`` uses 2 layers."""
     from hetero_cp_ringattn_b200.config import preset
@@ -217,30 +222,37 @@ def bench_decode(args, dev, pk):
     cfg.num_layers = 2 if args.small else (args.layers or cfg.num_layers)
     ctx = args.seq
     w = PreparedWeights.random(cfg, seed=0, device=dev)
-    eng = LlamaCPEngine(cfg, w, device=dev, max_context=ctx, max_batch=1, decode_reserve=args.iters + 16)
+    bmax = max(args.batches)
+    page = 256
+    pages = bmax * (-(-ctx // page) + -(-(args.iters + 16) // page) + 1) + 2  # every request's KV
+    eng = LlamaCPEngine(cfg, w, device=dev, max_context=ctx, max_batch=bmax,
+                        decode_reserve=args.iters + 16, page_size=page, kv_pages=pages)
     prompt = torch.randint(0, cfg.vocab_size, (ctx,), dtype=torch.int64)
-    tok, _ = eng.prefill(1, prompt, [ctx], decode_horizon=args.iters + 8)
-    cur = tok
-    for _ in range(3):
-        cur = eng.decode_step([1], cur, logits=False)
-    torch.cuda.synchronize()
-    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    n = args.iters
-    s.record()
-    for _ in range(n):
-        cur = eng.decode_step([1], cur, logits=False)
-    e.record()
-    e.synchronize()
-    ms = s.elapsed_time(e) / n
-    eng.check_device()
     per_layer_w = (cfg.hidden_size * (cfg.num_heads + 2 * cfg.kv_heads) * cfg.head_dim
                    + cfg.num_heads * cfg.head_dim * cfg.hidden_size + 3 * cfg.hidden_size * cfg.intermediate_size) * 2
-    kv = ctx * 2 * cfg.kv_heads * cfg.head_dim * 2
-    byts = cfg.num_layers * (per_layer_w + kv) + cfg.vocab_size * cfg.hidden_size * 2
-    emit(kernel="decode_step", model=args.model, layers=cfg.num_layers, context=ctx, ms_per_token=round(ms, 4),
-         tok_s=round(1e3 / ms, 1), gbs=round(byts / ms / 1e6, 1),
-         frac_of_measured_hbm=round(byts / ms / 1e6 / pk["hbm_gbs"], 3), peaks=pk["source"])
-    eng.release(1)
+    for B in args.batches:
+        ids = list(range(1, B + 1))
+        toks = [eng.prefill(r, prompt, [ctx], decode_horizon=args.iters + 8)[0].view(1) for r in ids]
+        cur = torch.cat(toks)
+        for _ in range(3):
+            cur = eng.decode_step(ids, cur, logits=False)
+        torch.cuda.synchronize()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        n = args.iters
+        s.record()
+        for _ in range(n):
+            cur = eng.decode_step(ids, cur, logits=False)
+        e.record()
+        e.synchronize()
+        ms = s.elapsed_time(e) / n
+        eng.check_device()
+        kv = B * ctx * 2 * cfg.kv_heads * cfg.head_dim * 2
+        byts = cfg.num_layers * (per_layer_w + kv) + cfg.vocab_size * cfg.hidden_size * 2
+        emit(kernel="decode_step", model=args.model, layers=cfg.num_layers, context=ctx, batch=B,
+             ms_per_token=round(ms, 4), tok_s=round(B * 1e3 / ms, 1), gbs=round(byts / ms / 1e6, 1),
+             frac_of_measured_hbm=round(byts / ms / 1e6 / pk["hbm_gbs"], 3), peaks=pk["source"])
+        for r in ids:
+            eng.release(r)
     eng.close()
 
 
@@ -389,6 +401,8 @@ def main(argv=None):
     ap.add_argument("--variants", type=lambda s: [int(x) for x in s.split(",")], default=[0],
                     help="attn: head_dim-64 kernel variants to time (0 default, 1, 2, 3 pipelined)")
     ap.add_argument("--reps", type=int, default=1, help="attn: alternating repetitions")
+    ap.add_argument("--batches", type=lambda s: [int(x) for x in s.split(",")], default=[1],
+                    help="gemv: decode rows (1, 2, 4, 8)")
     ap.add_argument("--gemm-variants", type=lambda s: [int(x) for x in s.split(",")], default=[0],
                     help="gemm: kernels to time (0 default, 1 one CTA per tile, 2 CTA pairs)")
     ap.add_argument("--orders", type=lambda s: [int(x) for x in s.split(",")], default=[-1],

@@ -169,7 +169,7 @@ void rmsnorm(torch::Tensor x, torch::Tensor w, torch::Tensor y, double eps) {
 void gemv(torch::Tensor x, torch::Tensor W, int64_t epi, c10::optional<torch::Tensor> bias,
           c10::optional<torch::Tensor> y_f32, c10::optional<torch::Tensor> y_bf16,
           c10::optional<torch::Tensor> argmax, c10::optional<torch::Tensor> norm_w, double eps,
-          int64_t index_base, std::vector<torch::Tensor> prefetch) {
+          int64_t index_base, std::vector<torch::Tensor> prefetch, int64_t tc) {
   check_cuda_bf16(x, "x");
   check_cuda_bf16(W, "W");
   const c10::cuda::CUDAGuard g(x.device());
@@ -191,6 +191,7 @@ void gemv(torch::Tensor x, torch::Tensor W, int64_t epi, c10::optional<torch::Te
   a.index_base = int(index_base);
   TORCH_CHECK(index_base >= 0 && index_base + a.N < (int64_t(1) << 31), "index_base out of range");
   a.pf = make_prefetch(prefetch);
+  a.tc = int(tc);
   a.num_sms = sm_count(x.get_device());
   a.norm_w = ptr_or_null<const __nv_bfloat16>(norm_w);
   a.eps = float(eps);
@@ -560,7 +561,7 @@ class PyRuntime {
                      c10::optional<torch::Tensor> norm_w, double eps, torch::Tensor pos,
                      torch::Tensor cos_t, torch::Tensor sin_t, int64_t layer,
                      torch::Tensor page_tables, torch::Tensor owner, torch::Tensor slot,
-                     torch::Tensor q_out, std::vector<torch::Tensor> prefetch) {
+                     torch::Tensor q_out, std::vector<torch::Tensor> prefetch, int64_t tc) {
     check_cuda_bf16(x, "x");
     check_cuda_bf16(w, "w");
     check_cuda_bf16(q_out, "q_out");
@@ -602,6 +603,7 @@ class PyRuntime {
     r.owner_stride = int(owner.size(1));
     r.status = rt_.status();
     a.pf = make_prefetch(prefetch);
+    a.tc = int(tc);
     HCP_CHECK_OK(hcp::dec::gemv(a, cur_stream()));
   }
 
@@ -734,7 +736,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemv", &gemv, py::arg("x"), py::arg("W"), py::arg("epi"), py::arg("bias") = py::none(),
         py::arg("y_f32") = py::none(), py::arg("y_bf16") = py::none(), py::arg("argmax") = py::none(),
         py::arg("norm_w") = py::none(), py::arg("eps") = 1e-6, py::arg("index_base") = 0,
-        py::arg("prefetch") = std::vector<torch::Tensor>{});
+        py::arg("prefetch") = std::vector<torch::Tensor>{}, py::arg("tc") = -1);
   m.def("fill_u64", &fill_u64);
   m.def("argmax_finalize", &argmax_finalize, py::arg("packed"), py::arg("tok32") = py::none(),
         py::arg("tok64") = py::none());
@@ -789,7 +791,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       .def("qkv_gemv_rope", &PyRuntime::qkv_gemv_rope, py::arg("x"), py::arg("w"), py::arg("bias"),
            py::arg("norm_w"), py::arg("eps"), py::arg("pos"), py::arg("cos_t"), py::arg("sin_t"),
            py::arg("layer"), py::arg("page_tables"), py::arg("owner"), py::arg("slot"),
-           py::arg("q_out"), py::arg("prefetch") = std::vector<torch::Tensor>{})
+           py::arg("q_out"), py::arg("prefetch") = std::vector<torch::Tensor>{}, py::arg("tc") = -1)
       .def("decode_combine", &PyRuntime::decode_combine)
       .def("o_proj_combine", &PyRuntime::o_proj_combine, py::arg("x"), py::arg("w"), py::arg("y"),
            py::arg("epoch_src"), py::arg("epoch_mul"), py::arg("epoch_add"))

@@ -88,44 +88,93 @@ __device__ __forceinline__ unsigned long long pack_argmax(float v, int idx) {
 // 16-byte columns l, l + 32, ... of a chunk; a row ends with one 5-step shuffle reduction and no
 // block barrier. x is staged once per CTA in shared memory; with NORM it is RMS-normalised
 // there first (the statistics of the 1-8 input rows cost far less than a separate launch).
-constexpr int GEMV_THREADS = 256;
+// D (+)= A B for one m16n8k16 bf16 tile (fp32 accumulate).
+__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
 
-template <int EPI, int B, bool NORM>
-__global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(GemvArgs a) {
-  extern __shared__ uint4 xs[];                     // [B][K/8] (normalised when NORM)
-  __shared__ float red[GEMV_THREADS / 32][B];
-  __shared__ float rstd[B];
-  constexpr bool PAIRED = (EPI == kGemvSwiGLU) || (EPI == kGemvQkvRope);
-  constexpr int NWR = PAIRED ? 2 : 1;  // weight rows per output item (gate/up, rotation pair)
-  constexpr int KC = 8 / NWR;          // 16-byte columns per lane per chunk and row
-  const int tid = threadIdx.x, lane = tid % 32, warp = tid / 32;
-  const int kvec = a.K / 8;
-  const int out_rows = PAIRED ? a.N / 2 : a.N;
-  const int half = (EPI == kGemvQkvRope) ? a.rope.D / 2 : 128;  // offset of the item's second row
-  const int nchunk = (kvec + 32 * KC - 1) / (32 * KC);
-  const int gw = blockIdx.x * (GEMV_THREADS / 32) + warp;
-  const int nwarps = gridDim.x * (GEMV_THREADS / 32);
-  const int my_rows = gw < out_rows ? (out_rows - 1 - gw) / nwarps + 1 : 0;
-  const int items = my_rows * nchunk;
-  auto load = [&](int item, uint4 (&buf)[NWR][KC]) {
-    const int o = gw + (item / nchunk) * nwarps;
-    const int c = item % nchunk;
-    const int w0 = PAIRED ? (o / half) * 2 * half + (o % half) : o;
-#pragma unroll
-    for (int q = 0; q < NWR; ++q) {
-      const uint4* wp = reinterpret_cast<const uint4*>(a.W + (long)(w0 + q * half) * a.K);
-#pragma unroll
-      for (int j = 0; j < KC; ++j) {
-        const int k = c * 32 * KC + j * 32 + lane;
-        buf[q][j] = k < kvec ? ld_stream(wp + k) : make_uint4(0u, 0u, 0u, 0u);
+// Epilogue of output item o (a weight row, or a gate / rotation pair of rows for the paired
+// epilogues, whose second row's sum is v2) for input row b, shared by both GEMV kernels. The
+// argmax epilogue only stores the logit here; the packed maxima are kept by the caller.
+template <int EPI>
+__device__ __forceinline__ void gemv_epilogue_one(const GemvArgs& a, int o, int b, float v, float v2,
+                                                  int half) {
+  if (EPI == kGemvF32) {
+    a.y_f32[(long)b * a.ldy + o] = a.bias ? v + __bfloat162float(a.bias[o]) : v;
+  } else if (EPI == kGemvResidual) {
+    __nv_bfloat16* y = a.y_bf16 + (long)b * a.ldy + o;
+    *y = __float2bfloat16(__bfloat162float(__float2bfloat16(v)) + __bfloat162float(*y));
+  } else if (EPI == kGemvSwiGLU) {
+    const float g = __bfloat162float(__float2bfloat16(v));
+    const float uu = __bfloat162float(__float2bfloat16(v2));
+    const float sg = g / (1.f + fast_exp2(-g * kLog2e));
+    a.y_bf16[(long)b * a.ldy + o] = __float2bfloat16(sg * uu);
+  } else if (EPI == kGemvArgmax) {
+    if (a.y_f32) a.y_f32[(long)b * a.ldy + o] = v;
+  } else if (EPI == kGemvQkvRope) {
+    const GemvRopeArgs& rp = a.rope;
+    const int r0 = (o / half) * 2 * half + (o % half);  // row j of head hh; its pair is j + half
+    const int hh = r0 / rp.D, j = r0 % rp.D;
+    float y1 = v, y2 = v2;
+    if (a.bias) {
+      y1 += __bfloat162float(a.bias[r0]);
+      y2 += __bfloat162float(a.bias[r0 + half]);
+    }
+    // the bf16 linear output, then the rotation
+    y1 = __bfloat162float(__float2bfloat16(y1));
+    y2 = __bfloat162float(__float2bfloat16(y2));
+    const int pos = rp.pos[b];
+    float o1 = y1, o2 = y2;
+    if (hh < rp.H + rp.Hkv) {
+      if (pos >= 0 && pos < rp.max_pos) {
+        const float c = rp.cos_t[(long)pos * half + j], sn = rp.sin_t[(long)pos * half + j];
+        o1 = y1 * c - y2 * sn;
+        o2 = y2 * c + y1 * sn;
+      } else if (j == 0 && hh == 0) {
+        report_error(rp.status, int(StatusCode::kOutOfBounds), 332, pos, b);
       }
     }
-  };
-  uint4 bufA[NWR][KC], bufB[NWR][KC];
-  pdl_trigger();
-  prefetch_l2_slices(a.pf);
-  if (items > 0) load(0, bufA);  // weights: nothing in flight writes them
-  pdl_wait();                    // x, residual rows, positions, ... come from predecessors
+    if (hh < rp.H) {
+      __nv_bfloat16* dst = rp.q_out + ((long)b * rp.H + hh) * rp.D;
+      dst[j] = __float2bfloat16(o1);
+      dst[j + half] = __float2bfloat16(o2);
+    } else if (rp.owner[b * rp.owner_stride + rp.layer]) {
+      const int slot = rp.slot[b * rp.owner_stride + rp.layer];
+      if (slot >= 0 && slot < rp.slot_cap) {
+        const int page = rp.page_tables[(long)b * rp.pt_stride + slot / rp.geom.page];
+        const int kv = hh < rp.H + rp.Hkv ? 0 : 1;
+        const int kh = hh - rp.H - kv * rp.Hkv;
+#if HCP_DEBUG_BOUNDS
+        if (page < 0 || page >= rp.geom.pages) {
+          if (j == 0) report_error(rp.status, int(StatusCode::kOutOfBounds), 333, page, b);
+        } else {
+#endif
+        __nv_bfloat16* dst = rp.arena + rp.geom.offset(rp.layer, page, kv, kh, slot % rp.geom.page);
+        dst[j] = __float2bfloat16(o1);
+        dst[j + half] = __float2bfloat16(o2);
+#if HCP_DEBUG_BOUNDS
+        }
+#endif
+      } else if (j == 0) {
+        report_error(rp.status, int(StatusCode::kOutOfBounds), 331, slot, b);
+      }
+    }
+  }
+}
+
+constexpr int GEMV_THREADS = 256;
+
+// x rows into shared memory (xs [B][K/8]), RMS-normalised there with NORM (the statistics of the
+// 1-8 input rows cost far less than a separate launch); the caller synchronises afterwards.
+template <int B, bool NORM>
+__device__ __forceinline__ void gemv_stage_x(const GemvArgs& a, uint4* xs, float (*red)[B],
+                                             float* rstd) {
+  const int tid = threadIdx.x, lane = tid % 32, warp = tid / 32;
+  const int kvec = a.K / 8;
   if (NORM) {
     float ss[B];
 #pragma unroll
@@ -168,7 +217,50 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(GemvArgs a) {
         xs[b * kvec + k] = make_uint4(o[0], o[1], o[2], o[3]);
       }
     }
-  } else if (EPI == kGemvResidual && a.cmb.xslot != nullptr) {
+  } else {
+    for (int k = tid; k < kvec; k += GEMV_THREADS)
+#pragma unroll
+      for (int b = 0; b < B; ++b) xs[b * kvec + k] = __ldg(reinterpret_cast<const uint4*>(a.x + (long)b * a.ldx) + k);
+  }
+}
+
+template <int EPI, int B, bool NORM>
+__global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(GemvArgs a) {
+  extern __shared__ uint4 xs[];                     // [B][K/8] (normalised when NORM)
+  __shared__ float red[GEMV_THREADS / 32][B];
+  __shared__ float rstd[B];
+  constexpr bool PAIRED = (EPI == kGemvSwiGLU) || (EPI == kGemvQkvRope);
+  constexpr int NWR = PAIRED ? 2 : 1;  // weight rows per output item (gate/up, rotation pair)
+  constexpr int KC = 8 / NWR;          // 16-byte columns per lane per chunk and row
+  const int tid = threadIdx.x, lane = tid % 32, warp = tid / 32;
+  const int kvec = a.K / 8;
+  const int out_rows = PAIRED ? a.N / 2 : a.N;
+  const int half = (EPI == kGemvQkvRope) ? a.rope.D / 2 : 128;  // offset of the item's second row
+  const int nchunk = (kvec + 32 * KC - 1) / (32 * KC);
+  const int gw = blockIdx.x * (GEMV_THREADS / 32) + warp;
+  const int nwarps = gridDim.x * (GEMV_THREADS / 32);
+  const int my_rows = gw < out_rows ? (out_rows - 1 - gw) / nwarps + 1 : 0;
+  const int items = my_rows * nchunk;
+  auto load = [&](int item, uint4 (&buf)[NWR][KC]) {
+    const int o = gw + (item / nchunk) * nwarps;
+    const int c = item % nchunk;
+    const int w0 = PAIRED ? (o / half) * 2 * half + (o % half) : o;
+#pragma unroll
+    for (int q = 0; q < NWR; ++q) {
+      const uint4* wp = reinterpret_cast<const uint4*>(a.W + (long)(w0 + q * half) * a.K);
+#pragma unroll
+      for (int j = 0; j < KC; ++j) {
+        const int k = c * 32 * KC + j * 32 + lane;
+        buf[q][j] = k < kvec ? ld_stream(wp + k) : make_uint4(0u, 0u, 0u, 0u);
+      }
+    }
+  };
+  uint4 bufA[NWR][KC], bufB[NWR][KC];
+  pdl_trigger();
+  prefetch_l2_slices(a.pf);
+  if (items > 0) load(0, bufA);  // weights: nothing in flight writes them
+  pdl_wait();                    // x, residual rows, positions, ... come from predecessors
+  if (EPI == kGemvResidual && !NORM && a.cmb.xslot != nullptr) {
     // x = the rank-order log-sum-exp combine of every rank's (O, LSE) partial (see
     // GemvCombineArgs); thread k builds the 8 columns [8k, 8k + 8) of head 8k / D of every row
     const GemvCombineArgs& c = a.cmb;
@@ -211,9 +303,7 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(GemvArgs a) {
       }
     }
   } else {
-    for (int k = tid; k < kvec; k += GEMV_THREADS)
-#pragma unroll
-      for (int b = 0; b < B; ++b) xs[b * kvec + k] = __ldg(reinterpret_cast<const uint4*>(a.x + (long)b * a.ldx) + k);
+    gemv_stage_x<B, NORM>(a, xs, red, rstd);
   }
   __syncthreads();
 
@@ -256,67 +346,7 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(GemvArgs a) {
         best[b] = cnd > best[b] ? cnd : best[b];
       }
       if (lane != b) continue;
-      if (EPI == kGemvF32) {
-        a.y_f32[(long)b * a.ldy + o] = a.bias ? v + __bfloat162float(a.bias[o]) : v;
-      } else if (EPI == kGemvResidual) {
-        __nv_bfloat16* y = a.y_bf16 + (long)b * a.ldy + o;
-        *y = __float2bfloat16(__bfloat162float(__float2bfloat16(v)) + __bfloat162float(*y));
-      } else if (EPI == kGemvSwiGLU) {
-        const float g = __bfloat162float(__float2bfloat16(v));
-        const float uu = __bfloat162float(__float2bfloat16(acc[NWR - 1][b]));
-        const float sg = g / (1.f + fast_exp2(-g * kLog2e));
-        a.y_bf16[(long)b * a.ldy + o] = __float2bfloat16(sg * uu);
-      } else if (EPI == kGemvArgmax) {
-        if (a.y_f32) a.y_f32[(long)b * a.ldy + o] = v;
-      } else if (EPI == kGemvQkvRope) {
-        const GemvRopeArgs& rp = a.rope;
-        const int r0 = (o / half) * 2 * half + (o % half);  // row j of head hh; its pair is j + half
-        const int hh = r0 / rp.D, j = r0 % rp.D;
-        float y1 = v, y2 = acc[1][b];
-        if (a.bias) {
-          y1 += __bfloat162float(a.bias[r0]);
-          y2 += __bfloat162float(a.bias[r0 + half]);
-        }
-        // the bf16 linear output, then the rotation
-        y1 = __bfloat162float(__float2bfloat16(y1));
-        y2 = __bfloat162float(__float2bfloat16(y2));
-        const int pos = rp.pos[b];
-        float o1 = y1, o2 = y2;
-        if (hh < rp.H + rp.Hkv) {
-          if (pos >= 0 && pos < rp.max_pos) {
-            const float c = rp.cos_t[(long)pos * half + j], sn = rp.sin_t[(long)pos * half + j];
-            o1 = y1 * c - y2 * sn;
-            o2 = y2 * c + y1 * sn;
-          } else if (j == 0 && hh == 0) {
-            report_error(rp.status, int(StatusCode::kOutOfBounds), 332, pos, b);
-          }
-        }
-        if (hh < rp.H) {
-          __nv_bfloat16* dst = rp.q_out + ((long)b * rp.H + hh) * rp.D;
-          dst[j] = __float2bfloat16(o1);
-          dst[j + half] = __float2bfloat16(o2);
-        } else if (rp.owner[b * rp.owner_stride + rp.layer]) {
-          const int slot = rp.slot[b * rp.owner_stride + rp.layer];
-          if (slot >= 0 && slot < rp.slot_cap) {
-            const int page = rp.page_tables[(long)b * rp.pt_stride + slot / rp.geom.page];
-            const int kv = hh < rp.H + rp.Hkv ? 0 : 1;
-            const int kh = hh - rp.H - kv * rp.Hkv;
-#if HCP_DEBUG_BOUNDS
-            if (page < 0 || page >= rp.geom.pages) {
-              if (j == 0) report_error(rp.status, int(StatusCode::kOutOfBounds), 333, page, b);
-            } else {
-#endif
-            __nv_bfloat16* dst = rp.arena + rp.geom.offset(rp.layer, page, kv, kh, slot % rp.geom.page);
-            dst[j] = __float2bfloat16(o1);
-            dst[j + half] = __float2bfloat16(o2);
-#if HCP_DEBUG_BOUNDS
-            }
-#endif
-          } else if (j == 0) {
-            report_error(rp.status, int(StatusCode::kOutOfBounds), 331, slot, b);
-          }
-        }
-      }
+      gemv_epilogue_one<EPI>(a, o, b, v, NWR > 1 ? acc[NWR - 1][b] : 0.f, half);
     }
   };
   for (int i = 0; i < items; i += 2) {
@@ -334,19 +364,166 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(GemvArgs a) {
   }
 }
 
+// Tensor-core decode GEMV for several input rows: the same products and epilogues as gemv_kernel,
+// computed with warp-level m16n8k16 bf16 MMAs (fp32 accumulate). A tile of 16 output items (16
+// weight rows, or 16 gate / rotation pairs) is the MMA's M side and the input rows (up to 8)
+// its N side, so every 16-byte weight load feeds all B rows with a handful of instructions,
+// where the CUDA-core kernel spends 8 FMAs per weight pair and row and turns compute-bound at
+// B = 8. The 8 warps of a CTA split the tile's K into contiguous ranges of 64-element chunks and
+// meet in shared memory: partial sums in a fixed warp order, then threads (row, input row) run
+// the epilogue. K is permuted identically for W and x: lane t of a row group reads the 16-byte
+// pieces t and 4 + t of every 64-element chunk of its two rows (full 32-byte sectors per
+// instruction) and uses their elements 4 ks .. 4 ks + 3 as the k-step ks columns {2t, 2t + 1}
+// and {2t + 8, 2t + 9}; the x fragment of input row g takes the same pieces of x.
+template <int EPI, int B, bool NORM>
+__global__ void __launch_bounds__(GEMV_THREADS) gemv_tc_kernel(GemvArgs a) {
+  extern __shared__ uint4 xs[];                     // [B][K/8] (normalised when NORM)
+  __shared__ float red_n[GEMV_THREADS / 32][B];
+  __shared__ float rstd[B];
+  constexpr bool PAIRED = (EPI == kGemvSwiGLU) || (EPI == kGemvQkvRope);
+  constexpr int NWR = PAIRED ? 2 : 1;
+  constexpr int NWARP = GEMV_THREADS / 32;
+  __shared__ float part[2][NWARP][NWR][16][8];      // [tile parity][warp][row group][row][input row]
+  const int tid = threadIdx.x, lane = tid % 32, warp = tid / 32;
+  const int g = lane / 4, t = lane % 4;
+  const int kvec = a.K / 8;
+  const int out_rows = PAIRED ? a.N / 2 : a.N;
+  const int half = (EPI == kGemvQkvRope) ? a.rope.D / 2 : 128;
+  const int tiles = out_rows / 16;
+  const int nch = a.K / 64;
+  const int c_lo = warp * nch / NWARP, c_hi = (warp + 1) * nch / NWARP;  // >= 1 chunk (nch >= 8)
+  const int my_chunks = c_hi - c_lo;
+  const int my_tiles = tiles > int(blockIdx.x) ? (tiles - 1 - int(blockIdx.x)) / int(gridDim.x) + 1 : 0;
+  const int items = my_tiles * my_chunks;
+  // item i: chunk c_lo + i % my_chunks of the CTA's (i / my_chunks)-th tile
+  auto load = [&](int item, uint4 (&buf)[NWR][2][2]) {
+    const int tile = int(blockIdx.x) + (item / my_chunks) * int(gridDim.x);
+    const int c = c_lo + item % my_chunks;
+    const int o0 = tile * 16;
+    const int w0 = PAIRED ? (o0 / half) * 2 * half + (o0 % half) : o0;
+#pragma unroll
+    for (int q = 0; q < NWR; ++q)
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        const uint4* wp = reinterpret_cast<const uint4*>(a.W + (long)(w0 + q * half + g + 8 * r) * a.K) + c * 8;
+        buf[q][r][0] = ld_stream(wp + t);
+        buf[q][r][1] = ld_stream(wp + 4 + t);
+      }
+  };
+  uint4 bufA[NWR][2][2], bufB[NWR][2][2];
+  pdl_trigger();
+  prefetch_l2_slices(a.pf);
+  if (items > 0) load(0, bufA);  // weights: nothing in flight writes them
+  pdl_wait();
+  gemv_stage_x<B, NORM>(a, xs, red_n, rstd);
+  __syncthreads();
+  float d[NWR][4];
+#pragma unroll
+  for (int q = 0; q < NWR; ++q) d[q][0] = d[q][1] = d[q][2] = d[q][3] = 0.f;
+  unsigned long long best = 0ull;                   // argmax: this thread's input row's maximum
+  const int er = tid % 16, eb = tid / 16;            // epilogue: output row er of the tile, input row eb
+  auto consume = [&](int item, const uint4 (&buf)[NWR][2][2]) {
+    const int c = c_lo + item % my_chunks;
+    uint32_t xb[8];
+    if (g < B) {
+      const uint4 x0 = xs[g * kvec + c * 8 + t], x1 = xs[g * kvec + c * 8 + 4 + t];
+      xb[0] = x0.x; xb[1] = x0.y; xb[2] = x0.z; xb[3] = x0.w;
+      xb[4] = x1.x; xb[5] = x1.y; xb[6] = x1.z; xb[7] = x1.w;
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) xb[j] = 0u;
+    }
+#pragma unroll
+    for (int q = 0; q < NWR; ++q) {
+      const uint32_t lo[8] = {buf[q][0][0].x, buf[q][0][0].y, buf[q][0][0].z, buf[q][0][0].w,
+                              buf[q][0][1].x, buf[q][0][1].y, buf[q][0][1].z, buf[q][0][1].w};
+      const uint32_t hi[8] = {buf[q][1][0].x, buf[q][1][0].y, buf[q][1][0].z, buf[q][1][0].w,
+                              buf[q][1][1].x, buf[q][1][1].y, buf[q][1][1].z, buf[q][1][1].w};
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks) {
+        const uint32_t af[4] = {lo[2 * ks], hi[2 * ks], lo[2 * ks + 1], hi[2 * ks + 1]};
+        mma16816(d[q], af, xb[2 * ks], xb[2 * ks + 1]);
+      }
+    }
+    if (item % my_chunks != my_chunks - 1) return;
+    // the warp's K range of this tile is done: partial sums to shared memory, every warp meets
+    // here once per tile (named barrier), then the epilogue threads add the 8 warps in order
+    const int k_tile = item / my_chunks;
+    const int par = k_tile & 1;
+#pragma unroll
+    for (int q = 0; q < NWR; ++q) {
+      part[par][warp][q][g][2 * t] = d[q][0];
+      part[par][warp][q][g][2 * t + 1] = d[q][1];
+      part[par][warp][q][g + 8][2 * t] = d[q][2];
+      part[par][warp][q][g + 8][2 * t + 1] = d[q][3];
+      d[q][0] = d[q][1] = d[q][2] = d[q][3] = 0.f;
+    }
+    asm volatile("bar.sync 1, %0;" ::"r"(GEMV_THREADS) : "memory");
+    if (eb < B) {
+      float v = 0.f, v2 = 0.f;
+#pragma unroll
+      for (int w = 0; w < NWARP; ++w) {
+        v += part[par][w][0][er][eb];
+        if (PAIRED) v2 += part[par][w][NWR - 1][er][eb];
+      }
+      const int o = (int(blockIdx.x) + k_tile * int(gridDim.x)) * 16 + er;
+      if (EPI == kGemvArgmax) {
+        const unsigned long long cnd = pack_argmax(v, o + a.index_base);
+        best = cnd > best ? cnd : best;
+      }
+      gemv_epilogue_one<EPI>(a, o, eb, v, v2, half);
+    }
+  };
+  for (int i = 0; i < items; i += 2) {
+    if (i + 1 < items) load(i + 1, bufB);
+    consume(i, bufA);
+    if (i + 1 < items) {
+      if (i + 2 < items) load(i + 2, bufA);
+      consume(i + 1, bufB);
+    }
+  }
+  if (EPI == kGemvArgmax && eb < B && best) atomicMax(a.argmax + eb, best);
+}
+
+// Tensor-core kernel for B >= HCP_GEMV_TC input rows (default 8; 0: never), when the shape fits
+// it: 16-item output tiles, K a multiple of 64 and at least 8 chunks (one per warp), gate /
+// rotation pairs aligned to the tiles, and no combine prologue (CUDA-core kernel only). Measured
+// in the Llama-3.2-1B decode step at 32k (ms per step, CUDA-core / tensor-core GEMVs): B = 2
+// 1.41 / 2.16, B = 4 2.03 / 2.27, B = 8 3.99 / 2.74; at B <= 4 the CUDA-core kernel is not yet
+// compute-bound and the tensor-core kernel's per-tile barrier costs more than it saves.
+static bool gemv_use_tc_shape(const GemvArgs& a) {
+  const bool paired = a.epi == kGemvSwiGLU || a.epi == kGemvQkvRope;
+  const int out_rows = paired ? a.N / 2 : a.N;
+  const int half = a.epi == kGemvQkvRope ? a.rope.D / 2 : 128;
+  return a.cmb.xslot == nullptr && out_rows % 16 == 0 && a.K % 64 == 0 && a.K >= 512 &&
+         !(paired && half % 16);
+}
+
+static bool gemv_use_tc(const GemvArgs& a) {
+  static int min_b = -2;
+  if (min_b == -2) {
+    const char* e = getenv("HCP_GEMV_TC");
+    min_b = (e && *e) ? atoi(e) : 8;
+  }
+  return min_b > 0 && a.B >= min_b && gemv_use_tc_shape(a);
+}
+
 template <int EPI, bool NORM>
 static cudaError_t gemv_launch(const GemvArgs& a, cudaStream_t s) {
   const size_t smem = size_t(a.B) * a.K * 2;
+  const bool tc = a.tc >= 0 ? (a.tc != 0 && gemv_use_tc_shape(a)) : gemv_use_tc(a);
   auto go = [&](auto kernel) -> cudaError_t {
     // the whole decode chain runs with the maximum shared-memory carveout, so consecutive
-    // (overlapping) kernels never need the SM's L1 / shared split reconfigured
-    static std::atomic<unsigned long long> carveout{0};
-    cudaError_t ce = once_per_device(carveout, [&] {
+    // (overlapping) kernels never need the SM's L1 / shared split reconfigured; set per kernel
+    // (every batch size and both kernels go through this one helper)
+    cudaError_t ce = once_per_device_kernel(reinterpret_cast<const void*>(kernel), [&] {
       return cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
                                   cudaSharedmemCarveoutMaxShared);
     });
     if (ce != cudaSuccess) return ce;
-    if (smem > 48 * 1024) {
+    // the dynamic x stage needs the opt-in once static + dynamic shared memory passes 48 KB (the
+    // tensor-core kernel holds up to 16.5 KB of static partial sums)
+    if (smem + 17 * 1024 > 48 * 1024) {
       cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
       if (e != cudaSuccess) return e;
     }
@@ -354,10 +531,20 @@ static cudaError_t gemv_launch(const GemvArgs& a, cudaStream_t s) {
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kernel, GEMV_THREADS, smem) != cudaSuccess || occ < 1)
       occ = 1;
     const int out_rows = (EPI == kGemvSwiGLU || EPI == kGemvQkvRope) ? a.N / 2 : a.N;
-    const int need = (out_rows + GEMV_THREADS / 32 - 1) / (GEMV_THREADS / 32);
+    // one warp per output item (CUDA-core kernel) or one CTA per 16-item tile (tensor cores)
+    const int need = tc ? out_rows / 16 : (out_rows + GEMV_THREADS / 32 - 1) / (GEMV_THREADS / 32);
     const int grid = need < occ * a.num_sms ? need : occ * a.num_sms;
     return launch_pdl(kernel, dim3(grid), dim3(GEMV_THREADS), smem, s, a);
   };
+  if (tc) {
+    switch (a.B) {
+      case 1: return go(gemv_tc_kernel<EPI, 1, NORM>);
+      case 2: return go(gemv_tc_kernel<EPI, 2, NORM>);
+      case 4: return go(gemv_tc_kernel<EPI, 4, NORM>);
+      case 8: return go(gemv_tc_kernel<EPI, 8, NORM>);
+      default: return cudaErrorInvalidValue;
+    }
+  }
   switch (a.B) {
     case 1: return go(gemv_kernel<EPI, 1, NORM>);
     case 2: return go(gemv_kernel<EPI, 2, NORM>);
@@ -454,13 +641,6 @@ struct DecCfg {
   static constexpr int SMEM = 1024 + STAGES * STAGE;     // + alignment slack
 };
 
-__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%0,%1,%2,%3};"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
 
 __device__ __forceinline__ void ldsm_x4_trans(uint32_t (&r)[4], uint32_t addr) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"

@@ -85,6 +85,8 @@ struct GemvArgs {
   GemvRopeArgs rope;           // kGemvQkvRope only
   GemvCombineArgs cmb;         // kGemvResidual only (optional)
   L2Prefetch pf;               // optional
+  int tc = -1;                 // tensor-core kernel: -1 by batch size (HCP_GEMV_TC, default B = 8), 0 never,
+                               // 1 whenever the shape allows it
 };
 
 struct DecodeAttnArgs {

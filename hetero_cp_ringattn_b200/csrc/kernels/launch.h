@@ -7,6 +7,9 @@
 
 #include <atomic>
 #include <cstdlib>
+#include <mutex>
+#include <set>
+#include <utility>
 
 namespace hcp {
 
@@ -49,6 +52,27 @@ cudaError_t once_per_device(std::atomic<unsigned long long>& done, F&& set) {
   if (bit && (done.load(std::memory_order_acquire) & bit)) return cudaSuccess;
   e = set();
   if (e == cudaSuccess && bit) done.fetch_or(bit, std::memory_order_acq_rel);
+  return e;
+}
+
+// The same for a call site shared by several kernels (one launch helper for every batch size or
+// kernel variant): remembered per (device, kernel address), so each kernel gets its attributes.
+template <typename F>
+cudaError_t once_per_device_kernel(const void* kernel, F&& set) {
+  static std::mutex mu;
+  static std::set<std::pair<int, const void*>> done;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (done.count({dev, kernel})) return cudaSuccess;
+  }
+  e = set();
+  if (e == cudaSuccess) {
+    std::lock_guard<std::mutex> lock(mu);
+    done.insert({dev, kernel});
+  }
   return e;
 }
 

@@ -166,25 +166,28 @@ def test_rmsnorm_embedding(dev):
     assert torch.equal(e, emb[ids.long()])
 
 
+@pytest.mark.parametrize("tc", [0, 1])
 @pytest.mark.parametrize("b", [1, 2, 4, 8])
-def test_gemv(dev, b):
+def test_gemv(dev, b, tc):
+    """Decode GEMV epilogues (f32 + bias, residual, SwiGLU, argmax with logits) on the CUDA-core
+    kernel (tc=0) and the tensor-core kernel (tc=1) against float32."""
     torch.manual_seed(6)
     kdim, n = 2048, 3072
     x = torch.randn(b, kdim, device=dev, dtype=torch.bfloat16)
     w = torch.randn(n, kdim, device=dev, dtype=torch.bfloat16) / math.sqrt(kdim)
     bias = torch.randn(n, device=dev, dtype=torch.bfloat16)
     y = torch.empty(b, n, device=dev, dtype=torch.float32)
-    K.gemv(x, w, "f32", bias=bias, y_f32=y)
+    K.gemv(x, w, "f32", bias=bias, y_f32=y, tc=tc)
     r = x.float() @ w.float().t() + bias.float()
     assert rel_err(y, r) < 1e-3
     res = torch.randn(b, n, device=dev, dtype=torch.bfloat16)
     expect = (x.float() @ w.float().t()).bfloat16().float() + res.float()
-    K.gemv(x, w, "residual", y_bf16=res)
+    K.gemv(x, w, "residual", y_bf16=res, tc=tc)
     assert rel_err(res, expect) < 1e-2
     g = torch.randn(1024, kdim, device=dev, dtype=torch.bfloat16) / math.sqrt(kdim)
     u = torch.randn(1024, kdim, device=dev, dtype=torch.bfloat16) / math.sqrt(kdim)
     out = torch.empty(b, 1024, device=dev, dtype=torch.bfloat16)
-    K.gemv(x, K.interleave_gate_up(g, u), "swiglu", y_bf16=out)
+    K.gemv(x, K.interleave_gate_up(g, u), "swiglu", y_bf16=out, tc=tc)
     gg = (x.float() @ g.float().t()).bfloat16().float()
     uu = (x.float() @ u.float().t()).bfloat16().float()
     assert rel_err(out, torch.nn.functional.silu(gg) * uu) < 2e-2
@@ -192,7 +195,7 @@ def test_gemv(dev, b):
     wl = torch.randn(vocab, kdim, device=dev, dtype=torch.bfloat16)
     am = torch.zeros(b, dtype=torch.int64, device=dev)
     logits = torch.empty(b, vocab, device=dev, dtype=torch.float32)
-    K.gemv(x, wl, "argmax", y_f32=logits, argmax=am)
+    K.gemv(x, wl, "argmax", y_f32=logits, argmax=am, tc=tc)
     tok = torch.empty(b, dtype=torch.int64, device=dev)
     native().argmax_finalize(am, None, tok)
     rl = x.float() @ wl.float().t()
@@ -200,47 +203,51 @@ def test_gemv(dev, b):
     assert rel_err(logits, rl) < 1e-3
 
 
+@pytest.mark.parametrize("tc", [0, 1])
 @pytest.mark.parametrize("b", [1, 8])
-def test_gemv_fused_rmsnorm(dev, b):
+def test_gemv_fused_rmsnorm(dev, b, tc):
     torch.manual_seed(7)
     kdim, n = 2048, 1024
     x = torch.randn(b, kdim, device=dev, dtype=torch.bfloat16) * 3
     nw = (torch.rand(kdim, device=dev) + 0.5).bfloat16()
     w = torch.randn(n, kdim, device=dev, dtype=torch.bfloat16) / math.sqrt(kdim)
     y = torch.empty(b, n, device=dev, dtype=torch.float32)
-    K.gemv(x, w, "f32", y_f32=y, norm_w=nw, eps=1e-5)
+    K.gemv(x, w, "f32", y_f32=y, norm_w=nw, eps=1e-5, tc=tc)
     xn = K.rmsnorm(x, nw, 1e-5)
     r = xn.float() @ w.float().t()
     assert rel_err(y, r) < 1e-3
     g = torch.randn(512, kdim, device=dev, dtype=torch.bfloat16) / math.sqrt(kdim)
     u = torch.randn(512, kdim, device=dev, dtype=torch.bfloat16) / math.sqrt(kdim)
     out = torch.empty(b, 512, device=dev, dtype=torch.bfloat16)
-    K.gemv(x, K.interleave_gate_up(g, u), "swiglu", y_bf16=out, norm_w=nw, eps=1e-5)
+    K.gemv(x, K.interleave_gate_up(g, u), "swiglu", y_bf16=out, norm_w=nw, eps=1e-5, tc=tc)
     gg = (xn.float() @ g.float().t()).bfloat16().float()
     uu = (xn.float() @ u.float().t()).bfloat16().float()
     assert rel_err(out, torch.nn.functional.silu(gg) * uu) < 2e-2
 
 
-@pytest.mark.parametrize("kdim,n", [(8192, 2048), (11008, 1001), (1000, 37)])
+@pytest.mark.parametrize("kdim,n", [(8192, 2048), (11008, 1001), (1000, 37), (896, 4864), (576, 1600)])
 def test_gemv_k_chunks_and_row_tails(dev, kdim, n):
-    """K that spans several per-lane chunks or ends mid-chunk, and row counts that leave a
-    partial row group, against an fp32 reference."""
+    """K that spans several per-lane chunks or ends mid-chunk, row counts that leave a partial
+    row group, and (tensor-core kernel, B = 4 and 8) K ranges that give the 8 warps 1 or 2
+    64-element chunks each, against an fp32 reference; shapes the tensor-core kernel does not
+    take (rows not a multiple of 16, K not a multiple of 64) run on the CUDA-core kernel."""
     torch.manual_seed(8)
-    for b in (1, 4):
+    for b in (1, 4, 8):
         x = torch.randn(b, kdim, device=dev, dtype=torch.bfloat16)
         w = torch.randn(n, kdim, device=dev, dtype=torch.bfloat16) / math.sqrt(kdim)
         y = torch.empty(b, n, device=dev, dtype=torch.float32)
-        K.gemv(x, w, "f32", y_f32=y)
+        K.gemv(x, w, "f32", y_f32=y, tc=1)
         assert rel_err(y, x.float() @ w.float().t()) < 1e-3
         am = torch.zeros(b, dtype=torch.int64, device=dev)
         logits = torch.empty(b, n, device=dev, dtype=torch.float32)
-        K.gemv(x, w, "argmax", y_f32=logits, argmax=am)
+        K.gemv(x, w, "argmax", y_f32=logits, argmax=am, tc=1)
         tok = torch.empty(b, dtype=torch.int64, device=dev)
         native().argmax_finalize(am, None, tok)
         assert torch.equal(tok, logits.argmax(-1))
 
 
-def test_gemv_batch_larger_than_staging(dev):
+@pytest.mark.parametrize("tc", [0, 1])
+def test_gemv_batch_larger_than_staging(dev, tc):
     """B x K too large for one shared-memory x stage (8 rows x 14336, the Llama-3-8B down
     projection at batch 8): the batch is run in halves; same result as per-row GEMVs."""
     torch.manual_seed(9)
@@ -249,7 +256,7 @@ def test_gemv_batch_larger_than_staging(dev):
     w = torch.randn(n, kdim, device=dev, dtype=torch.bfloat16) / math.sqrt(kdim)
     res = torch.randn(b, n, device=dev, dtype=torch.bfloat16)
     expect = (x.float() @ w.float().t()).bfloat16().float() + res.float()
-    K.gemv(x, w, "residual", y_bf16=res)
+    K.gemv(x, w, "residual", y_bf16=res, tc=tc)
     assert rel_err(res, expect) < 1e-2
 
 

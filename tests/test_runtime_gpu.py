@@ -259,8 +259,8 @@ def test_fused_projection_push(dev, d, chunks, strategy):
         rt.shutdown()
 
 
-@pytest.mark.parametrize("b,d", [(1, 64), (4, 128)])
-def test_qkv_gemv_rope_matches_two_kernel_path(dev, b, d):
+@pytest.mark.parametrize("b,d,tc", [(1, 64, 0), (4, 128, 0), (4, 64, 1), (8, 128, 1)])
+def test_qkv_gemv_rope_matches_two_kernel_path(dev, b, d, tc):
     """Decode QKV GEMV with the RoPE + KV-append epilogue against GEMV (fp32 out) + qkv_decode."""
     from hetero_cp_ringattn_b200.ops import kernels as K
     torch.manual_seed(13)
@@ -273,14 +273,16 @@ def test_qkv_gemv_rope_matches_two_kernel_path(dev, b, d):
     nw = (torch.rand(hid, device=dev) + 0.5).bfloat16()
     cos, sin = ref.rope_cos_sin(torch.arange(2048, device=dev), d, 10000.0)
     cos, sin = cos.contiguous(), sin.contiguous()
-    pos = torch.tensor([5, 700, 1000, 33][:b], dtype=torch.int32, device=dev)
+    pos = torch.tensor([5, 700, 1000, 33, 2, 1500, 64, 999][:b], dtype=torch.int32, device=dev)
     pt = torch.tensor([[1, 2, 3]] * b, dtype=torch.int32, device=dev)
-    owner = torch.tensor([[1, 1], [0, 1], [1, 0], [1, 1]][:b], dtype=torch.int32, device=dev)
-    slot = torch.tensor([[3, 3], [300, 301], [600, 7], [17, 18]][:b], dtype=torch.int32, device=dev)
+    owner = torch.tensor([[1, 1], [0, 1], [1, 0], [1, 1], [0, 0], [1, 1], [1, 0], [0, 1]][:b],
+                         dtype=torch.int32, device=dev)
+    slot = torch.tensor([[3, 3], [300, 301], [600, 7], [17, 18], [5, 6], [400, 401], [700, 9],
+                         [10, 767]][:b], dtype=torch.int32, device=dev)
     layer = 1
     qa = torch.empty(b, H, d, device=dev, dtype=torch.bfloat16)
     rt.arena().zero_()
-    rt.qkv_gemv_rope(x, w, bias, nw, 1e-5, pos, cos, sin, layer, pt, owner, slot, qa)
+    rt.qkv_gemv_rope(x, w, bias, nw, 1e-5, pos, cos, sin, layer, pt, owner, slot, qa, tc=tc)
     torch.cuda.synchronize()
     arena_a = rt.arena().clone()
     rt.arena().zero_()
