@@ -169,7 +169,8 @@ void rmsnorm(torch::Tensor x, torch::Tensor w, torch::Tensor y, double eps) {
 void gemv(torch::Tensor x, torch::Tensor W, int64_t epi, c10::optional<torch::Tensor> bias,
           c10::optional<torch::Tensor> y_f32, c10::optional<torch::Tensor> y_bf16,
           c10::optional<torch::Tensor> argmax, c10::optional<torch::Tensor> norm_w, double eps,
-          int64_t index_base, std::vector<torch::Tensor> prefetch, int64_t tc) {
+          int64_t index_base, std::vector<torch::Tensor> prefetch, int64_t tc, int64_t bulk,
+          c10::optional<torch::Tensor> status) {
   check_cuda_bf16(x, "x");
   check_cuda_bf16(W, "W");
   const c10::cuda::CUDAGuard g(x.device());
@@ -192,6 +193,8 @@ void gemv(torch::Tensor x, torch::Tensor W, int64_t epi, c10::optional<torch::Te
   TORCH_CHECK(index_base >= 0 && index_base + a.N < (int64_t(1) << 31), "index_base out of range");
   a.pf = make_prefetch(prefetch);
   a.tc = int(tc);
+  a.bulk = int(bulk);
+  a.status = ptr_or_null<int>(status);
   a.num_sms = sm_count(x.get_device());
   a.norm_w = ptr_or_null<const __nv_bfloat16>(norm_w);
   a.eps = float(eps);
@@ -736,7 +739,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemv", &gemv, py::arg("x"), py::arg("W"), py::arg("epi"), py::arg("bias") = py::none(),
         py::arg("y_f32") = py::none(), py::arg("y_bf16") = py::none(), py::arg("argmax") = py::none(),
         py::arg("norm_w") = py::none(), py::arg("eps") = 1e-6, py::arg("index_base") = 0,
-        py::arg("prefetch") = std::vector<torch::Tensor>{}, py::arg("tc") = -1);
+        py::arg("prefetch") = std::vector<torch::Tensor>{}, py::arg("tc") = -1, py::arg("bulk") = -1,
+        py::arg("status") = py::none());
   m.def("fill_u64", &fill_u64);
   m.def("argmax_finalize", &argmax_finalize, py::arg("packed"), py::arg("tok32") = py::none(),
         py::arg("tok64") = py::none());

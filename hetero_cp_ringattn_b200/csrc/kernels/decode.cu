@@ -167,6 +167,7 @@ __device__ __forceinline__ void gemv_epilogue_one(const GemvArgs& a, int o, int 
 }
 
 constexpr int GEMV_THREADS = 256;
+constexpr int kBulkMaxStages = 12;  // ring stages of the streaming GEMV at most
 
 // x rows into shared memory (xs [B][K/8]), RMS-normalised there with NORM (the statistics of the
 // 1-8 input rows cost far less than a separate launch); the caller synchronises afterwards.
@@ -224,6 +225,76 @@ __device__ __forceinline__ void gemv_stage_x(const GemvArgs& a, uint4* xs, float
   }
 }
 
+// x = the rank-order log-sum-exp combine of every rank's (O, LSE) partial (see GemvCombineArgs);
+// thread k builds the 8 columns [8k, 8k + 8) of head 8k / D of every row. If a flag wait runs out
+// (bounded, reported into the status word), x is staged as zeros.
+template <int B>
+__device__ __forceinline__ void gemv_stage_combined(const GemvArgs& a, uint4* xs) {
+  const int tid = threadIdx.x;
+  const int kvec = a.K / 8;
+  const GemvCombineArgs& c = a.cmb;
+  const unsigned long long e = *c.epoch_src * c.epoch_mul + c.epoch_add;
+  __shared__ int ok;
+  if (tid == 0) ok = 1;
+  __syncthreads();
+  if (tid < c.ranks && !wait_flag_geq_sys(c.ready + tid, e, c.budget_ns, c.status, 402, tid)) ok = 0;
+  __syncthreads();
+  const long rank_stride = (long)c.slot_B * c.H * (c.D + 1);
+  const float* xsl = c.xslot + (long)(e & 1ull) * c.ranks * rank_stride;
+  for (int k = tid; k < kvec; k += GEMV_THREADS) {
+    const int hh = (k * 8) / c.D, d0 = (k * 8) % c.D;
+#pragma unroll
+    for (int b = 0; b < B; ++b) {
+      float out[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) out[j] = 0.f;
+      const float* row = xsl + ((long)(c.row0 + b) * c.H + hh) * (c.D + 1);
+      if (ok) {
+        float mx = -INFINITY;
+        for (int r = 0; r < c.ranks; ++r) mx = fmaxf(mx, __ldcg(row + r * rank_stride + c.D));
+        if (mx > -INFINITY) {
+          float ws = 0.f, acc[8];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+          for (int r = 0; r < c.ranks; ++r) {
+            const float* src = row + r * rank_stride;
+            const float w = fast_exp2(__ldcg(src + c.D) - mx);
+            ws += w;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) acc[j] += w * __ldcg(src + d0 + j);
+          }
+#pragma unroll
+          for (int j = 0; j < 8; ++j) out[j] = acc[j] / ws;
+        }
+      }
+      xs[b * kvec + k] = make_uint4(pack_bf16x2(out[0], out[1]), pack_bf16x2(out[2], out[3]),
+                                    pack_bf16x2(out[4], out[5]), pack_bf16x2(out[6], out[7]));
+    }
+  }
+}
+
+// Output item o complete (acc holds each lane's partial sums over k = lane + 32 m): every lane
+// gets every warp sum, lane b runs the epilogue of input row b, and the argmax epilogue folds the
+// logit into the warp's running maxima.
+template <int EPI, int B, int NWR>
+__device__ __forceinline__ void gemv_item_done(const GemvArgs& a, int o, int lane, int half,
+                                               float (&acc)[NWR][B], unsigned long long (&best)[B]) {
+#pragma unroll
+  for (int q = 0; q < NWR; ++q)
+#pragma unroll
+    for (int b = 0; b < B; ++b) acc[q][b] = warp_sum(acc[q][b]);
+#pragma unroll
+  for (int b = 0; b < B; ++b) {
+    const float v = acc[0][b];
+    if (EPI == kGemvArgmax) {
+      const unsigned long long cnd = pack_argmax(v, o + a.index_base);
+      best[b] = cnd > best[b] ? cnd : best[b];
+    }
+    if (lane != b) continue;
+    gemv_epilogue_one<EPI>(a, o, b, v, NWR > 1 ? acc[NWR - 1][b] : 0.f, half);
+  }
+}
+
 template <int EPI, int B, bool NORM>
 __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(GemvArgs a) {
   extern __shared__ uint4 xs[];                     // [B][K/8] (normalised when NORM)
@@ -261,47 +332,7 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(GemvArgs a) {
   if (items > 0) load(0, bufA);  // weights: nothing in flight writes them
   pdl_wait();                    // x, residual rows, positions, ... come from predecessors
   if (EPI == kGemvResidual && !NORM && a.cmb.xslot != nullptr) {
-    // x = the rank-order log-sum-exp combine of every rank's (O, LSE) partial (see
-    // GemvCombineArgs); thread k builds the 8 columns [8k, 8k + 8) of head 8k / D of every row
-    const GemvCombineArgs& c = a.cmb;
-    const unsigned long long e = *c.epoch_src * c.epoch_mul + c.epoch_add;
-    __shared__ int ok;
-    if (tid == 0) ok = 1;
-    __syncthreads();
-    if (tid < c.ranks && !wait_flag_geq_sys(c.ready + tid, e, c.budget_ns, c.status, 402, tid)) ok = 0;
-    __syncthreads();
-    const long rank_stride = (long)c.slot_B * c.H * (c.D + 1);
-    const float* xsl = c.xslot + (long)(e & 1ull) * c.ranks * rank_stride;
-    for (int k = tid; k < kvec; k += GEMV_THREADS) {
-      const int hh = (k * 8) / c.D, d0 = (k * 8) % c.D;
-#pragma unroll
-      for (int b = 0; b < B; ++b) {
-        float out[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) out[j] = 0.f;
-        const float* row = xsl + ((long)(c.row0 + b) * c.H + hh) * (c.D + 1);
-        if (ok) {
-          float mx = -INFINITY;
-          for (int r = 0; r < c.ranks; ++r) mx = fmaxf(mx, __ldcg(row + r * rank_stride + c.D));
-          if (mx > -INFINITY) {
-            float ws = 0.f, acc[8];
-#pragma unroll
-            for (int j = 0; j < 8; ++j) acc[j] = 0.f;
-            for (int r = 0; r < c.ranks; ++r) {
-              const float* src = row + r * rank_stride;
-              const float w = fast_exp2(__ldcg(src + c.D) - mx);
-              ws += w;
-#pragma unroll
-              for (int j = 0; j < 8; ++j) acc[j] += w * __ldcg(src + d0 + j);
-            }
-#pragma unroll
-            for (int j = 0; j < 8; ++j) out[j] = acc[j] / ws;
-          }
-        }
-        xs[b * kvec + k] = make_uint4(pack_bf16x2(out[0], out[1]), pack_bf16x2(out[2], out[3]),
-                                      pack_bf16x2(out[4], out[5]), pack_bf16x2(out[6], out[7]));
-      }
-    }
+    gemv_stage_combined<B>(a, xs);
   } else {
     gemv_stage_x<B, NORM>(a, xs, red, rstd);
   }
@@ -332,22 +363,7 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(GemvArgs a) {
         }
       }
     }
-    if (c != nchunk - 1) return;
-    // row complete: every lane gets every sum; lane b finishes input row b
-#pragma unroll
-    for (int q = 0; q < NWR; ++q)
-#pragma unroll
-      for (int b = 0; b < B; ++b) acc[q][b] = warp_sum(acc[q][b]);
-#pragma unroll
-    for (int b = 0; b < B; ++b) {
-      const float v = acc[0][b];
-      if (EPI == kGemvArgmax) {
-        const unsigned long long cnd = pack_argmax(v, o + a.index_base);
-        best[b] = cnd > best[b] ? cnd : best[b];
-      }
-      if (lane != b) continue;
-      gemv_epilogue_one<EPI>(a, o, b, v, NWR > 1 ? acc[NWR - 1][b] : 0.f, half);
-    }
+    if (c == nchunk - 1) gemv_item_done<EPI, B, NWR>(a, o, lane, half, acc, best);
   };
   for (int i = 0; i < items; i += 2) {
     if (i + 1 < items) load(i + 1, bufB);
@@ -356,6 +372,131 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(GemvArgs a) {
       if (i + 2 < items) load(i + 2, bufA);
       consume(i + 1, bufB);
     }
+  }
+  if (EPI == kGemvArgmax && lane == 0) {
+#pragma unroll
+    for (int b = 0; b < B; ++b)
+      if (best[b]) atomicMax(a.argmax + b, best[b]);
+  }
+}
+
+// Streaming decode GEMV for 1-4 input rows: the products, the per-lane summation order and the
+// epilogues of gemv_kernel (so the results are the same bits), with the weights brought in by the
+// copy engine instead of by register loads. Each CTA owns a contiguous run of 8-item groups (8
+// consecutive output items; their weight rows - both rows of each gate / rotation pair for the
+// paired epilogues - are one or two contiguous runs of 8 full rows) and streams them through a
+// ring of stages in shared memory: a stage is one group, brought in by one untiled bulk copy
+// (cp.async.bulk) per run, issued by one thread, completing on the stage's mbarrier. Measured on
+// B200, bulk copies stream DRAM at up to 0.97 of the measured HBM copy rate when each copy moves
+// 32-64 KB and 3-4 of them are in flight per SM, while copies of 1-8 KB stay at 0.4-0.6 (a cost
+// per copy), hence whole 8-row runs (32 KB at K = 2048) and no K chunking. Weights are written by
+// nothing in flight, so the whole ring is requested before the dependency wait: every CTA's
+// first stages stream while the previous kernel of the decode chain finishes. Warp w computes
+// item w of each stage against x in shared memory and releases the stage on its "empty"
+// mbarrier; thread 0 refills a slot once all 8 warps have released it. Every wait is bounded and
+// reports into the status word.
+template <int EPI, int B, bool NORM>
+__global__ void __launch_bounds__(GEMV_THREADS) gemv_bulk_kernel(GemvArgs a) {
+  extern __shared__ __align__(128) unsigned char gsm[];  // [x rows][ring of stages]
+  __shared__ float red[GEMV_THREADS / 32][B];
+  __shared__ float rstd[B];
+  __shared__ __align__(8) uint64_t full_bar[kBulkMaxStages];
+  __shared__ __align__(8) uint64_t empty_bar[kBulkMaxStages];
+  constexpr bool PAIRED = (EPI == kGemvSwiGLU) || (EPI == kGemvQkvRope);
+  constexpr int NWR = PAIRED ? 2 : 1;          // weight rows per output item
+  constexpr int IPS = GEMV_THREADS / 32;       // items per stage: one per warp
+  const int tid = threadIdx.x, lane = tid % 32, warp = tid / 32;
+  const int kvec = a.K / 8;
+  const int half = (EPI == kGemvQkvRope) ? a.rope.D / 2 : 128;
+  const int nst = a.bulk_nst;
+  const size_t stage_elems = size_t(IPS) * NWR * a.K;
+  uint4* xs = reinterpret_cast<uint4*>(gsm);
+  __nv_bfloat16* ring =
+      reinterpret_cast<__nv_bfloat16*>(gsm + ((size_t(B) * a.K * 2 + 127) & ~size_t(127)));
+  const int ngroups = (PAIRED ? a.N / 2 : a.N) / IPS;
+  const int g0 = int((long)blockIdx.x * ngroups / gridDim.x);
+  const int nstage = int((long)(blockIdx.x + 1) * ngroups / gridDim.x) - g0;
+  int* st = a.status ? a.status : (EPI == kGemvQkvRope ? a.rope.status : a.cmb.status);
+
+  // stage s: items [8 g, 8 g + 8) of group g = g0 + s, into slot s % nst
+  auto issue = [&](int s) {
+    const int slot = s % nst;
+    const int o = (g0 + s) * IPS;
+    const int w0 = PAIRED ? (o / half) * 2 * half + (o % half) : o;
+    const uint32_t run_bytes = uint32_t(IPS) * uint32_t(a.K) * 2u;
+    __nv_bfloat16* dst = ring + slot * stage_elems;
+    mbar_arrive_expect_tx(&full_bar[slot], NWR * run_bytes);
+#pragma unroll
+    for (int q = 0; q < NWR; ++q)
+      bulk_load(dst + size_t(q) * IPS * a.K, a.W + (long)(w0 + q * half) * a.K, run_bytes, &full_bar[slot]);
+  };
+
+  pdl_trigger();
+  prefetch_l2_slices(a.pf);
+  int issued = 0;
+  if (tid == 0) {
+    for (int i = 0; i < nst; ++i) {
+      mbar_init(&full_bar[i], 1);
+      mbar_init(&empty_bar[i], IPS);
+    }
+    fence_barrier_init();
+    for (; issued < nst && issued < nstage; ++issued) issue(issued);
+  }
+  pdl_wait();                    // x, residual rows, positions, ... come from predecessors
+  if (EPI == kGemvResidual && !NORM && a.cmb.xslot != nullptr) {
+    gemv_stage_combined<B>(a, xs);
+  } else {
+    gemv_stage_x<B, NORM>(a, xs, red, rstd);
+  }
+  __syncthreads();               // x staged; the barriers initialised
+
+  float acc[NWR][B];
+  unsigned long long best[B];
+#pragma unroll
+  for (int b = 0; b < B; ++b) best[b] = 0ull;
+  bool ok = true;
+  int s = 0;
+  for (; s < nstage; ++s) {
+    const int slot = s % nst;
+    const uint32_t par = uint32_t(s / nst) & 1u;
+    if (!mbar_wait(&full_bar[slot], par, st, 350)) {
+      ok = false;
+      break;
+    }
+#pragma unroll
+    for (int q = 0; q < NWR; ++q)
+#pragma unroll
+      for (int b = 0; b < B; ++b) acc[q][b] = 0.f;
+    const uint4* wr[NWR];
+#pragma unroll
+    for (int q = 0; q < NWR; ++q)
+      wr[q] = reinterpret_cast<const uint4*>(ring + slot * stage_elems + size_t(q * IPS + warp) * a.K);
+    // lane l visits k = l + 32 m in increasing m, the order of gemv_kernel
+#pragma unroll 8
+    for (int k = lane; k < kvec; k += 32) {
+#pragma unroll
+      for (int b = 0; b < B; ++b) {
+        const uint4 xv = xs[b * kvec + k];
+#pragma unroll
+        for (int q = 0; q < NWR; ++q) dot8_acc(wr[q][k], xv, acc[q][b]);
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty_bar[slot]);
+    if (tid == 0 && issued < nstage) {   // refill this slot with stage s + nst
+      if (mbar_wait(&empty_bar[slot], par, st, 351)) {
+        issue(issued++);
+      } else {
+        ok = false;
+      }
+    }
+    gemv_item_done<EPI, B, NWR>(a, (g0 + s) * IPS + warp, lane, half, acc, best);
+    if (!ok) break;
+  }
+  if (!ok && tid == 0) {
+    // a wait ran out: let the copies still in flight land before the CTA exits (bounded)
+    for (int t = s + 1; t < issued; ++t)
+      if (!mbar_wait(&full_bar[t % nst], uint32_t(t / nst) & 1u, st, 352)) break;
   }
   if (EPI == kGemvArgmax && lane == 0) {
 #pragma unroll
@@ -508,34 +649,95 @@ static bool gemv_use_tc(const GemvArgs& a) {
   return min_b > 0 && a.B >= min_b && gemv_use_tc_shape(a);
 }
 
+static int env_int(const char* name, int dflt) {
+  const char* e = getenv(name);
+  return (e && *e) ? atoi(e) : dflt;
+}
+
+// Stage plan of the streaming kernel: a stage is 8 items x NWR full weight rows (at most 64 KB;
+// larger rows stay on the CUDA-core kernel), the ring as many stages as fit in
+// HCP_GEMV_BULK_RING_KB (default 64 KB; at least 2, at most kBulkMaxStages).
+struct GemvBulkPlan {
+  int nst = 0;
+  size_t smem = 0;
+};
+
+static bool gemv_bulk_plan(const GemvArgs& a, GemvBulkPlan& p) {
+  static const int ring_kb = env_int("HCP_GEMV_BULK_RING_KB", 64);
+  const bool paired = a.epi == kGemvSwiGLU || a.epi == kGemvQkvRope;
+  const int nwr = paired ? 2 : 1;
+  const int out_rows = paired ? a.N / 2 : a.N;
+  const int half = a.epi == kGemvQkvRope ? a.rope.D / 2 : 128;
+  if (a.B > 4 || out_rows % 8 || (paired && half % 8)) return false;
+  const size_t stage = size_t(8) * nwr * a.K * 2;
+  if (stage > 64 * 1024) return false;
+  size_t nst = size_t(ring_kb) * 1024 / stage;
+  if (nst < 2) nst = 2;
+  if (nst > size_t(kBulkMaxStages)) nst = kBulkMaxStages;
+  p.nst = int(nst);
+  p.smem = ((size_t(a.B) * a.K * 2 + 127) & ~size_t(127)) + nst * stage;
+  return p.smem <= 200 * 1024;
+}
+
+static bool gemv_use_bulk(const GemvArgs& a) {
+  static const int mode = env_int("HCP_GEMV_BULK", 1);
+  return a.bulk >= 0 ? a.bulk != 0 : mode != 0;
+}
+
 template <int EPI, bool NORM>
-static cudaError_t gemv_launch(const GemvArgs& a, cudaStream_t s) {
-  const size_t smem = size_t(a.B) * a.K * 2;
-  const bool tc = a.tc >= 0 ? (a.tc != 0 && gemv_use_tc_shape(a)) : gemv_use_tc(a);
+static cudaError_t gemv_launch(const GemvArgs& a0, cudaStream_t s) {
+  const bool tc = a0.tc >= 0 ? (a0.tc != 0 && gemv_use_tc_shape(a0)) : gemv_use_tc(a0);
+  GemvBulkPlan bp;
+  const bool bulk = !tc && gemv_use_bulk(a0) && gemv_bulk_plan(a0, bp);
+  GemvArgs a = a0;
+  a.bulk_nst = bp.nst;
+  const size_t smem = bulk ? bp.smem : size_t(a.B) * a.K * 2;
   auto go = [&](auto kernel) -> cudaError_t {
     // the whole decode chain runs with the maximum shared-memory carveout, so consecutive
-    // (overlapping) kernels never need the SM's L1 / shared split reconfigured; set per kernel
-    // (every batch size and both kernels go through this one helper)
+    // (overlapping) kernels never need the SM's L1 / shared split reconfigured; the same
+    // once-per-kernel step opens dynamic shared memory up to the opt-in limit less the kernel's
+    // static shared memory, so no launch needs it again (every batch size and all three
+    // kernels go through this one helper)
     cudaError_t ce = once_per_device_kernel(reinterpret_cast<const void*>(kernel), [&] {
-      return cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
-                                  cudaSharedmemCarveoutMaxShared);
+      cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                           cudaSharedmemCarveoutMaxShared);
+      if (e != cudaSuccess) return e;
+      cudaFuncAttributes fa;
+      int dev = 0, optin = 0;
+      if ((e = cudaFuncGetAttributes(&fa, kernel)) != cudaSuccess) return e;
+      if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
+      if ((e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev)) != cudaSuccess)
+        return e;
+      return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  optin - int(fa.sharedSizeBytes));
     });
     if (ce != cudaSuccess) return ce;
-    // the dynamic x stage needs the opt-in once static + dynamic shared memory passes 48 KB (the
-    // tensor-core kernel holds up to 16.5 KB of static partial sums)
-    if (smem + 17 * 1024 > 48 * 1024) {
-      cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
-      if (e != cudaSuccess) return e;
-    }
     int occ = 0;
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kernel, GEMV_THREADS, smem) != cudaSuccess || occ < 1)
       occ = 1;
     const int out_rows = (EPI == kGemvSwiGLU || EPI == kGemvQkvRope) ? a.N / 2 : a.N;
-    // one warp per output item (CUDA-core kernel) or one CTA per 16-item tile (tensor cores)
-    const int need = tc ? out_rows / 16 : (out_rows + GEMV_THREADS / 32 - 1) / (GEMV_THREADS / 32);
-    const int grid = need < occ * a.num_sms ? need : occ * a.num_sms;
+    int need, cap = occ * a.num_sms;
+    if (bulk) {
+      // up to HCP_GEMV_BULK_CTAS CTAs per SM (default 2, as many as fit)
+      static const int per_sm = env_int("HCP_GEMV_BULK_CTAS", 2);
+      need = out_rows / 8;
+      cap = (per_sm < occ ? (per_sm > 0 ? per_sm : 1) : occ) * a.num_sms;
+    } else if (tc) {
+      need = out_rows / 16;    // one CTA per 16-item tile
+    } else {
+      need = (out_rows + GEMV_THREADS / 32 - 1) / (GEMV_THREADS / 32);  // one warp per item
+    }
+    const int grid = need < cap ? need : cap;
     return launch_pdl(kernel, dim3(grid), dim3(GEMV_THREADS), smem, s, a);
   };
+  if (bulk) {
+    switch (a.B) {
+      case 1: return go(gemv_bulk_kernel<EPI, 1, NORM>);
+      case 2: return go(gemv_bulk_kernel<EPI, 2, NORM>);
+      case 4: return go(gemv_bulk_kernel<EPI, 4, NORM>);
+      default: return cudaErrorInvalidValue;
+    }
+  }
   if (tc) {
     switch (a.B) {
       case 1: return go(gemv_tc_kernel<EPI, 1, NORM>);

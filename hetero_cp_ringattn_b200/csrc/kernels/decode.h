@@ -87,6 +87,10 @@ struct GemvArgs {
   L2Prefetch pf;               // optional
   int tc = -1;                 // tensor-core kernel: -1 by batch size (HCP_GEMV_TC, default B = 8), 0 never,
                                // 1 whenever the shape allows it
+  int bulk = -1;               // bulk-copy streaming kernel where the tensor-core one is not used:
+                               // -1 by HCP_GEMV_BULK, 0 never, 1 whenever the shape allows it
+  int bulk_nst = 0;            // set by the launcher: ring stages of the streaming kernel
+  int* status = nullptr;       // optional status word for the pipeline waits
 };
 
 struct DecodeAttnArgs {

@@ -138,12 +138,15 @@ def embedding(ids: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = 
 # --------------------------------------------------------------------------- GEMV (decode)
 def gemv(x: torch.Tensor, w: torch.Tensor, epi: str, bias=None, y_f32=None, y_bf16=None,
          argmax=None, norm_w=None, eps: float = 1e-6, index_base: int = 0, prefetch=(),
-         tc: int = -1):
+         tc: int = -1, bulk: int = -1, status=None):
     """Decode GEMV y = f(x) @ w.T with a fused epilogue; `norm_w` applies RMSNorm to x first.
     With the "argmax" epilogue `index_base` is added to every row index of the packed maximum
     (w is then the vocabulary slice starting at that row). `prefetch`: up to two contiguous weight
     tensors of later kernels that the launch pulls into L2 while it runs. `tc`: the tensor-core
-    kernel (-1: by batch size, 0: never, 1: whenever the shape allows)."""
+    kernel (-1: by batch size, 0: never, 1: whenever the shape allows). `bulk`: the streaming kernel
+    that brings the weights in with bulk copies, where the tensor-core one is not used (-1: by
+    HCP_GEMV_BULK, on unless it is 0; 0: never; 1: whenever the shape allows). `status`: an int32
+    status word for its bounded pipeline waits."""
     if not x.is_cuda:
         if norm_w is not None:
             x = ref.rmsnorm(x, norm_w, eps)
@@ -164,6 +167,6 @@ def gemv(x: torch.Tensor, w: torch.Tensor, epi: str, bias=None, y_f32=None, y_bf
                 y_f32.copy_(y)
             return y.argmax(-1) + index_base
     native().gemv(x, w, GEMV[epi], bias, y_f32, y_bf16, argmax, norm_w, eps, index_base,
-                  list(prefetch), tc)
+                  list(prefetch), tc, bulk, status)
     launches.count()
     return y_bf16 if y_bf16 is not None else y_f32

@@ -107,6 +107,7 @@ def _strategy_worker(rank, world, port, out):
         if rank == 0:
             want = reference_model.forward(w, prompt, last_only=True)[0]
             torch.save(float((logits - want).abs().max()), out)
+        dist.barrier()   # neither rank tears the group down while the other still uses it
     finally:
         dist.destroy_process_group()
 

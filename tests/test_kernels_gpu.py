@@ -166,28 +166,33 @@ def test_rmsnorm_embedding(dev):
     assert torch.equal(e, emb[ids.long()])
 
 
-@pytest.mark.parametrize("tc", [0, 1])
+# the three decode GEMV kernels: CUDA-core register loads, bulk-copy streaming, tensor cores
+GEMV_KERNELS = {"cuda": dict(tc=0, bulk=0), "bulk": dict(tc=0, bulk=1), "tc": dict(tc=1, bulk=0)}
+
+
+@pytest.mark.parametrize("kern", list(GEMV_KERNELS))
 @pytest.mark.parametrize("b", [1, 2, 4, 8])
-def test_gemv(dev, b, tc):
-    """Decode GEMV epilogues (f32 + bias, residual, SwiGLU, argmax with logits) on the CUDA-core
-    kernel (tc=0) and the tensor-core kernel (tc=1) against float32."""
+def test_gemv(dev, b, kern):
+    """Decode GEMV epilogues (f32 + bias, residual, SwiGLU, argmax with logits) on each GEMV
+    kernel against float32 (the streaming kernel takes batches up to 4, 8 runs on CUDA cores)."""
+    tc = GEMV_KERNELS[kern]
     torch.manual_seed(6)
     kdim, n = 2048, 3072
     x = torch.randn(b, kdim, device=dev, dtype=torch.bfloat16)
     w = torch.randn(n, kdim, device=dev, dtype=torch.bfloat16) / math.sqrt(kdim)
     bias = torch.randn(n, device=dev, dtype=torch.bfloat16)
     y = torch.empty(b, n, device=dev, dtype=torch.float32)
-    K.gemv(x, w, "f32", bias=bias, y_f32=y, tc=tc)
+    K.gemv(x, w, "f32", bias=bias, y_f32=y, **tc)
     r = x.float() @ w.float().t() + bias.float()
     assert rel_err(y, r) < 1e-3
     res = torch.randn(b, n, device=dev, dtype=torch.bfloat16)
     expect = (x.float() @ w.float().t()).bfloat16().float() + res.float()
-    K.gemv(x, w, "residual", y_bf16=res, tc=tc)
+    K.gemv(x, w, "residual", y_bf16=res, **tc)
     assert rel_err(res, expect) < 1e-2
     g = torch.randn(1024, kdim, device=dev, dtype=torch.bfloat16) / math.sqrt(kdim)
     u = torch.randn(1024, kdim, device=dev, dtype=torch.bfloat16) / math.sqrt(kdim)
     out = torch.empty(b, 1024, device=dev, dtype=torch.bfloat16)
-    K.gemv(x, K.interleave_gate_up(g, u), "swiglu", y_bf16=out, tc=tc)
+    K.gemv(x, K.interleave_gate_up(g, u), "swiglu", y_bf16=out, **tc)
     gg = (x.float() @ g.float().t()).bfloat16().float()
     uu = (x.float() @ u.float().t()).bfloat16().float()
     assert rel_err(out, torch.nn.functional.silu(gg) * uu) < 2e-2
@@ -195,7 +200,7 @@ def test_gemv(dev, b, tc):
     wl = torch.randn(vocab, kdim, device=dev, dtype=torch.bfloat16)
     am = torch.zeros(b, dtype=torch.int64, device=dev)
     logits = torch.empty(b, vocab, device=dev, dtype=torch.float32)
-    K.gemv(x, wl, "argmax", y_f32=logits, argmax=am, tc=tc)
+    K.gemv(x, wl, "argmax", y_f32=logits, argmax=am, **tc)
     tok = torch.empty(b, dtype=torch.int64, device=dev)
     native().argmax_finalize(am, None, tok)
     rl = x.float() @ wl.float().t()
@@ -203,23 +208,24 @@ def test_gemv(dev, b, tc):
     assert rel_err(logits, rl) < 1e-3
 
 
-@pytest.mark.parametrize("tc", [0, 1])
-@pytest.mark.parametrize("b", [1, 8])
-def test_gemv_fused_rmsnorm(dev, b, tc):
+@pytest.mark.parametrize("kern", list(GEMV_KERNELS))
+@pytest.mark.parametrize("b", [1, 4, 8])
+def test_gemv_fused_rmsnorm(dev, b, kern):
+    tc = GEMV_KERNELS[kern]
     torch.manual_seed(7)
     kdim, n = 2048, 1024
     x = torch.randn(b, kdim, device=dev, dtype=torch.bfloat16) * 3
     nw = (torch.rand(kdim, device=dev) + 0.5).bfloat16()
     w = torch.randn(n, kdim, device=dev, dtype=torch.bfloat16) / math.sqrt(kdim)
     y = torch.empty(b, n, device=dev, dtype=torch.float32)
-    K.gemv(x, w, "f32", y_f32=y, norm_w=nw, eps=1e-5, tc=tc)
+    K.gemv(x, w, "f32", y_f32=y, norm_w=nw, eps=1e-5, **tc)
     xn = K.rmsnorm(x, nw, 1e-5)
     r = xn.float() @ w.float().t()
     assert rel_err(y, r) < 1e-3
     g = torch.randn(512, kdim, device=dev, dtype=torch.bfloat16) / math.sqrt(kdim)
     u = torch.randn(512, kdim, device=dev, dtype=torch.bfloat16) / math.sqrt(kdim)
     out = torch.empty(b, 512, device=dev, dtype=torch.bfloat16)
-    K.gemv(x, K.interleave_gate_up(g, u), "swiglu", y_bf16=out, norm_w=nw, eps=1e-5, tc=tc)
+    K.gemv(x, K.interleave_gate_up(g, u), "swiglu", y_bf16=out, norm_w=nw, eps=1e-5, **tc)
     gg = (xn.float() @ g.float().t()).bfloat16().float()
     uu = (xn.float() @ u.float().t()).bfloat16().float()
     assert rel_err(out, torch.nn.functional.silu(gg) * uu) < 2e-2
@@ -232,31 +238,68 @@ def test_gemv_k_chunks_and_row_tails(dev, kdim, n):
     64-element chunks each, against an fp32 reference; shapes the tensor-core kernel does not
     take (rows not a multiple of 16, K not a multiple of 64) run on the CUDA-core kernel."""
     torch.manual_seed(8)
-    for b in (1, 4, 8):
+    for b, kw in ((1, GEMV_KERNELS["tc"]), (4, GEMV_KERNELS["tc"]), (8, GEMV_KERNELS["tc"]),
+                  (1, GEMV_KERNELS["bulk"]), (2, GEMV_KERNELS["bulk"])):
         x = torch.randn(b, kdim, device=dev, dtype=torch.bfloat16)
         w = torch.randn(n, kdim, device=dev, dtype=torch.bfloat16) / math.sqrt(kdim)
         y = torch.empty(b, n, device=dev, dtype=torch.float32)
-        K.gemv(x, w, "f32", y_f32=y, tc=1)
+        K.gemv(x, w, "f32", y_f32=y, **kw)
         assert rel_err(y, x.float() @ w.float().t()) < 1e-3
         am = torch.zeros(b, dtype=torch.int64, device=dev)
         logits = torch.empty(b, n, device=dev, dtype=torch.float32)
-        K.gemv(x, w, "argmax", y_f32=logits, argmax=am, tc=1)
+        K.gemv(x, w, "argmax", y_f32=logits, argmax=am, **kw)
         tok = torch.empty(b, dtype=torch.int64, device=dev)
         native().argmax_finalize(am, None, tok)
         assert torch.equal(tok, logits.argmax(-1))
 
 
-@pytest.mark.parametrize("tc", [0, 1])
-def test_gemv_batch_larger_than_staging(dev, tc):
+@pytest.mark.parametrize("kdim", [2048, 4096, 896])
+@pytest.mark.parametrize("b", [1, 2, 4])
+def test_gemv_bulk_bit_identical_to_cuda_core(dev, b, kdim):
+    """The streaming kernel keeps the CUDA-core kernel's per-lane summation order: every epilogue
+    (f32 + bias, fused RMSNorm, residual, SwiGLU, argmax with logits) gives the same bits, for
+    32 KB stages (K = 2048), 64 KB stages (K = 4096; its SwiGLU rows exceed a stage and run on
+    the CUDA-core kernel) and a K that is not a multiple of 256 (896)."""
+    torch.manual_seed(14)
+    n = 1536
+    x = torch.randn(b, kdim, device=dev, dtype=torch.bfloat16)
+    w = torch.randn(n, kdim, device=dev, dtype=torch.bfloat16) / math.sqrt(kdim)
+    bias = torch.randn(n, device=dev, dtype=torch.bfloat16)
+    nw = (torch.rand(kdim, device=dev) + 0.5).bfloat16()
+    res0 = torch.randn(b, n, device=dev, dtype=torch.bfloat16)
+    st = status_tensor(dev)
+    out = {}
+    for kern in ("cuda", "bulk"):
+        kw = dict(GEMV_KERNELS[kern], status=st)
+        y = torch.empty(b, n, device=dev, dtype=torch.float32)
+        K.gemv(x, w, "f32", bias=bias, y_f32=y, **kw)
+        yn = torch.empty(b, n, device=dev, dtype=torch.float32)
+        K.gemv(x, w, "f32", y_f32=yn, norm_w=nw, eps=1e-5, **kw)
+        res = res0.clone()
+        K.gemv(x, w, "residual", y_bf16=res, **kw)
+        sw = torch.empty(b, n // 2, device=dev, dtype=torch.bfloat16)
+        K.gemv(x, w, "swiglu", y_bf16=sw, **kw)
+        am = torch.zeros(b, dtype=torch.int64, device=dev)
+        logits = torch.empty(b, n, device=dev, dtype=torch.float32)
+        K.gemv(x, w, "argmax", y_f32=logits, argmax=am, index_base=7, **kw)
+        out[kern] = (y, yn, res, sw, am, logits)
+    assert_status_clean(st)
+    for u, v in zip(out["cuda"], out["bulk"]):
+        assert torch.equal(u, v)
+
+
+@pytest.mark.parametrize("kern", list(GEMV_KERNELS))
+def test_gemv_batch_larger_than_staging(dev, kern):
     """B x K too large for one shared-memory x stage (8 rows x 14336, the Llama-3-8B down
     projection at batch 8): the batch is run in halves; same result as per-row GEMVs."""
+    tc = GEMV_KERNELS[kern]
     torch.manual_seed(9)
     b, kdim, n = 8, 14336, 256
     x = torch.randn(b, kdim, device=dev, dtype=torch.bfloat16)
     w = torch.randn(n, kdim, device=dev, dtype=torch.bfloat16) / math.sqrt(kdim)
     res = torch.randn(b, n, device=dev, dtype=torch.bfloat16)
     expect = (x.float() @ w.float().t()).bfloat16().float() + res.float()
-    K.gemv(x, w, "residual", y_bf16=res, tc=tc)
+    K.gemv(x, w, "residual", y_bf16=res, **tc)
     assert rel_err(res, expect) < 1e-2
 
 
