@@ -166,6 +166,50 @@ void rmsnorm(torch::Tensor x, torch::Tensor w, torch::Tensor y, double eps) {
                                 float(eps), cur_stream()));
 }
 
+// GEMV chain recording: between gemv_chain_begin() and gemv_chain_end() the decode GEMV entry
+// points (gemv, qkv_gemv_rope, o_proj_combine) check their arguments and record them instead of
+// launching; gemv_chain_end launches the recorded GEMVs as one chain kernel when they form its
+// phase sequence, else one after the other. Per host thread (the thread that captures a decode
+// graph records its own GEMVs).
+thread_local bool g_chain_recording = false;
+thread_local std::vector<hcp::dec::GemvArgs> g_chain_phases;
+
+static void launch_gemv(const hcp::dec::GemvArgs& a) {
+  if (g_chain_recording) {
+    HCP_CHECK_OK(hcp::dec::gemv_check(a));
+    g_chain_phases.push_back(a);
+    return;
+  }
+  HCP_CHECK_OK(hcp::dec::gemv(a, cur_stream()));
+}
+
+// Starts a recording; one left open by an exception in the middle of a recorded region is
+// discarded.
+void gemv_chain_begin() {
+  g_chain_phases.clear();
+  g_chain_recording = true;
+}
+
+// Returns true when the recorded GEMVs ran as one chain launch. `ctr`: a zeroed int32 pair on
+// the GEMVs' device, owned by this launch site.
+bool gemv_chain_end(torch::Tensor ctr, c10::optional<torch::Tensor> status, bool chain) {
+  TORCH_CHECK(g_chain_recording, "gemv_chain_end without gemv_chain_begin");
+  g_chain_recording = false;
+  std::vector<hcp::dec::GemvArgs> ph;
+  ph.swap(g_chain_phases);
+  const int n = int(ph.size());
+  if (chain && hcp::dec::gemv_chain_supported(ph.data(), n)) {
+    TORCH_CHECK(ctr.is_cuda() && ctr.scalar_type() == torch::kInt32 && ctr.numel() >= 2 && ctr.is_contiguous(),
+                "gemv_chain_end: ctr must be a contiguous CUDA int32 tensor of 2 elements");
+    const c10::cuda::CUDAGuard g(ctr.device());
+    HCP_CHECK_OK(hcp::dec::gemv_chain(ph.data(), n, reinterpret_cast<unsigned int*>(ctr.data_ptr()),
+                                      ptr_or_null<int>(status), cur_stream()));
+    return true;
+  }
+  for (const auto& a : ph) HCP_CHECK_OK(hcp::dec::gemv(a, cur_stream()));
+  return false;
+}
+
 void gemv(torch::Tensor x, torch::Tensor W, int64_t epi, c10::optional<torch::Tensor> bias,
           c10::optional<torch::Tensor> y_f32, c10::optional<torch::Tensor> y_bf16,
           c10::optional<torch::Tensor> argmax, c10::optional<torch::Tensor> norm_w, double eps,
@@ -203,7 +247,7 @@ void gemv(torch::Tensor x, torch::Tensor W, int64_t epi, c10::optional<torch::Te
   if (epi == hcp::dec::kGemvF32) TORCH_CHECK(a.y_f32 != nullptr, "y_f32 required");
   if (epi == hcp::dec::kGemvResidual || epi == hcp::dec::kGemvSwiGLU)
     TORCH_CHECK(a.y_bf16 != nullptr, "y_bf16 required");
-  HCP_CHECK_OK(hcp::dec::gemv(a, cur_stream()));
+  launch_gemv(a);
 }
 
 void fill_u64(torch::Tensor t, int64_t v) {
@@ -607,7 +651,7 @@ class PyRuntime {
     r.status = rt_.status();
     a.pf = make_prefetch(prefetch);
     a.tc = int(tc);
-    HCP_CHECK_OK(hcp::dec::gemv(a, cur_stream()));
+    launch_gemv(a);
   }
 
   // Output projection of a decode step on several ranks with the cross-rank combine in its
@@ -648,7 +692,7 @@ class PyRuntime {
     m.row0 = 0;
     m.budget_ns = c.peer_wait_budget_ns;
     m.status = rt_.status();
-    HCP_CHECK_OK(hcp::dec::gemv(a, cur_stream()));
+    launch_gemv(a);
   }
 
   void decode_combine(torch::Tensor out, int64_t B, int64_t H, c10::optional<torch::Tensor> epoch_src,
@@ -741,6 +785,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("norm_w") = py::none(), py::arg("eps") = 1e-6, py::arg("index_base") = 0,
         py::arg("prefetch") = std::vector<torch::Tensor>{}, py::arg("tc") = -1, py::arg("bulk") = -1,
         py::arg("status") = py::none());
+  m.def("gemv_chain_begin", &gemv_chain_begin);
+  m.def("gemv_chain_end", &gemv_chain_end, py::arg("ctr"), py::arg("status") = py::none(),
+        py::arg("chain") = true);
   m.def("fill_u64", &fill_u64);
   m.def("argmax_finalize", &argmax_finalize, py::arg("packed"), py::arg("tok32") = py::none(),
         py::arg("tok64") = py::none());

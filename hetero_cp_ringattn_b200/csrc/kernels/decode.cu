@@ -107,7 +107,7 @@ __device__ __forceinline__ void gemv_epilogue_one(const GemvArgs& a, int o, int 
     a.y_f32[(long)b * a.ldy + o] = a.bias ? v + __bfloat162float(a.bias[o]) : v;
   } else if (EPI == kGemvResidual) {
     __nv_bfloat16* y = a.y_bf16 + (long)b * a.ldy + o;
-    *y = __float2bfloat16(__bfloat162float(__float2bfloat16(v)) + __bfloat162float(*y));
+    *y = __float2bfloat16(__bfloat162float(__float2bfloat16(v)) + __bfloat162float(__ldcg(y)));
   } else if (EPI == kGemvSwiGLU) {
     const float g = __bfloat162float(__float2bfloat16(v));
     const float uu = __bfloat162float(__float2bfloat16(v2));
@@ -170,7 +170,9 @@ constexpr int GEMV_THREADS = 256;
 constexpr int kBulkMaxStages = 12;  // ring stages of the streaming GEMV at most
 
 // x rows into shared memory (xs [B][K/8]), RMS-normalised there with NORM (the statistics of the
-// 1-8 input rows cost far less than a separate launch); the caller synchronises afterwards.
+// 1-8 input rows cost far less than a separate launch); the caller synchronises afterwards. x is
+// read through L2 (ld.global.cg): in a GEMV chain it was written by other SMs earlier in the same
+// launch, so no SM may serve it from its own L1.
 template <int B, bool NORM>
 __device__ __forceinline__ void gemv_stage_x(const GemvArgs& a, uint4* xs, float (*red)[B],
                                              float* rstd) {
@@ -183,7 +185,7 @@ __device__ __forceinline__ void gemv_stage_x(const GemvArgs& a, uint4* xs, float
     for (int k = tid; k < kvec; k += GEMV_THREADS) {
 #pragma unroll
       for (int b = 0; b < B; ++b) {
-        const uint4 v = __ldg(reinterpret_cast<const uint4*>(a.x + (long)b * a.ldx) + k);
+        const uint4 v = __ldcg(reinterpret_cast<const uint4*>(a.x + (long)b * a.ldx) + k);
         const uint32_t vv[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
         for (int j = 0; j < 4; ++j) ss[b] += bf16_lo(vv[j]) * bf16_lo(vv[j]) + bf16_hi(vv[j]) * bf16_hi(vv[j]);
@@ -206,7 +208,7 @@ __device__ __forceinline__ void gemv_stage_x(const GemvArgs& a, uint4* xs, float
       const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
 #pragma unroll
       for (int b = 0; b < B; ++b) {
-        const uint4 v = __ldg(reinterpret_cast<const uint4*>(a.x + (long)b * a.ldx) + k);
+        const uint4 v = __ldcg(reinterpret_cast<const uint4*>(a.x + (long)b * a.ldx) + k);
         const uint32_t vv[4] = {v.x, v.y, v.z, v.w};
         uint32_t o[4];
 #pragma unroll
@@ -221,7 +223,7 @@ __device__ __forceinline__ void gemv_stage_x(const GemvArgs& a, uint4* xs, float
   } else {
     for (int k = tid; k < kvec; k += GEMV_THREADS)
 #pragma unroll
-      for (int b = 0; b < B; ++b) xs[b * kvec + k] = __ldg(reinterpret_cast<const uint4*>(a.x + (long)b * a.ldx) + k);
+      for (int b = 0; b < B; ++b) xs[b * kvec + k] = __ldcg(reinterpret_cast<const uint4*>(a.x + (long)b * a.ldx) + k);
   }
 }
 
@@ -295,11 +297,13 @@ __device__ __forceinline__ void gemv_item_done(const GemvArgs& a, int o, int lan
   }
 }
 
-template <int EPI, int B, bool NORM>
-__global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(GemvArgs a) {
-  extern __shared__ uint4 xs[];                     // [B][K/8] (normalised when NORM)
-  __shared__ float red[GEMV_THREADS / 32][B];
-  __shared__ float rstd[B];
+// The register-load GEMV over the whole grid (warp gw takes items gw, gw + warps, ...): each warp
+// loads its first weight chunk, then `before_x()` (the dependency wait of a launch of its own, or
+// the grid barrier between the phases of a GEMV chain; false: skip the phase), then x is staged
+// and the items run with the next chunk's loads in flight. xs [B][K/8] is the x stage.
+template <int EPI, int B, bool NORM, class BeforeX>
+__device__ __forceinline__ void gemv_body(const GemvArgs& a, uint4* xs, float (*red)[B], float* rstd,
+                                          BeforeX&& before_x) {
   constexpr bool PAIRED = (EPI == kGemvSwiGLU) || (EPI == kGemvQkvRope);
   constexpr int NWR = PAIRED ? 2 : 1;  // weight rows per output item (gate/up, rotation pair)
   constexpr int KC = 8 / NWR;          // 16-byte columns per lane per chunk and row
@@ -327,10 +331,8 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(GemvArgs a) {
     }
   };
   uint4 bufA[NWR][KC], bufB[NWR][KC];
-  pdl_trigger();
-  prefetch_l2_slices(a.pf);
   if (items > 0) load(0, bufA);  // weights: nothing in flight writes them
-  pdl_wait();                    // x, residual rows, positions, ... come from predecessors
+  if (!before_x()) return;       // x, residual rows, positions, ... come from predecessors
   if (EPI == kGemvResidual && !NORM && a.cmb.xslot != nullptr) {
     gemv_stage_combined<B>(a, xs);
   } else {
@@ -378,6 +380,19 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(GemvArgs a) {
     for (int b = 0; b < B; ++b)
       if (best[b]) atomicMax(a.argmax + b, best[b]);
   }
+}
+
+template <int EPI, int B, bool NORM>
+__global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(GemvArgs a) {
+  extern __shared__ uint4 xs[];                     // [B][K/8] (normalised when NORM)
+  __shared__ float red[GEMV_THREADS / 32][B];
+  __shared__ float rstd[B];
+  pdl_trigger();
+  prefetch_l2_slices(a.pf);
+  gemv_body<EPI, B, NORM>(a, xs, red, rstd, [] {
+    pdl_wait();
+    return true;
+  });
 }
 
 // Streaming decode GEMV for 1-4 input rows: the products, the per-lane summation order and the
@@ -761,7 +776,7 @@ static cudaError_t gemv_dispatch(const GemvArgs& a, cudaStream_t s) {
   return a.norm_w ? gemv_launch<EPI, true>(a, s) : gemv_launch<EPI, false>(a, s);
 }
 
-const char* gemv(const GemvArgs& a, cudaStream_t s) {
+const char* gemv_check(const GemvArgs& a) {
   if (a.K % 8 || a.ldx % 8) return "gemv: K and ldx must be multiples of 8";
   if (a.B != 1 && a.B != 2 && a.B != 4 && a.B != 8) return "gemv: B must be 1, 2, 4 or 8";
   if (a.epi == kGemvSwiGLU && a.N % 256) return "gemv: SwiGLU needs N % 256 == 0";
@@ -779,6 +794,11 @@ const char* gemv(const GemvArgs& a, cudaStream_t s) {
        !a.cmb.ready || !a.cmb.epoch_src))
     return "gemv: the combine prologue needs the residual epilogue, no norm, K = H * D, D % 8 == 0";
   if (size_t(a.K) * 2 > 200 * 1024) return "gemv: needs K*2 <= 200 KB (x is staged in shared memory)";
+  return nullptr;
+}
+
+const char* gemv(const GemvArgs& a, cudaStream_t s) {
+  if (const char* err = gemv_check(a)) return err;
   if (size_t(a.B) * a.K * 2 > 200 * 1024) {
     // x rows are staged in shared memory: run the batch in halves (their rows are independent)
     GemvArgs lo = a, hi = a;
@@ -807,6 +827,152 @@ const char* gemv(const GemvArgs& a, cudaStream_t s) {
     case kGemvArgmax: e = gemv_dispatch<kGemvArgmax>(a, s); break;
     case kGemvQkvRope: e = gemv_dispatch<kGemvQkvRope>(a, s); break;
     default: return "gemv: unknown epilogue";
+  }
+  return e == cudaSuccess ? nullptr : cudaGetErrorString(e);
+}
+
+// ----------------------------------------------------------------------------- GEMV chain
+// Grid barrier of the chain kernel: every CTA arrives on ctr[0] (release), then waits (bounded)
+// until the grid's CTAs have arrived `target` times in all (acquire). CTA-uniform result.
+__device__ __forceinline__ bool chain_barrier(unsigned int* ctr, unsigned int target, int* status,
+                                              int site) {
+  __shared__ int s_ok;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    atomicAdd(ctr, 1u);
+    int ok = 1;
+    const uint64_t t0 = globaltimer_ns();
+    for (int it = 0;; ++it) {
+      unsigned int v;
+      asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(ctr) : "memory");
+      if (v >= target) break;
+      if (it >= 8) __nanosleep(32);   // back off: every CTA of the grid polls this one word
+      if ((it & 255) == 255) {
+        if (error_raised(status)) {
+          ok = 0;
+          break;
+        }
+        if (globaltimer_ns() - t0 > kPipeTimeoutNs) {
+          report_error(status, int(StatusCode::kMbarTimeout), site, int(target), int(v));
+          ok = 0;
+          break;
+        }
+      }
+    }
+    s_ok = ok;
+  }
+  __syncthreads();
+  return s_ok != 0;
+}
+
+// The decode GEMVs between two attention launches as one cooperative launch: the output
+// projection (+ residual; with the cross-rank combine in its prologue when its arguments carry
+// one), RMSNorm + gate/up + SwiGLU, the down projection (+ residual), then RMSNorm + either the
+// next layer's QKV projection with RoPE and the KV append (LAST = kGemvQkvRope) or the LM head
+// with the argmax (LAST = kGemvArgmax). The phases run the register-load GEMV body over the whole
+// grid, separated by grid barriers, and every warp requests its first weight chunk of a phase
+// before it waits at the barrier. One launch replaces four, whose boundaries (the drain of one
+// grid, the ramp of the next, the dependency wait) cost several microseconds each in the decode
+// step. The phase sequence is fixed at compile time, so every phase reads its arguments at a
+// constant offset. Measured on B200 it is slower than the four launches it replaces (Llama-3.2-1B
+// decode at 32k: 1.18-1.27 against 1.09-1.12 ms per token at batch 1, 2.50-2.61 against
+// 1.96-2.09 at batch 4, also with a back-off in the barrier poll and with the launch allowed to
+// start early), so the engine runs it only with HCP_DECODE_CHAIN=1. The dependent launch (the next attention) is released once the last barrier
+// is passed. ctr[0] counts barrier arrivals and ctr[1] CTAs done; the last CTA out sets both back
+// to zero, so one counter pair serves every replay of a captured graph.
+template <int B, int LAST>
+__global__ void __launch_bounds__(GEMV_THREADS) gemv_chain_kernel(const __grid_constant__ GemvChainArgs c) {
+  extern __shared__ uint4 xs[];
+  __shared__ float red[GEMV_THREADS / 32][B];
+  __shared__ float rstd[B];
+  bool ok = true;
+  auto barrier = [&](int phase) {
+    if (!chain_barrier(c.ctr, unsigned(phase) * gridDim.x, c.status, 360 + phase)) {
+      ok = false;
+      return false;
+    }
+    if (phase == 3) pdl_trigger();
+    return true;
+  };
+  gemv_body<kGemvResidual, B, false>(c.ph[0], xs, red, rstd, [] {
+    pdl_wait();
+    return true;
+  });
+  gemv_body<kGemvSwiGLU, B, true>(c.ph[1], xs, red, rstd, [&] { return barrier(1); });
+  if (ok) gemv_body<kGemvResidual, B, false>(c.ph[2], xs, red, rstd, [&] { return barrier(2); });
+  if (ok) gemv_body<LAST, B, true>(c.ph[3], xs, red, rstd, [&] { return barrier(3); });
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    if (atomicAdd(c.ctr + 1, 1u) == gridDim.x - 1) {   // every CTA is past every barrier wait
+      atomicExch(c.ctr, 0u);
+      atomicExch(c.ctr + 1, 0u);
+    }
+  }
+}
+
+template <int B, int LAST>
+static cudaError_t launch_chain(const GemvChainArgs& c, size_t smem, cudaStream_t s) {
+  auto kernel = gemv_chain_kernel<B, LAST>;
+  cudaError_t ce = once_per_device_kernel(reinterpret_cast<const void*>(kernel), [&] {
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                         cudaSharedmemCarveoutMaxShared);
+    if (e != cudaSuccess) return e;
+    return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+  });
+  if (ce != cudaSuccess) return ce;
+  int occ = 0;
+  if ((ce = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kernel, GEMV_THREADS, smem)) != cudaSuccess)
+    return ce;
+  if (occ < 1) return cudaErrorInvalidConfiguration;
+  // a cooperative launch: all CTAs are resident together (they wait for one another)
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(occ * c.ph[0].num_sms);
+  cfg.blockDim = dim3(GEMV_THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, c);
+}
+
+bool gemv_chain_supported(const GemvArgs* ph, int n) {
+  if (n != kGemvChainPhases) return false;
+  const int epi[3] = {kGemvResidual, kGemvSwiGLU, kGemvResidual};
+  for (int i = 0; i < n; ++i) {
+    const GemvArgs& a = ph[i];
+    if (a.B != ph[0].B || a.B > 4 || size_t(a.B) * a.K * 2 > 200 * 1024 || a.num_sms != ph[0].num_sms)
+      return false;
+    if (i < 3 && (a.epi != epi[i] || (a.norm_w != nullptr) != (i == 1))) return false;
+    if (i == 3 && ((a.epi != kGemvQkvRope && a.epi != kGemvArgmax) || a.norm_w == nullptr)) return false;
+  }
+  return true;
+}
+
+const char* gemv_chain(const GemvArgs* ph, int n, unsigned int* ctr, int* status, cudaStream_t s) {
+  if (!gemv_chain_supported(ph, n))
+    return "gemv_chain: residual, norm + SwiGLU, residual, norm + (QKV rope | argmax); 1, 2 or 4 rows";
+  if (ctr == nullptr) return "gemv_chain: needs a zeroed counter pair";
+  GemvChainArgs c;
+  size_t smem = 0;
+  for (int i = 0; i < n; ++i) {
+    if (const char* err = gemv_check(ph[i])) return err;
+    c.ph[i] = ph[i];
+    const size_t need = size_t(ph[i].B) * ph[i].K * 2;
+    smem = need > smem ? need : smem;
+  }
+  c.ctr = ctr;
+  c.status = status;
+  const bool qkv = ph[3].epi == kGemvQkvRope;
+  cudaError_t e;
+  switch (ph[0].B) {
+    case 1: e = qkv ? launch_chain<1, kGemvQkvRope>(c, smem, s) : launch_chain<1, kGemvArgmax>(c, smem, s); break;
+    case 2: e = qkv ? launch_chain<2, kGemvQkvRope>(c, smem, s) : launch_chain<2, kGemvArgmax>(c, smem, s); break;
+    default: e = qkv ? launch_chain<4, kGemvQkvRope>(c, smem, s) : launch_chain<4, kGemvArgmax>(c, smem, s); break;
   }
   return e == cudaSuccess ? nullptr : cudaGetErrorString(e);
 }

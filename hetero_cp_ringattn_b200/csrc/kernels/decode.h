@@ -162,6 +162,23 @@ struct ArgmaxXchgArgs {
 };
 
 const char* gemv(const GemvArgs& a, cudaStream_t s);
+// The argument checks of gemv() alone (nullptr when the launch would be accepted).
+const char* gemv_check(const GemvArgs& a);
+
+// The four decode GEMVs between two attention launches as one cooperative launch with grid
+// barriers between them, in this order: residual (output projection, optionally with the
+// cross-rank combine prologue), RMSNorm + SwiGLU (gate/up), residual (down projection), RMSNorm +
+// QKV rope (the next layer) or RMSNorm + argmax (LM head). Same batch size (1, 2 or 4 rows) in
+// every phase. `ctr` is a zeroed pair of 32-bit counters owned by this launch site (the launch
+// leaves it zeroed again); `status` receives barrier timeouts.
+constexpr int kGemvChainPhases = 4;
+struct GemvChainArgs {
+  GemvArgs ph[kGemvChainPhases];
+  unsigned int* ctr = nullptr;
+  int* status = nullptr;
+};
+bool gemv_chain_supported(const GemvArgs* ph, int n);
+const char* gemv_chain(const GemvArgs* ph, int n, unsigned int* ctr, int* status, cudaStream_t s);
 const char* argmax_exchange(const ArgmaxXchgArgs& a, cudaStream_t s);
 const char* decode_attn(const DecodeAttnArgs& a, cudaStream_t s);
 // Resident decode_attn CTAs per SM for (head_dim, GQA group size); 0 when unsupported. Callers

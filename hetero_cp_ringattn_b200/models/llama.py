@@ -812,6 +812,8 @@ class DecodeGraph:
         self.part_o = torch.zeros(B * eng.H * self.splits * eng.D, dtype=torch.float32, device=dev)
         self.part_l = torch.zeros(B * eng.H * self.splits, dtype=torch.float32, device=dev)
         self.counters = torch.zeros(B * eng.Hkv + 1, dtype=torch.int32, device=dev)
+        # one zeroed barrier-counter pair per GEMV chain launch site (one per layer)
+        self.chain_ctr = torch.zeros(L, 2, dtype=torch.int32, device=dev)
         self.graphs: Dict[bool, torch.cuda.CUDAGraph] = {}
         self.graph_launches: Dict[bool, int] = {}
         self.copied = None
@@ -823,14 +825,40 @@ class DecodeGraph:
         nat.add_u64(e.dec_step, 1)
         launches.count()
         K.embedding(self.tokens, w.embed, out=self.x)
+        nat.fill_u64(self.am, 0)
+        launches.count()
         eps = cfg.rms_norm_eps
         single = e.world == 1
         head = e.lm_head_slice if split else w.lm_head
         pf = self.prefetch_plan(head)
-        for li, lw in enumerate(w.layers):
+        L = len(w.layers)
+        # HCP_DECODE_CHAIN=1: the GEMVs between two attentions (output projection, gate/up,
+        # down, then the next layer's QKV projection or the LM head) run as one cooperative
+        # chain launch with grid barriers between them (batches of up to 4 rows; measured
+        # slower than the four launches, so off by default)
+        chain = e.env.decode_chain and self.B <= 4
+
+        def qkv(li: int) -> None:
+            lw = w.layers[li]
             # RMSNorm + QKV GEMV whose epilogue applies RoPE, writes q and appends k/v on the owner
             rt.qkv_gemv_rope(self.x, lw.wqkv, lw.bqkv, lw.in_norm, eps, self.pos, e.cos, e.sin, li,
                              self.pt, self.owner, self.slot, self.q, prefetch=pf[li][0])
+
+        def lm_head() -> None:
+            if split:
+                # greedy step, head split over the vocabulary: this rank's rows only (no logits),
+                # then every rank stores its packed maxima into every rank's slots and takes the
+                # max
+                K.gemv(self.x, e.lm_head_slice, "argmax", argmax=self.am, norm_w=w.final_norm,
+                       eps=eps, index_base=e.vocab_lo)
+            else:
+                K.gemv(self.x, w.lm_head, "argmax", y_f32=self.logits, argmax=self.am,
+                       norm_w=w.final_norm, eps=eps)
+
+        head_done = False
+        for li, lw in enumerate(w.layers):
+            if li == 0 or not chain:       # else the previous layer's chain ran it
+                qkv(li)
             # split-KV attention; on one rank its last CTA writes the layer output directly.
             # With several ranks the rank's (O, LSE) partial goes into every rank's slots and
             # the log-sum-exp combine in rank order follows a bounded wait for the other ranks'
@@ -845,7 +873,9 @@ class DecodeGraph:
                            prefetch=pf[li][1])
             if mode == "launch":
                 rt.decode_combine(self.o, self.B, e.H, e.dec_step, e.L, li + 1)
-            launches.count(3 if mode == "launch" else 2)
+            launches.count((3 if mode == "launch" else 2) - (1 if chain and li > 0 else 0))
+            if chain:
+                nat.gemv_chain_begin()
             if mode == "gemv":
                 rt.o_proj_combine(self.o, lw.wo, self.x, e.dec_step, e.L, li + 1)
                 launches.count()
@@ -854,18 +884,24 @@ class DecodeGraph:
             K.gemv(self.x, lw.wgu, "swiglu", y_bf16=self.g, norm_w=lw.post_norm, eps=eps,
                    prefetch=pf[li][3])
             K.gemv(self.g, lw.wd, "residual", y_bf16=self.x)
-        nat.fill_u64(self.am, 0)
+            if chain:
+                last = li + 1 == L
+                if last:
+                    lm_head()
+                    head_done = True
+                else:
+                    qkv(li + 1)
+                ran = nat.gemv_chain_end(self.chain_ctr[li])
+                # counted so far in the chain: o, gate/up, down (+ the LM head); launched: one
+                # chain kernel, or the four GEMVs one by one
+                launches.count((1 if ran else 4) - (4 if last else 3))
+        if not head_done:
+            lm_head()
         if split:
-            # greedy step, head split over the vocabulary: this rank's rows only (no logits),
-            # then every rank stores its packed maxima into every rank's slots and takes the max
-            K.gemv(self.x, e.lm_head_slice, "argmax", argmax=self.am, norm_w=w.final_norm, eps=eps,
-                   index_base=e.vocab_lo)
             rt.argmax_exchange(self.am, e.dec_step, self.tokens, self.out_tok)
         else:
-            K.gemv(self.x, w.lm_head, "argmax", y_f32=self.logits, argmax=self.am,
-                   norm_w=w.final_norm, eps=eps)
             nat.argmax_finalize(self.am, self.tokens, self.out_tok)
-        launches.count(2)
+        launches.count()
 
     def prefetch_plan(self, head: torch.Tensor) -> list:
         """Per layer, the weights each decode kernel pulls into L2 for a later kernel while it

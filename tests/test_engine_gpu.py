@@ -96,12 +96,14 @@ def test_session_append_matches_oracle():
 
 
 @pytest.mark.parametrize("env_kwargs", [dict(decode_prefetch=1), dict(decode_prefetch=3),
-                                        dict(decode_splits=8), dict(decode_combine="gemv")])
+                                        dict(decode_splits=8), dict(decode_combine="gemv"),
+                                        dict(decode_chain=True)])
 def test_decode_switches_keep_the_tokens(env_kwargs):
     """Decode switches that only move work around (L2 prefetch of later weights, a cap on the
-    KV splits, where the cross-rank combine runs: unused on one rank) give the default engine's
-    greedy tokens; the split cap changes the attention's summation order, so its logits are
-    held to the bf16 tolerance instead of bit equality."""
+    KV splits, where the cross-rank combine runs: unused on one rank, the GEMVs between two
+    attentions as one chain launch instead of four launches) give the default engine's greedy
+    tokens; the split cap changes the attention's summation order, so its logits are held to the
+    bf16 tolerance instead of bit equality."""
     from hetero_cp_ringattn_b200.config import EnvConfig, preset
     from hetero_cp_ringattn_b200.models.llama import LlamaCPEngine
     from hetero_cp_ringattn_b200.models.weights import ModelWeights, PreparedWeights

@@ -288,6 +288,50 @@ def test_gemv_bulk_bit_identical_to_cuda_core(dev, b, kdim):
         assert torch.equal(u, v)
 
 
+@pytest.mark.parametrize("b", [1, 2, 4])
+def test_gemv_chain_matches_separate_launches(dev, b):
+    """One cooperative chain launch (output projection + residual, RMSNorm + gate/up + SwiGLU,
+    down projection + residual, RMSNorm + LM head + argmax with logits; each phase reads what
+    the previous one wrote) gives the same bits as the four GEMVs launched one by one, on two
+    launches in a row that share one counter pair (each launch leaves it zeroed)."""
+    torch.manual_seed(15)
+    hid, inter, vocab = 2048, 8192, 32000
+    o = torch.randn(b, hid, device=dev, dtype=torch.bfloat16)
+    wo = torch.randn(hid, hid, device=dev, dtype=torch.bfloat16) / math.sqrt(hid)
+    wgu = torch.randn(2 * inter, hid, device=dev, dtype=torch.bfloat16) / math.sqrt(hid)
+    wd = torch.randn(hid, inter, device=dev, dtype=torch.bfloat16) / math.sqrt(inter)
+    wl = torch.randn(vocab, hid, device=dev, dtype=torch.bfloat16) / math.sqrt(hid)
+    n1 = (torch.rand(hid, device=dev) + 0.5).bfloat16()
+    n2 = (torch.rand(hid, device=dev) + 0.5).bfloat16()
+    x0 = torch.randn(b, hid, device=dev, dtype=torch.bfloat16)
+    ctr = torch.zeros(2, dtype=torch.int32, device=dev)
+
+    def run(chain):
+        x = x0.clone()
+        g = torch.empty(b, inter, device=dev, dtype=torch.bfloat16)
+        am = torch.zeros(b, dtype=torch.int64, device=dev)
+        logits = torch.empty(b, vocab, device=dev, dtype=torch.float32)
+        st = status_tensor(dev)
+        if chain:
+            native().gemv_chain_begin()
+        K.gemv(o, wo, "residual", y_bf16=x)
+        K.gemv(x, wgu, "swiglu", y_bf16=g, norm_w=n1, eps=1e-5)
+        K.gemv(g, wd, "residual", y_bf16=x)
+        K.gemv(x, wl, "argmax", y_f32=logits, argmax=am, norm_w=n2, eps=1e-5)
+        if chain:
+            assert native().gemv_chain_end(ctr, st)
+        torch.cuda.synchronize()
+        assert_status_clean(st)
+        return x, g, am, logits
+
+    want = run(False)
+    for _ in range(2):
+        got = run(True)
+        for u, v in zip(want, got):
+            assert torch.equal(u, v)
+        assert int(ctr.abs().sum()) == 0
+
+
 @pytest.mark.parametrize("kern", list(GEMV_KERNELS))
 def test_gemv_batch_larger_than_staging(dev, kern):
     """B x K too large for one shared-memory x stage (8 rows x 14336, the Llama-3-8B down
