@@ -409,7 +409,9 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(GemvArgs a) {
 // first stages stream while the previous kernel of the decode chain finishes. Warp w computes
 // item w of each stage against x in shared memory and releases the stage on its "empty"
 // mbarrier; thread 0 refills a slot once all 8 warps have released it. Every wait is bounded and
-// reports into the status word.
+// reports into the status word. Parity: the decode-token projections of the reference's layers
+// (x.matmul(W^T) in rust/src/model/layers/mlp.rs:42-67 and the attention projections), with
+// their norms, activation and residuals fused as epilogues.
 template <int EPI, int B, bool NORM>
 __global__ void __launch_bounds__(GEMV_THREADS) gemv_bulk_kernel(GemvArgs a) {
   extern __shared__ __align__(128) unsigned char gsm[];  // [x rows][ring of stages]
@@ -878,7 +880,10 @@ __device__ __forceinline__ bool chain_barrier(unsigned int* ctr, unsigned int ta
 // constant offset. Measured on B200 it is slower than the four launches it replaces (Llama-3.2-1B
 // decode at 32k: 1.18-1.27 against 1.09-1.12 ms per token at batch 1, 2.50-2.61 against
 // 1.96-2.09 at batch 4, also with a back-off in the barrier poll and with the launch allowed to
-// start early), so the engine runs it only with HCP_DECODE_CHAIN=1. The dependent launch (the next attention) is released once the last barrier
+// start early), so the engine runs it only with HCP_DECODE_CHAIN=1. Parity: the decoder layer's
+// attention residual, post-attention RMSNorm, MLP and MLP residual (rust/src/model/layers/mod.rs:
+// 59-77; the MLP rust/src/model/layers/mlp.rs:42-67), then the next layer's input RMSNorm and
+// projection or the final norm and LM head, for one decode token per row. The dependent launch (the next attention) is released once the last barrier
 // is passed. ctr[0] counts barrier arrivals and ctr[1] CTAs done; the last CTA out sets both back
 // to zero, so one counter pair serves every replay of a captured graph.
 template <int B, int LAST>
