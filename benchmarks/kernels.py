@@ -256,6 +256,62 @@ def bench_decode(args, dev, pk):
     eng.close()
 
 
+def bench_chunked(args, dev, pk):
+    """Prefill of a ``--seq``-token prompt in one call against the chunked prefill of
+    ``serve --prefill-chunk-tokens P`` for each P of ``--pieces``: the first P tokens through
+    ``prefill`` (ring layout, session kept), the rest as continuation segments of P tokens
+    through ``append`` (each attends to every stored row of the session). One rank; ms per
+    prompt, CUDA events around the whole prompt (host work included, as in serving)."""
+    from hetero_cp_ringattn_b200.config import preset
+    from hetero_cp_ringattn_b200.models.llama import LlamaCPEngine
+    from hetero_cp_ringattn_b200.models.weights import PreparedWeights
+    cfg = preset(args.model)
+    cfg.num_layers = 2 if args.small else (args.layers or cfg.num_layers)
+    ctx = 8192 if args.small else args.seq
+    w = PreparedWeights.random(cfg, seed=0, device=dev)
+    eng = LlamaCPEngine(cfg, w, device=dev, max_context=ctx, max_batch=1, decode_reserve=16)
+    prompt = torch.randint(0, cfg.vocab_size, (ctx,), dtype=torch.int64)
+
+    def whole():
+        tok, _ = eng.prefill(1, prompt, [ctx], decode_horizon=8)
+        eng.release(1)
+        return tok
+
+    def pieces(p):
+        tok, _ = eng.prefill(1, prompt[:p], [p], decode_horizon=8, keep_kv=True)
+        done = p
+        while done < ctx:
+            end = min(ctx, done + p)
+            tok, _ = eng.append(1, prompt[done:end], list(range(done, end)), [1])
+            done = end
+        eng.release(1)
+        return tok
+
+    def time_it(fn):
+        for _ in range(2):
+            fn()
+        torch.cuda.synchronize()
+        best = float("inf")
+        for _ in range(max(1, args.iters)):
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            tok = fn()
+            e.record()
+            e.synchronize()
+            best = min(best, s.elapsed_time(e))
+        return best, int(tok)
+
+    ms_whole, tok_whole = time_it(whole)
+    for p in args.pieces:
+        if p >= ctx:
+            continue
+        ms, tok = time_it(lambda: pieces(p))
+        emit(kernel="chunked_prefill", model=args.model, layers=cfg.num_layers, prompt=ctx, piece=p,
+             segments=-(-ctx // p), ms=round(ms, 2), ms_whole=round(ms_whole, 2),
+             ratio=round(ms / ms_whole, 3), same_token=tok == tok_whole)
+    eng.close()
+
+
 # ----------------------------------------------------------------------------- ring sweep
 def parse_ratio(text: str, n: int) -> list:
     """'1:1' -> equal; 'a:b' with n > 2 -> first half of the ranks weight a, second half b."""
@@ -385,12 +441,14 @@ def bench_ring(args, pk):
 
 def main(argv=None):
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
-    ap.add_argument("what", choices=["gemm", "attn", "gemv", "norm", "decode", "ring"])
+    ap.add_argument("what", choices=["gemm", "attn", "gemv", "norm", "decode", "ring", "chunked"])
     ap.add_argument("--small", action="store_true", help="one small case (sized for an ncu capture)")
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--tokens", type=int, default=32768)
     ap.add_argument("--seqs", type=lambda s: [int(x) for x in s.split(",")], default=[8192, 32768])
     ap.add_argument("--seq", type=int, default=32768)
+    ap.add_argument("--pieces", type=lambda s: [int(x) for x in s.split(",")], default=[4096, 8192],
+                    help="chunked: prefill piece sizes")
     ap.add_argument("--layers", type=int, default=0, help="decode: layers (0 = the model's)")
     ap.add_argument("--model", default="llama-3.2-1b", help="decode: model preset")
     ap.add_argument("--ratio", default="1:1")
@@ -421,7 +479,7 @@ def main(argv=None):
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     {"gemm": bench_gemm, "attn": bench_attn, "gemv": bench_gemv, "norm": bench_norm,
-     "decode": bench_decode}[args.what](args, dev, pk)
+     "decode": bench_decode, "chunked": bench_chunked}[args.what](args, dev, pk)
 
 
 if __name__ == "__main__":
