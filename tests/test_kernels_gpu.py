@@ -332,6 +332,43 @@ def test_gemv_chain_matches_separate_launches(dev, b):
         assert int(ctr.abs().sum()) == 0
 
 
+def test_gemv_chain_falls_back_to_separate_launches(dev):
+    """A recorded sequence that is not the chain's phase order (two GEMVs), or the chain's order
+    at a batch of 8 rows, runs as separate launches: gemv_chain_end returns False and the results
+    are those of direct launches."""
+    torch.manual_seed(16)
+    hid, inter = 2048, 4096
+    wo = torch.randn(hid, hid, device=dev, dtype=torch.bfloat16) / math.sqrt(hid)
+    wgu = torch.randn(2 * inter, hid, device=dev, dtype=torch.bfloat16) / math.sqrt(hid)
+    wd = torch.randn(hid, inter, device=dev, dtype=torch.bfloat16) / math.sqrt(inter)
+    wl = torch.randn(1024, hid, device=dev, dtype=torch.bfloat16) / math.sqrt(hid)
+    nw = (torch.rand(hid, device=dev) + 0.5).bfloat16()
+    ctr = torch.zeros(2, dtype=torch.int32, device=dev)
+    for b, full in ((2, False), (8, True)):
+        o = torch.randn(b, hid, device=dev, dtype=torch.bfloat16)
+        x0 = torch.randn(b, hid, device=dev, dtype=torch.bfloat16)
+
+        def run(record):
+            x = x0.clone()
+            g = torch.zeros(b, inter, device=dev, dtype=torch.bfloat16)
+            am = torch.zeros(b, dtype=torch.int64, device=dev)
+            if record:
+                native().gemv_chain_begin()
+            K.gemv(o, wo, "residual", y_bf16=x)
+            K.gemv(x, wgu, "swiglu", y_bf16=g, norm_w=nw, eps=1e-5)
+            if full:
+                K.gemv(g, wd, "residual", y_bf16=x)
+                K.gemv(x, wl, "argmax", argmax=am, norm_w=nw, eps=1e-5)
+            if record:
+                assert native().gemv_chain_end(ctr) is False
+            torch.cuda.synchronize()
+            return x, g, am
+
+        for u, v in zip(run(False), run(True)):
+            assert torch.equal(u, v)
+    assert int(ctr.abs().sum()) == 0
+
+
 @pytest.mark.parametrize("kern", list(GEMV_KERNELS))
 def test_gemv_batch_larger_than_staging(dev, kern):
     """B x K too large for one shared-memory x stage (8 rows x 14336, the Llama-3-8B down
